@@ -1,0 +1,275 @@
+/*
+ * ns_b200.h -- C ABI of the B200 (sm_100a) backend for NeuralSuite's GPT
+ * training step.
+ *
+ * The reference (NeuralSuite, a C++17 CPU library) has no plugin or FFI layer:
+ * its boundary is the C++ API of Tensor / Layer::Forward / Layer::Backward /
+ * Loss / Optimizer.  Each entry point below replaces one function or method of
+ * that API; the reference symbol it stands in for is cited beside it
+ * (paths inside the NeuralSuite project).  A C++ shim with the reference's
+ * class names (neuralsuite_b200/csrc/gpt_device.h) sits on top of these calls,
+ * and the model-level ns_gpt_* calls drive that shim for callers in other
+ * languages.
+ *
+ * Conventions
+ *  - Every buffer argument is a DEVICE pointer to fp32 row-major data unless
+ *    its name says host_ / int32.  Token ids are int32 (the reference carries
+ *    them as float and truncates, include/layers/embedding.h:43).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Every call returns an ns_status; on failure ns_last_error() returns a
+ *    thread-local message.  No C++ exception crosses this boundary; the C++
+ *    shim rethrows std::invalid_argument / std::out_of_range like the
+ *    reference.
+ *  - Kernels are asynchronous on `stream`.  Entry points with a `workspace`
+ *    argument take caller-owned device scratch of at least the size the
+ *    matching *_workspace_size query returns; none of the kernel entry
+ *    points allocates memory.
+ */
+#ifndef NS_B200_H_
+#define NS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NS_API __attribute__((visibility("default")))
+#else
+#define NS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  NS_OK = 0,
+  NS_ERR_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+  NS_ERR_OUT_OF_RANGE = 2,     /* reference: std::out_of_range (bad token id) */
+  NS_ERR_CUDA = 3,             /* a CUDA runtime error */
+  NS_ERR_UNSUPPORTED = 4,      /* e.g. no sm_100 device */
+  NS_ERR_COMM = 5,             /* NCCL error or communicator aborted */
+  NS_ERR_TIMEOUT = 6           /* a bounded host wait ran out */
+} ns_status;
+
+NS_API const char* ns_last_error(void);
+NS_API int ns_version(void);
+/* 1 when the current device is an sm_100 part the tcgen05 kernels can run on. */
+NS_API int ns_device_supported(void);
+
+/* ------------------------------------------------------------------ K1 GEMM
+ * C[M,N] = op(A) * op(B)  (+ epilogue), fp32 in / fp32 out, 3xTF32 on the
+ * tcgen05 tensor cores (A = Ahi + Alo, B = Bhi + Blo, C ~ Ahi*Bhi + Ahi*Blo +
+ * Alo*Bhi, accumulated in TMEM).
+ *   a_trans = 0: A stored [M,K] (row stride lda);  1: A stored [K,M] (A^T).
+ *   b_trans = 0: B stored [K,N] (row stride ldb);  1: B stored [N,K] (B^T).
+ * Replaces MatMul (src/tensor.cpp:198-271) together with the Transpose copies
+ * Linear / GPTModel make before the "T" products (src/tensor.cpp:275-288,
+ * include/layers/linear.h:95-102, include/gpt.h:226-252).
+ *
+ * Epilogues (the element of the GEMM result is `acc`):
+ *   NS_EPI_STORE      C = acc                       (MatMul; beta=1 adds into C)
+ *   NS_EPI_BIAS       C = acc + bias[n]             (Linear::Forward, linear.h:69-76)
+ *   NS_EPI_BIAS_GELU  C = acc + bias[n]; aux_out = gelu(C)
+ *                     (Linear::Forward then GeluForward, src/tensor.cpp:428-443)
+ *   NS_EPI_BIAS_RESID C = aux[m,n] + (acc + bias[n])
+ *                     (Linear::Forward then ElementwiseAdd, include/gpt.h:70,77)
+ *   NS_EPI_GELU_BWD   C = acc * gelu'(aux[m,n])     (Linear::Backward dX then
+ *                     GeluBackward, src/tensor.cpp:445-461)
+ * beta is 0 (overwrite, the reference's MatMul Resize+Zeros) or 1 (accumulate
+ * into C, used for the weight-tied wte gradient, include/gpt.h:266-269); it is
+ * only accepted with NS_EPI_STORE.  aux/aux_out rows use stride ldc.
+ *
+ * `workspace` (may be NULL) lets the kernel split K across CTAs when the
+ * output has too few tiles to fill the GPU (the dW products); partial tiles
+ * are summed in a fixed order, so results do not depend on timing.  With less
+ * than ns_gemm_workspace_size bytes the call runs without splitting.
+ */
+enum {
+  NS_EPI_STORE = 0,
+  NS_EPI_BIAS = 1,
+  NS_EPI_BIAS_GELU = 2,
+  NS_EPI_BIAS_RESID = 3,
+  NS_EPI_GELU_BWD = 4
+};
+NS_API size_t ns_gemm_workspace_size(int M, int N, int K);
+NS_API ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
+                  int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
+                  const float* bias, const float* aux, float* aux_out, void* workspace,
+                  size_t workspace_bytes, void* stream);
+/* Selects the GEMM engine for subsequent calls on this thread: 0 = automatic
+ * (tcgen05 wherever the operands allow TMA, SIMT fp32 otherwise), 1 = always
+ * the SIMT fp32 kernel.  Used by tests to cross-check the two engines. */
+NS_API ns_status ns_gemm_set_engine(int engine);
+/* NS_ERR_TIMEOUT if any kernel of this library gave up a bounded wait on the
+ * current device since the last call (the flag is cleared by the call). */
+NS_API ns_status ns_kernel_health(void);
+
+/* Column sums db[n] = sum_m dY[m,n]: the bias gradient of Linear::Backward
+ * (include/layers/linear.h:104-111, overwritten).  Deterministic two-stage
+ * reduction through `workspace`. */
+NS_API size_t ns_bias_grad_workspace_size(int M, int N);
+NS_API ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ K2 attention
+ * Fused causal self-attention on the interleaved c_attn output
+ * qkv[B*T, 3*H*D] (Q of head h at columns h*D, K at C+h*D, V at 2C+h*D, the
+ * layout of MultiHeadAttention::Extraer, include/layers/attention.h:563-575).
+ * Forward writes out[B*T, H*D] (head h at columns h*D, attention.h:379-382)
+ * and lse[B*H*T], the per-row log-sum-exp of the scaled scores, instead of the
+ * reference's [B,H,T,T] probability cache (attention.h:361-378).
+ * Replaces the per-(b,h) loop of MultiHeadAttention::Forward
+ * (attention.h:364-384) and ::Backward (attention.h:405-461); backward writes
+ * dqkv[B*T, 3C] in the same interleaved layout and needs `workspace` of
+ * ns_attn_bwd_workspace_size bytes.  Scale = 1/sqrt(D) applied after Q.K^T
+ * (attention.h:362, 372-374). */
+NS_API ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
+                      void* stream);
+NS_API size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D);
+NS_API ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, const float* lse,
+                      int B, int T, int H, int D, float* dqkv, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------ K3 bandwidth kernels */
+/* LayerNormForward, src/tensor.cpp:290-322 (last axis, biased variance). */
+NS_API ns_status ns_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* out,
+                           float* mean, float* rstd, int rows, int dim, float eps, void* stream);
+/* LayerNormBackward, src/tensor.cpp:324-359.  dgamma/dbeta are overwritten
+ * (deterministic two-stage column sums through `workspace`).  If `dresid` is
+ * non-NULL the result is dx = dresid + dx_ln: the ElementwiseAdd of the
+ * residual gradient in GPTBlock::Backward (include/gpt.h:89-97). */
+NS_API size_t ns_layernorm_bwd_workspace_size(int rows, int dim);
+NS_API ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma,
+                           const float* mean, const float* rstd, const float* dresid, float* dx,
+                           float* dgamma, float* dbeta, int rows, int dim, void* workspace,
+                           size_t workspace_bytes, void* stream);
+/* GeluForward / GeluBackward, src/tensor.cpp:428-461. */
+NS_API ns_status ns_gelu_fwd(const float* x, float* y, int64_t n, void* stream);
+NS_API ns_status ns_gelu_bwd(const float* dout, const float* x, float* dx, int64_t n, void* stream);
+/* ElementwiseAdd, src/tensor.cpp:534-540. */
+NS_API ns_status ns_add(const float* a, const float* b, float* out, int64_t n, void* stream);
+/* CrossEntropyLoss::Forward + ::Backward fused (include/losses.h:34-86):
+ * loss_out (one device float) = mean over rows of -log softmax(logits)[t];
+ * dlogits = (softmax - onehot(t)) / denom, where denom = rows for the
+ * reference's single-process step and rows*world_size under data parallel.
+ * Targets out of [0, classes) are reported as NS_ERR_OUT_OF_RANGE after the
+ * fact through *err_flag (device int, may be NULL). */
+NS_API size_t ns_cross_entropy_workspace_size(int rows, int classes);
+NS_API ns_status ns_cross_entropy(const float* logits, const int32_t* targets, int rows, int classes,
+                           float denom, float* loss_out, float* dlogits, int32_t* err_flag,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ K4 embedding
+ * out[b,t,:] = wte[tok[b,t],:] + wpe[t,:]  (Embedding::Forward twice plus the
+ * add of GPTModel::Forward, include/layers/embedding.h:34-59,
+ * include/gpt.h:197-212).  A token outside [0, vocab) sets *err_flag (device
+ * int) and its row is written as zeros; host callers validate first, which is
+ * where the reference's std::out_of_range comes from (embedding.h:45-49). */
+NS_API ns_status ns_embedding_fwd(const int32_t* tokens, int B, int T, const float* wte, int vocab,
+                           const float* wpe, int block, int dim, float* out, int32_t* err_flag,
+                           void* stream);
+/* Embedding::Backward for wte and wpe (embedding.h:61-80) followed by the
+ * weight-tying add of GPTModel::Backward (gpt.h:262-269):
+ *   dwte[v,:] = (sum over rows r with tok[r]==v, ascending r, of dx[r,:]) + dwte[v,:]
+ *   dwpe[t,:] =  sum over b ascending of dx[b,t,:]     (rows t >= T zeroed)
+ * Sums run in the reference's order, so the result is bit-identical to it.
+ * If accumulate_wte is 0 the incoming dwte is treated as zero. */
+NS_API ns_status ns_embedding_bwd(const int32_t* tokens, int B, int T, const float* dx, int vocab,
+                           int block, int dim, float* dwte, int accumulate_wte, float* dwpe,
+                           void* stream);
+
+/* -------------------------------------------------------------- K5 AdamW
+ * One launch over every tensor of a flat parameter buffer (AdamW::Step,
+ * include/optimizers.h:206-234): per element, in the reference's order,
+ *   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g;
+ *   p -= lr*wd_t*p (if wd_t > 0);  p -= lr*(m/bc1)/(sqrt(v/bc2)+eps)
+ * Segment t covers [seg_offsets[t], seg_offsets[t+1]) with decay seg_decay[t]
+ * (host arrays, n_seg entries; offsets has n_seg+1).  bc1 = 1 - b1^step and
+ * bc2 = 1 - b2^step are computed by the caller in double and rounded to float,
+ * as the reference does (optimizers.h:208-210). */
+NS_API ns_status ns_adamw_flat(float* params, const float* grads, float* m, float* v, int64_t n_total,
+                        const int64_t* host_seg_offsets, const float* host_seg_decay, int n_seg,
+                        float lr, float b1, float b2, float eps, float bc1, float bc2,
+                        void* stream);
+/* Sum of squares of a flat gradient buffer into one device float (the norm of
+ * ClipGradients, train_llm.cpp:112-121), and the in-place scale by
+ * min(1, max_norm / sqrt(sumsq)) of train_llm.cpp:122-128, read on the device. */
+NS_API size_t ns_sumsq_workspace_size(int64_t n);
+NS_API ns_status ns_sumsq(const float* x, int64_t n, float* out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+NS_API ns_status ns_clip_scale(float* x, int64_t n, const float* sumsq, float max_norm, void* stream);
+
+/* ------------------------------------------------- data-parallel comm (NCCL)
+ * One communicator per process/GPU over NVLink.  NCCL is loaded at run time
+ * (dlopen libnccl.so.2), so the library loads on machines without it.  The
+ * reference has no distributed code; these exist for the data-parallel step. */
+typedef struct ns_comm ns_comm;
+NS_API ns_status ns_comm_unique_id(uint8_t host_id_out[128]);
+NS_API ns_status ns_comm_init(const uint8_t host_id[128], int world_size, int rank, ns_comm** out);
+/* In-place sum over ranks of count floats on `stream`. */
+NS_API ns_status ns_comm_allreduce_sum(ns_comm* comm, float* buf, int64_t count, void* stream);
+/* Host poll of the communicator's asynchronous error state. */
+NS_API ns_status ns_comm_check(ns_comm* comm);
+NS_API ns_status ns_comm_abort(ns_comm* comm);
+NS_API ns_status ns_comm_destroy(ns_comm* comm);
+
+/* ------------------------------------------------------------ GPT model
+ * The device GPTModel (include/gpt.h:136-327) + CrossEntropyLoss + AdamW, with
+ * parameters, gradients, optimizer state and every activation resident in
+ * HBM.  Parameters are one flat buffer in Module::Parameters() registration
+ * order (include/module.h:44-52):
+ *   wte, wpe, per block [ln_1 g b, c_attn W b, c_proj W b, ln_2 g b,
+ *   mlp_fc W b, mlp_proj W b], ln_f g b
+ * and gradients a second flat buffer with the same offsets. */
+typedef struct ns_gpt ns_gpt;
+typedef struct {
+  int vocab_size, block_size, n_layer, n_head, n_embd; /* GPTConfig, gpt.h:33-39 */
+  int max_batch;                                        /* sequences per step on this GPU */
+} ns_gpt_config;
+
+NS_API ns_status ns_gpt_create(const ns_gpt_config* cfg, ns_gpt** out);
+NS_API ns_status ns_gpt_destroy(ns_gpt* model);
+NS_API int ns_gpt_num_tensors(const ns_gpt* model);
+NS_API int64_t ns_gpt_tensor_numel(const ns_gpt* model, int i);
+NS_API int ns_gpt_tensor_rank(const ns_gpt* model, int i);
+NS_API int64_t ns_gpt_tensor_offset(const ns_gpt* model, int i);
+NS_API int64_t ns_gpt_num_params(const ns_gpt* model);
+NS_API float* ns_gpt_params(ns_gpt* model); /* device, num_params floats */
+NS_API float* ns_gpt_grads(ns_gpt* model);  /* device, num_params floats */
+/* Device buffers of the last step: logits [B*T, V], dlogits, loss (1 float). */
+NS_API float* ns_gpt_logits(ns_gpt* model);
+NS_API float* ns_gpt_loss(ns_gpt* model);
+
+/* GPTModel::Forward (gpt.h:192-232) on device int32 tokens [B,T]. */
+NS_API ns_status ns_gpt_forward(ns_gpt* model, const int32_t* tokens, int B, int T, void* stream);
+/* CrossEntropyLoss Forward/Backward on the last logits (losses.h:34-86);
+ * dlogits are scaled by 1/(B*T*world_size). */
+NS_API ns_status ns_gpt_loss_backward(ns_gpt* model, const int32_t* targets, void* stream);
+/* GPTModel::Backward (gpt.h:234-272), gradients overwritten.  With a
+ * communicator attached, gradient buckets are all-reduced over NCCL as their
+ * blocks finish, overlapped with the rest of the backward. */
+NS_API ns_status ns_gpt_backward(ns_gpt* model, void* stream);
+/* AdamW (optimizers.h:148-162): configure, then Step (206-234). */
+NS_API ns_status ns_gpt_adamw_init(ns_gpt* model, float lr, float b1, float b2, float eps, float wd);
+NS_API ns_status ns_gpt_adamw_set_lr(ns_gpt* model, float lr);
+NS_API ns_status ns_gpt_adamw_step(ns_gpt* model, void* stream);
+/* ClipGradients(params, max_norm), train_llm.cpp:112-129, device-side. */
+NS_API ns_status ns_gpt_clip_gradients(ns_gpt* model, float max_norm, void* stream);
+/* One whole training step: forward, loss, backward (+ all-reduce), optional
+ * clip (max_norm <= 0 disables), AdamW step.  host_loss may be NULL; if set,
+ * the step synchronises the stream and returns the loss. */
+NS_API ns_status ns_gpt_train_step(ns_gpt* model, const int32_t* tokens, const int32_t* targets, int B,
+                            int T, float max_norm, float* host_loss, void* stream);
+/* Data parallel: attach a communicator (NULL detaches).  bucket_floats caps a
+ * gradient bucket (0 = one bucket per GPTBlock). */
+NS_API ns_status ns_gpt_set_comm(ns_gpt* model, ns_comm* comm, int world_size, int64_t bucket_floats);
+/* Gradient-bucket plan of the attached world (host-only; usable without a
+ * GPU): writes up to max_buckets [begin, end) float ranges in launch order. */
+NS_API int ns_gpt_plan_buckets(const ns_gpt_config* cfg, int64_t bucket_floats, int64_t* begin,
+                        int64_t* end, int max_buckets);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NS_B200_H_ */

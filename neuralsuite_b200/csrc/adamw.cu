@@ -1,0 +1,113 @@
+// K5: AdamW over every parameter tensor in one launch (AdamW::Step,
+// include/optimizers.h:206-234).  Parameters, gradients and both moments are
+// flat buffers in registration order; the host cuts them into chunks of at
+// most kChunk elements that never straddle a tensor, and passes the chunk
+// table by value (kernel parameter space), so one CTA = one chunk with a
+// uniform weight decay.  28 bytes of HBM traffic per parameter.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+
+namespace nsb {
+namespace {
+
+constexpr int kMaxChunks = 512;      // per launch: 512 x 16 B of kernel parameters
+constexpr int64_t kChunk = 1 << 17;  // elements per CTA
+
+struct AdamChunk {
+  int64_t start;
+  int32_t len;
+  float decay;
+};
+
+struct AdamTable {
+  AdamChunk c[kMaxChunks];
+};
+
+// The update, with every multiply/add rounded separately as in the reference.
+__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, float lr, float b1,
+                                         float b2, float eps, float bc1, float bc2, float decay) {
+  m = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(__fsub_rn(1.0f, b1), g));
+  v = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+  const float mh = __fdiv_rn(m, bc1);
+  const float vh = __fdiv_rn(v, bc2);
+  if (decay > 0.0f) p = __fsub_rn(p, __fmul_rn(__fmul_rn(lr, decay), p));
+  p = __fsub_rn(p, __fdiv_rn(__fmul_rn(lr, mh), __fadd_rn(__fsqrt_rn(vh), eps)));
+}
+
+__global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __restrict__ P,
+                                               const float* __restrict__ G, float* __restrict__ M,
+                                               float* __restrict__ V, float lr, float b1, float b2,
+                                               float eps, float bc1, float bc2) {
+  const AdamChunk ch = tab.c[blockIdx.x];
+  const int64_t s = ch.start;
+  const int n = ch.len;
+  // Scalar head up to a 16-byte boundary, float4 body, scalar tail.
+  const int head = min(n, (int)((4 - (s & 3)) & 3));
+  for (int i = threadIdx.x; i < head; i += blockDim.x) {
+    float p = P[s + i], m = M[s + i], v = V[s + i];
+    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    P[s + i] = p; M[s + i] = m; V[s + i] = v;
+  }
+  const int body4 = (n - head) >> 2;
+  float4* P4 = reinterpret_cast<float4*>(P + s + head);
+  const float4* G4 = reinterpret_cast<const float4*>(G + s + head);
+  float4* M4 = reinterpret_cast<float4*>(M + s + head);
+  float4* V4 = reinterpret_cast<float4*>(V + s + head);
+  for (int i = threadIdx.x; i < body4; i += blockDim.x) {
+    float4 p = P4[i], m = M4[i], v = V4[i];
+    const float4 g = G4[i];
+    adam_one(p.x, g.x, m.x, v.x, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p.y, g.y, m.y, v.y, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p.z, g.z, m.z, v.z, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p.w, g.w, m.w, v.w, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    P4[i] = p; M4[i] = m; V4[i] = v;
+  }
+  for (int i = head + body4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+    float p = P[s + i], m = M[s + i], v = V[s + i];
+    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    P[s + i] = p; M[s + i] = m; V[s + i] = v;
+  }
+}
+
+}  // namespace
+}  // namespace nsb
+
+using namespace nsb;
+
+extern "C" ns_status ns_adamw_flat(float* params, const float* grads, float* m, float* v,
+                                   int64_t n_total, const int64_t* host_seg_offsets,
+                                   const float* host_seg_decay, int n_seg, float lr, float b1,
+                                   float b2, float eps, float bc1, float bc2, void* stream) {
+  NS_REQUIRE(n_seg >= 0 && host_seg_offsets && (n_seg == 0 || host_seg_decay),
+             "ns_adamw_flat: bad segment table");
+  NS_REQUIRE(((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(grads) |
+               reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15) == 0,
+             "ns_adamw_flat: buffers must be 16-byte aligned");
+  NS_REQUIRE(host_seg_offsets[0] >= 0 && host_seg_offsets[n_seg] <= n_total,
+             "ns_adamw_flat: segments exceed the buffer");
+  cudaStream_t s = as_stream(stream);
+  AdamTable tab;
+  int used = 0;
+  auto flush = [&]() -> ns_status {
+    if (used == 0) return NS_OK;
+    adamw_k<<<used, 256, 0, s>>>(tab, params, grads, m, v, lr, b1, b2, eps, bc1, bc2);
+    used = 0;
+    return check_launch("ns_adamw_flat");
+  };
+  for (int t = 0; t < n_seg; ++t) {
+    const int64_t a = host_seg_offsets[t], b = host_seg_offsets[t + 1];
+    NS_REQUIRE(b >= a, "ns_adamw_flat: segment offsets must be ascending");
+    for (int64_t st = a; st < b; st += kChunk) {
+      tab.c[used].start = st;
+      tab.c[used].len = (int32_t)std::min<int64_t>(kChunk, b - st);
+      tab.c[used].decay = host_seg_decay[t];
+      if (++used == kMaxChunks) {
+        ns_status rc = flush();
+        if (rc != NS_OK) return rc;
+      }
+    }
+  }
+  return flush();
+}

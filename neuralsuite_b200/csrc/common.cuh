@@ -1,0 +1,83 @@
+// Shared helpers for the sm_100a kernels and the C ABI: status plumbing,
+// launch checks and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "ns_b200.h"
+
+namespace nsb {
+
+// Thread-local last-error string behind ns_last_error().
+void set_error(const std::string& msg);
+ns_status fail(ns_status code, const std::string& msg);
+ns_status cuda_fail(cudaError_t err, const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Checks the launch that was just issued.
+inline ns_status check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return NS_OK;
+}
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int sm_count();  // multiprocessors of the current device (cached per device)
+
+}  // namespace nsb
+
+#define NS_TRY_CUDA(call, what)                          \
+  do {                                                   \
+    cudaError_t _e = (call);                             \
+    if (_e != cudaSuccess) return nsb::cuda_fail(_e, what); \
+  } while (0)
+
+#define NS_REQUIRE(cond, msg) \
+  do {                        \
+    if (!(cond)) return nsb::fail(NS_ERR_INVALID_ARGUMENT, msg); \
+  } while (0)
+
+// ----------------------------------------------------------------- device side
+namespace nsb {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// The reference's tanh GELU and its derivative (src/tensor.cpp:436-458), with
+// the products written as separate IEEE multiplies and adds (no FMA
+// contraction) to stay as close to the reference's arithmetic as the device
+// tanhf allows.
+__device__ __forceinline__ float gelu_f(float x) {
+  const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  const float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, cube));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ float gelu_grad_f(float x) {
+  const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  const float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, cube));
+  const float th = tanhf(inner);
+  const float d_inner =
+      __fmul_rn(0.7978845608f, __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f * 0.044715f, x), x)));
+  const float a = __fmul_rn(0.5f, __fadd_rn(1.0f, th));
+  const float b = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, x), __fsub_rn(1.0f, __fmul_rn(th, th))),
+                            d_inner);
+  return __fadd_rn(a, b);
+}
+
+}  // namespace nsb

@@ -1,0 +1,144 @@
+// K1 dispatcher: ns_gemm routes to the tcgen05 3xTF32 kernel whenever the
+// operands can be described to TMA (row pitches and base addresses 16-byte
+// aligned), and to a plain fp32 SIMT kernel otherwise (ragged pitches such as
+// the reference's odd test shapes).  Both run on the GPU; there is no host
+// fallback.
+#include <algorithm>
+
+#include "epilogue.cuh"
+#include "gemm_tc.cuh"
+
+namespace nsb {
+namespace {
+
+thread_local int t_engine = 0;  // 0 auto, 1 SIMT
+
+constexpr int kSB = 64, kSK = 16;
+
+// SIMT fp32 GEMM: 64x64 tile, 256 threads, 4x4 outputs per thread, any
+// transpose flags, any pitches.  C = op(A) op(B), epilogue applied per element.
+template <bool AT, bool BT>
+__global__ void __launch_bounds__(256) gemm_simt_k(int M, int N, int K, const float* __restrict__ A,
+                                                   int lda, const float* __restrict__ B, int ldb,
+                                                   EpiArgs e) {
+  __shared__ float As[kSK][kSB + 4];
+  __shared__ float Bs[kSK][kSB + 4];
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int m0 = blockIdx.y * kSB, n0 = blockIdx.x * kSB;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += kSK) {
+    for (int i = tid; i < kSB * kSK; i += 256) {
+      int mm, kk;
+      if (AT) { kk = i / kSB; mm = i % kSB; } else { mm = i / kSK; kk = i % kSK; }
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? (AT ? A[(size_t)k * lda + m] : A[(size_t)m * lda + k]) : 0.f;
+      int nn, kb;
+      if (BT) { nn = i / kSK; kb = i % kSK; } else { kb = i / kSB; nn = i % kSB; }
+      const int n = n0 + nn, k2 = k0 + kb;
+      Bs[kb][nn] = (n < N && k2 < K) ? (BT ? B[(size_t)n * ldb + k2] : B[(size_t)k2 * ldb + n]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kSK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n < N) epi_store(e, m, n, acc[i][j]);
+    }
+  }
+}
+
+ns_status gemm_simt(int M, int N, int K, const float* A, int lda, int at, const float* B, int ldb,
+                    int bt, const EpiArgs& e, cudaStream_t s) {
+  const dim3 grid(ceil_div(N, kSB), ceil_div(M, kSB)), block(256);
+  if (!at && !bt) gemm_simt_k<false, false><<<grid, block, 0, s>>>(M, N, K, A, lda, B, ldb, e);
+  else if (!at && bt) gemm_simt_k<false, true><<<grid, block, 0, s>>>(M, N, K, A, lda, B, ldb, e);
+  else if (at && !bt) gemm_simt_k<true, false><<<grid, block, 0, s>>>(M, N, K, A, lda, B, ldb, e);
+  else gemm_simt_k<true, true><<<grid, block, 0, s>>>(M, N, K, A, lda, B, ldb, e);
+  return check_launch("ns_gemm simt");
+}
+
+bool tma_ok(const float* p, int ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % 4 == 0 && ld > 0;
+}
+
+bool use_tc(int M, int N, int K, const float* A, int lda, const float* B, int ldb) {
+  if (t_engine == 1) return false;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (!tma_ok(A, lda) || !tma_ok(B, ldb)) return false;
+  static int supported = -1;
+  if (supported < 0) supported = ns_device_supported();
+  return supported == 1;
+}
+
+}  // namespace
+}  // namespace nsb
+
+using namespace nsb;
+
+extern "C" {
+
+size_t ns_gemm_workspace_size(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const tc::Plan p = tc::plan(M, N, K, true);
+  return tc::split_workspace_bytes(p, M, N);
+}
+
+ns_status ns_gemm_set_engine(int engine) {
+  NS_REQUIRE(engine == 0 || engine == 1, "ns_gemm_set_engine: engine must be 0 or 1");
+  t_engine = engine;
+  return NS_OK;
+}
+
+ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
+                  int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
+                  const float* bias, const float* aux, float* aux_out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(M >= 0 && N >= 0 && K >= 0, "ns_gemm: negative dimension");
+  NS_REQUIRE(epilogue >= NS_EPI_STORE && epilogue <= NS_EPI_GELU_BWD, "ns_gemm: unknown epilogue");
+  NS_REQUIRE(beta == 0.0f || beta == 1.0f, "ns_gemm: beta must be 0 or 1");
+  NS_REQUIRE(beta == 0.0f || epilogue == NS_EPI_STORE, "ns_gemm: beta=1 needs NS_EPI_STORE");
+  NS_REQUIRE(ldc >= N, "ns_gemm: ldc < N");
+  NS_REQUIRE(lda >= (a_trans ? M : K) && ldb >= (b_trans ? K : N), "ns_gemm: leading dimension too small");
+  const bool need_bias = epilogue == NS_EPI_BIAS || epilogue == NS_EPI_BIAS_GELU ||
+                         epilogue == NS_EPI_BIAS_RESID;
+  NS_REQUIRE(!need_bias || bias, "ns_gemm: epilogue needs bias");
+  NS_REQUIRE(!(epilogue == NS_EPI_BIAS_RESID || epilogue == NS_EPI_GELU_BWD) || aux,
+             "ns_gemm: epilogue needs aux");
+  NS_REQUIRE(epilogue != NS_EPI_BIAS_GELU || aux_out, "ns_gemm: epilogue needs aux_out");
+  if (M == 0 || N == 0) return NS_OK;
+  EpiArgs e{C, ldc, epilogue, beta, bias, aux, aux_out};
+  cudaStream_t s = as_stream(stream);
+  if (K == 0 || !use_tc(M, N, K, A, lda, B, ldb))
+    return gemm_simt(M, N, K, A, lda, a_trans, B, ldb, b_trans, e, s);
+  tc::Plan pl = tc::plan(M, N, K, true);
+  if (tc::split_workspace_bytes(pl, M, N) > workspace_bytes || !workspace ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+    pl = tc::plan(M, N, K, false);
+  return tc::run(pl, M, N, K, A, lda, a_trans, B, ldb, b_trans ? 0 : 1, e,
+                 static_cast<float*>(workspace), s);
+}
+
+ns_status ns_kernel_health(void) {
+  if (tc::consume_timeout_flag())
+    return fail(NS_ERR_TIMEOUT, "a tcgen05 GEMM gave up a bounded wait (see ns_gemm)");
+  return NS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,688 @@
+// K1: fp32 GEMM on the 5th-generation tensor cores, 3xTF32.
+//
+//   C = Ahi.Bhi + Ahi.Blo + Alo.Bhi,   X = Xhi + Xlo,  Xhi = tf32(X)
+//
+// One persistent CTA per SM, warp-specialised (384 threads), tile 128 x 128:
+//   warp 0      TMA producer: fp32 A/B tiles (BK = 32 = one 128-byte row) into
+//               a 3-deep ring.  K-major operands land in the 16-byte-chunk
+//               128B swizzle, MN-major operands (the transposed reads of dX and
+//               dW) in the 32-byte-chunk 128B swizzle, so the reference's
+//               Transpose copies never happen.
+//   warps 2,3,8-11  split: lo = x - trunc_tf32(x) written beside each tile
+//               (elementwise, so the same code serves every operand layout).
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::tf32
+//               (M=128, N=128, K=8) into TMEM; the tensor core reads the raw
+//               fp32 tile as its tf32 "hi" part (it ignores the 13 low
+//               mantissa bits), so the hi.hi product starts as soon as the TMA
+//               lands and only the two lo products wait for the split.
+//   warps 4-7   fold + epilogue: the tensor core accumulates with
+//               round-toward-zero, so every 2 k-blocks the MMA switches to a
+//               fresh chunk buffer and these warps add the finished chunk into
+//               the tile's running sum with round-to-nearest (TMEM ld/st);
+//               then tcgen05.ld of the sum, fused bias / GELU / residual /
+//               GELU-backward, fp32 stores.  Running sums are double buffered,
+//               so tile t+1 accumulates while tile t drains.
+// K can be split over CTAs for the small-output dW products; partial tiles go
+// to caller workspace and are summed in split order (deterministic).
+//
+// Every mbarrier wait is bounded (2 s of %globaltimer); a timeout raises a
+// device flag that ns_kernel_health() reports, and the CTA drains and exits.
+#include <algorithm>
+#include <cstring>
+
+#include "gemm_tc.cuh"
+
+namespace nsb {
+namespace tc {
+
+__device__ int g_timeout;
+
+namespace {
+
+constexpr int kThreads = 384;
+constexpr int kSplitThreads = 192;  // warps 2, 3, 8, 9, 10, 11
+constexpr int kEpiThreads = 128;    // warps 4..7 (TMEM lanes 0..127)
+constexpr unsigned long long kTimeoutNs = 2000000000ull;
+
+struct KParams {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_total, kb_per;
+  int a_mn, b_mn;
+  EpiArgs e;
+  float* ws;
+  int vec_ok;  // 16-byte vector epilogue allowed
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of `parity`; false if the CTA is aborting.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort = 1;
+        atomicExch(&g_timeout, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// Wait that ignores the abort flag (used while draining), still bounded.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try(bar, parity)) {
+    if (globaltimer() - t0 > kTimeoutNs) {
+      atomicExch(&g_timeout, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns of the accumulator.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor with the Blackwell version bits.
+// layout: 2 = 128-byte swizzle (16-byte chunks), 1 = 128-byte swizzle with
+// 32-byte chunks, the only layout the tensor core takes for MN-major 32-bit
+// operands.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+// Descriptor of MMA k-step kk (8 tf32) of an operand tile at `base`.
+// K-major: rows of 128 B (32 fp32 of K), 8-row groups 1024 B apart, 16-byte
+//          swizzle; k-steps advance 32 B inside the swizzled row.
+// MN-major: boxes of 32 (M or N) x 32 (K) fp32, 4096 B apart (LBO); K rows of
+//          128 B with 32-byte swizzle atoms, 4-row groups 512 B apart (SBO);
+//          k-steps advance 8 rows = 1024 B.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int kk) {
+  return mn_major ? smem_desc(base + kk * 1024, 4096, 512, 1u)
+                  : smem_desc(base + kk * 32, 16, 1024, 2u);
+}
+
+// Instruction descriptor: kind::tf32, fp32 accumulate, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t instr_desc(int bn, int a_mn, int b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void decode_unit(const KParams& p, int u, int& tm, int& tn, int& split,
+                                            int& kb0, int& kb1) {
+  split = u % p.splits;
+  const int t = u / p.splits;
+  tn = t % p.tiles_n;
+  tm = t / p.tiles_n;
+  kb0 = split * p.kb_per;
+  kb1 = min(p.kb_total, kb0 + p.kb_per);
+}
+
+// Accumulation chunk: the tensor core adds into its fp32 accumulator with
+// round-toward-zero, a bias that grows linearly with K (relative error ~1e-5
+// per 1000 terms).  The MMA therefore accumulates kChunk k-blocks (64 terms)
+// at a time into a fresh TMEM buffer, and the epilogue warps fold each chunk
+// into the tile's running sum with round-to-nearest adds, which bounds the
+// error at the level of a sequential fp32 loop whatever K is.
+constexpr int kChunk = 2;
+
+template <int BN, int STAGES>
+struct Layout {
+  static_assert(BN == 128, "TMEM holds 2 running sums + 2 chunk buffers of 128 columns");
+  static constexpr uint32_t kA = kBM * kBK * 4;  // 16 KB
+  static constexpr uint32_t kB = BN * kBK * 4;
+  static constexpr uint32_t kRaw = kA + kB;        // raw A | raw B
+  static constexpr uint32_t kStage = 2 * kRaw;     // then lo A | lo B
+  static constexpr uint32_t kBars = STAGES * kStage;
+  static constexpr uint32_t kNumBars = 3 * STAGES + 9;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;  // alignment slack
+  // columns [0,BN) and [BN,2BN): running sums R0, R1 (one per tile in flight);
+  // [2BN,3BN) and [3BN,4BN): chunk buffers C0, C1.
+  static constexpr uint32_t kTmemCols = 4 * BN;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  using L = Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto split_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (2 * STAGES + s); };
+  auto accf_bar = [&](int a) { return bar0 + 8u * (3 * STAGES + a); };      // running sum done
+  auto acce_bar = [&](int a) { return bar0 + 8u * (3 * STAGES + 2 + a); };  // running sum drained
+  auto chf_bar = [&](int c) { return bar0 + 8u * (3 * STAGES + 4 + c); };   // chunk written
+  auto che_bar = [&](int c) { return bar0 + 8u * (3 * STAGES + 6 + c); };   // chunk folded
+  const uint32_t drain_bar = bar0 + 8u * (3 * STAGES + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(split_bar(s), kSplitThreads);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), kEpiThreads);
+      mbar_init(chf_bar(a), 1);
+      mbar_init(che_bar(a), kEpiThreads);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int n_units = p.tiles_m * p.tiles_n * p.splits;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int issued_stage[STAGES];
+      uint32_t issued_phase[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued_stage[s] = 0, issued_phase[s] = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        int tm, tn, split, kb0, kb1;
+        decode_unit(p, u, tm, tn, split, kb0, kb1);
+        const int m0 = tm * kBM, n0 = tn * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(full_bar(s), L::kRaw);
+          issued_stage[s] = 1;
+          issued_phase[s] = ph;
+          const uint32_t a_dst = sbase + s * L::kStage;
+          const uint32_t b_dst = a_dst + L::kA;
+          const int k0 = kb * kBK;
+          if (!p.a_mn) {
+            tma_load_2d(a_dst, &tmA, full_bar(s), k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 32; ++j) tma_load_2d(a_dst + j * 4096, &tmA, full_bar(s), m0 + 32 * j, k0);
+          }
+          if (!p.b_mn) {
+            tma_load_2d(b_dst, &tmB, full_bar(s), k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_dst + j * 4096, &tmB, full_bar(s), n0 + 32 * j, k0);
+          }
+        }
+      }
+      if (!ok) {
+        // Aborting: let every copy this thread issued land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_stage[s]) mbar_wait_drain(full_bar(s), issued_phase[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(BN, p.a_mn, p.b_mn);
+      uint32_t it = 0, uit = 0, cit = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++uit) {
+        int tm, tn, split, kb0, kb1;
+        decode_unit(p, u, tm, tn, split, kb0, kb1);
+        const int r = uit & 1;
+        if (!mbar_wait(acce_bar(r), ((uit >> 1) & 1u) ^ 1u, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk) {
+          uint32_t d_tmem = tmem_base + r * BN;  // chunk 0 goes straight into the running sum
+          int cb = -1;
+          if (c0 > kb0) {
+            cb = cit & 1;
+            if (!mbar_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + (2 + cb) * BN;
+          }
+          const int c1 = min(kb1, c0 + kChunk);
+          for (int kb = c0; kb < c1; ++kb, ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1u;
+            const uint32_t a_raw = sbase + s * L::kStage;
+            const uint32_t b_raw = a_raw + L::kA;
+            const uint32_t a_lo = a_raw + L::kRaw;
+            const uint32_t b_lo = a_lo + L::kA;
+            if (!mbar_wait(full_bar(s), ph, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kBK / 8; ++kk)
+              mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                       idesc, (kb > c0 || kk > 0) ? 1u : 0u);
+            if (!mbar_wait(split_bar(s), ph, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kBK / 8; ++kk) {
+              mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
+                       idesc, 1u);
+              mma_tf32(d_tmem, operand_desc(a_lo, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                       idesc, 1u);
+            }
+            tc_commit(empty_bar(s));
+          }
+          if (!ok) break;
+          if (cb >= 0) {
+            tc_commit(chf_bar(cb));
+            ++cit;
+          }
+        }
+        if (!ok) break;
+        tc_commit(accf_bar(r));
+      }
+      if (!ok) {
+        // Aborting: wait for every MMA already issued before TMEM is freed.
+        tc_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ fold + epilogue
+    const int ew = warp - 4;  // TMEM lanes 32*ew .. 32*ew+31
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    uint32_t uit = 0, cit = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++uit) {
+      int tm, tn, split, kb0, kb1;
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+      const int r = uit & 1;
+      const uint32_t r_tmem = tmem_base + lane_off + r * BN;
+      // Fold chunks 1.. of this tile into the running sum, round to nearest.
+      for (int c0 = kb0 + kChunk; c0 < kb1; c0 += kChunk, ++cit) {
+        const int cb = cit & 1;
+        if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t c_tmem = tmem_base + lane_off + (2 + cb) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t a[32], b[32];
+          tmem_ld32(c_tmem + c * 32, a);
+          tmem_ld32(r_tmem + c * 32, b);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            b[j] = __float_as_uint(__fadd_rn(__uint_as_float(b[j]), __uint_as_float(a[j])));
+          tmem_st32(r_tmem + c * 32, b);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(che_bar(cb));
+      }
+      if (!ok) break;
+      if (!mbar_wait(accf_bar(r), (uit >> 1) & 1u, abort)) break;
+      tc_fence_after();
+      const int m = tm * kBM + ew * 32 + lane;
+      const int n_base = tn * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(r_tmem + c * 32, v);
+        const int n0 = n_base + c * 32;
+        if (m < p.M && n0 < p.N) {
+          if (p.splits > 1) {
+            float* dst = p.ws + ((size_t)split * p.M + m) * p.N + n0;
+            if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) =
+                    make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+            } else {
+              for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = __uint_as_float(v[j]);
+            }
+          } else if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              epi_store4(p.e, m, n0 + j,
+                         make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                     __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])));
+          } else {
+            for (int j = 0; j < 32 && n0 + j < p.N; ++j) epi_store(p.e, m, n0 + j, __uint_as_float(v[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce_bar(r));
+    }
+  } else {
+    // ------------------------------------------------------------ hi/lo split
+    const int tt = (warp < 4) ? (warp - 2) * 32 + lane : (warp - 6) * 32 + lane;  // 0..191
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+      int tm, tn, split, kb0, kb1;
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!mbar_wait(full_bar(s), ph, abort)) {
+          ok = false;
+          break;
+        }
+        const float4* raw = reinterpret_cast<const float4*>(smem + s * L::kStage);
+        float4* lo = reinterpret_cast<float4*>(smem + s * L::kStage + L::kRaw);
+#pragma unroll 4
+        for (int i = tt; i < (int)(L::kRaw / 16); i += kSplitThreads) {
+          const float4 x = raw[i];
+          float4 r;
+          r.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+          r.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+          r.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+          r.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+          lo[i] = r;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(split_bar(s));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols)
+                 : "memory");
+  }
+}
+
+// Ordered sum of the split-K partial tiles, then the epilogue.
+__global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M, int N,
+                                EpiArgs e, int vec) {
+  const int64_t total = (int64_t)M * N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < total; i += stride * 4) {
+      float4 a = *reinterpret_cast<const float4*>(ws + i);
+      for (int s = 1; s < splits; ++s) {
+        const float4 b = *reinterpret_cast<const float4*>(ws + (size_t)s * total + i);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+      }
+      epi_store4(e, (int)(i / N), (int)(i % N), a);
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+      float a = ws[i];
+      for (int s = 1; s < splits; ++s) a += ws[(size_t)s * total + i];
+      epi_store(e, (int)(i / N), (int)(i % N), a);
+    }
+  }
+}
+
+// ------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D fp32 map over a row-major [rows, inner] matrix with row stride ld,
+// box {32, box_rows}, out-of-bounds elements read as zero.  K-major operands
+// use the 16-byte-chunk 128B swizzle, MN-major operands the 32-byte-chunk one
+// (the two layouts the descriptors above describe).
+ns_status make_map(CUtensorMap* map, const float* ptr, int inner, int rows, int ld, int box_rows,
+                   bool mn_major) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(NS_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+  cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NS_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed");
+  return NS_OK;
+}
+
+template <int BN, int STAGES>
+ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
+                 cudaStream_t s) {
+  using L = Layout<BN, STAGES>;
+  static_assert(L::kDynSmem <= 232448, "shared memory budget");
+  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, STAGES>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
+              "ns_gemm attr");
+  gemm_tf32x3_kernel<BN, STAGES><<<pl.grid, kThreads, L::kDynSmem, s>>>(ta, tb, kp);
+  return check_launch("ns_gemm tcgen05");
+}
+
+}  // namespace
+
+Plan plan(int M, int N, int K, bool allow_split) {
+  const int sms = sm_count();
+  const int kb_total = std::max(1, ceil_div(K, kBK));
+  Plan best{};
+  double best_cost = 1e30;
+  for (int bn : {128}) {
+    const int tiles_m = ceil_div(M, kBM), tiles_n = ceil_div(N, bn);
+    const int tiles = tiles_m * tiles_n;
+    const int max_split = allow_split ? std::min(kb_total, 16) : 1;
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const int kb_per = ceil_div(kb_total, sp);
+      const int splits = ceil_div(kb_total, kb_per);
+      if (splits != sp) continue;
+      const int units = tiles * splits;
+      const int waves = ceil_div(units, sms);
+      // cycles: 12 MMAs of N=bn per k-block (bn/2 cycles each) + fixed cost per unit
+      double cost = (double)waves * ((double)kb_per * 6.0 * bn + 3000.0);
+      if (splits > 1)  // partial tiles out and back in, ~5 TB/s at ~1.9 GHz
+        cost += (double)(2 * splits + 1) * M * (double)N * 4.0 / 5e12 * 1.9e9;
+      if (cost < best_cost * 0.98) {
+        best_cost = cost;
+        best.bn = bn;
+        best.stages = 3;
+        best.tiles_m = tiles_m;
+        best.tiles_n = tiles_n;
+        best.splits = splits;
+        best.kb_total = kb_total;
+        best.kb_per = kb_per;
+        best.grid = std::min(units, sms);
+      }
+    }
+  }
+  return best;
+}
+
+size_t split_workspace_bytes(const Plan& p, int M, int N) {
+  return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
+}
+
+ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
+              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws,
+              cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  std::memset(&ta, 0, sizeof(ta));
+  std::memset(&tb, 0, sizeof(tb));
+  ns_status rc = a_mn ? make_map(&ta, A, M, K, lda, 32, true) : make_map(&ta, A, K, M, lda, kBM, false);
+  if (rc != NS_OK) return rc;
+  rc = b_mn ? make_map(&tb, B, N, K, ldb, 32, true) : make_map(&tb, B, K, N, ldb, pl.bn, false);
+  if (rc != NS_OK) return rc;
+  KParams kp;
+  kp.M = M; kp.N = N; kp.K = K;
+  kp.tiles_m = pl.tiles_m; kp.tiles_n = pl.tiles_n; kp.splits = pl.splits;
+  kp.kb_total = pl.kb_total; kp.kb_per = pl.kb_per;
+  kp.a_mn = a_mn; kp.b_mn = b_mn;
+  kp.e = e;
+  kp.ws = ws;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
+                       reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
+                       reinterpret_cast<uintptr_t>(ws);
+  kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
+  rc = launch<128, 3>(pl, ta, tb, kp, stream);
+  if (rc != NS_OK || pl.splits == 1) return rc;
+  const int64_t total = (int64_t)M * N;
+  const int vec = kp.vec_ok;
+  const int64_t work = vec ? total / 4 : total;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
+  splitk_reduce_k<<<grid, 256, 0, stream>>>(ws, pl.splits, M, N, e, vec);
+  return check_launch("ns_gemm split-K reduce");
+}
+
+int consume_timeout_flag() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int)) != cudaSuccess) return 0;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace tc
+}  // namespace nsb

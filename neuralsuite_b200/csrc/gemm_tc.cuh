@@ -1,0 +1,38 @@
+// Interface between the GEMM dispatcher and the tcgen05 kernel.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace nsb {
+namespace tc {
+
+constexpr int kBM = 128;  // MMA M (one CTA, cta_group::1)
+constexpr int kBK = 32;   // fp32 K per stage = one 128-byte swizzle row
+
+struct Plan {
+  int bn;          // 128 or 256
+  int stages;
+  int tiles_m, tiles_n;
+  int splits;      // K splits (>= 1), every split non-empty
+  int kb_total;    // ceil(K / kBK)
+  int kb_per;      // k-blocks per split
+  int grid;        // persistent CTAs
+};
+
+Plan plan(int M, int N, int K, bool allow_split);
+size_t split_workspace_bytes(const Plan& p, int M, int N);
+
+// Runs C = op(A) op(B) (+ epilogue) on the tcgen05 path.  `ws` holds the
+// split-K partial tiles when plan.splits > 1.
+ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
+              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws,
+              cudaStream_t stream);
+
+// 1 if a kernel hit a bounded-wait timeout since the last call (clears it).
+int consume_timeout_flag();
+
+}  // namespace tc
+}  // namespace nsb

@@ -1,0 +1,419 @@
+// K3: LayerNorm forward / backward and the deterministic column sums used for
+// dgamma, dbeta and the Linear bias gradient.  HBM-bound: one warp per row,
+// float4 loads, warp-shuffle reductions; column sums are two-stage (per-CTA
+// partials in caller workspace, then an ordered sum over CTAs) so every run
+// gives the same bits.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace nsb {
+namespace {
+
+constexpr int kRowsWarps = 8;          // warps per CTA in the row kernels
+constexpr int kMaxPartials = 296;      // 2 x 148 SMs: cap on stage-1 CTAs
+constexpr int kMaxVec = 8;             // float4 per lane => dim <= 1024 on the fast path
+
+// ----------------------------------------------------------- forward
+// LayerNormForward (src/tensor.cpp:290-322): mean = sum/D, var = sum((x-m)^2)/D,
+// rstd = 1/sqrt(var+eps), out = ((x-m)*rstd)*gamma + beta.
+template <int NV>
+__global__ void __launch_bounds__(256) ln_fwd_vec(const float* __restrict__ x,
+                                                  const float* __restrict__ gamma,
+                                                  const float* __restrict__ beta,
+                                                  float* __restrict__ out, float* __restrict__ mean,
+                                                  float* __restrict__ rstd, int rows, int dim,
+                                                  float eps) {
+  const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nv = dim >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+  float4 v[NV];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    v[i] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  s = warp_sum(s);
+  const float m = __fdiv_rn(s, (float)dim);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nv) {
+      const float a = v[i].x - m, b = v[i].y - m, cc = v[i].z - m, d = v[i].w - m;
+      q += (a * a + b * b) + (cc * cc + d * d);
+    }
+  }
+  q = warp_sum(q);
+  const float var = __fdiv_rn(q, (float)dim);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(var + eps));
+  if (lane == 0) {
+    mean[row] = m;
+    rstd[row] = rs;
+  }
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  float4* o4 = reinterpret_cast<float4*>(out + (size_t)row * dim);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nv) {
+      const float4 g = g4[c], bb = b4[c];
+      float4 r;
+      r.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].x, m), rs), g.x), bb.x);
+      r.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].y, m), rs), g.y), bb.y);
+      r.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].z, m), rs), g.z), bb.z);
+      r.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].w, m), rs), g.w), bb.w);
+      o4[c] = r;
+    }
+  }
+}
+
+// Any dim: strided scalar passes over the row (re-read from L1/L2).
+__global__ void __launch_bounds__(256) ln_fwd_any(const float* __restrict__ x,
+                                                  const float* __restrict__ gamma,
+                                                  const float* __restrict__ beta,
+                                                  float* __restrict__ out, float* __restrict__ mean,
+                                                  float* __restrict__ rstd, int rows, int dim,
+                                                  float eps) {
+  const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * dim;
+  float s = 0.0f;
+  for (int c = lane; c < dim; c += 32) s += xr[c];
+  s = warp_sum(s);
+  const float m = __fdiv_rn(s, (float)dim);
+  float q = 0.0f;
+  for (int c = lane; c < dim; c += 32) {
+    const float d = xr[c] - m;
+    q += d * d;
+  }
+  q = warp_sum(q);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(q, (float)dim) + eps));
+  if (lane == 0) {
+    mean[row] = m;
+    rstd[row] = rs;
+  }
+  for (int c = lane; c < dim; c += 32)
+    out[(size_t)row * dim + c] =
+        __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], m), rs), gamma[c]), beta[c]);
+}
+
+// ----------------------------------------------------------- backward
+// LayerNormBackward (src/tensor.cpp:324-359) per row:
+//   xh = (x-m)*rs, dxh = dout*gamma, s1 = sum dxh, s2 = sum dxh*xh,
+//   dx = (rs/D) * (D*dxh - s1 - xh*s2)   [+ dresid]
+// and per-CTA partial column sums of dout*xh (dgamma) and dout (dbeta).
+template <int NV>
+__global__ void __launch_bounds__(256) ln_bwd_vec(
+    const float* __restrict__ dout, const float* __restrict__ x, const float* __restrict__ gamma,
+    const float* __restrict__ mean, const float* __restrict__ rstd,
+    const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
+    float* __restrict__ part_b, int rows, int dim, int rows_per_cta) {
+  extern __shared__ float red[];  // [kRowsWarps][2][dim]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = dim >> 2;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(rows, r0 + rows_per_cta);
+  float4 pg[NV], pb[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) pg[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float fdim = (float)dim;
+  for (int row = r0 + warp; row < r1; row += kRowsWarps) {
+    const float m = mean[row], rs = rstd[row];
+    const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+    const float4* d4 = reinterpret_cast<const float4*>(dout + (size_t)row * dim);
+    float4 xh[NV], dh[NV];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + i * 32;
+      if (c < nv) {
+        const float4 xv = x4[c], dv = d4[c], g = g4[c];
+        xh[i].x = __fmul_rn(__fsub_rn(xv.x, m), rs);
+        xh[i].y = __fmul_rn(__fsub_rn(xv.y, m), rs);
+        xh[i].z = __fmul_rn(__fsub_rn(xv.z, m), rs);
+        xh[i].w = __fmul_rn(__fsub_rn(xv.w, m), rs);
+        pg[i].x += dv.x * xh[i].x; pg[i].y += dv.y * xh[i].y;
+        pg[i].z += dv.z * xh[i].z; pg[i].w += dv.w * xh[i].w;
+        pb[i].x += dv.x; pb[i].y += dv.y; pb[i].z += dv.z; pb[i].w += dv.w;
+        dh[i].x = __fmul_rn(dv.x, g.x); dh[i].y = __fmul_rn(dv.y, g.y);
+        dh[i].z = __fmul_rn(dv.z, g.z); dh[i].w = __fmul_rn(dv.w, g.w);
+        s1 += (dh[i].x + dh[i].y) + (dh[i].z + dh[i].w);
+        s2 += (dh[i].x * xh[i].x + dh[i].y * xh[i].y) + (dh[i].z * xh[i].z + dh[i].w * xh[i].w);
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float scale = __fdiv_rn(rs, fdim);
+    float4* o4 = reinterpret_cast<float4*>(dx + (size_t)row * dim);
+    const float4* r4 = dresid ? reinterpret_cast<const float4*>(dresid + (size_t)row * dim) : nullptr;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + i * 32;
+      if (c < nv) {
+        float4 o;
+        o.x = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].x), s1), __fmul_rn(xh[i].x, s2)));
+        o.y = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].y), s1), __fmul_rn(xh[i].y, s2)));
+        o.z = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].z), s1), __fmul_rn(xh[i].z, s2)));
+        o.w = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].w), s1), __fmul_rn(xh[i].w, s2)));
+        if (r4) {
+          const float4 rr = r4[c];
+          o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
+          o.z = __fadd_rn(rr.z, o.z); o.w = __fadd_rn(rr.w, o.w);
+        }
+        o4[c] = o;
+      }
+    }
+  }
+  // Fixed-order reduction of the 8 warps' column partials.
+  float* rg = red + (size_t)warp * 2 * dim;
+  float* rb = rg + dim;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nv) {
+      reinterpret_cast<float4*>(rg)[c] = pg[i];
+      reinterpret_cast<float4*>(rb)[c] = pb[i];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+    float sg = 0.f, sb = 0.f;
+    for (int w = 0; w < kRowsWarps; ++w) {
+      sg += red[(size_t)w * 2 * dim + c];
+      sb += red[(size_t)w * 2 * dim + dim + c];
+    }
+    part_g[(size_t)blockIdx.x * dim + c] = sg;
+    part_b[(size_t)blockIdx.x * dim + c] = sb;
+  }
+}
+
+__global__ void __launch_bounds__(256) ln_bwd_any(
+    const float* __restrict__ dout, const float* __restrict__ x, const float* __restrict__ gamma,
+    const float* __restrict__ mean, const float* __restrict__ rstd,
+    const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
+    float* __restrict__ part_b, int rows, int dim, int rows_per_cta) {
+  // One CTA walks its rows; each thread owns columns c = tid + k*256 for the
+  // dgamma/dbeta partials (kept in the output workspace directly).
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(rows, r0 + rows_per_cta);
+  const float fdim = (float)dim;
+  // Pass 1: dx per row, one warp per row.
+  for (int row = r0 + warp; row < r1; row += kRowsWarps) {
+    const float m = mean[row], rs = rstd[row];
+    const float* xr = x + (size_t)row * dim;
+    const float* dr = dout + (size_t)row * dim;
+    float s1 = 0.f, s2 = 0.f;
+    for (int c = lane; c < dim; c += 32) {
+      const float xh = __fmul_rn(__fsub_rn(xr[c], m), rs);
+      const float dh = __fmul_rn(dr[c], gamma[c]);
+      s1 += dh;
+      s2 += dh * xh;
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float scale = __fdiv_rn(rs, fdim);
+    for (int c = lane; c < dim; c += 32) {
+      const float xh = __fmul_rn(__fsub_rn(xr[c], m), rs);
+      const float dh = __fmul_rn(dr[c], gamma[c]);
+      float o = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh), s1), __fmul_rn(xh, s2)));
+      if (dresid) o = __fadd_rn(dresid[(size_t)row * dim + c], o);
+      dx[(size_t)row * dim + c] = o;
+    }
+  }
+  // Pass 2: column partials, rows in order.
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+    float sg = 0.f, sb = 0.f;
+    for (int row = r0; row < r1; ++row) {
+      const float d = dout[(size_t)row * dim + c];
+      const float xh = __fmul_rn(__fsub_rn(x[(size_t)row * dim + c], mean[row]), rstd[row]);
+      sg += d * xh;
+      sb += d;
+    }
+    part_g[(size_t)blockIdx.x * dim + c] = sg;
+    part_b[(size_t)blockIdx.x * dim + c] = sb;
+  }
+}
+
+// Stage 2 of every column sum: out[n] = sum over p (ascending) of part[p][n].
+__global__ void colsum_finish(const float* __restrict__ part, int n_part, int N,
+                              float* __restrict__ out) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int p = 0; p < n_part; ++p) s += part[(size_t)p * N + n];
+  out[n] = s;
+}
+
+// Stage 1 of the bias gradient: CTA (chunk) sums rows [r0, r1) of a
+// 128-column slab (lane = 4 consecutive columns, warp = rows strided by 8).
+__global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ y, int M, int N,
+                                                      int rows_per_cta, float* __restrict__ part) {
+  __shared__ float4 red[kRowsWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = (blockIdx.x * 32 + lane) * 4;
+  const int r0 = blockIdx.y * rows_per_cta;
+  const int r1 = min(M, r0 + rows_per_cta);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  const bool vec = (N & 3) == 0;
+  if (col < N) {
+    for (int r = r0 + warp; r < r1; r += kRowsWarps) {
+      const float* p = y + (size_t)r * N + col;
+      if (vec) {
+        const float4 v = *reinterpret_cast<const float4*>(p);
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      } else {
+        s.x += p[0];
+        if (col + 1 < N) s.y += p[1];
+        if (col + 2 < N) s.z += p[2];
+        if (col + 3 < N) s.w += p[3];
+      }
+    }
+  }
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && col < N) {
+    float4 t = red[0][lane];
+    for (int w = 1; w < kRowsWarps; ++w) {
+      const float4 u = red[w][lane];
+      t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+    }
+    float* o = part + (size_t)blockIdx.y * N + col;
+    o[0] = t.x;
+    if (col + 1 < N) o[1] = t.y;
+    if (col + 2 < N) o[2] = t.z;
+    if (col + 3 < N) o[3] = t.w;
+  }
+}
+
+int ln_bwd_ctas(int rows) { return std::max(1, std::min(ceil_div(rows, 4 * kRowsWarps), kMaxPartials)); }
+
+int bias_chunks(int M, int N) {
+  const int col_blocks = ceil_div(N, 128);
+  const int want = std::max(1, (2 * 148) / std::max(1, col_blocks));
+  return std::max(1, std::min(std::min(want, ceil_div(M, 64)), 64));
+}
+
+}  // namespace
+}  // namespace nsb
+
+using namespace nsb;
+
+extern "C" {
+
+ns_status ns_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* out,
+                           float* mean, float* rstd, int rows, int dim, float eps, void* stream) {
+  NS_REQUIRE(rows >= 0 && dim > 0, "ns_layernorm_fwd: rows must be >= 0 and dim > 0");
+  if (rows == 0) return NS_OK;
+  const dim3 grid(ceil_div(rows, kRowsWarps)), block(32 * kRowsWarps);
+  cudaStream_t s = as_stream(stream);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                         reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) &
+                        15) == 0;
+  if (dim % 4 == 0 && aligned && dim <= 128 * kMaxVec) {
+    const int nv = dim / 4;
+    if (nv <= 32)
+      ln_fwd_vec<1><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+    else if (nv <= 64)
+      ln_fwd_vec<2><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+    else if (nv <= 128)
+      ln_fwd_vec<4><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+    else
+      ln_fwd_vec<8><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+  } else {
+    ln_fwd_any<<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+  }
+  return check_launch("ns_layernorm_fwd");
+}
+
+size_t ns_layernorm_bwd_workspace_size(int rows, int dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  return (size_t)2 * ln_bwd_ctas(rows) * dim * sizeof(float);
+}
+
+ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma,
+                           const float* mean, const float* rstd, const float* dresid, float* dx,
+                           float* dgamma, float* dbeta, int rows, int dim, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(rows >= 0 && dim > 0, "ns_layernorm_bwd: rows must be >= 0 and dim > 0");
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    NS_TRY_CUDA(cudaMemsetAsync(dgamma, 0, sizeof(float) * dim, s), "ns_layernorm_bwd memset");
+    NS_TRY_CUDA(cudaMemsetAsync(dbeta, 0, sizeof(float) * dim, s), "ns_layernorm_bwd memset");
+    return NS_OK;
+  }
+  NS_REQUIRE(workspace_bytes >= ns_layernorm_bwd_workspace_size(rows, dim) && workspace,
+             "ns_layernorm_bwd: workspace too small");
+  const int ctas = ln_bwd_ctas(rows);
+  const int rpc = ceil_div(rows, ctas);
+  float* part_g = static_cast<float*>(workspace);
+  float* part_b = part_g + (size_t)ctas * dim;
+  const dim3 block(32 * kRowsWarps);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dout) |
+                       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
+                       reinterpret_cast<uintptr_t>(dresid);
+  if (dim % 4 == 0 && (al & 15) == 0 && dim <= 128 * kMaxVec) {
+    const int nv = dim / 4;
+    const size_t smem = (size_t)kRowsWarps * 2 * dim * sizeof(float);
+    if (nv <= 32)
+      ln_bwd_vec<1><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    else if (nv <= 64)
+      ln_bwd_vec<2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    else if (nv <= 128) {
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem), "ns_layernorm_bwd attr");
+      ln_bwd_vec<4><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    } else {
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem), "ns_layernorm_bwd attr");
+      ln_bwd_vec<8><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    }
+  } else {
+    ln_bwd_any<<<ctas, block, 0, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g, part_b,
+                                      rows, dim, rpc);
+  }
+  NS_TRY_CUDA(cudaGetLastError(), "ns_layernorm_bwd stage 1");
+  colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_g, ctas, dim, dgamma);
+  colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_b, ctas, dim, dbeta);
+  return check_launch("ns_layernorm_bwd stage 2");
+}
+
+size_t ns_bias_grad_workspace_size(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return (size_t)bias_chunks(M, N) * N * sizeof(float);
+}
+
+ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(M >= 0 && N > 0, "ns_bias_grad: bad shape");
+  cudaStream_t s = as_stream(stream);
+  if (M == 0) {
+    NS_TRY_CUDA(cudaMemsetAsync(db, 0, sizeof(float) * N, s), "ns_bias_grad memset");
+    return NS_OK;
+  }
+  NS_REQUIRE(workspace && workspace_bytes >= ns_bias_grad_workspace_size(M, N),
+             "ns_bias_grad: workspace too small");
+  NS_REQUIRE((reinterpret_cast<uintptr_t>(dY) & 15) == 0 || (N & 3) != 0,
+             "ns_bias_grad: dY must be 16-byte aligned");
+  const int chunks = bias_chunks(M, N);
+  const int rpc = ceil_div(M, chunks);
+  float* part = static_cast<float*>(workspace);
+  colsum_partial<<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part);
+  NS_TRY_CUDA(cudaGetLastError(), "ns_bias_grad stage 1");
+  colsum_finish<<<ceil_div(N, 256), 256, 0, s>>>(part, chunks, N, db);
+  return check_launch("ns_bias_grad stage 2");
+}
+
+}  // extern "C"

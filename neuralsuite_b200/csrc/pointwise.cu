@@ -1,0 +1,236 @@
+// K3: GELU, residual add, fused cross-entropy forward+backward, gradient
+// sum-of-squares and clip.  All HBM-bound; float4 grid-stride loops, one warp
+// per row for the cross-entropy, deterministic fixed-order reductions.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace nsb {
+namespace {
+
+int pointwise_grid(int64_t n4) {
+  const int64_t want = ceil_div64(n4, 256);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sm_count() * 8));
+}
+
+__global__ void gelu_fwd_k(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 v = reinterpret_cast<const float4*>(x)[i];
+    v.x = gelu_f(v.x); v.y = gelu_f(v.y); v.z = gelu_f(v.z); v.w = gelu_f(v.w);
+    reinterpret_cast<float4*>(y)[i] = v;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = gelu_f(x[i]);
+}
+
+__global__ void gelu_bwd_k(const float* __restrict__ d, const float* __restrict__ x,
+                           float* __restrict__ dx, int64_t n) {
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    const float4 g = reinterpret_cast<const float4*>(d)[i];
+    float4 o;
+    o.x = __fmul_rn(g.x, gelu_grad_f(v.x)); o.y = __fmul_rn(g.y, gelu_grad_f(v.y));
+    o.z = __fmul_rn(g.z, gelu_grad_f(v.z)); o.w = __fmul_rn(g.w, gelu_grad_f(v.w));
+    reinterpret_cast<float4*>(dx)[i] = o;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    dx[i] = __fmul_rn(d[i], gelu_grad_f(x[i]));
+}
+
+__global__ void add_k(const float* __restrict__ a, const float* __restrict__ b,
+                      float* __restrict__ o, int64_t n) {
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 u = reinterpret_cast<const float4*>(a)[i];
+    const float4 v = reinterpret_cast<const float4*>(b)[i];
+    reinterpret_cast<float4*>(o)[i] =
+        make_float4(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y), __fadd_rn(u.z, v.z), __fadd_rn(u.w, v.w));
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    o[i] = __fadd_rn(a[i], b[i]);
+}
+
+// CrossEntropyLoss (include/losses.h:34-86), one warp per row:
+//   row_loss = -((x_t - max) - log(sum exp(x - max)))
+//   dlogits  = (exp(x - max)/sum - onehot) / denom
+__global__ void __launch_bounds__(256) ce_rows_k(const float* __restrict__ logits,
+                                                 const int32_t* __restrict__ targets, int rows,
+                                                 int classes, float denom,
+                                                 float* __restrict__ dlogits,
+                                                 float* __restrict__ row_loss,
+                                                 int32_t* __restrict__ err) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* p = logits + (size_t)row * classes;
+  float* d = dlogits + (size_t)row * classes;
+  const int t = targets[row];
+  const bool bad = t < 0 || t >= classes;
+  float mx = -INFINITY;
+  for (int c = lane; c < classes; c += 32) mx = fmaxf(mx, p[c]);
+  mx = warp_max(mx);
+  float s = 0.f;
+  for (int c = lane; c < classes; c += 32) s += expf(__fsub_rn(p[c], mx));
+  s = warp_sum(s);
+  for (int c = lane; c < classes; c += 32) {
+    const float prob = __fdiv_rn(expf(__fsub_rn(p[c], mx)), s);
+    const float tv = (c == t) ? 1.0f : 0.0f;
+    d[c] = __fdiv_rn(__fsub_rn(prob, tv), denom);
+  }
+  if (lane == 0) {
+    if (bad) {
+      if (err) atomicExch(err, 1);
+      row_loss[row] = 0.0f;
+    } else {
+      row_loss[row] = -__fsub_rn(__fsub_rn(p[t], mx), logf(s));
+    }
+  }
+}
+
+// Ordered single-CTA reduction: out[0] = (sum of x[0..n)) / div.
+__global__ void __launch_bounds__(1024) sum_finish_k(const float* __restrict__ x, int64_t n,
+                                                     float div, float* __restrict__ out) {
+  __shared__ float sh[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) out[0] = __fdiv_rn(v, div);
+  }
+}
+
+// Per-CTA partial sums of squares (grid-stride, float4), one float per CTA.
+__global__ void __launch_bounds__(256) sumsq_partial_k(const float* __restrict__ x, int64_t n,
+                                                       float* __restrict__ part) {
+  __shared__ float sh[8];
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float s = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    s += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    s += x[i] * x[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += sh[w];
+    part[blockIdx.x] = t;
+  }
+}
+
+// ClipGradients' rescale (train_llm.cpp:121-128) with the norm read on device.
+__global__ void clip_scale_k(float* __restrict__ x, int64_t n, const float* __restrict__ sumsq,
+                             float max_norm) {
+  const float norm = __fsqrt_rn(sumsq[0]);
+  if (!(norm > max_norm && norm > 0.0f)) return;
+  const float scale = __fdiv_rn(max_norm, norm);
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 v = reinterpret_cast<float4*>(x)[i];
+    v.x = __fmul_rn(v.x, scale); v.y = __fmul_rn(v.y, scale);
+    v.z = __fmul_rn(v.z, scale); v.w = __fmul_rn(v.w, scale);
+    reinterpret_cast<float4*>(x)[i] = v;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    x[i] = __fmul_rn(x[i], scale);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+constexpr int kSumsqCtas = 592;  // 4 x 148
+
+}  // namespace
+}  // namespace nsb
+
+using namespace nsb;
+
+extern "C" {
+
+ns_status ns_gelu_fwd(const float* x, float* y, int64_t n, void* stream) {
+  NS_REQUIRE(n >= 0, "ns_gelu_fwd: n < 0");
+  NS_REQUIRE(al16(x) && al16(y), "ns_gelu_fwd: pointers must be 16-byte aligned");
+  if (n == 0) return NS_OK;
+  gelu_fwd_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, y, n);
+  return check_launch("ns_gelu_fwd");
+}
+
+ns_status ns_gelu_bwd(const float* dout, const float* x, float* dx, int64_t n, void* stream) {
+  NS_REQUIRE(n >= 0, "ns_gelu_bwd: n < 0");
+  NS_REQUIRE(al16(x) && al16(dout) && al16(dx), "ns_gelu_bwd: pointers must be 16-byte aligned");
+  if (n == 0) return NS_OK;
+  gelu_bwd_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(dout, x, dx, n);
+  return check_launch("ns_gelu_bwd");
+}
+
+ns_status ns_add(const float* a, const float* b, float* out, int64_t n, void* stream) {
+  NS_REQUIRE(n >= 0, "ns_add: n < 0");
+  NS_REQUIRE(al16(a) && al16(b) && al16(out), "ns_add: pointers must be 16-byte aligned");
+  if (n == 0) return NS_OK;
+  add_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(a, b, out, n);
+  return check_launch("ns_add");
+}
+
+size_t ns_cross_entropy_workspace_size(int rows, int classes) {
+  (void)classes;
+  return rows > 0 ? (size_t)rows * sizeof(float) : 0;
+}
+
+ns_status ns_cross_entropy(const float* logits, const int32_t* targets, int rows, int classes,
+                           float denom, float* loss_out, float* dlogits, int32_t* err_flag,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(rows > 0 && classes > 0, "ns_cross_entropy: rows and classes must be positive");
+  NS_REQUIRE(denom > 0.0f, "ns_cross_entropy: denom must be positive");
+  NS_REQUIRE(workspace && workspace_bytes >= ns_cross_entropy_workspace_size(rows, classes),
+             "ns_cross_entropy: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  float* row_loss = static_cast<float*>(workspace);
+  ce_rows_k<<<ceil_div(rows, 8), 256, 0, s>>>(logits, targets, rows, classes, denom, dlogits,
+                                              row_loss, err_flag);
+  NS_TRY_CUDA(cudaGetLastError(), "ns_cross_entropy rows");
+  sum_finish_k<<<1, 1024, 0, s>>>(row_loss, rows, (float)rows, loss_out);
+  return check_launch("ns_cross_entropy finish");
+}
+
+size_t ns_sumsq_workspace_size(int64_t n) {
+  (void)n;
+  return kSumsqCtas * sizeof(float);
+}
+
+ns_status ns_sumsq(const float* x, int64_t n, float* out, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  NS_REQUIRE(n >= 0, "ns_sumsq: n < 0");
+  NS_REQUIRE(al16(x), "ns_sumsq: x must be 16-byte aligned");
+  NS_REQUIRE(workspace && workspace_bytes >= ns_sumsq_workspace_size(n),
+             "ns_sumsq: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  float* part = static_cast<float*>(workspace);
+  sumsq_partial_k<<<kSumsqCtas, 256, 0, s>>>(x, n, part);
+  NS_TRY_CUDA(cudaGetLastError(), "ns_sumsq partial");
+  sum_finish_k<<<1, 1024, 0, s>>>(part, kSumsqCtas, 1.0f, out);
+  return check_launch("ns_sumsq finish");
+}
+
+ns_status ns_clip_scale(float* x, int64_t n, const float* sumsq, float max_norm, void* stream) {
+  NS_REQUIRE(n >= 0, "ns_clip_scale: n < 0");
+  NS_REQUIRE(al16(x), "ns_clip_scale: x must be 16-byte aligned");
+  if (n == 0) return NS_OK;
+  clip_scale_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, n, sumsq,
+                                                                                max_norm);
+  return check_launch("ns_clip_scale");
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+"""Tensor-level wrappers of the kernel entry points of the C ABI.
+
+Each function takes CUDA torch tensors (fp32, contiguous; int32 for token ids),
+calls exactly one ``ns_*`` entry point on the current torch stream and returns
+the outputs.  Torch is only the allocator here; every number is produced by
+libns_b200.so.  The reference function each wrapper stands for is named in its
+docstring (paths inside the NeuralSuite project).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_f32 = torch.float32
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _req(t, name, dtype=_f32):
+    if not (t.is_cuda and t.dtype == dtype and t.is_contiguous()):
+        raise ValueError(f"{name} must be a contiguous CUDA {dtype} tensor")
+
+
+def _ws(nbytes, device):
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def set_gemm_engine(engine: int) -> None:
+    """0 = automatic (tcgen05 where TMA allows), 1 = SIMT fp32 everywhere."""
+    _lib.check(_lib.load().ns_gemm_set_engine(engine))
+
+
+def kernel_health() -> None:
+    _lib.check(_lib.load().ns_kernel_health())
+
+
+def gemm(A, B, a_trans=False, b_trans=False, epilogue=_lib.EPI_STORE, bias=None, aux=None,
+         out=None, aux_out=None, beta=0.0, split=True):
+    """MatMul (src/tensor.cpp:198-271) with transposed operands read in place.
+
+    ``A`` is [M,K] (or [K,M] if a_trans), ``B`` is [K,N] (or [N,K] if b_trans).
+    """
+    lib = _lib.load()
+    _req(A, "A")
+    _req(B, "B")
+    M, K = (A.shape[1], A.shape[0]) if a_trans else (A.shape[0], A.shape[1])
+    KB, N = (B.shape[1], B.shape[0]) if b_trans else (B.shape[0], B.shape[1])
+    if K != KB:
+        raise ValueError(f"gemm: inner dimensions differ ({K} vs {KB})")
+    if out is None:
+        out = torch.empty((M, N), dtype=_f32, device=A.device)
+    if epilogue == _lib.EPI_BIAS_GELU and aux_out is None:
+        aux_out = torch.empty((M, N), dtype=_f32, device=A.device)
+    ws_bytes = lib.ns_gemm_workspace_size(M, N, K) if split else 0
+    ws = _ws(ws_bytes, A.device) if ws_bytes else None
+    _lib.check(lib.ns_gemm(M, N, K, _p(A), A.shape[1], int(a_trans), _p(B), B.shape[1],
+                           int(b_trans), _p(out), out.shape[1], float(beta), epilogue, _p(bias),
+                           _p(aux), _p(aux_out), _p(ws), ws_bytes, _stream()))
+    return (out, aux_out) if epilogue == _lib.EPI_BIAS_GELU else out
+
+
+def bias_grad(dY):
+    """db = column sums of dY (include/layers/linear.h:104-111)."""
+    lib = _lib.load()
+    _req(dY, "dY")
+    M, N = dY.shape
+    db = torch.empty(N, dtype=_f32, device=dY.device)
+    nb = lib.ns_bias_grad_workspace_size(M, N)
+    ws = _ws(nb, dY.device)
+    _lib.check(lib.ns_bias_grad(_p(dY), M, N, _p(db), _p(ws), nb, _stream()))
+    return db
+
+
+def attn_fwd(qkv, B, T, H, D):
+    """MultiHeadAttention core forward (include/layers/attention.h:364-384)."""
+    lib = _lib.load()
+    _req(qkv, "qkv")
+    out = torch.empty((B * T, H * D), dtype=_f32, device=qkv.device)
+    lse = torch.empty((B * H * T,), dtype=_f32, device=qkv.device)
+    _lib.check(lib.ns_attn_fwd(_p(qkv), B, T, H, D, _p(out), _p(lse), _stream()))
+    return out, lse
+
+
+def attn_bwd(qkv, out, dout, lse, B, T, H, D):
+    """MultiHeadAttention core backward (include/layers/attention.h:405-461)."""
+    lib = _lib.load()
+    for t, n in ((qkv, "qkv"), (out, "out"), (dout, "dout"), (lse, "lse")):
+        _req(t, n)
+    dqkv = torch.empty_like(qkv)
+    nb = lib.ns_attn_bwd_workspace_size(B, T, H, D)
+    ws = _ws(nb, qkv.device)
+    _lib.check(lib.ns_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), B, T, H, D, _p(dqkv), _p(ws),
+                               nb, _stream()))
+    return dqkv
+
+
+def layernorm_fwd(x, gamma, beta, eps=1e-5):
+    """LayerNormForward (src/tensor.cpp:290-322)."""
+    lib = _lib.load()
+    _req(x, "x")
+    D = x.shape[-1]
+    N = x.numel() // D
+    out = torch.empty_like(x)
+    mean = torch.empty(N, dtype=_f32, device=x.device)
+    rstd = torch.empty(N, dtype=_f32, device=x.device)
+    _lib.check(lib.ns_layernorm_fwd(_p(x), _p(gamma), _p(beta), _p(out), _p(mean), _p(rstd), N, D,
+                                    eps, _stream()))
+    return out, mean, rstd
+
+
+def layernorm_bwd(dout, x, gamma, mean, rstd, dresid=None):
+    """LayerNormBackward (src/tensor.cpp:324-359), plus dresid if given."""
+    lib = _lib.load()
+    _req(x, "x")
+    _req(dout, "dout")
+    D = x.shape[-1]
+    N = x.numel() // D
+    dx = torch.empty_like(x)
+    dg = torch.empty(D, dtype=_f32, device=x.device)
+    db = torch.empty(D, dtype=_f32, device=x.device)
+    nb = lib.ns_layernorm_bwd_workspace_size(N, D)
+    ws = _ws(nb, x.device)
+    _lib.check(lib.ns_layernorm_bwd(_p(dout), _p(x), _p(gamma), _p(mean), _p(rstd), _p(dresid),
+                                    _p(dx), _p(dg), _p(db), N, D, _p(ws), nb, _stream()))
+    return dx, dg, db
+
+
+def gelu_fwd(x):
+    """GeluForward (src/tensor.cpp:428-443)."""
+    _req(x, "x")
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().ns_gelu_fwd(_p(x), _p(y), x.numel(), _stream()))
+    return y
+
+
+def gelu_bwd(dout, x):
+    """GeluBackward (src/tensor.cpp:445-461)."""
+    _req(x, "x")
+    dx = torch.empty_like(x)
+    _lib.check(_lib.load().ns_gelu_bwd(_p(dout), _p(x), _p(dx), x.numel(), _stream()))
+    return dx
+
+
+def add(a, b):
+    """ElementwiseAdd (src/tensor.cpp:534-540)."""
+    out = torch.empty_like(a)
+    _lib.check(_lib.load().ns_add(_p(a), _p(b), _p(out), a.numel(), _stream()))
+    return out
+
+
+def cross_entropy(logits, targets, denom=None):
+    """CrossEntropyLoss Forward+Backward (include/losses.h:34-86).
+
+    Returns (loss tensor [1], dlogits, err flag tensor [1]).
+    """
+    lib = _lib.load()
+    _req(logits, "logits")
+    _req(targets, "targets", torch.int32)
+    N, V = logits.shape
+    loss = torch.empty(1, dtype=_f32, device=logits.device)
+    d = torch.empty_like(logits)
+    err = torch.zeros(1, dtype=torch.int32, device=logits.device)
+    nb = lib.ns_cross_entropy_workspace_size(N, V)
+    ws = _ws(nb, logits.device)
+    _lib.check(lib.ns_cross_entropy(_p(logits), _p(targets), N, V, float(denom or N), _p(loss),
+                                    _p(d), _p(err), _p(ws), nb, _stream()))
+    return loss, d, err
+
+
+def embedding_fwd(tokens, wte, wpe):
+    """Embedding::Forward for wte and wpe plus the add (include/gpt.h:197-212)."""
+    lib = _lib.load()
+    _req(tokens, "tokens", torch.int32)
+    B, T = tokens.shape
+    V, C = wte.shape
+    out = torch.empty((B, T, C), dtype=_f32, device=wte.device)
+    err = torch.zeros(1, dtype=torch.int32, device=wte.device)
+    _lib.check(lib.ns_embedding_fwd(_p(tokens), B, T, _p(wte), V, _p(wpe), wpe.shape[0], C,
+                                    _p(out), _p(err), _stream()))
+    return out, err
+
+
+def embedding_bwd(tokens, dx, vocab, block, dwte=None, dwpe=None, accumulate_wte=False):
+    """Embedding::Backward for wte and wpe (include/layers/embedding.h:61-80)."""
+    lib = _lib.load()
+    B, T = tokens.shape
+    C = dx.shape[-1]
+    if dwte is None:
+        dwte = torch.zeros((vocab, C), dtype=_f32, device=dx.device)
+    if dwpe is None:
+        dwpe = torch.empty((block, C), dtype=_f32, device=dx.device)
+    _lib.check(lib.ns_embedding_bwd(_p(tokens), B, T, _p(dx), vocab, block, C, _p(dwte),
+                                    int(accumulate_wte), _p(dwpe), _stream()))
+    return dwte, dwpe
+
+
+def adamw_flat(params, grads, m, v, seg_offsets, seg_decay, lr, b1, b2, eps, bc1, bc2):
+    """AdamW::Step (include/optimizers.h:206-234) over flat buffers."""
+    import ctypes
+
+    lib = _lib.load()
+    n_seg = len(seg_decay)
+    offs = (ctypes.c_int64 * (n_seg + 1))(*seg_offsets)
+    dec = (ctypes.c_float * max(1, n_seg))(*seg_decay)
+    _lib.check(lib.ns_adamw_flat(_p(params), _p(grads), _p(m), _p(v), params.numel(),
+                                 ctypes.cast(offs, ctypes.c_void_p), ctypes.cast(dec, ctypes.c_void_p),
+                                 n_seg, lr, b1, b2, eps, bc1, bc2, _stream()))
+
+
+def sumsq(x):
+    lib = _lib.load()
+    out = torch.empty(1, dtype=_f32, device=x.device)
+    nb = lib.ns_sumsq_workspace_size(x.numel())
+    ws = _ws(nb, x.device)
+    _lib.check(lib.ns_sumsq(_p(x), x.numel(), _p(out), _p(ws), nb, _stream()))
+    return out
+
+
+def clip_scale(x, sumsq_t, max_norm):
+    _lib.check(_lib.load().ns_clip_scale(_p(x), x.numel(), _p(sumsq_t), max_norm, _stream()))

@@ -1,0 +1,198 @@
+"""Test infrastructure: float64 numpy restatement of the GPT training step. NOT product code.
+
+Used in two ways by the tests:
+
+* as the adjudicator of float tolerances (the approach of the reference's
+  tools/parity/precision_probe.py:91-96): where the CUDA result and the fp32
+  reference differ by more than the stated tolerance, the element passes only
+  if the CUDA result is no farther from this float64 computation than the fp32
+  reference is;
+* as the checker at sizes where the fp32 C oracle would take minutes (the
+  MatMul sweep at 8192-16384 rows, attention at T=1024).
+
+Each function states the reference function it restates (paths inside the
+NeuralSuite project).  Layouts are the reference's (row-major).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+GELU_C = 0.7978845608
+GELU_A = 0.044715
+
+
+def f64(a):
+    return np.asarray(a, dtype=np.float64)
+
+
+def matmul(A, B):
+    """src/tensor.cpp:198-271 (exact product, float64 accumulation)."""
+    return f64(A) @ f64(B)
+
+
+def gelu(x):
+    """src/tensor.cpp:428-443"""
+    x = f64(x)
+    return 0.5 * x * (1.0 + np.tanh(GELU_C * (x + GELU_A * x ** 3)))
+
+
+def gelu_grad(x):
+    """src/tensor.cpp:445-461 (the derivative factor)."""
+    x = f64(x)
+    th = np.tanh(GELU_C * (x + GELU_A * x ** 3))
+    return 0.5 * (1.0 + th) + 0.5 * x * (1.0 - th * th) * GELU_C * (1.0 + 3.0 * GELU_A * x * x)
+
+
+def layernorm_fwd(x, g, b, eps=1e-5):
+    """src/tensor.cpp:290-322"""
+    x = f64(x)
+    m = x.mean(-1, keepdims=True)
+    v = ((x - m) ** 2).mean(-1, keepdims=True)
+    rs = 1.0 / np.sqrt(v + eps)
+    return (x - m) * rs * f64(g) + f64(b), m[..., 0], rs[..., 0]
+
+
+def layernorm_bwd(dout, x, g, mean, rstd):
+    """src/tensor.cpp:324-359"""
+    x, dout, g = f64(x), f64(dout), f64(g)
+    D = x.shape[-1]
+    xh = (x - f64(mean)[..., None]) * f64(rstd)[..., None]
+    dxh = dout * g
+    s1 = dxh.sum(-1, keepdims=True)
+    s2 = (dxh * xh).sum(-1, keepdims=True)
+    dx = (f64(rstd)[..., None] / D) * (D * dxh - s1 - xh * s2)
+    rows = dout.reshape(-1, D)
+    return dx, (rows * xh.reshape(-1, D)).sum(0), rows.sum(0)
+
+
+def cross_entropy(logits, targets):
+    """include/losses.h:34-86 -> (mean loss, dlogits)."""
+    z = f64(logits)
+    t = np.asarray(targets).astype(np.int64)
+    z = z - z.max(-1, keepdims=True)
+    lse = np.log(np.exp(z).sum(-1))
+    n = z.shape[0]
+    loss = float(np.mean(lse - z[np.arange(n), t]))
+    p = np.exp(z - lse[:, None])
+    p[np.arange(n), t] -= 1.0
+    return loss, p / n
+
+
+def attention_fwd(qkv, B, T, H, D):
+    """Core of MultiHeadAttention::Forward (include/layers/attention.h:364-384).
+
+    Returns out [B*T, C] and the probabilities [B, H, T, T]."""
+    C = H * D
+    x = f64(qkv).reshape(B, T, 3, H, D)
+    q = x[:, :, 0].transpose(0, 2, 1, 3)
+    k = x[:, :, 1].transpose(0, 2, 1, 3)
+    v = x[:, :, 2].transpose(0, 2, 1, 3)
+    s = (q @ k.transpose(0, 1, 3, 2)) * (1.0 / np.sqrt(D))
+    mask = np.triu(np.ones((T, T), dtype=bool), 1)
+    s = np.where(mask, -np.inf, s)
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    o = p @ v
+    return o.transpose(0, 2, 1, 3).reshape(B * T, C), p
+
+
+def attention_bwd(qkv, p, dout, B, T, H, D):
+    """Core of MultiHeadAttention::Backward (include/layers/attention.h:405-461)."""
+    C = H * D
+    x = f64(qkv).reshape(B, T, 3, H, D)
+    q = x[:, :, 0].transpose(0, 2, 1, 3)
+    k = x[:, :, 1].transpose(0, 2, 1, 3)
+    v = x[:, :, 2].transpose(0, 2, 1, 3)
+    do = f64(dout).reshape(B, T, H, D).transpose(0, 2, 1, 3)
+    scale = 1.0 / np.sqrt(D)
+    dp = do @ v.transpose(0, 1, 3, 2)
+    dv = p.transpose(0, 1, 3, 2) @ do
+    ds = p * (dp - (dp * p).sum(-1, keepdims=True)) * scale
+    dq = ds @ k
+    dk = ds.transpose(0, 1, 3, 2) @ q
+    out = np.zeros((B, T, 3, H, D))
+    out[:, :, 0] = dq.transpose(0, 2, 1, 3)
+    out[:, :, 1] = dk.transpose(0, 2, 1, 3)
+    out[:, :, 2] = dv.transpose(0, 2, 1, 3)
+    return out.reshape(B * T, 3 * C)
+
+
+def param_shapes(V, block, L, C):
+    """Registration order of GPTModel::Parameters() (include/gpt.h:143-149, 59-63)."""
+    shapes = [(V, C), (block, C)]
+    for _ in range(L):
+        shapes += [(C,), (C,), (C, 3 * C), (3 * C,), (C, C), (C,), (C,), (C,), (C, 4 * C),
+                   (4 * C,), (4 * C, C), (C,)]
+    shapes += [(C,), (C,)]
+    return shapes
+
+
+def split_params(flat, V, block, L, C):
+    out, off = [], 0
+    for s in param_shapes(V, block, L, C):
+        n = int(np.prod(s))
+        out.append(f64(flat[off:off + n]).reshape(s))
+        off += n
+    return out
+
+
+def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C):
+    """GPTModel Forward -> CrossEntropy -> Backward (include/gpt.h:192-272) in float64.
+
+    Returns (loss, logits [B,T,V], grads flat)."""
+    P = split_params(flat, V, block, L, C)
+    idx = np.asarray(idx).astype(np.int64)
+    B, T = idx.shape
+    M, D = B * T, C // H
+    wte, wpe = P[0], P[1]
+    x = (wte[idx] + wpe[np.arange(T)][None]).reshape(M, C)
+    caches = []
+    for l in range(L):
+        g1, b1, Wa, ba, Wp, bp, g2, b2, Wf, bf, Wm, bm = P[2 + 12 * l: 14 + 12 * l]
+        h1, m1, r1 = layernorm_fwd(x, g1, b1)
+        qkv = h1 @ Wa + ba
+        att, probs = attention_fwd(qkv, B, T, H, D)
+        x1 = x + (att @ Wp + bp)
+        h2, m2, r2 = layernorm_fwd(x1, g2, b2)
+        fc = h2 @ Wf + bf
+        ge = gelu(fc)
+        x2 = x1 + (ge @ Wm + bm)
+        caches.append((x, h1, m1, r1, qkv, att, probs, x1, h2, m2, r2, fc, ge))
+        x = x2
+    gf, bfn = P[-2], P[-1]
+    xf, mf, rf = layernorm_fwd(x, gf, bfn)
+    logits = xf @ wte.T
+    loss, dl = cross_entropy(logits, np.asarray(targets).reshape(-1))
+    G = [np.zeros_like(p) for p in P]
+    dx = dl @ wte
+    dwte_head = dl.T @ xf
+    dcur, G[-2], G[-1] = layernorm_bwd(dx, x, gf, mf, rf)
+    for l in reversed(range(L)):
+        g1, b1, Wa, ba, Wp, bp, g2, b2, Wf, bf, Wm, bm = P[2 + 12 * l: 14 + 12 * l]
+        xin, h1, m1, r1, qkv, att, probs, x1, h2, m2, r2, fc, ge = caches[l]
+        o = 2 + 12 * l
+        G[o + 10] = ge.T @ dcur
+        G[o + 11] = dcur.sum(0)
+        dge = (dcur @ Wm.T) * gelu_grad(fc)
+        G[o + 8] = h2.T @ dge
+        G[o + 9] = dge.sum(0)
+        dh2 = dge @ Wf.T
+        dxn2, G[o + 6], G[o + 7] = layernorm_bwd(dh2, x1, g2, m2, r2)
+        dx1 = dcur + dxn2
+        G[o + 4] = att.T @ dx1
+        G[o + 5] = dx1.sum(0)
+        datt = dx1 @ Wp.T
+        dqkv = attention_bwd(qkv, probs, datt, B, T, H, D)
+        G[o + 2] = h1.T @ dqkv
+        G[o + 3] = dqkv.sum(0)
+        dh1 = dqkv @ Wa.T
+        dxn1, G[o + 0], G[o + 1] = layernorm_bwd(dh1, xin, g1, m1, r1)
+        dcur = dx1 + dxn1
+    dwte = np.zeros_like(wte)
+    np.add.at(dwte, idx.reshape(-1), dcur)
+    G[0] = dwte + dwte_head
+    dwpe = np.zeros_like(wpe)
+    dwpe[:T] = dcur.reshape(B, T, C).sum(0)
+    G[1] = dwpe
+    return loss, logits.reshape(B, T, V), np.concatenate([g.reshape(-1) for g in G])

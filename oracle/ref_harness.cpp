@@ -1,0 +1,334 @@
+// Test infrastructure: NOT part of the product.
+//
+// A thin C ABI over the NeuralSuite reference's own C++ classes, so the tests
+// and the CPU-baseline leg of bench.py can run the reference implementation of
+// the GPT training step on identical inputs.  It is compiled (by
+// oracle/Makefile) against the reference's headers and its src/tensor.cpp +
+// src/tokenizer.cpp, with the reference's Release flags, into
+// oracle/_ref/libnsref.so.  Nothing here re-implements arithmetic: every
+// number comes from the reference's MatMul / LayerNorm* / Gelu* /
+// MultiHeadAttention / Embedding / GPTModel / CrossEntropyLoss / AdamW.
+//
+// Reference entry points wrapped (paths inside the NeuralSuite project):
+//   MatMul                  src/tensor.cpp:198-271
+//   LayerNormForward/Bwd    src/tensor.cpp:290-359
+//   GeluForward/Backward    src/tensor.cpp:428-461
+//   CausalSoftmaxForward    src/tensor.cpp:394-426
+//   CrossEntropyLoss        include/losses.h:32-91
+//   Embedding               include/layers/embedding.h:24-92
+//   MultiHeadAttention      include/layers/attention.h:330-588
+//   GPTModel                include/gpt.h:136-327
+//   AdamW                   include/optimizers.h:143-253
+//   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
+//                           function of the training program, not a library
+//                           symbol)
+//   parallel::ThreadCount   include/parallel.h:58-64
+
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gpt.h"
+#include "losses.h"
+#include "optimizers.h"
+#include "parallel.h"
+#include "tensor.h"
+
+using namespace neuralsuite;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <typename Fn>
+int Guard(Fn&& fn) {
+  try {
+    fn();
+    return 0;
+  } catch (const std::out_of_range& e) {
+    g_last_error = std::string("out_of_range: ") + e.what();
+    return 3;
+  } catch (const std::invalid_argument& e) {
+    g_last_error = std::string("invalid_argument: ") + e.what();
+    return 2;
+  } catch (const std::exception& e) {
+    g_last_error = std::string("exception: ") + e.what();
+    return 1;
+  }
+}
+
+Tensor FromHost(const float* p, std::vector<int> shape) {
+  Tensor t(shape);
+  if (t.TotalSize() > 0) std::memcpy(t.Data(), p, t.TotalSize() * sizeof(float));
+  return t;
+}
+
+void ToHost(const Tensor& t, float* p) {
+  if (p != nullptr && t.TotalSize() > 0) std::memcpy(p, t.Data(), t.TotalSize() * sizeof(float));
+}
+
+struct GptHandle {
+  GPTConfig cfg;
+  std::unique_ptr<GPTModel> model;
+  std::unique_ptr<AdamW> opt;
+  CrossEntropyLoss criterion;
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* nsref_last_error(void) { return g_last_error.c_str(); }
+
+void nsref_set_threads(int n) { parallel::ThreadCount() = n > 0 ? n : 1; }
+int nsref_threads(void) { return parallel::ThreadCount(); }
+
+int nsref_matmul(const float* A, const float* B, float* C, int M, int K, int N) {
+  return Guard([&] {
+    Tensor a = FromHost(A, {M, K});
+    Tensor b = FromHost(B, {K, N});
+    Tensor c;
+    MatMul(a, b, c);
+    ToHost(c, C);
+  });
+}
+
+int nsref_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* out,
+                        float* mean, float* rstd, int rows, int dim, float eps) {
+  return Guard([&] {
+    Tensor tx = FromHost(x, {rows, dim});
+    Tensor g = FromHost(gamma, {dim});
+    Tensor b = FromHost(beta, {dim});
+    Tensor o, m, r;
+    LayerNormForward(tx, g, b, o, m, r, eps);
+    ToHost(o, out);
+    ToHost(m, mean);
+    ToHost(r, rstd);
+  });
+}
+
+int nsref_layernorm_bwd(const float* dout, const float* x, const float* gamma, const float* mean,
+                        const float* rstd, float* dx, float* dgamma, float* dbeta, int rows,
+                        int dim) {
+  return Guard([&] {
+    Tensor td = FromHost(dout, {rows, dim});
+    Tensor tx = FromHost(x, {rows, dim});
+    Tensor g = FromHost(gamma, {dim});
+    Tensor m = FromHost(mean, {rows});
+    Tensor r = FromHost(rstd, {rows});
+    Tensor o, dg, db;
+    LayerNormBackward(td, tx, g, m, r, o, dg, db);
+    ToHost(o, dx);
+    ToHost(dg, dgamma);
+    ToHost(db, dbeta);
+  });
+}
+
+int nsref_gelu_fwd(const float* x, float* y, int n) {
+  return Guard([&] {
+    Tensor tx = FromHost(x, {n});
+    Tensor ty;
+    GeluForward(tx, ty);
+    ToHost(ty, y);
+  });
+}
+
+int nsref_gelu_bwd(const float* dout, const float* x, float* dx, int n) {
+  return Guard([&] {
+    Tensor td = FromHost(dout, {n});
+    Tensor tx = FromHost(x, {n});
+    Tensor o;
+    GeluBackward(td, tx, o);
+    ToHost(o, dx);
+  });
+}
+
+int nsref_causal_softmax(const float* in, float* out, int batch, int T) {
+  return Guard([&] {
+    Tensor ti = FromHost(in, {batch, T, T});
+    Tensor to;
+    CausalSoftmaxForward(ti, to, T);
+    ToHost(to, out);
+  });
+}
+
+// CrossEntropyLoss::Forward then ::Backward on [rows, classes] logits.
+int nsref_cross_entropy(const float* logits, const float* targets, int rows, int classes,
+                        float* loss, float* dlogits) {
+  return Guard([&] {
+    Tensor tl = FromHost(logits, {rows, classes});
+    Tensor tt = FromHost(targets, {rows});
+    CrossEntropyLoss ce;
+    *loss = ce.Forward(tl, tt);
+    Tensor d = ce.Backward();
+    ToHost(d, dlogits);
+  });
+}
+
+// Embedding::Forward followed by Embedding::Backward with `dout`.
+int nsref_embedding(const float* weight, int num, int dim, const float* idx, int batch, int T,
+                    const float* dout, float* out, float* dweight) {
+  return Guard([&] {
+    Embedding emb(num, dim);
+    std::memcpy(emb.Weight().Data(), weight, sizeof(float) * num * dim);
+    Tensor ti = FromHost(idx, {batch, T});
+    Tensor o = emb.Forward(ti);
+    ToHost(o, out);
+    if (dout != nullptr) {
+      Tensor td = FromHost(dout, {batch, T, dim});
+      emb.Backward(td);
+      ToHost(emb.WeightParam().Grad(), dweight);
+    }
+  });
+}
+
+// MultiHeadAttention::Forward + ::Backward with the given projection weights.
+// grads: c_attn.weight, c_attn.bias, c_proj.weight, c_proj.bias (registration order).
+int nsref_mha(int B, int T, int C, int H, const float* w_attn, const float* b_attn,
+              const float* w_proj, const float* b_proj, const float* x, const float* dout,
+              float* y, float* dx, float* g_w_attn, float* g_b_attn, float* g_w_proj,
+              float* g_b_proj) {
+  return Guard([&] {
+    MultiHeadAttention attn(C, H);
+    std::vector<Tensor*> p = attn.GetParameters();
+    std::memcpy(p[0]->Data(), w_attn, sizeof(float) * C * 3 * C);
+    std::memcpy(p[1]->Data(), b_attn, sizeof(float) * 3 * C);
+    std::memcpy(p[2]->Data(), w_proj, sizeof(float) * C * C);
+    std::memcpy(p[3]->Data(), b_proj, sizeof(float) * C);
+    Tensor tx = FromHost(x, {B, T, C});
+    Tensor ty = attn.Forward(tx);
+    ToHost(ty, y);
+    Tensor td = FromHost(dout, {B, T, C});
+    Tensor tdx = attn.Backward(td);
+    ToHost(tdx, dx);
+    std::vector<Tensor*> g = attn.GetGradients();
+    ToHost(*g[0], g_w_attn);
+    ToHost(*g[1], g_b_attn);
+    ToHost(*g[2], g_w_proj);
+    ToHost(*g[3], g_b_proj);
+  });
+}
+
+// ---------------------------------------------------------------- GPT model
+
+void* nsref_gpt_create(int vocab, int block, int n_layer, int n_head, int n_embd) {
+  GptHandle* h = nullptr;
+  int rc = Guard([&] {
+    auto owned = std::make_unique<GptHandle>();
+    owned->cfg.vocab_size = vocab;
+    owned->cfg.block_size = block;
+    owned->cfg.n_layer = n_layer;
+    owned->cfg.n_head = n_head;
+    owned->cfg.n_embd = n_embd;
+    owned->model = std::make_unique<GPTModel>(owned->cfg);
+    h = owned.release();
+  });
+  return rc == 0 ? h : nullptr;
+}
+
+void nsref_gpt_destroy(void* handle) { delete static_cast<GptHandle*>(handle); }
+
+int nsref_gpt_num_tensors(void* handle) {
+  return static_cast<int>(static_cast<GptHandle*>(handle)->model->Parameters().size());
+}
+
+long long nsref_gpt_tensor_numel(void* handle, int i) {
+  return static_cast<long long>(
+      static_cast<GptHandle*>(handle)->model->Parameters()[i]->TotalSize());
+}
+
+int nsref_gpt_tensor_rank(void* handle, int i) {
+  return static_cast<int>(static_cast<GptHandle*>(handle)->model->Parameters()[i]->Shape().size());
+}
+
+// Copies the registration-order parameter list into / out of one flat buffer.
+void nsref_gpt_set_params(void* handle, const float* flat) {
+  size_t off = 0;
+  for (Tensor* t : static_cast<GptHandle*>(handle)->model->GetParameters()) {
+    std::memcpy(t->Data(), flat + off, t->TotalSize() * sizeof(float));
+    off += t->TotalSize();
+  }
+}
+
+void nsref_gpt_get_params(void* handle, float* flat) {
+  size_t off = 0;
+  for (Tensor* t : static_cast<GptHandle*>(handle)->model->GetParameters()) {
+    std::memcpy(flat + off, t->Data(), t->TotalSize() * sizeof(float));
+    off += t->TotalSize();
+  }
+}
+
+void nsref_gpt_get_grads(void* handle, float* flat) {
+  size_t off = 0;
+  for (Tensor* t : static_cast<GptHandle*>(handle)->model->GetGradients()) {
+    std::memcpy(flat + off, t->Data(), t->TotalSize() * sizeof(float));
+    off += t->TotalSize();
+  }
+}
+
+// One Forward -> CrossEntropy -> Backward, the sequence of
+// tools/parity/parity_gpt.cpp:86-97 and train_llm.cpp:216-226.
+int nsref_gpt_fwd_bwd(void* handle, const float* idx, const float* targets, int B, int T,
+                      float* loss, float* logits_out) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  return Guard([&] {
+    const int V = h->cfg.vocab_size;
+    Tensor ti = FromHost(idx, {B, T});
+    Tensor tt = FromHost(targets, {B * T});
+    Tensor logits = h->model->Forward(ti);
+    ToHost(logits, logits_out);
+    Tensor logits_2d({B * T, V});
+    std::memcpy(logits_2d.Data(), logits.Data(), logits.TotalSize() * sizeof(float));
+    *loss = h->criterion.Forward(logits_2d, tt);
+    Tensor d2 = h->criterion.Backward();
+    Tensor dlogits({B, T, V});
+    std::memcpy(dlogits.Data(), d2.Data(), d2.TotalSize() * sizeof(float));
+    h->model->Backward(dlogits);
+  });
+}
+
+// Global-norm clip with the serial float sum of train_llm.cpp:112-129.
+float nsref_gpt_clip_gradients(void* handle, float max_norm) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  float total = 0.0f;
+  for (Parameter* p : h->model->Parameters()) {
+    const Tensor& g = p->Grad();
+    for (size_t i = 0; i < g.TotalSize(); ++i) total += g[i] * g[i];
+  }
+  const float norm = std::sqrt(total);
+  if (norm > max_norm && norm > 0.0f) {
+    const float scale = max_norm / norm;
+    for (Parameter* p : h->model->Parameters()) {
+      Tensor& g = p->Grad();
+      for (size_t i = 0; i < g.TotalSize(); ++i) g[i] *= scale;
+    }
+  }
+  return norm;
+}
+
+int nsref_gpt_adamw_init(void* handle, float lr, float b1, float b2, float eps, float wd) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  return Guard([&] {
+    h->opt = std::make_unique<AdamW>(h->model->Parameters(), lr, b1, b2, eps, wd);
+  });
+}
+
+void nsref_gpt_adamw_set_lr(void* handle, float lr) {
+  static_cast<GptHandle*>(handle)->opt->SetLearningRate(lr);
+}
+
+int nsref_gpt_adamw_step(void* handle) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  return Guard([&] { h->opt->Step(); });
+}
+
+int nsref_gpt_zero_grad(void* handle) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  return Guard([&] { h->model->ZeroGrad(); });
+}
+
+}  // extern "C"
