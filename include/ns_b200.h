@@ -53,6 +53,9 @@ typedef enum {
 
 NS_API const char* ns_last_error(void);
 NS_API int ns_version(void);
+/* Kernels this library has launched in this process (a host-side counter,
+ * for benchmarks that report how much of a step ran in this library). */
+NS_API long long ns_launch_count(void);
 /* 1 when the current device is an sm_100 part the tcgen05 kernels can run on. */
 NS_API int ns_device_supported(void);
 
@@ -191,6 +194,15 @@ NS_API ns_status ns_adamw_flat(float* params, const float* grads, float* m, floa
                         const int64_t* host_seg_offsets, const float* host_seg_decay, int n_seg,
                         float lr, float b1, float b2, float eps, float bc1, float bc2,
                         void* stream);
+/* The same update with its hyper-parameters in DEVICE memory, so that a step
+ * captured in a CUDA graph replays correctly: dev_hyper = float[7]
+ * {lr, b1, b2, eps, bc1, bc2, step}, step stored as int32 bits.  Each call
+ * first increments step and recomputes bc1/bc2 on the device (double pow
+ * rounded to float), then updates every segment. */
+NS_API ns_status ns_adamw_flat_device(float* params, const float* grads, float* m, float* v,
+                               int64_t n_total, const int64_t* host_seg_offsets,
+                               const float* host_seg_decay, int n_seg, float* dev_hyper,
+                               void* stream);
 /* Sum of squares of a flat gradient buffer into one device float (the norm of
  * ClipGradients, train_llm.cpp:112-121), and the in-place scale by
  * min(1, max_norm / sqrt(sumsq)) of train_llm.cpp:122-128, read on the device. */

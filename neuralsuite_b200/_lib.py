@@ -44,6 +44,7 @@ class ns_gpt_config(ctypes.Structure):
 _SIGS = {
     "ns_last_error": (ctypes.c_char_p, []),
     "ns_version": (c_int, []),
+    "ns_launch_count": (ctypes.c_longlong, []),
     "ns_device_supported": (c_int, []),
     "ns_gemm_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "ns_gemm": (c_int, [c_int, c_int, c_int, P, c_int, c_int, P, c_int, c_int, P, c_int, c_float,
@@ -67,6 +68,7 @@ _SIGS = {
     "ns_embedding_bwd": (c_int, [P, c_int, c_int, P, c_int, c_int, c_int, P, c_int, P, P]),
     "ns_adamw_flat": (c_int, [P, P, P, P, c_int64, P, P, c_int, c_float, c_float, c_float,
                               c_float, c_float, c_float, P]),
+    "ns_adamw_flat_device": (c_int, [P, P, P, P, c_int64, P, P, c_int, P, P]),
     "ns_sumsq_workspace_size": (c_size_t, [c_int64]),
     "ns_sumsq": (c_int, [P, c_int64, P, P, c_size_t, P]),
     "ns_clip_scale": (c_int, [P, c_int64, P, c_float, P]),

@@ -36,10 +36,20 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = __fsub_rn(p, __fdiv_rn(__fmul_rn(lr, mh), __fadd_rn(__fsqrt_rn(vh), eps)));
 }
 
+// Device-side hyper-parameters, so a captured step replays with the current
+// step count and learning rate: [lr, b1, b2, eps, bc1, bc2, step(as float bits)].
+struct AdamHyper {
+  const float* dev;  // nullptr: use the by-value fields
+  float lr, b1, b2, eps, bc1, bc2;
+};
+
 __global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __restrict__ P,
                                                const float* __restrict__ G, float* __restrict__ M,
-                                               float* __restrict__ V, float lr, float b1, float b2,
-                                               float eps, float bc1, float bc2) {
+                                               float* __restrict__ V, AdamHyper hp) {
+  float lr = hp.lr, b1 = hp.b1, b2 = hp.b2, eps = hp.eps, bc1 = hp.bc1, bc2 = hp.bc2;
+  if (hp.dev) {
+    lr = hp.dev[0]; b1 = hp.dev[1]; b2 = hp.dev[2]; eps = hp.dev[3]; bc1 = hp.dev[4]; bc2 = hp.dev[5];
+  }
   const AdamChunk ch = tab.c[blockIdx.x];
   const int64_t s = ch.start;
   const int n = ch.len;
@@ -71,15 +81,37 @@ __global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __res
   }
 }
 
+// Step counter + bias corrections on the device (AdamW::Step's first three
+// lines, include/optimizers.h:208-210): step += 1; bc = 1 - pow(beta, step)
+// evaluated in double and rounded to float, as std::pow(float, int) does.
+__global__ void adamw_prep_k(float* hyper) {
+  int step = __float_as_int(hyper[6]) + 1;
+  hyper[6] = __int_as_float(step);
+  hyper[4] = (float)(1.0 - pow((double)hyper[1], (double)step));
+  hyper[5] = (float)(1.0 - pow((double)hyper[2], (double)step));
+}
+
+ns_status adamw_run(float* params, const float* grads, float* m, float* v, int64_t n_total,
+                    const int64_t* host_seg_offsets, const float* host_seg_decay, int n_seg,
+                    AdamHyper hp, cudaStream_t s);
+
 }  // namespace
-}  // namespace nsb
 
-using namespace nsb;
+// Prep + update with the hyper-parameters read on the device.
+ns_status adamw_step_device(float* params, const float* grads, float* m, float* v,
+                            int64_t n_total, const int64_t* host_seg_offsets,
+                            const float* host_seg_decay, int n_seg, float* hyper,
+                            cudaStream_t s) {
+  adamw_prep_k<<<1, 1, 0, s>>>(hyper);
+  { ns_status _rc = check_launch("adamw prep"); if (_rc != NS_OK) return _rc; }
+  AdamHyper hp{hyper, 0.f, 0.f, 0.f, 0.f, 1.f, 1.f};
+  return adamw_run(params, grads, m, v, n_total, host_seg_offsets, host_seg_decay, n_seg, hp, s);
+}
 
-extern "C" ns_status ns_adamw_flat(float* params, const float* grads, float* m, float* v,
-                                   int64_t n_total, const int64_t* host_seg_offsets,
-                                   const float* host_seg_decay, int n_seg, float lr, float b1,
-                                   float b2, float eps, float bc1, float bc2, void* stream) {
+namespace {
+ns_status adamw_run(float* params, const float* grads, float* m, float* v, int64_t n_total,
+                    const int64_t* host_seg_offsets, const float* host_seg_decay, int n_seg,
+                    AdamHyper hp, cudaStream_t s) {
   NS_REQUIRE(n_seg >= 0 && host_seg_offsets && (n_seg == 0 || host_seg_decay),
              "ns_adamw_flat: bad segment table");
   NS_REQUIRE(((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(grads) |
@@ -87,12 +119,11 @@ extern "C" ns_status ns_adamw_flat(float* params, const float* grads, float* m, 
              "ns_adamw_flat: buffers must be 16-byte aligned");
   NS_REQUIRE(host_seg_offsets[0] >= 0 && host_seg_offsets[n_seg] <= n_total,
              "ns_adamw_flat: segments exceed the buffer");
-  cudaStream_t s = as_stream(stream);
   AdamTable tab;
   int used = 0;
   auto flush = [&]() -> ns_status {
     if (used == 0) return NS_OK;
-    adamw_k<<<used, 256, 0, s>>>(tab, params, grads, m, v, lr, b1, b2, eps, bc1, bc2);
+    adamw_k<<<used, 256, 0, s>>>(tab, params, grads, m, v, hp);
     used = 0;
     return check_launch("ns_adamw_flat");
   };
@@ -110,4 +141,26 @@ extern "C" ns_status ns_adamw_flat(float* params, const float* grads, float* m, 
     }
   }
   return flush();
+}
+}  // namespace
+}  // namespace nsb
+
+using namespace nsb;
+
+extern "C" ns_status ns_adamw_flat(float* params, const float* grads, float* m, float* v,
+                                   int64_t n_total, const int64_t* host_seg_offsets,
+                                   const float* host_seg_decay, int n_seg, float lr, float b1,
+                                   float b2, float eps, float bc1, float bc2, void* stream) {
+  AdamHyper hp{nullptr, lr, b1, b2, eps, bc1, bc2};
+  return adamw_run(params, grads, m, v, n_total, host_seg_offsets, host_seg_decay, n_seg, hp,
+                   as_stream(stream));
+}
+
+extern "C" ns_status ns_adamw_flat_device(float* params, const float* grads, float* m, float* v,
+                                          int64_t n_total, const int64_t* host_seg_offsets,
+                                          const float* host_seg_decay, int n_seg,
+                                          float* dev_hyper, void* stream) {
+  NS_REQUIRE(dev_hyper, "ns_adamw_flat_device: dev_hyper is NULL");
+  return adamw_step_device(params, grads, m, v, n_total, host_seg_offsets, host_seg_decay, n_seg,
+                           dev_hyper, as_stream(stream));
 }

@@ -403,7 +403,7 @@ ns_status launch_bwd(const float* qkv, const float* dout, const float* lse, cons
   const float scale = 1.0f / sqrtf((float)D);
   const dim3 grid((T + kBr - 1) / kBr, B * H);
   attn_bwd_dkdv_k<DP><<<grid, kThreads, smem, s>>>(qkv, dout, lse, delta, dqkv, T, H, D, scale);
-  NS_TRY_CUDA(cudaGetLastError(), "ns_attn_bwd dkdv");
+  { ns_status _rc = check_launch("ns_attn_bwd dkdv"); if (_rc != NS_OK) return _rc; }
   attn_bwd_dq_k<DP><<<grid, kThreads, smem, s>>>(qkv, dout, lse, delta, dqkv, T, H, D, scale);
   return check_launch("ns_attn_bwd dq");
 }
@@ -445,7 +445,7 @@ ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, con
   float* delta = static_cast<float*>(workspace);
   const int64_t n = (int64_t)B * H * T;
   attn_delta_k<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(out, dout, B, T, H, D, delta);
-  NS_TRY_CUDA(cudaGetLastError(), "ns_attn_bwd delta");
+  { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 32) return launch_bwd<32>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 64) return launch_bwd<64>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

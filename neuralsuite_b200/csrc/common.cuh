@@ -18,10 +18,14 @@ ns_status cuda_fail(cudaError_t err, const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-// Checks the launch that was just issued.
+// Kernels launched by this library in this process (host-side count).
+void count_launch();
+
+// Checks (and counts) the launch that was just issued.
 inline ns_status check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, what);
+  count_launch();
   return NS_OK;
 }
 

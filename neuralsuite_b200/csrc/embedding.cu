@@ -157,12 +157,12 @@ ns_status ns_embedding_bwd(const int32_t* tokens, int B, int T, const float* dx,
   const int rows = B * T;
   if (dwte) {
     emb_bwd_wte_k<<<vocab, kEmbThreads, 0, s>>>(tokens, rows, dx, dim, dwte, accumulate_wte);
-    NS_TRY_CUDA(cudaGetLastError(), "ns_embedding_bwd wte");
+    { ns_status _rc = check_launch("ns_embedding_bwd wte"); if (_rc != NS_OK) return _rc; }
   }
   if (dwpe) {
     const int64_t n = (int64_t)block * dim;
     emb_bwd_wpe_k<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(dx, B, T, block, dim, dwpe);
-    NS_TRY_CUDA(cudaGetLastError(), "ns_embedding_bwd wpe");
+    { ns_status _rc = check_launch("ns_embedding_bwd wpe"); if (_rc != NS_OK) return _rc; }
   }
   return NS_OK;
 }

@@ -1,0 +1,263 @@
+// Model-level C ABI: the device GPTModel + CrossEntropyLoss + AdamW of
+// gpt_device.h behind ns_gpt_*, plus the data-parallel gradient all-reduce.
+//
+// Data parallel: each process owns one GPU and a full replica.  The backward
+// hands every bucket group to a second stream as soon as its gradients are
+// final (an event recorded after the group's last kernel), and NCCL sums it
+// there while the backward of the earlier blocks continues; the compute
+// stream joins the comm stream before the optimizer.  Because the
+// cross-entropy gradient is divided by rows * world_size, the sum over ranks
+// is the gradient of the global-batch mean loss.
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <vector>
+
+#include "comm.h"
+#include "common.cuh"
+#include "gpt_device.h"
+
+using neuralsuite::cuda::AdamW;
+using neuralsuite::cuda::Bucket;
+using neuralsuite::cuda::GPTConfig;
+using neuralsuite::cuda::GPTModel;
+
+struct ns_gpt {
+  std::unique_ptr<GPTModel> model;
+  std::unique_ptr<AdamW> opt;
+  ns_comm* comm = nullptr;
+  int world = 1;
+  std::vector<Bucket> buckets;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> group_ready;
+  cudaEvent_t comm_done = nullptr;
+  cudaEvent_t step_done = nullptr;
+  float* host_small = nullptr;  // pinned: loss + error flags
+  int B = 0, T = 0;
+};
+
+namespace {
+
+template <typename Fn>
+ns_status Guard(Fn&& fn) {
+  try {
+    return fn();
+  } catch (const std::out_of_range& e) {
+    return nsb::fail(NS_ERR_OUT_OF_RANGE, e.what());
+  } catch (const std::invalid_argument& e) {
+    return nsb::fail(NS_ERR_INVALID_ARGUMENT, e.what());
+  } catch (const std::exception& e) {
+    return nsb::fail(NS_ERR_CUDA, e.what());
+  }
+}
+
+GPTConfig ToConfig(const ns_gpt_config* c) {
+  GPTConfig g;
+  g.vocab_size = c->vocab_size;
+  g.block_size = c->block_size;
+  g.n_layer = c->n_layer;
+  g.n_head = c->n_head;
+  g.n_embd = c->n_embd;
+  return g;
+}
+
+void release_comm_resources(ns_gpt* h) {
+  for (cudaEvent_t e : h->group_ready) cudaEventDestroy(e);
+  h->group_ready.clear();
+  if (h->comm_done) cudaEventDestroy(h->comm_done);
+  h->comm_done = nullptr;
+  if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
+  h->comm_stream = nullptr;
+}
+
+ns_status backward_impl(ns_gpt* h, cudaStream_t s) {
+  GPTModel& m = *h->model;
+  m.SetStream(s);
+  if (!h->comm || h->world == 1) {
+    m.Backward();
+    return NS_OK;
+  }
+  ns_status rc = NS_OK;
+  m.Backward([&](int g) {
+    if (rc != NS_OK) return;
+    cudaEvent_t ev = h->group_ready[g];
+    if (cudaEventRecord(ev, s) != cudaSuccess || cudaStreamWaitEvent(h->comm_stream, ev, 0) != cudaSuccess) {
+      rc = nsb::fail(NS_ERR_CUDA, "bucket event");
+      return;
+    }
+    for (const Bucket& b : h->buckets) {
+      if (b.group != g) continue;
+      rc = nsb::comm::allreduce(h->comm, m.Grads() + b.begin, b.end - b.begin, h->comm_stream);
+      if (rc != NS_OK) return;
+    }
+  });
+  if (rc != NS_OK) return rc;
+  // The per-rank mean losses are summed too; the host divides by world.
+  rc = nsb::comm::allreduce(h->comm, m.Small(), 1, h->comm_stream);
+  if (rc != NS_OK) return rc;
+  NS_TRY_CUDA(cudaEventRecord(h->comm_done, h->comm_stream), "comm join");
+  NS_TRY_CUDA(cudaStreamWaitEvent(s, h->comm_done, 0), "comm join");
+  return NS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+ns_status ns_gpt_create(const ns_gpt_config* cfg, ns_gpt** out) {
+  NS_REQUIRE(cfg && out, "ns_gpt_create: NULL argument");
+  return Guard([&]() -> ns_status {
+    auto h = std::make_unique<ns_gpt>();
+    h->model = std::make_unique<GPTModel>(ToConfig(cfg), cfg->max_batch);
+    NS_TRY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&h->host_small), 16 * sizeof(float)),
+                "cudaMallocHost");
+    NS_TRY_CUDA(cudaEventCreateWithFlags(&h->step_done, cudaEventDisableTiming), "event");
+    *out = h.release();
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_destroy(ns_gpt* h) {
+  if (!h) return NS_OK;
+  cudaDeviceSynchronize();
+  release_comm_resources(h);
+  if (h->step_done) cudaEventDestroy(h->step_done);
+  if (h->host_small) cudaFreeHost(h->host_small);
+  delete h;
+  return NS_OK;
+}
+
+int ns_gpt_num_tensors(const ns_gpt* h) { return (int)h->model->Ranks().size(); }
+int64_t ns_gpt_tensor_numel(const ns_gpt* h, int i) {
+  return h->model->Offsets()[i + 1] - h->model->Offsets()[i];
+}
+int ns_gpt_tensor_rank(const ns_gpt* h, int i) { return h->model->Ranks()[i]; }
+int64_t ns_gpt_tensor_offset(const ns_gpt* h, int i) { return h->model->Offsets()[i]; }
+int64_t ns_gpt_num_params(const ns_gpt* h) { return h->model->NumParams(); }
+float* ns_gpt_params(ns_gpt* h) { return h->model->Values(); }
+float* ns_gpt_grads(ns_gpt* h) { return h->model->Grads(); }
+float* ns_gpt_logits(ns_gpt* h) { return h->model->Logits().Data(); }
+float* ns_gpt_loss(ns_gpt* h) { return h->model->Small(); }
+
+ns_status ns_gpt_forward(ns_gpt* h, const int32_t* tokens, int B, int T, void* stream) {
+  return Guard([&]() -> ns_status {
+    h->model->SetStream(nsb::as_stream(stream));
+    h->model->Forward(tokens, B, T);
+    h->B = B;
+    h->T = T;
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_loss_backward(ns_gpt* h, const int32_t* targets, void* stream) {
+  return Guard([&]() -> ns_status {
+    NS_REQUIRE(h->B > 0, "ns_gpt_loss_backward: no forward pass yet");
+    h->model->SetStream(nsb::as_stream(stream));
+    h->model->LossBackward(targets, (float)((double)h->B * h->T * h->world));
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_backward(ns_gpt* h, void* stream) {
+  return Guard([&]() -> ns_status { return backward_impl(h, nsb::as_stream(stream)); });
+}
+
+ns_status ns_gpt_adamw_init(ns_gpt* h, float lr, float b1, float b2, float eps, float wd) {
+  return Guard([&]() -> ns_status {
+    h->opt = std::make_unique<AdamW>(*h->model, lr, b1, b2, eps, wd);
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_adamw_set_lr(ns_gpt* h, float lr) {
+  NS_REQUIRE(h->opt, "ns_gpt_adamw_set_lr: optimizer not initialised");
+  return Guard([&]() -> ns_status {
+    h->opt->SetLearningRate(lr);
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_adamw_step(ns_gpt* h, void* stream) {
+  NS_REQUIRE(h->opt, "ns_gpt_adamw_step: optimizer not initialised");
+  return Guard([&]() -> ns_status {
+    h->model->SetStream(nsb::as_stream(stream));
+    h->opt->Step();
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_clip_gradients(ns_gpt* h, float max_norm, void* stream) {
+  GPTModel& m = *h->model;
+  cudaStream_t s = nsb::as_stream(stream);
+  float* sumsq = m.Small() + 3;
+  ns_status rc = ns_sumsq(m.Grads(), m.NumParams(), sumsq, m.Ctx().scratch, m.Ctx().scratch_bytes, s);
+  if (rc != NS_OK) return rc;
+  return ns_clip_scale(m.Grads(), m.NumParams(), sumsq, max_norm, s);
+}
+
+ns_status ns_gpt_train_step(ns_gpt* h, const int32_t* tokens, const int32_t* targets, int B, int T,
+                            float max_norm, float* host_loss, void* stream) {
+  NS_REQUIRE(h->opt, "ns_gpt_train_step: call ns_gpt_adamw_init first");
+  cudaStream_t s = nsb::as_stream(stream);
+  ns_status rc = ns_gpt_forward(h, tokens, B, T, stream);
+  if (rc != NS_OK) return rc;
+  rc = ns_gpt_loss_backward(h, targets, stream);
+  if (rc != NS_OK) return rc;
+  rc = ns_gpt_backward(h, stream);
+  if (rc != NS_OK) return rc;
+  if (max_norm > 0.0f) {
+    rc = ns_gpt_clip_gradients(h, max_norm, stream);
+    if (rc != NS_OK) return rc;
+  }
+  rc = ns_gpt_adamw_step(h, stream);
+  if (rc != NS_OK) return rc;
+  if (host_loss) {
+    NS_TRY_CUDA(cudaMemcpyAsync(h->host_small, h->model->Small(), 4 * sizeof(float),
+                                cudaMemcpyDeviceToHost, s),
+                "loss copy");
+    NS_TRY_CUDA(cudaEventRecord(h->step_done, s), "step event");
+    rc = nsb::comm::wait_event(h->comm, h->step_done, 600.0);
+    if (rc != NS_OK) return rc;
+    int32_t tok_err, tgt_err;
+    std::memcpy(&tok_err, h->host_small + 1, 4);
+    std::memcpy(&tgt_err, h->host_small + 2, 4);
+    if (tok_err || tgt_err)
+      return nsb::fail(NS_ERR_OUT_OF_RANGE, "a token or target id is outside [0, vocab_size)");
+    *host_loss = h->host_small[0] / (float)h->world;
+  }
+  return NS_OK;
+}
+
+ns_status ns_gpt_set_comm(ns_gpt* h, ns_comm* comm, int world_size, int64_t bucket_floats) {
+  NS_REQUIRE(world_size >= 1, "ns_gpt_set_comm: world_size < 1");
+  NS_TRY_CUDA(cudaDeviceSynchronize(), "ns_gpt_set_comm sync");
+  release_comm_resources(h);
+  h->comm = comm;
+  h->world = comm ? world_size : 1;
+  if (!comm) return NS_OK;
+  h->buckets = neuralsuite::cuda::PlanBuckets(h->model->Config(), bucket_floats);
+  int groups = 0;
+  for (const Bucket& b : h->buckets) groups = std::max(groups, b.group + 1);
+  NS_TRY_CUDA(cudaStreamCreateWithFlags(&h->comm_stream, cudaStreamNonBlocking), "comm stream");
+  for (int g = 0; g < groups; ++g) {
+    cudaEvent_t e;
+    NS_TRY_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+    h->group_ready.push_back(e);
+  }
+  NS_TRY_CUDA(cudaEventCreateWithFlags(&h->comm_done, cudaEventDisableTiming), "event");
+  return NS_OK;
+}
+
+int ns_gpt_plan_buckets(const ns_gpt_config* cfg, int64_t bucket_floats, int64_t* begin,
+                        int64_t* end, int max_buckets) {
+  if (!cfg) return 0;
+  const auto b = neuralsuite::cuda::PlanBuckets(ToConfig(cfg), bucket_floats);
+  const int n = (int)b.size();
+  for (int i = 0; i < n && i < max_buckets; ++i) {
+    if (begin) begin[i] = b[i].begin;
+    if (end) end[i] = b[i].end;
+  }
+  return n;
+}
+
+}  // extern "C"

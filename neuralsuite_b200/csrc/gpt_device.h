@@ -440,5 +440,276 @@ class GPTBlock : public Layer {
   Tensor x1_, fc_pre_, gelu_;
 };
 
+// Sizes of GPTModel's parameters in registration order (include/gpt.h:143-149,
+// 59-63, layers' Register calls): wte, wpe, per block 12 tensors, ln_f 2.
+struct ParamSpec {
+  int64_t numel;
+  int rank;
+};
+inline std::vector<ParamSpec> GPTParamSpecs(const GPTConfig& c) {
+  const int64_t C = c.n_embd;
+  std::vector<ParamSpec> v = {{(int64_t)c.vocab_size * C, 2}, {(int64_t)c.block_size * C, 2}};
+  for (int l = 0; l < c.n_layer; ++l) {
+    const ParamSpec blk[12] = {{C, 1},         {C, 1},     {C * 3 * C, 2}, {3 * C, 1},
+                               {C * C, 2},     {C, 1},     {C, 1},         {C, 1},
+                               {C * 4 * C, 2}, {4 * C, 1}, {4 * C * C, 2}, {C, 1}};
+    v.insert(v.end(), blk, blk + 12);
+  }
+  v.push_back({C, 1});
+  v.push_back({C, 1});
+  return v;
+}
+
+// Gradient buckets for the data-parallel all-reduce, in launch order.  A
+// bucket can be launched once every gradient in it is final, so the natural
+// groups follow the backward order: [block L-1 .. ln_f], block L-2, ...,
+// block 0, [wte, wpe] (wte's is final only after the embedding backward).
+// Each group is cut into pieces of at most `cap` floats (0 = no cap).
+struct Bucket {
+  int64_t begin, end;
+  int group;  // index of the readiness group (0 = first launched)
+};
+inline std::vector<Bucket> PlanBuckets(const GPTConfig& c, int64_t cap) {
+  const auto specs = GPTParamSpecs(c);
+  std::vector<int64_t> off(specs.size() + 1, 0);
+  for (size_t i = 0; i < specs.size(); ++i) off[i + 1] = off[i] + specs[i].numel;
+  auto block_begin = [&](int l) { return off[2 + 12 * l]; };
+  std::vector<std::pair<int64_t, int64_t>> groups;
+  const int64_t total = off.back();
+  if (c.n_layer > 0) {
+    groups.emplace_back(block_begin(c.n_layer - 1), total);
+    for (int l = c.n_layer - 2; l >= 0; --l) groups.emplace_back(block_begin(l), block_begin(l + 1));
+    groups.emplace_back(0, block_begin(0));
+  } else {
+    groups.emplace_back(off[2], total);
+    groups.emplace_back(0, off[2]);
+  }
+  std::vector<Bucket> out;
+  for (size_t g = 0; g < groups.size(); ++g) {
+    int64_t b = groups[g].first;
+    const int64_t e = groups[g].second;
+    while (b < e) {
+      const int64_t n = (cap > 0) ? std::min<int64_t>(cap, e - b) : (e - b);
+      out.push_back({b, b + n, (int)g});
+      b += n;
+    }
+  }
+  return out;
+}
+
+// include/losses.h:32-91 on device: Forward computes the mean loss into a
+// device float and the gradient (softmax - onehot) / denom in one pass;
+// Backward returns that gradient.
+class CrossEntropyLoss {
+ public:
+  void Forward(const Tensor& logits, const int32_t* targets, float denom, float* loss_out,
+               int32_t* err_flag, Context* ctx) {
+    const int V = logits.Shape().back();
+    const int n = Rows(logits, V);
+    Tensor d = Scratch(dlogits_, n, V);
+    Check(ns_cross_entropy(logits.Data(), targets, n, V, denom, loss_out, d.Data(), err_flag,
+                           ctx->scratch, ctx->scratch_bytes, ctx->stream));
+    last_ = d;
+  }
+  Tensor Backward() { return last_; }
+
+ private:
+  Tensor dlogits_, last_;
+};
+
+// include/gpt.h:136-327.  Parameters and gradients are two flat device
+// buffers in registration order, bound into the layers' Parameter views.
+class GPTModel : public Module {
+ public:
+  GPTModel(const GPTConfig& cfg, int max_batch)
+      : config_(cfg), max_batch_(max_batch), wte_(cfg.vocab_size, cfg.n_embd),
+        wpe_(cfg.block_size, cfg.n_embd), ln_f_(cfg.n_embd) {
+    if (cfg.vocab_size <= 0 || cfg.block_size <= 0 || cfg.n_layer < 0 || cfg.n_embd <= 0 ||
+        max_batch <= 0)
+      throw std::invalid_argument("GPTModel: sizes must be positive");
+    Register(&wte_, "wte");
+    Register(&wpe_, "wpe");
+    for (int i = 0; i < cfg.n_layer; ++i) {
+      blocks_.push_back(std::make_unique<GPTBlock>(cfg));
+      Register(blocks_.back().get(), "blocks." + std::to_string(i));
+    }
+    Register(&ln_f_, "ln_f");
+    auto params = Parameters();
+    offsets_.assign(params.size() + 1, 0);
+    for (size_t i = 0; i < params.size(); ++i) {
+      offsets_[i + 1] = offsets_[i] + (int64_t)params[i]->TotalSize();
+      ranks_.push_back((int)params[i]->Shape().size());
+    }
+    // Every tensor starts on a 16-byte boundary only if the sizes allow it;
+    // the kernels check alignment and fall back to scalar paths otherwise.
+    const int64_t total = offsets_.back();
+    values_ = std::make_shared<DeviceBuffer>(total * sizeof(float));
+    grads_ = std::make_shared<DeviceBuffer>(total * sizeof(float));
+    CheckCuda(cudaMemset(grads_->get(), 0, total * sizeof(float)), "cudaMemset");
+    for (size_t i = 0; i < params.size(); ++i)
+      params[i]->Bind(Values() + offsets_[i], Grads() + offsets_[i]);
+    // One scratch area sized for the largest workspace any kernel of the step needs.
+    const int M = max_batch * cfg.block_size, C = cfg.n_embd, V = cfg.vocab_size;
+    size_t ws = 0;
+    auto gw = [&](int m, int n, int k) { ws = std::max(ws, ns_gemm_workspace_size(m, n, k)); };
+    gw(M, 3 * C, C); gw(M, C, C); gw(M, 4 * C, C); gw(M, C, 4 * C); gw(M, V, C);
+    gw(M, C, 3 * C); gw(M, C, V); gw(C, 3 * C, M); gw(C, C, M); gw(C, 4 * C, M);
+    gw(4 * C, C, M); gw(V, C, M);
+    ws = std::max(ws, ns_layernorm_bwd_workspace_size(M, C));
+    for (int n : {3 * C, C, 4 * C}) ws = std::max(ws, ns_bias_grad_workspace_size(M, n));
+    if (cfg.n_head > 0)
+      ws = std::max(ws, ns_attn_bwd_workspace_size(max_batch, cfg.block_size, cfg.n_head,
+                                                   C / cfg.n_head));
+    ws = std::max(ws, ns_cross_entropy_workspace_size(M, V));
+    ws = std::max(ws, ns_sumsq_workspace_size(total));
+    scratch_ = std::make_shared<DeviceBuffer>(std::max<size_t>(ws, 256));
+    ctx_storage_.scratch = scratch_->get();
+    ctx_storage_.scratch_bytes = scratch_->bytes();
+    SetContext(&ctx_storage_);
+    small_ = std::make_shared<DeviceBuffer>(64 * sizeof(float));
+    CheckCuda(cudaMemset(small_->get(), 0, 64 * sizeof(float)), "cudaMemset");
+    tokens_ = std::make_shared<DeviceBuffer>((size_t)M * sizeof(int32_t));
+    x0_ = Tensor::Empty({M, C});
+  }
+
+  const GPTConfig& Config() const { return config_; }
+  int MaxBatch() const { return max_batch_; }
+  float* Values() { return static_cast<float*>(values_->get()); }
+  float* Grads() { return static_cast<float*>(grads_->get()); }
+  int64_t NumParams() const { return offsets_.back(); }
+  const std::vector<int64_t>& Offsets() const { return offsets_; }
+  const std::vector<int>& Ranks() const { return ranks_; }
+  // Device scalars: [0] loss, [1] token error flag (int bits), [2] target error flag,
+  // [3] grad sum of squares, [8..15] AdamW hyper-parameters.
+  float* Small() { return static_cast<float*>(small_->get()); }
+  Tensor& Logits() { return logits_; }
+  void SetStream(cudaStream_t s) { ctx_storage_.stream = s; }
+  const Context& Ctx() const { return ctx_storage_; }
+  cudaStream_t Stream() const { return ctx_storage_.stream; }
+
+  // GPTModel::Forward (gpt.h:192-232) on device int32 tokens [B, T].
+  Tensor Forward(const int32_t* tokens, int B, int T) {
+    if (B <= 0 || B > max_batch_) throw std::invalid_argument("GPTModel::Forward: batch exceeds max_batch");
+    if (T <= 0) throw std::invalid_argument("GPTModel::Forward: empty sequence");
+    if (T > config_.block_size)
+      throw std::out_of_range("GPTModel::Forward: sequence longer than block_size");
+    B_ = B;
+    T_ = T;
+    const int M = B * T, C = config_.n_embd;
+    CheckCuda(cudaMemcpyAsync(tokens_->get(), tokens, (size_t)M * sizeof(int32_t),
+                              cudaMemcpyDeviceToDevice, Stream()),
+              "token copy");
+    Tensor x = x0_.View({B, T, C});
+    Check(ns_embedding_fwd(Tokens(), B, T, wte_.WeightParam().Value().Data(), config_.vocab_size,
+                           wpe_.WeightParam().Value().Data(), config_.block_size, C, x.Data(),
+                           reinterpret_cast<int32_t*>(Small() + 1), Stream()));
+    for (auto& blk : blocks_) x = blk->Forward(x);
+    xf_ = ln_f_.Forward(x).View({M, C});
+    // logits = x_2d . wte^T (gpt.h:226-228): wte read as a K-major operand, no transpose copy.
+    logits_ = Scratch(logits_buf_, M, config_.vocab_size);
+    Check(ns_gemm(M, config_.vocab_size, C, xf_.Data(), C, 0, wte_.WeightParam().Value().Data(), C,
+                  1, logits_.Data(), config_.vocab_size, 0.0f, NS_EPI_STORE, nullptr, nullptr,
+                  nullptr, ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
+    return logits_;
+  }
+
+  // CrossEntropyLoss on the last logits; denom = rows * world_size.
+  void LossBackward(const int32_t* targets, float denom) {
+    criterion_.Forward(logits_, targets, denom, Small(), reinterpret_cast<int32_t*>(Small() + 2),
+                       &ctx_storage_);
+  }
+
+  // GPTModel::Backward (gpt.h:234-272).  `on_group_ready(g)` is called in
+  // stream order when every gradient of bucket group g is final.
+  template <typename OnReady>
+  void Backward(OnReady&& on_group_ready) {
+    const int M = B_ * T_, C = config_.n_embd, V = config_.vocab_size;
+    Tensor dlogits = criterion_.Backward();
+    // dx = dlogits . wte  (wte read N-major in place)
+    Tensor dx = Scratch(dx_head_, M, C);
+    Check(ns_gemm(M, C, V, dlogits.Data(), V, 0, wte_.WeightParam().Value().Data(), C, 0, dx.Data(),
+                  C, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ctx_storage_.scratch,
+                  ctx_storage_.scratch_bytes, Stream()));
+    // head term of the tied wte gradient, dlogits^T . x, written first (the
+    // embedding backward adds its own sum to it at the end, gpt.h:262-269).
+    Check(ns_gemm(V, C, M, dlogits.Data(), V, 1, xf_.Data(), C, 0,
+                  wte_.WeightParam().Grad().Data(), C, 0.0f, NS_EPI_STORE, nullptr, nullptr,
+                  nullptr, ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
+    Tensor d = ln_f_.Backward(dx.View({B_, T_, C}));
+    int group = 0;
+    for (int l = (int)blocks_.size() - 1; l >= 0; --l) {
+      d = blocks_[l]->Backward(d);
+      on_group_ready(group++);
+    }
+    if (blocks_.empty()) on_group_ready(group++);
+    Check(ns_embedding_bwd(Tokens(), B_, T_, d.Data(), V, config_.block_size, C,
+                           wte_.WeightParam().Grad().Data(), 1, wpe_.WeightParam().Grad().Data(),
+                           Stream()));
+    on_group_ready(group++);
+  }
+  void Backward() {
+    Backward([](int) {});
+  }
+
+  int32_t* Tokens() { return static_cast<int32_t*>(tokens_->get()); }
+
+ private:
+  GPTConfig config_;
+  int max_batch_;
+  Embedding wte_, wpe_;
+  std::vector<std::unique_ptr<GPTBlock>> blocks_;
+  LayerNormLayer ln_f_;
+  CrossEntropyLoss criterion_;
+  std::vector<int64_t> offsets_;
+  std::vector<int> ranks_;
+  std::shared_ptr<DeviceBuffer> values_, grads_, scratch_, small_, tokens_;
+  Context ctx_storage_;
+  Tensor x0_, xf_, logits_, logits_buf_, dx_head_;
+  int B_ = 0, T_ = 0;
+};
+
+// include/optimizers.h:143-253 over the model's flat buffers: one launch per
+// step, decay wd on rank >= 2 tensors (the reference's heuristic without
+// parameter groups), hyper-parameters in device memory.
+class AdamW {
+ public:
+  AdamW(GPTModel& model, float lr = 1e-3f, float b1 = 0.9f, float b2 = 0.95f, float eps = 1e-8f,
+        float wd = 0.01f)
+      : model_(model) {
+    const int64_t n = model.NumParams();
+    m_ = std::make_shared<DeviceBuffer>(n * sizeof(float));
+    v_ = std::make_shared<DeviceBuffer>(n * sizeof(float));
+    CheckCuda(cudaMemset(m_->get(), 0, n * sizeof(float)), "cudaMemset");
+    CheckCuda(cudaMemset(v_->get(), 0, n * sizeof(float)), "cudaMemset");
+    for (int r : model.Ranks()) decay_.push_back(r >= 2 ? wd : 0.0f);
+    const float h[7] = {lr, b1, b2, eps, 1.0f, 1.0f, 0.0f};
+    CheckCuda(cudaMemcpy(Hyper(), h, sizeof(h), cudaMemcpyHostToDevice), "cudaMemcpy");
+  }
+  void SetLearningRate(float lr) {
+    lr_host_ = lr;
+    CheckCuda(cudaMemcpyAsync(Hyper(), &lr_host_, sizeof(float), cudaMemcpyHostToDevice,
+                              model_.Stream()),
+              "cudaMemcpyAsync");
+    CheckCuda(cudaStreamSynchronize(model_.Stream()), "cudaStreamSynchronize");
+  }
+  void Step() {
+    Check(ns_adamw_flat_device(model_.Values(), model_.Grads(), static_cast<float*>(m_->get()),
+                               static_cast<float*>(v_->get()), model_.NumParams(),
+                               model_.Offsets().data(), decay_.data(), (int)decay_.size(), Hyper(),
+                               model_.Stream()));
+  }
+  void ZeroGrad() {
+    CheckCuda(cudaMemsetAsync(model_.Grads(), 0, model_.NumParams() * sizeof(float), model_.Stream()),
+              "cudaMemsetAsync");
+  }
+  float* Hyper() { return model_.Small() + 8; }
+
+ private:
+  GPTModel& model_;
+  std::shared_ptr<DeviceBuffer> m_, v_;
+  std::vector<float> decay_;
+  float lr_host_ = 0.0f;
+};
+
 }  // namespace cuda
 }  // namespace neuralsuite

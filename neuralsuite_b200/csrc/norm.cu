@@ -384,7 +384,7 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
     ln_bwd_any<<<ctas, block, 0, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g, part_b,
                                       rows, dim, rpc);
   }
-  NS_TRY_CUDA(cudaGetLastError(), "ns_layernorm_bwd stage 1");
+  { ns_status _rc = check_launch("ns_layernorm_bwd stage 1"); if (_rc != NS_OK) return _rc; }
   colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_g, ctas, dim, dgamma);
   colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_b, ctas, dim, dbeta);
   return check_launch("ns_layernorm_bwd stage 2");
@@ -411,7 +411,7 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
   colsum_partial<<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part);
-  NS_TRY_CUDA(cudaGetLastError(), "ns_bias_grad stage 1");
+  { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
   colsum_finish<<<ceil_div(N, 256), 256, 0, s>>>(part, chunks, N, db);
   return check_launch("ns_bias_grad stage 2");
 }

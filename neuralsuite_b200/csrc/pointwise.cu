@@ -200,7 +200,7 @@ ns_status ns_cross_entropy(const float* logits, const int32_t* targets, int rows
   float* row_loss = static_cast<float*>(workspace);
   ce_rows_k<<<ceil_div(rows, 8), 256, 0, s>>>(logits, targets, rows, classes, denom, dlogits,
                                               row_loss, err_flag);
-  NS_TRY_CUDA(cudaGetLastError(), "ns_cross_entropy rows");
+  { ns_status _rc = check_launch("ns_cross_entropy rows"); if (_rc != NS_OK) return _rc; }
   sum_finish_k<<<1, 1024, 0, s>>>(row_loss, rows, (float)rows, loss_out);
   return check_launch("ns_cross_entropy finish");
 }
@@ -219,7 +219,7 @@ ns_status ns_sumsq(const float* x, int64_t n, float* out, void* workspace, size_
   cudaStream_t s = as_stream(stream);
   float* part = static_cast<float*>(workspace);
   sumsq_partial_k<<<kSumsqCtas, 256, 0, s>>>(x, n, part);
-  NS_TRY_CUDA(cudaGetLastError(), "ns_sumsq partial");
+  { ns_status _rc = check_launch("ns_sumsq partial"); if (_rc != NS_OK) return _rc; }
   sum_finish_k<<<1, 1024, 0, s>>>(part, kSumsqCtas, 1.0f, out);
   return check_launch("ns_sumsq finish");
 }

@@ -1,4 +1,5 @@
 // Status plumbing of the C ABI: thread-local last error, device queries.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -10,6 +11,12 @@ namespace nsb {
 namespace {
 thread_local std::string t_last_error;
 }
+
+namespace {
+std::atomic<long long> g_launches{0};
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
@@ -44,6 +51,8 @@ extern "C" {
 const char* ns_last_error(void) { return nsb::t_last_error.c_str(); }
 
 int ns_version(void) { return 1; }
+
+long long ns_launch_count(void) { return nsb::g_launches.load(std::memory_order_relaxed); }
 
 int ns_device_supported(void) {
   int dev = 0;

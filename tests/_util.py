@@ -65,20 +65,11 @@ def rel_l2(x, ref):
 
 
 def gpt_init(shapes, r, std=0.02, ln_noise=0.0):
-    """Reference initialisation: N(0, std) for matrices (wte, wpe, Linear W;
-    include/layers/embedding.h:31, linear.h:51-52), LayerNorm gamma = 1 and
-    beta = 0 (layernorm.h:31-32), Linear bias = 0 (linear.h:56).  ln_noise > 0
-    perturbs the 1-D parameters so every gradient path is exercised."""
-    parts = []
+    """Reference initialisation (see neuralsuite_b200.model.init_params) for a
+    shape list from param_shapes()."""
+    from neuralsuite_b200.model import GPTConfig, init_params
+
+    V, C = shapes[0]
+    block = shapes[1][0]
     L = (len(shapes) - 4) // 12
-    for i, s in enumerate(shapes):
-        n = int(np.prod(s))
-        if len(s) == 2:
-            parts.append(normal(r, n, std))
-        else:
-            is_gamma = (i >= 2 and i < 2 + 12 * L and (i - 2) % 12 in (0, 6)) or i == len(shapes) - 2
-            base = np.ones(n, np.float32) if is_gamma else np.zeros(n, np.float32)
-            if ln_noise:
-                base = base + normal(r, n, ln_noise)
-            parts.append(base.astype(np.float32))
-    return np.concatenate(parts).astype(np.float32)
+    return init_params(GPTConfig(V, block, L, 1, C), r, std, ln_noise)

@@ -73,10 +73,12 @@ FULL = [(8192, 768, 3072), (8192, 3072, 768), (16384, 1024, 4096)]
 @pytest.mark.slow
 @pytest.mark.parametrize("M,K,N", FULL)
 def test_gemm_sweep_full(cuda, M, K, N):
-    """The MatMul sweep shapes: every form against float64 (relative L2 error
-    <= 1e-5, the reference's own bar for its fast-vs-literal attention,
-    test_suite.cpp:3148-3150) and per element within 1e-4 relative of the
-    float64 value where |value| >= 1e-2 * rms."""
+    """The MatMul sweep shapes: every form against float64.  Relative L2
+    error <= 5e-6 (the reference's own bar for its fast-vs-literal attention
+    is 1e-5, test_suite.cpp:3148-3150; an fp32 k-sequential loop lands near
+    1e-6 here) and, per element, within 1e-4 relative of the float64 value
+    wherever |value| >= 0.1 * rms (smaller values carry the same absolute
+    rounding as any fp32 accumulation of K products)."""
     r = rng(M + K + N)
     X, W, dY = normal(r, (M, K)), normal(r, (K, N)), normal(r, (M, N))
     Xd, Wd, dYd = dev(X, cuda), dev(W, cuda), dev(dY, cuda)
@@ -89,10 +91,10 @@ def test_gemm_sweep_full(cuda, M, K, N):
         t = ref()
         e = rel_l2(g, t)
         rms = np.sqrt(np.mean(t * t))
-        big = np.abs(t) >= 1e-2 * rms
+        big = np.abs(t) >= 0.1 * rms
         worst = float((np.abs(g - t)[big] / np.abs(t[big])).max())
-        print(f"{name} {M}x{K}x{N}: relL2 {e:.2e} worst rel (|ref|>=1e-2 rms) {worst:.2e}")
-        assert e < 1e-5, (name, e)
+        print(f"{name} {M}x{K}x{N}: relL2 {e:.2e} worst rel (|ref|>=0.1 rms) {worst:.2e}")
+        assert e < 5e-6, (name, e)
         assert worst < 1e-4, (name, worst)
         del g, t
     nk.kernel_health()
