@@ -161,6 +161,24 @@ NS_API size_t ns_cross_entropy_workspace_size(int rows, int classes);
 NS_API ns_status ns_cross_entropy(const float* logits, const int32_t* targets, int rows, int classes,
                            float denom, float* loss_out, float* dlogits, int32_t* err_flag,
                            void* workspace, size_t workspace_bytes, void* stream);
+/* No counterpart in the reference: the same cross-entropy forward+backward
+ * for callers that cannot allocate device memory when they call it -- code
+ * recording a CUDA graph (cudaMalloc may not be called while a stream is
+ * being captured), hosts whose device memory is fully owned by another
+ * allocator, and loops that cannot afford cudaMalloc's implicit device
+ * synchronisation.  The per-row loss scratch is a static device array inside
+ * the library (NS_CE_NOALLOC_MAX_ROWS floats = 256 KiB, held by every GPU
+ * that loads the library until the process exits), so nothing is allocated
+ * and no workspace is passed.  rows > NS_CE_NOALLOC_MAX_ROWS is rejected with
+ * NS_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the one array, so calls that may
+ * overlap on the GPU (different streams without ordering) race; each call
+ * overwrites every scratch entry it reads, so no clearing is needed. */
+#define NS_CE_NOALLOC_MAX_ROWS 65536
+NS_API ns_status ns_cross_entropy_noalloc(const float* logits, const int32_t* targets, int rows,
+                                   int classes, float denom, float* loss_out, float* dlogits,
+                                   int32_t* err_flag, void* stream);
 
 /* ------------------------------------------------------------ K4 embedding
  * out[b,t,:] = wte[tok[b,t],:] + wpe[t,:]  (Embedding::Forward twice plus the

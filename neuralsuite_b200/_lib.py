@@ -64,6 +64,7 @@ _SIGS = {
     "ns_add": (c_int, [P, P, P, c_int64, P]),
     "ns_cross_entropy_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_cross_entropy": (c_int, [P, P, c_int, c_int, c_float, P, P, P, P, c_size_t, P]),
+    "ns_cross_entropy_noalloc": (c_int, [P, P, c_int, c_int, c_float, P, P, P, P]),
     "ns_embedding_fwd": (c_int, [P, c_int, c_int, P, c_int, P, c_int, c_int, P, P, P]),
     "ns_embedding_bwd": (c_int, [P, c_int, c_int, P, c_int, c_int, c_int, P, c_int, P, P]),
     "ns_adamw_flat": (c_int, [P, P, P, P, c_int64, P, P, c_int, c_float, c_float, c_float,

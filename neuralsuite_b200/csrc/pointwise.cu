@@ -2,6 +2,7 @@
 // sum-of-squares and clip.  All HBM-bound; float4 grid-stride loops, one warp
 // per row for the cross-entropy, deterministic fixed-order reductions.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -234,3 +235,59 @@ ns_status ns_clip_scale(float* x, int64_t n, const float* sumsq, float max_norm,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Allocation-free variant of ns_cross_entropy for callers that cannot call
+// cudaMalloc at the point of the call (see ns_b200.h).  Its only scratch, one
+// float of loss per row, is this file-scope device array.
+namespace nsb {
+namespace {
+
+static __device__ __align__(256) float g_ce_noalloc_rows[NS_CE_NOALLOC_MAX_ROWS];
+
+// Device address of g_ce_noalloc_rows for the current device, looked up once
+// per device with that device current.  Host code must not pass the symbol
+// itself to a kernel: on the host it names a shadow variable, not device
+// memory.
+ns_status ce_noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  NS_TRY_CUDA(cudaGetDevice(&dev), "ns_cross_entropy_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(NS_ERR_UNSUPPORTED, "ns_cross_entropy_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    NS_TRY_CUDA(cudaGetSymbolAddress(&p, g_ce_noalloc_rows),
+                "ns_cross_entropy_noalloc: cudaGetSymbolAddress");
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return NS_OK;
+}
+
+}  // namespace
+}  // namespace nsb
+
+extern "C" ns_status ns_cross_entropy_noalloc(const float* logits, const int32_t* targets,
+                                              int rows, int classes, float denom, float* loss_out,
+                                              float* dlogits, int32_t* err_flag, void* stream) {
+  NS_REQUIRE(rows > 0 && classes > 0, "ns_cross_entropy_noalloc: rows and classes must be positive");
+  NS_REQUIRE(denom > 0.0f, "ns_cross_entropy_noalloc: denom must be positive");
+  if (rows > NS_CE_NOALLOC_MAX_ROWS)
+    return fail(NS_ERR_INVALID_ARGUMENT,
+                "ns_cross_entropy_noalloc: rows = " + std::to_string(rows) +
+                    " exceeds the static scratch of NS_CE_NOALLOC_MAX_ROWS = " +
+                    std::to_string(NS_CE_NOALLOC_MAX_ROWS) +
+                    " rows; use ns_cross_entropy with a caller workspace");
+  float* row_loss = nullptr;
+  ns_status rc = ce_noalloc_scratch(&row_loss);
+  if (rc != NS_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  ce_rows_k<<<ceil_div(rows, 8), 256, 0, s>>>(logits, targets, rows, classes, denom, dlogits,
+                                              row_loss, err_flag);
+  rc = check_launch("ns_cross_entropy_noalloc rows");
+  if (rc != NS_OK) return rc;
+  sum_finish_k<<<1, 1024, 0, s>>>(row_loss, rows, (float)rows, loss_out);
+  return check_launch("ns_cross_entropy_noalloc finish");
+}
