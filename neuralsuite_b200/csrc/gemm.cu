@@ -97,7 +97,7 @@ extern "C" {
 size_t ns_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const tc::Plan p = tc::plan(M, N, K, true);
-  return tc::split_workspace_bytes(p, M, N);
+  return ((tc::split_workspace_bytes(p, M, N) + 255) & ~(size_t)255) + tc::lo_workspace_bytes(M, N, K);
 }
 
 ns_status ns_gemm_set_engine(int engine) {
@@ -127,12 +127,22 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
   cudaStream_t s = as_stream(stream);
   if (K == 0 || !use_tc(M, N, K, A, lda, B, ldb))
     return gemm_simt(M, N, K, A, lda, a_trans, B, ldb, b_trans, e, s);
+  // Workspace: [split-K partials | lo(A) | lo(B)], each part used only if it fits.
   tc::Plan pl = tc::plan(M, N, K, true);
-  if (tc::split_workspace_bytes(pl, M, N) > workspace_bytes || !workspace ||
-      (reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+  const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
+  size_t part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
+  if (!ws_ok || part > workspace_bytes) {
     pl = tc::plan(M, N, K, false);
+    part = 0;
+  }
+  // The pre-split path needs 16-byte rows for the compact lo copies.
+  const int a_cols = a_trans ? M : K, b_cols = b_trans ? K : N;
+  float* lo = nullptr;
+  if (ws_ok && part + tc::lo_workspace_bytes(M, N, K) <= workspace_bytes && a_cols % 4 == 0 &&
+      b_cols % 4 == 0)
+    lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
   return tc::run(pl, M, N, K, A, lda, a_trans, B, ldb, b_trans ? 0 : 1, e,
-                 static_cast<float*>(workspace), s);
+                 static_cast<float*>(workspace), lo, s);
 }
 
 ns_status ns_kernel_health(void) {

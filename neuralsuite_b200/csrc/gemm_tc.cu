@@ -243,10 +243,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       : "memory");
 }
 
-template <int BN, int STAGES>
+// PRE = true: the lo parts of both operands were written to global memory by
+// split_lo_k beforehand and arrive by TMA next to the raw tiles, so the split
+// warps and their barrier drop out of the pipeline.
+template <int BN, int STAGES, bool PRE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
-                       const __grid_constant__ CUtensorMap tmB, const KParams p) {
+                       const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmAlo,
+                       const __grid_constant__ CUtensorMap tmBlo, const KParams p) {
   using L = Layout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -313,23 +318,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(full_bar(s), L::kRaw);
+          mbar_expect_tx(full_bar(s), PRE ? 2 * L::kRaw : L::kRaw);
           issued_stage[s] = 1;
           issued_phase[s] = ph;
           const uint32_t a_dst = sbase + s * L::kStage;
           const uint32_t b_dst = a_dst + L::kA;
           const int k0 = kb * kBK;
-          if (!p.a_mn) {
-            tma_load_2d(a_dst, &tmA, full_bar(s), k0, m0);
-          } else {
 #pragma unroll
-            for (int j = 0; j < kBM / 32; ++j) tma_load_2d(a_dst + j * 4096, &tmA, full_bar(s), m0 + 32 * j, k0);
-          }
-          if (!p.b_mn) {
-            tma_load_2d(b_dst, &tmB, full_bar(s), k0, n0);
-          } else {
+          for (int part = 0; part < (PRE ? 2 : 1); ++part) {
+            const CUtensorMap* ma = part ? &tmAlo : &tmA;
+            const CUtensorMap* mb = part ? &tmBlo : &tmB;
+            const uint32_t off = part ? L::kRaw : 0u;  // lo tiles sit right after the raw ones
+            if (!p.a_mn) {
+              tma_load_2d(a_dst + off, ma, full_bar(s), k0, m0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_dst + j * 4096, &tmB, full_bar(s), n0 + 32 * j, k0);
+              for (int j = 0; j < kBM / 32; ++j)
+                tma_load_2d(a_dst + off + j * 4096, ma, full_bar(s), m0 + 32 * j, k0);
+            }
+            if (!p.b_mn) {
+              tma_load_2d(b_dst + off, mb, full_bar(s), k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_2d(b_dst + off + j * 4096, mb, full_bar(s), n0 + 32 * j, k0);
+            }
           }
         }
       }
@@ -383,11 +396,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < kBK / 8; ++kk)
               mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
                        idesc, (kb > c0 || kk > 0) ? 1u : 0u);
-            if (!mbar_wait(split_bar(s), ph, abort)) {
-              ok = false;
-              break;
+            if (!PRE) {
+              if (!mbar_wait(split_bar(s), ph, abort)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
             }
-            tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
               mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
@@ -482,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(acce_bar(r));
     }
-  } else {
+  } else if (!PRE) {
     // ------------------------------------------------------------ hi/lo split
     const int tt = (warp < 4) ? (warp - 2) * 32 + lane : (warp - 6) * 32 + lane;  // 0..191
     uint32_t it = 0;
@@ -522,6 +537,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(L::kTmemCols)
                  : "memory");
+  }
+}
+
+// lo = x - trunc_tf32(x) of a [rows, cols] operand with row stride ld, written
+// compact (row stride cols).  trunc keeps the 10 explicit mantissa bits the
+// tensor core reads from a tf32 operand, so hi + lo == x exactly.
+__global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int ld,
+                           float* __restrict__ lo, int vec) {
+  const int64_t total = (int64_t)rows * cols;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const int c4 = cols >> 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total / 4; i += stride) {
+      const int64_t r = i / c4, c = (i % c4) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(x + r * ld + c);
+      float4 o;
+      o.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+      o.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+      o.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+      o.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+      *reinterpret_cast<float4*>(lo + r * cols + c) = o;
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+      const int64_t r = i / cols, c = i % cols;
+      const float v = x[r * ld + c];
+      lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    }
   }
 }
 
@@ -590,16 +633,27 @@ ns_status make_map(CUtensorMap* map, const float* ptr, int inner, int rows, int 
   return NS_OK;
 }
 
-template <int BN, int STAGES>
-ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
+template <int BN, int STAGES, bool PRE>
+ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
+                 const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
                  cudaStream_t s) {
   using L = Layout<BN, STAGES>;
   static_assert(L::kDynSmem <= 232448, "shared memory budget");
-  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, STAGES>,
+  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, STAGES, PRE>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
               "ns_gemm attr");
-  gemm_tf32x3_kernel<BN, STAGES><<<pl.grid, kThreads, L::kDynSmem, s>>>(ta, tb, kp);
+  gemm_tf32x3_kernel<BN, STAGES, PRE><<<pl.grid, kThreads, L::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
   return check_launch("ns_gemm tcgen05");
+}
+
+ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {
+  const int64_t total = (int64_t)rows * cols;
+  const int vec = ((cols & 3) == 0 && (ld & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0);
+  const int64_t work = vec ? total / 4 : total;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
+  split_lo_k<<<grid, 256, 0, s>>>(x, rows, cols, ld, lo, vec);
+  return check_launch("ns_gemm operand split");
 }
 
 }  // namespace
@@ -643,16 +697,40 @@ size_t split_workspace_bytes(const Plan& p, int M, int N) {
   return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
 }
 
+// Floats of the compact lo copy of A, rounded up to 64 B so B's copy is aligned.
+size_t lo_elems_a(int M, int K) { return ((size_t)M * K + 15) & ~(size_t)15; }
+size_t lo_workspace_bytes(int M, int N, int K) {
+  return (lo_elems_a(M, K) + (size_t)K * N) * sizeof(float);
+}
+
 ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
-              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws,
+              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws, float* lo_ws,
               cudaStream_t stream) {
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ta_lo, tb_lo;
   std::memset(&ta, 0, sizeof(ta));
   std::memset(&tb, 0, sizeof(tb));
+  std::memset(&ta_lo, 0, sizeof(ta_lo));
+  std::memset(&tb_lo, 0, sizeof(tb_lo));
   ns_status rc = a_mn ? make_map(&ta, A, M, K, lda, 32, true) : make_map(&ta, A, K, M, lda, kBM, false);
   if (rc != NS_OK) return rc;
   rc = b_mn ? make_map(&tb, B, N, K, ldb, 32, true) : make_map(&tb, B, K, N, ldb, pl.bn, false);
   if (rc != NS_OK) return rc;
+  const bool pre = lo_ws != nullptr;
+  if (pre) {
+    // Compact lo copies: A as stored ([M,K] or [K,M]), then B as stored.
+    float* a_lo = lo_ws;
+    float* b_lo = lo_ws + lo_elems_a(M, K);
+    const int a_rows = a_mn ? K : M, a_cols = a_mn ? M : K;
+    const int b_rows = b_mn ? K : N, b_cols = b_mn ? N : K;
+    rc = split_lo(A, a_rows, a_cols, lda, a_lo, stream);
+    if (rc != NS_OK) return rc;
+    rc = split_lo(B, b_rows, b_cols, ldb, b_lo, stream);
+    if (rc != NS_OK) return rc;
+    rc = a_mn ? make_map(&ta_lo, a_lo, M, K, M, 32, true) : make_map(&ta_lo, a_lo, K, M, K, kBM, false);
+    if (rc != NS_OK) return rc;
+    rc = b_mn ? make_map(&tb_lo, b_lo, N, K, N, 32, true) : make_map(&tb_lo, b_lo, K, N, K, pl.bn, false);
+    if (rc != NS_OK) return rc;
+  }
   KParams kp;
   kp.M = M; kp.N = N; kp.K = K;
   kp.tiles_m = pl.tiles_m; kp.tiles_n = pl.tiles_n; kp.splits = pl.splits;
@@ -664,7 +742,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                        reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
                        reinterpret_cast<uintptr_t>(ws);
   kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
-  rc = launch<128, 3>(pl, ta, tb, kp, stream);
+  rc = pre ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
+           : launch<128, 3, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
   if (rc != NS_OK || pl.splits == 1) return rc;
   const int64_t total = (int64_t)M * N;
   const int vec = kp.vec_ok;

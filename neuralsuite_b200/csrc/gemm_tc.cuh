@@ -25,10 +25,17 @@ struct Plan {
 Plan plan(int M, int N, int K, bool allow_split);
 size_t split_workspace_bytes(const Plan& p, int M, int N);
 
+size_t lo_elems_a(int M, int K);
+// Bytes for the compact lo copies of both operands (the pre-split path).
+size_t lo_workspace_bytes(int M, int N, int K);
+
 // Runs C = op(A) op(B) (+ epilogue) on the tcgen05 path.  `ws` holds the
-// split-K partial tiles when plan.splits > 1.
+// split-K partial tiles when plan.splits > 1.  With `lo_ws` (at least
+// lo_workspace_bytes) the operands are split into hi/lo in global memory
+// first and the kernel loads both parts by TMA; without it the kernel splits
+// each tile in shared memory.
 ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
-              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws,
+              const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws, float* lo_ws,
               cudaStream_t stream);
 
 // 1 if a kernel hit a bounded-wait timeout since the last call (clears it).
