@@ -290,7 +290,7 @@ def run_ours(args, rank, world, local):
     barrier()
     ms = max_over_ranks(s.elapsed_time(e)) / args.steps
     clk = clocks.stop()
-    loss_dev = float(model.loss_tensor().item())
+    loss_dev = float(model.loss_tensor().item()) / world  # device holds the sum over ranks
 
     # -- end-to-end leg through the public API: pinned host tokens/targets in,
     # loss out, every step
