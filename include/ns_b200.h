@@ -124,10 +124,16 @@ NS_API ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* wo
  * Replaces the per-(b,h) loop of MultiHeadAttention::Forward
  * (attention.h:364-384) and ::Backward (attention.h:405-461); backward writes
  * dqkv[B*T, 3C] in the same interleaved layout and needs `workspace` of
- * ns_attn_bwd_workspace_size bytes.  Scale = 1/sqrt(D) applied after Q.K^T
+ * ns_attn_bwd_workspace_size bytes; forward needs ns_attn_fwd_workspace_size
+ * bytes (16-byte aligned; 0 for head sizes without a tensor-core kernel).  Scale = 1/sqrt(D) applied after Q.K^T
  * (attention.h:362, 372-374). */
+NS_API size_t ns_attn_fwd_workspace_size(int B, int T, int H, int D);
 NS_API ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
-                      void* stream);
+                      void* workspace, size_t workspace_bytes, void* stream);
+/* 0 (default): head_dim 32 / 64 run on the tensor cores (3xTF32, tcgen05), other
+ * sizes on the SIMT kernels; 1: SIMT kernels for every size.  Per host thread.
+ * No reference counterpart (engine selection for tests and profiling). */
+NS_API ns_status ns_attn_set_engine(int engine);
 NS_API size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D);
 NS_API ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, const float* lse,
                       int B, int T, int H, int D, float* dqkv, void* workspace,

@@ -53,7 +53,9 @@ _SIGS = {
     "ns_kernel_health": (c_int, []),
     "ns_bias_grad_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_bias_grad": (c_int, [P, c_int, c_int, P, P, c_size_t, P]),
-    "ns_attn_fwd": (c_int, [P, c_int, c_int, c_int, c_int, P, P, P]),
+    "ns_attn_fwd_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "ns_attn_fwd": (c_int, [P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
+    "ns_attn_set_engine": (c_int, [c_int]),
     "ns_attn_bwd_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ns_attn_bwd": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int, P, P, c_size_t, P]),
     "ns_layernorm_fwd": (c_int, [P, P, P, P, P, P, c_int, c_int, c_float, P]),

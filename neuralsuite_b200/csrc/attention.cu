@@ -17,10 +17,13 @@
 // fp32 SIMT: each thread owns a 4 x 4 tile of the 64 x 64 score block.
 #include <algorithm>
 
+#include "attention_tc.cuh"
 #include "common.cuh"
 
 namespace nsb {
 namespace {
+
+thread_local int t_attn_engine = 0;  // 0 auto (tensor cores where supported), 1 SIMT
 
 constexpr int kBr = 64;   // query rows per block
 constexpr int kBc = 64;   // keys per block
@@ -415,12 +418,29 @@ using namespace nsb;
 
 extern "C" {
 
+size_t ns_attn_fwd_workspace_size(int B, int T, int H, int D) {
+  if (B <= 0 || T <= 0 || H <= 0 || (D != 32 && D != 64)) return 0;
+  return attn_tc::fwd_workspace_bytes(B, T, H, D);
+}
+
+ns_status ns_attn_set_engine(int engine) {
+  NS_REQUIRE(engine == 0 || engine == 1, "ns_attn_set_engine: engine must be 0 or 1");
+  t_attn_engine = engine;
+  return NS_OK;
+}
+
 ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
-                      void* stream) {
+                      void* workspace, size_t workspace_bytes, void* stream) {
   NS_REQUIRE(B >= 0 && T >= 0 && H > 0 && D > 0, "ns_attn_fwd: bad shape");
   NS_REQUIRE(D <= 128, "ns_attn_fwd: head_dim > 128 is not supported");
   if (B == 0 || T == 0) return NS_OK;
+  const size_t need = ns_attn_fwd_workspace_size(B, T, H, D);
+  NS_REQUIRE(workspace_bytes >= need && (need == 0 || workspace),
+             "ns_attn_fwd: workspace too small");
   cudaStream_t s = as_stream(stream);
+  if (t_attn_engine == 0 && need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0 &&
+      attn_tc::fwd_supported(qkv, out, B, T, H, D))
+    return attn_tc::fwd(qkv, B, T, H, D, out, lse, static_cast<float*>(workspace), s);
   if (D <= 16) return launch_fwd<16>(qkv, B, T, H, D, out, lse, s);
   if (D <= 32) return launch_fwd<32>(qkv, B, T, H, D, out, lse, s);
   if (D <= 64) return launch_fwd<64>(qkv, B, T, H, D, out, lse, s);

@@ -1,0 +1,529 @@
+// K2 on the 5th-generation tensor cores: fused causal attention forward for
+// head_dim 32 and 64, 3xTF32 (the attention.cu SIMT kernels serve every other
+// head size).  Same contract as the SIMT forward: out[B*T, C] and lse[B*H*T]
+// from the interleaved qkv[B*T, 3C] (MultiHeadAttention::Forward,
+// include/layers/attention.h:364-384).
+//
+// One CTA per (b, h, 128-query block), 384 threads, warp-specialised:
+//   warp 0      TMA producer: per 64-key block the K and V tiles of this head
+//               and their tf32 lo parts (split beforehand into the workspace)
+//               into a shared-memory ring.  K lands K-major (16-byte chunk
+//               128B swizzle), V MN-major (32-byte chunk 128B swizzle).
+//   warp 1      MMA issuer (converged warp, elected lane), A operands from TMEM:
+//                 S_j  = Qhi.Khi + Qhi.Klo + Qlo.Khi      (M=128, N=64,  K=D)
+//                 O_j  = Phi.Vhi + Phi.Vlo + Plo.Vhi      (M=128, N=D,   K=64)
+//   warps 4-7   softmax warpgroup 0 (even key blocks), warps 8-11 softmax
+//               warpgroup 1 (odd key blocks); one query row per thread (TMEM
+//               lane = row).  Each warpgroup keeps its own running max m, sum
+//               l and output accumulator: per block it reads S_j, applies the
+//               causal mask, P = 2^(S*scale*log2e - m*scale*log2e), writes Phi
+//               (over S_j) and Plo to TMEM, and folds the previous O into its
+//               registers as acc = acc * alpha + O with round-to-nearest (each
+//               O_j is a 64-term tensor-core sum; its round-toward-zero
+//               accumulation stays at the 1e-7 level).  The two warpgroups
+//               alternate, so the tensor core always has the other one's S or
+//               O to compute; their partial results merge at the end.
+// TMEM (512 columns): Qhi [0,D), Qlo [D,2D); per warpgroup w: S/Phi at
+// 128+64w, Plo at 256+64w, O at 384+Dw.
+// Every mbarrier wait is bounded (2 s); a timeout raises a device flag that
+// ns_kernel_health() reports, and the CTA drains its copies and MMAs and exits.
+#include <algorithm>
+
+#include "attention_tc.cuh"
+#include "tc_common.cuh"
+
+namespace nsb {
+namespace attn_tc {
+
+__device__ int g_timeout;
+
+namespace {
+
+using namespace tcx;
+
+constexpr int kBQ = 128;  // queries per CTA (MMA M)
+constexpr int kBKV = 64;  // keys per block
+constexpr int kThreads = 384;
+constexpr int kWgThreads = 128;  // one softmax warpgroup
+
+constexpr uint32_t kTS = 128, kTPlo = 256, kTO = 384, kTmemCols = 512;
+
+template <int D>
+struct FwdLayout {
+  static constexpr int kStages = D == 64 ? 3 : 4;
+  static constexpr uint32_t kTile = kBKV * D * 4;  // 64 keys x D fp32 (D/32 boxes of 8 KB)
+  static constexpr uint32_t kStage = 4 * kTile;    // K raw | K lo | V raw | V lo
+  static constexpr uint32_t kXchg = kStages * kStage;  // [3][128] floats: m, m*c, l of warpgroup 1
+  static constexpr uint32_t kBars = kXchg + 3 * kBQ * 4;
+  static constexpr uint32_t kNumBars = 2 * kStages + 10;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;
+  static_assert(kDynSmem <= 232448, "shared memory budget");
+  static_assert(kDynSmem > 232448 / 2, "one CTA per SM (the CTA takes all 512 TMEM columns)");
+};
+
+struct FwdParams {
+  const float* qkv;
+  float* out;
+  float* lse;
+  int T, H, C;
+  float scale;       // 1/sqrt(D)
+  float scale_log2;  // scale * log2(e)
+};
+
+// K tile (keys x D, K-major): 8-row groups 1024 B apart, 16-byte chunks;
+// k-step kk (8 of D) is +32 B inside the 128-byte row, next 32 columns in the
+// next 8 KB box.
+__device__ __forceinline__ uint64_t k_desc(uint32_t base, int kk) {
+  return smem_desc(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024, 2u);
+}
+// V tile (keys x D, MN-major for O = P.V): boxes of 32 columns x 64 keys,
+// 8 KB apart (LBO); 4-row groups 512 B apart; k-step kk (8 keys) is +1024 B.
+__device__ __forceinline__ uint64_t v_desc(uint32_t base, int kk) {
+  return smem_desc(base + kk * 1024, 8192, 512, 1u);
+}
+
+// Register split: the CTA launches with 384 x kLaunchRegs; warps 0-3 (TMA,
+// MMA, idle) give theirs down to kLowRegs so that the eight softmax warps can
+// hold a full S row and output row each.  4*32*kLowRegs + 8*32*kHighRegs must
+// not exceed 384 * (registers per thread at launch), which the host checks
+// before launching.
+constexpr int kLowRegs = 48, kHighRegs = 208;
+constexpr int kMinLaunchRegs = (4 * 32 * kLowRegs + 8 * 32 * kHighRegs + kThreads - 1) / kThreads;
+
+__device__ __forceinline__ void reg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
+}
+
+__device__ __forceinline__ void wg_pair_sync() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");  // warps 4..11
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmKlo,
+                       const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmVlo, const FwdParams p) {
+  using L = FwdLayout<D>;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  auto kv_full = [&](int s) { return bar0 + 8u * s; };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t q_ready = bar0 + 8u * (2 * S);
+  auto s_full = [&](int w) { return bar0 + 8u * (2 * S + 1 + w); };
+  auto p_full = [&](int w) { return bar0 + 8u * (2 * S + 3 + w); };
+  auto o_full = [&](int w) { return bar0 + 8u * (2 * S + 5 + w); };
+  auto o_empty = [&](int w) { return bar0 + 8u * (2 * S + 7 + w); };
+  const uint32_t drain = bar0 + 8u * (2 * S + 9);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xchg = reinterpret_cast<float*>(smem + L::kXchg);
+
+  const int nqb = (p.T + kBQ - 1) / kBQ;
+  const int qb = nqb - 1 - (int)blockIdx.x;  // longest rows first
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int q0 = qb * kBQ;
+  const int n_kb = (min(q0 + kBQ, p.T) + kBKV - 1) / kBKV;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    mbar_init(q_ready, 2 * kWgThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(p_full(i), kWgThreads);
+      mbar_init(o_full(i), 1);
+      mbar_init(o_empty(i), kWgThreads);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    // setmaxnreg runs at one instruction for a whole warpgroup.
+    reg_dec();
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        int issued[S];
+        uint32_t issued_ph[S];
+        for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
+        bool ok = true;
+        const int row0 = b * p.T;
+        for (int j = 0; j < n_kb; ++j) {
+          const int s = j % S;
+          const uint32_t ph = (uint32_t)(j / S) & 1u;
+          if (!mbar_wait(kv_empty(s), ph ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(kv_full(s), L::kStage);
+          issued[s] = 1;
+          issued_ph[s] = ph;
+          const uint32_t dst = sbase + s * L::kStage;
+          const int row = row0 + j * kBKV;
+  #pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            const int x = h * D + 32 * c;
+            tma_load_2d(dst + c * 8192, &tmK, kv_full(s), p.C + x, row);
+            tma_load_2d(dst + L::kTile + c * 8192, &tmKlo, kv_full(s), x, row);
+            tma_load_2d(dst + 2 * L::kTile + c * 8192, &tmV, kv_full(s), 2 * p.C + x, row);
+            tma_load_2d(dst + 3 * L::kTile + c * 8192, &tmVlo, kv_full(s), p.C + x, row);
+          }
+        }
+        if (!ok)
+          for (int s = 0; s < S; ++s)
+            if (issued[s]) mbar_wait_drain(kv_full(s), issued_ph[s], &g_timeout);
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      // The whole warp runs this loop converged; the elected lane issues.
+      constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
+      constexpr uint32_t id_o = instr_desc(D, 0, 1);
+      bool ok = warp_wait(q_ready, 0, abort, &g_timeout);
+      fence_after();
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % S;
+        if (!warp_wait(kv_full(s), (uint32_t)(j / S) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          const uint32_t d = tmem + kTS + (j & 1) * kBKV;
+          const uint32_t k_raw = sbase + s * L::kStage, k_lo = k_raw + L::kTile;
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk)
+            mma_ts(d, tmem + kk * 8, k_desc(k_raw, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk) {
+            mma_ts(d, tmem + kk * 8, k_desc(k_lo, kk), id_s, 1u);
+            mma_ts(d, tmem + D + kk * 8, k_desc(k_raw, kk), id_s, 1u);
+          }
+          commit(s_full(j & 1));
+        }
+        __syncwarp();
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_kb > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < n_kb; ++j) {
+        const int w = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!warp_wait(p_full(w), ph, abort, &g_timeout) ||
+            !warp_wait(o_empty(w), ph ^ 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int s = j % S;
+        if (elect_one()) {
+          const uint32_t v_raw = sbase + s * L::kStage + 2 * L::kTile, v_lo = v_raw + L::kTile;
+          const uint32_t o = tmem + kTO + w * D;
+          const uint32_t phi = tmem + kTS + w * kBKV, plo = tmem + kTPlo + w * kBKV;
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk)
+            mma_ts(o, phi + kk * 8, v_desc(v_raw, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk) {
+            mma_ts(o, phi + kk * 8, v_desc(v_lo, kk), id_o, 1u);
+            mma_ts(o, plo + kk * 8, v_desc(v_raw, kk), id_o, 1u);
+          }
+          commit(o_full(w));
+          commit(kv_empty(s));
+        }
+        __syncwarp();
+        // S_{j+2} reuses this warpgroup's S/P columns: issued after O_j, and
+        // the tensor core runs one CTA's MMAs in issue order.
+        if (j + 2 < n_kb) ok = issue_s(j + 2);
+      }
+      if (!ok) {
+        // Wait for every MMA already issued before TMEM is freed.
+        if (elect_one()) commit(drain);
+        __syncwarp();
+        mbar_wait_drain(drain, 0, &g_timeout);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
+    const int wg = (warp - 4) >> 2;  // key blocks wg, wg+2, wg+4, ...
+    const int ew = warp & 3;         // TMEM lanes 32*ew .. 32*ew+31
+    const int row = ew * 32 + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    const float c = p.scale_log2;
+    {
+      // Q row -> Qhi / Qlo columns; warpgroup wg writes 32-column chunks wg, wg+2.
+      const float* qrow =
+          p.qkv + ((size_t)b * p.T + (q < p.T ? q : 0)) * (size_t)(3 * p.C) + (size_t)h * D;
+      for (int cc = wg; cc < D / 32; cc += 2) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 x = q < p.T ? *reinterpret_cast<const float4*>(qrow + 32 * cc + i)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
+            lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
+          }
+        }
+        tmem_st32(tmem + lane_off + 32 * cc, hi);
+        tmem_st32(tmem + lane_off + D + 32 * cc, lo);
+      }
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(q_ready);
+    }
+    const uint32_t s_t = tmem + lane_off + kTS + wg * kBKV;
+    const uint32_t pl_t = tmem + lane_off + kTPlo + wg * kBKV;
+    const uint32_t o_t = tmem + lane_off + kTO + wg * D;
+    float acc[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) acc[d] = 0.0f;
+    float m = -INFINITY, mc = 0.0f, l = 0.0f, alpha_prev = 0.0f;
+    bool ok = true;
+    int t = 0;
+    auto fold = [&](uint32_t ph, float alpha) -> bool {
+      if (!mbar_wait(o_full(wg), ph, abort, &g_timeout)) return false;
+      fence_after();
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(o_t + 32 * cc, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          acc[32 * cc + i] = fmaf(acc[32 * cc + i], alpha, __uint_as_float(v[i]));
+      }
+      return true;
+    };
+    for (int j = wg; j < n_kb; j += 2, ++t) {
+      if (!mbar_wait(s_full(wg), (uint32_t)t & 1u, abort, &g_timeout)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      // S_j completing implies this warpgroup's previous O is complete too
+      // (same MMA thread, issued earlier): fold it and free the O columns.
+      if (t > 0) {
+        if (!fold((uint32_t)(t - 1) & 1u, alpha_prev)) {
+          ok = false;
+          break;
+        }
+        fence_before();
+        mbar_arrive(o_empty(wg));
+      }
+      const int k0 = j * kBKV;
+      uint32_t s0[32], s1[32];
+      tmem_ld32(s_t, s0);
+      tmem_ld32(s_t + 32, s1);
+      float x[64];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] = __uint_as_float(s0[i]);
+        x[32 + i] = __uint_as_float(s1[i]);
+      }
+      if (k0 + kBKV - 1 > q) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (k0 + i > q) x[i] = -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = x[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+      const float m_new = fmaxf(m, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
+      // m_new = -inf: every key so far is masked (P = 0 below).
+      const float mc_new = m_new == -INFINITY ? 0.0f : m_new * c;
+      const float alpha = m == -INFINITY ? 0.0f : exp2f(mc - mc_new);
+      float rs[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rs[i] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        x[i] = exp2f(fmaf(x[i], c, -mc_new));
+        rs[i & 7] += x[i];
+      }
+      l = l * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
+      m = m_new;
+      mc = mc_new;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s0[i] = __float_as_uint(tf32_hi(x[i]));
+        s1[i] = __float_as_uint(tf32_hi(x[32 + i]));
+      }
+      tmem_st32(s_t, s0);
+      tmem_st32(s_t + 32, s1);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s0[i] = __float_as_uint(tf32_lo(x[i]));
+        s1[i] = __float_as_uint(tf32_lo(x[32 + i]));
+      }
+      tmem_st32(pl_t, s0);
+      tmem_st32(pl_t + 32, s1);
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(p_full(wg));
+      alpha_prev = alpha;
+    }
+    if (ok && t > 0) ok = fold((uint32_t)(t - 1) & 1u, alpha_prev);
+    // Merge: warpgroup 1 hands its accumulator over through its own O columns
+    // (no MMA writes them any more) and m, m*c, l through shared memory.
+    if (wg == 1) {
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[32 * cc + i]);
+        tmem_st32(o_t + 32 * cc, v);
+      }
+      xchg[row] = m;
+      xchg[kBQ + row] = mc;
+      xchg[2 * kBQ + row] = l;
+      tmem_wait_st();
+      fence_before();
+    }
+    wg_pair_sync();
+    if (wg == 0) {
+      fence_after();
+      const float m1 = xchg[row], mc1 = xchg[kBQ + row], l1 = xchg[2 * kBQ + row];
+      const float m_tot = fmaxf(m, m1);  // finite: key 0 is never masked
+      const float mc_tot = m_tot * c;
+      const float a0 = exp2f(mc - mc_tot);
+      const float a1 = m1 == -INFINITY ? 0.0f : exp2f(mc1 - mc_tot);
+      const float l_tot = l * a0 + l1 * a1;
+      const float inv = 1.0f / l_tot;
+      const uint32_t o1 = tmem + lane_off + kTO + D;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(o1 + 32 * cc, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          acc[32 * cc + i] = fmaf(acc[32 * cc + i], a0, __uint_as_float(v[i]) * a1) * inv;
+      }
+      if (ok && q < p.T) {
+        float* dst = p.out + ((size_t)b * p.T + q) * p.C + (size_t)h * D;
+#pragma unroll
+        for (int d = 0; d < D; d += 4)
+          *reinterpret_cast<float4*>(dst + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
+        p.lse[(size_t)bh * p.T + q] = m_tot * p.scale + logf(l_tot);
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// lo[r, c] = tf32 lo part of qkv[r, C + c] for c in [0, 2C): the K and V
+// columns, compact (row stride 2C).  2C is a multiple of 4.
+__global__ void split_kv_lo_k(const float* __restrict__ qkv, int64_t rows, int C,
+                              float* __restrict__ lo) {
+  const int c4 = (2 * C) >> 2;
+  const int64_t total = rows * c4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / c4, c = (i % c4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(qkv + r * 3 * C + C + c);
+    *reinterpret_cast<float4*>(lo + r * 2 * C + c) =
+        make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+  }
+}
+
+template <int D>
+ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* lse, float* lo,
+                     cudaStream_t s) {
+  using L = FwdLayout<D>;
+  const int C = H * D, rows = B * T;
+  {
+    const int64_t work = (int64_t)rows * (2 * C / 4);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
+    split_kv_lo_k<<<grid, 256, 0, s>>>(qkv, rows, C, lo);
+    ns_status rc = check_launch("ns_attn_fwd kv split");
+    if (rc != NS_OK) return rc;
+  }
+  CUtensorMap tk, tklo, tv, tvlo;
+  ns_status rc = make_map(&tk, qkv, 3 * C, rows, 3 * C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&tklo, lo, 2 * C, rows, 2 * C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&tv, qkv, 3 * C, rows, 3 * C, kBKV, true);
+  if (rc == NS_OK) rc = make_map(&tvlo, lo, 2 * C, rows, 2 * C, kBKV, true);
+  if (rc != NS_OK) return rc;
+  const float scale = 1.0f / sqrtf((float)D);
+  FwdParams p{qkv, out, lse, T, H, C, scale, scale * 1.4426950408889634f};
+  NS_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<D>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
+              "ns_attn_fwd attr");
+  {
+    // setmaxnreg.inc would wait forever if the launch held fewer registers
+    // than the split hands out.
+    cudaFuncAttributes fa;
+    NS_TRY_CUDA(cudaFuncGetAttributes(&fa, attn_fwd_tc_kernel<D>), "ns_attn_fwd attributes");
+    if (fa.numRegs < kMinLaunchRegs)
+      return fail(NS_ERR_UNSUPPORTED, "ns_attn_fwd: kernel compiled with too few registers for its split");
+  }
+  const dim3 grid((T + kBQ - 1) / kBQ, B * H);
+  attn_fwd_tc_kernel<D><<<grid, kThreads, L::kDynSmem, s>>>(tk, tklo, tv, tvlo, p);
+  return check_launch("ns_attn_fwd tcgen05");
+}
+
+}  // namespace
+
+bool fwd_supported(const float* qkv, const float* out, int B, int T, int H, int D) {
+  if (D != 32 && D != 64) return false;
+  if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out)) & 15) != 0) return false;
+  if ((int64_t)B * T >= (1ll << 31) || (int64_t)3 * H * D >= (1ll << 31)) return false;
+  static int supported = -1;
+  if (supported < 0) supported = ns_device_supported();
+  return supported == 1;
+}
+
+size_t fwd_workspace_bytes(int B, int T, int H, int D) {
+  return (size_t)B * T * 2 * H * D * sizeof(float);
+}
+
+ns_status fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse, float* lo,
+              cudaStream_t s) {
+  return D == 64 ? launch_fwd<64>(qkv, B, T, H, out, lse, lo, s)
+                 : launch_fwd<32>(qkv, B, T, H, out, lse, lo, s);
+}
+
+int consume_timeout_flag() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int)) != cudaSuccess) return 0;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace attn_tc
+}  // namespace nsb

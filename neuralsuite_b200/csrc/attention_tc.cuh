@@ -1,0 +1,24 @@
+// Interface between the attention entry points and the tcgen05 attention kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace nsb {
+namespace attn_tc {
+
+// True when the tensor-core forward handles this shape on this device
+// (head_dim 32 or 64, 16-byte aligned qkv and out, sm_100).
+bool fwd_supported(const float* qkv, const float* out, int B, int T, int H, int D);
+
+// Bytes of the K/V lo-part copy the tensor-core forward needs ([B*T, 2*H*D] fp32).
+size_t fwd_workspace_bytes(int B, int T, int H, int D);
+
+// out / lse from qkv; `lo` holds fwd_workspace_bytes, 16-byte aligned.
+ns_status fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse, float* lo,
+              cudaStream_t s);
+
+// 1 if an attention kernel hit a bounded-wait timeout since the last call (clears it).
+int consume_timeout_flag();
+
+}  // namespace attn_tc
+}  // namespace nsb

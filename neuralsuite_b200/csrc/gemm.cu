@@ -6,6 +6,7 @@
 #include <algorithm>
 
 #include "epilogue.cuh"
+#include "attention_tc.cuh"
 #include "gemm_tc.cuh"
 
 namespace nsb {
@@ -148,6 +149,8 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
 ns_status ns_kernel_health(void) {
   if (tc::consume_timeout_flag())
     return fail(NS_ERR_TIMEOUT, "a tcgen05 GEMM gave up a bounded wait (see ns_gemm)");
+  if (attn_tc::consume_timeout_flag())
+    return fail(NS_ERR_TIMEOUT, "a tcgen05 attention kernel gave up a bounded wait");
   return NS_OK;
 }
 

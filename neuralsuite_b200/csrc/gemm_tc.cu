@@ -10,7 +10,8 @@
 //               Transpose copies never happen.
 //   warps 2,3,8-11  split: lo = x - trunc_tf32(x) written beside each tile
 //               (elementwise, so the same code serves every operand layout).
-//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::tf32
+//   warp 1      MMA issuer: the elected lane of the converged warp issues
+//               tcgen05.mma.kind::tf32
 //               (M=128, N=128, K=8) into TMEM; the tensor core reads the raw
 //               fp32 tile as its tf32 "hi" part (it ignores the 13 low
 //               mantissa bits), so the hi.hi product starts as soon as the TMA
@@ -31,6 +32,7 @@
 #include <cstring>
 
 #include "gemm_tc.cuh"
+#include "tc_common.cuh"
 
 namespace nsb {
 namespace tc {
@@ -39,10 +41,11 @@ __device__ int g_timeout;
 
 namespace {
 
+using namespace tcx;
+
 constexpr int kThreads = 384;
 constexpr int kSplitThreads = 192;  // warps 2, 3, 8, 9, 10, 11
 constexpr int kEpiThreads = 128;    // warps 4..7 (TMEM lanes 0..127)
-constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
 struct KParams {
   int M, N, K;
@@ -53,132 +56,6 @@ struct KParams {
   int vec_ok;  // 16-byte vector epilogue allowed
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait for the phase of `parity`; false if the CTA is aborting.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try(bar, parity)) return true;
-    if ((it & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kTimeoutNs) {
-        *abort = 1;
-        atomicExch(&g_timeout, 1);
-        return false;
-      }
-    }
-  }
-}
-
-// Wait that ignores the abort flag (used while draining), still bounded.
-__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
-  const unsigned long long t0 = globaltimer();
-  while (!mbar_try(bar, parity)) {
-    if (globaltimer() - t0 > kTimeoutNs) {
-      atomicExch(&g_timeout, 1);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns of the accumulator.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
-        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
-        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor with the Blackwell version bits.
-// layout: 2 = 128-byte swizzle (16-byte chunks), 1 = 128-byte swizzle with
-// 32-byte chunks, the only layout the tensor core takes for MN-major 32-bit
-// operands.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-
 // Descriptor of MMA k-step kk (8 tf32) of an operand tile at `base`.
 // K-major: rows of 128 B (32 fp32 of K), 8-row groups 1024 B apart, 16-byte
 //          swizzle; k-steps advance 32 B inside the swizzled row.
@@ -188,12 +65,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int kk) {
   return mn_major ? smem_desc(base + kk * 1024, 4096, 512, 1u)
                   : smem_desc(base + kk * 32, 16, 1024, 2u);
-}
-
-// Instruction descriptor: kind::tf32, fp32 accumulate, M = 128, N = bn.
-__host__ __device__ constexpr uint32_t instr_desc(int bn, int a_mn, int b_mn) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
 __device__ __forceinline__ void decode_unit(const KParams& p, int u, int& tm, int& tn, int& split,
@@ -229,19 +100,6 @@ struct Layout {
   // [2BN,3BN) and [3BN,4BN): chunk buffers C0, C1.
   static constexpr uint32_t kTmemCols = 4 * BN;
 };
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-      "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
 
 // PRE = true: the lo parts of both operands were written to global memory by
 // split_lo_k beforehand and arrive by TMA next to the raw tiles, so the split
@@ -293,9 +151,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
-  tc_fence_after();
+  fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int n_units = p.tiles_m * p.tiles_n * p.splits;
 
@@ -314,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort)) {
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort, &g_timeout)) {
             ok = false;
             break;
           }
@@ -349,83 +207,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         // Aborting: let every copy this thread issued land before the CTA exits.
         for (int s = 0; s < STAGES; ++s)
-          if (issued_stage[s]) mbar_wait_drain(full_bar(s), issued_phase[s]);
+          if (issued_stage[s]) mbar_wait_drain(full_bar(s), issued_phase[s], &g_timeout);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = instr_desc(BN, p.a_mn, p.b_mn);
-      uint32_t it = 0, uit = 0, cit = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++uit) {
-        int tm, tn, split, kb0, kb1;
-        decode_unit(p, u, tm, tn, split, kb0, kb1);
-        const int r = uit & 1;
-        if (!mbar_wait(acce_bar(r), ((uit >> 1) & 1u) ^ 1u, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk) {
-          uint32_t d_tmem = tmem_base + r * BN;  // chunk 0 goes straight into the running sum
-          int cb = -1;
-          if (c0 > kb0) {
-            cb = cit & 1;
-            if (!mbar_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            d_tmem = tmem_base + (2 + cb) * BN;
+    // The whole warp runs this loop converged; the elected lane issues.
+    const uint32_t idesc = instr_desc(BN, p.a_mn, p.b_mn);
+    uint32_t it = 0, uit = 0, cit = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++uit) {
+      int tm, tn, split, kb0, kb1;
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+      const int r = uit & 1;
+      if (!warp_wait(acce_bar(r), ((uit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk) {
+        uint32_t d_tmem = tmem_base + r * BN;  // chunk 0 goes straight into the running sum
+        int cb = -1;
+        if (c0 > kb0) {
+          cb = cit & 1;
+          if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
           }
-          const int c1 = min(kb1, c0 + kChunk);
-          for (int kb = c0; kb < c1; ++kb, ++it) {
-            const int s = it % STAGES;
-            const uint32_t ph = (it / STAGES) & 1u;
-            const uint32_t a_raw = sbase + s * L::kStage;
-            const uint32_t b_raw = a_raw + L::kA;
-            const uint32_t a_lo = a_raw + L::kRaw;
-            const uint32_t b_lo = a_lo + L::kA;
-            if (!mbar_wait(full_bar(s), ph, abort)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+          fence_after();
+          d_tmem = tmem_base + (2 + cb) * BN;
+        }
+        const int c1 = min(kb1, c0 + kChunk);
+        for (int kb = c0; kb < c1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          const uint32_t a_raw = sbase + s * L::kStage;
+          const uint32_t b_raw = a_raw + L::kA;
+          const uint32_t a_lo = a_raw + L::kRaw;
+          const uint32_t b_lo = a_lo + L::kA;
+          if (!warp_wait(full_bar(s), ph, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk)
-              mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
-                       idesc, (kb > c0 || kk > 0) ? 1u : 0u);
-            if (!PRE) {
-              if (!mbar_wait(split_bar(s), ph, abort)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+              mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                     idesc, (kb > c0 || kk > 0) ? 1u : 0u);
+          }
+          __syncwarp();
+          if (!PRE) {
+            if (!warp_wait(split_bar(s), ph, abort, &g_timeout)) {
+              ok = false;
+              break;
             }
+            fence_after();
+          }
+          if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
-              mma_tf32(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
-                       idesc, 1u);
-              mma_tf32(d_tmem, operand_desc(a_lo, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
-                       idesc, 1u);
+              mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
+                     idesc, 1u);
+              mma_ss(d_tmem, operand_desc(a_lo, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                     idesc, 1u);
             }
-            tc_commit(empty_bar(s));
+            commit(empty_bar(s));
           }
-          if (!ok) break;
-          if (cb >= 0) {
-            tc_commit(chf_bar(cb));
-            ++cit;
-          }
+          __syncwarp();
         }
         if (!ok) break;
-        tc_commit(accf_bar(r));
+        if (cb >= 0) {
+          if (elect_one()) commit(chf_bar(cb));
+          __syncwarp();
+          ++cit;
+        }
       }
-      if (!ok) {
-        // Aborting: wait for every MMA already issued before TMEM is freed.
-        tc_commit(drain_bar);
-        mbar_wait_drain(drain_bar, 0);
-      }
+      if (!ok) break;
+      if (elect_one()) commit(accf_bar(r));
+      __syncwarp();
+    }
+    if (!ok) {
+      // Aborting: wait for every MMA already issued before TMEM is freed.
+      if (elect_one()) commit(drain_bar);
+      __syncwarp();
+      mbar_wait_drain(drain_bar, 0, &g_timeout);
     }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ fold + epilogue
@@ -441,11 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Fold chunks 1.. of this tile into the running sum, round to nearest.
       for (int c0 = kb0 + kChunk; c0 < kb1; c0 += kChunk, ++cit) {
         const int cb = cit & 1;
-        if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort)) {
+        if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
           ok = false;
           break;
         }
-        tc_fence_after();
+        fence_after();
         const uint32_t c_tmem = tmem_base + lane_off + (2 + cb) * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -457,13 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             b[j] = __float_as_uint(__fadd_rn(__uint_as_float(b[j]), __uint_as_float(a[j])));
           tmem_st32(r_tmem + c * 32, b);
         }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        tc_fence_before();
+        tmem_wait_st();
+        fence_before();
         mbar_arrive(che_bar(cb));
       }
       if (!ok) break;
-      if (!mbar_wait(accf_bar(r), (uit >> 1) & 1u, abort)) break;
-      tc_fence_after();
+      if (!mbar_wait(accf_bar(r), (uit >> 1) & 1u, abort, &g_timeout)) break;
+      fence_after();
       const int m = tm * kBM + ew * 32 + lane;
       const int n_base = tn * BN;
 #pragma unroll 1
@@ -494,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tc_fence_before();
+      fence_before();
       mbar_arrive(acce_bar(r));
     }
   } else if (!PRE) {
@@ -508,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        if (!mbar_wait(full_bar(s), ph, abort)) {
+        if (!mbar_wait(full_bar(s), ph, abort, &g_timeout)) {
           ok = false;
           break;
         }
@@ -530,10 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  tc_fence_before();
+  fence_before();
   __syncthreads();
   if (warp == 1) {
-    tc_fence_after();
+    fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(L::kTmemCols)
                  : "memory");
@@ -592,46 +458,6 @@ __global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M,
 }
 
 // ------------------------------------------------------------ host side
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-// 2-D fp32 map over a row-major [rows, inner] matrix with row stride ld,
-// box {32, box_rows}, out-of-bounds elements read as zero.  K-major operands
-// use the 16-byte-chunk 128B swizzle, MN-major operands the 32-byte-chunk one
-// (the two layouts the descriptors above describe).
-ns_status make_map(CUtensorMap* map, const float* ptr, int inner, int rows, int ld, int box_rows,
-                   bool mn_major) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return fail(NS_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
-  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
-  cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(NS_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed");
-  return NS_OK;
-}
 
 template <int BN, int STAGES, bool PRE>
 ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -711,9 +537,9 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   std::memset(&tb, 0, sizeof(tb));
   std::memset(&ta_lo, 0, sizeof(ta_lo));
   std::memset(&tb_lo, 0, sizeof(tb_lo));
-  ns_status rc = a_mn ? make_map(&ta, A, M, K, lda, 32, true) : make_map(&ta, A, K, M, lda, kBM, false);
+  ns_status rc = a_mn ? tcx::make_map(&ta, A, M, K, lda, 32, true) : tcx::make_map(&ta, A, K, M, lda, kBM, false);
   if (rc != NS_OK) return rc;
-  rc = b_mn ? make_map(&tb, B, N, K, ldb, 32, true) : make_map(&tb, B, K, N, ldb, pl.bn, false);
+  rc = b_mn ? tcx::make_map(&tb, B, N, K, ldb, 32, true) : tcx::make_map(&tb, B, K, N, ldb, pl.bn, false);
   if (rc != NS_OK) return rc;
   const bool pre = lo_ws != nullptr;
   if (pre) {
@@ -726,9 +552,9 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
     if (rc != NS_OK) return rc;
     rc = split_lo(B, b_rows, b_cols, ldb, b_lo, stream);
     if (rc != NS_OK) return rc;
-    rc = a_mn ? make_map(&ta_lo, a_lo, M, K, M, 32, true) : make_map(&ta_lo, a_lo, K, M, K, kBM, false);
+    rc = a_mn ? tcx::make_map(&ta_lo, a_lo, M, K, M, 32, true) : tcx::make_map(&ta_lo, a_lo, K, M, K, kBM, false);
     if (rc != NS_OK) return rc;
-    rc = b_mn ? make_map(&tb_lo, b_lo, N, K, N, 32, true) : make_map(&tb_lo, b_lo, K, N, K, pl.bn, false);
+    rc = b_mn ? tcx::make_map(&tb_lo, b_lo, N, K, N, 32, true) : tcx::make_map(&tb_lo, b_lo, K, N, K, pl.bn, false);
     if (rc != NS_OK) return rc;
   }
   KParams kp;

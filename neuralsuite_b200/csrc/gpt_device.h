@@ -361,7 +361,7 @@ class MultiHeadAttention : public Layer {
     att_ = Scratch(att_buf_, M, n_embd_);
     lse_ = Scratch(lse_buf_, batch_ * n_head_, seq_);
     Check(ns_attn_fwd(qkv_.Data(), batch_, seq_, n_head_, head_dim_, att_.Data(), lse_.Data(),
-                      stream()));
+                      ctx_->scratch, ctx_->scratch_bytes, stream()));
     Tensor y = resid ? c_proj_.ForwardResidual(att_, resid->View({M, n_embd_}))
                      : c_proj_.Forward(att_);
     return y.View({batch_, seq_, n_embd_});
@@ -557,9 +557,12 @@ class GPTModel : public Module {
     gw(4 * C, C, M); gw(V, C, M);
     ws = std::max(ws, ns_layernorm_bwd_workspace_size(M, C));
     for (int n : {3 * C, C, 4 * C}) ws = std::max(ws, ns_bias_grad_workspace_size(M, n));
-    if (cfg.n_head > 0)
+    if (cfg.n_head > 0) {
+      ws = std::max(ws, ns_attn_fwd_workspace_size(max_batch, cfg.block_size, cfg.n_head,
+                                                   C / cfg.n_head));
       ws = std::max(ws, ns_attn_bwd_workspace_size(max_batch, cfg.block_size, cfg.n_head,
                                                    C / cfg.n_head));
+    }
     ws = std::max(ws, ns_cross_entropy_workspace_size(M, V));
     ws = std::max(ws, ns_sumsq_workspace_size(total));
     scratch_ = std::make_shared<DeviceBuffer>(std::max<size_t>(ws, 256));

@@ -84,8 +84,15 @@ def attn_fwd(qkv, B, T, H, D):
     _req(qkv, "qkv")
     out = torch.empty((B * T, H * D), dtype=_f32, device=qkv.device)
     lse = torch.empty((B * H * T,), dtype=_f32, device=qkv.device)
-    _lib.check(lib.ns_attn_fwd(_p(qkv), B, T, H, D, _p(out), _p(lse), _stream()))
+    nb = lib.ns_attn_fwd_workspace_size(B, T, H, D)
+    ws = _ws(nb, qkv.device)
+    _lib.check(lib.ns_attn_fwd(_p(qkv), B, T, H, D, _p(out), _p(lse), _p(ws), nb, _stream()))
     return out, lse
+
+
+def attn_set_engine(engine):
+    """0: tensor-core attention where the head size has a kernel; 1: SIMT only."""
+    _lib.check(_lib.load().ns_attn_set_engine(engine))
 
 
 def attn_bwd(qkv, out, dout, lse, B, T, H, D):

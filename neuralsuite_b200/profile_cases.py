@@ -1,7 +1,7 @@
 """Small, self-contained kernel cases for profilers (ncu) and quick timing.
 
     python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps]
-    python -m neuralsuite_b200.profile_cases attn B T H D [reps]
+    python -m neuralsuite_b200.profile_cases attn B T H D [reps [engine]]
     python -m neuralsuite_b200.profile_cases ln ROWS DIM [reps]
 
 Each case allocates its operands once (seeded normal data), runs the kernel
@@ -48,10 +48,15 @@ def main(argv):
         reps = int(argv[5]) if len(argv) > 5 else 3
         qkv = torch.randn(Bb * T, 3 * H * D, device=dev)
         dout = torch.randn(Bb * T, H * D, device=dev)
-        out, lse = nk.attn_fwd(qkv, Bb, T, H, D)
-        f = _time(lambda: nk.attn_fwd(qkv, Bb, T, H, D), reps)
-        b = _time(lambda: nk.attn_bwd(qkv, out, dout, lse, Bb, T, H, D), reps)
-        print(f"attention B={Bb} T={T} H={H} D={D}: fwd {f:.3f} ms, bwd {b:.3f} ms")
+        engines = [int(argv[6])] if len(argv) > 6 else [0, 1]
+        for eng in engines:
+            nk.attn_set_engine(eng)
+            out, lse = nk.attn_fwd(qkv, Bb, T, H, D)
+            f = _time(lambda: nk.attn_fwd(qkv, Bb, T, H, D), reps)
+            b = _time(lambda: nk.attn_bwd(qkv, out, dout, lse, Bb, T, H, D), reps)
+            name = "simt" if eng else "auto"
+            print(f"attention[{name}] B={Bb} T={T} H={H} D={D}: fwd {f:.3f} ms, bwd {b:.3f} ms")
+        nk.attn_set_engine(0)
     elif case == "ln":
         rows, dim = int(argv[1]), int(argv[2])
         reps = int(argv[3]) if len(argv) > 3 else 3

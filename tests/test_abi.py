@@ -32,3 +32,16 @@ def test_binding_signatures_cover_header():
     from neuralsuite_b200 import _lib
 
     assert set(declared_symbols()) <= set(_lib._SIGS), set(declared_symbols()) - set(_lib._SIGS)
+
+
+def test_attention_forward_rejects_a_missing_workspace():
+    """Argument checks run before any device work: head size 64 needs the
+    K/V lo-part workspace, head size 16 needs none."""
+    from neuralsuite_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.ns_attn_fwd_workspace_size(2, 128, 4, 64) == 2 * 128 * 2 * 4 * 64 * 4
+    assert lib.ns_attn_fwd_workspace_size(2, 128, 4, 16) == 0
+    rc = lib.ns_attn_fwd(None, 1, 4, 1, 64, None, None, None, 0, None)
+    assert rc == 1  # NS_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.ns_last_error()

@@ -166,14 +166,26 @@ def test_bias_grad(cuda, port):
 # -------------------------------------------------------------- attention
 
 ATT_CASES = [(2, 64, 4, 32), (1, 8, 2, 8), (1, 1, 2, 4), (3, 16, 8, 4), (2, 5, 1, 4),
-             (1, 32, 4, 16), (2, 100, 3, 64), (1, 70, 2, 128)]
+             (1, 32, 4, 16), (2, 100, 3, 64), (1, 70, 2, 128),
+             # tensor-core shapes: T not a multiple of the 64-key / 128-query
+             # blocks, one-token sequences, batches whose key blocks straddle
+             # the next sequence
+             (1, 1, 1, 64), (3, 33, 2, 32), (2, 129, 2, 64), (1, 300, 1, 64), (2, 200, 2, 32)]
+
+
+@pytest.fixture(params=[0, 1], ids=["auto", "simt"])
+def attn_engine(request):
+    nk.attn_set_engine(request.param)
+    yield request.param
+    nk.attn_set_engine(0)
 
 
 @pytest.mark.parametrize("B,T,H,D", ATT_CASES)
-def test_attention_core(cuda, B, T, H, D):
+def test_attention_core(cuda, attn_engine, B, T, H, D):
     """Forward output and dqkv against the float64 restatement of the
     reference's per-(b,h) loop; includes the reference test_suite's
-    fast-vs-literal shapes (test_suite.cpp:3112-3119)."""
+    fast-vs-literal shapes (test_suite.cpp:3112-3119).  Engine "auto" runs
+    head sizes 32 and 64 on the tensor cores."""
     r = rng(B * 1000 + T * 10 + H + D)
     C = H * D
     qkv = normal(r, (B * T, 3 * C))
@@ -185,6 +197,14 @@ def test_attention_core(cuda, B, T, H, D):
     o = host(out)
     assert rel_l2(o, o64) < 1e-5
     assert np.allclose(o, o64, rtol=1e-4, atol=1e-5), np.abs(o - o64).max()
+    # lse = m + log(sum exp(s - m)) per (b, h, row)
+    q = qkv[:, :C].reshape(B, T, H, D).transpose(0, 2, 1, 3).astype(np.float64)
+    k = qkv[:, C:2 * C].reshape(B, T, H, D).transpose(0, 2, 1, 3).astype(np.float64)
+    s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
+    s = np.where(np.tril(np.ones((T, T), bool)), s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    lse64 = (mx[..., 0] + np.log(np.exp(s - mx).sum(-1))).reshape(-1)
+    assert np.allclose(host(lse), lse64, rtol=1e-5, atol=1e-5), np.abs(host(lse) - lse64).max()
     dq = host(nk.attn_bwd(qd, out, dev(dout, cuda), lse, B, T, H, D))
     assert rel_l2(dq, dq64) < 1e-5
     assert np.allclose(dq, dq64, rtol=1e-4, atol=1e-5), np.abs(dq - dq64).max()
