@@ -130,8 +130,9 @@ NS_API ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* wo
 NS_API size_t ns_attn_fwd_workspace_size(int B, int T, int H, int D);
 NS_API ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
                       void* workspace, size_t workspace_bytes, void* stream);
-/* 0 (default): head_dim 32 / 64 run on the tensor cores (3xTF32, tcgen05), other
- * sizes on the SIMT kernels; 1: SIMT kernels for every size.  Per host thread.
+/* 0 (default): head_dim 32 / 64 run on the tensor cores (3xTF32, tcgen05) in
+ * both directions, other sizes on the SIMT kernels; 1: SIMT kernels for every
+ * size.  Per host thread.
  * No reference counterpart (engine selection for tests and profiling). */
 NS_API ns_status ns_attn_set_engine(int engine);
 NS_API size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D);

@@ -448,9 +448,10 @@ ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, 
 }
 
 size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D) {
-  (void)D;
-  if (B <= 0 || T <= 0 || H <= 0) return 0;
-  return (size_t)B * H * T * sizeof(float);
+  if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return 0;
+  const size_t delta = ((size_t)B * H * T * sizeof(float) + 255) & ~(size_t)255;
+  if (D != 32 && D != 64) return delta;
+  return delta + attn_tc::bwd_lo_bytes(B, T, H, D);
 }
 
 ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, const float* lse,
@@ -466,6 +467,11 @@ ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, con
   const int64_t n = (int64_t)B * H * T;
   attn_delta_k<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(out, dout, B, T, H, D, delta);
   { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
+  const size_t delta_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
+  float* lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + delta_bytes);
+  if (t_attn_engine == 0 && (D == 32 || D == 64) && (reinterpret_cast<uintptr_t>(lo) & 15) == 0 &&
+      attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D))
+    return attn_tc::bwd(qkv, dout, lse, delta, B, T, H, D, dqkv, lo, s);
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 32) return launch_bwd<32>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 64) return launch_bwd<64>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

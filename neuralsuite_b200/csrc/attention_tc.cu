@@ -494,6 +494,457 @@ ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* l
   return check_launch("ns_attn_fwd tcgen05");
 }
 
+// ------------------------------------------------------------------ backward
+//
+// Three tensor-core kernels, one per gradient, on one skeleton: a 128-row
+// "major" block whose A operands sit in TMEM (hi/lo), and a loop over 64-wide
+// "minor" blocks whose B tiles (raw and lo) arrive by TMA:
+//   kDV  rows = keys,    minor = queries:  S^T = K.Q^T -> P^T;           dV += P^T.dO
+//   kDK  rows = keys,    minor = queries:  S^T, dP^T = V.dO^T -> dS^T;   dK += dS^T.Q
+//   kDQ  rows = queries, minor = keys:     S = Q.K^T, dP = dO.V^T -> dS; dQ += dS.K
+// with P = exp(scale*S - lse) and dS = P * (dP - Delta), Delta_i = dO_i . O_i
+// (MultiHeadAttention::Backward, include/layers/attention.h:405-461).  A
+// tensor that one kernel reads both K-major (for S or dP) and MN-major (for
+// the gradient product) is loaded twice, once per swizzle, because the
+// tensor core reads MN-major tf32 operands only from the 32-byte-atom swizzle
+// and K-major ones only from the 16-byte-chunk one.  With every operand held
+// as hi + lo, TMEM has room for one set of S / dP / product buffers, so the
+// tensor core computes S_{i+1} (and dP_{i+1}) while the element-wise warps
+// fold the previous product, and waits while they turn S_i into P_i / dS_i.
+// The eight element-wise warps split each 64-column block in halves: once
+// lse is known, no row reduction is needed.  Each block's product (a 64-term
+// tensor-core sum) is folded into registers with round-to-nearest adds.
+
+enum BwdMode { kDV = 0, kDK = 1, kDQ = 2 };
+
+constexpr float kLog2e = 1.4426950408889634f;
+// TMEM columns of the backward kernels.
+constexpr uint32_t kBA1 = 0, kBA2 = 128, kBS = 256, kBdP = 320, kBElo = 384, kBO = 448;
+
+template <int MODE, int D>
+struct BwdLayout {
+  static constexpr int kTiles = MODE == kDV ? 2 : 3;  // B tiles per stage
+  static constexpr int kStages = D == 64 ? (MODE == kDV ? 3 : 2) : (MODE == kDV ? 4 : 3);
+  static constexpr uint32_t kTile = kBKV * D * 4;  // 64 x D fp32 (D/32 boxes of 8 KB)
+  static constexpr uint32_t kVecOff = kTiles * 2 * kTile;
+  static constexpr uint32_t kVec = MODE == kDQ ? 0 : 1024;  // lse*log2e [64], Delta [64]
+  static constexpr uint32_t kStage = kVecOff + kVec;
+  static constexpr uint32_t kBars = kStages * kStage;
+  static constexpr uint32_t kNumBars = 2 * kStages + 6;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;
+  static_assert(kDynSmem <= 232448, "shared memory budget");
+  static_assert(kDynSmem > 232448 / 2, "one CTA per SM (the CTA takes all 512 TMEM columns)");
+};
+
+struct BwdParams {
+  const float* qkv;
+  const float* dout;
+  const float* lse;
+  const float* delta;
+  float* dqkv;
+  int T, H, C;
+  float scale, scale_log2;
+  int xb0, xb1, xb2;  // column of tile t's tensor for head 0 (head h adds h*D)
+};
+
+template <int MODE, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm0lo,
+                       const __grid_constant__ CUtensorMap tm1, const __grid_constant__ CUtensorMap tm1lo,
+                       const __grid_constant__ CUtensorMap tm2, const __grid_constant__ CUtensorMap tm2lo,
+                       const BwdParams p) {
+  using L = BwdLayout<MODE, D>;
+  constexpr int S = L::kStages;
+  constexpr bool kKeyMajor = MODE != kDQ;
+  constexpr bool kTwoA = MODE != kDV;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  auto kv_full = [&](int s) { return bar0 + 8u * s; };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t a_ready = bar0 + 8u * (2 * S);
+  const uint32_t s_full = a_ready + 8u, ew_done = a_ready + 16u, out_full = a_ready + 24u;
+  const uint32_t out_empty = a_ready + 32u, drain = a_ready + 40u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int n_all = (p.T + kBKV - 1) / kBKV;
+  int r0, blk0, n_blk;
+  if (kKeyMajor) {  // keys [r0, r0+128); query blocks from the diagonal to the end
+    r0 = (int)blockIdx.x * kBQ;
+    blk0 = r0 / kBKV;
+    n_blk = n_all - blk0;
+  } else {  // queries [r0, r0+128); key blocks up to the diagonal
+    const int nqb = (p.T + kBQ - 1) / kBQ;
+    r0 = (nqb - 1 - (int)blockIdx.x) * kBQ;
+    blk0 = 0;
+    n_blk = (min(r0 + kBQ, p.T) + kBKV - 1) / kBKV;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(kv_full(s), kKeyMajor ? 2 : 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    mbar_init(a_ready, 2 * kWgThreads);
+    mbar_init(s_full, 1);
+    mbar_init(ew_done, 2 * kWgThreads);
+    mbar_init(out_full, 1);
+    mbar_init(out_empty, 2 * kWgThreads);
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    reg_dec();
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      int issued[S];
+      uint32_t issued_ph[S];
+      for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
+      bool ok = true;
+      for (int i = 0; i < n_blk; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (uint32_t)(i / S) & 1u;
+        if (!warp_wait(kv_empty(s), ph ^ 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        issued[s] = 1;
+        issued_ph[s] = ph;
+        const int blk = blk0 + i;
+        const int row = b * p.T + blk * kBKV;
+        const uint32_t dst = sbase + s * L::kStage;
+        if (elect_one()) {
+          mbar_expect_tx(kv_full(s), L::kVecOff);
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            const int xo = h * D + 32 * c;
+            tma_load_2d(dst + c * 8192, &tm0, kv_full(s), p.xb0 + xo, row);
+            tma_load_2d(dst + L::kTile + c * 8192, &tm0lo, kv_full(s), p.xb0 + xo, row);
+            tma_load_2d(dst + 2 * L::kTile + c * 8192, &tm1, kv_full(s), p.xb1 + xo, row);
+            tma_load_2d(dst + 3 * L::kTile + c * 8192, &tm1lo, kv_full(s), p.xb1 + xo, row);
+            if (L::kTiles == 3) {
+              tma_load_2d(dst + 4 * L::kTile + c * 8192, &tm2, kv_full(s), p.xb2 + xo, row);
+              tma_load_2d(dst + 5 * L::kTile + c * 8192, &tm2lo, kv_full(s), p.xb2 + xo, row);
+            }
+          }
+        }
+        __syncwarp();
+        if (kKeyMajor) {
+          // lse (in log2 units) and Delta of this block's 64 queries.
+          float* vec = reinterpret_cast<float*>(smem + s * L::kStage + L::kVecOff);
+          for (int c = lane; c < kBKV; c += 32) {
+            const int q = blk * kBKV + c;
+            const bool in = q < p.T;
+            vec[c] = in ? p.lse[(size_t)bh * p.T + q] * kLog2e : 0.0f;
+            vec[kBKV + c] = in ? p.delta[(size_t)bh * p.T + q] : 0.0f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(kv_full(s));
+          __syncwarp();
+        }
+      }
+      if (!ok && lane == 0)
+        for (int s = 0; s < S; ++s)
+          if (issued[s]) mbar_wait_drain(kv_full(s), issued_ph[s], &g_timeout);
+    } else if (warp == 1) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
+      constexpr uint32_t id_o = instr_desc(D, 0, 1);
+      bool ok = warp_wait(a_ready, 0, abort, &g_timeout);
+      fence_after();
+      auto issue_sdp = [&](int i) -> bool {
+        const int s = i % S;
+        if (!warp_wait(kv_full(s), (uint32_t)(i / S) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          const uint32_t t0 = sbase + s * L::kStage, t0lo = t0 + L::kTile;
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk)
+            mma_ts(tmem + kBS, tmem + kBA1 + kk * 8, k_desc(t0, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk) {
+            mma_ts(tmem + kBS, tmem + kBA1 + kk * 8, k_desc(t0lo, kk), id_s, 1u);
+            mma_ts(tmem + kBS, tmem + kBA1 + D + kk * 8, k_desc(t0, kk), id_s, 1u);
+          }
+          if (kTwoA) {
+            const uint32_t t1 = t0 + 2 * L::kTile, t1lo = t1 + L::kTile;
+#pragma unroll
+            for (int kk = 0; kk < D / 8; ++kk)
+              mma_ts(tmem + kBdP, tmem + kBA2 + kk * 8, k_desc(t1, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < D / 8; ++kk) {
+              mma_ts(tmem + kBdP, tmem + kBA2 + kk * 8, k_desc(t1lo, kk), id_s, 1u);
+              mma_ts(tmem + kBdP, tmem + kBA2 + D + kk * 8, k_desc(t1, kk), id_s, 1u);
+            }
+          }
+          commit(s_full);
+        }
+        __syncwarp();
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int i = 0; ok && i < n_blk; ++i) {
+        if (!warp_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout) ||
+            (i > 0 && !warp_wait(out_empty, (uint32_t)(i - 1) & 1u, abort, &g_timeout))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int s = i % S;
+        if (elect_one()) {
+          // The MN-major tile is the last of the stage; the element-wise
+          // product (P^T or dS) sits in TMEM: hi over S (kDV) or dP, lo apart.
+          const uint32_t tb = sbase + s * L::kStage + (L::kTiles - 1) * 2 * L::kTile;
+          const uint32_t tblo = tb + L::kTile;
+          const uint32_t ehi = tmem + (MODE == kDV ? kBS : kBdP), elo = tmem + kBElo;
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk)
+            mma_ts(tmem + kBO, ehi + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk) {
+            mma_ts(tmem + kBO, ehi + kk * 8, v_desc(tblo, kk), id_o, 1u);
+            mma_ts(tmem + kBO, elo + kk * 8, v_desc(tb, kk), id_o, 1u);
+          }
+          commit(out_full);
+          commit(kv_empty(s));
+        }
+        __syncwarp();
+        // S_{i+1} / dP_{i+1} overwrite the columns the product just read:
+        // issued after it, and one CTA's MMAs run in issue order.
+        if (i + 1 < n_blk) ok = issue_sdp(i + 1);
+      }
+      if (!ok) {
+        if (elect_one()) commit(drain);
+        __syncwarp();
+        mbar_wait_drain(drain, 0, &g_timeout);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ element-wise
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
+    const int wg = (warp - 4) >> 2;  // columns [32*wg, 32*wg + 32) of every block
+    const int ew = warp & 3;
+    const int row = ew * 32 + lane;
+    const int r = r0 + row;  // key (kDV, kDK) or query (kDQ) index
+    const bool r_in = r < p.T;
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    const size_t ld = (size_t)3 * p.C;
+    {
+      // A operands of this row -> TMEM (hi at base, lo at base + D).
+      const size_t grow = (size_t)b * p.T + (r_in ? r : 0);
+      const float* a1 = p.qkv + grow * ld + (kKeyMajor ? p.C : 0) + (size_t)h * D;
+      const float* a2 = MODE == kDK ? p.qkv + grow * ld + 2 * (size_t)p.C + (size_t)h * D
+                                    : p.dout + grow * (size_t)p.C + (size_t)h * D;
+#pragma unroll
+      for (int t = 0; t < (kTwoA ? 2 : 1); ++t) {
+        const float* src = t ? a2 : a1;
+        const uint32_t base = tmem + lane_off + (t ? kBA2 : kBA1);
+        for (int cc = wg; cc < D / 32; cc += 2) {
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 x = r_in ? *reinterpret_cast<const float4*>(src + 32 * cc + i)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
+              lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
+            }
+          }
+          tmem_st32(base + 32 * cc, hi);
+          tmem_st32(base + D + 32 * cc, lo);
+        }
+      }
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(a_ready);
+    }
+    float lse2_row = 0.0f, delta_row = 0.0f;
+    if (!kKeyMajor && r_in) {
+      lse2_row = p.lse[(size_t)bh * p.T + r] * kLog2e;
+      delta_row = p.delta[(size_t)bh * p.T + r];
+    }
+    const bool folds = D == 64 || wg == 0;  // output columns [32*wg, 32*wg + 32)
+    float acc[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
+    const float c2 = p.scale_log2;
+    bool ok = true;
+    auto fold = [&](int i) -> bool {
+      if (!mbar_wait(out_full, (uint32_t)i & 1u, abort, &g_timeout)) return false;
+      fence_after();
+      if (folds) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + kBO + 32 * wg, v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) acc[c] = __fadd_rn(acc[c], __uint_as_float(v[c]));
+      }
+      return true;
+    };
+    for (int i = 0; i < n_blk; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(s_full, (uint32_t)i & 1u, abort, &g_timeout) ||
+          (kKeyMajor && !mbar_wait(kv_full(s), (uint32_t)(i / S) & 1u, abort, &g_timeout))) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      // The previous product finished before S_i (same MMA thread, issued earlier).
+      if (i > 0) {
+        if (!fold(i - 1)) {
+          ok = false;
+          break;
+        }
+        fence_before();
+        mbar_arrive(out_empty);
+      }
+      const int m0 = (blk0 + i) * kBKV + 32 * wg;  // minor index of column 0 of this half
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
+      if (kTwoA) tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
+      const float* vec = reinterpret_cast<const float*>(smem + s * L::kStage + L::kVecOff) + 32 * wg;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int m = m0 + c;
+        const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
+        const float l2 = kKeyMajor ? vec[c] : lse2_row;
+        const float pv = valid ? exp2f(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
+        float e = pv;
+        if (kTwoA) {
+          const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
+          e = pv * (__uint_as_float(dv[c]) - dl);
+        }
+        sv[c] = __float_as_uint(tf32_hi(e));
+        dv[c] = __float_as_uint(tf32_lo(e));
+      }
+      tmem_st32(tmem + lane_off + (MODE == kDV ? kBS : kBdP) + 32 * wg, sv);
+      tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(ew_done);
+    }
+    if (ok) ok = fold(n_blk - 1);
+    if (ok && r_in && folds) {
+      const float f = MODE == kDV ? 1.0f : p.scale;
+      const int col = (MODE == kDQ ? 0 : MODE == kDK ? p.C : 2 * p.C) + h * D + 32 * wg;
+      float* dst = p.dqkv + ((size_t)b * p.T + r) * ld + col;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<float4*>(dst + c) =
+            make_float4(acc[c] * f, acc[c + 1] * f, acc[c + 2] * f, acc[c + 3] * f);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// lo[r, c] = tf32 lo part of x[r, c] for a [rows, cols] matrix with row
+// stride ld, written compact (row stride cols).  cols and ld are multiples of 4.
+__global__ void split_lo_rows_k(const float* __restrict__ x, int64_t rows, int cols, int64_t ld,
+                                float* __restrict__ lo) {
+  const int c4 = cols >> 2;
+  const int64_t total = rows * c4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / c4, c = (i % c4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + r * ld + c);
+    *reinterpret_cast<float4*>(lo + r * cols + c) =
+        make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+  }
+}
+
+ns_status split_rows(const float* x, int64_t rows, int cols, float* lo, cudaStream_t s) {
+  const int64_t work = rows * (cols / 4);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
+  split_lo_rows_k<<<grid, 256, 0, s>>>(x, rows, cols, cols, lo);
+  return check_launch("ns_attn_bwd operand split");
+}
+
+template <int MODE, int D>
+ns_status launch_bwd_mode(const CUtensorMap* maps, const BwdParams& p, int B, int T, int H,
+                          cudaStream_t s) {
+  using L = BwdLayout<MODE, D>;
+  auto kern = attn_bwd_tc_kernel<MODE, D>;
+  NS_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
+              "ns_attn_bwd attr");
+  cudaFuncAttributes fa;
+  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, kern), "ns_attn_bwd attributes");
+  if (fa.numRegs < kMinLaunchRegs)
+    return fail(NS_ERR_UNSUPPORTED, "ns_attn_bwd: kernel compiled with too few registers for its split");
+  const dim3 grid((T + kBQ - 1) / kBQ, B * H);
+  kern<<<grid, kThreads, L::kDynSmem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
+  return check_launch(MODE == kDV ? "ns_attn_bwd dV tcgen05"
+                                  : MODE == kDK ? "ns_attn_bwd dK tcgen05" : "ns_attn_bwd dQ tcgen05");
+}
+
+template <int D>
+ns_status launch_bwd(const float* qkv, const float* dout, const float* lse, const float* delta,
+                     int B, int T, int H, float* dqkv, float* qkv_lo, float* dout_lo,
+                     cudaStream_t s) {
+  const int C = H * D, rows = B * T;
+  ns_status rc = split_rows(qkv, rows, 3 * C, qkv_lo, s);
+  if (rc == NS_OK) rc = split_rows(dout, rows, C, dout_lo, s);
+  if (rc != NS_OK) return rc;
+  // qkv and dout (and their lo copies), each as a K-major and an MN-major map.
+  CUtensorMap qk, qmn, qlk, qlmn, dk, dmn, dlk, dlmn;
+  rc = make_map(&qk, qkv, 3 * C, rows, 3 * C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&qmn, qkv, 3 * C, rows, 3 * C, kBKV, true);
+  if (rc == NS_OK) rc = make_map(&qlk, qkv_lo, 3 * C, rows, 3 * C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&qlmn, qkv_lo, 3 * C, rows, 3 * C, kBKV, true);
+  if (rc == NS_OK) rc = make_map(&dk, dout, C, rows, C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&dmn, dout, C, rows, C, kBKV, true);
+  if (rc == NS_OK) rc = make_map(&dlk, dout_lo, C, rows, C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&dlmn, dout_lo, C, rows, C, kBKV, true);
+  if (rc != NS_OK) return rc;
+  const float scale = 1.0f / sqrtf((float)D);
+  BwdParams p{qkv, dout, lse, delta, dqkv, T, H, C, scale, scale * kLog2e, 0, 0, 0};
+  {  // dV: Q (K-major), dO (MN-major)
+    const CUtensorMap m[6] = {qk, qlk, dmn, dlmn, dmn, dlmn};
+    p.xb0 = 0; p.xb1 = 0; p.xb2 = 0;
+    rc = launch_bwd_mode<kDV, D>(m, p, B, T, H, s);
+    if (rc != NS_OK) return rc;
+  }
+  {  // dK: Q (K-major), dO (K-major), Q (MN-major)
+    const CUtensorMap m[6] = {qk, qlk, dk, dlk, qmn, qlmn};
+    p.xb0 = 0; p.xb1 = 0; p.xb2 = 0;
+    rc = launch_bwd_mode<kDK, D>(m, p, B, T, H, s);
+    if (rc != NS_OK) return rc;
+  }
+  {  // dQ: K (K-major), V (K-major), K (MN-major)
+    const CUtensorMap m[6] = {qk, qlk, qk, qlk, qmn, qlmn};
+    p.xb0 = C; p.xb1 = 2 * C; p.xb2 = C;
+    rc = launch_bwd_mode<kDQ, D>(m, p, B, T, H, s);
+  }
+  return rc;
+}
+
 }  // namespace
 
 bool fwd_supported(const float* qkv, const float* out, int B, int T, int H, int D) {
@@ -513,6 +964,24 @@ ns_status fwd(const float* qkv, int B, int T, int H, int D, float* out, float* l
               cudaStream_t s) {
   return D == 64 ? launch_fwd<64>(qkv, B, T, H, out, lse, lo, s)
                  : launch_fwd<32>(qkv, B, T, H, out, lse, lo, s);
+}
+
+bool bwd_supported(const float* qkv, const float* dout, const float* dqkv, int B, int T, int H,
+                   int D) {
+  if (((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dqkv)) & 15) != 0) return false;
+  return fwd_supported(qkv, qkv, B, T, H, D);
+}
+
+size_t bwd_lo_bytes(int B, int T, int H, int D) {
+  return (size_t)B * T * 4 * H * D * sizeof(float);
+}
+
+ns_status bwd(const float* qkv, const float* dout, const float* lse, const float* delta, int B,
+              int T, int H, int D, float* dqkv, float* lo, cudaStream_t s) {
+  float* qkv_lo = lo;
+  float* dout_lo = lo + (size_t)B * T * 3 * H * D;
+  return D == 64 ? launch_bwd<64>(qkv, dout, lse, delta, B, T, H, dqkv, qkv_lo, dout_lo, s)
+                 : launch_bwd<32>(qkv, dout, lse, delta, B, T, H, dqkv, qkv_lo, dout_lo, s);
 }
 
 int consume_timeout_flag() {

@@ -17,6 +17,19 @@ size_t fwd_workspace_bytes(int B, int T, int H, int D);
 ns_status fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse, float* lo,
               cudaStream_t s);
 
+// True when the tensor-core backward handles this shape (as forward, plus
+// 16-byte aligned dout and dqkv).
+bool bwd_supported(const float* qkv, const float* dout, const float* dqkv, int B, int T, int H,
+                   int D);
+
+// Bytes of the lo-part copies of qkv and dout the tensor-core backward needs.
+size_t bwd_lo_bytes(int B, int T, int H, int D);
+
+// dqkv from qkv, dout, lse and delta (= rowsum(dout * out)); `lo` holds
+// bwd_lo_bytes, 16-byte aligned.
+ns_status bwd(const float* qkv, const float* dout, const float* lse, const float* delta, int B,
+              int T, int H, int D, float* dqkv, float* lo, cudaStream_t s);
+
 // 1 if an attention kernel hit a bounded-wait timeout since the last call (clears it).
 int consume_timeout_flag();
 
