@@ -12,7 +12,7 @@
 namespace nsb {
 namespace {
 
-thread_local int t_engine = 0;  // 0 auto, 1 SIMT
+thread_local int t_engine = 0;  // 0 auto, 1 SIMT, 2 tcgen05 with in-kernel operand split
 
 constexpr int kSB = 64, kSK = 16;
 
@@ -97,12 +97,17 @@ extern "C" {
 
 size_t ns_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const tc::Plan p = tc::plan(M, N, K, true);
-  return ((tc::split_workspace_bytes(p, M, N) + 255) & ~(size_t)255) + tc::lo_workspace_bytes(M, N, K);
+  // Enough for either plan: wide tiles (pre-split) or 128-wide tiles.
+  size_t part = 0;
+  for (bool wide : {true, false}) {
+    const tc::Plan p = tc::plan(M, N, K, true, wide);
+    part = std::max(part, (tc::split_workspace_bytes(p, M, N) + 255) & ~(size_t)255);
+  }
+  return part + tc::lo_workspace_bytes(M, N, K);
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine == 0 || engine == 1, "ns_gemm_set_engine: engine must be 0 or 1");
+  NS_REQUIRE(engine >= 0 && engine <= 2, "ns_gemm_set_engine: engine must be 0, 1 or 2");
   t_engine = engine;
   return NS_OK;
 }
@@ -129,19 +134,34 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
   if (K == 0 || !use_tc(M, N, K, A, lda, B, ldb))
     return gemm_simt(M, N, K, A, lda, a_trans, B, ldb, b_trans, e, s);
   // Workspace: [split-K partials | lo(A) | lo(B)], each part used only if it fits.
-  tc::Plan pl = tc::plan(M, N, K, true);
+  // The pre-split path (lo parts written by a split pass, loaded by TMA) allows
+  // 128 x 256 tiles; otherwise the kernel splits in shared memory.
   const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
-  size_t part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
-  if (!ws_ok || part > workspace_bytes) {
-    pl = tc::plan(M, N, K, false);
-    part = 0;
-  }
-  // The pre-split path needs 16-byte rows for the compact lo copies.
-  const int a_cols = a_trans ? M : K, b_cols = b_trans ? K : N;
+  const int a_cols = a_trans ? M : K, b_cols = b_trans ? K : N;  // lo copies need 16-byte rows
+  const bool pre_ok = t_engine == 0 && ws_ok && a_cols % 4 == 0 && b_cols % 4 == 0;
+  const size_t lo_bytes = tc::lo_workspace_bytes(M, N, K);
+  tc::Plan pl{};
+  size_t part = 0;
   float* lo = nullptr;
-  if (ws_ok && part + tc::lo_workspace_bytes(M, N, K) <= workspace_bytes && a_cols % 4 == 0 &&
-      b_cols % 4 == 0)
-    lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
+  bool chosen = false;
+  for (bool wide : {true, false}) {
+    if (!pre_ok) break;
+    pl = tc::plan(M, N, K, true, wide);
+    part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
+    if (part + lo_bytes <= workspace_bytes) {
+      lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
+      chosen = true;
+      break;
+    }
+  }
+  if (!chosen) {
+    pl = tc::plan(M, N, K, ws_ok, false);
+    part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
+    if (!ws_ok || part > workspace_bytes) {
+      pl = tc::plan(M, N, K, false, false);
+      part = 0;
+    }
+  }
   return tc::run(pl, M, N, K, A, lda, a_trans, B, ldb, b_trans ? 0 : 1, e,
                  static_cast<float*>(workspace), lo, s);
 }

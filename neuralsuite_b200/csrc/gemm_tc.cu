@@ -16,7 +16,8 @@
 //               fp32 tile as its tf32 "hi" part (it ignores the 13 low
 //               mantissa bits), so the hi.hi product starts as soon as the TMA
 //               lands and only the two lo products wait for the split.
-//   warps 4-7   fold + epilogue: the tensor core accumulates with
+//   warps 4-7   fold + epilogue (with pre-split operands warps 8-11 join
+//               them, each group on half of the columns): the tensor core accumulates with
 //               round-toward-zero, so every 2 k-blocks the MMA switches to a
 //               fresh chunk buffer and these warps add the finished chunk into
 //               the tile's running sum with round-to-nearest (TMEM ld/st);
@@ -45,7 +46,11 @@ using namespace tcx;
 
 constexpr int kThreads = 384;
 constexpr int kSplitThreads = 192;  // warps 2, 3, 8, 9, 10, 11
-constexpr int kEpiThreads = 128;    // warps 4..7 (TMEM lanes 0..127)
+// Fold + epilogue warps: 4..7 (TMEM lanes 0..127, all columns); with
+// pre-split operands the split warps are free and warps 8..11 take the upper
+// half of the columns.
+template <bool PRE>
+constexpr int kEpiThreads = PRE ? 256 : 128;
 
 struct KParams {
   int M, N, K;
@@ -85,15 +90,20 @@ __device__ __forceinline__ void decode_unit(const KParams& p, int u, int& tm, in
 // error at the level of a sequential fp32 loop whatever K is.
 constexpr int kChunk = 2;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PRE>
 struct Layout {
   static_assert(BN == 128, "TMEM holds 2 running sums + 2 chunk buffers of 128 columns");
   static constexpr uint32_t kA = kBM * kBK * 4;  // 16 KB
   static constexpr uint32_t kB = BN * kBK * 4;
-  static constexpr uint32_t kRaw = kA + kB;        // raw A | raw B
-  static constexpr uint32_t kStage = 2 * kRaw;     // then lo A | lo B
-  static constexpr uint32_t kBars = STAGES * kStage;
-  static constexpr uint32_t kNumBars = 3 * STAGES + 9;
+  static constexpr uint32_t kRaw = kA + kB;  // raw A | raw B
+  // PRE: each stage holds raw A | raw B | lo A | lo B, all loaded by TMA.
+  // Otherwise stages hold the raw tiles only, and the split warps write the lo
+  // parts into a separate 2-deep ring: the TMA ring then runs deeper for the
+  // same shared memory and moves half the bytes.
+  static constexpr uint32_t kStage = PRE ? 2 * kRaw : kRaw;
+  static constexpr uint32_t kLoRing = STAGES * kStage;
+  static constexpr uint32_t kBars = kLoRing + (PRE ? 0 : 2 * kRaw);
+  static constexpr uint32_t kNumBars = 2 * STAGES + 13;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;  // alignment slack
   // columns [0,BN) and [BN,2BN): running sums R0, R1 (one per tile in flight);
@@ -110,20 +120,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBlo, const KParams p) {
-  using L = Layout<BN, STAGES>;
+  using L = Layout<BN, STAGES, PRE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBars;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto split_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (2 * STAGES + s); };
-  auto accf_bar = [&](int a) { return bar0 + 8u * (3 * STAGES + a); };      // running sum done
-  auto acce_bar = [&](int a) { return bar0 + 8u * (3 * STAGES + 2 + a); };  // running sum drained
-  auto chf_bar = [&](int c) { return bar0 + 8u * (3 * STAGES + 4 + c); };   // chunk written
-  auto che_bar = [&](int c) { return bar0 + 8u * (3 * STAGES + 6 + c); };   // chunk folded
-  const uint32_t drain_bar = bar0 + 8u * (3 * STAGES + 8);
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto lof_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };       // lo ring written
+  auto loe_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };   // lo ring read
+  auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 4 + a); };  // running sum done
+  auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 6 + a); };  // running sum drained
+  auto chf_bar = [&](int c) { return bar0 + 8u * (2 * STAGES + 8 + c); };   // chunk written
+  auto che_bar = [&](int c) { return bar0 + 8u * (2 * STAGES + 10 + c); };  // chunk folded
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 12);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -131,14 +142,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(split_bar(s), kSplitThreads);
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
+      mbar_init(lof_bar(a), kSplitThreads);
+      mbar_init(loe_bar(a), 1);
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), kEpiThreads);
+      mbar_init(acce_bar(a), kEpiThreads<PRE>);
       mbar_init(chf_bar(a), 1);
-      mbar_init(che_bar(a), kEpiThreads);
+      mbar_init(che_bar(a), kEpiThreads<PRE>);
     }
     mbar_init(drain_bar, 1);
     *abort = 0;
@@ -243,7 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ph = (it / STAGES) & 1u;
           const uint32_t a_raw = sbase + s * L::kStage;
           const uint32_t b_raw = a_raw + L::kA;
-          const uint32_t a_lo = a_raw + L::kRaw;
+          const int lb = it & 1;
+          const uint32_t a_lo = PRE ? a_raw + L::kRaw : sbase + L::kLoRing + lb * L::kRaw;
           const uint32_t b_lo = a_lo + L::kA;
           if (!warp_wait(full_bar(s), ph, abort, &g_timeout)) {
             ok = false;
@@ -258,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
           if (!PRE) {
-            if (!warp_wait(split_bar(s), ph, abort, &g_timeout)) {
+            if (!warp_wait(lof_bar(lb), (it >> 1) & 1u, abort, &g_timeout)) {
               ok = false;
               break;
             }
@@ -273,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      idesc, 1u);
             }
             commit(empty_bar(s));
+            if (!PRE) commit(loe_bar(lb));
           }
           __syncwarp();
         }
@@ -293,10 +307,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       mbar_wait_drain(drain_bar, 0, &g_timeout);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && (PRE || warp < 8)) {
     // ------------------------------------------------------------ fold + epilogue
-    const int ew = warp - 4;  // TMEM lanes 32*ew .. 32*ew+31
+    const int ew = warp & 3;  // TMEM lanes 32*ew .. 32*ew+31
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    constexpr int kGroupCols = PRE ? BN / 2 : BN;  // columns this warp folds and stores
+    const int col0 = PRE ? (warp >> 3) * kGroupCols : 0;
     uint32_t uit = 0, cit = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++uit) {
@@ -314,14 +330,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         const uint32_t c_tmem = tmem_base + lane_off + (2 + cb) * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = col0; c < col0 + kGroupCols; c += 32) {
           uint32_t a[32], b[32];
-          tmem_ld32(c_tmem + c * 32, a);
-          tmem_ld32(r_tmem + c * 32, b);
+          tmem_ld32_nowait(c_tmem + c, a);
+          tmem_ld32_nowait(r_tmem + c, b);
+          tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             b[j] = __float_as_uint(__fadd_rn(__uint_as_float(b[j]), __uint_as_float(a[j])));
-          tmem_st32(r_tmem + c * 32, b);
+          tmem_st32(r_tmem + c, b);
         }
         tmem_wait_st();
         fence_before();
@@ -333,10 +350,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = tm * kBM + ew * 32 + lane;
       const int n_base = tn * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = col0; c < col0 + kGroupCols; c += 32) {
         uint32_t v[32];
-        tmem_ld32(r_tmem + c * 32, v);
-        const int n0 = n_base + c * 32;
+        tmem_ld32(r_tmem + c, v);
+        const int n0 = n_base + c;
         if (m < p.M && n0 < p.N) {
           if (p.splits > 1) {
             float* dst = p.ws + ((size_t)split * p.M + m) * p.N + n0;
@@ -374,12 +391,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        if (!mbar_wait(full_bar(s), ph, abort, &g_timeout)) {
+        const int lb = it & 1;
+        if (!mbar_wait(full_bar(s), ph, abort, &g_timeout) ||
+            !mbar_wait(loe_bar(lb), ((it >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
           ok = false;
           break;
         }
         const float4* raw = reinterpret_cast<const float4*>(smem + s * L::kStage);
-        float4* lo = reinterpret_cast<float4*>(smem + s * L::kStage + L::kRaw);
+        float4* lo = reinterpret_cast<float4*>(smem + L::kLoRing + lb * L::kRaw);
 #pragma unroll 4
         for (int i = tt; i < (int)(L::kRaw / 16); i += kSplitThreads) {
           const float4 x = raw[i];
@@ -391,7 +410,276 @@ __global__ void __launch_bounds__(kThreads, 1)
           lo[i] = r;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(split_bar(s));
+        mbar_arrive(lof_bar(lb));
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- wide tiles
+//
+// 128 x 256 tiles (N=256 MMAs) for the pre-split path.  Each 3xTF32 k-step
+// reads its operands from shared memory three times, and at 128 x 128 those
+// reads plus the TMA writes exceed what shared memory delivers while the
+// tensor core runs at full rate; an N=256 MMA reads the A slice once for
+// twice the work.  TMEM then holds two 256-column chunk buffers and nothing
+// else: the running sums live in the registers of the eight fold warps
+// (warps 4-7 columns 0-127, warps 8-11 columns 128-255), which add each
+// finished chunk with round-to-nearest and store the tile from registers.
+// The MMA runs up to two chunks ahead of the folds, which covers a tile's
+// epilogue.
+constexpr int kWideBN = 256;
+constexpr int kWideStages = 2;
+constexpr int kWideThreads = 384;
+constexpr int kWideFoldThreads = 256;
+constexpr int kWideLowRegs = 48, kWideHighRegs = 216;
+constexpr int kWideMinLaunchRegs =
+    (4 * 32 * kWideLowRegs + 8 * 32 * kWideHighRegs + kWideThreads - 1) / kWideThreads;
+
+struct WideLayout {
+  static constexpr uint32_t kA = kBM * kBK * 4;      // 16 KB
+  static constexpr uint32_t kB = kWideBN * kBK * 4;  // 32 KB
+  static constexpr uint32_t kRaw = kA + kB;
+  static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
+  static constexpr uint32_t kBars = kWideStages * kStage;
+  static constexpr uint32_t kNumBars = 2 * kWideStages + 5;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * kWideBN;  // chunk buffers C0, C1
+  static_assert(kDynSmem <= 232448, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(kWideThreads, 1)
+    gemm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmAlo,
+                     const __grid_constant__ CUtensorMap tmBlo, const KParams p) {
+  using L = WideLayout;
+  constexpr int S = kWideStages;
+  constexpr int BN = kWideBN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  auto chf_bar = [&](int c) { return bar0 + 8u * (2 * S + c); };      // chunk written
+  auto che_bar = [&](int c) { return bar0 + 8u * (2 * S + 2 + c); };  // chunk folded
+  const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(chf_bar(c), 1);
+      mbar_init(che_bar(c), kWideFoldThreads);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int n_units = p.tiles_m * p.tiles_n * p.splits;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWideLowRegs));
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        uint32_t it = 0;
+        int issued[S];
+        uint32_t issued_ph[S];
+        for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+          int tm, tn, split, kb0, kb1;
+          decode_unit(p, u, tm, tn, split, kb0, kb1);
+          const int m0 = tm * kBM, n0 = tn * BN;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1u;
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(full_bar(s), 2 * L::kRaw);
+            issued[s] = 1;
+            issued_ph[s] = ph;
+            const uint32_t a_dst = sbase + s * L::kStage;
+            const uint32_t b_dst = a_dst + L::kA;
+            const int k0 = kb * kBK;
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+              const CUtensorMap* ma = part ? &tmAlo : &tmA;
+              const CUtensorMap* mb = part ? &tmBlo : &tmB;
+              const uint32_t off = part ? L::kRaw : 0u;
+              if (!p.a_mn) {
+                tma_load_2d(a_dst + off, ma, full_bar(s), k0, m0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < kBM / 32; ++j)
+                  tma_load_2d(a_dst + off + j * 4096, ma, full_bar(s), m0 + 32 * j, k0);
+              }
+              if (!p.b_mn) {
+                tma_load_2d(b_dst + off, mb, full_bar(s), k0, n0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BN / 32; ++j)
+                  tma_load_2d(b_dst + off + j * 4096, mb, full_bar(s), n0 + 32 * j, k0);
+              }
+            }
+          }
+        }
+        if (!ok)
+          for (int s = 0; s < S; ++s)
+            if (issued[s]) mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
+      }
+    } else if (warp == 1) {
+      // ---------------------------------------------------------- MMA issuer
+      const uint32_t idesc = instr_desc(BN, p.a_mn, p.b_mn);
+      uint32_t it = 0, cit = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        int tm, tn, split, kb0, kb1;
+        decode_unit(p, u, tm, tn, split, kb0, kb1);
+        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk, ++cit) {
+          const int cb = cit & 1;
+          if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t d_tmem = tmem_base + cb * BN;
+          const int c1 = min(kb1, c0 + kChunk);
+          for (int kb = c0; kb < c1; ++kb, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1u;
+            if (!warp_wait(full_bar(s), ph, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            if (elect_one()) {
+              const uint32_t a_raw = sbase + s * L::kStage;
+              const uint32_t b_raw = a_raw + L::kA;
+              const uint32_t a_lo = a_raw + L::kRaw;
+              const uint32_t b_lo = a_lo + L::kA;
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk)
+                mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                       idesc, (kb > c0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk) {
+                mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
+                       idesc, 1u);
+                mma_ss(d_tmem, operand_desc(a_lo, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                       idesc, 1u);
+              }
+              commit(empty_bar(s));
+            }
+            __syncwarp();
+          }
+          if (!ok) break;
+          if (elect_one()) commit(chf_bar(cb));
+          __syncwarp();
+        }
+      }
+      if (!ok) {
+        if (elect_one()) commit(drain_bar);
+        __syncwarp();
+        mbar_wait_drain(drain_bar, 0, &g_timeout);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ fold + epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWideHighRegs));
+    const int ew = warp & 3;                 // TMEM lanes 32*ew .. 32*ew+31
+    const int col0 = ((warp - 4) >> 2) * 128;  // columns of this warp group
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    uint32_t cit = 0;
+    bool ok = true;
+    float acc[128];
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+      int tm, tn, split, kb0, kb1;
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int c0 = kb0; c0 < kb1; c0 += kChunk, ++cit) {
+        const int cb = cit & 1;
+        if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t c_tmem = tmem_base + lane_off + cb * BN + col0;
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t a[32], b[32];
+          tmem_ld32_nowait(c_tmem + 32 * c, a);
+          tmem_ld32_nowait(c_tmem + 32 * (c + 1), b);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            acc[32 * c + j] = __fadd_rn(acc[32 * c + j], __uint_as_float(a[j]));
+            acc[32 * (c + 1) + j] = __fadd_rn(acc[32 * (c + 1) + j], __uint_as_float(b[j]));
+          }
+        }
+        fence_before();
+        mbar_arrive(che_bar(cb));
+      }
+      if (!ok) break;
+      const int m = tm * kBM + ew * 32 + lane;
+      const int n_base = tn * BN + col0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int n0 = n_base + c * 32;
+        if (m < p.M && n0 < p.N) {
+          const float* v = acc + 32 * c;
+          if (p.splits > 1) {
+            float* dst = p.ws + ((size_t)split * p.M + m) * p.N + n0;
+            if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N) dst[j] = v[j];
+            }
+          } else if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              epi_store4(p.e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
+          }
+        }
       }
     }
   }
@@ -463,13 +751,29 @@ template <int BN, int STAGES, bool PRE>
 ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
                  const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
                  cudaStream_t s) {
-  using L = Layout<BN, STAGES>;
+  using L = Layout<BN, STAGES, PRE>;
   static_assert(L::kDynSmem <= 232448, "shared memory budget");
   NS_TRY_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, STAGES, PRE>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
               "ns_gemm attr");
   gemm_tf32x3_kernel<BN, STAGES, PRE><<<pl.grid, kThreads, L::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
   return check_launch("ns_gemm tcgen05");
+}
+
+ns_status launch_wide(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
+                      cudaStream_t s) {
+  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)WideLayout::kDynSmem),
+              "ns_gemm attr");
+  // setmaxnreg.inc would wait forever if the launch held fewer registers than
+  // the split hands out.
+  cudaFuncAttributes fa;
+  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_wide_kernel), "ns_gemm attributes");
+  if (fa.numRegs < kWideMinLaunchRegs)
+    return fail(NS_ERR_UNSUPPORTED, "ns_gemm: wide kernel compiled with too few registers for its split");
+  gemm_wide_kernel<<<pl.grid, kWideThreads, WideLayout::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
+  return check_launch("ns_gemm tcgen05 wide");
 }
 
 ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {
@@ -484,29 +788,32 @@ ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaSt
 
 }  // namespace
 
-Plan plan(int M, int N, int K, bool allow_split) {
+Plan plan(int M, int N, int K, bool allow_split, bool allow_wide) {
   const int sms = sm_count();
   const int kb_total = std::max(1, ceil_div(K, kBK));
   Plan best{};
   double best_cost = 1e30;
-  for (int bn : {128}) {
+  for (int bn : {128, 256}) {
+    if (bn == 256 && !allow_wide) continue;
     const int tiles_m = ceil_div(M, kBM), tiles_n = ceil_div(N, bn);
     const int tiles = tiles_m * tiles_n;
     const int max_split = allow_split ? std::min(kb_total, 16) : 1;
+    // Measured k-block times (cycles): 128 x 128 tiles are bound by shared-memory
+    // operand traffic near 1600, 128 x 256 tiles by the 2-stage TMA ring.
+    const double kb_cycles = bn == 128 ? 1600.0 : 2300.0;
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kb_per = ceil_div(kb_total, sp);
       const int splits = ceil_div(kb_total, kb_per);
       if (splits != sp) continue;
       const int units = tiles * splits;
       const int waves = ceil_div(units, sms);
-      // cycles: 12 MMAs of N=bn per k-block (bn/2 cycles each) + fixed cost per unit
-      double cost = (double)waves * ((double)kb_per * 6.0 * bn + 3000.0);
+      double cost = (double)waves * ((double)kb_per * kb_cycles + 3000.0);
       if (splits > 1)  // partial tiles out and back in, ~5 TB/s at ~1.9 GHz
         cost += (double)(2 * splits + 1) * M * (double)N * 4.0 / 5e12 * 1.9e9;
       if (cost < best_cost * 0.98) {
         best_cost = cost;
         best.bn = bn;
-        best.stages = 3;
+        best.stages = bn == 128 ? 3 : kWideStages;
         best.tiles_m = tiles_m;
         best.tiles_n = tiles_n;
         best.splits = splits;
@@ -568,8 +875,10 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                        reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
                        reinterpret_cast<uintptr_t>(ws);
   kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
-  rc = pre ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
-           : launch<128, 3, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
+  if (pl.bn == kWideBN && !pre) return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
+  rc = pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
+       : pre            ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
+                        : launch<128, 5, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
   if (rc != NS_OK || pl.splits == 1) return rc;
   const int64_t total = (int64_t)M * N;
   const int vec = kp.vec_ok;

@@ -22,7 +22,8 @@ struct Plan {
   int grid;        // persistent CTAs
 };
 
-Plan plan(int M, int N, int K, bool allow_split);
+// allow_wide: 128 x 256 tiles may be chosen (they need pre-split operands).
+Plan plan(int M, int N, int K, bool allow_split, bool allow_wide);
 size_t split_workspace_bytes(const Plan& p, int M, int N);
 
 size_t lo_elems_a(int M, int K);

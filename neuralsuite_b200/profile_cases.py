@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profilers (ncu) and quick timing.
 
-    python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps]
+    python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps [engine]]
     python -m neuralsuite_b200.profile_cases attn B T H D [reps [engine]]
     python -m neuralsuite_b200.profile_cases ln ROWS DIM [reps]
 
@@ -38,6 +38,8 @@ def main(argv):
         at = int(argv[4]) if len(argv) > 4 else 0
         bt = int(argv[5]) if len(argv) > 5 else 0
         reps = int(argv[6]) if len(argv) > 6 else 3
+        if len(argv) > 7:
+            nk.set_gemm_engine(int(argv[7]))
         A = torch.randn((K, M) if at else (M, K), device=dev)
         B = torch.randn((N, K) if bt else (K, N), device=dev)
         out = torch.empty(M, N, device=dev)

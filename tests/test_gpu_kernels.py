@@ -70,15 +70,23 @@ def test_gemm_tf32_split_recovers_fp32(cuda):
 FULL = [(8192, 768, 3072), (8192, 3072, 768), (16384, 1024, 4096)]
 
 
+@pytest.fixture(params=[0, 2], ids=["presplit", "inkernel"])
+def gemm_engine(request):
+    nk.set_gemm_engine(request.param)
+    yield request.param
+    nk.set_gemm_engine(0)
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("M,K,N", FULL)
-def test_gemm_sweep_full(cuda, M, K, N):
+def test_gemm_sweep_full(cuda, gemm_engine, M, K, N):
     """The MatMul sweep shapes: every form against float64.  Relative L2
     error <= 5e-6 (the reference's own bar for its fast-vs-literal attention
     is 1e-5, test_suite.cpp:3148-3150; an fp32 k-sequential loop lands near
     1e-6 here) and, per element, within 1e-4 relative of the float64 value
     wherever |value| >= 0.1 * rms (smaller values carry the same absolute
-    rounding as any fp32 accumulation of K products)."""
+    rounding as any fp32 accumulation of K products).  Both tcgen05 operand
+    paths: lo parts pre-split into the workspace, and split in the kernel."""
     r = rng(M + K + N)
     X, W, dY = normal(r, (M, K)), normal(r, (K, N)), normal(r, (M, N))
     Xd, Wd, dYd = dev(X, cuda), dev(W, cuda), dev(dY, cuda)
@@ -108,7 +116,7 @@ def test_gemm_engines_agree_and_epilogues(cuda, port):
     Xd, Wd, bd, Rd = dev(X, cuda), dev(W, cuda), dev(b, cuda), dev(R, cuda)
     base = port.matmul(X, W)
     base64 = fp64.matmul(X, W)
-    for engine in (0, 1):
+    for engine in (0, 1, 2):
         nk.set_gemm_engine(engine)
         try:
             y = host(nk.gemm(Xd, Wd, epilogue=_lib.EPI_BIAS, bias=bd))
