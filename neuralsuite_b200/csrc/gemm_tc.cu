@@ -451,7 +451,7 @@ struct WideLayout {
   static constexpr uint32_t kRaw = kA + kB;
   static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
   static constexpr uint32_t kBars = kWideStages * kStage;
-  static constexpr uint32_t kNumBars = 2 * kWideStages + 5;
+  static constexpr uint32_t kNumBars = 3 * kWideStages + 5;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 2 * kWideBN;  // chunk buffers C0, C1
@@ -470,11 +470,14 @@ __global__ void __launch_bounds__(kWideThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBars;
+  // Raw and lo tiles of a stage land on separate barriers: the hi.hi MMAs
+  // (a third of the work) start while the lo tiles are still in flight.
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
-  auto chf_bar = [&](int c) { return bar0 + 8u * (2 * S + c); };      // chunk written
-  auto che_bar = [&](int c) { return bar0 + 8u * (2 * S + 2 + c); };  // chunk folded
-  const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
+  auto lofull_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (2 * S + s); };
+  auto chf_bar = [&](int c) { return bar0 + 8u * (3 * S + c); };      // chunk written
+  auto che_bar = [&](int c) { return bar0 + 8u * (3 * S + 2 + c); };  // chunk folded
+  const uint32_t drain_bar = bar0 + 8u * (3 * S + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -482,6 +485,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
+      mbar_init(lofull_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
     for (int c = 0; c < 2; ++c) {
@@ -526,7 +530,8 @@ __global__ void __launch_bounds__(kWideThreads, 1)
               ok = false;
               break;
             }
-            mbar_expect_tx(full_bar(s), 2 * L::kRaw);
+            mbar_expect_tx(full_bar(s), L::kRaw);
+            mbar_expect_tx(lofull_bar(s), L::kRaw);
             issued[s] = 1;
             issued_ph[s] = ph;
             const uint32_t a_dst = sbase + s * L::kStage;
@@ -537,26 +542,30 @@ __global__ void __launch_bounds__(kWideThreads, 1)
               const CUtensorMap* ma = part ? &tmAlo : &tmA;
               const CUtensorMap* mb = part ? &tmBlo : &tmB;
               const uint32_t off = part ? L::kRaw : 0u;
+              const uint32_t bar = part ? lofull_bar(s) : full_bar(s);
               if (!p.a_mn) {
-                tma_load_2d(a_dst + off, ma, full_bar(s), k0, m0);
+                tma_load_2d(a_dst + off, ma, bar, k0, m0);
               } else {
 #pragma unroll
                 for (int j = 0; j < kBM / 32; ++j)
-                  tma_load_2d(a_dst + off + j * 4096, ma, full_bar(s), m0 + 32 * j, k0);
+                  tma_load_2d(a_dst + off + j * 4096, ma, bar, m0 + 32 * j, k0);
               }
               if (!p.b_mn) {
-                tma_load_2d(b_dst + off, mb, full_bar(s), k0, n0);
+                tma_load_2d(b_dst + off, mb, bar, k0, n0);
               } else {
 #pragma unroll
                 for (int j = 0; j < BN / 32; ++j)
-                  tma_load_2d(b_dst + off + j * 4096, mb, full_bar(s), n0 + 32 * j, k0);
+                  tma_load_2d(b_dst + off + j * 4096, mb, bar, n0 + 32 * j, k0);
               }
             }
           }
         }
         if (!ok)
           for (int s = 0; s < S; ++s)
-            if (issued[s]) mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
+            if (issued[s]) {
+              mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
+              mbar_wait_drain(lofull_bar(s), issued_ph[s], &g_timeout);
+            }
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
@@ -583,15 +592,23 @@ __global__ void __launch_bounds__(kWideThreads, 1)
               break;
             }
             fence_after();
+            const uint32_t a_raw = sbase + s * L::kStage;
+            const uint32_t b_raw = a_raw + L::kA;
+            const uint32_t a_lo = a_raw + L::kRaw;
+            const uint32_t b_lo = a_lo + L::kA;
             if (elect_one()) {
-              const uint32_t a_raw = sbase + s * L::kStage;
-              const uint32_t b_raw = a_raw + L::kA;
-              const uint32_t a_lo = a_raw + L::kRaw;
-              const uint32_t b_lo = a_lo + L::kA;
 #pragma unroll
               for (int kk = 0; kk < kBK / 8; ++kk)
                 mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
                        idesc, (kb > c0 || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
+            if (!warp_wait(lofull_bar(s), ph, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            if (elect_one()) {
 #pragma unroll
               for (int kk = 0; kk < kBK / 8; ++kk) {
                 mma_ss(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
