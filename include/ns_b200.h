@@ -99,6 +99,24 @@ NS_API ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_tra
                   int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
                   const float* bias, const float* aux, float* aux_out, void* workspace,
                   size_t workspace_bytes, void* stream);
+/* lo = x - trunc_tf32(x) for a [rows, cols] matrix with row stride ld, written
+ * compact (row stride cols): the low part of the 3xTF32 operand split that
+ * ns_gemm otherwise computes into its workspace on every call.  Callers that
+ * feed one operand to several products (an activation to its forward GEMM and
+ * its weight-gradient GEMM; a weight to its forward and input-gradient GEMMs)
+ * split it once and pass the copy to ns_gemm_lo.  cols must be a multiple of 4
+ * and lo 16-byte aligned for ns_gemm_lo to use it.  No reference counterpart
+ * (part of the MatMul implementation, src/tensor.cpp:198-271). */
+NS_API ns_status ns_split_lo(const float* x, int rows, int cols, int ld, float* lo, void* stream);
+/* ns_gemm with the operands' lo parts supplied: a_lo is ns_split_lo of A as
+ * stored ([M,K], or [K,M] with a_trans), b_lo likewise of B ([K,N] or [N,K]).
+ * Either may be NULL; a missing one is split into the workspace as ns_gemm
+ * does.  Same results as ns_gemm, bit for bit. */
+NS_API ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_trans,
+                     const float* a_lo, const float* B, int ldb, int b_trans, const float* b_lo,
+                     float* C, int ldc, float beta, int epilogue, const float* bias,
+                     const float* aux, float* aux_out, void* workspace, size_t workspace_bytes,
+                     void* stream);
 /* Selects the GEMM engine for subsequent calls on this thread: 0 = automatic
  * (tcgen05 wherever the operands allow TMA, SIMT fp32 otherwise), 1 = always
  * the SIMT fp32 kernel, 2 = tcgen05 with the operands' tf32 lo parts always

@@ -49,6 +49,9 @@ _SIGS = {
     "ns_gemm_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "ns_gemm": (c_int, [c_int, c_int, c_int, P, c_int, c_int, P, c_int, c_int, P, c_int, c_float,
                         c_int, P, P, P, P, c_size_t, P]),
+    "ns_gemm_lo": (c_int, [c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P, P, c_int,
+                           c_float, c_int, P, P, P, P, c_size_t, P]),
+    "ns_split_lo": (c_int, [P, c_int, c_int, c_int, P, P]),
     "ns_gemm_set_engine": (c_int, [c_int]),
     "ns_kernel_health": (c_int, []),
     "ns_bias_grad_workspace_size": (c_size_t, [c_int, c_int]),

@@ -112,10 +112,14 @@ ns_status ns_gemm_set_engine(int engine) {
   return NS_OK;
 }
 
-ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
-                  int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
-                  const float* bias, const float* aux, float* aux_out, void* workspace,
-                  size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
+                    int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
+                    const float* bias, const float* aux, float* aux_out, const float* a_lo_in,
+                    const float* b_lo_in, void* workspace, size_t workspace_bytes, void* stream) {
   NS_REQUIRE(M >= 0 && N >= 0 && K >= 0, "ns_gemm: negative dimension");
   NS_REQUIRE(epilogue >= NS_EPI_STORE && epilogue <= NS_EPI_GELU_BWD, "ns_gemm: unknown epilogue");
   NS_REQUIRE(beta == 0.0f || beta == 1.0f, "ns_gemm: beta must be 0 or 1");
@@ -128,33 +132,44 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
   NS_REQUIRE(!(epilogue == NS_EPI_BIAS_RESID || epilogue == NS_EPI_GELU_BWD) || aux,
              "ns_gemm: epilogue needs aux");
   NS_REQUIRE(epilogue != NS_EPI_BIAS_GELU || aux_out, "ns_gemm: epilogue needs aux_out");
+  const int a_cols = a_trans ? M : K, b_cols = b_trans ? K : N;  // lo copies need 16-byte rows
+  NS_REQUIRE(!a_lo_in || (a_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(a_lo_in) & 15) == 0),
+             "ns_gemm_lo: a_lo needs 16-byte aligned rows (stored columns a multiple of 4)");
+  NS_REQUIRE(!b_lo_in || (b_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(b_lo_in) & 15) == 0),
+             "ns_gemm_lo: b_lo needs 16-byte aligned rows (stored columns a multiple of 4)");
   if (M == 0 || N == 0) return NS_OK;
   EpiArgs e{C, ldc, epilogue, beta, bias, aux, aux_out};
   cudaStream_t s = as_stream(stream);
   if (K == 0 || !use_tc(M, N, K, A, lda, B, ldb))
     return gemm_simt(M, N, K, A, lda, a_trans, B, ldb, b_trans, e, s);
-  // Workspace: [split-K partials | lo(A) | lo(B)], each part used only if it fits.
-  // The pre-split path (lo parts written by a split pass, loaded by TMA) allows
-  // 128 x 256 tiles; otherwise the kernel splits in shared memory.
+  // Workspace: [split-K partials | lo(A) | lo(B)], each part used only if it fits
+  // (lo parts the caller supplies take no room).  The pre-split path (lo parts
+  // loaded by TMA) allows 128 x 256 tiles; otherwise the kernel splits in
+  // shared memory.
   const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
-  const int a_cols = a_trans ? M : K, b_cols = b_trans ? K : N;  // lo copies need 16-byte rows
-  const bool pre_ok = t_engine == 0 && ws_ok && a_cols % 4 == 0 && b_cols % 4 == 0;
-  const size_t lo_bytes = tc::lo_workspace_bytes(M, N, K);
+  const bool pre_ok = t_engine == 0 && a_cols % 4 == 0 && b_cols % 4 == 0;
+  const size_t lo_bytes = (a_lo_in ? 0 : tc::lo_elems_a(M, K) * sizeof(float)) +
+                          (b_lo_in ? 0 : (size_t)K * N * sizeof(float));
   tc::Plan pl{};
   size_t part = 0;
   float* lo = nullptr;
   bool chosen = false;
   for (bool wide : {true, false}) {
     if (!pre_ok) break;
-    pl = tc::plan(M, N, K, true, wide);
+    pl = tc::plan(M, N, K, ws_ok, wide);
     part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
-    if (part + lo_bytes <= workspace_bytes) {
-      lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
+    if (lo_bytes == 0 && part == 0) {
+      chosen = true;
+      break;
+    }
+    if (ws_ok && part + lo_bytes <= workspace_bytes) {
+      if (lo_bytes) lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
       chosen = true;
       break;
     }
   }
   if (!chosen) {
+    a_lo_in = b_lo_in = nullptr;
     pl = tc::plan(M, N, K, ws_ok, false);
     part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
     if (!ws_ok || part > workspace_bytes) {
@@ -163,7 +178,33 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
     }
   }
   return tc::run(pl, M, N, K, A, lda, a_trans, B, ldb, b_trans ? 0 : 1, e,
-                 static_cast<float*>(workspace), lo, s);
+                 static_cast<float*>(workspace), lo, a_lo_in, b_lo_in, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
+                  int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
+                  const float* bias, const float* aux, float* aux_out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  return gemm_impl(M, N, K, A, lda, a_trans, B, ldb, b_trans, C, ldc, beta, epilogue, bias, aux,
+                   aux_out, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_trans, const float* a_lo,
+                     const float* B, int ldb, int b_trans, const float* b_lo, float* C, int ldc,
+                     float beta, int epilogue, const float* bias, const float* aux,
+                     float* aux_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_impl(M, N, K, A, lda, a_trans, B, ldb, b_trans, C, ldc, beta, epilogue, bias, aux,
+                   aux_out, a_lo, b_lo, workspace, workspace_bytes, stream);
+}
+
+ns_status ns_split_lo(const float* x, int rows, int cols, int ld, float* lo, void* stream) {
+  NS_REQUIRE(rows >= 0 && cols >= 0 && ld >= cols, "ns_split_lo: bad shape");
+  if (rows == 0 || cols == 0) return NS_OK;
+  return tc::split_operand(x, rows, cols, ld, lo, as_stream(stream));
 }
 
 ns_status ns_kernel_health(void) {

@@ -855,7 +855,7 @@ size_t lo_workspace_bytes(int M, int N, int K) {
 
 ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
               const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws, float* lo_ws,
-              cudaStream_t stream) {
+              const float* a_lo_in, const float* b_lo_in, cudaStream_t stream) {
   CUtensorMap ta, tb, ta_lo, tb_lo;
   std::memset(&ta, 0, sizeof(ta));
   std::memset(&tb, 0, sizeof(tb));
@@ -865,17 +865,25 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   if (rc != NS_OK) return rc;
   rc = b_mn ? tcx::make_map(&tb, B, N, K, ldb, 32, true) : tcx::make_map(&tb, B, K, N, ldb, pl.bn, false);
   if (rc != NS_OK) return rc;
-  const bool pre = lo_ws != nullptr;
+  const bool pre = lo_ws != nullptr || (a_lo_in && b_lo_in);
   if (pre) {
-    // Compact lo copies: A as stored ([M,K] or [K,M]), then B as stored.
-    float* a_lo = lo_ws;
-    float* b_lo = lo_ws + lo_elems_a(M, K);
+    // Compact lo copies (A as stored, [M,K] or [K,M], then B as stored): the
+    // caller's where given, otherwise split into the workspace here.
     const int a_rows = a_mn ? K : M, a_cols = a_mn ? M : K;
     const int b_rows = b_mn ? K : N, b_cols = b_mn ? N : K;
-    rc = split_lo(A, a_rows, a_cols, lda, a_lo, stream);
-    if (rc != NS_OK) return rc;
-    rc = split_lo(B, b_rows, b_cols, ldb, b_lo, stream);
-    if (rc != NS_OK) return rc;
+    const float* a_lo = a_lo_in;
+    const float* b_lo = b_lo_in;
+    if (!a_lo) {
+      rc = split_lo(A, a_rows, a_cols, lda, lo_ws, stream);
+      if (rc != NS_OK) return rc;
+      a_lo = lo_ws;
+    }
+    if (!b_lo) {
+      float* dst = lo_ws + (a_lo_in ? 0 : lo_elems_a(M, K));
+      rc = split_lo(B, b_rows, b_cols, ldb, dst, stream);
+      if (rc != NS_OK) return rc;
+      b_lo = dst;
+    }
     rc = a_mn ? tcx::make_map(&ta_lo, a_lo, M, K, M, 32, true) : tcx::make_map(&ta_lo, a_lo, K, M, K, kBM, false);
     if (rc != NS_OK) return rc;
     rc = b_mn ? tcx::make_map(&tb_lo, b_lo, N, K, N, 32, true) : tcx::make_map(&tb_lo, b_lo, K, N, K, pl.bn, false);
@@ -903,6 +911,10 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
   splitk_reduce_k<<<grid, 256, 0, stream>>>(ws, pl.splits, M, N, e, vec);
   return check_launch("ns_gemm split-K reduce");
+}
+
+ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {
+  return split_lo(x, rows, cols, ld, lo, s);
 }
 
 int consume_timeout_flag() {

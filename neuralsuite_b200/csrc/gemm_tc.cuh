@@ -35,9 +35,14 @@ size_t lo_workspace_bytes(int M, int N, int K);
 // lo_workspace_bytes) the operands are split into hi/lo in global memory
 // first and the kernel loads both parts by TMA; without it the kernel splits
 // each tile in shared memory.
+// a_lo_in / b_lo_in: the caller's compact lo copies (optional); the missing
+// ones are split into lo_ws.
 ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
               const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws, float* lo_ws,
-              cudaStream_t stream);
+              const float* a_lo_in, const float* b_lo_in, cudaStream_t stream);
+
+// lo = x - trunc_tf32(x) of a [rows, cols] matrix with row stride ld, compact.
+ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s);
 
 // 1 if a kernel hit a bounded-wait timeout since the last call (clears it).
 int consume_timeout_flag();

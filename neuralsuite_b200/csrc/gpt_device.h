@@ -230,15 +230,30 @@ class Linear : public Layer {
   int Out() const { return out_; }
 
  private:
+  // The 3xTF32 GEMMs read each operand's tf32 lo part.  The input X feeds the
+  // forward product and the dW product, the weight W the forward and dX
+  // products, dY the dX and dW products: each is split once (ns_split_lo)
+  // and the copy passed to every product that reads it (ns_gemm_lo).
+  bool SplitOk() const { return in_ % 4 == 0 && out_ % 4 == 0; }
+
   Tensor Run(const Tensor& x, int epi, const float* aux, float* aux_out) {
     if (x.Shape().empty() || x.Shape().back() != in_)
       throw std::invalid_argument("Linear: the last axis of the input is not in_features");
     const int n = Rows(x, in_);
     last_input_ = x;
+    const float* x_lo = nullptr;
+    const float* w_lo = nullptr;
+    if (SplitOk()) {
+      Tensor xl = Scratch(x_lo_buf_, n, in_), wl = Scratch(w_lo_buf_, in_, out_);
+      Check(ns_split_lo(x.Data(), n, in_, in_, xl.Data(), stream()));
+      Check(ns_split_lo(weight_.Value().Data(), in_, out_, out_, wl.Data(), stream()));
+      x_lo = xl.Data();
+      w_lo = wl.Data();
+    }
     Tensor y = Scratch(out_buf_, n, out_);
-    Check(ns_gemm(n, out_, in_, x.Data(), in_, 0, weight_.Value().Data(), out_, 0, y.Data(), out_,
-                  0.0f, epi, bias_.Value().Data(), aux, aux_out, ctx_->scratch,
-                  ctx_->scratch_bytes, stream()));
+    Check(ns_gemm_lo(n, out_, in_, x.Data(), in_, 0, x_lo, weight_.Value().Data(), out_, 0, w_lo,
+                     y.Data(), out_, 0.0f, epi, bias_.Value().Data(), aux, aux_out, ctx_->scratch,
+                     ctx_->scratch_bytes, stream()));
     std::vector<int> shape = x.Shape();
     shape.back() = out_;
     return y.View(shape);
@@ -247,13 +262,24 @@ class Linear : public Layer {
     const int n = Rows(last_input_, in_);
     if (Rows(dy, out_) != n) throw std::invalid_argument("Linear::Backward: batch mismatch");
     Tensor dx = Scratch(dx_buf_, n, in_);
+    // The lo copies of X and W made by the forward pass are still current.
+    const bool lo = SplitOk();
+    const float* x_lo = lo ? x_lo_buf_.Data() : nullptr;
+    const float* w_lo = lo ? w_lo_buf_.Data() : nullptr;
+    const float* dy_lo = nullptr;
+    if (lo) {
+      Tensor dl = Scratch(dy_lo_buf_, n, out_);
+      Check(ns_split_lo(dy.Data(), n, out_, out_, dl.Data(), stream()));
+      dy_lo = dl.Data();
+    }
     // dX = dY W^T  (W read transposed in place: no Transpose copy)
-    Check(ns_gemm(n, in_, out_, dy.Data(), out_, 0, weight_.Value().Data(), out_, 1, dx.Data(), in_,
-                  0.0f, epi, nullptr, aux, nullptr, ctx_->scratch, ctx_->scratch_bytes, stream()));
+    Check(ns_gemm_lo(n, in_, out_, dy.Data(), out_, 0, dy_lo, weight_.Value().Data(), out_, 1, w_lo,
+                     dx.Data(), in_, 0.0f, epi, nullptr, aux, nullptr, ctx_->scratch,
+                     ctx_->scratch_bytes, stream()));
     // dW = X^T dY, overwritten (MatMul's Resize+Zeros), X read transposed in place.
-    Check(ns_gemm(in_, out_, n, last_input_.Data(), in_, 1, dy.Data(), out_, 0,
-                  weight_.Grad().Data(), out_, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
-                  ctx_->scratch, ctx_->scratch_bytes, stream()));
+    Check(ns_gemm_lo(in_, out_, n, last_input_.Data(), in_, 1, x_lo, dy.Data(), out_, 0, dy_lo,
+                     weight_.Grad().Data(), out_, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
+                     ctx_->scratch, ctx_->scratch_bytes, stream()));
     // db = column sums of dY, overwritten.
     Check(ns_bias_grad(dy.Data(), n, out_, bias_.Grad().Data(), ctx_->scratch, ctx_->scratch_bytes,
                        stream()));
@@ -264,6 +290,7 @@ class Linear : public Layer {
   Parameter weight_, bias_;
   Tensor last_input_;
   Tensor out_buf_, post_, dx_buf_;
+  Tensor x_lo_buf_, w_lo_buf_, dy_lo_buf_;  // tf32 lo parts of X, W and dY
 };
 
 // include/layers/layernorm.h:22-59 (eps 1e-5, gamma = 1, beta = 0).

@@ -42,11 +42,21 @@ def kernel_health() -> None:
     _lib.check(_lib.load().ns_kernel_health())
 
 
+def split_lo(x):
+    """tf32 lo part of a 2-D fp32 tensor (x - trunc_tf32(x)), compact."""
+    lib = _lib.load()
+    _req(x, "x")
+    lo = torch.empty_like(x)
+    _lib.check(lib.ns_split_lo(_p(x), x.shape[0], x.shape[1], x.shape[1], _p(lo), _stream()))
+    return lo
+
+
 def gemm(A, B, a_trans=False, b_trans=False, epilogue=_lib.EPI_STORE, bias=None, aux=None,
-         out=None, aux_out=None, beta=0.0, split=True):
+         out=None, aux_out=None, beta=0.0, split=True, a_lo=None, b_lo=None):
     """MatMul (src/tensor.cpp:198-271) with transposed operands read in place.
 
     ``A`` is [M,K] (or [K,M] if a_trans), ``B`` is [K,N] (or [N,K] if b_trans).
+    ``a_lo`` / ``b_lo``: lo parts from split_lo of the same tensors (ns_gemm_lo).
     """
     lib = _lib.load()
     _req(A, "A")
@@ -61,9 +71,15 @@ def gemm(A, B, a_trans=False, b_trans=False, epilogue=_lib.EPI_STORE, bias=None,
         aux_out = torch.empty((M, N), dtype=_f32, device=A.device)
     ws_bytes = lib.ns_gemm_workspace_size(M, N, K) if split else 0
     ws = _ws(ws_bytes, A.device) if ws_bytes else None
-    _lib.check(lib.ns_gemm(M, N, K, _p(A), A.shape[1], int(a_trans), _p(B), B.shape[1],
-                           int(b_trans), _p(out), out.shape[1], float(beta), epilogue, _p(bias),
-                           _p(aux), _p(aux_out), _p(ws), ws_bytes, _stream()))
+    if a_lo is None and b_lo is None:
+        _lib.check(lib.ns_gemm(M, N, K, _p(A), A.shape[1], int(a_trans), _p(B), B.shape[1],
+                               int(b_trans), _p(out), out.shape[1], float(beta), epilogue,
+                               _p(bias), _p(aux), _p(aux_out), _p(ws), ws_bytes, _stream()))
+    else:
+        _lib.check(lib.ns_gemm_lo(M, N, K, _p(A), A.shape[1], int(a_trans), _p(a_lo), _p(B),
+                                  B.shape[1], int(b_trans), _p(b_lo), _p(out), out.shape[1],
+                                  float(beta), epilogue, _p(bias), _p(aux), _p(aux_out), _p(ws),
+                                  ws_bytes, _stream()))
     return (out, aux_out) if epilogue == _lib.EPI_BIAS_GELU else out
 
 

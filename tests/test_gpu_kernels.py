@@ -137,6 +137,32 @@ def test_gemm_engines_agree_and_epilogues(cuda, port):
             nk.set_gemm_engine(0)
 
 
+def test_split_lo_is_exact(cuda):
+    """ns_split_lo: x - trunc_tf32(x), bit for bit (hi + lo == x)."""
+    x = normal(rng(21), (300, 772)) * np.float32(37.0)
+    lo = host(nk.split_lo(dev(x, cuda)))
+    hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    assert np.array_equal(lo.view(np.uint32), (x - hi).view(np.uint32))
+    assert np.array_equal((hi + lo).view(np.uint32), x.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N,at,bt", [(8192, 768, 3072, 0, 0), (8192, 3072, 768, 0, 1),
+                                         (768, 8192, 3072, 1, 0), (300, 200, 1000, 0, 0),
+                                         (8192, 768, 256, 0, 1)])
+def test_gemm_lo_equals_gemm_bitwise(cuda, M, K, N, at, bt):
+    """ns_gemm_lo with caller-made lo copies (both, either, none) gives the
+    same bits as ns_gemm: same kernel, same operand split."""
+    r = rng(M + K + N + at + bt)
+    A = dev(normal(r, (K, M) if at else (M, K)), cuda)
+    B = dev(normal(r, (N, K) if bt else (K, N)), cuda)
+    ref = host(nk.gemm(A, B, a_trans=bool(at), b_trans=bool(bt))).view(np.uint32)
+    alo, blo = nk.split_lo(A), nk.split_lo(B)
+    for a_lo, b_lo in ((alo, blo), (alo, None), (None, blo)):
+        got = host(nk.gemm(A, B, a_trans=bool(at), b_trans=bool(bt), a_lo=a_lo, b_lo=b_lo))
+        assert np.array_equal(got.view(np.uint32), ref)
+    nk.kernel_health()
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
