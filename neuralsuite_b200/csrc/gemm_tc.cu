@@ -777,6 +777,386 @@ ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
   return check_launch("ns_gemm tcgen05");
 }
 
+// ---------------------------------------------------------------- pair tiles
+//
+// 256 x 256 tiles on a cluster of two CTAs (one per SM) with the pair MMA
+// (tcgen05.mma.cta_group::2, M=256, N=256): CTA r holds rows [128r, 128r+128)
+// of the A tile and rows [128r, 128r+128) of the N-extent of the B tile, and
+// each SM's tensor core reads only its own shared memory for its share, so a
+// CTA's operand traffic per FLOP is half that of a 128 x 256 tile.  Stages are
+// 64 KB, three deep.  The even CTA issues the MMAs; its commits arrive on the
+// barriers of both CTAs.  A thread of the odd CTA relays the odd CTA's TMA
+// completions to the even CTA, and the odd CTA's fold warps report folded
+// chunks to it, with cluster-scope mbarrier arrives.  Each CTA's TMEM holds
+// its 128 rows of two 256-column chunk buffers; the running sums live in the
+// registers of its eight fold warps as in the 128 x 256 kernel.
+constexpr int kPairStages = 3;
+
+struct PairLayout {
+  static constexpr uint32_t kA = kBM * kBK * 4;  // 16 KB: this CTA's 128 rows of A
+  static constexpr uint32_t kB = 128 * kBK * 4;  // 16 KB: this CTA's half of B
+  static constexpr uint32_t kRaw = kA + kB;
+  static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
+  static constexpr uint32_t kBars = kPairStages * kStage;
+  static constexpr uint32_t kNumBars = 5 * kPairStages + 5;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(kDynSmem <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of this CTA's shared variable `addr` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at this shared offset in both CTAs of the pair once
+// every pair MMA issued so far has completed.
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmAlo,
+                     const __grid_constant__ CUtensorMap tmBlo, const KParams p) {
+  using L = PairLayout;
+  constexpr int S = kPairStages;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };              // own raw tiles
+  auto lofull_bar = [&](int s) { return bar0 + 8u * (S + s); };      // own lo tiles
+  auto peer_bar = [&](int s) { return bar0 + 8u * (2 * S + s); };    // odd CTA's raw (even CTA)
+  auto peerlo_bar = [&](int s) { return bar0 + 8u * (3 * S + s); };  // odd CTA's lo (even CTA)
+  auto empty_bar = [&](int s) { return bar0 + 8u * (4 * S + s); };
+  auto chf_bar = [&](int c) { return bar0 + 8u * (5 * S + c); };
+  auto che_bar = [&](int c) { return bar0 + 8u * (5 * S + 2 + c); };
+  const uint32_t drain_bar = bar0 + 8u * (5 * S + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(lofull_bar(s), 1);
+      mbar_init(peer_bar(s), 1);
+      mbar_init(peerlo_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(chf_bar(c), 1);
+      // even CTA: its 256 fold threads plus one arrive per fold warp of the odd CTA
+      mbar_init(che_bar(c), kWideFoldThreads + 8);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int n_units = p.tiles_m * p.tiles_n * p.splits;
+  const int unit0 = (int)cluster_id_x(), unit_step = (int)cluster_count_x();
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWideLowRegs));
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer (both CTAs)
+      if (lane == 0) {
+        uint32_t it = 0;
+        int issued[S];
+        uint32_t issued_ph[S];
+        for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
+        bool ok = true;
+        for (int u = unit0; ok && u < n_units; u += unit_step) {
+          int tm, tn, split, kb0, kb1;
+          decode_unit(p, u, tm, tn, split, kb0, kb1);
+          const int m0 = tm * 256 + (int)rank * kBM, n0 = tn * BN + (int)rank * 128;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1u;
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(full_bar(s), L::kRaw);
+            mbar_expect_tx(lofull_bar(s), L::kRaw);
+            issued[s] = 1;
+            issued_ph[s] = ph;
+            const uint32_t a_dst = sbase + s * L::kStage;
+            const uint32_t b_dst = a_dst + L::kA;
+            const int k0 = kb * kBK;
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+              const CUtensorMap* ma = part ? &tmAlo : &tmA;
+              const CUtensorMap* mb = part ? &tmBlo : &tmB;
+              const uint32_t off = part ? L::kRaw : 0u;
+              const uint32_t bar = part ? lofull_bar(s) : full_bar(s);
+              if (!p.a_mn) {
+                tma_load_2d(a_dst + off, ma, bar, k0, m0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < kBM / 32; ++j)
+                  tma_load_2d(a_dst + off + j * 4096, ma, bar, m0 + 32 * j, k0);
+              }
+              if (!p.b_mn) {
+                tma_load_2d(b_dst + off, mb, bar, k0, n0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 128 / 32; ++j)
+                  tma_load_2d(b_dst + off + j * 4096, mb, bar, n0 + 32 * j, k0);
+              }
+            }
+          }
+        }
+        if (!ok)
+          for (int s = 0; s < S; ++s)
+            if (issued[s]) {
+              mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
+              mbar_wait_drain(lofull_bar(s), issued_ph[s], &g_timeout);
+            }
+      }
+    } else if (warp == 1 && rank == 0) {
+      // ---------------------------------------------------------- MMA issuer (even CTA)
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)p.a_mn << 15) |
+                             ((uint32_t)p.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);
+      uint32_t it = 0, cit = 0;
+      bool ok = true;
+      for (int u = unit0; ok && u < n_units; u += unit_step) {
+        int tm, tn, split, kb0, kb1;
+        decode_unit(p, u, tm, tn, split, kb0, kb1);
+        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk, ++cit) {
+          const int cb = cit & 1;
+          if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t d_tmem = tmem_base + cb * BN;
+          const int c1 = min(kb1, c0 + kChunk);
+          for (int kb = c0; kb < c1; ++kb, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1u;
+            if (!warp_wait(full_bar(s), ph, abort, &g_timeout) ||
+                !warp_wait(peer_bar(s), ph, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            const uint32_t a_raw = sbase + s * L::kStage;
+            const uint32_t b_raw = a_raw + L::kA;
+            const uint32_t a_lo = a_raw + L::kRaw;
+            const uint32_t b_lo = a_lo + L::kA;
+            if (elect_one()) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk)
+                mma_pair(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                         idesc, (kb > c0 || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
+            if (!warp_wait(lofull_bar(s), ph, abort, &g_timeout) ||
+                !warp_wait(peerlo_bar(s), ph, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            if (elect_one()) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk) {
+                mma_pair(d_tmem, operand_desc(a_raw, p.a_mn, kk), operand_desc(b_lo, p.b_mn, kk),
+                         idesc, 1u);
+                mma_pair(d_tmem, operand_desc(a_lo, p.a_mn, kk), operand_desc(b_raw, p.b_mn, kk),
+                         idesc, 1u);
+              }
+              commit_pair(empty_bar(s));
+            }
+            __syncwarp();
+          }
+          if (!ok) break;
+          if (elect_one()) commit_pair(chf_bar(cb));
+          __syncwarp();
+        }
+      }
+      if (!ok) {
+        if (elect_one()) commit_pair(drain_bar);
+        __syncwarp();
+        mbar_wait_drain(drain_bar, 0, &g_timeout);
+      }
+    } else if (warp == 2 && rank == 1 && lane == 0) {
+      // ---------------------------------------------------------- relay (odd CTA)
+      // Forward this CTA's TMA completions, in order, to the even CTA.
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = unit0; ok && u < n_units; u += unit_step) {
+        int tm, tn, split, kb0, kb1;
+        decode_unit(p, u, tm, tn, split, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(full_bar(s), ph, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          remote_arrive(map_rank(peer_bar(s), 0));
+          if (!mbar_wait(lofull_bar(s), ph, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          remote_arrive(map_rank(peerlo_bar(s), 0));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ fold + epilogue (both CTAs)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWideHighRegs));
+    const int ew = warp & 3;
+    const int col0 = ((warp - 4) >> 2) * 128;
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    uint32_t cit = 0;
+    bool ok = true;
+    float acc[128];
+    for (int u = unit0; ok && u < n_units; u += unit_step) {
+      int tm, tn, split, kb0, kb1;
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int c0 = kb0; c0 < kb1; c0 += kChunk, ++cit) {
+        const int cb = cit & 1;
+        if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t c_tmem = tmem_base + lane_off + cb * BN + col0;
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t a[32], b[32];
+          tmem_ld32_nowait(c_tmem + 32 * c, a);
+          tmem_ld32_nowait(c_tmem + 32 * (c + 1), b);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            acc[32 * c + j] = __fadd_rn(acc[32 * c + j], __uint_as_float(a[j]));
+            acc[32 * (c + 1) + j] = __fadd_rn(acc[32 * (c + 1) + j], __uint_as_float(b[j]));
+          }
+        }
+        fence_before();
+        if (rank == 0) {
+          mbar_arrive(che_bar(cb));
+        } else {
+          __syncwarp();
+          if (lane == 0) remote_arrive(map_rank(che_bar(cb), 0));
+        }
+      }
+      if (!ok) break;
+      const int m = tm * 256 + (int)rank * kBM + ew * 32 + lane;
+      const int n_base = tn * BN + col0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int n0 = n_base + c * 32;
+        if (m < p.M && n0 < p.N) {
+          const float* v = acc + 32 * c;
+          if (p.splits > 1) {
+            float* dst = p.ws + ((size_t)split * p.M + m) * p.N + n0;
+            if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N) dst[j] = v[j];
+            }
+          } else if (p.vec_ok && n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              epi_store4(p.e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
+          }
+        }
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // the even CTA's MMAs have read this CTA's tiles; no early exit
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols)
+                 : "memory");
+  }
+}
+
+ns_status launch_pair(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
+                      cudaStream_t s) {
+  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)PairLayout::kDynSmem),
+              "ns_gemm attr");
+  cudaFuncAttributes fa;
+  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_pair_kernel), "ns_gemm attributes");
+  if (fa.numRegs < kWideMinLaunchRegs)
+    return fail(NS_ERR_UNSUPPORTED, "ns_gemm: pair kernel compiled with too few registers for its split");
+  gemm_pair_kernel<<<2 * pl.grid, kWideThreads, PairLayout::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
+  return check_launch("ns_gemm tcgen05 pair");
+}
+
 ns_status launch_wide(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
                       const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
                       cudaStream_t s) {
@@ -810,33 +1190,37 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide) {
   const int kb_total = std::max(1, ceil_div(K, kBK));
   Plan best{};
   double best_cost = 1e30;
-  for (int bn : {128, 256}) {
-    if (bn == 256 && !allow_wide) continue;
-    const int tiles_m = ceil_div(M, kBM), tiles_n = ceil_div(N, bn);
+  // Kernels: 128 x 128 tiles; 128 x 256 tiles (one CTA); 256 x 256 tiles (a
+  // CTA pair).  The two wide ones need pre-split operands.
+  for (int kind = 0; kind < 3; ++kind) {
+    if (kind > 0 && !allow_wide) continue;
+    const int bm = kind == 2 ? 256 : kBM, bn = kind == 0 ? 128 : 256;
+    const int slots = kind == 2 ? sms / 2 : sms;  // concurrent units
+    const int tiles_m = ceil_div(M, bm), tiles_n = ceil_div(N, bn);
     const int tiles = tiles_m * tiles_n;
     const int max_split = allow_split ? std::min(kb_total, 16) : 1;
-    // Measured k-block times (cycles): 128 x 128 tiles are bound by shared-memory
-    // operand traffic near 1600, 128 x 256 tiles by the 2-stage TMA ring.
-    const double kb_cycles = bn == 128 ? 1600.0 : 2300.0;
+    // Measured cycles per k-block of a unit (the MMA alone needs 768, 1536, 1536).
+    const double kb_cycles = kind == 0 ? 1600.0 : kind == 1 ? 2100.0 : 4000.0;
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kb_per = ceil_div(kb_total, sp);
       const int splits = ceil_div(kb_total, kb_per);
       if (splits != sp) continue;
       const int units = tiles * splits;
-      const int waves = ceil_div(units, sms);
+      const int waves = ceil_div(units, slots);
       double cost = (double)waves * ((double)kb_per * kb_cycles + 3000.0);
       if (splits > 1)  // partial tiles out and back in, ~5 TB/s at ~1.9 GHz
         cost += (double)(2 * splits + 1) * M * (double)N * 4.0 / 5e12 * 1.9e9;
       if (cost < best_cost * 0.98) {
         best_cost = cost;
         best.bn = bn;
-        best.stages = bn == 128 ? 3 : kWideStages;
+        best.pair = kind == 2 ? 1 : 0;
+        best.stages = kind == 0 ? 3 : kind == 1 ? kWideStages : kPairStages;
         best.tiles_m = tiles_m;
         best.tiles_n = tiles_n;
         best.splits = splits;
         best.kb_total = kb_total;
         best.kb_per = kb_per;
-        best.grid = std::min(units, sms);
+        best.grid = std::min(units, slots);
       }
     }
   }
@@ -863,7 +1247,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   std::memset(&tb_lo, 0, sizeof(tb_lo));
   ns_status rc = a_mn ? tcx::make_map(&ta, A, M, K, lda, 32, true) : tcx::make_map(&ta, A, K, M, lda, kBM, false);
   if (rc != NS_OK) return rc;
-  rc = b_mn ? tcx::make_map(&tb, B, N, K, ldb, 32, true) : tcx::make_map(&tb, B, K, N, ldb, pl.bn, false);
+  const int b_box = pl.pair ? 128 : pl.bn;  // rows of B per CTA
+  rc = b_mn ? tcx::make_map(&tb, B, N, K, ldb, 32, true) : tcx::make_map(&tb, B, K, N, ldb, b_box, false);
   if (rc != NS_OK) return rc;
   const bool pre = lo_ws != nullptr || (a_lo_in && b_lo_in);
   if (pre) {
@@ -886,7 +1271,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
     }
     rc = a_mn ? tcx::make_map(&ta_lo, a_lo, M, K, M, 32, true) : tcx::make_map(&ta_lo, a_lo, K, M, K, kBM, false);
     if (rc != NS_OK) return rc;
-    rc = b_mn ? tcx::make_map(&tb_lo, b_lo, N, K, N, 32, true) : tcx::make_map(&tb_lo, b_lo, K, N, K, pl.bn, false);
+    rc = b_mn ? tcx::make_map(&tb_lo, b_lo, N, K, N, 32, true) : tcx::make_map(&tb_lo, b_lo, K, N, K, b_box, false);
     if (rc != NS_OK) return rc;
   }
   KParams kp;
@@ -901,7 +1286,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                        reinterpret_cast<uintptr_t>(ws);
   kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
   if (pl.bn == kWideBN && !pre) return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
-  rc = pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
+  rc = pl.pair             ? launch_pair(pl, ta, tb, ta_lo, tb_lo, kp, stream)
+       : pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pre            ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
                         : launch<128, 5, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
   if (rc != NS_OK || pl.splits == 1) return rc;

@@ -14,6 +14,7 @@ constexpr int kBK = 32;   // fp32 K per stage = one 128-byte swizzle row
 
 struct Plan {
   int bn;          // 128 or 256
+  int pair;        // 1: 256 x 256 tiles on a CTA pair (tiles_m counts 256-row tiles)
   int stages;
   int tiles_m, tiles_n;
   int splits;      // K splits (>= 1), every split non-empty
