@@ -90,4 +90,63 @@ __device__ __forceinline__ void epi_store4(const EpiArgs& e, int m, int n, float
   *reinterpret_cast<float4*>(e.C + off) = r;
 }
 
+// Stores `count` (<= R) consecutive rows m0.. of column n, values v[0..count):
+// the transposed GEMM epilogue.  The switch sits outside the loop, so each
+// epilogue kind is one straight-line loop over registers.
+template <int R>
+__device__ __forceinline__ void epi_store_col(const EpiArgs& e, int m0, int n, int count,
+                                              const float (&v)[R]) {
+  float* c = e.C + (size_t)m0 * e.ldc + n;
+  const size_t ld = (size_t)e.ldc;
+  switch (e.epi) {
+    case NS_EPI_STORE:
+      if (e.beta != 0.0f) {
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+          if (j < count) c[j * ld] = __fadd_rn(c[j * ld], v[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+          if (j < count) c[j * ld] = v[j];
+      }
+      break;
+    case NS_EPI_BIAS: {
+      const float b = e.bias[n];
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (j < count) c[j * ld] = __fadd_rn(v[j], b);
+      break;
+    }
+    case NS_EPI_BIAS_GELU: {
+      const float b = e.bias[n];
+      float* g = e.aux_out + (size_t)m0 * e.ldc + n;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (j < count) {
+          const float x = __fadd_rn(v[j], b);
+          c[j * ld] = x;
+          g[j * ld] = gelu_f(x);
+        }
+      break;
+    }
+    case NS_EPI_BIAS_RESID: {
+      const float b = e.bias[n];
+      const float* r = e.aux + (size_t)m0 * e.ldc + n;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (j < count) c[j * ld] = __fadd_rn(r[j * ld], __fadd_rn(v[j], b));
+      break;
+    }
+    case NS_EPI_GELU_BWD: {
+      const float* r = e.aux + (size_t)m0 * e.ldc + n;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (j < count) c[j * ld] = __fmul_rn(v[j], gelu_grad_f(r[j * ld]));
+      break;
+    }
+    default:
+      break;
+  }
+}
+
 }  // namespace nsb

@@ -12,7 +12,9 @@
 namespace nsb {
 namespace {
 
-thread_local int t_engine = 0;  // 0 auto, 1 SIMT, 2 tcgen05 with in-kernel operand split
+// 0 auto, 1 SIMT, 2 tcgen05 with in-kernel operand split, 3 / 4: pre-split operands on
+// 256 x 256 pair tiles / 128 x 256 tiles only, 5: 128 x 256 tiles storing rows (not C^T)
+thread_local int t_engine = 0;
 
 constexpr int kSB = 64, kSK = 16;
 
@@ -21,7 +23,8 @@ constexpr int kSB = 64, kSK = 16;
 template <bool AT, bool BT>
 __global__ void __launch_bounds__(256) gemm_simt_k(int M, int N, int K, const float* __restrict__ A,
                                                    int lda, const float* __restrict__ B, int ldb,
-                                                   EpiArgs e) {
+                                                   const EpiArgs e_param) {
+  const EpiArgs e = e_param;  // in registers, not re-read from parameter space
   __shared__ float As[kSK][kSB + 4];
   __shared__ float Bs[kSK][kSB + 4];
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
@@ -97,17 +100,20 @@ extern "C" {
 
 size_t ns_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  // Enough for either plan: wide tiles (pre-split) or 128-wide tiles.
+  // Enough for any plan ns_gemm may pick (every kernel, both store orientations).
   size_t part = 0;
-  for (bool wide : {true, false}) {
-    const tc::Plan p = tc::plan(M, N, K, true, wide);
-    part = std::max(part, (tc::split_workspace_bytes(p, M, N) + 255) & ~(size_t)255);
-  }
+  for (bool wide : {true, false})
+    for (int force = -1; force <= 2; ++force)
+      for (int trans = 0; trans <= 1; ++trans) {
+        if (!wide && force > 0) continue;
+        const tc::Plan p = tc::plan(M, N, K, true, wide, force, trans);
+        part = std::max(part, (tc::split_workspace_bytes(p, M, N) + 255) & ~(size_t)255);
+      }
   return part + tc::lo_workspace_bytes(M, N, K);
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine >= 0 && engine <= 2, "ns_gemm_set_engine: engine must be 0, 1 or 2");
+  NS_REQUIRE(engine >= 0 && engine <= 5, "ns_gemm_set_engine: engine must be 0..5");
   t_engine = engine;
   return NS_OK;
 }
@@ -147,16 +153,23 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
   // loaded by TMA) allows 128 x 256 tiles; otherwise the kernel splits in
   // shared memory.
   const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
-  const bool pre_ok = t_engine == 0 && a_cols % 4 == 0 && b_cols % 4 == 0;
-  const size_t lo_bytes = (a_lo_in ? 0 : tc::lo_elems_a(M, K) * sizeof(float)) +
-                          (b_lo_in ? 0 : (size_t)K * N * sizeof(float));
+  const bool pre_ok = (t_engine == 0 || t_engine >= 3) && a_cols % 4 == 0 && b_cols % 4 == 0;
+  const int force = t_engine == 3 ? 2 : (t_engine == 4 || t_engine == 5) ? 1 : -1;
+  // Compute C^T (coalesced column stores) unless the epilogue reads the aux
+  // operand: its loads are latency-bound either way, and row-wise they issue
+  // as 16-byte vectors.
+  const bool reads_aux = epilogue == NS_EPI_BIAS_RESID || epilogue == NS_EPI_GELU_BWD;
+  const int trans_mode = (t_engine == 5 || (t_engine == 0 && reads_aux)) ? 0 : 1;
+  const size_t lo_bytes = ((a_lo_in ? 0 : tc::lo_elems_a(M, K)) + (b_lo_in ? 0 : tc::lo_elems_a(N, K))) *
+                          sizeof(float);
   tc::Plan pl{};
   size_t part = 0;
   float* lo = nullptr;
   bool chosen = false;
   for (bool wide : {true, false}) {
     if (!pre_ok) break;
-    pl = tc::plan(M, N, K, ws_ok, wide);
+    if (force >= 0 && !wide) break;
+    pl = tc::plan(M, N, K, ws_ok, wide, force, trans_mode);
     part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
     if (lo_bytes == 0 && part == 0) {
       chosen = true;

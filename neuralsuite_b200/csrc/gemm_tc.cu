@@ -59,6 +59,10 @@ struct KParams {
   EpiArgs e;
   float* ws;
   int vec_ok;  // 16-byte vector epilogue allowed
+  // 1: the kernel computes the transposed product C^T = B^T A^T (rows of its
+  // tile are columns of C); the epilogue stores tile element (r, c) to C[c][r].
+  int trans_out;
+  int out_m, out_n;  // C's shape
 };
 
 // Descriptor of MMA k-step kk (8 tf32) of an operand tile at `base`.
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after();
       const int m = tm * kBM + ew * 32 + lane;
       const int n_base = tn * BN;
+      const EpiArgs e = p.e;  // in registers, not re-read from parameter space
 #pragma unroll 1
       for (int c = col0; c < col0 + kGroupCols; c += 32) {
         uint32_t v[32];
@@ -369,11 +374,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (p.vec_ok && n0 + 32 <= p.N) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
-              epi_store4(p.e, m, n0 + j,
+              epi_store4(e, m, n0 + j,
                          make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
                                      __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])));
           } else {
-            for (int j = 0; j < 32 && n0 + j < p.N; ++j) epi_store(p.e, m, n0 + j, __uint_as_float(v[j]));
+            for (int j = 0; j < 32 && n0 + j < p.N; ++j) epi_store(e, m, n0 + j, __uint_as_float(v[j]));
           }
         }
       }
@@ -671,6 +676,34 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       if (!ok) break;
       const int m = tm * kBM + ew * 32 + lane;
       const int n_base = tn * BN + col0;
+      if (p.trans_out) {
+        // This thread's TMEM lane is output column n; its registers hold 128
+        // consecutive output rows, so each warp store covers 32 consecutive
+        // columns of one row of C (coalesced).
+        const int n_out = m, m0_out = n_base;
+        const int rows = min(128, p.out_m - m0_out);
+        if (n_out < p.out_n && rows > 0) {
+          // Epilogue arguments in registers (not re-read from parameter space per element).
+          const EpiArgs e = p.e;
+          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f)) {
+            float* dst = p.splits > 1 ? p.ws + ((size_t)split * p.out_m + m0_out) * p.out_n + n_out
+                                      : e.C + (size_t)m0_out * e.ldc + n_out;
+            const size_t ld = p.splits > 1 ? (size_t)p.out_n : (size_t)e.ldc;
+            if (rows == 128) {
+#pragma unroll
+              for (int j = 0; j < 128; ++j) dst[j * ld] = acc[j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 128; ++j)
+                if (j < rows) dst[j * ld] = acc[j];
+            }
+          } else {
+            epi_store_col<128>(e, m0_out, n_out, rows, acc);
+          }
+        }
+        continue;
+      }
+      const EpiArgs e = p.e;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int n0 = n_base + c * 32;
@@ -690,11 +723,11 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           } else if (p.vec_ok && n0 + 32 <= p.N) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
-              epi_store4(p.e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+              epi_store4(e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
+              if (n0 + j < p.N) epi_store(e, m, n0 + j, v[j]);
           }
         }
       }
@@ -741,7 +774,8 @@ __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int 
 
 // Ordered sum of the split-K partial tiles, then the epilogue.
 __global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M, int N,
-                                EpiArgs e, int vec) {
+                                const EpiArgs e_param, int vec) {
+  const EpiArgs e = e_param;  // in registers, not re-read from parameter space
   const int64_t total = (int64_t)M * N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (vec) {
@@ -1102,6 +1136,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       if (!ok) break;
       const int m = tm * 256 + (int)rank * kBM + ew * 32 + lane;
       const int n_base = tn * BN + col0;
+      if (p.trans_out) {
+        // This thread's TMEM lane is output column n; its registers hold 128
+        // consecutive output rows, so each warp store covers 32 consecutive
+        // columns of one row of C (coalesced).
+        const int n_out = m, m0_out = n_base;
+        const int rows = min(128, p.out_m - m0_out);
+        if (n_out < p.out_n && rows > 0) {
+          // Epilogue arguments in registers (not re-read from parameter space per element).
+          const EpiArgs e = p.e;
+          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f)) {
+            float* dst = p.splits > 1 ? p.ws + ((size_t)split * p.out_m + m0_out) * p.out_n + n_out
+                                      : e.C + (size_t)m0_out * e.ldc + n_out;
+            const size_t ld = p.splits > 1 ? (size_t)p.out_n : (size_t)e.ldc;
+            if (rows == 128) {
+#pragma unroll
+              for (int j = 0; j < 128; ++j) dst[j * ld] = acc[j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 128; ++j)
+                if (j < rows) dst[j * ld] = acc[j];
+            }
+          } else {
+            epi_store_col<128>(e, m0_out, n_out, rows, acc);
+          }
+        }
+        continue;
+      }
+      const EpiArgs e = p.e;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int n0 = n_base + c * 32;
@@ -1121,11 +1183,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
           } else if (p.vec_ok && n0 + 32 <= p.N) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
-              epi_store4(p.e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+              epi_store4(e, m, n0 + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
+              if (n0 + j < p.N) epi_store(e, m, n0 + j, v[j]);
           }
         }
       }
@@ -1185,7 +1247,7 @@ ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaSt
 
 }  // namespace
 
-Plan plan(int M, int N, int K, bool allow_split, bool allow_wide) {
+Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind, int trans_mode) {
   const int sms = sm_count();
   const int kb_total = std::max(1, ceil_div(K, kBK));
   Plan best{};
@@ -1194,9 +1256,13 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide) {
   // CTA pair).  The two wide ones need pre-split operands.
   for (int kind = 0; kind < 3; ++kind) {
     if (kind > 0 && !allow_wide) continue;
+    if (force_kind >= 0 && kind != force_kind) continue;
     const int bm = kind == 2 ? 256 : kBM, bn = kind == 0 ? 128 : 256;
     const int slots = kind == 2 ? sms / 2 : sms;  // concurrent units
-    const int tiles_m = ceil_div(M, bm), tiles_n = ceil_div(N, bn);
+    // The wide kernels compute C^T (coalesced stores): their rows are C's columns.
+    const bool tr = kind != 0 && trans_mode == 1;
+    const int rows = tr ? N : M, cols = tr ? M : N;
+    const int tiles_m = ceil_div(rows, bm), tiles_n = ceil_div(cols, bn);
     const int tiles = tiles_m * tiles_n;
     const int max_split = allow_split ? std::min(kb_total, 16) : 1;
     // Measured cycles per k-block of a unit (the MMA alone needs 768, 1536, 1536).
@@ -1214,6 +1280,7 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide) {
         best_cost = cost;
         best.bn = bn;
         best.pair = kind == 2 ? 1 : 0;
+        best.trans = tr ? 1 : 0;
         best.stages = kind == 0 ? 3 : kind == 1 ? kWideStages : kPairStages;
         best.tiles_m = tiles_m;
         best.tiles_n = tiles_n;
@@ -1234,12 +1301,23 @@ size_t split_workspace_bytes(const Plan& p, int M, int N) {
 // Floats of the compact lo copy of A, rounded up to 64 B so B's copy is aligned.
 size_t lo_elems_a(int M, int K) { return ((size_t)M * K + 15) & ~(size_t)15; }
 size_t lo_workspace_bytes(int M, int N, int K) {
-  return (lo_elems_a(M, K) + (size_t)K * N) * sizeof(float);
+  // Either operand may come first (transposed plans swap them).
+  return (lo_elems_a(M, K) + lo_elems_a(N, K)) * sizeof(float);
 }
 
 ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int a_mn,
               const float* B, int ldb, int b_mn, const EpiArgs& e, float* ws, float* lo_ws,
               const float* a_lo_in, const float* b_lo_in, cudaStream_t stream) {
+  const int out_m = M, out_n = N;
+  if (pl.trans) {
+    // Compute C^T = op(B)^T op(A)^T: B becomes the first operand (its major
+    // order carries over), A the second.
+    std::swap(M, N);
+    std::swap(A, B);
+    std::swap(lda, ldb);
+    std::swap(a_mn, b_mn);
+    std::swap(a_lo_in, b_lo_in);
+  }
   CUtensorMap ta, tb, ta_lo, tb_lo;
   std::memset(&ta, 0, sizeof(ta));
   std::memset(&tb, 0, sizeof(tb));
@@ -1285,17 +1363,22 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                        reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
                        reinterpret_cast<uintptr_t>(ws);
   kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
+  kp.trans_out = pl.trans;
+  kp.out_m = out_m;
+  kp.out_n = out_n;
   if (pl.bn == kWideBN && !pre) return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
   rc = pl.pair             ? launch_pair(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pre            ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
                         : launch<128, 5, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
   if (rc != NS_OK || pl.splits == 1) return rc;
-  const int64_t total = (int64_t)M * N;
-  const int vec = kp.vec_ok;
+  const int64_t total = (int64_t)out_m * out_n;
+  const int vec = ((reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
+                    reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
+                    reinterpret_cast<uintptr_t>(ws)) & 15) == 0 && (e.ldc % 4) == 0 && (out_n % 4) == 0;
   const int64_t work = vec ? total / 4 : total;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
-  splitk_reduce_k<<<grid, 256, 0, stream>>>(ws, pl.splits, M, N, e, vec);
+  splitk_reduce_k<<<grid, 256, 0, stream>>>(ws, pl.splits, out_m, out_n, e, vec);
   return check_launch("ns_gemm split-K reduce");
 }
 

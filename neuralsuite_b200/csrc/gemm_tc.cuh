@@ -15,6 +15,7 @@ constexpr int kBK = 32;   // fp32 K per stage = one 128-byte swizzle row
 struct Plan {
   int bn;          // 128 or 256
   int pair;        // 1: 256 x 256 tiles on a CTA pair (tiles_m counts 256-row tiles)
+  int trans;       // 1: the kernel computes C^T (tiles_m over N, tiles_n over M)
   int stages;
   int tiles_m, tiles_n;
   int splits;      // K splits (>= 1), every split non-empty
@@ -24,7 +25,12 @@ struct Plan {
 };
 
 // allow_wide: 128 x 256 tiles may be chosen (they need pre-split operands).
-Plan plan(int M, int N, int K, bool allow_split, bool allow_wide);
+// force_kind >= 0 restricts the choice to one kernel: 0 = 128 x 128,
+// 1 = 128 x 256, 2 = 256 x 256 pair (tests and profiling).
+// trans_mode for the wide kernels: 1 = compute C^T (coalesced column stores),
+// 0 = compute C (row stores).
+Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind = -1,
+          int trans_mode = 1);
 size_t split_workspace_bytes(const Plan& p, int M, int N);
 
 size_t lo_elems_a(int M, int K);

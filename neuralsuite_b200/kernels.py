@@ -34,7 +34,8 @@ def _ws(nbytes, device):
 
 def set_gemm_engine(engine: int) -> None:
     """0 = automatic (tcgen05 where TMA allows), 1 = SIMT fp32 everywhere,
-    2 = tcgen05 with the operand split done inside the kernel."""
+    2 = tcgen05 with the operand split done inside the kernel, 3 / 4 = only
+    256 x 256 CTA-pair / 128 x 256 tiles (pre-split operands)."""
     _lib.check(_lib.load().ns_gemm_set_engine(engine))
 
 

@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profilers (ncu) and quick timing.
 
-    python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps [engine]]
+    python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps [engine [epilogue]]]
     python -m neuralsuite_b200.profile_cases attn B T H D [reps [engine]]
     python -m neuralsuite_b200.profile_cases ln ROWS DIM [reps]
 
@@ -40,11 +40,23 @@ def main(argv):
         reps = int(argv[6]) if len(argv) > 6 else 3
         if len(argv) > 7:
             nk.set_gemm_engine(int(argv[7]))
+        epi = int(argv[8]) if len(argv) > 8 else 0
         A = torch.randn((K, M) if at else (M, K), device=dev)
         B = torch.randn((N, K) if bt else (K, N), device=dev)
         out = torch.empty(M, N, device=dev)
-        ms = _time(lambda: nk.gemm(A, B, a_trans=bool(at), b_trans=bool(bt), out=out), reps)
-        print(f"gemm {M}x{N}x{K} at={at} bt={bt}: {ms:.4f} ms, {2 * M * N * K / ms / 1e9:.1f} TFLOP/s")
+        bias = torch.randn(N, device=dev)
+        aux = torch.randn(M, N, device=dev)
+        kw = {}
+        if epi in (1, 2, 3):
+            kw["bias"] = bias
+        if epi in (3, 4):
+            kw["aux"] = aux
+        if epi == 2:
+            kw["aux_out"] = torch.empty(M, N, device=dev)
+        ms = _time(lambda: nk.gemm(A, B, a_trans=bool(at), b_trans=bool(bt), out=out, epilogue=epi,
+                                   **kw), reps)
+        print(f"gemm {M}x{N}x{K} at={at} bt={bt} epi={epi}: {ms:.4f} ms, "
+              f"{2 * M * N * K / ms / 1e9:.1f} TFLOP/s")
     elif case == "attn":
         Bb, T, H, D = (int(x) for x in argv[1:5])
         reps = int(argv[5]) if len(argv) > 5 else 3

@@ -70,7 +70,7 @@ def test_gemm_tf32_split_recovers_fp32(cuda):
 FULL = [(8192, 768, 3072), (8192, 3072, 768), (16384, 1024, 4096)]
 
 
-@pytest.fixture(params=[0, 2], ids=["presplit", "inkernel"])
+@pytest.fixture(params=[0, 2, 3, 4, 5], ids=["auto", "inkernel", "pair", "wide", "widerows"])
 def gemm_engine(request):
     nk.set_gemm_engine(request.param)
     yield request.param
@@ -85,8 +85,9 @@ def test_gemm_sweep_full(cuda, gemm_engine, M, K, N):
     is 1e-5, test_suite.cpp:3148-3150; an fp32 k-sequential loop lands near
     1e-6 here) and, per element, within 1e-4 relative of the float64 value
     wherever |value| >= 0.1 * rms (smaller values carry the same absolute
-    rounding as any fp32 accumulation of K products).  Both tcgen05 operand
-    paths: lo parts pre-split into the workspace, and split in the kernel."""
+    rounding as any fp32 accumulation of K products).  Every tcgen05 kernel:
+    the planner's choice, in-kernel operand split, CTA-pair tiles, 128 x 256
+    tiles."""
     r = rng(M + K + N)
     X, W, dY = normal(r, (M, K)), normal(r, (K, N)), normal(r, (M, N))
     Xd, Wd, dYd = dev(X, cuda), dev(W, cuda), dev(dY, cuda)
@@ -116,7 +117,7 @@ def test_gemm_engines_agree_and_epilogues(cuda, port):
     Xd, Wd, bd, Rd = dev(X, cuda), dev(W, cuda), dev(b, cuda), dev(R, cuda)
     base = port.matmul(X, W)
     base64 = fp64.matmul(X, W)
-    for engine in (0, 1, 2):
+    for engine in (0, 1, 2, 3, 4, 5):
         nk.set_gemm_engine(engine)
         try:
             y = host(nk.gemm(Xd, Wd, epilogue=_lib.EPI_BIAS, bias=bd))
