@@ -819,9 +819,9 @@ ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
 // each SM's tensor core reads only its own shared memory for its share, so a
 // CTA's operand traffic per FLOP is half that of a 128 x 256 tile.  Stages are
 // 64 KB, three deep.  The even CTA issues the MMAs; its commits arrive on the
-// barriers of both CTAs.  A thread of the odd CTA relays the odd CTA's TMA
-// completions to the even CTA, and the odd CTA's fold warps report folded
-// chunks to it, with cluster-scope mbarrier arrives.  Each CTA's TMEM holds
+// barriers of both CTAs.  Both CTAs' TMA loads complete on the even CTA's
+// stage barriers (the pair form of the bulk tensor copy), and the odd CTA's
+// fold warps report folded chunks with cluster-scope mbarrier arrives.  Each CTA's TMEM holds
 // its 128 rows of two 256-column chunk buffers; the running sums live in the
 // registers of its eight fold warps as in the 128 x 256 kernel.
 constexpr int kPairStages = 3;
@@ -832,7 +832,7 @@ struct PairLayout {
   static constexpr uint32_t kRaw = kA + kB;
   static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
   static constexpr uint32_t kBars = kPairStages * kStage;
-  static constexpr uint32_t kNumBars = 5 * kPairStages + 5;
+  static constexpr uint32_t kNumBars = 3 * kPairStages + 5;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
@@ -897,14 +897,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBars;
-  auto full_bar = [&](int s) { return bar0 + 8u * s; };              // own raw tiles
-  auto lofull_bar = [&](int s) { return bar0 + 8u * (S + s); };      // own lo tiles
-  auto peer_bar = [&](int s) { return bar0 + 8u * (2 * S + s); };    // odd CTA's raw (even CTA)
-  auto peerlo_bar = [&](int s) { return bar0 + 8u * (3 * S + s); };  // odd CTA's lo (even CTA)
-  auto empty_bar = [&](int s) { return bar0 + 8u * (4 * S + s); };
-  auto chf_bar = [&](int c) { return bar0 + 8u * (5 * S + c); };
-  auto che_bar = [&](int c) { return bar0 + 8u * (5 * S + 2 + c); };
-  const uint32_t drain_bar = bar0 + 8u * (5 * S + 4);
+  // full / lofull: raw and lo tiles of both CTAs (used in the even CTA)
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto lofull_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (2 * S + s); };
+  auto chf_bar = [&](int c) { return bar0 + 8u * (3 * S + c); };
+  auto che_bar = [&](int c) { return bar0 + 8u * (3 * S + 2 + c); };
+  const uint32_t drain_bar = bar0 + 8u * (3 * S + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -914,8 +913,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(lofull_bar(s), 1);
-      mbar_init(peer_bar(s), 1);
-      mbar_init(peerlo_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
     for (int c = 0; c < 2; ++c) {
@@ -963,8 +960,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
               ok = false;
               break;
             }
-            mbar_expect_tx(full_bar(s), L::kRaw);
-            mbar_expect_tx(lofull_bar(s), L::kRaw);
+            // The even CTA expects the bytes of both CTAs; the odd CTA's copies
+            // complete on the even CTA's barriers.
+            if (rank == 0) {
+              mbar_expect_tx(full_bar(s), 2 * L::kRaw);
+              mbar_expect_tx(lofull_bar(s), 2 * L::kRaw);
+            }
             issued[s] = 1;
             issued_ph[s] = ph;
             const uint32_t a_dst = sbase + s * L::kStage;
@@ -975,30 +976,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
               const CUtensorMap* ma = part ? &tmAlo : &tmA;
               const CUtensorMap* mb = part ? &tmBlo : &tmB;
               const uint32_t off = part ? L::kRaw : 0u;
-              const uint32_t bar = part ? lofull_bar(s) : full_bar(s);
+              const uint32_t bar = map_rank(part ? lofull_bar(s) : full_bar(s), 0);
               if (!p.a_mn) {
-                tma_load_2d(a_dst + off, ma, bar, k0, m0);
+                tma_load_2d_pair(a_dst + off, ma, bar, k0, m0);
               } else {
 #pragma unroll
                 for (int j = 0; j < kBM / 32; ++j)
-                  tma_load_2d(a_dst + off + j * 4096, ma, bar, m0 + 32 * j, k0);
+                  tma_load_2d_pair(a_dst + off + j * 4096, ma, bar, m0 + 32 * j, k0);
               }
               if (!p.b_mn) {
-                tma_load_2d(b_dst + off, mb, bar, k0, n0);
+                tma_load_2d_pair(b_dst + off, mb, bar, k0, n0);
               } else {
 #pragma unroll
                 for (int j = 0; j < 128 / 32; ++j)
-                  tma_load_2d(b_dst + off + j * 4096, mb, bar, n0 + 32 * j, k0);
+                  tma_load_2d_pair(b_dst + off + j * 4096, mb, bar, n0 + 32 * j, k0);
               }
             }
           }
         }
-        if (!ok)
-          for (int s = 0; s < S; ++s)
-            if (issued[s]) {
-              mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
-              mbar_wait_drain(lofull_bar(s), issued_ph[s], &g_timeout);
+        if (!ok) {
+          if (rank == 0) {
+            for (int s = 0; s < S; ++s)
+              if (issued[s]) {
+                mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
+                mbar_wait_drain(lofull_bar(s), issued_ph[s], &g_timeout);
+              }
+          } else {
+            // This CTA's copies complete on the other CTA's barriers: give
+            // any in flight time to land (bounded) before the CTA can exit.
+            const unsigned long long t0 = globaltimer();
+            while (globaltimer() - t0 < 100000ull) {
             }
+          }
+        }
       }
     } else if (warp == 1 && rank == 0) {
       // ---------------------------------------------------------- MMA issuer (even CTA)
@@ -1022,8 +1032,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
           for (int kb = c0; kb < c1; ++kb, ++it) {
             const int s = it % S;
             const uint32_t ph = (it / S) & 1u;
-            if (!warp_wait(full_bar(s), ph, abort, &g_timeout) ||
-                !warp_wait(peer_bar(s), ph, abort, &g_timeout)) {
+            if (!warp_wait(full_bar(s), ph, abort, &g_timeout)) {
               ok = false;
               break;
             }
@@ -1039,8 +1048,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                          idesc, (kb > c0 || kk > 0) ? 1u : 0u);
             }
             __syncwarp();
-            if (!warp_wait(lofull_bar(s), ph, abort, &g_timeout) ||
-                !warp_wait(peerlo_bar(s), ph, abort, &g_timeout)) {
+            if (!warp_wait(lofull_bar(s), ph, abort, &g_timeout)) {
               ok = false;
               break;
             }
@@ -1066,29 +1074,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         if (elect_one()) commit_pair(drain_bar);
         __syncwarp();
         mbar_wait_drain(drain_bar, 0, &g_timeout);
-      }
-    } else if (warp == 2 && rank == 1 && lane == 0) {
-      // ---------------------------------------------------------- relay (odd CTA)
-      // Forward this CTA's TMA completions, in order, to the even CTA.
-      uint32_t it = 0;
-      bool ok = true;
-      for (int u = unit0; ok && u < n_units; u += unit_step) {
-        int tm, tn, split, kb0, kb1;
-        decode_unit(p, u, tm, tn, split, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait(full_bar(s), ph, abort, &g_timeout)) {
-            ok = false;
-            break;
-          }
-          remote_arrive(map_rank(peer_bar(s), 0));
-          if (!mbar_wait(lofull_bar(s), ph, abort, &g_timeout)) {
-            ok = false;
-            break;
-          }
-          remote_arrive(map_rank(peerlo_bar(s), 0));
-        }
       }
     }
   } else {
@@ -1266,7 +1251,7 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
     const int tiles = tiles_m * tiles_n;
     const int max_split = allow_split ? std::min(kb_total, 16) : 1;
     // Measured cycles per k-block of a unit (the MMA alone needs 768, 1536, 1536).
-    const double kb_cycles = kind == 0 ? 1600.0 : kind == 1 ? 2100.0 : 4000.0;
+    const double kb_cycles = kind == 0 ? 1600.0 : kind == 1 ? 2100.0 : 1950.0;
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kb_per = ceil_div(kb_total, sp);
       const int splits = ceil_div(kb_total, kb_per);
