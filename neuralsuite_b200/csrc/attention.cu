@@ -158,17 +158,34 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_k(const float* __restrict__
   }
 }
 
-// Delta[bh, r] = sum_d dO[b, r, h*D + d] * O[b, r, h*D + d].
-__global__ void attn_delta_k(const float* __restrict__ out, const float* __restrict__ dout, int B,
-                             int T, int H, int D, float* __restrict__ delta) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= (int64_t)B * H * T) return;
-  const int r = (int)(i % T);
-  const int bh = (int)(i / T), b = bh / H, h = bh % H;
-  const size_t off = ((size_t)b * T + r) * H * D + (size_t)h * D;
-  float s = 0.0f;
-  for (int d = 0; d < D; ++d) s = fmaf(dout[off + d], out[off + d], s);
-  delta[i] = s;
+// Delta[bh, r] = sum_d dO[b, r, h*D + d] * O[b, r, h*D + d]: one warp per
+// (b, r) row of all heads, lanes striding the C columns (coalesced), each
+// head's D products summed by its lanes with shuffles.
+__global__ void __launch_bounds__(256) attn_delta_k(const float* __restrict__ out,
+                                                    const float* __restrict__ dout, int B, int T,
+                                                    int H, int D, float* __restrict__ delta) {
+  const int64_t row = blockIdx.x * 8 + (threadIdx.x >> 5);  // b * T + r
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)B * T) return;
+  const int b = (int)(row / T), r = (int)(row % T);
+  const int C = H * D;
+  const float* o = out + row * C;
+  const float* g = dout + row * C;
+  if (D % 32 == 0) {
+    // lanes cover 32 consecutive columns of one head per step
+    for (int h = 0; h < H; ++h) {
+      float s = 0.0f;
+      for (int d = lane; d < D; d += 32) s = fmaf(g[h * D + d], o[h * D + d], s);
+      s = warp_sum(s);
+      if (lane == 0) delta[((size_t)b * H + h) * T + r] = s;
+    }
+  } else {
+    for (int h = lane; h < H; h += 32) {
+      float s = 0.0f;
+      for (int d = 0; d < D; ++d) s = fmaf(g[h * D + d], o[h * D + d], s);
+      delta[((size_t)b * H + h) * T + r] = s;
+    }
+  }
 }
 
 // Scores and dP of one (query block, key block) pair into P / dS smem tiles.
@@ -465,7 +482,7 @@ ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, con
   cudaStream_t s = as_stream(stream);
   float* delta = static_cast<float*>(workspace);
   const int64_t n = (int64_t)B * H * T;
-  attn_delta_k<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(out, dout, B, T, H, D, delta);
+  attn_delta_k<<<(unsigned)ceil_div64((int64_t)B * T, 8), 256, 0, s>>>(out, dout, B, T, H, D, delta);
   { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
   const size_t delta_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
   float* lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + delta_bytes);

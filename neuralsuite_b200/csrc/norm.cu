@@ -244,13 +244,25 @@ __global__ void __launch_bounds__(256) ln_bwd_any(
 }
 
 // Stage 2 of every column sum: out[n] = sum over p (ascending) of part[p][n].
-__global__ void colsum_finish(const float* __restrict__ part, int n_part, int N,
-                              float* __restrict__ out) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
+// Column sums of part[n_part][N]: CTA = 32 columns, warp w sums partials
+// w, w+8, w+16, ... in order, then the eight warp sums are added in warp order
+// (a fixed order: deterministic).
+__global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ part, int n_part,
+                                                     int N, float* __restrict__ out) {
+  __shared__ float red[kRowsWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int p = 0; p < n_part; ++p) s += part[(size_t)p * N + n];
-  out[n] = s;
+  if (n < N)
+    for (int p = warp; p < n_part; p += kRowsWarps) s += part[(size_t)p * N + n];
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && n < N) {
+    float t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < kRowsWarps; ++w) t += red[w][lane];
+    out[n] = t;
+  }
 }
 
 // Stage 1 of the bias gradient: CTA (chunk) sums rows [r0, r1) of a
@@ -369,10 +381,19 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
     else if (nv <= 64)
       ln_bwd_vec<2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
+    else if (nv <= 96)
+      ln_bwd_vec<3><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
     else if (nv <= 128) {
       NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem), "ns_layernorm_bwd attr");
       ln_bwd_vec<4><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    } else if (nv <= 192) {
+      // dim <= 768: six float4 per lane, not eight (registers decide occupancy here)
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<6>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem), "ns_layernorm_bwd attr");
+      ln_bwd_vec<6><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     } else {
       NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -385,8 +406,8 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
                                       rows, dim, rpc);
   }
   { ns_status _rc = check_launch("ns_layernorm_bwd stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_g, ctas, dim, dgamma);
-  colsum_finish<<<ceil_div(dim, 256), 256, 0, s>>>(part_b, ctas, dim, dbeta);
+  colsum_finish<<<ceil_div(dim, 32), 256, 0, s>>>(part_g, ctas, dim, dgamma);
+  colsum_finish<<<ceil_div(dim, 32), 256, 0, s>>>(part_b, ctas, dim, dbeta);
   return check_launch("ns_layernorm_bwd stage 2");
 }
 
@@ -412,7 +433,7 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   float* part = static_cast<float*>(workspace);
   colsum_partial<<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part);
   { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 256), 256, 0, s>>>(part, chunks, N, db);
+  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db);
   return check_launch("ns_bias_grad stage 2");
 }
 
