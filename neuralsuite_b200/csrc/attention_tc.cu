@@ -356,13 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
       // m_new = -inf: every key so far is masked (P = 0 below).
       const float mc_new = m_new == -INFINITY ? 0.0f : m_new * c;
-      const float alpha = m == -INFINITY ? 0.0f : exp2f(mc - mc_new);
+      const float alpha = m == -INFINITY ? 0.0f : fast_exp2(mc - mc_new);
       float rs[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) rs[i] = 0.0f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        x[i] = exp2f(fmaf(x[i], c, -mc_new));
+        x[i] = fast_exp2(fmaf(x[i], c, -mc_new));
         rs[i & 7] += x[i];
       }
       l = l * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
@@ -410,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m1 = xchg[row], mc1 = xchg[kBQ + row], l1 = xchg[2 * kBQ + row];
       const float m_tot = fmaxf(m, m1);  // finite: key 0 is never masked
       const float mc_tot = m_tot * c;
-      const float a0 = exp2f(mc - mc_tot);
-      const float a1 = m1 == -INFINITY ? 0.0f : exp2f(mc1 - mc_tot);
+      const float a0 = fast_exp2(mc - mc_tot);
+      const float a1 = m1 == -INFINITY ? 0.0f : fast_exp2(mc1 - mc_tot);
       const float l_tot = l * a0 + l1 * a1;
       const float inv = 1.0f / l_tot;
       const uint32_t o1 = tmem + lane_off + kTO + D;
@@ -823,19 +823,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
       if (kTwoA) tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
       const float* vec = reinterpret_cast<const float*>(smem + s * L::kStage + L::kVecOff) + 32 * wg;
+      // Blocks clear of the diagonal (and of the sequence end) need no mask;
+      // the test is uniform over the CTA.
+      const int mb0 = (blk0 + i) * kBKV;
+      const bool full = kKeyMajor ? (mb0 >= r0 + kBQ - 1 && mb0 + kBKV <= p.T)
+                                  : (mb0 + kBKV - 1 <= r0);
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int m = m0 + c;
-        const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
-        const float l2 = kKeyMajor ? vec[c] : lse2_row;
-        const float pv = valid ? exp2f(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
-        float e = pv;
-        if (kTwoA) {
-          const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
-          e = pv * (__uint_as_float(dv[c]) - dl);
+        for (int c = 0; c < 32; ++c) {
+          const float l2 = kKeyMajor ? vec[c] : lse2_row;
+          const float pv = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2));
+          float e = pv;
+          if (kTwoA) {
+            const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
+            e = pv * (__uint_as_float(dv[c]) - dl);
+          }
+          sv[c] = __float_as_uint(tf32_hi(e));
+          dv[c] = __float_as_uint(tf32_lo(e));
         }
-        sv[c] = __float_as_uint(tf32_hi(e));
-        dv[c] = __float_as_uint(tf32_lo(e));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int m = m0 + c;
+          const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
+          const float l2 = kKeyMajor ? vec[c] : lse2_row;
+          const float pv = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
+          float e = pv;
+          if (kTwoA) {
+            const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
+            e = pv * (__uint_as_float(dv[c]) - dl);
+          }
+          sv[c] = __float_as_uint(tf32_hi(e));
+          dv[c] = __float_as_uint(tf32_lo(e));
+        }
       }
       tmem_st32(tmem + lane_off + (MODE == kDV ? kBS : kBdP) + 32 * wg, sv);
       tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);

@@ -229,6 +229,15 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, int a_mn, int b_mn) {
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
+// 2^x with the hardware approximation (relative error about 2^-22; 2^-inf = 0):
+// the softmax / attention-backward exponentials, where a longer library
+// sequence would make the element-wise warps the bottleneck.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float tf32_lo(float x) {
   return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
