@@ -155,11 +155,9 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
   const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
   const bool pre_ok = (t_engine == 0 || t_engine >= 3) && a_cols % 4 == 0 && b_cols % 4 == 0;
   const int force = t_engine == 3 ? 2 : (t_engine == 4 || t_engine == 5) ? 1 : -1;
-  // Compute C^T (coalesced column stores) unless the epilogue reads the aux
-  // operand: its loads are latency-bound either way, and row-wise they issue
-  // as 16-byte vectors.
-  const bool reads_aux = epilogue == NS_EPI_BIAS_RESID || epilogue == NS_EPI_GELU_BWD;
-  const int trans_mode = (t_engine == 5 || (t_engine == 0 && reads_aux)) ? 0 : 1;
+  // The wide kernels compute C^T (coalesced column stores); epilogues that
+  // read the aux operand then run as a separate pass (tc::run).
+  const int trans_mode = t_engine == 5 ? 0 : 1;
   const size_t lo_bytes = ((a_lo_in ? 0 : tc::lo_elems_a(M, K)) + (b_lo_in ? 0 : tc::lo_elems_a(N, K))) *
                           sizeof(float);
   tc::Plan pl{};

@@ -772,6 +772,28 @@ __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int 
   }
 }
 
+// The epilogue as a separate pass over C (C holds the raw product): for
+// epilogues that read the aux operand after a transposed-product GEMM, whose
+// own stores cannot issue those loads efficiently.  Same operations, same
+// order as the fused epilogue.
+__global__ void epi_apply_k(int M, int N, const EpiArgs e_param, int vec) {
+  const EpiArgs e = e_param;
+  const int64_t total = (int64_t)M * N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < total; i += stride * 4) {
+      const int m = (int)(i / N), n = (int)(i % N);
+      const float4 a = *reinterpret_cast<const float4*>(e.C + (size_t)m * e.ldc + n);
+      epi_store4(e, m, n, a);
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+      const int m = (int)(i / N), n = (int)(i % N);
+      epi_store(e, m, n, e.C[(size_t)m * e.ldc + n]);
+    }
+  }
+}
+
 // Ordered sum of the split-K partial tiles, then the epilogue.
 __global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M, int N,
                                 const EpiArgs e_param, int vec) {
@@ -1351,12 +1373,31 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   kp.trans_out = pl.trans;
   kp.out_m = out_m;
   kp.out_n = out_n;
+  // Transposed single-pass plans store the raw product and apply epilogues
+  // that read aux in a separate coalesced pass.
+  const bool late_epi = pl.trans && pl.splits == 1 &&
+                        (e.epi == NS_EPI_BIAS_RESID || e.epi == NS_EPI_GELU_BWD);
+  if (late_epi) {
+    kp.e.epi = NS_EPI_STORE;
+    kp.e.beta = 0.0f;
+  }
   if (pl.bn == kWideBN && !pre) return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
   rc = pl.pair             ? launch_pair(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pre            ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)
                         : launch<128, 5, false>(pl, ta, tb, ta_lo, tb_lo, kp, stream);
-  if (rc != NS_OK || pl.splits == 1) return rc;
+  if (rc != NS_OK) return rc;
+  if (late_epi) {
+    const int64_t total = (int64_t)out_m * out_n;
+    const int vec = ((reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
+                      reinterpret_cast<uintptr_t>(e.bias)) & 15) == 0 && (e.ldc % 4) == 0 &&
+                    (out_n % 4) == 0;
+    const int64_t work = vec ? total / 4 : total;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
+    epi_apply_k<<<grid, 256, 0, stream>>>(out_m, out_n, e, vec);
+    return check_launch("ns_gemm epilogue pass");
+  }
+  if (pl.splits == 1) return rc;
   const int64_t total = (int64_t)out_m * out_n;
   const int vec = ((reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
                     reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
