@@ -121,9 +121,9 @@ NS_API ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_
  * (tcgen05 wherever the operands allow TMA, SIMT fp32 otherwise), 1 = always
  * the SIMT fp32 kernel, 2 = tcgen05 with the operands' tf32 lo parts always
  * computed inside the kernel (never pre-split into the workspace), 3 / 4 =
- * pre-split operands on 256 x 256 CTA-pair tiles / 128 x 256 tiles only
+ * pre-split operands on CTA-pair tiles (256 x 256, 192 or 128) / 128 x 256 tiles only
  * (where the workspace allows), 5 = as 4 but storing rows of C instead of
- * computing C^T.  Used by tests and profiling to cross-check
+ * computing C^T, 6 / 7 = CTA-pair tiles 256 x 192 / 256 x 128 only.  Used by tests and profiling to cross-check
  * the engines. */
 NS_API ns_status ns_gemm_set_engine(int engine);
 /* NS_ERR_TIMEOUT if any kernel of this library gave up a bounded wait on the

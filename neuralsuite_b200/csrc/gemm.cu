@@ -13,7 +13,8 @@ namespace nsb {
 namespace {
 
 // 0 auto, 1 SIMT, 2 tcgen05 with in-kernel operand split, 3 / 4: pre-split operands on
-// 256 x 256 pair tiles / 128 x 256 tiles only, 5: 128 x 256 tiles storing rows (not C^T)
+// 256 x 256 pair tiles / 128 x 256 tiles only, 5: 128 x 256 tiles storing rows (not C^T),
+// 6 / 7: pair tiles 256 x 192 / 256 x 128 only
 thread_local int t_engine = 0;
 
 constexpr int kSB = 64, kSK = 16;
@@ -103,7 +104,7 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
   // Enough for any plan ns_gemm may pick (every kernel, both store orientations).
   size_t part = 0;
   for (bool wide : {true, false})
-    for (int force = -1; force <= 2; ++force)
+    for (int force = -1; force <= 4; ++force)
       for (int trans = 0; trans <= 1; ++trans) {
         if (!wide && force > 0) continue;
         const tc::Plan p = tc::plan(M, N, K, true, wide, force, trans);
@@ -113,7 +114,7 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine >= 0 && engine <= 5, "ns_gemm_set_engine: engine must be 0..5");
+  NS_REQUIRE(engine >= 0 && engine <= 7, "ns_gemm_set_engine: engine must be 0..7");
   t_engine = engine;
   return NS_OK;
 }
@@ -154,7 +155,11 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
   // shared memory.
   const bool ws_ok = workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0;
   const bool pre_ok = (t_engine == 0 || t_engine >= 3) && a_cols % 4 == 0 && b_cols % 4 == 0;
-  const int force = t_engine == 3 ? 2 : (t_engine == 4 || t_engine == 5) ? 1 : -1;
+  const int force = t_engine == 3   ? 2
+                    : (t_engine == 4 || t_engine == 5) ? 1
+                    : t_engine == 6 ? 3
+                    : t_engine == 7 ? 4
+                                    : -1;
   // The wide kernels compute C^T (coalesced column stores); epilogues that
   // read the aux operand then run as a separate pass (tc::run).
   const int trans_mode = t_engine == 5 ? 0 : 1;

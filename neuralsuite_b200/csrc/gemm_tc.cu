@@ -846,15 +846,18 @@ ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
 // fold warps report folded chunks with cluster-scope mbarrier arrives.  Each CTA's TMEM holds
 // its 128 rows of two 256-column chunk buffers; the running sums live in the
 // registers of its eight fold warps as in the 128 x 256 kernel.
-constexpr int kPairStages = 3;
-
+// BN (the tile's second extent: 256, 192 or 128) is a template parameter so
+// that the planner can pick the width that packs a shape's tiles best onto
+// the 74 pairs; narrower tiles leave room for a fourth stage.
+template <int BN>
 struct PairLayout {
-  static constexpr uint32_t kA = kBM * kBK * 4;  // 16 KB: this CTA's 128 rows of A
-  static constexpr uint32_t kB = 128 * kBK * 4;  // 16 KB: this CTA's half of B
+  static constexpr uint32_t kA = kBM * kBK * 4;         // 16 KB: this CTA's 128 rows of A
+  static constexpr uint32_t kB = (BN / 2) * kBK * 4;    // this CTA's half of B
   static constexpr uint32_t kRaw = kA + kB;
   static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
-  static constexpr uint32_t kBars = kPairStages * kStage;
-  static constexpr uint32_t kNumBars = 3 * kPairStages + 5;
+  static constexpr int kStages = (4 * kStage + 2048 <= 232448) ? 4 : 3;
+  static constexpr uint32_t kBars = kStages * kStage;
+  static constexpr uint32_t kNumBars = 3 * kStages + 5;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
@@ -907,13 +910,14 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
       : "memory");
 }
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAlo,
                      const __grid_constant__ CUtensorMap tmBlo, const KParams p) {
-  using L = PairLayout;
-  constexpr int S = kPairStages;
-  constexpr int BN = 256;
+  using L = PairLayout<BN>;
+  constexpr int S = L::kStages;
+  constexpr int HB = BN / 2;  // this CTA's share of the tile's second extent
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -974,7 +978,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         for (int u = unit0; ok && u < n_units; u += unit_step) {
           int tm, tn, split, kb0, kb1;
           decode_unit(p, u, tm, tn, split, kb0, kb1);
-          const int m0 = tm * 256 + (int)rank * kBM, n0 = tn * BN + (int)rank * 128;
+          const int m0 = tm * 256 + (int)rank * kBM, n0 = tn * BN + (int)rank * HB;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = it % S;
             const uint32_t ph = (it / S) & 1u;
@@ -1010,7 +1014,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                 tma_load_2d_pair(b_dst + off, mb, bar, k0, n0);
               } else {
 #pragma unroll
-                for (int j = 0; j < 128 / 32; ++j)
+                for (int j = 0; j < HB / 32; ++j)
                   tma_load_2d_pair(b_dst + off + j * 4096, mb, bar, n0 + 32 * j, k0);
               }
             }
@@ -1102,16 +1106,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     // ------------------------------------------------------------ fold + epilogue (both CTAs)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWideHighRegs));
     const int ew = warp & 3;
-    const int col0 = ((warp - 4) >> 2) * 128;
+    const int col0 = ((warp - 4) >> 2) * HB;
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
     uint32_t cit = 0;
     bool ok = true;
-    float acc[128];
+    float acc[HB];
     for (int u = unit0; ok && u < n_units; u += unit_step) {
       int tm, tn, split, kb0, kb1;
       decode_unit(p, u, tm, tn, split, kb0, kb1);
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
       for (int c0 = kb0; c0 < kb1; c0 += kChunk, ++cit) {
         const int cb = cit & 1;
         if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
@@ -1121,15 +1125,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         fence_after();
         const uint32_t c_tmem = tmem_base + lane_off + cb * BN + col0;
 #pragma unroll
-        for (int c = 0; c < 4; c += 2) {
+        for (int c = 0; c < HB / 32; c += 2) {
           uint32_t a[32], b[32];
           tmem_ld32_nowait(c_tmem + 32 * c, a);
-          tmem_ld32_nowait(c_tmem + 32 * (c + 1), b);
+          if (c + 1 < HB / 32) tmem_ld32_nowait(c_tmem + 32 * (c + 1), b);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            acc[32 * c + j] = __fadd_rn(acc[32 * c + j], __uint_as_float(a[j]));
-            acc[32 * (c + 1) + j] = __fadd_rn(acc[32 * (c + 1) + j], __uint_as_float(b[j]));
+          for (int j = 0; j < 32; ++j) acc[32 * c + j] = __fadd_rn(acc[32 * c + j], __uint_as_float(a[j]));
+          if (c + 1 < HB / 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              acc[32 * (c + 1) + j] = __fadd_rn(acc[32 * (c + 1) + j], __uint_as_float(b[j]));
           }
         }
         fence_before();
@@ -1144,11 +1150,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       const int m = tm * 256 + (int)rank * kBM + ew * 32 + lane;
       const int n_base = tn * BN + col0;
       if (p.trans_out) {
-        // This thread's TMEM lane is output column n; its registers hold 128
+        // This thread's TMEM lane is output column n; its registers hold HB
         // consecutive output rows, so each warp store covers 32 consecutive
         // columns of one row of C (coalesced).
         const int n_out = m, m0_out = n_base;
-        const int rows = min(128, p.out_m - m0_out);
+        const int rows = min(HB, p.out_m - m0_out);
         if (n_out < p.out_n && rows > 0) {
           // Epilogue arguments in registers (not re-read from parameter space per element).
           const EpiArgs e = p.e;
@@ -1156,23 +1162,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
             float* dst = p.splits > 1 ? p.ws + ((size_t)split * p.out_m + m0_out) * p.out_n + n_out
                                       : e.C + (size_t)m0_out * e.ldc + n_out;
             const size_t ld = p.splits > 1 ? (size_t)p.out_n : (size_t)e.ldc;
-            if (rows == 128) {
+            if (rows == HB) {
 #pragma unroll
-              for (int j = 0; j < 128; ++j) dst[j * ld] = acc[j];
+              for (int j = 0; j < HB; ++j) dst[j * ld] = acc[j];
             } else {
 #pragma unroll
-              for (int j = 0; j < 128; ++j)
+              for (int j = 0; j < HB; ++j)
                 if (j < rows) dst[j * ld] = acc[j];
             }
           } else {
-            epi_store_col<128>(e, m0_out, n_out, rows, acc);
+            epi_store_col<HB>(e, m0_out, n_out, rows, acc);
           }
         }
         continue;
       }
       const EpiArgs e = p.e;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HB / 32; ++c) {
         const int n0 = n_base + c * 32;
         if (m < p.M && n0 < p.N) {
           const float* v = acc + 32 * c;
@@ -1212,18 +1218,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
   }
 }
 
+template <int BN>
+ns_status launch_pair_bn(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
+                         const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
+                         cudaStream_t s) {
+  using L = PairLayout<BN>;
+  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)L::kDynSmem),
+              "ns_gemm attr");
+  cudaFuncAttributes fa;
+  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_pair_kernel<BN>), "ns_gemm attributes");
+  if (fa.numRegs < kWideMinLaunchRegs)
+    return fail(NS_ERR_UNSUPPORTED, "ns_gemm: pair kernel compiled with too few registers for its split");
+  gemm_pair_kernel<BN><<<2 * pl.grid, kWideThreads, L::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
+  return check_launch("ns_gemm tcgen05 pair");
+}
+
 ns_status launch_pair(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
                       const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const KParams& kp,
                       cudaStream_t s) {
-  NS_TRY_CUDA(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)PairLayout::kDynSmem),
-              "ns_gemm attr");
-  cudaFuncAttributes fa;
-  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_pair_kernel), "ns_gemm attributes");
-  if (fa.numRegs < kWideMinLaunchRegs)
-    return fail(NS_ERR_UNSUPPORTED, "ns_gemm: pair kernel compiled with too few registers for its split");
-  gemm_pair_kernel<<<2 * pl.grid, kWideThreads, PairLayout::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
-  return check_launch("ns_gemm tcgen05 pair");
+  switch (pl.bn) {
+    case 256: return launch_pair_bn<256>(pl, ta, tb, ta_lo, tb_lo, kp, s);
+    case 192: return launch_pair_bn<192>(pl, ta, tb, ta_lo, tb_lo, kp, s);
+    case 128: return launch_pair_bn<128>(pl, ta, tb, ta_lo, tb_lo, kp, s);
+    default: return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: unsupported pair tile width");
+  }
 }
 
 ns_status launch_wide(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -1261,19 +1280,25 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
   double best_cost = 1e30;
   // Kernels: 128 x 128 tiles; 128 x 256 tiles (one CTA); 256 x 256 tiles (a
   // CTA pair).  The two wide ones need pre-split operands.
-  for (int kind = 0; kind < 3; ++kind) {
-    if (kind > 0 && !allow_wide) continue;
-    if (force_kind >= 0 && kind != force_kind) continue;
-    const int bm = kind == 2 ? 256 : kBM, bn = kind == 0 ? 128 : 256;
-    const int slots = kind == 2 ? sms / 2 : sms;  // concurrent units
+  for (int kind = 0; kind < 5; ++kind) {
+    // kind 2, 3, 4: CTA-pair tiles 256 x 256, 256 x 192, 256 x 128
+    const int fk = kind > 2 ? 2 : kind;
+    if (fk > 0 && !allow_wide) continue;
+    if (force_kind >= 0 && force_kind <= 2 && fk != force_kind) continue;
+    if (force_kind == 3 && kind != 3) continue;  // pair tiles 256 x 192 only
+    if (force_kind == 4 && kind != 4) continue;  // pair tiles 256 x 128 only
+    const int bm = fk == 2 ? 256 : kBM;
+    const int bn = kind == 0 ? 128 : kind == 3 ? 192 : kind == 4 ? 128 : 256;
+    const int slots = fk == 2 ? sms / 2 : sms;  // concurrent units
     // The wide kernels compute C^T (coalesced stores): their rows are C's columns.
-    const bool tr = kind != 0 && trans_mode == 1;
+    const bool tr = fk != 0 && trans_mode == 1;
     const int rows = tr ? N : M, cols = tr ? M : N;
     const int tiles_m = ceil_div(rows, bm), tiles_n = ceil_div(cols, bn);
     const int tiles = tiles_m * tiles_n;
     const int max_split = allow_split ? std::min(kb_total, 16) : 1;
-    // Measured cycles per k-block of a unit (the MMA alone needs 768, 1536, 1536).
-    const double kb_cycles = kind == 0 ? 1600.0 : kind == 1 ? 2100.0 : 1950.0;
+    // Measured cycles per k-block of a unit (the MMA alone needs 768, 1536, 1536
+    // for 256 x 256 pairs; narrower pairs scale with the width).
+    const double kb_cycles = kind == 0 ? 1600.0 : kind == 1 ? 2100.0 : 200.0 + 1750.0 * bn / 256.0;
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kb_per = ceil_div(kb_total, sp);
       const int splits = ceil_div(kb_total, kb_per);
@@ -1286,9 +1311,9 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
       if (cost < best_cost * 0.98) {
         best_cost = cost;
         best.bn = bn;
-        best.pair = kind == 2 ? 1 : 0;
+        best.pair = fk == 2 ? 1 : 0;
         best.trans = tr ? 1 : 0;
-        best.stages = kind == 0 ? 3 : kind == 1 ? kWideStages : kPairStages;
+        best.stages = 0;
         best.tiles_m = tiles_m;
         best.tiles_n = tiles_n;
         best.splits = splits;
@@ -1332,7 +1357,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   std::memset(&tb_lo, 0, sizeof(tb_lo));
   ns_status rc = a_mn ? tcx::make_map(&ta, A, M, K, lda, 32, true) : tcx::make_map(&ta, A, K, M, lda, kBM, false);
   if (rc != NS_OK) return rc;
-  const int b_box = pl.pair ? 128 : pl.bn;  // rows of B per CTA
+  const int b_box = pl.pair ? pl.bn / 2 : pl.bn;  // rows of B per CTA
   rc = b_mn ? tcx::make_map(&tb, B, N, K, ldb, 32, true) : tcx::make_map(&tb, B, K, N, ldb, b_box, false);
   if (rc != NS_OK) return rc;
   const bool pre = lo_ws != nullptr || (a_lo_in && b_lo_in);
@@ -1381,7 +1406,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
     kp.e.epi = NS_EPI_STORE;
     kp.e.beta = 0.0f;
   }
-  if (pl.bn == kWideBN && !pre) return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
+  if ((pl.pair || pl.bn == kWideBN) && !pre)
+    return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
   rc = pl.pair             ? launch_pair(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pl.bn == kWideBN ? launch_wide(pl, ta, tb, ta_lo, tb_lo, kp, stream)
        : pre            ? launch<128, 3, true>(pl, ta, tb, ta_lo, tb_lo, kp, stream)

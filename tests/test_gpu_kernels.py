@@ -70,7 +70,8 @@ def test_gemm_tf32_split_recovers_fp32(cuda):
 FULL = [(8192, 768, 3072), (8192, 3072, 768), (16384, 1024, 4096)]
 
 
-@pytest.fixture(params=[0, 2, 3, 4, 5], ids=["auto", "inkernel", "pair", "wide", "widerows"])
+@pytest.fixture(params=[0, 2, 3, 4, 5, 6, 7],
+                ids=["auto", "inkernel", "pair", "wide", "widerows", "pair192", "pair128"])
 def gemm_engine(request):
     nk.set_gemm_engine(request.param)
     yield request.param
@@ -117,7 +118,7 @@ def test_gemm_engines_agree_and_epilogues(cuda, port):
     Xd, Wd, bd, Rd = dev(X, cuda), dev(W, cuda), dev(b, cuda), dev(R, cuda)
     base = port.matmul(X, W)
     base64 = fp64.matmul(X, W)
-    for engine in (0, 1, 2, 3, 4, 5):
+    for engine in (0, 1, 2, 3, 4, 5, 6, 7):
         nk.set_gemm_engine(engine)
         try:
             y = host(nk.gemm(Xd, Wd, epilogue=_lib.EPI_BIAS, bias=bd))
