@@ -136,6 +136,13 @@ NS_API ns_status ns_kernel_health(void);
 NS_API size_t ns_bias_grad_workspace_size(int M, int N);
 NS_API ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace,
                        size_t workspace_bytes, void* stream);
+/* ns_bias_grad that also writes dy_lo = ns_split_lo(dY) from the same pass
+ * over dY (Linear::Backward needs both: db, and dY's tf32 lo part for the dX
+ * and dW products through ns_gemm_lo).  N a multiple of 4, 16-byte aligned
+ * pointers; same workspace as ns_bias_grad; db bit-identical to it.  No
+ * reference counterpart (a fusion of linear.h:104-111 with the operand split). */
+NS_API ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy_lo,
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------ K2 attention
  * Fused causal self-attention on the interleaved c_attn output

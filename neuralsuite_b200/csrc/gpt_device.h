@@ -268,8 +268,10 @@ class Linear : public Layer {
     const float* w_lo = lo ? w_lo_buf_.Data() : nullptr;
     const float* dy_lo = nullptr;
     if (lo) {
+      // db and dY's lo part from one pass over dY.
       Tensor dl = Scratch(dy_lo_buf_, n, out_);
-      Check(ns_split_lo(dy.Data(), n, out_, out_, dl.Data(), stream()));
+      Check(ns_bias_grad_split(dy.Data(), n, out_, bias_.Grad().Data(), dl.Data(), ctx_->scratch,
+                               ctx_->scratch_bytes, stream()));
       dy_lo = dl.Data();
     }
     // dX = dY W^T  (W read transposed in place: no Transpose copy)
@@ -280,9 +282,10 @@ class Linear : public Layer {
     Check(ns_gemm_lo(in_, out_, n, last_input_.Data(), in_, 1, x_lo, dy.Data(), out_, 0, dy_lo,
                      weight_.Grad().Data(), out_, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
                      ctx_->scratch, ctx_->scratch_bytes, stream()));
-    // db = column sums of dY, overwritten.
-    Check(ns_bias_grad(dy.Data(), n, out_, bias_.Grad().Data(), ctx_->scratch, ctx_->scratch_bytes,
-                       stream()));
+    // db = column sums of dY, overwritten (with the split above when it ran).
+    if (!lo)
+      Check(ns_bias_grad(dy.Data(), n, out_, bias_.Grad().Data(), ctx_->scratch, ctx_->scratch_bytes,
+                         stream()));
     return dx.View(last_input_.Shape());
   }
 

@@ -267,8 +267,12 @@ __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ p
 
 // Stage 1 of the bias gradient: CTA (chunk) sums rows [r0, r1) of a
 // 128-column slab (lane = 4 consecutive columns, warp = rows strided by 8).
+// With LO, the same pass also writes lo = y - trunc_tf32(y) (the GEMM operand
+// split of y, compact), so the bias gradient of dY costs no extra read.
+template <bool LO>
 __global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ y, int M, int N,
-                                                      int rows_per_cta, float* __restrict__ part) {
+                                                      int rows_per_cta, float* __restrict__ part,
+                                                      float* __restrict__ lo) {
   __shared__ float4 red[kRowsWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = (blockIdx.x * 32 + lane) * 4;
@@ -282,6 +286,14 @@ __global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ 
       if (vec) {
         const float4 v = *reinterpret_cast<const float4*>(p);
         s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+        if (LO) {
+          float4 l;
+          l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          *reinterpret_cast<float4*>(lo + (size_t)r * N + col) = l;
+        }
       } else {
         s.x += p[0];
         if (col + 1 < N) s.y += p[1];
@@ -431,10 +443,27 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part);
+  colsum_partial<false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, nullptr);
   { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
   colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db);
   return check_launch("ns_bias_grad stage 2");
+}
+
+ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy_lo,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(M > 0 && N > 0 && (N & 3) == 0, "ns_bias_grad_split: N must be a positive multiple of 4");
+  NS_REQUIRE(((reinterpret_cast<uintptr_t>(dY) | reinterpret_cast<uintptr_t>(dy_lo)) & 15) == 0,
+             "ns_bias_grad_split: dY and dy_lo must be 16-byte aligned");
+  NS_REQUIRE(workspace && workspace_bytes >= ns_bias_grad_workspace_size(M, N),
+             "ns_bias_grad_split: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  const int chunks = bias_chunks(M, N);
+  const int rpc = ceil_div(M, chunks);
+  float* part = static_cast<float*>(workspace);
+  colsum_partial<true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo);
+  { ns_status _rc = check_launch("ns_bias_grad_split stage 1"); if (_rc != NS_OK) return _rc; }
+  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db);
+  return check_launch("ns_bias_grad_split stage 2");
 }
 
 }  // extern "C"

@@ -126,6 +126,19 @@ def attn_bwd(qkv, out, dout, lse, B, T, H, D):
     return dqkv
 
 
+def bias_grad_split(dY):
+    """(db, lo part of dY) from one pass (ns_bias_grad_split)."""
+    lib = _lib.load()
+    _req(dY, "dY")
+    M, N = dY.shape
+    db = torch.empty(N, dtype=_f32, device=dY.device)
+    lo = torch.empty_like(dY)
+    nb = lib.ns_bias_grad_workspace_size(M, N)
+    ws = _ws(nb, dY.device)
+    _lib.check(lib.ns_bias_grad_split(_p(dY), M, N, _p(db), _p(lo), _p(ws), nb, _stream()))
+    return db, lo
+
+
 def layernorm_fwd(x, gamma, beta, eps=1e-5):
     """LayerNormForward (src/tensor.cpp:290-322)."""
     lib = _lib.load()

@@ -165,6 +165,14 @@ def test_gemm_lo_equals_gemm_bitwise(cuda, M, K, N, at, bt):
     nk.kernel_health()
 
 
+def test_bias_grad_split_matches_parts_bitwise(cuda):
+    """ns_bias_grad_split = ns_bias_grad + ns_split_lo, bit for bit."""
+    dY = dev(normal(rng(31), (8192, 768)), cuda)
+    db, lo = nk.bias_grad_split(dY)
+    assert np.array_equal(host(db).view(np.uint32), host(nk.bias_grad(dY)).view(np.uint32))
+    assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(dY)).view(np.uint32))
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
