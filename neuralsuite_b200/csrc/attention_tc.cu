@@ -507,13 +507,23 @@ ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* l
 // tensor that one kernel reads both K-major (for S or dP) and MN-major (for
 // the gradient product) is loaded twice, once per swizzle, because the
 // tensor core reads MN-major tf32 operands only from the 32-byte-atom swizzle
-// and K-major ones only from the 16-byte-chunk one.  With every operand held
-// as hi + lo, TMEM has room for one set of S / dP / product buffers, so the
-// tensor core computes S_{i+1} (and dP_{i+1}) while the element-wise warps
-// fold the previous product, and waits while they turn S_i into P_i / dS_i.
-// The eight element-wise warps split each 64-column block in halves: once
-// lse is known, no row reduction is needed.  Each block's product (a 64-term
-// tensor-core sum) is folded into registers with round-to-nearest adds.
+// and K-major ones only from the 16-byte-chunk one.
+//
+// Each B operand has its own TMA ring and producer warp (warp 0: the S
+// operand, warp 2: the dP operand, warp 3: the product operand plus the
+// block's lse / Delta vectors), because the three are consumed about one block
+// apart.  With every A operand held as hi + lo, TMEM has room for one S, one
+// dP, one product lo part and one product accumulator, so the order of work
+// is what overlaps the tensor core with the eight element-wise warps:
+//   tensor core:   ... product_j | dP_{j+1} | S_{j+2} | (wait E_{j+1}) product_{j+1} ...
+//   element-wise:  S_{j+1} read (frees S) -> P_{j+1} = exp(..) while product_j and
+//                  dP_{j+1} run -> fold product_j -> dS_{j+1} -> E_{j+1} hi/lo to TMEM
+// S is freed as soon as it is read, so S_{j+2} is computed while the
+// element-wise warps finish block j+1; the product's operand E (P^T or dS)
+// goes over dP (unused by kDV) with its lo part apart.  Each block's product
+// (a 64-term tensor-core sum) is folded into registers with round-to-nearest
+// adds; the eight element-wise warps split each 64-column block in halves
+// (once lse is known, no row reduction is needed).
 
 enum BwdMode { kDV = 0, kDK = 1, kDQ = 2 };
 
@@ -523,14 +533,19 @@ constexpr uint32_t kBA1 = 0, kBA2 = 128, kBS = 256, kBdP = 320, kBElo = 384, kBO
 
 template <int MODE, int D>
 struct BwdLayout {
-  static constexpr int kTiles = MODE == kDV ? 2 : 3;  // B tiles per stage
-  static constexpr int kStages = D == 64 ? (MODE == kDV ? 3 : 2) : (MODE == kDV ? 4 : 3);
+  static constexpr bool kTwoA = MODE != kDV;
+  static constexpr bool kKeyMajor = MODE != kDQ;
+  static constexpr int kRing = D == 64 ? (kTwoA ? 2 : 3) : (kTwoA ? 4 : 6);  // slots per ring
   static constexpr uint32_t kTile = kBKV * D * 4;  // 64 x D fp32 (D/32 boxes of 8 KB)
-  static constexpr uint32_t kVecOff = kTiles * 2 * kTile;
-  static constexpr uint32_t kVec = MODE == kDQ ? 0 : 1024;  // lse*log2e [64], Delta [64]
-  static constexpr uint32_t kStage = kVecOff + kVec;
-  static constexpr uint32_t kBars = kStages * kStage;
-  static constexpr uint32_t kNumBars = 2 * kStages + 6;
+  static constexpr uint32_t kSlot = 2 * kTile;     // raw | lo
+  // Product-ring slots also carry lse*log2e [64] and Delta [64] of the block's
+  // queries (key-major modes), padded to keep every tile 1024-byte aligned.
+  static constexpr uint32_t kSlot2 = kSlot + (kKeyMajor ? 1024 : 0);
+  static constexpr uint32_t kRing0 = 0;                                       // S operand
+  static constexpr uint32_t kRing1 = kRing0 + kRing * kSlot;                  // dP operand
+  static constexpr uint32_t kRing2 = kRing1 + (kTwoA ? kRing * kSlot : 0);    // product operand
+  static constexpr uint32_t kBars = kRing2 + kRing * kSlot2;
+  static constexpr uint32_t kNumBars = 6 * kRing + 7;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static_assert(kDynSmem <= 232448, "shared memory budget");
@@ -545,8 +560,64 @@ struct BwdParams {
   float* dqkv;
   int T, H, C;
   float scale, scale_log2;
-  int xb0, xb1, xb2;  // column of tile t's tensor for head 0 (head h adds h*D)
+  int xb0, xb1, xb2;  // column of ring r's tensor for head 0 (head h adds h*D)
 };
+
+// One producer warp: the ring of one B operand (raw and lo tiles of each
+// minor block; for the product ring of a key-major kernel also the block's
+// lse / Delta vectors).  Returns false if a wait gave up; the copies already
+// issued have landed when it returns.
+template <int D, int R, bool VEC>
+__device__ bool produce_ring(uint32_t ring, uint32_t slot_bytes, uint32_t full0, uint32_t empty0,
+                             const CUtensorMap* m, const CUtensorMap* mlo, int xcol, int row0,
+                             int blk0, int n_blk, uint8_t* smem_ring, const BwdParams& p, int bh,
+                             volatile int* abort) {
+  constexpr uint32_t kTile = kBKV * D * 4;
+  const int lane = threadIdx.x & 31;
+  bool issued[R];
+  uint32_t issued_ph[R];
+#pragma unroll
+  for (int s = 0; s < R; ++s) issued[s] = false, issued_ph[s] = 0;
+  bool ok = true;
+  for (int i = 0; i < n_blk; ++i) {
+    const int s = i % R;
+    const uint32_t ph = (uint32_t)(i / R) & 1u;
+    if (!warp_wait(empty0 + 8u * s, ph ^ 1u, abort, &g_timeout)) {
+      ok = false;
+      break;
+    }
+    issued[s] = true;
+    issued_ph[s] = ph;
+    const int blk = blk0 + i;
+    const int row = row0 + blk * kBKV;
+    const uint32_t dst = ring + s * slot_bytes;
+    if (elect_one()) {
+      mbar_expect_tx(full0 + 8u * s, 2 * kTile);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        tma_load_2d(dst + c * 8192, m, full0 + 8u * s, xcol + 32 * c, row);
+        tma_load_2d(dst + kTile + c * 8192, mlo, full0 + 8u * s, xcol + 32 * c, row);
+      }
+    }
+    __syncwarp();
+    if (VEC) {
+      float* vec = reinterpret_cast<float*>(smem_ring + s * slot_bytes + 2 * kTile);
+      for (int c = lane; c < kBKV; c += 32) {
+        const int q = blk * kBKV + c;
+        const bool in = q < p.T;
+        vec[c] = in ? p.lse[(size_t)bh * p.T + q] * kLog2e : 0.0f;
+        vec[kBKV + c] = in ? p.delta[(size_t)bh * p.T + q] : 0.0f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full0 + 8u * s);
+      __syncwarp();
+    }
+  }
+  if (!ok && lane == 0)
+    for (int s = 0; s < R; ++s)
+      if (issued[s]) mbar_wait_drain(full0 + 8u * s, issued_ph[s], &g_timeout);
+  return ok;
+}
 
 template <int MODE, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -555,19 +626,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tm2, const __grid_constant__ CUtensorMap tm2lo,
                        const BwdParams p) {
   using L = BwdLayout<MODE, D>;
-  constexpr int S = L::kStages;
-  constexpr bool kKeyMajor = MODE != kDQ;
-  constexpr bool kTwoA = MODE != kDV;
+  constexpr int R = L::kRing;
+  constexpr bool kKeyMajor = L::kKeyMajor;
+  constexpr bool kTwoA = L::kTwoA;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBars;
-  auto kv_full = [&](int s) { return bar0 + 8u * s; };
-  auto kv_empty = [&](int s) { return bar0 + 8u * (S + s); };
-  const uint32_t a_ready = bar0 + 8u * (2 * S);
-  const uint32_t s_full = a_ready + 8u, ew_done = a_ready + 16u, out_full = a_ready + 24u;
-  const uint32_t out_empty = a_ready + 32u, drain = a_ready + 40u;
+  const uint32_t full0 = bar0, empty0 = bar0 + 8u * R;
+  const uint32_t full1 = bar0 + 16u * R, empty1 = bar0 + 24u * R;
+  const uint32_t full2 = bar0 + 32u * R, empty2 = bar0 + 40u * R;
+  const uint32_t a_ready = bar0 + 48u * R;
+  const uint32_t s_full = a_ready + 8u, s_free = a_ready + 16u, dp_full = a_ready + 24u;
+  const uint32_t ew_done = a_ready + 32u, out_full = a_ready + 40u, drain = a_ready + 48u;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -587,15 +659,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(kv_full(s), kKeyMajor ? 2 : 1);
-      mbar_init(kv_empty(s), 1);
+    for (int s = 0; s < R; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+      mbar_init(full1 + 8u * s, 1);
+      mbar_init(empty1 + 8u * s, 1);
+      mbar_init(full2 + 8u * s, kKeyMajor ? 2 : 1);
+      mbar_init(empty2 + 8u * s, 1);
     }
     mbar_init(a_ready, 2 * kWgThreads);
     mbar_init(s_full, 1);
+    mbar_init(s_free, 2 * kWgThreads);
+    mbar_init(dp_full, 1);
     mbar_init(ew_done, 2 * kWgThreads);
     mbar_init(out_full, 1);
-    mbar_init(out_empty, 2 * kWgThreads);
     mbar_init(drain, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -614,123 +691,117 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
     reg_dec();
+    const int xo = h * D;
     if (warp == 0) {
-      // ---------------------------------------------------------- producer
-      int issued[S];
-      uint32_t issued_ph[S];
-      for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
-      bool ok = true;
-      for (int i = 0; i < n_blk; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (!warp_wait(kv_empty(s), ph ^ 1u, abort, &g_timeout)) {
-          ok = false;
-          break;
-        }
-        issued[s] = 1;
-        issued_ph[s] = ph;
-        const int blk = blk0 + i;
-        const int row = b * p.T + blk * kBKV;
-        const uint32_t dst = sbase + s * L::kStage;
-        if (elect_one()) {
-          mbar_expect_tx(kv_full(s), L::kVecOff);
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            const int xo = h * D + 32 * c;
-            tma_load_2d(dst + c * 8192, &tm0, kv_full(s), p.xb0 + xo, row);
-            tma_load_2d(dst + L::kTile + c * 8192, &tm0lo, kv_full(s), p.xb0 + xo, row);
-            tma_load_2d(dst + 2 * L::kTile + c * 8192, &tm1, kv_full(s), p.xb1 + xo, row);
-            tma_load_2d(dst + 3 * L::kTile + c * 8192, &tm1lo, kv_full(s), p.xb1 + xo, row);
-            if (L::kTiles == 3) {
-              tma_load_2d(dst + 4 * L::kTile + c * 8192, &tm2, kv_full(s), p.xb2 + xo, row);
-              tma_load_2d(dst + 5 * L::kTile + c * 8192, &tm2lo, kv_full(s), p.xb2 + xo, row);
-            }
-          }
-        }
-        __syncwarp();
-        if (kKeyMajor) {
-          // lse (in log2 units) and Delta of this block's 64 queries.
-          float* vec = reinterpret_cast<float*>(smem + s * L::kStage + L::kVecOff);
-          for (int c = lane; c < kBKV; c += 32) {
-            const int q = blk * kBKV + c;
-            const bool in = q < p.T;
-            vec[c] = in ? p.lse[(size_t)bh * p.T + q] * kLog2e : 0.0f;
-            vec[kBKV + c] = in ? p.delta[(size_t)bh * p.T + q] : 0.0f;
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(kv_full(s));
-          __syncwarp();
-        }
-      }
-      if (!ok && lane == 0)
-        for (int s = 0; s < S; ++s)
-          if (issued[s]) mbar_wait_drain(kv_full(s), issued_ph[s], &g_timeout);
-    } else if (warp == 1) {
+      // ---------------------------------------------------------- S operand
+      produce_ring<D, R, false>(sbase + L::kRing0, L::kSlot, full0, empty0, &tm0, &tm0lo,
+                                p.xb0 + xo, b * p.T, blk0, n_blk, smem + L::kRing0, p, bh, abort);
+    } else if (warp == 2) {
+      // ---------------------------------------------------------- dP operand
+      if (kTwoA)
+        produce_ring<D, R, false>(sbase + L::kRing1, L::kSlot, full1, empty1, &tm1, &tm1lo,
+                                  p.xb1 + xo, b * p.T, blk0, n_blk, smem + L::kRing1, p, bh, abort);
+    } else if (warp == 3) {
+      // ---------------------------------------------------------- product operand
+      produce_ring<D, R, kKeyMajor>(sbase + L::kRing2, L::kSlot2, full2, empty2, &tm2, &tm2lo,
+                                    p.xb2 + xo, b * p.T, blk0, n_blk, smem + L::kRing2, p, bh,
+                                    abort);
+    } else {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
       constexpr uint32_t id_o = instr_desc(D, 0, 1);
-      bool ok = warp_wait(a_ready, 0, abort, &g_timeout);
-      fence_after();
-      auto issue_sdp = [&](int i) -> bool {
-        const int s = i % S;
-        if (!warp_wait(kv_full(s), (uint32_t)(i / S) & 1u, abort, &g_timeout)) return false;
+      // d = a.b over K = D with a (hi at a, lo at a + D) in TMEM and b's
+      // K-major raw / lo tiles at t / t + kTile: hi.hi first, then the two
+      // cross terms per k-step.
+      auto issue_k = [&](uint32_t d, uint32_t a, uint32_t t) {
+#pragma unroll
+        for (int kk = 0; kk < D / 8; ++kk)
+          mma_ts(d, a + kk * 8, k_desc(t, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < D / 8; ++kk) {
+          mma_ts(d, a + kk * 8, k_desc(t + L::kTile, kk), id_s, 1u);
+          mma_ts(d, a + D + kk * 8, k_desc(t, kk), id_s, 1u);
+        }
+      };
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % R;
+        if (!warp_wait(full0 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
         fence_after();
         if (elect_one()) {
-          const uint32_t t0 = sbase + s * L::kStage, t0lo = t0 + L::kTile;
-#pragma unroll
-          for (int kk = 0; kk < D / 8; ++kk)
-            mma_ts(tmem + kBS, tmem + kBA1 + kk * 8, k_desc(t0, kk), id_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < D / 8; ++kk) {
-            mma_ts(tmem + kBS, tmem + kBA1 + kk * 8, k_desc(t0lo, kk), id_s, 1u);
-            mma_ts(tmem + kBS, tmem + kBA1 + D + kk * 8, k_desc(t0, kk), id_s, 1u);
-          }
-          if (kTwoA) {
-            const uint32_t t1 = t0 + 2 * L::kTile, t1lo = t1 + L::kTile;
-#pragma unroll
-            for (int kk = 0; kk < D / 8; ++kk)
-              mma_ts(tmem + kBdP, tmem + kBA2 + kk * 8, k_desc(t1, kk), id_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < D / 8; ++kk) {
-              mma_ts(tmem + kBdP, tmem + kBA2 + kk * 8, k_desc(t1lo, kk), id_s, 1u);
-              mma_ts(tmem + kBdP, tmem + kBA2 + D + kk * 8, k_desc(t1, kk), id_s, 1u);
-            }
-          }
+          issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s * L::kSlot);
+          commit(empty0 + 8u * s);
           commit(s_full);
         }
         __syncwarp();
         return true;
       };
-      if (ok) ok = issue_sdp(0);
+      auto issue_dp = [&](int j) -> bool {
+        const int s = j % R;
+        if (!warp_wait(full1 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s * L::kSlot);
+          commit(empty1 + 8u * s);
+          commit(dp_full);
+        }
+        __syncwarp();
+        return true;
+      };
+      // Product of block j: A = E (hi over dP, lo apart), B = the MN-major tile.
+      auto issue_out = [&](int j) -> bool {
+        const int s = j % R;
+        if (!warp_wait(full2 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          const uint32_t tb = sbase + L::kRing2 + s * L::kSlot2, tblo = tb + L::kTile;
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk)
+            mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kBKV / 8; ++kk) {
+            mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tblo, kk), id_o, 1u);
+            mma_ts(tmem + kBO, tmem + kBElo + kk * 8, v_desc(tb, kk), id_o, 1u);
+          }
+          commit(empty2 + 8u * s);
+          commit(out_full);
+        }
+        __syncwarp();
+        return true;
+      };
+      bool ok = warp_wait(a_ready, 0, abort, &g_timeout);
+      fence_after();
+      if (ok) ok = issue_s(0);
+      if (ok && kTwoA) ok = issue_dp(0);
+      if (ok && n_blk > 1) {
+        ok = warp_wait(s_free, 0, abort, &g_timeout);
+        fence_after();
+        if (ok) ok = issue_s(1);
+      }
+      // dP_{i+1} overwrites the columns product_i reads and S_{i+2} those S_{i+1}
+      // was read from: each is issued after the MMAs or the reads it must
+      // follow (one CTA's MMAs run in issue order).
       for (int i = 0; ok && i < n_blk; ++i) {
-        if (!warp_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout) ||
-            (i > 0 && !warp_wait(out_empty, (uint32_t)(i - 1) & 1u, abort, &g_timeout))) {
+        if (!warp_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout)) {
           ok = false;
           break;
         }
         fence_after();
-        const int s = i % S;
-        if (elect_one()) {
-          // The MN-major tile is the last of the stage; the element-wise
-          // product (P^T or dS) sits in TMEM: hi over S (kDV) or dP, lo apart.
-          const uint32_t tb = sbase + s * L::kStage + (L::kTiles - 1) * 2 * L::kTile;
-          const uint32_t tblo = tb + L::kTile;
-          const uint32_t ehi = tmem + (MODE == kDV ? kBS : kBdP), elo = tmem + kBElo;
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk)
-            mma_ts(tmem + kBO, ehi + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk) {
-            mma_ts(tmem + kBO, ehi + kk * 8, v_desc(tblo, kk), id_o, 1u);
-            mma_ts(tmem + kBO, elo + kk * 8, v_desc(tb, kk), id_o, 1u);
-          }
-          commit(out_full);
-          commit(kv_empty(s));
+        if (!issue_out(i)) {
+          ok = false;
+          break;
         }
-        __syncwarp();
-        // S_{i+1} / dP_{i+1} overwrite the columns the product just read:
-        // issued after it, and one CTA's MMAs run in issue order.
-        if (i + 1 < n_blk) ok = issue_sdp(i + 1);
+        if (kTwoA && i + 1 < n_blk && !issue_dp(i + 1)) {
+          ok = false;
+          break;
+        }
+        if (i + 2 < n_blk) {
+          if (!warp_wait(s_free, (uint32_t)(i + 1) & 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          ok = issue_s(i + 2);
+        }
       }
       if (!ok) {
         if (elect_one()) commit(drain);
@@ -802,44 +873,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     for (int i = 0; i < n_blk; ++i) {
-      const int s = i % S;
+      const int s = i % R;
       if (!mbar_wait(s_full, (uint32_t)i & 1u, abort, &g_timeout) ||
-          (kKeyMajor && !mbar_wait(kv_full(s), (uint32_t)(i / S) & 1u, abort, &g_timeout))) {
+          (kKeyMajor && !mbar_wait(full2 + 8u * s, (uint32_t)(i / R) & 1u, abort, &g_timeout))) {
         ok = false;
         break;
       }
       fence_after();
-      // The previous product finished before S_i (same MMA thread, issued earlier).
-      if (i > 0) {
-        if (!fold(i - 1)) {
-          ok = false;
-          break;
-        }
-        fence_before();
-        mbar_arrive(out_empty);
-      }
-      const int m0 = (blk0 + i) * kBKV + 32 * wg;  // minor index of column 0 of this half
-      uint32_t sv[32], dv[32];
+      uint32_t sv[32];
       tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
-      if (kTwoA) tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
-      const float* vec = reinterpret_cast<const float*>(smem + s * L::kStage + L::kVecOff) + 32 * wg;
+      fence_before();
+      mbar_arrive(s_free);
+      const float* vec =
+          reinterpret_cast<const float*>(smem + L::kRing2 + s * L::kSlot2 + 2 * L::kTile) + 32 * wg;
       // Blocks clear of the diagonal (and of the sequence end) need no mask;
       // the test is uniform over the CTA.
+      const int m0 = (blk0 + i) * kBKV + 32 * wg;  // minor index of column 0 of this half
       const int mb0 = (blk0 + i) * kBKV;
       const bool full = kKeyMajor ? (mb0 >= r0 + kBQ - 1 && mb0 + kBKV <= p.T)
                                   : (mb0 + kBKV - 1 <= r0);
+      float e[32];
       if (full) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const float l2 = kKeyMajor ? vec[c] : lse2_row;
-          const float pv = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2));
-          float e = pv;
-          if (kTwoA) {
-            const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
-            e = pv * (__uint_as_float(dv[c]) - dl);
-          }
-          sv[c] = __float_as_uint(tf32_hi(e));
-          dv[c] = __float_as_uint(tf32_lo(e));
+          e[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2));
         }
       } else {
 #pragma unroll
@@ -847,17 +905,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int m = m0 + c;
           const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
           const float l2 = kKeyMajor ? vec[c] : lse2_row;
-          const float pv = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
-          float e = pv;
-          if (kTwoA) {
-            const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
-            e = pv * (__uint_as_float(dv[c]) - dl);
-          }
-          sv[c] = __float_as_uint(tf32_hi(e));
-          dv[c] = __float_as_uint(tf32_lo(e));
+          e[c] = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
         }
       }
-      tmem_st32(tmem + lane_off + (MODE == kDV ? kBS : kBdP) + 32 * wg, sv);
+      // dP_i done implies product_{i-1} done (issued before it).
+      if (kTwoA && !mbar_wait(dp_full, (uint32_t)i & 1u, abort, &g_timeout)) {
+        ok = false;
+        break;
+      }
+      if (i > 0 && !fold(i - 1)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      uint32_t dv[32];
+      if (kTwoA) {
+        tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
+          e[c] = e[c] * (__uint_as_float(dv[c]) - dl);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        sv[c] = __float_as_uint(tf32_hi(e[c]));
+        dv[c] = __float_as_uint(tf32_lo(e[c]));
+      }
+      tmem_st32(tmem + lane_off + kBdP + 32 * wg, sv);
       tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);
       tmem_wait_st();
       fence_before();
