@@ -723,84 +723,109 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts(d, a + D + kk * 8, k_desc(t, kk), id_s, 1u);
         }
       };
-      auto issue_s = [&](int j) -> bool {
+      // MMAs and commits of one operation (the elected lane); the waits for
+      // its operands come before.
+      auto emit_s = [&](int j) {
         const int s = j % R;
-        if (!warp_wait(full0 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
-        fence_after();
-        if (elect_one()) {
-          issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s * L::kSlot);
-          commit(empty0 + 8u * s);
-          commit(s_full);
-        }
-        __syncwarp();
-        return true;
+        issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s * L::kSlot);
+        commit(empty0 + 8u * s);
+        commit(s_full);
       };
-      auto issue_dp = [&](int j) -> bool {
+      auto emit_dp = [&](int j) {
         const int s = j % R;
-        if (!warp_wait(full1 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
-        fence_after();
-        if (elect_one()) {
-          issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s * L::kSlot);
-          commit(empty1 + 8u * s);
-          commit(dp_full);
-        }
-        __syncwarp();
-        return true;
+        issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s * L::kSlot);
+        commit(empty1 + 8u * s);
+        commit(dp_full);
       };
       // Product of block j: A = E (hi over dP, lo apart), B = the MN-major tile.
-      auto issue_out = [&](int j) -> bool {
+      auto emit_out = [&](int j) {
         const int s = j % R;
-        if (!warp_wait(full2 + 8u * s, (uint32_t)(j / R) & 1u, abort, &g_timeout)) return false;
+        const uint32_t tb = sbase + L::kRing2 + s * L::kSlot2, tblo = tb + L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 8; ++kk)
+          mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 8; ++kk) {
+          mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tblo, kk), id_o, 1u);
+          mma_ts(tmem + kBO, tmem + kBElo + kk * 8, v_desc(tb, kk), id_o, 1u);
+        }
+        commit(empty2 + 8u * s);
+        commit(out_full);
+      };
+      // Tile barrier of ring r (0: S operand, 1: dP operand, 2: product operand) for block j.
+      auto tile_full = [&](int r, int j) {
+        return (r == 0 ? full0 : r == 1 ? full1 : full2) + 8u * (uint32_t)(j % R);
+      };
+      auto tile_ph = [&](int j) { return (uint32_t)(j / R) & 1u; };
+      auto issue = [&](int r, int j) -> bool {
+        if (!warp_wait(tile_full(r, j), tile_ph(j), abort, &g_timeout)) return false;
         fence_after();
         if (elect_one()) {
-          const uint32_t tb = sbase + L::kRing2 + s * L::kSlot2, tblo = tb + L::kTile;
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk)
-            mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk) {
-            mma_ts(tmem + kBO, tmem + kBdP + kk * 8, v_desc(tblo, kk), id_o, 1u);
-            mma_ts(tmem + kBO, tmem + kBElo + kk * 8, v_desc(tb, kk), id_o, 1u);
-          }
-          commit(empty2 + 8u * s);
-          commit(out_full);
+          if (r == 0)
+            emit_s(j);
+          else if (r == 1)
+            emit_dp(j);
+          else
+            emit_out(j);
         }
         __syncwarp();
         return true;
       };
       bool ok = warp_wait(a_ready, 0, abort, &g_timeout);
       fence_after();
-      if (ok) ok = issue_s(0);
-      if (ok && kTwoA) ok = issue_dp(0);
+      if (ok) ok = issue(0, 0);
+      if (ok && kTwoA) ok = issue(1, 0);
       if (ok && n_blk > 1) {
         ok = warp_wait(s_free, 0, abort, &g_timeout);
         fence_after();
-        if (ok) ok = issue_s(1);
+        if (ok) ok = issue(0, 1);
       }
       // dP_{i+1} overwrites the columns product_i reads and S_{i+2} those S_{i+1}
       // was read from: each is issued after the MMAs or the reads it must
-      // follow (one CTA's MMAs run in issue order).
+      // follow (one CTA's MMAs run in issue order).  The tensor core queues
+      // almost no MMAs, so every wait or re-convergence between them idles it:
+      // the tile barriers (nearly always complete) are probed while waiting
+      // for the element-wise warps, and the MMAs that follow one such wait go
+      // out in one elected run.
       for (int i = 0; ok && i < n_blk; ++i) {
-        if (!warp_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout)) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        if (!issue_out(i)) {
-          ok = false;
-          break;
-        }
-        if (kTwoA && i + 1 < n_blk && !issue_dp(i + 1)) {
-          ok = false;
-          break;
-        }
-        if (i + 2 < n_blk) {
-          if (!warp_wait(s_free, (uint32_t)(i + 1) & 1u, abort, &g_timeout)) {
+        const bool dp_next = kTwoA && i + 1 < n_blk;
+        {
+          const bool r2 = mbar_try(tile_full(2, i), tile_ph(i));
+          const bool r1 = dp_next ? mbar_try(tile_full(1, i + 1), tile_ph(i + 1)) : true;
+          const bool e = mbar_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout);
+          const uint32_t bits =
+              __shfl_sync(0xffffffffu, (e ? 1u : 0u) | (r2 ? 2u : 0u) | (r1 ? 4u : 0u), 0);
+          if (!(bits & 1u)) {
             ok = false;
             break;
           }
           fence_after();
-          ok = issue_s(i + 2);
+          if ((bits & 6u) == 6u) {
+            if (elect_one()) {
+              emit_out(i);
+              if (dp_next) emit_dp(i + 1);
+            }
+            __syncwarp();
+          } else if (!issue(2, i) || (dp_next && !issue(1, i + 1))) {
+            ok = false;
+            break;
+          }
+        }
+        if (i + 2 < n_blk) {
+          const bool r0 = mbar_try(tile_full(0, i + 2), tile_ph(i + 2));
+          const bool f = mbar_wait(s_free, (uint32_t)(i + 1) & 1u, abort, &g_timeout);
+          const uint32_t bits = __shfl_sync(0xffffffffu, (f ? 1u : 0u) | (r0 ? 2u : 0u), 0);
+          if (!(bits & 1u)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          if (bits & 2u) {
+            if (elect_one()) emit_s(i + 2);
+            __syncwarp();
+          } else {
+            ok = issue(0, i + 2);
+          }
         }
       }
       if (!ok) {
