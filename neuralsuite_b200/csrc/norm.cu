@@ -247,14 +247,35 @@ __global__ void __launch_bounds__(256) ln_bwd_any(
 // Column sums of part[n_part][N]: CTA = 32 columns, warp w sums partials
 // w, w+8, w+16, ... in order, then the eight warp sums are added in warp order
 // (a fixed order: deterministic).
+// blockIdx.y == 1 sums part2 into out2 (two column sums of one shape in one
+// launch: LayerNorm's dgamma and dbeta).  Four partials are loaded before
+// they are added, in the same order.
 __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ part, int n_part,
-                                                     int N, float* __restrict__ out) {
+                                                     int N, float* __restrict__ out,
+                                                     const float* __restrict__ part2,
+                                                     float* __restrict__ out2) {
   __shared__ float red[kRowsWarps][32];
+  if (blockIdx.y == 1) {
+    part = part2;
+    out = out2;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * 32 + lane;
   float s = 0.f;
-  if (n < N)
-    for (int p = warp; p < n_part; p += kRowsWarps) s += part[(size_t)p * N + n];
+  if (n < N) {
+    int p = warp;
+    for (; p + 3 * kRowsWarps < n_part; p += 4 * kRowsWarps) {
+      const float a = part[(size_t)p * N + n];
+      const float b = part[(size_t)(p + kRowsWarps) * N + n];
+      const float c = part[(size_t)(p + 2 * kRowsWarps) * N + n];
+      const float d = part[(size_t)(p + 3 * kRowsWarps) * N + n];
+      s += a;
+      s += b;
+      s += c;
+      s += d;
+    }
+    for (; p < n_part; p += kRowsWarps) s += part[(size_t)p * N + n];
+  }
   red[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && n < N) {
@@ -280,20 +301,36 @@ __global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ 
   const int r1 = min(M, r0 + rows_per_cta);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   const bool vec = (N & 3) == 0;
+  auto take = [&](int r, const float4 v) {
+    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    if (LO) {
+      float4 l;
+      l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+      l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+      l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+      l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+      *reinterpret_cast<float4*>(lo + (size_t)r * N + col) = l;
+    }
+  };
   if (col < N) {
-    for (int r = r0 + warp; r < r1; r += kRowsWarps) {
+    int r = r0 + warp;
+    if (vec) {
+      // Four rows' loads in flight before they are added (in row order).
+      for (; r + 3 * kRowsWarps < r1; r += 4 * kRowsWarps) {
+        const float4 v0 = *reinterpret_cast<const float4*>(y + (size_t)r * N + col);
+        const float4 v1 = *reinterpret_cast<const float4*>(y + (size_t)(r + kRowsWarps) * N + col);
+        const float4 v2 = *reinterpret_cast<const float4*>(y + (size_t)(r + 2 * kRowsWarps) * N + col);
+        const float4 v3 = *reinterpret_cast<const float4*>(y + (size_t)(r + 3 * kRowsWarps) * N + col);
+        take(r, v0);
+        take(r + kRowsWarps, v1);
+        take(r + 2 * kRowsWarps, v2);
+        take(r + 3 * kRowsWarps, v3);
+      }
+    }
+    for (; r < r1; r += kRowsWarps) {
       const float* p = y + (size_t)r * N + col;
       if (vec) {
-        const float4 v = *reinterpret_cast<const float4*>(p);
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-        if (LO) {
-          float4 l;
-          l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-          *reinterpret_cast<float4*>(lo + (size_t)r * N + col) = l;
-        }
+        take(r, *reinterpret_cast<const float4*>(p));
       } else {
         s.x += p[0];
         if (col + 1 < N) s.y += p[1];
@@ -418,8 +455,7 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
                                       rows, dim, rpc);
   }
   { ns_status _rc = check_launch("ns_layernorm_bwd stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(dim, 32), 256, 0, s>>>(part_g, ctas, dim, dgamma);
-  colsum_finish<<<ceil_div(dim, 32), 256, 0, s>>>(part_b, ctas, dim, dbeta);
+  colsum_finish<<<dim3(ceil_div(dim, 32), 2), 256, 0, s>>>(part_g, ctas, dim, dgamma, part_b, dbeta);
   return check_launch("ns_layernorm_bwd stage 2");
 }
 
@@ -445,7 +481,7 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   float* part = static_cast<float*>(workspace);
   colsum_partial<false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, nullptr);
   { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db);
+  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
   return check_launch("ns_bias_grad stage 2");
 }
 
@@ -462,7 +498,7 @@ ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy
   float* part = static_cast<float*>(workspace);
   colsum_partial<true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo);
   { ns_status _rc = check_launch("ns_bias_grad_split stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db);
+  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
   return check_launch("ns_bias_grad_split stage 2");
 }
 
