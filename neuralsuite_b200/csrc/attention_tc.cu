@@ -53,9 +53,11 @@ struct FwdLayout {
   static constexpr int kStages = D == 64 ? 3 : 4;
   static constexpr uint32_t kTile = kBKV * D * 4;  // 64 keys x D fp32 (D/32 boxes of 8 KB)
   static constexpr uint32_t kStage = 4 * kTile;    // K raw | K lo | V raw | V lo
-  static constexpr uint32_t kXchg = kStages * kStage;  // [3][128] floats: m, m*c, l of warpgroup 1
+  // The next work item's Q rows (128 x D, D/32 boxes of 16 KB, 128B swizzle).
+  static constexpr uint32_t kQ = kStages * kStage;
+  static constexpr uint32_t kXchg = kQ + kBQ * D * 4;  // [3][128] floats: m, m*c, l of warpgroup 1
   static constexpr uint32_t kBars = kXchg + 3 * kBQ * 4;
-  static constexpr uint32_t kNumBars = 2 * kStages + 10;
+  static constexpr uint32_t kNumBars = 2 * kStages + 14;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static_assert(kDynSmem <= 232448, "shared memory budget");
@@ -69,6 +71,8 @@ struct FwdParams {
   int T, H, C;
   float scale;       // 1/sqrt(D)
   float scale_log2;  // scale * log2(e)
+  int n_items;       // (128-query block, batch x head) pairs
+  int nqb;           // query blocks per sequence
 };
 
 // K tile (keys x D, K-major): 8-row groups 1024 B apart, 16-byte chunks;
@@ -99,9 +103,25 @@ __device__ __forceinline__ void wg_pair_sync() {
   asm volatile("bar.sync 1, 256;" ::: "memory");  // warps 4..11
 }
 
+// Work item k of CTA c in a grid of G: the items (query block, batch x head)
+// are ordered longest first (the last query block has the most keys) and
+// dealt in a snake (c, then G-1-c, ...), which balances the CTAs' total
+// lengths.  -1 when the CTA has no item k.
+__device__ __forceinline__ int fwd_item(int c, int k, int G, int n_items) {
+  const int w = k * G + ((k & 1) ? (G - 1 - c) : c);
+  return w < n_items ? w : -1;
+}
+
+// Persistent: one CTA per SM loops over work items.  Per item the element-wise
+// warps copy the item's Q rows (brought into shared memory by TMA while the
+// previous item ran) into TMEM as soon as the previous item's last S MMA is
+// done, and only then finish the previous item (last O fold, merge of the two
+// warpgroups, output), so the tensor core starts the next item's S blocks
+// while the previous item's epilogue runs.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                       const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmKlo,
                        const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmVlo, const FwdParams p) {
@@ -114,21 +134,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar0 = sbase + L::kBars;
   auto kv_full = [&](int s) { return bar0 + 8u * s; };
   auto kv_empty = [&](int s) { return bar0 + 8u * (S + s); };
-  const uint32_t q_ready = bar0 + 8u * (2 * S);
-  auto s_full = [&](int w) { return bar0 + 8u * (2 * S + 1 + w); };
-  auto p_full = [&](int w) { return bar0 + 8u * (2 * S + 3 + w); };
-  auto o_full = [&](int w) { return bar0 + 8u * (2 * S + 5 + w); };
-  auto o_empty = [&](int w) { return bar0 + 8u * (2 * S + 7 + w); };
-  const uint32_t drain = bar0 + 8u * (2 * S + 9);
+  const uint32_t q_full = bar0 + 8u * (2 * S), q_empty = q_full + 8u;
+  const uint32_t q_ready = q_full + 16u, q_free = q_full + 24u;
+  auto s_full = [&](int w) { return bar0 + 8u * (2 * S + 4 + w); };
+  auto p_full = [&](int w) { return bar0 + 8u * (2 * S + 6 + w); };
+  auto o_full = [&](int w) { return bar0 + 8u * (2 * S + 8 + w); };
+  auto o_empty = [&](int w) { return bar0 + 8u * (2 * S + 10 + w); };
+  const uint32_t drain = bar0 + 8u * (2 * S + 12);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xchg = reinterpret_cast<float*>(smem + L::kXchg);
 
-  const int nqb = (p.T + kBQ - 1) / kBQ;
-  const int qb = nqb - 1 - (int)blockIdx.x;  // longest rows first
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int q0 = qb * kBQ;
-  const int n_kb = (min(q0 + kBQ, p.T) + kBKV - 1) / kBKV;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+  const int BH = p.n_items / p.nqb;
+  // Item w: query block nqb-1-w/BH (longest first), batch x head w%BH.
+  auto item_q0 = [&](int w) { return (p.nqb - 1 - w / BH) * kBQ; };
+  auto item_bh = [&](int w) { return w % BH; };
+  auto item_nkb = [&](int w) { return (min(item_q0(w) + kBQ, p.T) + kBKV - 1) / kBKV; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -136,7 +158,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 2 * kWgThreads);
     mbar_init(q_ready, 2 * kWgThreads);
+    mbar_init(q_free, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
       mbar_init(p_full(i), kWgThreads);
@@ -163,48 +188,80 @@ __global__ void __launch_bounds__(kThreads, 1)
     // setmaxnreg runs at one instruction for a whole warpgroup.
     reg_dec();
     if (warp == 0) {
-      // ------------------------------------------------------------ producer
+      // ------------------------------------------------------------ K / V producer
       if (lane == 0) {
         int issued[S];
         uint32_t issued_ph[S];
         for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
         bool ok = true;
-        const int row0 = b * p.T;
-        for (int j = 0; j < n_kb; ++j) {
-          const int s = j % S;
-          const uint32_t ph = (uint32_t)(j / S) & 1u;
-          if (!mbar_wait(kv_empty(s), ph ^ 1u, abort, &g_timeout)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(kv_full(s), L::kStage);
-          issued[s] = 1;
-          issued_ph[s] = ph;
-          const uint32_t dst = sbase + s * L::kStage;
-          const int row = row0 + j * kBKV;
-  #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            const int x = h * D + 32 * c;
-            tma_load_2d(dst + c * 8192, &tmK, kv_full(s), p.C + x, row);
-            tma_load_2d(dst + L::kTile + c * 8192, &tmKlo, kv_full(s), x, row);
-            tma_load_2d(dst + 2 * L::kTile + c * 8192, &tmV, kv_full(s), 2 * p.C + x, row);
-            tma_load_2d(dst + 3 * L::kTile + c * 8192, &tmVlo, kv_full(s), p.C + x, row);
+        uint32_t g = 0;  // key blocks loaded so far (all items)
+        for (int k = 0; ok; ++k) {
+          const int w = fwd_item(cta, k, G, p.n_items);
+          if (w < 0) break;
+          const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
+          const int n_kb = item_nkb(w);
+          for (int j = 0; j < n_kb; ++j, ++g) {
+            const int s = g % S;
+            const uint32_t ph = (g / S) & 1u;
+            if (!mbar_wait(kv_empty(s), ph ^ 1u, abort, &g_timeout)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(kv_full(s), L::kStage);
+            issued[s] = 1;
+            issued_ph[s] = ph;
+            const uint32_t dst = sbase + s * L::kStage;
+            const int row = b * p.T + j * kBKV;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              const int x = h * D + 32 * c;
+              tma_load_2d(dst + c * 8192, &tmK, kv_full(s), p.C + x, row);
+              tma_load_2d(dst + L::kTile + c * 8192, &tmKlo, kv_full(s), x, row);
+              tma_load_2d(dst + 2 * L::kTile + c * 8192, &tmV, kv_full(s), 2 * p.C + x, row);
+              tma_load_2d(dst + 3 * L::kTile + c * 8192, &tmVlo, kv_full(s), p.C + x, row);
+            }
           }
         }
         if (!ok)
           for (int s = 0; s < S; ++s)
             if (issued[s]) mbar_wait_drain(kv_full(s), issued_ph[s], &g_timeout);
       }
+    } else if (warp == 2) {
+      // ------------------------------------------------------------ Q producer
+      if (lane == 0) {
+        bool ok = true, pending = false;
+        uint32_t pend_ph = 0;
+        for (int k = 0;; ++k) {
+          const int w = fwd_item(cta, k, G, p.n_items);
+          if (w < 0) break;
+          // The element-wise warps have copied the previous item's Q out.
+          if (!mbar_wait(q_empty, ((uint32_t)k & 1u) ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
+          }
+          const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
+          mbar_expect_tx(q_full, (uint32_t)(kBQ * D * 4));
+          pending = true;
+          pend_ph = (uint32_t)k & 1u;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c)
+            tma_load_2d(sbase + L::kQ + c * 16384, &tmQ, q_full, h * D + 32 * c, b * p.T + item_q0(w));
+        }
+        if (!ok && pending) mbar_wait_drain(q_full, pend_ph, &g_timeout);
+      }
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer
       // The whole warp runs this loop converged; the elected lane issues.
       constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
       constexpr uint32_t id_o = instr_desc(D, 0, 1);
-      bool ok = warp_wait(q_ready, 0, abort, &g_timeout);
-      fence_after();
+      uint32_t g = 0;               // key blocks of earlier items (ring position)
+      uint32_t tw[2] = {0u, 0u};    // blocks of each warpgroup so far (all items)
+      bool ok = true;
+      // S_j of the current item: its K tile is ring entry g + j.
       auto issue_s = [&](int j) -> bool {
-        const int s = j % S;
-        if (!warp_wait(kv_full(s), (uint32_t)(j / S) & 1u, abort, &g_timeout)) return false;
+        const uint32_t gj = g + (uint32_t)j;
+        const int s = gj % S;
+        if (!warp_wait(kv_full(s), (gj / S) & 1u, abort, &g_timeout)) return false;
         fence_after();
         if (elect_one()) {
           const uint32_t d = tmem + kTS + (j & 1) * kBKV;
@@ -222,37 +279,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         return true;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && n_kb > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < n_kb; ++j) {
-        const int w = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!warp_wait(p_full(w), ph, abort, &g_timeout) ||
-            !warp_wait(o_empty(w), ph ^ 1u, abort, &g_timeout)) {
+      // After the item's last S: Q's TMEM columns may take the next item's rows.
+      auto release_q = [&]() {
+        if (elect_one()) commit(q_free);
+        __syncwarp();
+      };
+      for (int k = 0; ok; ++k) {
+        const int w = fwd_item(cta, k, G, p.n_items);
+        if (w < 0) break;
+        const int n_kb = item_nkb(w);
+        if (!warp_wait(q_ready, (uint32_t)k & 1u, abort, &g_timeout)) {
           ok = false;
           break;
         }
         fence_after();
-        const int s = j % S;
-        if (elect_one()) {
-          const uint32_t v_raw = sbase + s * L::kStage + 2 * L::kTile, v_lo = v_raw + L::kTile;
-          const uint32_t o = tmem + kTO + w * D;
-          const uint32_t phi = tmem + kTS + w * kBKV, plo = tmem + kTPlo + w * kBKV;
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk)
-            mma_ts(o, phi + kk * 8, v_desc(v_raw, kk), id_o, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 8; ++kk) {
-            mma_ts(o, phi + kk * 8, v_desc(v_lo, kk), id_o, 1u);
-            mma_ts(o, plo + kk * 8, v_desc(v_raw, kk), id_o, 1u);
+        ok = issue_s(0);
+        if (ok && n_kb > 1) ok = issue_s(1);
+        if (ok && n_kb <= 2) release_q();
+        for (int j = 0; ok && j < n_kb; ++j) {
+          const int wg = j & 1;
+          const uint32_t t = tw[wg]++;
+          if (!warp_wait(p_full(wg), t & 1u, abort, &g_timeout) ||
+              !warp_wait(o_empty(wg), (t & 1u) ^ 1u, abort, &g_timeout)) {
+            ok = false;
+            break;
           }
-          commit(o_full(w));
-          commit(kv_empty(s));
+          fence_after();
+          const uint32_t gj = g + (uint32_t)j;
+          const int s = gj % S;
+          if (elect_one()) {
+            const uint32_t v_raw = sbase + s * L::kStage + 2 * L::kTile, v_lo = v_raw + L::kTile;
+            const uint32_t o = tmem + kTO + wg * D;
+            const uint32_t phi = tmem + kTS + wg * kBKV, plo = tmem + kTPlo + wg * kBKV;
+#pragma unroll
+            for (int kk = 0; kk < kBKV / 8; ++kk)
+              mma_ts(o, phi + kk * 8, v_desc(v_raw, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < kBKV / 8; ++kk) {
+              mma_ts(o, phi + kk * 8, v_desc(v_lo, kk), id_o, 1u);
+              mma_ts(o, plo + kk * 8, v_desc(v_raw, kk), id_o, 1u);
+            }
+            commit(o_full(wg));
+            commit(kv_empty(s));
+          }
+          __syncwarp();
+          // S_{j+2} reuses this warpgroup's S/P columns: issued after O_j, and
+          // the tensor core runs one CTA's MMAs in issue order.
+          if (j + 2 < n_kb) {
+            ok = issue_s(j + 2);
+            if (ok && j + 2 == n_kb - 1) release_q();
+          }
         }
-        __syncwarp();
-        // S_{j+2} reuses this warpgroup's S/P columns: issued after O_j, and
-        // the tensor core runs one CTA's MMAs in issue order.
-        if (j + 2 < n_kb) ok = issue_s(j + 2);
+        g += (uint32_t)n_kb;
       }
       if (!ok) {
         // Wait for every MMA already issued before TMEM is freed.
@@ -264,45 +342,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
-    const int wg = (warp - 4) >> 2;  // key blocks wg, wg+2, wg+4, ...
+    const int wg = (warp - 4) >> 2;  // key blocks wg, wg+2, wg+4, ... of each item
     const int ew = warp & 3;         // TMEM lanes 32*ew .. 32*ew+31
     const int row = ew * 32 + lane;
-    const int q = q0 + row;
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
     const float c = p.scale_log2;
-    {
-      // Q row -> Qhi / Qlo columns; warpgroup wg writes 32-column chunks wg, wg+2.
-      const float* qrow =
-          p.qkv + ((size_t)b * p.T + (q < p.T ? q : 0)) * (size_t)(3 * p.C) + (size_t)h * D;
-      for (int cc = wg; cc < D / 32; cc += 2) {
-        uint32_t hi[32], lo[32];
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 x = q < p.T ? *reinterpret_cast<const float4*>(qrow + 32 * cc + i)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
-            lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
-          }
-        }
-        tmem_st32(tmem + lane_off + 32 * cc, hi);
-        tmem_st32(tmem + lane_off + D + 32 * cc, lo);
-      }
-      tmem_wait_st();
-      fence_before();
-      mbar_arrive(q_ready);
-    }
     const uint32_t s_t = tmem + lane_off + kTS + wg * kBKV;
     const uint32_t pl_t = tmem + lane_off + kTPlo + wg * kBKV;
     const uint32_t o_t = tmem + lane_off + kTO + wg * D;
     float acc[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) acc[d] = 0.0f;
     float m = -INFINITY, mc = 0.0f, l = 0.0f, alpha_prev = 0.0f;
+    uint32_t T = 0;  // this warpgroup's blocks so far (all items)
+    int t = 0;       // ... of the current item
+    int prev_w = -1;
     bool ok = true;
-    int t = 0;
     auto fold = [&](uint32_t ph, float alpha) -> bool {
       if (!mbar_wait(o_full(wg), ph, abort, &g_timeout)) return false;
       fence_after();
@@ -316,121 +369,195 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
-    for (int j = wg; j < n_kb; j += 2, ++t) {
-      if (!mbar_wait(s_full(wg), (uint32_t)t & 1u, abort, &g_timeout)) {
-        ok = false;
-        break;
-      }
-      fence_after();
-      // S_j completing implies this warpgroup's previous O is complete too
-      // (same MMA thread, issued earlier): fold it and free the O columns.
+    // Last fold, merge of the two warpgroups and the output of item w (whose
+    // blocks this warpgroup has all turned into P).
+    auto finish = [&](int w) -> bool {
       if (t > 0) {
-        if (!fold((uint32_t)(t - 1) & 1u, alpha_prev)) {
+        if (!fold((T - 1) & 1u, alpha_prev)) return false;
+        if (wg == 0) {
+          fence_before();
+          mbar_arrive(o_empty(0));
+        }
+      }
+      // Warpgroup 1 hands its accumulator over through its own O columns (no
+      // MMA writes them until it releases them below) and m, m*c, l through
+      // shared memory.
+      if (wg == 1) {
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[32 * cc + i]);
+          tmem_st32(o_t + 32 * cc, v);
+        }
+        xchg[row] = m;
+        xchg[kBQ + row] = mc;
+        xchg[2 * kBQ + row] = l;
+        tmem_wait_st();
+        fence_before();
+      }
+      wg_pair_sync();
+      if (wg == 0) {
+        fence_after();
+        const float m1 = xchg[row], mc1 = xchg[kBQ + row], l1 = xchg[2 * kBQ + row];
+        const float m_tot = fmaxf(m, m1);  // finite: key 0 is never masked
+        const float mc_tot = m_tot * c;
+        const float a0 = fast_exp2(mc - mc_tot);
+        const float a1 = m1 == -INFINITY ? 0.0f : fast_exp2(mc1 - mc_tot);
+        const float l_tot = l * a0 + l1 * a1;
+        const float inv = 1.0f / l_tot;
+        const uint32_t o1 = tmem + lane_off + kTO + D;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(o1 + 32 * cc, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            acc[32 * cc + i] = fmaf(acc[32 * cc + i], a0, __uint_as_float(v[i]) * a1) * inv;
+        }
+        fence_before();
+        const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
+        const int q = item_q0(w) + row;
+        if (q < p.T) {
+          float* dst = p.out + ((size_t)b * p.T + q) * p.C + (size_t)h * D;
+#pragma unroll
+          for (int d = 0; d < D; d += 4)
+            *reinterpret_cast<float4*>(dst + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
+          p.lse[(size_t)bh * p.T + q] = m_tot * p.scale + logf(l_tot);
+        }
+      }
+      wg_pair_sync();  // warpgroup 0 has read O1 and the exchange
+      if (wg == 1 && t > 0) {
+        fence_before();
+        mbar_arrive(o_empty(1));
+      }
+      return true;
+    };
+    for (int k = 0; ok; ++k) {
+      const int w = fwd_item(cta, k, G, p.n_items);
+      if (w < 0) break;
+      const int bh = item_bh(w), b = bh / p.H;
+      const int q0 = item_q0(w), q = q0 + row;
+      const int n_kb = item_nkb(w);
+      {
+        // This item's Q rows: shared memory (128B swizzle: 16-byte chunk i of
+        // row r sits at chunk i ^ (r & 7)) -> Qhi / Qlo columns, once the
+        // previous item's last S MMA has read the old ones.
+        if (!mbar_wait(q_full, (uint32_t)k & 1u, abort, &g_timeout) ||
+            (k > 0 && !mbar_wait(q_free, (uint32_t)(k - 1) & 1u, abort, &g_timeout))) {
           ok = false;
           break;
         }
+        fence_after();
+        for (int cc = wg; cc < D / 32; cc += 2) {
+          const uint8_t* qs = smem + L::kQ + cc * 16384 + row * 128;
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 x = q < p.T ? *reinterpret_cast<const float4*>(qs + ((i ^ (row & 7)) << 4))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[4 * i + e] = __float_as_uint(tf32_hi(xs[e]));
+              lo[4 * i + e] = __float_as_uint(tf32_lo(xs[e]));
+            }
+          }
+          tmem_st32(tmem + lane_off + 32 * cc, hi);
+          tmem_st32(tmem + lane_off + D + 32 * cc, lo);
+        }
+        mbar_arrive(q_empty);
+        tmem_wait_st();
         fence_before();
-        mbar_arrive(o_empty(wg));
+        mbar_arrive(q_ready);
       }
-      const int k0 = j * kBKV;
-      uint32_t s0[32], s1[32];
-      tmem_ld32(s_t, s0);
-      tmem_ld32(s_t + 32, s1);
-      float x[64];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        x[i] = __uint_as_float(s0[i]);
-        x[32 + i] = __uint_as_float(s1[i]);
+      if (prev_w >= 0 && !finish(prev_w)) {
+        ok = false;
+        break;
       }
-      if (k0 + kBKV - 1 > q) {
+      (void)b;
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (k0 + i > q) x[i] = -INFINITY;
+      for (int d = 0; d < D; ++d) acc[d] = 0.0f;
+      m = -INFINITY;
+      mc = 0.0f;
+      l = 0.0f;
+      alpha_prev = 0.0f;
+      t = 0;
+      for (int j = wg; j < n_kb; j += 2, ++t, ++T) {
+        if (!mbar_wait(s_full(wg), T & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        // S_j completing implies this warpgroup's previous O is complete too
+        // (same MMA thread, issued earlier): fold it and free the O columns.
+        if (t > 0) {
+          if (!fold((T - 1) & 1u, alpha_prev)) {
+            ok = false;
+            break;
+          }
+          fence_before();
+          mbar_arrive(o_empty(wg));
+        }
+        const int k0 = j * kBKV;
+        uint32_t s0[32], s1[32];
+        tmem_ld32(s_t, s0);
+        tmem_ld32(s_t + 32, s1);
+        float x[64];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(s0[i]);
+          x[32 + i] = __uint_as_float(s1[i]);
+        }
+        if (k0 + kBKV - 1 > q) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (k0 + i > q) x[i] = -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = x[i];
+#pragma unroll
+        for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+        const float m_new = fmaxf(m, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
+        // m_new = -inf: every key so far is masked (P = 0 below).
+        const float mc_new = m_new == -INFINITY ? 0.0f : m_new * c;
+        const float alpha = m == -INFINITY ? 0.0f : fast_exp2(mc - mc_new);
+        float rs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rs[i] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          x[i] = fast_exp2(fmaf(x[i], c, -mc_new));
+          rs[i & 7] += x[i];
+        }
+        l = l * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
+        m = m_new;
+        mc = mc_new;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s0[i] = __float_as_uint(tf32_hi(x[i]));
+          s1[i] = __float_as_uint(tf32_hi(x[32 + i]));
+        }
+        tmem_st32(s_t, s0);
+        tmem_st32(s_t + 32, s1);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s0[i] = __float_as_uint(tf32_lo(x[i]));
+          s1[i] = __float_as_uint(tf32_lo(x[32 + i]));
+        }
+        tmem_st32(pl_t, s0);
+        tmem_st32(pl_t + 32, s1);
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(p_full(wg));
+        alpha_prev = alpha;
       }
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = x[i];
-#pragma unroll
-      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
-      const float m_new = fmaxf(m, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
-      // m_new = -inf: every key so far is masked (P = 0 below).
-      const float mc_new = m_new == -INFINITY ? 0.0f : m_new * c;
-      const float alpha = m == -INFINITY ? 0.0f : fast_exp2(mc - mc_new);
-      float rs[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) rs[i] = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        x[i] = fast_exp2(fmaf(x[i], c, -mc_new));
-        rs[i & 7] += x[i];
-      }
-      l = l * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
-      m = m_new;
-      mc = mc_new;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s0[i] = __float_as_uint(tf32_hi(x[i]));
-        s1[i] = __float_as_uint(tf32_hi(x[32 + i]));
-      }
-      tmem_st32(s_t, s0);
-      tmem_st32(s_t + 32, s1);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s0[i] = __float_as_uint(tf32_lo(x[i]));
-        s1[i] = __float_as_uint(tf32_lo(x[32 + i]));
-      }
-      tmem_st32(pl_t, s0);
-      tmem_st32(pl_t + 32, s1);
-      tmem_wait_st();
-      fence_before();
-      mbar_arrive(p_full(wg));
-      alpha_prev = alpha;
+      if (!ok) break;
+      prev_w = w;
     }
-    if (ok && t > 0) ok = fold((uint32_t)(t - 1) & 1u, alpha_prev);
-    // Merge: warpgroup 1 hands its accumulator over through its own O columns
-    // (no MMA writes them any more) and m, m*c, l through shared memory.
-    if (wg == 1) {
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[32 * cc + i]);
-        tmem_st32(o_t + 32 * cc, v);
-      }
-      xchg[row] = m;
-      xchg[kBQ + row] = mc;
-      xchg[2 * kBQ + row] = l;
-      tmem_wait_st();
-      fence_before();
-    }
-    wg_pair_sync();
-    if (wg == 0) {
-      fence_after();
-      const float m1 = xchg[row], mc1 = xchg[kBQ + row], l1 = xchg[2 * kBQ + row];
-      const float m_tot = fmaxf(m, m1);  // finite: key 0 is never masked
-      const float mc_tot = m_tot * c;
-      const float a0 = fast_exp2(mc - mc_tot);
-      const float a1 = m1 == -INFINITY ? 0.0f : fast_exp2(mc1 - mc_tot);
-      const float l_tot = l * a0 + l1 * a1;
-      const float inv = 1.0f / l_tot;
-      const uint32_t o1 = tmem + lane_off + kTO + D;
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(o1 + 32 * cc, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          acc[32 * cc + i] = fmaf(acc[32 * cc + i], a0, __uint_as_float(v[i]) * a1) * inv;
-      }
-      if (ok && q < p.T) {
-        float* dst = p.out + ((size_t)b * p.T + q) * p.C + (size_t)h * D;
-#pragma unroll
-        for (int d = 0; d < D; d += 4)
-          *reinterpret_cast<float4*>(dst + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
-        p.lse[(size_t)bh * p.T + q] = m_tot * p.scale + logf(l_tot);
-      }
-    }
+    if (ok && prev_w >= 0) ok = finish(prev_w);
   }
 
   fence_before();
@@ -470,14 +597,17 @@ ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* l
     ns_status rc = check_launch("ns_attn_fwd kv split");
     if (rc != NS_OK) return rc;
   }
-  CUtensorMap tk, tklo, tv, tvlo;
-  ns_status rc = make_map(&tk, qkv, 3 * C, rows, 3 * C, kBKV, false);
+  CUtensorMap tq, tk, tklo, tv, tvlo;
+  ns_status rc = make_map(&tq, qkv, 3 * C, rows, 3 * C, kBQ, false);
+  if (rc == NS_OK) rc = make_map(&tk, qkv, 3 * C, rows, 3 * C, kBKV, false);
   if (rc == NS_OK) rc = make_map(&tklo, lo, 2 * C, rows, 2 * C, kBKV, false);
   if (rc == NS_OK) rc = make_map(&tv, qkv, 3 * C, rows, 3 * C, kBKV, true);
   if (rc == NS_OK) rc = make_map(&tvlo, lo, 2 * C, rows, 2 * C, kBKV, true);
   if (rc != NS_OK) return rc;
   const float scale = 1.0f / sqrtf((float)D);
-  FwdParams p{qkv, out, lse, T, H, C, scale, scale * 1.4426950408889634f};
+  const int nqb = (T + kBQ - 1) / kBQ;
+  const int n_items = nqb * B * H;
+  FwdParams p{qkv, out, lse, T, H, C, scale, scale * 1.4426950408889634f, n_items, nqb};
   NS_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<D>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
               "ns_attn_fwd attr");
@@ -489,8 +619,8 @@ ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* l
     if (fa.numRegs < kMinLaunchRegs)
       return fail(NS_ERR_UNSUPPORTED, "ns_attn_fwd: kernel compiled with too few registers for its split");
   }
-  const dim3 grid((T + kBQ - 1) / kBQ, B * H);
-  attn_fwd_tc_kernel<D><<<grid, kThreads, L::kDynSmem, s>>>(tk, tklo, tv, tvlo, p);
+  const int grid = std::min(n_items, sm_count());
+  attn_fwd_tc_kernel<D><<<grid, kThreads, L::kDynSmem, s>>>(tq, tk, tklo, tv, tvlo, p);
   return check_launch("ns_attn_fwd tcgen05");
 }
 
