@@ -257,25 +257,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;               // key blocks of earlier items (ring position)
       uint32_t tw[2] = {0u, 0u};    // blocks of each warpgroup so far (all items)
       bool ok = true;
-      // S_j of the current item: its K tile is ring entry g + j.
-      auto issue_s = [&](int j) -> bool {
+      // S_j of the current item (the elected lane): its K tile is ring entry g + j.
+      auto emit_s = [&](int j) {
         const uint32_t gj = g + (uint32_t)j;
         const int s = gj % S;
-        if (!warp_wait(kv_full(s), (gj / S) & 1u, abort, &g_timeout)) return false;
-        fence_after();
-        if (elect_one()) {
-          const uint32_t d = tmem + kTS + (j & 1) * kBKV;
-          const uint32_t k_raw = sbase + s * L::kStage, k_lo = k_raw + L::kTile;
+        const uint32_t d = tmem + kTS + (j & 1) * kBKV;
+        const uint32_t k_raw = sbase + s * L::kStage, k_lo = k_raw + L::kTile;
 #pragma unroll
-          for (int kk = 0; kk < D / 8; ++kk)
-            mma_ts(d, tmem + kk * 8, k_desc(k_raw, kk), id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 8; ++kk)
+          mma_ts(d, tmem + kk * 8, k_desc(k_raw, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < D / 8; ++kk) {
-            mma_ts(d, tmem + kk * 8, k_desc(k_lo, kk), id_s, 1u);
-            mma_ts(d, tmem + D + kk * 8, k_desc(k_raw, kk), id_s, 1u);
-          }
-          commit(s_full(j & 1));
+        for (int kk = 0; kk < D / 8; ++kk) {
+          mma_ts(d, tmem + kk * 8, k_desc(k_lo, kk), id_s, 1u);
+          mma_ts(d, tmem + D + kk * 8, k_desc(k_raw, kk), id_s, 1u);
         }
+        commit(s_full(j & 1));
+      };
+      auto issue_s = [&](int j) -> bool {
+        const uint32_t gj = g + (uint32_t)j;
+        if (!warp_wait(kv_full(gj % S), (gj / S) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) emit_s(j);
         __syncwarp();
         return true;
       };
@@ -299,11 +301,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; ok && j < n_kb; ++j) {
           const int wg = j & 1;
           const uint32_t t = tw[wg]++;
-          if (!warp_wait(p_full(wg), t & 1u, abort, &g_timeout) ||
-              !warp_wait(o_empty(wg), (t & 1u) ^ 1u, abort, &g_timeout)) {
+          // The K tile of S_{j+2} is nearly always there: tested while waiting
+          // for P_j, so that O_j and S_{j+2} go out in one elected run (each
+          // wait or re-convergence between MMAs idles the tensor core).
+          const uint32_t g2 = g + (uint32_t)j + 2u;
+          const bool next_s = j + 2 < n_kb;
+          bool k_ready = next_s && mbar_test(kv_full(g2 % S), (g2 / S) & 1u);
+          const bool pe = mbar_wait(p_full(wg), t & 1u, abort, &g_timeout) &&
+                          mbar_wait(o_empty(wg), (t & 1u) ^ 1u, abort, &g_timeout);
+          const uint32_t bits = __shfl_sync(0xffffffffu, (pe ? 1u : 0u) | (k_ready ? 2u : 0u), 0);
+          if (!(bits & 1u)) {
             ok = false;
             break;
           }
+          k_ready = (bits & 2u) != 0;
           fence_after();
           const uint32_t gj = g + (uint32_t)j;
           const int s = gj % S;
@@ -321,12 +332,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             commit(o_full(wg));
             commit(kv_empty(s));
+            if (k_ready) emit_s(j + 2);
           }
           __syncwarp();
           // S_{j+2} reuses this warpgroup's S/P columns: issued after O_j, and
           // the tensor core runs one CTA's MMAs in issue order.
-          if (j + 2 < n_kb) {
-            ok = issue_s(j + 2);
+          if (next_s) {
+            if (!k_ready) ok = issue_s(j + 2);
             if (ok && j + 2 == n_kb - 1) release_q();
           }
         }
@@ -920,8 +932,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; ok && i < n_blk; ++i) {
         const bool dp_next = kTwoA && i + 1 < n_blk;
         {
-          const bool r2 = mbar_try(tile_full(2, i), tile_ph(i));
-          const bool r1 = dp_next ? mbar_try(tile_full(1, i + 1), tile_ph(i + 1)) : true;
+          const bool r2 = mbar_test(tile_full(2, i), tile_ph(i));
+          const bool r1 = dp_next ? mbar_test(tile_full(1, i + 1), tile_ph(i + 1)) : true;
           const bool e = mbar_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout);
           const uint32_t bits =
               __shfl_sync(0xffffffffu, (e ? 1u : 0u) | (r2 ? 2u : 0u) | (r1 ? 4u : 0u), 0);
@@ -942,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (i + 2 < n_blk) {
-          const bool r0 = mbar_try(tile_full(0, i + 2), tile_ph(i + 2));
+          const bool r0 = mbar_test(tile_full(0, i + 2), tile_ph(i + 2));
           const bool f = mbar_wait(s_free, (uint32_t)(i + 1) & 1u, abort, &g_timeout);
           const uint32_t bits = __shfl_sync(0xffffffffu, (f ? 1u : 0u) | (r0 ? 2u : 0u), 0);
           if (!(bits & 1u)) {
