@@ -88,11 +88,12 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t base, int kk) {
 }
 
 // Register split: the CTA launches with 384 x kLaunchRegs; warps 0-3 (TMA,
-// MMA, idle) give theirs down to kLowRegs so that the eight softmax warps can
-// hold a full S row and output row each.  4*32*kLowRegs + 8*32*kHighRegs must
-// not exceed 384 * (registers per thread at launch), which the host checks
-// before launching.
-constexpr int kLowRegs = 48, kHighRegs = 208;
+// MMA) give theirs down to kLowRegs (enough for their work-item and ring
+// bookkeeping) so that the eight softmax / element-wise warps can hold a full
+// S row and output row each.  4*32*kLowRegs + 8*32*kHighRegs must not exceed
+// 384 * (registers per thread at launch): with 168 at launch it is exact, and
+// the host checks it before launching.
+constexpr int kLowRegs = 88, kHighRegs = 208;
 constexpr int kMinLaunchRegs = (4 * 32 * kLowRegs + 8 * 32 * kHighRegs + kThreads - 1) / kThreads;
 
 __device__ __forceinline__ void reg_dec() {
@@ -107,7 +108,7 @@ __device__ __forceinline__ void wg_pair_sync() {
 // are ordered longest first (the last query block has the most keys) and
 // dealt in a snake (c, then G-1-c, ...), which balances the CTAs' total
 // lengths.  -1 when the CTA has no item k.
-__device__ __forceinline__ int fwd_item(int c, int k, int G, int n_items) {
+__device__ __forceinline__ int work_item(int c, int k, int G, int n_items) {
   const int w = k * G + ((k & 1) ? (G - 1 - c) : c);
   return w < n_items ? w : -1;
 }
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         uint32_t g = 0;  // key blocks loaded so far (all items)
         for (int k = 0; ok; ++k) {
-          const int w = fwd_item(cta, k, G, p.n_items);
+          const int w = work_item(cta, k, G, p.n_items);
           if (w < 0) break;
           const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
           const int n_kb = item_nkb(w);
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true, pending = false;
         uint32_t pend_ph = 0;
         for (int k = 0;; ++k) {
-          const int w = fwd_item(cta, k, G, p.n_items);
+          const int w = work_item(cta, k, G, p.n_items);
           if (w < 0) break;
           // The element-wise warps have copied the previous item's Q out.
           if (!mbar_wait(q_empty, ((uint32_t)k & 1u) ^ 1u, abort, &g_timeout)) {
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
       };
       for (int k = 0; ok; ++k) {
-        const int w = fwd_item(cta, k, G, p.n_items);
+        const int w = work_item(cta, k, G, p.n_items);
         if (w < 0) break;
         const int n_kb = item_nkb(w);
         if (!warp_wait(q_ready, (uint32_t)k & 1u, abort, &g_timeout)) {
@@ -446,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     for (int k = 0; ok; ++k) {
-      const int w = fwd_item(cta, k, G, p.n_items);
+      const int w = work_item(cta, k, G, p.n_items);
       if (w < 0) break;
       const int bh = item_bh(w), b = bh / p.H;
       const int q0 = item_q0(w), q = q0 + row;
@@ -463,20 +464,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         for (int cc = wg; cc < D / 32; cc += 2) {
           const uint8_t* qs = smem + L::kQ + cc * 16384 + row * 128;
-          uint32_t hi[32], lo[32];
+          // hi, then lo (the previous item's accumulator is still live here)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 x = q < p.T ? *reinterpret_cast<const float4*>(qs + ((i ^ (row & 7)) << 4))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float xs[4] = {x.x, x.y, x.z, x.w};
+          for (int part = 0; part < 2; ++part) {
+            uint32_t v[32];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              hi[4 * i + e] = __float_as_uint(tf32_hi(xs[e]));
-              lo[4 * i + e] = __float_as_uint(tf32_lo(xs[e]));
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = q < p.T ? *reinterpret_cast<const float4*>(qs + ((i ^ (row & 7)) << 4))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                v[4 * i + e] = __float_as_uint(part ? tf32_lo(xs[e]) : tf32_hi(xs[e]));
             }
+            tmem_st32(tmem + lane_off + part * D + 32 * cc, v);
           }
-          tmem_st32(tmem + lane_off + 32 * cc, hi);
-          tmem_st32(tmem + lane_off + D + 32 * cc, lo);
         }
         mbar_arrive(q_empty);
         tmem_wait_st();
@@ -687,7 +689,7 @@ struct BwdLayout {
   static constexpr uint32_t kRing1 = kRing0 + kRing * kSlot;                  // dP operand
   static constexpr uint32_t kRing2 = kRing1 + (kTwoA ? kRing * kSlot : 0);    // product operand
   static constexpr uint32_t kBars = kRing2 + kRing * kSlot2;
-  static constexpr uint32_t kNumBars = 6 * kRing + 7;
+  static constexpr uint32_t kNumBars = 6 * kRing + 8;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static_assert(kDynSmem <= 232448, "shared memory budget");
@@ -703,17 +705,46 @@ struct BwdParams {
   int T, H, C;
   float scale, scale_log2;
   int xb0, xb1, xb2;  // column of ring r's tensor for head 0 (head h adds h*D)
+  int n_items;        // (128-row block, batch x head) pairs
+  int nrb;            // 128-row blocks per sequence
 };
 
-// One producer warp: the ring of one B operand (raw and lo tiles of each
-// minor block; for the product ring of a key-major kernel also the block's
-// lse / Delta vectors).  Returns false if a wait gave up; the copies already
-// issued have landed when it returns.
-template <int D, int R, bool VEC>
-__device__ bool produce_ring(uint32_t ring, uint32_t slot_bytes, uint32_t full0, uint32_t empty0,
-                             const CUtensorMap* m, const CUtensorMap* mlo, int xcol, int row0,
-                             int blk0, int n_blk, uint8_t* smem_ring, const BwdParams& p, int bh,
-                             volatile int* abort) {
+// One work item: the 128 "major" rows [r0, r0+128) of head h of sequence b
+// and their minor blocks blk0 .. blk0+n_blk-1.  Items are numbered longest
+// first: key-major items start at the diagonal (the first key block has the
+// most query blocks), query-major items end there (the last query block has
+// the most key blocks).
+struct BwdItem {
+  int bh, b, h, r0, blk0, n_blk;
+};
+template <bool KEY_MAJOR>
+__device__ __forceinline__ BwdItem bwd_item(int w, const BwdParams& p) {
+  const int BH = p.n_items / p.nrb;
+  BwdItem it;
+  it.bh = w % BH;
+  it.b = it.bh / p.H;
+  it.h = it.bh % p.H;
+  const int n_all = (p.T + kBKV - 1) / kBKV;
+  if (KEY_MAJOR) {
+    it.r0 = (w / BH) * kBQ;
+    it.blk0 = it.r0 / kBKV;
+    it.n_blk = n_all - it.blk0;
+  } else {
+    it.r0 = (p.nrb - 1 - w / BH) * kBQ;
+    it.blk0 = 0;
+    it.n_blk = (min(it.r0 + kBQ, p.T) + kBKV - 1) / kBKV;
+  }
+  return it;
+}
+
+// One producer warp: the ring of one B operand over all of the CTA's items
+// (raw and lo tiles of each minor block; for the product ring of a key-major
+// kernel also the block's lse / Delta vectors).  The copies already issued
+// have landed when it returns.
+template <int D, int R, bool VEC, bool KEY_MAJOR>
+__device__ void produce_ring(uint32_t ring, uint32_t slot_bytes, uint32_t full0, uint32_t empty0,
+                             const CUtensorMap* m, const CUtensorMap* mlo, int xb, uint8_t* smem_ring,
+                             const BwdParams& p, volatile int* abort) {
   constexpr uint32_t kTile = kBKV * D * 4;
   const int lane = threadIdx.x & 31;
   bool issued[R];
@@ -721,46 +752,58 @@ __device__ bool produce_ring(uint32_t ring, uint32_t slot_bytes, uint32_t full0,
 #pragma unroll
   for (int s = 0; s < R; ++s) issued[s] = false, issued_ph[s] = 0;
   bool ok = true;
-  for (int i = 0; i < n_blk; ++i) {
-    const int s = i % R;
-    const uint32_t ph = (uint32_t)(i / R) & 1u;
-    if (!warp_wait(empty0 + 8u * s, ph ^ 1u, abort, &g_timeout)) {
-      ok = false;
-      break;
-    }
-    issued[s] = true;
-    issued_ph[s] = ph;
-    const int blk = blk0 + i;
-    const int row = row0 + blk * kBKV;
-    const uint32_t dst = ring + s * slot_bytes;
-    if (elect_one()) {
-      mbar_expect_tx(full0 + 8u * s, 2 * kTile);
+  uint32_t g = 0;  // minor blocks loaded so far (all items)
+  for (int k = 0; ok; ++k) {
+    const int w = work_item((int)blockIdx.x, k, (int)gridDim.x, p.n_items);
+    if (w < 0) break;
+    const BwdItem it = bwd_item<KEY_MAJOR>(w, p);
+    const int xcol = xb + it.h * D;
+    for (int i = 0; i < it.n_blk; ++i, ++g) {
+      const int s = g % R;
+      const uint32_t ph = (g / R) & 1u;
+      if (!warp_wait(empty0 + 8u * s, ph ^ 1u, abort, &g_timeout)) {
+        ok = false;
+        break;
+      }
+      issued[s] = true;
+      issued_ph[s] = ph;
+      const int blk = it.blk0 + i;
+      const int row = it.b * p.T + blk * kBKV;
+      const uint32_t dst = ring + s * slot_bytes;
+      if (elect_one()) {
+        mbar_expect_tx(full0 + 8u * s, 2 * kTile);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        tma_load_2d(dst + c * 8192, m, full0 + 8u * s, xcol + 32 * c, row);
-        tma_load_2d(dst + kTile + c * 8192, mlo, full0 + 8u * s, xcol + 32 * c, row);
-      }
-    }
-    __syncwarp();
-    if (VEC) {
-      float* vec = reinterpret_cast<float*>(smem_ring + s * slot_bytes + 2 * kTile);
-      for (int c = lane; c < kBKV; c += 32) {
-        const int q = blk * kBKV + c;
-        const bool in = q < p.T;
-        vec[c] = in ? p.lse[(size_t)bh * p.T + q] * kLog2e : 0.0f;
-        vec[kBKV + c] = in ? p.delta[(size_t)bh * p.T + q] : 0.0f;
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_2d(dst + c * 8192, m, full0 + 8u * s, xcol + 32 * c, row);
+          tma_load_2d(dst + kTile + c * 8192, mlo, full0 + 8u * s, xcol + 32 * c, row);
+        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(full0 + 8u * s);
-      __syncwarp();
+      if (VEC) {
+        float* vec = reinterpret_cast<float*>(smem_ring + s * slot_bytes + 2 * kTile);
+        for (int c = lane; c < kBKV; c += 32) {
+          const int q = blk * kBKV + c;
+          const bool in = q < p.T;
+          vec[c] = in ? p.lse[(size_t)it.bh * p.T + q] * kLog2e : 0.0f;
+          vec[kBKV + c] = in ? p.delta[(size_t)it.bh * p.T + q] : 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full0 + 8u * s);
+        __syncwarp();
+      }
     }
   }
   if (!ok && lane == 0)
     for (int s = 0; s < R; ++s)
       if (issued[s]) mbar_wait_drain(full0 + 8u * s, issued_ph[s], &g_timeout);
-  return ok;
 }
 
+// Persistent: one CTA per SM loops over work items (dealt like the forward's).
+// Per item the element-wise warps load the item's A rows into TMEM as soon as
+// the previous item's last S / dP MMA is done, and only then fold the previous
+// item's last product and store its gradient rows, so the tensor core starts
+// the next item while the previous one's epilogue runs; the next item's A rows
+// are prefetched into L2 meanwhile.
 template <int MODE, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm0lo,
@@ -782,22 +825,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_ready = bar0 + 48u * R;
   const uint32_t s_full = a_ready + 8u, s_free = a_ready + 16u, dp_full = a_ready + 24u;
   const uint32_t ew_done = a_ready + 32u, out_full = a_ready + 40u, drain = a_ready + 48u;
+  const uint32_t a_free = a_ready + 56u;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int n_all = (p.T + kBKV - 1) / kBKV;
-  int r0, blk0, n_blk;
-  if (kKeyMajor) {  // keys [r0, r0+128); query blocks from the diagonal to the end
-    r0 = (int)blockIdx.x * kBQ;
-    blk0 = r0 / kBKV;
-    n_blk = n_all - blk0;
-  } else {  // queries [r0, r0+128); key blocks up to the diagonal
-    const int nqb = (p.T + kBQ - 1) / kBQ;
-    r0 = (nqb - 1 - (int)blockIdx.x) * kBQ;
-    blk0 = 0;
-    n_blk = (min(r0 + kBQ, p.T) + kBKV - 1) / kBKV;
-  }
+  const int cta = (int)blockIdx.x, G = (int)gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -816,6 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(ew_done, 2 * kWgThreads);
     mbar_init(out_full, 1);
     mbar_init(drain, 1);
+    mbar_init(a_free, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -833,21 +866,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
     reg_dec();
-    const int xo = h * D;
     if (warp == 0) {
       // ---------------------------------------------------------- S operand
-      produce_ring<D, R, false>(sbase + L::kRing0, L::kSlot, full0, empty0, &tm0, &tm0lo,
-                                p.xb0 + xo, b * p.T, blk0, n_blk, smem + L::kRing0, p, bh, abort);
+      produce_ring<D, R, false, kKeyMajor>(sbase + L::kRing0, L::kSlot, full0, empty0, &tm0, &tm0lo,
+                                           p.xb0, smem + L::kRing0, p, abort);
     } else if (warp == 2) {
       // ---------------------------------------------------------- dP operand
       if (kTwoA)
-        produce_ring<D, R, false>(sbase + L::kRing1, L::kSlot, full1, empty1, &tm1, &tm1lo,
-                                  p.xb1 + xo, b * p.T, blk0, n_blk, smem + L::kRing1, p, bh, abort);
+        produce_ring<D, R, false, kKeyMajor>(sbase + L::kRing1, L::kSlot, full1, empty1, &tm1,
+                                             &tm1lo, p.xb1, smem + L::kRing1, p, abort);
     } else if (warp == 3) {
       // ---------------------------------------------------------- product operand
-      produce_ring<D, R, kKeyMajor>(sbase + L::kRing2, L::kSlot2, full2, empty2, &tm2, &tm2lo,
-                                    p.xb2 + xo, b * p.T, blk0, n_blk, smem + L::kRing2, p, bh,
-                                    abort);
+      produce_ring<D, R, kKeyMajor, kKeyMajor>(sbase + L::kRing2, L::kSlot2, full2, empty2, &tm2,
+                                               &tm2lo, p.xb2, smem + L::kRing2, p, abort);
     } else {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
@@ -865,23 +896,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts(d, a + D + kk * 8, k_desc(t, kk), id_s, 1u);
         }
       };
-      // MMAs and commits of one operation (the elected lane); the waits for
-      // its operands come before.
-      auto emit_s = [&](int j) {
-        const int s = j % R;
+      // MMAs and commits of one operation on minor block g (global index over
+      // the CTA's items; the elected lane); the waits for its operands come before.
+      auto emit_s = [&](uint32_t g) {
+        const int s = g % R;
         issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s * L::kSlot);
         commit(empty0 + 8u * s);
         commit(s_full);
       };
-      auto emit_dp = [&](int j) {
-        const int s = j % R;
+      auto emit_dp = [&](uint32_t g) {
+        const int s = g % R;
         issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s * L::kSlot);
         commit(empty1 + 8u * s);
         commit(dp_full);
       };
-      // Product of block j: A = E (hi over dP, lo apart), B = the MN-major tile.
-      auto emit_out = [&](int j) {
-        const int s = j % R;
+      // Product of block g: A = E (hi over dP, lo apart), B = the MN-major tile.
+      auto emit_out = [&](uint32_t g) {
+        const int s = g % R;
         const uint32_t tb = sbase + L::kRing2 + s * L::kSlot2, tblo = tb + L::kTile;
 #pragma unroll
         for (int kk = 0; kk < kBKV / 8; ++kk)
@@ -894,81 +925,99 @@ __global__ void __launch_bounds__(kThreads, 1)
         commit(empty2 + 8u * s);
         commit(out_full);
       };
-      // Tile barrier of ring r (0: S operand, 1: dP operand, 2: product operand) for block j.
-      auto tile_full = [&](int r, int j) {
-        return (r == 0 ? full0 : r == 1 ? full1 : full2) + 8u * (uint32_t)(j % R);
+      // Tile barrier of ring r (0: S operand, 1: dP operand, 2: product operand) for block g.
+      auto tile_full = [&](int r, uint32_t g) {
+        return (r == 0 ? full0 : r == 1 ? full1 : full2) + 8u * (g % R);
       };
-      auto tile_ph = [&](int j) { return (uint32_t)(j / R) & 1u; };
-      auto issue = [&](int r, int j) -> bool {
-        if (!warp_wait(tile_full(r, j), tile_ph(j), abort, &g_timeout)) return false;
+      auto tile_ph = [&](uint32_t g) { return (g / R) & 1u; };
+      auto issue = [&](int r, uint32_t g) -> bool {
+        if (!warp_wait(tile_full(r, g), tile_ph(g), abort, &g_timeout)) return false;
         fence_after();
         if (elect_one()) {
           if (r == 0)
-            emit_s(j);
+            emit_s(g);
           else if (r == 1)
-            emit_dp(j);
+            emit_dp(g);
           else
-            emit_out(j);
+            emit_out(g);
         }
         __syncwarp();
         return true;
       };
-      bool ok = warp_wait(a_ready, 0, abort, &g_timeout);
-      fence_after();
-      if (ok) ok = issue(0, 0);
-      if (ok && kTwoA) ok = issue(1, 0);
-      if (ok && n_blk > 1) {
-        ok = warp_wait(s_free, 0, abort, &g_timeout);
+      // After the item's last S and dP: the A columns may take the next item's rows.
+      auto release_a = [&]() {
+        if (elect_one()) commit(a_free);
+        __syncwarp();
+      };
+      bool ok = true;
+      uint32_t g = 0;  // minor blocks of earlier items
+      for (int k = 0; ok; ++k) {
+        const int w = work_item(cta, k, G, p.n_items);
+        if (w < 0) break;
+        const int n_blk = bwd_item<kKeyMajor>(w, p).n_blk;
+        ok = warp_wait(a_ready, (uint32_t)k & 1u, abort, &g_timeout);
         fence_after();
-        if (ok) ok = issue(0, 1);
-      }
-      // dP_{i+1} overwrites the columns product_i reads and S_{i+2} those S_{i+1}
-      // was read from: each is issued after the MMAs or the reads it must
-      // follow (one CTA's MMAs run in issue order).  The tensor core queues
-      // almost no MMAs, so every wait or re-convergence between them idles it:
-      // the tile barriers (nearly always complete) are probed while waiting
-      // for the element-wise warps, and the MMAs that follow one such wait go
-      // out in one elected run.
-      for (int i = 0; ok && i < n_blk; ++i) {
-        const bool dp_next = kTwoA && i + 1 < n_blk;
-        {
-          const bool r2 = mbar_test(tile_full(2, i), tile_ph(i));
-          const bool r1 = dp_next ? mbar_test(tile_full(1, i + 1), tile_ph(i + 1)) : true;
-          const bool e = mbar_wait(ew_done, (uint32_t)i & 1u, abort, &g_timeout);
-          const uint32_t bits =
-              __shfl_sync(0xffffffffu, (e ? 1u : 0u) | (r2 ? 2u : 0u) | (r1 ? 4u : 0u), 0);
-          if (!(bits & 1u)) {
-            ok = false;
-            break;
-          }
+        if (ok) ok = issue(0, g);
+        if (ok && kTwoA) ok = issue(1, g);
+        if (ok && n_blk > 1) {
+          ok = warp_wait(s_free, g & 1u, abort, &g_timeout);
           fence_after();
-          if ((bits & 6u) == 6u) {
-            if (elect_one()) {
-              emit_out(i);
-              if (dp_next) emit_dp(i + 1);
+          if (ok) ok = issue(0, g + 1);
+        }
+        // The last S is S_{n-1}; with a dP operand the last dP (dP_{n-1}) comes later.
+        if (ok && (n_blk == 1 || (!kTwoA && n_blk == 2))) release_a();
+        // dP_{i+1} overwrites the columns product_i reads and S_{i+2} those S_{i+1}
+        // was read from: each is issued after the MMAs or the reads it must
+        // follow (one CTA's MMAs run in issue order).  The tensor core queues
+        // almost no MMAs, so every wait or re-convergence between them idles it:
+        // the tile barriers (nearly always complete) are tested while waiting
+        // for the element-wise warps, and the MMAs that follow one such wait go
+        // out in one elected run.
+        for (int i = 0; ok && i < n_blk; ++i) {
+          const uint32_t gi = g + (uint32_t)i;
+          const bool dp_next = kTwoA && i + 1 < n_blk;
+          {
+            const bool r2 = mbar_test(tile_full(2, gi), tile_ph(gi));
+            const bool r1 = dp_next ? mbar_test(tile_full(1, gi + 1), tile_ph(gi + 1)) : true;
+            const bool e = mbar_wait(ew_done, gi & 1u, abort, &g_timeout);
+            const uint32_t bits =
+                __shfl_sync(0xffffffffu, (e ? 1u : 0u) | (r2 ? 2u : 0u) | (r1 ? 4u : 0u), 0);
+            if (!(bits & 1u)) {
+              ok = false;
+              break;
             }
-            __syncwarp();
-          } else if (!issue(2, i) || (dp_next && !issue(1, i + 1))) {
-            ok = false;
-            break;
+            fence_after();
+            if ((bits & 6u) == 6u) {
+              if (elect_one()) {
+                emit_out(gi);
+                if (dp_next) emit_dp(gi + 1);
+              }
+              __syncwarp();
+            } else if (!issue(2, gi) || (dp_next && !issue(1, gi + 1))) {
+              ok = false;
+              break;
+            }
+            if (dp_next && i + 2 == n_blk) release_a();
+          }
+          if (i + 2 < n_blk) {
+            const bool r0 = mbar_test(tile_full(0, gi + 2), tile_ph(gi + 2));
+            const bool f = mbar_wait(s_free, (gi + 1) & 1u, abort, &g_timeout);
+            const uint32_t bits = __shfl_sync(0xffffffffu, (f ? 1u : 0u) | (r0 ? 2u : 0u), 0);
+            if (!(bits & 1u)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            if (bits & 2u) {
+              if (elect_one()) emit_s(gi + 2);
+              __syncwarp();
+            } else {
+              ok = issue(0, gi + 2);
+            }
+            if (ok && !kTwoA && i + 3 == n_blk) release_a();
           }
         }
-        if (i + 2 < n_blk) {
-          const bool r0 = mbar_test(tile_full(0, i + 2), tile_ph(i + 2));
-          const bool f = mbar_wait(s_free, (uint32_t)(i + 1) & 1u, abort, &g_timeout);
-          const uint32_t bits = __shfl_sync(0xffffffffu, (f ? 1u : 0u) | (r0 ? 2u : 0u), 0);
-          if (!(bits & 1u)) {
-            ok = false;
-            break;
-          }
-          fence_after();
-          if (bits & 2u) {
-            if (elect_one()) emit_s(i + 2);
-            __syncwarp();
-          } else {
-            ok = issue(0, i + 2);
-          }
-        }
+        g += (uint32_t)n_blk;
       }
       if (!ok) {
         if (elect_one()) commit(drain);
@@ -982,54 +1031,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg = (warp - 4) >> 2;  // columns [32*wg, 32*wg + 32) of every block
     const int ew = warp & 3;
     const int row = ew * 32 + lane;
-    const int r = r0 + row;  // key (kDV, kDK) or query (kDQ) index
-    const bool r_in = r < p.T;
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
     const size_t ld = (size_t)3 * p.C;
-    {
-      // A operands of this row -> TMEM (hi at base, lo at base + D).
-      const size_t grow = (size_t)b * p.T + (r_in ? r : 0);
-      const float* a1 = p.qkv + grow * ld + (kKeyMajor ? p.C : 0) + (size_t)h * D;
-      const float* a2 = MODE == kDK ? p.qkv + grow * ld + 2 * (size_t)p.C + (size_t)h * D
-                                    : p.dout + grow * (size_t)p.C + (size_t)h * D;
-#pragma unroll
-      for (int t = 0; t < (kTwoA ? 2 : 1); ++t) {
-        const float* src = t ? a2 : a1;
-        const uint32_t base = tmem + lane_off + (t ? kBA2 : kBA1);
-        for (int cc = wg; cc < D / 32; cc += 2) {
-          uint32_t hi[32], lo[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 x = r_in ? *reinterpret_cast<const float4*>(src + 32 * cc + i)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
-              lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
-            }
-          }
-          tmem_st32(base + 32 * cc, hi);
-          tmem_st32(base + D + 32 * cc, lo);
-        }
-      }
-      tmem_wait_st();
-      fence_before();
-      mbar_arrive(a_ready);
-    }
-    float lse2_row = 0.0f, delta_row = 0.0f;
-    if (!kKeyMajor && r_in) {
-      lse2_row = p.lse[(size_t)bh * p.T + r] * kLog2e;
-      delta_row = p.delta[(size_t)bh * p.T + r];
-    }
     const bool folds = D == 64 || wg == 0;  // output columns [32*wg, 32*wg + 32)
-    float acc[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
     const float c2 = p.scale_log2;
+    // A rows of an item: A1 = K (key-major kernels) or Q (dQ) from qkv, A2 =
+    // V (dK) or dO (dQ); the dV kernel has A1 only.
+    auto a_rows = [&](const BwdItem& it, const float*& a1, const float*& a2) -> bool {
+      const int r = it.r0 + row;
+      const bool r_in = r < p.T;
+      const size_t grow = (size_t)it.b * p.T + (r_in ? r : 0);
+      a1 = p.qkv + grow * ld + (kKeyMajor ? p.C : 0) + (size_t)it.h * D;
+      a2 = MODE == kDK ? p.qkv + grow * ld + 2 * (size_t)p.C + (size_t)it.h * D
+                       : p.dout + grow * (size_t)p.C + (size_t)it.h * D;
+      return r_in;
+    };
+    float acc[32];
     bool ok = true;
-    auto fold = [&](int i) -> bool {
-      if (!mbar_wait(out_full, (uint32_t)i & 1u, abort, &g_timeout)) return false;
+    uint32_t g = 0;      // minor blocks of earlier items
+    int prev_w = -1;
+    uint32_t prev_last = 0;  // global index of the previous item's last block
+    auto fold = [&](uint32_t gi) -> bool {
+      if (!mbar_wait(out_full, gi & 1u, abort, &g_timeout)) return false;
       fence_after();
       if (folds) {
         uint32_t v[32];
@@ -1039,82 +1062,159 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
-    for (int i = 0; i < n_blk; ++i) {
-      const int s = i % R;
-      if (!mbar_wait(s_full, (uint32_t)i & 1u, abort, &g_timeout) ||
-          (kKeyMajor && !mbar_wait(full2 + 8u * s, (uint32_t)(i / R) & 1u, abort, &g_timeout))) {
+    // Last fold and gradient rows of item w.
+    auto finish = [&](int w) -> bool {
+      if (!fold(prev_last)) return false;
+      const BwdItem it = bwd_item<kKeyMajor>(w, p);
+      const int r = it.r0 + row;
+      if (r < p.T && folds) {
+        const float f = MODE == kDV ? 1.0f : p.scale;
+        const int col = (MODE == kDQ ? 0 : MODE == kDK ? p.C : 2 * p.C) + it.h * D + 32 * wg;
+        float* dst = p.dqkv + ((size_t)it.b * p.T + r) * ld + col;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+          *reinterpret_cast<float4*>(dst + c) =
+              make_float4(acc[c] * f, acc[c + 1] * f, acc[c + 2] * f, acc[c + 3] * f);
+      }
+      return true;
+    };
+    for (int k = 0; ok; ++k) {
+      const int w = work_item(cta, k, G, p.n_items);
+      if (w < 0) break;
+      const BwdItem it = bwd_item<kKeyMajor>(w, p);
+      const int r = it.r0 + row;  // key (kDV, kDK) or query (kDQ) index
+      {
+        // A operands of this row -> TMEM (hi at base, lo at base + D), once the
+        // previous item's last S / dP MMA has read the old ones.
+        const float* a1;
+        const float* a2;
+        const bool r_in = a_rows(it, a1, a2);
+        if (k > 0 && !mbar_wait(a_free, (uint32_t)(k - 1) & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll
+        for (int t = 0; t < (kTwoA ? 2 : 1); ++t) {
+          const float* src = t ? a2 : a1;
+          const uint32_t base = tmem + lane_off + (t ? kBA2 : kBA1);
+          for (int cc = wg; cc < D / 32; cc += 2) {
+            uint32_t hi[32], lo[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 x = r_in ? *reinterpret_cast<const float4*>(src + 32 * cc + i)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
+                lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
+              }
+            }
+            tmem_st32(base + 32 * cc, hi);
+            tmem_st32(base + D + 32 * cc, lo);
+          }
+        }
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(a_ready);
+        // The next item's A rows -> L2 while this item runs.
+        const int wn = work_item(cta, k + 1, G, p.n_items);
+        if (wn >= 0) {
+          const float* n1;
+          const float* n2;
+          if (a_rows(bwd_item<kKeyMajor>(wn, p), n1, n2)) {
+            for (int cc = wg; cc < D / 32; cc += 2) {
+              asm volatile("prefetch.L2 [%0];" ::"l"(n1 + 32 * cc));
+              if (kTwoA) asm volatile("prefetch.L2 [%0];" ::"l"(n2 + 32 * cc));
+            }
+          }
+        }
+      }
+      if (prev_w >= 0 && !finish(prev_w)) {
         ok = false;
         break;
       }
-      fence_after();
-      uint32_t sv[32];
-      tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
-      fence_before();
-      mbar_arrive(s_free);
-      const float* vec =
-          reinterpret_cast<const float*>(smem + L::kRing2 + s * L::kSlot2 + 2 * L::kTile) + 32 * wg;
-      // Blocks clear of the diagonal (and of the sequence end) need no mask;
-      // the test is uniform over the CTA.
-      const int m0 = (blk0 + i) * kBKV + 32 * wg;  // minor index of column 0 of this half
-      const int mb0 = (blk0 + i) * kBKV;
-      const bool full = kKeyMajor ? (mb0 >= r0 + kBQ - 1 && mb0 + kBKV <= p.T)
-                                  : (mb0 + kBKV - 1 <= r0);
-      float e[32];
-      if (full) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
+      float lse2_row = 0.0f, delta_row = 0.0f;
+      if (!kKeyMajor && r < p.T) {
+        lse2_row = p.lse[(size_t)it.bh * p.T + r] * kLog2e;
+        delta_row = p.delta[(size_t)it.bh * p.T + r];
+      }
+      for (int i = 0; i < it.n_blk; ++i) {
+        const uint32_t gi = g + (uint32_t)i;
+        const int s = gi % R;
+        if (!mbar_wait(s_full, gi & 1u, abort, &g_timeout) ||
+            (kKeyMajor && !mbar_wait(full2 + 8u * s, (gi / R) & 1u, abort, &g_timeout))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        uint32_t sv[32];
+        tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
+        fence_before();
+        mbar_arrive(s_free);
+        const float* vec =
+            reinterpret_cast<const float*>(smem + L::kRing2 + s * L::kSlot2 + 2 * L::kTile) + 32 * wg;
+        // Blocks clear of the diagonal (and of the sequence end) need no mask;
+        // the test is uniform over the CTA.
+        const int m0 = (it.blk0 + i) * kBKV + 32 * wg;  // minor index of column 0 of this half
+        const int mb0 = (it.blk0 + i) * kBKV;
+        const bool full = kKeyMajor ? (mb0 >= it.r0 + kBQ - 1 && mb0 + kBKV <= p.T)
+                                    : (mb0 + kBKV - 1 <= it.r0);
+        float e[32];
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float l2 = kKeyMajor ? vec[c] : lse2_row;
+            e[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int m = m0 + c;
+            const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
+            const float l2 = kKeyMajor ? vec[c] : lse2_row;
+            e[c] = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
+          }
+        }
+        // dP_i done implies product_{i-1} done (issued before it).
+        if (kTwoA && !mbar_wait(dp_full, gi & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        if (i > 0 && !fold(gi - 1)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        uint32_t dv[32];
+        if (kTwoA) {
+          tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
+            e[c] = e[c] * (__uint_as_float(dv[c]) - dl);
+          }
+        }
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float l2 = kKeyMajor ? vec[c] : lse2_row;
-          e[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2));
+          sv[c] = __float_as_uint(tf32_hi(e[c]));
+          dv[c] = __float_as_uint(tf32_lo(e[c]));
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int m = m0 + c;
-          const bool valid = kKeyMajor ? (m >= r && m < p.T) : (m <= r);
-          const float l2 = kKeyMajor ? vec[c] : lse2_row;
-          e[c] = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -l2)) : 0.0f;
-        }
+        tmem_st32(tmem + lane_off + kBdP + 32 * wg, sv);
+        tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(ew_done);
       }
-      // dP_i done implies product_{i-1} done (issued before it).
-      if (kTwoA && !mbar_wait(dp_full, (uint32_t)i & 1u, abort, &g_timeout)) {
-        ok = false;
-        break;
-      }
-      if (i > 0 && !fold(i - 1)) {
-        ok = false;
-        break;
-      }
-      fence_after();
-      uint32_t dv[32];
-      if (kTwoA) {
-        tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float dl = kKeyMajor ? vec[kBKV + c] : delta_row;
-          e[c] = e[c] * (__uint_as_float(dv[c]) - dl);
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        sv[c] = __float_as_uint(tf32_hi(e[c]));
-        dv[c] = __float_as_uint(tf32_lo(e[c]));
-      }
-      tmem_st32(tmem + lane_off + kBdP + 32 * wg, sv);
-      tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);
-      tmem_wait_st();
-      fence_before();
-      mbar_arrive(ew_done);
+      if (!ok) break;
+      g += (uint32_t)it.n_blk;
+      prev_w = w;
+      prev_last = g - 1u;
     }
-    if (ok) ok = fold(n_blk - 1);
-    if (ok && r_in && folds) {
-      const float f = MODE == kDV ? 1.0f : p.scale;
-      const int col = (MODE == kDQ ? 0 : MODE == kDK ? p.C : 2 * p.C) + h * D + 32 * wg;
-      float* dst = p.dqkv + ((size_t)b * p.T + r) * ld + col;
-#pragma unroll
-      for (int c = 0; c < 32; c += 4)
-        *reinterpret_cast<float4*>(dst + c) =
-            make_float4(acc[c] * f, acc[c + 1] * f, acc[c + 2] * f, acc[c + 3] * f);
-    }
+    if (ok && prev_w >= 0) ok = finish(prev_w);
   }
 
   fence_before();
@@ -1160,7 +1260,7 @@ ns_status launch_bwd_mode(const CUtensorMap* maps, const BwdParams& p, int B, in
   NS_TRY_CUDA(cudaFuncGetAttributes(&fa, kern), "ns_attn_bwd attributes");
   if (fa.numRegs < kMinLaunchRegs)
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_bwd: kernel compiled with too few registers for its split");
-  const dim3 grid((T + kBQ - 1) / kBQ, B * H);
+  const int grid = std::min(p.n_items, sm_count());
   kern<<<grid, kThreads, L::kDynSmem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
   return check_launch(MODE == kDV ? "ns_attn_bwd dV tcgen05"
                                   : MODE == kDK ? "ns_attn_bwd dK tcgen05" : "ns_attn_bwd dQ tcgen05");
@@ -1186,7 +1286,8 @@ ns_status launch_bwd(const float* qkv, const float* dout, const float* lse, cons
   if (rc == NS_OK) rc = make_map(&dlmn, dout_lo, C, rows, C, kBKV, true);
   if (rc != NS_OK) return rc;
   const float scale = 1.0f / sqrtf((float)D);
-  BwdParams p{qkv, dout, lse, delta, dqkv, T, H, C, scale, scale * kLog2e, 0, 0, 0};
+  const int nrb = (T + kBQ - 1) / kBQ;
+  BwdParams p{qkv, dout, lse, delta, dqkv, T, H, C, scale, scale * kLog2e, 0, 0, 0, nrb * B * H, nrb};
   {  // dV: Q (K-major), dO (MN-major)
     const CUtensorMap m[6] = {qk, qlk, dmn, dlmn, dmn, dlmn};
     p.xb0 = 0; p.xb1 = 0; p.xb2 = 0;
