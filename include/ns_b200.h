@@ -143,6 +143,14 @@ NS_API ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* wo
  * reference counterpart (a fusion of linear.h:104-111 with the operand split). */
 NS_API ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy_lo,
                              void* workspace, size_t workspace_bytes, void* stream);
+/* GeluBackward fused on the way into ns_bias_grad_split: dY (the gradient at
+ * the GELU output) is replaced in place by dY * gelu'(pre), and db and dy_lo
+ * are those of the product (include/layers/activation.h GeluBackward followed
+ * by linear.h:104-111's bias sum; one pass instead of three).  Same
+ * requirements and workspace as ns_bias_grad_split; pre 16-byte aligned. */
+NS_API ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, float* db,
+                                  float* dy_lo, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 /* ------------------------------------------------------------ K2 attention
  * Fused causal self-attention on the interleaved c_attn output

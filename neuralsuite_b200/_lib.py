@@ -57,6 +57,7 @@ _SIGS = {
     "ns_bias_grad_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_bias_grad": (c_int, [P, c_int, c_int, P, P, c_size_t, P]),
     "ns_bias_grad_split": (c_int, [P, c_int, c_int, P, P, P, c_size_t, P]),
+    "ns_bias_grad_split_gelu": (c_int, [P, P, c_int, c_int, P, P, P, c_size_t, P]),
     "ns_attn_fwd_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ns_attn_fwd": (c_int, [P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
     "ns_attn_set_engine": (c_int, [c_int]),

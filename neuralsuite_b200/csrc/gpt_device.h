@@ -219,10 +219,12 @@ class Linear : public Layer {
   Tensor ForwardResidual(const Tensor& x, const Tensor& resid) {
     return Run(x, NS_EPI_BIAS_RESID, resid.Data(), nullptr);
   }
-  Tensor Backward(const Tensor& dy) override { return BackwardImpl(dy, NS_EPI_STORE, nullptr); }
-  // dX = (dY W^T) * gelu'(pre): Linear::Backward followed by GeluBackward.
-  Tensor BackwardGelu(const Tensor& dy, const Tensor& gelu_input) {
-    return BackwardImpl(dy, NS_EPI_GELU_BWD, gelu_input.Data());
+  Tensor Backward(const Tensor& dy) override { return BackwardImpl(dy, nullptr); }
+  // GeluBackward then Linear::Backward: `dpost` is the gradient at gelu(Y)
+  // for this layer's output Y = `pre`; it is overwritten by dpost * gelu'(pre),
+  // the gradient at Y (in the same pass as the bias sum and the operand split).
+  Tensor BackwardThroughGelu(const Tensor& dpost, const Tensor& pre) {
+    return BackwardImpl(dpost, pre.Data());
   }
   Parameter& WeightParam() { return weight_; }
   Parameter& BiasParam() { return bias_; }
@@ -258,7 +260,7 @@ class Linear : public Layer {
     shape.back() = out_;
     return y.View(shape);
   }
-  Tensor BackwardImpl(const Tensor& dy, int epi, const float* aux) {
+  Tensor BackwardImpl(const Tensor& dy, const float* gelu_pre) {
     const int n = Rows(last_input_, in_);
     if (Rows(dy, out_) != n) throw std::invalid_argument("Linear::Backward: batch mismatch");
     Tensor dx = Scratch(dx_buf_, n, in_);
@@ -268,15 +270,21 @@ class Linear : public Layer {
     const float* w_lo = lo ? w_lo_buf_.Data() : nullptr;
     const float* dy_lo = nullptr;
     if (lo) {
-      // db and dY's lo part from one pass over dY.
+      // db and dY's lo part from one pass over dY (with the GELU backward).
       Tensor dl = Scratch(dy_lo_buf_, n, out_);
-      Check(ns_bias_grad_split(dy.Data(), n, out_, bias_.Grad().Data(), dl.Data(), ctx_->scratch,
-                               ctx_->scratch_bytes, stream()));
+      if (gelu_pre)
+        Check(ns_bias_grad_split_gelu(dy.Data(), gelu_pre, n, out_, bias_.Grad().Data(), dl.Data(),
+                                      ctx_->scratch, ctx_->scratch_bytes, stream()));
+      else
+        Check(ns_bias_grad_split(dy.Data(), n, out_, bias_.Grad().Data(), dl.Data(), ctx_->scratch,
+                                 ctx_->scratch_bytes, stream()));
       dy_lo = dl.Data();
+    } else if (gelu_pre) {
+      Check(ns_gelu_bwd(dy.Data(), gelu_pre, dy.Data(), static_cast<int64_t>(n) * out_, stream()));
     }
     // dX = dY W^T  (W read transposed in place: no Transpose copy)
     Check(ns_gemm_lo(n, in_, out_, dy.Data(), out_, 0, dy_lo, weight_.Value().Data(), out_, 1, w_lo,
-                     dx.Data(), in_, 0.0f, epi, nullptr, aux, nullptr, ctx_->scratch,
+                     dx.Data(), in_, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ctx_->scratch,
                      ctx_->scratch_bytes, stream()));
     // dW = X^T dY, overwritten (MatMul's Resize+Zeros), X read transposed in place.
     Check(ns_gemm_lo(in_, out_, n, last_input_.Data(), in_, 1, x_lo, dy.Data(), out_, 0, dy_lo,
@@ -449,12 +457,13 @@ class GPTBlock : public Layer {
     return x2.View(x.Shape());
   }
   // GPTBlock::Backward (gpt.h:82-100) with the GELU backward fused into the
-  // mlp_proj dX GEMM and both residual adds fused into LayerNorm backward.
+  // mlp_fc bias-gradient pass and both residual adds fused into LayerNorm
+  // backward.
   Tensor Backward(const Tensor& dout) override {
     const int C = dout.Shape().back();
     const int M = Rows(dout, C);
-    Tensor dfc = mlp_proj_.BackwardGelu(dout.View({M, C}), fc_pre_);
-    Tensor dh2 = mlp_fc_.Backward(dfc);
+    Tensor dgelu = mlp_proj_.Backward(dout.View({M, C}));
+    Tensor dh2 = mlp_fc_.BackwardThroughGelu(dgelu, fc_pre_);
     Tensor dx1 = ln_2_.BackwardAdd(dh2, &dout);
     Tensor dh1 = attn_.Backward(dx1.View(dout.Shape()));
     Tensor dx = ln_1_.BackwardAdd(dh1, &dx1);

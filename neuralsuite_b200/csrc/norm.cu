@@ -290,10 +290,13 @@ __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ p
 // 128-column slab (lane = 4 consecutive columns, warp = rows strided by 8).
 // With LO, the same pass also writes lo = y - trunc_tf32(y) (the GEMM operand
 // split of y, compact), so the bias gradient of dY costs no extra read.
-template <bool LO>
-__global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ y, int M, int N,
+// With GELU, y is first replaced in place by y * gelu'(pre) (GeluBackward on
+// the way in: the column sums, the lo part and y itself are of the product).
+template <bool LO, bool GELU>
+__global__ void __launch_bounds__(256) colsum_partial(float* __restrict__ y, int M, int N,
                                                       int rows_per_cta, float* __restrict__ part,
-                                                      float* __restrict__ lo) {
+                                                      float* __restrict__ lo,
+                                                      const float* __restrict__ pre) {
   __shared__ float4 red[kRowsWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = (blockIdx.x * 32 + lane) * 4;
@@ -301,7 +304,15 @@ __global__ void __launch_bounds__(256) colsum_partial(const float* __restrict__ 
   const int r1 = min(M, r0 + rows_per_cta);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   const bool vec = (N & 3) == 0;
-  auto take = [&](int r, const float4 v) {
+  auto take = [&](int r, float4 v) {
+    if (GELU) {
+      const float4 x = *reinterpret_cast<const float4*>(pre + (size_t)r * N + col);
+      v.x = __fmul_rn(v.x, gelu_grad_f(x.x));
+      v.y = __fmul_rn(v.y, gelu_grad_f(x.y));
+      v.z = __fmul_rn(v.z, gelu_grad_f(x.z));
+      v.w = __fmul_rn(v.w, gelu_grad_f(x.w));
+      *reinterpret_cast<float4*>(y + (size_t)r * N + col) = v;
+    }
     s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
     if (LO) {
       float4 l;
@@ -479,7 +490,7 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, nullptr);
+  colsum_partial<false, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, nullptr, nullptr);
   { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
   colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
   return check_launch("ns_bias_grad stage 2");
@@ -496,10 +507,29 @@ ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo);
+  colsum_partial<true, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, dy_lo, nullptr);
   { ns_status _rc = check_launch("ns_bias_grad_split stage 1"); if (_rc != NS_OK) return _rc; }
   colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
   return check_launch("ns_bias_grad_split stage 2");
+}
+
+ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, float* db, float* dy_lo,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  NS_REQUIRE(M > 0 && N > 0 && (N & 3) == 0,
+             "ns_bias_grad_split_gelu: N must be a positive multiple of 4");
+  NS_REQUIRE(((reinterpret_cast<uintptr_t>(dY) | reinterpret_cast<uintptr_t>(dy_lo) |
+               reinterpret_cast<uintptr_t>(pre)) & 15) == 0,
+             "ns_bias_grad_split_gelu: dY, pre and dy_lo must be 16-byte aligned");
+  NS_REQUIRE(workspace && workspace_bytes >= ns_bias_grad_workspace_size(M, N),
+             "ns_bias_grad_split_gelu: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  const int chunks = bias_chunks(M, N);
+  const int rpc = ceil_div(M, chunks);
+  float* part = static_cast<float*>(workspace);
+  colsum_partial<true, true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo, pre);
+  { ns_status _rc = check_launch("ns_bias_grad_split_gelu stage 1"); if (_rc != NS_OK) return _rc; }
+  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
+  return check_launch("ns_bias_grad_split_gelu stage 2");
 }
 
 }  // extern "C"

@@ -139,6 +139,21 @@ def bias_grad_split(dY):
     return db, lo
 
 
+def bias_grad_split_gelu(dY, pre):
+    """dY * gelu'(pre) (in place), its column sums and its lo part (ns_bias_grad_split_gelu)."""
+    lib = _lib.load()
+    _req(dY, "dY")
+    _req(pre, "pre")
+    M, N = dY.shape
+    db = torch.empty(N, dtype=_f32, device=dY.device)
+    lo = torch.empty_like(dY)
+    nb = lib.ns_bias_grad_workspace_size(M, N)
+    ws = _ws(nb, dY.device)
+    _lib.check(lib.ns_bias_grad_split_gelu(_p(dY), _p(pre), M, N, _p(db), _p(lo), _p(ws), nb,
+                                           _stream()))
+    return dY, db, lo
+
+
 def layernorm_fwd(x, gamma, beta, eps=1e-5):
     """LayerNormForward (src/tensor.cpp:290-322)."""
     lib = _lib.load()

@@ -173,6 +173,17 @@ def test_bias_grad_split_matches_parts_bitwise(cuda):
     assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(dY)).view(np.uint32))
 
 
+def test_bias_grad_split_gelu_matches_parts_bitwise(cuda):
+    """ns_bias_grad_split_gelu = ns_gelu_bwd, then ns_bias_grad + ns_split_lo, bit for bit."""
+    dpost = dev(normal(rng(32), (4096, 3072)), cuda)
+    pre = dev(normal(rng(33), (4096, 3072), std=2.0), cuda)
+    want = nk.gelu_bwd(dpost, pre)
+    got, db, lo = nk.bias_grad_split_gelu(dpost.clone(), pre)
+    assert np.array_equal(host(got).view(np.uint32), host(want).view(np.uint32))
+    assert np.array_equal(host(db).view(np.uint32), host(nk.bias_grad(want)).view(np.uint32))
+    assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(want)).view(np.uint32))
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
