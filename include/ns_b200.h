@@ -117,6 +117,15 @@ NS_API ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_
                      float* C, int ldc, float beta, int epilogue, const float* bias,
                      const float* aux, float* aux_out, void* workspace, size_t workspace_bytes,
                      void* stream);
+/* ns_gemm_lo that also writes out_lo = the tf32 lo part (x - trunc_tf32(x))
+ * of the epilogue's activation output (aux_out for NS_EPI_BIAS_GELU, C
+ * otherwise; row stride ldc, not aliasing C): the next product's operand
+ * split in the same pass as the store.  No reference counterpart. */
+NS_API ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, int a_trans,
+                         const float* a_lo, const float* B, int ldb, int b_trans,
+                         const float* b_lo, float* C, int ldc, float beta, int epilogue,
+                         const float* bias, const float* aux, float* aux_out, float* out_lo,
+                         void* workspace, size_t workspace_bytes, void* stream);
 /* Selects the GEMM engine for subsequent calls on this thread: 0 = automatic
  * (tcgen05 wherever the operands allow TMA, SIMT fp32 otherwise), 1 = always
  * the SIMT fp32 kernel, 2 = tcgen05 with the operands' tf32 lo parts always
@@ -168,6 +177,16 @@ NS_API ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int
 NS_API size_t ns_attn_fwd_workspace_size(int B, int T, int H, int D);
 NS_API ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
                       void* workspace, size_t workspace_bytes, void* stream);
+/* ns_attn_fwd with the 3xTF32 operand splits shared with the neighbouring
+ * GEMMs: qkv_lo (optional) is the tf32 lo part of all of qkv (as written by
+ * ns_gemm_lo_out for the c_attn product), so no K/V split runs and no
+ * workspace is needed; out_lo (optional) receives the tf32 lo part of out
+ * (the c_proj product's A operand split).  16-byte aligned; workspace as
+ * ns_attn_fwd when qkv_lo is null.  No reference counterpart (a fusion of
+ * include/layers/attention.h:364-384 with the operand splits). */
+NS_API ns_status ns_attn_fwd_lo(const float* qkv, const float* qkv_lo, int B, int T, int H, int D,
+                         float* out, float* out_lo, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream);
 /* 0 (default): head_dim 32 / 64 run on the tensor cores (3xTF32, tcgen05) in
  * both directions, other sizes on the SIMT kernels; 1: SIMT kernels for every
  * size.  Per host thread.
@@ -177,6 +196,11 @@ NS_API size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D);
 NS_API ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, const float* lse,
                       int B, int T, int H, int D, float* dqkv, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* ns_attn_bwd with qkv's tf32 lo part given (qkv_lo, optional, 16-byte
+ * aligned; the forward's), so it is not split again.  Same workspace. */
+NS_API ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out,
+                         const float* dout, const float* lse, int B, int T, int H, int D,
+                         float* dqkv, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------ K3 bandwidth kernels */
 /* LayerNormForward, src/tensor.cpp:290-322 (last axis, biased variance). */

@@ -51,6 +51,8 @@ _SIGS = {
                         c_int, P, P, P, P, c_size_t, P]),
     "ns_gemm_lo": (c_int, [c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P, P, c_int,
                            c_float, c_int, P, P, P, P, c_size_t, P]),
+    "ns_gemm_lo_out": (c_int, [c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P, P,
+                               c_int, c_float, c_int, P, P, P, P, P, c_size_t, P]),
     "ns_split_lo": (c_int, [P, c_int, c_int, c_int, P, P]),
     "ns_gemm_set_engine": (c_int, [c_int]),
     "ns_kernel_health": (c_int, []),
@@ -60,9 +62,11 @@ _SIGS = {
     "ns_bias_grad_split_gelu": (c_int, [P, P, c_int, c_int, P, P, P, c_size_t, P]),
     "ns_attn_fwd_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ns_attn_fwd": (c_int, [P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
+    "ns_attn_fwd_lo": (c_int, [P, P, c_int, c_int, c_int, c_int, P, P, P, P, c_size_t, P]),
     "ns_attn_set_engine": (c_int, [c_int]),
     "ns_attn_bwd_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ns_attn_bwd": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int, P, P, c_size_t, P]),
+    "ns_attn_bwd_lo": (c_int, [P, P, P, P, P, c_int, c_int, c_int, c_int, P, P, c_size_t, P]),
     "ns_layernorm_fwd": (c_int, [P, P, P, P, P, P, c_int, c_int, c_float, P]),
     "ns_layernorm_bwd_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_layernorm_bwd": (c_int, [P, P, P, P, P, P, P, P, P, c_int, c_int, P, c_size_t, P]),

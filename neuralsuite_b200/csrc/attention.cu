@@ -448,20 +448,36 @@ ns_status ns_attn_set_engine(int engine) {
 
 ns_status ns_attn_fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse,
                       void* workspace, size_t workspace_bytes, void* stream) {
+  return ns_attn_fwd_lo(qkv, nullptr, B, T, H, D, out, nullptr, lse, workspace, workspace_bytes,
+                        stream);
+}
+
+ns_status ns_attn_fwd_lo(const float* qkv, const float* qkv_lo, int B, int T, int H, int D,
+                         float* out, float* out_lo, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   NS_REQUIRE(B >= 0 && T >= 0 && H > 0 && D > 0, "ns_attn_fwd: bad shape");
   NS_REQUIRE(D <= 128, "ns_attn_fwd: head_dim > 128 is not supported");
+  NS_REQUIRE(!qkv_lo || (reinterpret_cast<uintptr_t>(qkv_lo) & 15) == 0,
+             "ns_attn_fwd_lo: qkv_lo must be 16-byte aligned");
+  NS_REQUIRE(!out_lo || ((reinterpret_cast<uintptr_t>(out_lo) & 15) == 0 && out_lo != out),
+             "ns_attn_fwd_lo: out_lo must be 16-byte aligned and apart from out");
   if (B == 0 || T == 0) return NS_OK;
-  const size_t need = ns_attn_fwd_workspace_size(B, T, H, D);
+  // The K/V lo copy is needed only when the caller gives no qkv_lo.
+  const size_t need = qkv_lo ? 0 : ns_attn_fwd_workspace_size(B, T, H, D);
   NS_REQUIRE(workspace_bytes >= need && (need == 0 || workspace),
              "ns_attn_fwd: workspace too small");
   cudaStream_t s = as_stream(stream);
-  if (t_attn_engine == 0 && need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0 &&
+  const bool ws_ok = qkv_lo ? true : (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0);
+  if (t_attn_engine == 0 && (D == 32 || D == 64) && ws_ok &&
       attn_tc::fwd_supported(qkv, out, B, T, H, D))
-    return attn_tc::fwd(qkv, B, T, H, D, out, lse, static_cast<float*>(workspace), s);
-  if (D <= 16) return launch_fwd<16>(qkv, B, T, H, D, out, lse, s);
-  if (D <= 32) return launch_fwd<32>(qkv, B, T, H, D, out, lse, s);
-  if (D <= 64) return launch_fwd<64>(qkv, B, T, H, D, out, lse, s);
-  return launch_fwd<128>(qkv, B, T, H, D, out, lse, s);
+    return attn_tc::fwd(qkv, qkv_lo, B, T, H, D, out, out_lo, lse, static_cast<float*>(workspace), s);
+  ns_status rc;
+  if (D <= 16) rc = launch_fwd<16>(qkv, B, T, H, D, out, lse, s);
+  else if (D <= 32) rc = launch_fwd<32>(qkv, B, T, H, D, out, lse, s);
+  else if (D <= 64) rc = launch_fwd<64>(qkv, B, T, H, D, out, lse, s);
+  else rc = launch_fwd<128>(qkv, B, T, H, D, out, lse, s);
+  if (rc != NS_OK || !out_lo) return rc;
+  return ns_split_lo(out, B * T, H * D, H * D, out_lo, stream);
 }
 
 size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D) {
@@ -474,8 +490,17 @@ size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D) {
 ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, const float* lse,
                       int B, int T, int H, int D, float* dqkv, void* workspace,
                       size_t workspace_bytes, void* stream) {
+  return ns_attn_bwd_lo(qkv, nullptr, out, dout, lse, B, T, H, D, dqkv, workspace,
+                        workspace_bytes, stream);
+}
+
+ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out,
+                         const float* dout, const float* lse, int B, int T, int H, int D,
+                         float* dqkv, void* workspace, size_t workspace_bytes, void* stream) {
   NS_REQUIRE(B >= 0 && T >= 0 && H > 0 && D > 0, "ns_attn_bwd: bad shape");
   NS_REQUIRE(D <= 128, "ns_attn_bwd: head_dim > 128 is not supported");
+  NS_REQUIRE(!qkv_lo || (reinterpret_cast<uintptr_t>(qkv_lo) & 15) == 0,
+             "ns_attn_bwd_lo: qkv_lo must be 16-byte aligned");
   if (B == 0 || T == 0) return NS_OK;
   NS_REQUIRE(workspace && workspace_bytes >= ns_attn_bwd_workspace_size(B, T, H, D),
              "ns_attn_bwd: workspace too small");
@@ -488,7 +513,7 @@ ns_status ns_attn_bwd(const float* qkv, const float* out, const float* dout, con
   float* lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + delta_bytes);
   if (t_attn_engine == 0 && (D == 32 || D == 64) && (reinterpret_cast<uintptr_t>(lo) & 15) == 0 &&
       attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D))
-    return attn_tc::bwd(qkv, dout, lse, delta, B, T, H, D, dqkv, lo, s);
+    return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, s);
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 32) return launch_bwd<32>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 64) return launch_bwd<64>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

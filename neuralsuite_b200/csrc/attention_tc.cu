@@ -73,6 +73,8 @@ struct FwdParams {
   float scale_log2;  // scale * log2(e)
   int n_items;       // (128-query block, batch x head) pairs
   int nqb;           // query blocks per sequence
+  int klo0, vlo0;    // columns of K's and V's lo parts in the lo tensor (head 0)
+  float* out_lo;     // optional: tf32 lo part of out
 };
 
 // K tile (keys x D, K-major): 8-row groups 1024 B apart, 16-byte chunks;
@@ -217,9 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < D / 32; ++c) {
               const int x = h * D + 32 * c;
               tma_load_2d(dst + c * 8192, &tmK, kv_full(s), p.C + x, row);
-              tma_load_2d(dst + L::kTile + c * 8192, &tmKlo, kv_full(s), x, row);
+              tma_load_2d(dst + L::kTile + c * 8192, &tmKlo, kv_full(s), p.klo0 + x, row);
               tma_load_2d(dst + 2 * L::kTile + c * 8192, &tmV, kv_full(s), 2 * p.C + x, row);
-              tma_load_2d(dst + 3 * L::kTile + c * 8192, &tmVlo, kv_full(s), p.C + x, row);
+              tma_load_2d(dst + 3 * L::kTile + c * 8192, &tmVlo, kv_full(s), p.vlo0 + x, row);
             }
           }
         }
@@ -432,10 +434,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
         const int q = item_q0(w) + row;
         if (q < p.T) {
-          float* dst = p.out + ((size_t)b * p.T + q) * p.C + (size_t)h * D;
+          const size_t o = ((size_t)b * p.T + q) * p.C + (size_t)h * D;
+          float* dst = p.out + o;
 #pragma unroll
           for (int d = 0; d < D; d += 4)
             *reinterpret_cast<float4*>(dst + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
+          if (p.out_lo) {
+            float* dlo = p.out_lo + o;
+#pragma unroll
+            for (int d = 0; d < D; d += 4)
+              *reinterpret_cast<float4*>(dlo + d) = make_float4(tf32_lo(acc[d]), tf32_lo(acc[d + 1]),
+                                                                tf32_lo(acc[d + 2]), tf32_lo(acc[d + 3]));
+          }
           p.lse[(size_t)bh * p.T + q] = m_tot * p.scale + logf(l_tot);
         }
       }
@@ -599,29 +609,34 @@ __global__ void split_kv_lo_k(const float* __restrict__ qkv, int64_t rows, int C
   }
 }
 
+// qkv_lo: the caller's tf32 lo part of all of qkv ([B*T, 3C]), or null: then
+// K's and V's are split into `lo` ([B*T, 2C]) first.
 template <int D>
-ns_status launch_fwd(const float* qkv, int B, int T, int H, float* out, float* lse, float* lo,
-                     cudaStream_t s) {
+ns_status launch_fwd(const float* qkv, const float* qkv_lo, int B, int T, int H, float* out,
+                     float* out_lo, float* lse, float* lo, cudaStream_t s) {
   using L = FwdLayout<D>;
   const int C = H * D, rows = B * T;
-  {
+  if (!qkv_lo) {
     const int64_t work = (int64_t)rows * (2 * C / 4);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
     split_kv_lo_k<<<grid, 256, 0, s>>>(qkv, rows, C, lo);
     ns_status rc = check_launch("ns_attn_fwd kv split");
     if (rc != NS_OK) return rc;
   }
+  const float* lo_t = qkv_lo ? qkv_lo : lo;
+  const int lo_w = qkv_lo ? 3 * C : 2 * C;
   CUtensorMap tq, tk, tklo, tv, tvlo;
   ns_status rc = make_map(&tq, qkv, 3 * C, rows, 3 * C, kBQ, false);
   if (rc == NS_OK) rc = make_map(&tk, qkv, 3 * C, rows, 3 * C, kBKV, false);
-  if (rc == NS_OK) rc = make_map(&tklo, lo, 2 * C, rows, 2 * C, kBKV, false);
+  if (rc == NS_OK) rc = make_map(&tklo, lo_t, lo_w, rows, lo_w, kBKV, false);
   if (rc == NS_OK) rc = make_map(&tv, qkv, 3 * C, rows, 3 * C, kBKV, true);
-  if (rc == NS_OK) rc = make_map(&tvlo, lo, 2 * C, rows, 2 * C, kBKV, true);
+  if (rc == NS_OK) rc = make_map(&tvlo, lo_t, lo_w, rows, lo_w, kBKV, true);
   if (rc != NS_OK) return rc;
   const float scale = 1.0f / sqrtf((float)D);
   const int nqb = (T + kBQ - 1) / kBQ;
   const int n_items = nqb * B * H;
-  FwdParams p{qkv, out, lse, T, H, C, scale, scale * 1.4426950408889634f, n_items, nqb};
+  FwdParams p{qkv, out, lse, T, H, C, scale, scale * 1.4426950408889634f, n_items, nqb,
+              qkv_lo ? C : 0, qkv_lo ? 2 * C : C, out_lo};
   NS_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<D>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
               "ns_attn_fwd attr");
@@ -1267,11 +1282,13 @@ ns_status launch_bwd_mode(const CUtensorMap* maps, const BwdParams& p, int B, in
 }
 
 template <int D>
-ns_status launch_bwd(const float* qkv, const float* dout, const float* lse, const float* delta,
-                     int B, int T, int H, float* dqkv, float* qkv_lo, float* dout_lo,
-                     cudaStream_t s) {
+ns_status launch_bwd(const float* qkv, const float* qkv_lo_in, const float* dout, const float* lse,
+                     const float* delta, int B, int T, int H, float* dqkv, float* qkv_lo_ws,
+                     float* dout_lo, cudaStream_t s) {
   const int C = H * D, rows = B * T;
-  ns_status rc = split_rows(qkv, rows, 3 * C, qkv_lo, s);
+  ns_status rc = NS_OK;
+  if (!qkv_lo_in) rc = split_rows(qkv, rows, 3 * C, qkv_lo_ws, s);
+  const float* qkv_lo = qkv_lo_in ? qkv_lo_in : qkv_lo_ws;
   if (rc == NS_OK) rc = split_rows(dout, rows, C, dout_lo, s);
   if (rc != NS_OK) return rc;
   // qkv and dout (and their lo copies), each as a K-major and an MN-major map.
@@ -1323,10 +1340,10 @@ size_t fwd_workspace_bytes(int B, int T, int H, int D) {
   return (size_t)B * T * 2 * H * D * sizeof(float);
 }
 
-ns_status fwd(const float* qkv, int B, int T, int H, int D, float* out, float* lse, float* lo,
-              cudaStream_t s) {
-  return D == 64 ? launch_fwd<64>(qkv, B, T, H, out, lse, lo, s)
-                 : launch_fwd<32>(qkv, B, T, H, out, lse, lo, s);
+ns_status fwd(const float* qkv, const float* qkv_lo, int B, int T, int H, int D, float* out,
+              float* out_lo, float* lse, float* lo, cudaStream_t s) {
+  return D == 64 ? launch_fwd<64>(qkv, qkv_lo, B, T, H, out, out_lo, lse, lo, s)
+                 : launch_fwd<32>(qkv, qkv_lo, B, T, H, out, out_lo, lse, lo, s);
 }
 
 bool bwd_supported(const float* qkv, const float* dout, const float* dqkv, int B, int T, int H,
@@ -1339,12 +1356,13 @@ size_t bwd_lo_bytes(int B, int T, int H, int D) {
   return (size_t)B * T * 4 * H * D * sizeof(float);
 }
 
-ns_status bwd(const float* qkv, const float* dout, const float* lse, const float* delta, int B,
-              int T, int H, int D, float* dqkv, float* lo, cudaStream_t s) {
-  float* qkv_lo = lo;
+ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const float* lse,
+              const float* delta, int B, int T, int H, int D, float* dqkv, float* lo,
+              cudaStream_t s) {
+  float* qkv_lo_ws = lo;
   float* dout_lo = lo + (size_t)B * T * 3 * H * D;
-  return D == 64 ? launch_bwd<64>(qkv, dout, lse, delta, B, T, H, dqkv, qkv_lo, dout_lo, s)
-                 : launch_bwd<32>(qkv, dout, lse, delta, B, T, H, dqkv, qkv_lo, dout_lo, s);
+  return D == 64 ? launch_bwd<64>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo, s)
+                 : launch_bwd<32>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo, s);
 }
 
 int consume_timeout_flag() {

@@ -126,7 +126,8 @@ namespace {
 ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, const float* B,
                     int ldb, int b_trans, float* C, int ldc, float beta, int epilogue,
                     const float* bias, const float* aux, float* aux_out, const float* a_lo_in,
-                    const float* b_lo_in, void* workspace, size_t workspace_bytes, void* stream) {
+                    const float* b_lo_in, float* out_lo, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   NS_REQUIRE(M >= 0 && N >= 0 && K >= 0, "ns_gemm: negative dimension");
   NS_REQUIRE(epilogue >= NS_EPI_STORE && epilogue <= NS_EPI_GELU_BWD, "ns_gemm: unknown epilogue");
   NS_REQUIRE(beta == 0.0f || beta == 1.0f, "ns_gemm: beta must be 0 or 1");
@@ -144,8 +145,9 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
              "ns_gemm_lo: a_lo needs 16-byte aligned rows (stored columns a multiple of 4)");
   NS_REQUIRE(!b_lo_in || (b_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(b_lo_in) & 15) == 0),
              "ns_gemm_lo: b_lo needs 16-byte aligned rows (stored columns a multiple of 4)");
+  NS_REQUIRE(!out_lo || out_lo != C, "ns_gemm_lo_out: out_lo must not alias C");
   if (M == 0 || N == 0) return NS_OK;
-  EpiArgs e{C, ldc, epilogue, beta, bias, aux, aux_out};
+  EpiArgs e{C, ldc, epilogue, beta, bias, aux, aux_out, out_lo};
   cudaStream_t s = as_stream(stream);
   if (K == 0 || !use_tc(M, N, K, A, lda, B, ldb))
     return gemm_simt(M, N, K, A, lda, a_trans, B, ldb, b_trans, e, s);
@@ -206,7 +208,7 @@ ns_status ns_gemm(int M, int N, int K, const float* A, int lda, int a_trans, con
                   const float* bias, const float* aux, float* aux_out, void* workspace,
                   size_t workspace_bytes, void* stream) {
   return gemm_impl(M, N, K, A, lda, a_trans, B, ldb, b_trans, C, ldc, beta, epilogue, bias, aux,
-                   aux_out, nullptr, nullptr, workspace, workspace_bytes, stream);
+                   aux_out, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_trans, const float* a_lo,
@@ -214,7 +216,16 @@ ns_status ns_gemm_lo(int M, int N, int K, const float* A, int lda, int a_trans, 
                      float beta, int epilogue, const float* bias, const float* aux,
                      float* aux_out, void* workspace, size_t workspace_bytes, void* stream) {
   return gemm_impl(M, N, K, A, lda, a_trans, B, ldb, b_trans, C, ldc, beta, epilogue, bias, aux,
-                   aux_out, a_lo, b_lo, workspace, workspace_bytes, stream);
+                   aux_out, a_lo, b_lo, nullptr, workspace, workspace_bytes, stream);
+}
+
+ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, int a_trans, const float* a_lo,
+                         const float* B, int ldb, int b_trans, const float* b_lo, float* C, int ldc,
+                         float beta, int epilogue, const float* bias, const float* aux,
+                         float* aux_out, float* out_lo, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return gemm_impl(M, N, K, A, lda, a_trans, B, ldb, b_trans, C, ldc, beta, epilogue, bias, aux,
+                   aux_out, a_lo, b_lo, out_lo, workspace, workspace_bytes, stream);
 }
 
 ns_status ns_split_lo(const float* x, int rows, int cols, int ld, float* lo, void* stream) {

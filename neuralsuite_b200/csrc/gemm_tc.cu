@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         if (n_out < p.out_n && rows > 0) {
           // Epilogue arguments in registers (not re-read from parameter space per element).
           const EpiArgs e = p.e;
-          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f)) {
+          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f && !e.lo_out)) {
             float* dst = p.splits > 1 ? p.ws + ((size_t)split * p.out_m + m0_out) * p.out_n + n_out
                                       : e.C + (size_t)m0_out * e.ldc + n_out;
             const size_t ld = p.splits > 1 ? (size_t)p.out_n : (size_t)e.ldc;
@@ -1158,7 +1158,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         if (n_out < p.out_n && rows > 0) {
           // Epilogue arguments in registers (not re-read from parameter space per element).
           const EpiArgs e = p.e;
-          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f)) {
+          if (p.splits > 1 || (e.epi == NS_EPI_STORE && e.beta == 0.0f && !e.lo_out)) {
             float* dst = p.splits > 1 ? p.ws + ((size_t)split * p.out_m + m0_out) * p.out_n + n_out
                                       : e.C + (size_t)m0_out * e.ldc + n_out;
             const size_t ld = p.splits > 1 ? (size_t)p.out_n : (size_t)e.ldc;
@@ -1390,9 +1390,11 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   kp.kb_total = pl.kb_total; kp.kb_per = pl.kb_per;
   kp.a_mn = a_mn; kp.b_mn = b_mn;
   kp.e = e;
+  if (pl.splits > 1) kp.e.lo_out = nullptr;  // the split-K reduce writes it
   kp.ws = ws;
   const uintptr_t al = reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
                        reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
+                       reinterpret_cast<uintptr_t>(e.lo_out) |
                        reinterpret_cast<uintptr_t>(ws);
   kp.vec_ok = ((al & 15) == 0 && (e.ldc % 4) == 0 && (N % 4) == 0) ? 1 : 0;
   kp.trans_out = pl.trans;
@@ -1405,6 +1407,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   if (late_epi) {
     kp.e.epi = NS_EPI_STORE;
     kp.e.beta = 0.0f;
+    kp.e.lo_out = nullptr;  // the pass below writes it from the final values
   }
   if ((pl.pair || pl.bn == kWideBN) && !pre)
     return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: wide tiles need pre-split operands");
@@ -1416,8 +1419,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   if (late_epi) {
     const int64_t total = (int64_t)out_m * out_n;
     const int vec = ((reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
-                      reinterpret_cast<uintptr_t>(e.bias)) & 15) == 0 && (e.ldc % 4) == 0 &&
-                    (out_n % 4) == 0;
+                      reinterpret_cast<uintptr_t>(e.bias) | reinterpret_cast<uintptr_t>(e.lo_out)) &
+                     15) == 0 && (e.ldc % 4) == 0 && (out_n % 4) == 0;
     const int64_t work = vec ? total / 4 : total;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
     epi_apply_k<<<grid, 256, 0, stream>>>(out_m, out_n, e, vec);
@@ -1427,6 +1430,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   const int64_t total = (int64_t)out_m * out_n;
   const int vec = ((reinterpret_cast<uintptr_t>(e.C) | reinterpret_cast<uintptr_t>(e.aux) |
                     reinterpret_cast<uintptr_t>(e.aux_out) | reinterpret_cast<uintptr_t>(e.bias) |
+                       reinterpret_cast<uintptr_t>(e.lo_out) |
                     reinterpret_cast<uintptr_t>(ws)) & 15) == 0 && (e.ldc % 4) == 0 && (out_n % 4) == 0;
   const int64_t work = vec ? total / 4 : total;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));

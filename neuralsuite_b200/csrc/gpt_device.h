@@ -207,17 +207,24 @@ class Linear : public Layer {
     Register(&bias_, "bias");
   }
   Tensor Forward(const Tensor& x) override { return Run(x, NS_EPI_BIAS, nullptr, nullptr); }
-  // Y = X W + b, and post = gelu(Y) (GeluForward fused into the epilogue).
-  Tensor ForwardGelu(const Tensor& x, Tensor* post) {
+  // Forward with the 3xTF32 operand splits shared with the neighbours: x_lo
+  // (or null) is X's tf32 lo part, made by X's producer (it must stay intact
+  // until Backward); y_lo (or null) receives Y's, written by the epilogue.
+  Tensor ForwardLo(const Tensor& x, const float* x_lo, float* y_lo) {
+    return Run(x, NS_EPI_BIAS, nullptr, nullptr, x_lo, y_lo);
+  }
+  // Y = X W + b, and post = gelu(Y) (GeluForward fused into the epilogue);
+  // post_lo (or null) receives post's tf32 lo part.
+  Tensor ForwardGelu(const Tensor& x, Tensor* post, float* post_lo = nullptr) {
     const int n = Rows(x, in_);
     Tensor g = Scratch(post_, n, out_);
-    Tensor y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data());
+    Tensor y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data(), nullptr, post_lo);
     *post = g;
     return y;
   }
   // Y = resid + (X W + b)  (the GPTBlock residual ElementwiseAdd fused).
-  Tensor ForwardResidual(const Tensor& x, const Tensor& resid) {
-    return Run(x, NS_EPI_BIAS_RESID, resid.Data(), nullptr);
+  Tensor ForwardResidual(const Tensor& x, const Tensor& resid, const float* x_lo = nullptr) {
+    return Run(x, NS_EPI_BIAS_RESID, resid.Data(), nullptr, x_lo);
   }
   Tensor Backward(const Tensor& dy) override { return BackwardImpl(dy, nullptr); }
   // GeluBackward then Linear::Backward: `dpost` is the gradient at gelu(Y)
@@ -238,7 +245,8 @@ class Linear : public Layer {
   // and the copy passed to every product that reads it (ns_gemm_lo).
   bool SplitOk() const { return in_ % 4 == 0 && out_ % 4 == 0; }
 
-  Tensor Run(const Tensor& x, int epi, const float* aux, float* aux_out) {
+  Tensor Run(const Tensor& x, int epi, const float* aux, float* aux_out,
+             const float* x_lo_in = nullptr, float* out_lo = nullptr) {
     if (x.Shape().empty() || x.Shape().back() != in_)
       throw std::invalid_argument("Linear: the last axis of the input is not in_features");
     const int n = Rows(x, in_);
@@ -246,16 +254,22 @@ class Linear : public Layer {
     const float* x_lo = nullptr;
     const float* w_lo = nullptr;
     if (SplitOk()) {
-      Tensor xl = Scratch(x_lo_buf_, n, in_), wl = Scratch(w_lo_buf_, in_, out_);
-      Check(ns_split_lo(x.Data(), n, in_, in_, xl.Data(), stream()));
+      Tensor wl = Scratch(w_lo_buf_, in_, out_);
       Check(ns_split_lo(weight_.Value().Data(), in_, out_, out_, wl.Data(), stream()));
-      x_lo = xl.Data();
       w_lo = wl.Data();
+      if (x_lo_in) {
+        x_lo = x_lo_in;
+      } else {
+        Tensor xl = Scratch(x_lo_buf_, n, in_);
+        Check(ns_split_lo(x.Data(), n, in_, in_, xl.Data(), stream()));
+        x_lo = xl.Data();
+      }
     }
+    last_x_lo_ = x_lo;
     Tensor y = Scratch(out_buf_, n, out_);
-    Check(ns_gemm_lo(n, out_, in_, x.Data(), in_, 0, x_lo, weight_.Value().Data(), out_, 0, w_lo,
-                     y.Data(), out_, 0.0f, epi, bias_.Value().Data(), aux, aux_out, ctx_->scratch,
-                     ctx_->scratch_bytes, stream()));
+    Check(ns_gemm_lo_out(n, out_, in_, x.Data(), in_, 0, x_lo, weight_.Value().Data(), out_, 0,
+                         w_lo, y.Data(), out_, 0.0f, epi, bias_.Value().Data(), aux, aux_out,
+                         out_lo, ctx_->scratch, ctx_->scratch_bytes, stream()));
     std::vector<int> shape = x.Shape();
     shape.back() = out_;
     return y.View(shape);
@@ -264,9 +278,9 @@ class Linear : public Layer {
     const int n = Rows(last_input_, in_);
     if (Rows(dy, out_) != n) throw std::invalid_argument("Linear::Backward: batch mismatch");
     Tensor dx = Scratch(dx_buf_, n, in_);
-    // The lo copies of X and W made by the forward pass are still current.
+    // The lo copies of X and W made (or taken) by the forward pass are still current.
     const bool lo = SplitOk();
-    const float* x_lo = lo ? x_lo_buf_.Data() : nullptr;
+    const float* x_lo = lo ? last_x_lo_ : nullptr;
     const float* w_lo = lo ? w_lo_buf_.Data() : nullptr;
     const float* dy_lo = nullptr;
     if (lo) {
@@ -302,6 +316,7 @@ class Linear : public Layer {
   Tensor last_input_;
   Tensor out_buf_, post_, dx_buf_;
   Tensor x_lo_buf_, w_lo_buf_, dy_lo_buf_;  // tf32 lo parts of X, W and dY
+  const float* last_x_lo_ = nullptr;        // X's lo part used by the last Forward
 };
 
 // include/layers/layernorm.h:22-59 (eps 1e-5, gamma = 1, beta = 0).
@@ -380,8 +395,8 @@ class MultiHeadAttention : public Layer {
     const int B = batch_, T = seq_, M = B * T;
     Tensor datt = c_proj_.Backward(dy);
     Tensor dqkv = Scratch(dqkv_buf_, M, 3 * n_embd_);
-    Check(ns_attn_bwd(qkv_.Data(), att_.Data(), datt.Data(), lse_.Data(), B, T, n_head_, head_dim_,
-                      dqkv.Data(), ctx_->scratch, ctx_->scratch_bytes, stream()));
+    Check(ns_attn_bwd_lo(qkv_.Data(), qkv_lo_, att_.Data(), datt.Data(), lse_.Data(), B, T, n_head_,
+                         head_dim_, dqkv.Data(), ctx_->scratch, ctx_->scratch_bytes, stream()));
     Tensor dx = c_attn_.Backward(dqkv);
     return dx.View({B, T, n_embd_});
   }
@@ -395,13 +410,19 @@ class MultiHeadAttention : public Layer {
     batch_ = x.Shape()[0];
     seq_ = x.Shape()[1];
     const int M = batch_ * seq_;
-    qkv_ = c_attn_.Forward(x.View({M, n_embd_}));
+    // qkv's lo part comes out of the c_attn epilogue (the attention kernels'
+    // K/V/Q operand split) and the attention output's out of the attention
+    // epilogue (c_proj's X split), when rows stay 16-byte aligned.
+    const bool lo = n_embd_ % 4 == 0;
+    qkv_lo_ = lo ? Scratch(qkv_lo_buf_, M, 3 * n_embd_).Data() : nullptr;
+    float* att_lo = lo ? Scratch(att_lo_buf_, M, n_embd_).Data() : nullptr;
+    qkv_ = c_attn_.ForwardLo(x.View({M, n_embd_}), nullptr, qkv_lo_);
     att_ = Scratch(att_buf_, M, n_embd_);
     lse_ = Scratch(lse_buf_, batch_ * n_head_, seq_);
-    Check(ns_attn_fwd(qkv_.Data(), batch_, seq_, n_head_, head_dim_, att_.Data(), lse_.Data(),
-                      ctx_->scratch, ctx_->scratch_bytes, stream()));
-    Tensor y = resid ? c_proj_.ForwardResidual(att_, resid->View({M, n_embd_}))
-                     : c_proj_.Forward(att_);
+    Check(ns_attn_fwd_lo(qkv_.Data(), qkv_lo_, batch_, seq_, n_head_, head_dim_, att_.Data(), att_lo,
+                         lse_.Data(), ctx_->scratch, ctx_->scratch_bytes, stream()));
+    Tensor y = resid ? c_proj_.ForwardResidual(att_, resid->View({M, n_embd_}), att_lo)
+                     : c_proj_.ForwardLo(att_, att_lo, nullptr);
     return y.View({batch_, seq_, n_embd_});
   }
 
@@ -409,7 +430,8 @@ class MultiHeadAttention : public Layer {
   Linear c_attn_, c_proj_;
   int batch_ = 0, seq_ = 0;
   Tensor qkv_, att_, lse_;
-  Tensor att_buf_, lse_buf_, dqkv_buf_;
+  Tensor att_buf_, lse_buf_, dqkv_buf_, qkv_lo_buf_, att_lo_buf_;
+  float* qkv_lo_ = nullptr;
 };
 
 // include/layers/embedding.h:24-92, the table only; GPTModel drives the
@@ -452,8 +474,11 @@ class GPTBlock : public Layer {
     Tensor h1 = ln_1_.Forward(x);
     x1_ = attn_.ForwardResidual(h1, x);
     Tensor h2 = ln_2_.Forward(x1_);
-    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({Rows(h2, h2.Shape().back()), h2.Shape().back()}), &gelu_);
-    Tensor x2 = mlp_proj_.ForwardResidual(gelu_, x1_.View({Rows(x1_, x1_.Shape().back()), x1_.Shape().back()}));
+    const int C = h2.Shape().back(), M = Rows(h2, C);
+    // gelu's lo part comes out of the mlp_fc epilogue (mlp_proj's X split).
+    float* gelu_lo = mlp_fc_.Out() % 4 == 0 ? Scratch(gelu_lo_buf_, M, mlp_fc_.Out()).Data() : nullptr;
+    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({M, C}), &gelu_, gelu_lo);
+    Tensor x2 = mlp_proj_.ForwardResidual(gelu_, x1_.View({M, C}), gelu_lo);
     return x2.View(x.Shape());
   }
   // GPTBlock::Backward (gpt.h:82-100) with the GELU backward fused into the
@@ -476,7 +501,7 @@ class GPTBlock : public Layer {
   LayerNormLayer ln_2_;
   Linear mlp_fc_;
   Linear mlp_proj_;
-  Tensor x1_, fc_pre_, gelu_;
+  Tensor x1_, fc_pre_, gelu_, gelu_lo_buf_;
 };
 
 // Sizes of GPTModel's parameters in registration order (include/gpt.h:143-149,

@@ -53,11 +53,12 @@ def split_lo(x):
 
 
 def gemm(A, B, a_trans=False, b_trans=False, epilogue=_lib.EPI_STORE, bias=None, aux=None,
-         out=None, aux_out=None, beta=0.0, split=True, a_lo=None, b_lo=None):
+         out=None, aux_out=None, beta=0.0, split=True, a_lo=None, b_lo=None, out_lo=None):
     """MatMul (src/tensor.cpp:198-271) with transposed operands read in place.
 
     ``A`` is [M,K] (or [K,M] if a_trans), ``B`` is [K,N] (or [N,K] if b_trans).
     ``a_lo`` / ``b_lo``: lo parts from split_lo of the same tensors (ns_gemm_lo).
+    ``out_lo``: receives the tf32 lo part of the activation output (ns_gemm_lo_out).
     """
     lib = _lib.load()
     _req(A, "A")
@@ -72,7 +73,12 @@ def gemm(A, B, a_trans=False, b_trans=False, epilogue=_lib.EPI_STORE, bias=None,
         aux_out = torch.empty((M, N), dtype=_f32, device=A.device)
     ws_bytes = lib.ns_gemm_workspace_size(M, N, K) if split else 0
     ws = _ws(ws_bytes, A.device) if ws_bytes else None
-    if a_lo is None and b_lo is None:
+    if out_lo is not None:
+        _lib.check(lib.ns_gemm_lo_out(M, N, K, _p(A), A.shape[1], int(a_trans), _p(a_lo), _p(B),
+                                      B.shape[1], int(b_trans), _p(b_lo), _p(out), out.shape[1],
+                                      float(beta), epilogue, _p(bias), _p(aux), _p(aux_out),
+                                      _p(out_lo), _p(ws), ws_bytes, _stream()))
+    elif a_lo is None and b_lo is None:
         _lib.check(lib.ns_gemm(M, N, K, _p(A), A.shape[1], int(a_trans), _p(B), B.shape[1],
                                int(b_trans), _p(out), out.shape[1], float(beta), epilogue,
                                _p(bias), _p(aux), _p(aux_out), _p(ws), ws_bytes, _stream()))
@@ -106,6 +112,31 @@ def attn_fwd(qkv, B, T, H, D):
     ws = _ws(nb, qkv.device)
     _lib.check(lib.ns_attn_fwd(_p(qkv), B, T, H, D, _p(out), _p(lse), _p(ws), nb, _stream()))
     return out, lse
+
+
+def attn_fwd_lo(qkv, qkv_lo, B, T, H, D):
+    """(out, out_lo, lse) with qkv's lo part given (ns_attn_fwd_lo)."""
+    lib = _lib.load()
+    _req(qkv, "qkv")
+    out = torch.empty((B * T, H * D), dtype=_f32, device=qkv.device)
+    out_lo = torch.empty_like(out)
+    lse = torch.empty((B * H * T,), dtype=_f32, device=qkv.device)
+    nb = 0 if qkv_lo is not None else lib.ns_attn_fwd_workspace_size(B, T, H, D)
+    ws = _ws(nb, qkv.device) if nb else None
+    _lib.check(lib.ns_attn_fwd_lo(_p(qkv), _p(qkv_lo), B, T, H, D, _p(out), _p(out_lo), _p(lse),
+                                  _p(ws), nb, _stream()))
+    return out, out_lo, lse
+
+
+def attn_bwd_lo(qkv, qkv_lo, out, dout, lse, B, T, H, D):
+    """ns_attn_bwd with qkv's lo part given (ns_attn_bwd_lo)."""
+    lib = _lib.load()
+    dqkv = torch.empty_like(qkv)
+    nb = lib.ns_attn_bwd_workspace_size(B, T, H, D)
+    ws = _ws(nb, qkv.device)
+    _lib.check(lib.ns_attn_bwd_lo(_p(qkv), _p(qkv_lo), _p(out), _p(dout), _p(lse), B, T, H, D,
+                                  _p(dqkv), _p(ws), nb, _stream()))
+    return dqkv
 
 
 def attn_set_engine(engine):

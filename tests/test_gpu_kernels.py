@@ -184,6 +184,52 @@ def test_bias_grad_split_gelu_matches_parts_bitwise(cuda):
     assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(want)).view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K", [(8192, 2304, 768), (8192, 3072, 768), (768, 768, 8192),
+                                   (300, 200, 100), (256, 264, 2048)])
+@pytest.mark.parametrize("epi", [_lib.EPI_STORE, _lib.EPI_BIAS, _lib.EPI_BIAS_GELU,
+                                 _lib.EPI_BIAS_RESID, _lib.EPI_GELU_BWD])
+def test_gemm_out_lo_is_split_of_output(cuda, M, N, K, epi):
+    """ns_gemm_lo_out: same C (and aux_out) as ns_gemm_lo, plus out_lo = split of the activation."""
+    r = rng(M + N + K + epi)
+    A = dev(normal(r, (M, K)), cuda)
+    B = dev(normal(r, (K, N)), cuda)
+    bias = dev(normal(r, (N,)), cuda)
+    aux = dev(normal(r, (M, N)), cuda) if epi in (_lib.EPI_BIAS_RESID, _lib.EPI_GELU_BWD) else None
+    a_lo, b_lo = nk.split_lo(A), nk.split_lo(B)
+    kw = dict(epilogue=epi, bias=bias if epi in (_lib.EPI_BIAS, _lib.EPI_BIAS_GELU, _lib.EPI_BIAS_RESID) else None,
+              aux=aux, a_lo=a_lo, b_lo=b_lo)
+    want = nk.gemm(A, B, **kw)
+    lo = torch.empty((M, N), device=cuda)
+    got = nk.gemm(A, B, out_lo=lo, **kw)
+    if epi == _lib.EPI_BIAS_GELU:
+        (wc, wg), (gc, gg) = want, got
+        assert np.array_equal(host(gc).view(np.uint32), host(wc).view(np.uint32))
+        assert np.array_equal(host(gg).view(np.uint32), host(wg).view(np.uint32))
+        act = wg
+    else:
+        assert np.array_equal(host(got).view(np.uint32), host(want).view(np.uint32))
+        act = want
+    assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(act)).view(np.uint32))
+
+
+@pytest.mark.parametrize("B,T,H,D", [(2, 1024, 4, 64), (2, 300, 3, 64), (3, 200, 2, 32)])
+def test_attn_with_given_lo_parts_bitwise(cuda, B, T, H, D):
+    """ns_attn_fwd_lo / ns_attn_bwd_lo with qkv's lo part given equal the plain entries."""
+    r = rng(B * T + H * D)
+    C = H * D
+    qkv = dev(normal(r, (B * T, 3 * C)), cuda)
+    dout = dev(normal(r, (B * T, C)), cuda)
+    qkv_lo = nk.split_lo(qkv)
+    out, lse = nk.attn_fwd(qkv, B, T, H, D)
+    out2, out_lo, lse2 = nk.attn_fwd_lo(qkv, qkv_lo, B, T, H, D)
+    assert np.array_equal(host(out2).view(np.uint32), host(out).view(np.uint32))
+    assert np.array_equal(host(lse2).view(np.uint32), host(lse).view(np.uint32))
+    assert np.array_equal(host(out_lo).view(np.uint32), host(nk.split_lo(out)).view(np.uint32))
+    want = nk.attn_bwd(qkv, out, dout, lse, B, T, H, D)
+    got = nk.attn_bwd_lo(qkv, qkv_lo, out, dout, lse, B, T, H, D)
+    assert np.array_equal(host(got).view(np.uint32), host(want).view(np.uint32))
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
