@@ -217,6 +217,11 @@ NS_API ns_status ns_layernorm_bwd(const float* dout, const float* x, const float
                            size_t workspace_bytes, void* stream);
 /* GeluForward / GeluBackward, src/tensor.cpp:428-461. */
 NS_API ns_status ns_gelu_fwd(const float* x, float* y, int64_t n, void* stream);
+/* ns_gelu_fwd that also writes y_lo = y - trunc_tf32(y), the next product's
+ * operand split (a pass that streams at memory speed, where the same work in
+ * a GEMM epilogue holds up the GEMM).  16-byte aligned.  No reference
+ * counterpart (GeluForward src/tensor.cpp:428-443 plus the split). */
+NS_API ns_status ns_gelu_fwd_lo(const float* x, float* y, float* y_lo, int64_t n, void* stream);
 NS_API ns_status ns_gelu_bwd(const float* dout, const float* x, float* dx, int64_t n, void* stream);
 /* ElementwiseAdd, src/tensor.cpp:534-540. */
 NS_API ns_status ns_add(const float* a, const float* b, float* out, int64_t n, void* stream);

@@ -71,6 +71,7 @@ _SIGS = {
     "ns_layernorm_bwd_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_layernorm_bwd": (c_int, [P, P, P, P, P, P, P, P, P, c_int, c_int, P, c_size_t, P]),
     "ns_gelu_fwd": (c_int, [P, P, c_int64, P]),
+    "ns_gelu_fwd_lo": (c_int, [P, P, P, c_int64, P]),
     "ns_gelu_bwd": (c_int, [P, P, P, c_int64, P]),
     "ns_add": (c_int, [P, P, P, c_int64, P]),
     "ns_cross_entropy_workspace_size": (c_size_t, [c_int, c_int]),

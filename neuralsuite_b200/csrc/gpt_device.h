@@ -213,12 +213,20 @@ class Linear : public Layer {
   Tensor ForwardLo(const Tensor& x, const float* x_lo, float* y_lo) {
     return Run(x, NS_EPI_BIAS, nullptr, nullptr, x_lo, y_lo);
   }
-  // Y = X W + b, and post = gelu(Y) (GeluForward fused into the epilogue);
-  // post_lo (or null) receives post's tf32 lo part.
+  // Y = X W + b, and post = gelu(Y); post_lo (or null) receives post's tf32
+  // lo part.  With post_lo the GELU runs as one streaming pass after the
+  // GEMM (cheaper than GELU and two more stores in the GEMM epilogue, which
+  // hold up its tensor core); without, it is fused into the epilogue.
   Tensor ForwardGelu(const Tensor& x, Tensor* post, float* post_lo = nullptr) {
     const int n = Rows(x, in_);
     Tensor g = Scratch(post_, n, out_);
-    Tensor y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data(), nullptr, post_lo);
+    Tensor y;
+    if (post_lo) {
+      y = Run(x, NS_EPI_BIAS, nullptr, nullptr);
+      Check(ns_gelu_fwd_lo(y.Data(), g.Data(), post_lo, static_cast<int64_t>(n) * out_, stream()));
+    } else {
+      y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data());
+    }
     *post = g;
     return y;
   }

@@ -26,6 +26,25 @@ __global__ void gelu_fwd_k(const float* __restrict__ x, float* __restrict__ y, i
     y[i] = gelu_f(x[i]);
 }
 
+// y = gelu(x) and y_lo = y - trunc_tf32(y) (the next GEMM's operand split).
+__global__ void gelu_fwd_lo_k(const float* __restrict__ x, float* __restrict__ y,
+                              float* __restrict__ y_lo, int64_t n) {
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  auto lo = [](float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); };
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 v = reinterpret_cast<const float4*>(x)[i];
+    v.x = gelu_f(v.x); v.y = gelu_f(v.y); v.z = gelu_f(v.z); v.w = gelu_f(v.w);
+    reinterpret_cast<float4*>(y)[i] = v;
+    reinterpret_cast<float4*>(y_lo)[i] = make_float4(lo(v.x), lo(v.y), lo(v.z), lo(v.w));
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float v = gelu_f(x[i]);
+    y[i] = v;
+    y_lo[i] = lo(v);
+  }
+}
+
 __global__ void gelu_bwd_k(const float* __restrict__ d, const float* __restrict__ x,
                            float* __restrict__ dx, int64_t n) {
   const int64_t n4 = n >> 2;
@@ -167,6 +186,14 @@ ns_status ns_gelu_fwd(const float* x, float* y, int64_t n, void* stream) {
   if (n == 0) return NS_OK;
   gelu_fwd_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, y, n);
   return check_launch("ns_gelu_fwd");
+}
+
+ns_status ns_gelu_fwd_lo(const float* x, float* y, float* y_lo, int64_t n, void* stream) {
+  NS_REQUIRE(n >= 0, "ns_gelu_fwd_lo: n < 0");
+  NS_REQUIRE(al16(x) && al16(y) && al16(y_lo), "ns_gelu_fwd_lo: pointers must be 16-byte aligned");
+  if (n == 0) return NS_OK;
+  gelu_fwd_lo_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, y, y_lo, n);
+  return check_launch("ns_gelu_fwd_lo");
 }
 
 ns_status ns_gelu_bwd(const float* dout, const float* x, float* dx, int64_t n, void* stream) {

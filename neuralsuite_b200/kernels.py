@@ -224,6 +224,15 @@ def gelu_fwd(x):
     return y
 
 
+def gelu_fwd_lo(x):
+    """(gelu(x), its tf32 lo part) in one pass (ns_gelu_fwd_lo)."""
+    _req(x, "x")
+    y = torch.empty_like(x)
+    lo = torch.empty_like(x)
+    _lib.check(_lib.load().ns_gelu_fwd_lo(_p(x), _p(y), _p(lo), x.numel(), _stream()))
+    return y, lo
+
+
 def gelu_bwd(dout, x):
     """GeluBackward (src/tensor.cpp:445-461)."""
     _req(x, "x")

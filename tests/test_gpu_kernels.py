@@ -230,6 +230,17 @@ def test_attn_with_given_lo_parts_bitwise(cuda, B, T, H, D):
     assert np.array_equal(host(got).view(np.uint32), host(want).view(np.uint32))
 
 
+def test_gelu_fwd_lo_matches_parts_bitwise(cuda):
+    """ns_gelu_fwd_lo = ns_gelu_fwd + ns_split_lo, bit for bit (ragged length too)."""
+    x = dev(normal(rng(34), (4 * 1024 * 1024 + 3,), std=2.0), cuda)
+    y, lo = nk.gelu_fwd_lo(x)
+    want = nk.gelu_fwd(x)
+    assert np.array_equal(host(y).view(np.uint32), host(want).view(np.uint32))
+    w = host(want)
+    want_lo = w - (w.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    assert np.array_equal(host(lo).view(np.uint32), want_lo.view(np.uint32))
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
