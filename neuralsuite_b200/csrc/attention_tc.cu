@@ -55,9 +55,8 @@ struct FwdLayout {
   static constexpr uint32_t kStage = 4 * kTile;    // K raw | K lo | V raw | V lo
   // The next work item's Q rows (128 x D, D/32 boxes of 16 KB, 128B swizzle).
   static constexpr uint32_t kQ = kStages * kStage;
-  static constexpr uint32_t kXchg = kQ + kBQ * D * 4;  // [3][128] floats: m, m*c, l of warpgroup 1
-  static constexpr uint32_t kBars = kXchg + 3 * kBQ * 4;
-  static constexpr uint32_t kNumBars = 2 * kStages + 14;
+  static constexpr uint32_t kBars = kQ + kBQ * D * 4;
+  static constexpr uint32_t kNumBars = 2 * kStages + 26;
   static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static_assert(kDynSmem <= 232448, "shared memory budget");
@@ -102,10 +101,6 @@ __device__ __forceinline__ void reg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
 }
 
-__device__ __forceinline__ void wg_pair_sync() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");  // warps 4..11
-}
-
 // Work item k of CTA c in a grid of G: the items (query block, batch x head)
 // are ordered longest first (the last query block has the most keys) and
 // dealt in a snake (c, then G-1-c, ...), which balances the CTAs' total
@@ -118,9 +113,18 @@ __device__ __forceinline__ int work_item(int c, int k, int G, int n_items) {
 // Persistent: one CTA per SM loops over work items.  Per item the element-wise
 // warps copy the item's Q rows (brought into shared memory by TMA while the
 // previous item ran) into TMEM as soon as the previous item's last S MMA is
-// done, and only then finish the previous item (last O fold, merge of the two
-// warpgroups, output), so the tensor core starts the next item's S blocks
-// while the previous item's epilogue runs.
+// done, and only then finish the previous item (last O fold, output), so the
+// tensor core starts the next item's S blocks while the previous item's
+// epilogue runs.
+//
+// Both softmax warpgroups work on every 64-key block, warpgroup w on keys
+// [32w, 32w+32) of it and on output columns [D/2 w, D/2 w + D/2) (D=32: the
+// output by warpgroup 0 alone): per block the two halves of a row exchange
+// their maxima through a TMEM column of the block's O buffer (free until the
+// block's O MMA) under an mbarrier of the two warps sharing the row's TMEM
+// lanes; the row sums stay per half and meet at the end.  S/P, Plo and O are
+// double-buffered in TMEM by block parity, so the tensor core computes
+// S_{j+1} while both warpgroups turn S_j into P_j.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmVlo, const FwdParams p) {
   using L = FwdLayout<D>;
   constexpr int S = L::kStages;
+  constexpr int kHalfD = 32;  // output columns one warpgroup folds (D=32: warpgroup 0 all)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -139,14 +144,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto kv_empty = [&](int s) { return bar0 + 8u * (S + s); };
   const uint32_t q_full = bar0 + 8u * (2 * S), q_empty = q_full + 8u;
   const uint32_t q_ready = q_full + 16u, q_free = q_full + 24u;
-  auto s_full = [&](int w) { return bar0 + 8u * (2 * S + 4 + w); };
-  auto p_full = [&](int w) { return bar0 + 8u * (2 * S + 6 + w); };
-  auto o_full = [&](int w) { return bar0 + 8u * (2 * S + 8 + w); };
-  auto o_empty = [&](int w) { return bar0 + 8u * (2 * S + 10 + w); };
+  auto s_full = [&](int b) { return bar0 + 8u * (2 * S + 4 + b); };
+  auto p_full = [&](int b) { return bar0 + 8u * (2 * S + 6 + b); };
+  auto o_full = [&](int b) { return bar0 + 8u * (2 * S + 8 + b); };
+  auto o_empty = [&](int b) { return bar0 + 8u * (2 * S + 10 + b); };
   const uint32_t drain = bar0 + 8u * (2 * S + 12);
+  // row-quadrant e (warps 4+e and 8+e): block-max exchange per buffer, row-sum exchange
+  auto mx_bar = [&](int e, int b) { return bar0 + 8u * (2 * S + 13 + 2 * e + b); };
+  auto lx_bar = [&](int e) { return bar0 + 8u * (2 * S + 21 + e); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* xchg = reinterpret_cast<float*>(smem + L::kXchg);
 
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int BH = p.n_items / p.nqb;
@@ -167,11 +174,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(q_free, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(p_full(i), kWgThreads);
+      mbar_init(p_full(i), 2 * kWgThreads);
       mbar_init(o_full(i), 1);
-      mbar_init(o_empty(i), kWgThreads);
+      mbar_init(o_empty(i), 2 * kWgThreads);
     }
     mbar_init(drain, 1);
+    for (int e = 0; e < 4; ++e) {
+      mbar_init(mx_bar(e, 0), 64);
+      mbar_init(mx_bar(e, 1), 64);
+      mbar_init(lx_bar(e), 64);
+    }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -255,16 +267,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer
       // The whole warp runs this loop converged; the elected lane issues.
+      // Block G (counted over all items) uses S/P, Plo and O buffer G & 1.
       constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
       constexpr uint32_t id_o = instr_desc(D, 0, 1);
-      uint32_t g = 0;               // key blocks of earlier items (ring position)
-      uint32_t tw[2] = {0u, 0u};    // blocks of each warpgroup so far (all items)
+      uint32_t g = 0;  // key blocks of earlier items (ring position and block count)
       bool ok = true;
-      // S_j of the current item (the elected lane): its K tile is ring entry g + j.
-      auto emit_s = [&](int j) {
-        const uint32_t gj = g + (uint32_t)j;
-        const int s = gj % S;
-        const uint32_t d = tmem + kTS + (j & 1) * kBKV;
+      auto emit_s = [&](uint32_t G) {
+        const int s = G % S;
+        const uint32_t d = tmem + kTS + (G & 1u) * kBKV;
         const uint32_t k_raw = sbase + s * L::kStage, k_lo = k_raw + L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 8; ++kk)
@@ -274,13 +284,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts(d, tmem + kk * 8, k_desc(k_lo, kk), id_s, 1u);
           mma_ts(d, tmem + D + kk * 8, k_desc(k_raw, kk), id_s, 1u);
         }
-        commit(s_full(j & 1));
+        commit(s_full(G & 1u));
       };
-      auto issue_s = [&](int j) -> bool {
-        const uint32_t gj = g + (uint32_t)j;
-        if (!warp_wait(kv_full(gj % S), (gj / S) & 1u, abort, &g_timeout)) return false;
+      auto issue_s = [&](uint32_t G) -> bool {
+        if (!warp_wait(kv_full(G % S), (G / S) & 1u, abort, &g_timeout)) return false;
         fence_after();
-        if (elect_one()) emit_s(j);
+        if (elect_one()) emit_s(G);
         __syncwarp();
         return true;
       };
@@ -298,20 +307,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         fence_after();
-        ok = issue_s(0);
-        if (ok && n_kb > 1) ok = issue_s(1);
+        ok = issue_s(g);
+        if (ok && n_kb > 1) ok = issue_s(g + 1);
         if (ok && n_kb <= 2) release_q();
         for (int j = 0; ok && j < n_kb; ++j) {
-          const int wg = j & 1;
-          const uint32_t t = tw[wg]++;
+          const uint32_t Gj = g + (uint32_t)j;
+          const uint32_t b = Gj & 1u, ph = (Gj >> 1) & 1u;
           // The K tile of S_{j+2} is nearly always there: tested while waiting
           // for P_j, so that O_j and S_{j+2} go out in one elected run (each
           // wait or re-convergence between MMAs idles the tensor core).
-          const uint32_t g2 = g + (uint32_t)j + 2u;
           const bool next_s = j + 2 < n_kb;
-          bool k_ready = next_s && mbar_test(kv_full(g2 % S), (g2 / S) & 1u);
-          const bool pe = mbar_wait(p_full(wg), t & 1u, abort, &g_timeout) &&
-                          mbar_wait(o_empty(wg), (t & 1u) ^ 1u, abort, &g_timeout);
+          bool k_ready = next_s && mbar_test(kv_full((Gj + 2) % S), ((Gj + 2) / S) & 1u);
+          const bool pe = mbar_wait(p_full(b), ph, abort, &g_timeout) &&
+                          mbar_wait(o_empty(b), ph ^ 1u, abort, &g_timeout);
           const uint32_t bits = __shfl_sync(0xffffffffu, (pe ? 1u : 0u) | (k_ready ? 2u : 0u), 0);
           if (!(bits & 1u)) {
             ok = false;
@@ -319,12 +327,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           k_ready = (bits & 2u) != 0;
           fence_after();
-          const uint32_t gj = g + (uint32_t)j;
-          const int s = gj % S;
+          const int s = Gj % S;
           if (elect_one()) {
             const uint32_t v_raw = sbase + s * L::kStage + 2 * L::kTile, v_lo = v_raw + L::kTile;
-            const uint32_t o = tmem + kTO + wg * D;
-            const uint32_t phi = tmem + kTS + wg * kBKV, plo = tmem + kTPlo + wg * kBKV;
+            const uint32_t o = tmem + kTO + b * 64u;
+            const uint32_t phi = tmem + kTS + b * kBKV, plo = tmem + kTPlo + b * kBKV;
 #pragma unroll
             for (int kk = 0; kk < kBKV / 8; ++kk)
               mma_ts(o, phi + kk * 8, v_desc(v_raw, kk), id_o, kk > 0 ? 1u : 0u);
@@ -333,15 +340,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_ts(o, phi + kk * 8, v_desc(v_lo, kk), id_o, 1u);
               mma_ts(o, plo + kk * 8, v_desc(v_raw, kk), id_o, 1u);
             }
-            commit(o_full(wg));
+            commit(o_full(b));
             commit(kv_empty(s));
-            if (k_ready) emit_s(j + 2);
+            if (k_ready) emit_s(Gj + 2);
           }
           __syncwarp();
-          // S_{j+2} reuses this warpgroup's S/P columns: issued after O_j, and
-          // the tensor core runs one CTA's MMAs in issue order.
+          // S_{j+2} reuses block j's S/P columns: issued after O_j, and the
+          // tensor core runs one CTA's MMAs in issue order.
           if (next_s) {
-            if (!k_ready) ok = issue_s(j + 2);
+            if (!k_ready) ok = issue_s(Gj + 2);
             if (ok && j + 2 == n_kb - 1) release_q();
           }
         }
@@ -357,109 +364,70 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
-    const int wg = (warp - 4) >> 2;  // key blocks wg, wg+2, wg+4, ... of each item
+    const int wg = (warp - 4) >> 2;  // keys [32wg, 32wg+32) of every block
     const int ew = warp & 3;         // TMEM lanes 32*ew .. 32*ew+31
     const int row = ew * 32 + lane;
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
     const float c = p.scale_log2;
-    const uint32_t s_t = tmem + lane_off + kTS + wg * kBKV;
-    const uint32_t pl_t = tmem + lane_off + kTPlo + wg * kBKV;
-    const uint32_t o_t = tmem + lane_off + kTO + wg * D;
-    float acc[D];
+    const bool folds = D == 64 || wg == 0;  // output columns [kHalfD*wg, kHalfD*wg + kHalfD)
+    float acc[kHalfD];
     float m = -INFINITY, mc = 0.0f, l = 0.0f, alpha_prev = 0.0f;
-    uint32_t T = 0;  // this warpgroup's blocks so far (all items)
+    uint32_t T = 0;  // blocks so far (all items)
     int t = 0;       // ... of the current item
-    int prev_w = -1;
+    int prev_w = -1, prev_k = -1;
     bool ok = true;
-    auto fold = [&](uint32_t ph, float alpha) -> bool {
-      if (!mbar_wait(o_full(wg), ph, abort, &g_timeout)) return false;
+    // acc = acc * alpha + O of block Gb (buffer Gb & 1), then the O buffer is free.
+    auto fold = [&](uint32_t Gb, float alpha) -> bool {
+      if (!mbar_wait(o_full(Gb & 1u), (Gb >> 1) & 1u, abort, &g_timeout)) return false;
       fence_after();
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
+      if (folds) {
         uint32_t v[32];
-        tmem_ld32(o_t + 32 * cc, v);
+        tmem_ld32(tmem + lane_off + kTO + (Gb & 1u) * 64u + kHalfD * wg, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          acc[32 * cc + i] = fmaf(acc[32 * cc + i], alpha, __uint_as_float(v[i]));
+        for (int i = 0; i < kHalfD; ++i) acc[i] = fmaf(acc[i], alpha, __uint_as_float(v[i]));
       }
+      fence_before();
+      mbar_arrive(o_empty(Gb & 1u));
       return true;
     };
-    // Last fold, merge of the two warpgroups and the output of item w (whose
-    // blocks this warpgroup has all turned into P).
-    auto finish = [&](int w) -> bool {
-      if (t > 0) {
-        if (!fold((T - 1) & 1u, alpha_prev)) return false;
-        if (wg == 0) {
-          fence_before();
-          mbar_arrive(o_empty(0));
+    // Last fold and output of item w (whose blocks are all turned into P).
+    // The row sums of the two halves meet through a column of the last
+    // block's O buffer, free after the fold.
+    auto finish = [&](int w, uint32_t k_item) -> bool {
+      if (!fold(T - 1, alpha_prev)) return false;
+      const uint32_t xcol = tmem + lane_off + kTO + ((T - 1) & 1u) * 64u;
+      tmem_st1(xcol + 32 * wg, l);
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(lx_bar(ew));
+      if (!mbar_wait(lx_bar(ew), k_item & 1u, abort, &g_timeout)) return false;
+      fence_after();
+      const float l_tot = l + tmem_ld1(xcol + 32 * (wg ^ 1));
+      const float inv = 1.0f / l_tot;
+      const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
+      const int q = item_q0(w) + row;
+      if (q < p.T && folds) {
+        const size_t o = ((size_t)b * p.T + q) * p.C + (size_t)h * D + kHalfD * wg;
+        float* dst = p.out + o;
+#pragma unroll
+        for (int d = 0; d < kHalfD; d += 4)
+          *reinterpret_cast<float4*>(dst + d) =
+              make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+        if (p.out_lo) {
+          float* dlo = p.out_lo + o;
+#pragma unroll
+          for (int d = 0; d < kHalfD; d += 4)
+            *reinterpret_cast<float4*>(dlo + d) =
+                make_float4(tf32_lo(acc[d] * inv), tf32_lo(acc[d + 1] * inv),
+                            tf32_lo(acc[d + 2] * inv), tf32_lo(acc[d + 3] * inv));
         }
-      }
-      // Warpgroup 1 hands its accumulator over through its own O columns (no
-      // MMA writes them until it releases them below) and m, m*c, l through
-      // shared memory.
-      if (wg == 1) {
-#pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[32 * cc + i]);
-          tmem_st32(o_t + 32 * cc, v);
-        }
-        xchg[row] = m;
-        xchg[kBQ + row] = mc;
-        xchg[2 * kBQ + row] = l;
-        tmem_wait_st();
-        fence_before();
-      }
-      wg_pair_sync();
-      if (wg == 0) {
-        fence_after();
-        const float m1 = xchg[row], mc1 = xchg[kBQ + row], l1 = xchg[2 * kBQ + row];
-        const float m_tot = fmaxf(m, m1);  // finite: key 0 is never masked
-        const float mc_tot = m_tot * c;
-        const float a0 = fast_exp2(mc - mc_tot);
-        const float a1 = m1 == -INFINITY ? 0.0f : fast_exp2(mc1 - mc_tot);
-        const float l_tot = l * a0 + l1 * a1;
-        const float inv = 1.0f / l_tot;
-        const uint32_t o1 = tmem + lane_off + kTO + D;
-#pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(o1 + 32 * cc, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            acc[32 * cc + i] = fmaf(acc[32 * cc + i], a0, __uint_as_float(v[i]) * a1) * inv;
-        }
-        fence_before();
-        const int bh = item_bh(w), b = bh / p.H, h = bh % p.H;
-        const int q = item_q0(w) + row;
-        if (q < p.T) {
-          const size_t o = ((size_t)b * p.T + q) * p.C + (size_t)h * D;
-          float* dst = p.out + o;
-#pragma unroll
-          for (int d = 0; d < D; d += 4)
-            *reinterpret_cast<float4*>(dst + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
-          if (p.out_lo) {
-            float* dlo = p.out_lo + o;
-#pragma unroll
-            for (int d = 0; d < D; d += 4)
-              *reinterpret_cast<float4*>(dlo + d) = make_float4(tf32_lo(acc[d]), tf32_lo(acc[d + 1]),
-                                                                tf32_lo(acc[d + 2]), tf32_lo(acc[d + 3]));
-          }
-          p.lse[(size_t)bh * p.T + q] = m_tot * p.scale + logf(l_tot);
-        }
-      }
-      wg_pair_sync();  // warpgroup 0 has read O1 and the exchange
-      if (wg == 1 && t > 0) {
-        fence_before();
-        mbar_arrive(o_empty(1));
+        if (wg == 0) p.lse[(size_t)bh * p.T + q] = m * p.scale + logf(l_tot);
       }
       return true;
     };
     for (int k = 0; ok; ++k) {
       const int w = work_item(cta, k, G, p.n_items);
       if (w < 0) break;
-      const int bh = item_bh(w), b = bh / p.H;
       const int q0 = item_q0(w), q = q0 + row;
       const int n_kb = item_nkb(w);
       {
@@ -495,56 +463,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_before();
         mbar_arrive(q_ready);
       }
-      if (prev_w >= 0 && !finish(prev_w)) {
+      if (prev_w >= 0 && !finish(prev_w, (uint32_t)prev_k)) {
         ok = false;
         break;
       }
-      (void)b;
 #pragma unroll
-      for (int d = 0; d < D; ++d) acc[d] = 0.0f;
+      for (int d = 0; d < kHalfD; ++d) acc[d] = 0.0f;
       m = -INFINITY;
       mc = 0.0f;
       l = 0.0f;
       alpha_prev = 0.0f;
       t = 0;
-      for (int j = wg; j < n_kb; j += 2, ++t, ++T) {
-        if (!mbar_wait(s_full(wg), T & 1u, abort, &g_timeout)) {
+      for (int j = 0; j < n_kb; ++j, ++t, ++T) {
+        const uint32_t b = T & 1u, ph = (T >> 1) & 1u;
+        if (!mbar_wait(s_full(b), ph, abort, &g_timeout)) {
           ok = false;
           break;
         }
         fence_after();
-        // S_j completing implies this warpgroup's previous O is complete too
-        // (same MMA thread, issued earlier): fold it and free the O columns.
-        if (t > 0) {
-          if (!fold((T - 1) & 1u, alpha_prev)) {
-            ok = false;
-            break;
-          }
-          fence_before();
-          mbar_arrive(o_empty(wg));
-        }
-        const int k0 = j * kBKV;
-        uint32_t s0[32], s1[32];
-        tmem_ld32(s_t, s0);
-        tmem_ld32(s_t + 32, s1);
-        float x[64];
+        const uint32_t s_t = tmem + lane_off + kTS + b * kBKV + 32 * wg;
+        const uint32_t pl_t = tmem + lane_off + kTPlo + b * kBKV + 32 * wg;
+        const int k0 = j * kBKV + 32 * wg;  // key of this half's column 0
+        uint32_t sv[32];
+        tmem_ld32(s_t, sv);
+        float x[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = __uint_as_float(s0[i]);
-          x[32 + i] = __uint_as_float(s1[i]);
-        }
-        if (k0 + kBKV - 1 > q) {
+        for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(sv[i]);
+        if (k0 + 31 > q) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
+          for (int i = 0; i < 32; ++i)
             if (k0 + i > q) x[i] = -INFINITY;
         }
         float mx[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) mx[i] = x[i];
 #pragma unroll
-        for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
-        const float m_new = fmaxf(m, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
+        for (int i = 8; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+        const float mh = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        // The other half's maximum, through this block's O buffer (no MMA
+        // writes it before P_j is complete).
+        const uint32_t xcol = tmem + lane_off + kTO + b * 64u;
+        tmem_st1(xcol + 32 * wg, mh);
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(mx_bar(ew, b));
+        if (!mbar_wait(mx_bar(ew, b), ph, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const float m_blk = fmaxf(mh, tmem_ld1(xcol + 32 * (wg ^ 1)));
+        const float m_new = fmaxf(m, m_blk);
         // m_new = -inf: every key so far is masked (P = 0 below).
         const float mc_new = m_new == -INFINITY ? 0.0f : m_new * c;
         const float alpha = m == -INFINITY ? 0.0f : fast_exp2(mc - mc_new);
@@ -552,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) rs[i] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
           x[i] = fast_exp2(fmaf(x[i], c, -mc_new));
           rs[i & 7] += x[i];
         }
@@ -560,28 +530,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
         mc = mc_new;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s0[i] = __float_as_uint(tf32_hi(x[i]));
-          s1[i] = __float_as_uint(tf32_hi(x[32 + i]));
-        }
-        tmem_st32(s_t, s0);
-        tmem_st32(s_t + 32, s1);
+        for (int i = 0; i < 32; ++i) sv[i] = __float_as_uint(tf32_hi(x[i]));
+        tmem_st32(s_t, sv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s0[i] = __float_as_uint(tf32_lo(x[i]));
-          s1[i] = __float_as_uint(tf32_lo(x[32 + i]));
-        }
-        tmem_st32(pl_t, s0);
-        tmem_st32(pl_t + 32, s1);
+        for (int i = 0; i < 32; ++i) sv[i] = __float_as_uint(tf32_lo(x[i]));
+        tmem_st32(pl_t, sv);
         tmem_wait_st();
         fence_before();
-        mbar_arrive(p_full(wg));
+        mbar_arrive(p_full(b));
+        // Now the previous block's O (its MMA ran while this block's softmax did).
+        if (t > 0 && !fold(T - 1, alpha_prev)) {
+          ok = false;
+          break;
+        }
         alpha_prev = alpha;
       }
       if (!ok) break;
       prev_w = w;
+      prev_k = k;
     }
-    if (ok && prev_w >= 0) ok = finish(prev_w);
+    if (ok && prev_w >= 0) ok = finish(prev_w, (uint32_t)prev_k);
   }
 
   fence_before();
