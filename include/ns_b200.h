@@ -206,6 +206,17 @@ NS_API ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const flo
 /* LayerNormForward, src/tensor.cpp:290-322 (last axis, biased variance). */
 NS_API ns_status ns_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* out,
                            float* mean, float* rstd, int rows, int dim, float eps, void* stream);
+/* ns_layernorm_fwd with the neighbours' work fused in: with resid, the row is
+ * first formed as x = resid + (x_raw + bias) (the residual add of the
+ * producing GEMM's bias epilogue, same rounding; x_raw is that GEMM's plain
+ * product) and written to x_out (which may be x_raw); with out_lo (optional),
+ * out's tf32 lo part is written too (the next GEMM's operand split).  No
+ * reference counterpart (ElementwiseAdd src/tensor.cpp:534-540 + LayerNorm
+ * 290-322 + the split). */
+NS_API ns_status ns_layernorm_fwd_ex(const float* x_raw, const float* bias, const float* resid,
+                              float* x_out, const float* gamma, const float* beta, float* out,
+                              float* out_lo, float* mean, float* rstd, int rows, int dim,
+                              float eps, void* stream);
 /* LayerNormBackward, src/tensor.cpp:324-359.  dgamma/dbeta are overwritten
  * (deterministic two-stage column sums through `workspace`).  If `dresid` is
  * non-NULL the result is dx = dresid + dx_ln: the ElementwiseAdd of the

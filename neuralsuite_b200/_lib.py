@@ -68,6 +68,7 @@ _SIGS = {
     "ns_attn_bwd": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int, P, P, c_size_t, P]),
     "ns_attn_bwd_lo": (c_int, [P, P, P, P, P, c_int, c_int, c_int, c_int, P, P, c_size_t, P]),
     "ns_layernorm_fwd": (c_int, [P, P, P, P, P, P, c_int, c_int, c_float, P]),
+    "ns_layernorm_fwd_ex": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_float, P]),
     "ns_layernorm_bwd_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_layernorm_bwd": (c_int, [P, P, P, P, P, P, P, P, P, c_int, c_int, P, c_size_t, P]),
     "ns_gelu_fwd": (c_int, [P, P, c_int64, P]),

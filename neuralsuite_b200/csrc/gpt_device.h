@@ -217,18 +217,24 @@ class Linear : public Layer {
   // lo part.  With post_lo the GELU runs as one streaming pass after the
   // GEMM (cheaper than GELU and two more stores in the GEMM epilogue, which
   // hold up its tensor core); without, it is fused into the epilogue.
-  Tensor ForwardGelu(const Tensor& x, Tensor* post, float* post_lo = nullptr) {
+  Tensor ForwardGelu(const Tensor& x, Tensor* post, float* post_lo = nullptr,
+                     const float* x_lo = nullptr) {
     const int n = Rows(x, in_);
     Tensor g = Scratch(post_, n, out_);
     Tensor y;
     if (post_lo) {
-      y = Run(x, NS_EPI_BIAS, nullptr, nullptr);
+      y = Run(x, NS_EPI_BIAS, nullptr, nullptr, x_lo);
       Check(ns_gelu_fwd_lo(y.Data(), g.Data(), post_lo, static_cast<int64_t>(n) * out_, stream()));
     } else {
-      y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data());
+      y = Run(x, NS_EPI_BIAS_GELU, nullptr, g.Data(), x_lo);
     }
     *post = g;
     return y;
+  }
+  // X W alone, bias not added: for a consumer that adds bias and residual in
+  // its own pass (ns_layernorm_fwd_ex).
+  Tensor ForwardNoBias(const Tensor& x, const float* x_lo = nullptr) {
+    return Run(x, NS_EPI_STORE, nullptr, nullptr, x_lo);
   }
   // Y = resid + (X W + b)  (the GPTBlock residual ElementwiseAdd fused).
   Tensor ForwardResidual(const Tensor& x, const Tensor& resid, const float* x_lo = nullptr) {
@@ -343,6 +349,20 @@ class LayerNormLayer : public Layer {
                            mean.Data(), rstd.Data(), n, dim_, eps_, stream()));
     return y.View(x.Shape());
   }
+  // Forward with the neighbours fused (ns_layernorm_fwd_ex): with resid, the
+  // input is formed as resid + (raw + bias) and written over `raw` (the layer
+  // input kept for backward); y_lo (or null) receives the output's tf32 lo part.
+  Tensor ForwardEx(const Tensor& raw, const float* bias, const Tensor* resid, float* y_lo) {
+    const int n = Rows(raw, dim_);
+    last_input_ = raw;
+    Tensor y = Scratch(out_buf_, n, dim_);
+    Tensor mean = Scratch(mean_, n, 1), rstd = Scratch(rstd_, n, 1);
+    Check(ns_layernorm_fwd_ex(raw.Data(), bias, resid ? resid->Data() : nullptr,
+                              resid ? raw.Data() : nullptr, gamma_.Value().Data(),
+                              beta_.Value().Data(), y.Data(), y_lo, mean.Data(), rstd.Data(), n,
+                              dim_, eps_, stream()));
+    return y.View(raw.Shape());
+  }
   Tensor Backward(const Tensor& dy) override { return BackwardAdd(dy, nullptr); }
   // dx = dresid + LayerNormBackward(dy): the residual ElementwiseAdd fused.
   Tensor BackwardAdd(const Tensor& dy, const Tensor* dresid) {
@@ -396,9 +416,15 @@ class MultiHeadAttention : public Layer {
     Register(&c_attn_, "c_attn");
     Register(&c_proj_, "c_proj");
   }
-  Tensor Forward(const Tensor& x) override { return ForwardImpl(x, nullptr); }
+  Tensor Forward(const Tensor& x) override { return ForwardImpl(x, nullptr, nullptr, false); }
   // c_proj output added to `resid` (GPTBlock's first residual add fused).
-  Tensor ForwardResidual(const Tensor& x, const Tensor& resid) { return ForwardImpl(x, &resid); }
+  Tensor ForwardResidual(const Tensor& x, const Tensor& resid) {
+    return ForwardImpl(x, &resid, nullptr, false);
+  }
+  // c_proj's product without its bias (the caller adds bias and residual in
+  // the next LayerNorm); x_lo (or null) is x's tf32 lo part.
+  Tensor ForwardNoBias(const Tensor& x, const float* x_lo) { return ForwardImpl(x, nullptr, x_lo, true); }
+  const float* OutBias() { return c_proj_.BiasParam().Value().Data(); }
   Tensor Backward(const Tensor& dy) override {
     const int B = batch_, T = seq_, M = B * T;
     Tensor datt = c_proj_.Backward(dy);
@@ -412,7 +438,7 @@ class MultiHeadAttention : public Layer {
   Linear& OutProjection() { return c_proj_; }
 
  private:
-  Tensor ForwardImpl(const Tensor& x, const Tensor* resid) {
+  Tensor ForwardImpl(const Tensor& x, const Tensor* resid, const float* x_lo, bool no_bias) {
     if (x.Shape().size() != 3 || x.Shape()[2] != n_embd_)
       throw std::invalid_argument("MultiHeadAttention: input must be [B, T, n_embd]");
     batch_ = x.Shape()[0];
@@ -424,13 +450,14 @@ class MultiHeadAttention : public Layer {
     const bool lo = n_embd_ % 4 == 0;
     qkv_lo_ = lo ? Scratch(qkv_lo_buf_, M, 3 * n_embd_).Data() : nullptr;
     float* att_lo = lo ? Scratch(att_lo_buf_, M, n_embd_).Data() : nullptr;
-    qkv_ = c_attn_.ForwardLo(x.View({M, n_embd_}), nullptr, qkv_lo_);
+    qkv_ = c_attn_.ForwardLo(x.View({M, n_embd_}), x_lo, qkv_lo_);
     att_ = Scratch(att_buf_, M, n_embd_);
     lse_ = Scratch(lse_buf_, batch_ * n_head_, seq_);
     Check(ns_attn_fwd_lo(qkv_.Data(), qkv_lo_, batch_, seq_, n_head_, head_dim_, att_.Data(), att_lo,
                          lse_.Data(), ctx_->scratch, ctx_->scratch_bytes, stream()));
-    Tensor y = resid ? c_proj_.ForwardResidual(att_, resid->View({M, n_embd_}), att_lo)
-                     : c_proj_.ForwardLo(att_, att_lo, nullptr);
+    Tensor y = no_bias ? c_proj_.ForwardNoBias(att_, att_lo)
+               : resid ? c_proj_.ForwardResidual(att_, resid->View({M, n_embd_}), att_lo)
+                       : c_proj_.ForwardLo(att_, att_lo, nullptr);
     return y.View({batch_, seq_, n_embd_});
   }
 
@@ -478,14 +505,21 @@ class GPTBlock : public Layer {
     Register(&mlp_proj_, "mlp_proj");
   }
   // x1 = x + attn(ln_1(x)); x2 = x1 + mlp_proj(gelu(mlp_fc(ln_2(x1))))
+  // The operand lo parts come from the producers: ln_1 -> c_attn, ln_2 ->
+  // mlp_fc, the GELU pass -> mlp_proj (attention handles its own); the first
+  // residual add runs inside ln_2 on c_proj's plain product.
   Tensor Forward(const Tensor& x) override {
-    Tensor h1 = ln_1_.Forward(x);
-    x1_ = attn_.ForwardResidual(h1, x);
-    Tensor h2 = ln_2_.Forward(x1_);
-    const int C = h2.Shape().back(), M = Rows(h2, C);
-    // gelu's lo part comes out of the mlp_fc epilogue (mlp_proj's X split).
+    const int C = x.Shape().back(), M = Rows(x, C);
+    const bool lo = C % 4 == 0;
+    float* h1_lo = lo ? Scratch(h1_lo_buf_, M, C).Data() : nullptr;
+    Tensor h1 = ln_1_.ForwardEx(x, nullptr, nullptr, h1_lo);
+    Tensor raw1 = attn_.ForwardNoBias(h1, h1_lo);
+    float* h2_lo = lo ? Scratch(h2_lo_buf_, M, C).Data() : nullptr;
+    const Tensor x2d = x.View({M, C});
+    Tensor h2 = ln_2_.ForwardEx(raw1, attn_.OutBias(), &x2d, h2_lo);
+    x1_ = raw1;  // now x + attn(ln_1(x)), written by ln_2
     float* gelu_lo = mlp_fc_.Out() % 4 == 0 ? Scratch(gelu_lo_buf_, M, mlp_fc_.Out()).Data() : nullptr;
-    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({M, C}), &gelu_, gelu_lo);
+    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({M, C}), &gelu_, gelu_lo, h2_lo);
     Tensor x2 = mlp_proj_.ForwardResidual(gelu_, x1_.View({M, C}), gelu_lo);
     return x2.View(x.Shape());
   }
@@ -509,7 +543,7 @@ class GPTBlock : public Layer {
   LayerNormLayer ln_2_;
   Linear mlp_fc_;
   Linear mlp_proj_;
-  Tensor x1_, fc_pre_, gelu_, gelu_lo_buf_;
+  Tensor x1_, fc_pre_, gelu_, gelu_lo_buf_, h1_lo_buf_, h2_lo_buf_;
 };
 
 // Sizes of GPTModel's parameters in registration order (include/gpt.h:143-149,

@@ -4,6 +4,7 @@
 // partials in caller workspace, then an ordered sum over CTAs) so every run
 // gives the same bits.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -17,13 +18,18 @@ constexpr int kMaxVec = 8;             // float4 per lane => dim <= 1024 on the 
 // ----------------------------------------------------------- forward
 // LayerNormForward (src/tensor.cpp:290-322): mean = sum/D, var = sum((x-m)^2)/D,
 // rstd = 1/sqrt(var+eps), out = ((x-m)*rstd)*gamma + beta.
-template <int NV>
-__global__ void __launch_bounds__(256) ln_fwd_vec(const float* __restrict__ x,
+// RES: the row is first formed as x = resid + (raw + bias) (the residual add
+// of a GEMM's bias epilogue, same rounding) and written to x_out.  LO: the
+// output's tf32 lo part goes to out_lo as well (the next GEMM's operand split).
+template <int NV, bool RES, bool LO>
+__global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias x_out
                                                   const float* __restrict__ gamma,
                                                   const float* __restrict__ beta,
                                                   float* __restrict__ out, float* __restrict__ mean,
                                                   float* __restrict__ rstd, int rows, int dim,
-                                                  float eps) {
+                                                  float eps, const float* __restrict__ bias,
+                                                  const float* __restrict__ resid, float* x_out,
+                                                  float* __restrict__ out_lo) {
   const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -35,6 +41,15 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* __restrict__ x,
   for (int i = 0; i < NV; ++i) {
     const int c = lane + i * 32;
     v[i] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (RES && c < nv) {
+      const float4 r = reinterpret_cast<const float4*>(resid + (size_t)row * dim)[c];
+      const float4 b = reinterpret_cast<const float4*>(bias)[c];
+      v[i].x = __fadd_rn(r.x, __fadd_rn(v[i].x, b.x));
+      v[i].y = __fadd_rn(r.y, __fadd_rn(v[i].y, b.y));
+      v[i].z = __fadd_rn(r.z, __fadd_rn(v[i].z, b.z));
+      v[i].w = __fadd_rn(r.w, __fadd_rn(v[i].w, b.w));
+      reinterpret_cast<float4*>(x_out + (size_t)row * dim)[c] = v[i];
+    }
     s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
   s = warp_sum(s);
@@ -69,8 +84,24 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* __restrict__ x,
       r.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].z, m), rs), g.z), bb.z);
       r.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].w, m), rs), g.w), bb.w);
       o4[c] = r;
+      if (LO) {
+        auto lo = [](float a) { return a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u); };
+        reinterpret_cast<float4*>(out_lo + (size_t)row * dim)[c] =
+            make_float4(lo(r.x), lo(r.y), lo(r.z), lo(r.w));
+      }
     }
   }
+}
+
+// x_out = resid + (raw + bias), element-wise (the fused LayerNorm's fallback
+// for shapes without its vector path).
+__global__ void resid_bias_add_k(const float* __restrict__ raw, const float* __restrict__ bias,
+                                 const float* __restrict__ resid, float* __restrict__ x_out,
+                                 int64_t rows, int dim) {
+  const int64_t n = rows * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    x_out[i] = __fadd_rn(resid[i], __fadd_rn(raw[i], bias[i % dim]));
 }
 
 // Any dim: strided scalar passes over the row (re-read from L1/L2).
@@ -383,27 +414,54 @@ extern "C" {
 
 ns_status ns_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* out,
                            float* mean, float* rstd, int rows, int dim, float eps, void* stream) {
+  return ns_layernorm_fwd_ex(x, nullptr, nullptr, nullptr, gamma, beta, out, nullptr, mean, rstd,
+                             rows, dim, eps, stream);
+}
+
+ns_status ns_layernorm_fwd_ex(const float* x, const float* bias, const float* resid, float* x_out,
+                              const float* gamma, const float* beta, float* out, float* out_lo,
+                              float* mean, float* rstd, int rows, int dim, float eps, void* stream) {
   NS_REQUIRE(rows >= 0 && dim > 0, "ns_layernorm_fwd: rows must be >= 0 and dim > 0");
+  NS_REQUIRE(!resid || (bias && x_out), "ns_layernorm_fwd_ex: resid needs bias and x_out");
   if (rows == 0) return NS_OK;
   const dim3 grid(ceil_div(rows, kRowsWarps)), block(32 * kRowsWarps);
   cudaStream_t s = as_stream(stream);
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
-                         reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) &
+                         reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta) |
+                         reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(resid) |
+                         reinterpret_cast<uintptr_t>(x_out) | reinterpret_cast<uintptr_t>(out_lo)) &
                         15) == 0;
   if (dim % 4 == 0 && aligned && dim <= 128 * kMaxVec) {
     const int nv = dim / 4;
-    if (nv <= 32)
-      ln_fwd_vec<1><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
-    else if (nv <= 64)
-      ln_fwd_vec<2><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
-    else if (nv <= 128)
-      ln_fwd_vec<4><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
-    else
-      ln_fwd_vec<8><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
-  } else {
-    ln_fwd_any<<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps);
+    auto go = [&](auto nvt) {
+      constexpr int NV = decltype(nvt)::value;
+      if (resid && out_lo)
+        ln_fwd_vec<NV, true, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+      else if (resid)
+        ln_fwd_vec<NV, true, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+      else if (out_lo)
+        ln_fwd_vec<NV, false, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+      else
+        ln_fwd_vec<NV, false, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+    };
+    if (nv <= 32) go(std::integral_constant<int, 1>());
+    else if (nv <= 64) go(std::integral_constant<int, 2>());
+    else if (nv <= 128) go(std::integral_constant<int, 4>());
+    else go(std::integral_constant<int, 8>());
+    return check_launch("ns_layernorm_fwd");
   }
-  return check_launch("ns_layernorm_fwd");
+  const float* xin = x;
+  if (resid) {
+    const int64_t n = (int64_t)rows * dim;
+    resid_bias_add_k<<<(unsigned)std::min<int64_t>(ceil_div64(n, 256), 148 * 8), 256, 0, s>>>(
+        x, bias, resid, x_out, rows, dim);
+    { ns_status _rc = check_launch("ns_layernorm_fwd residual"); if (_rc != NS_OK) return _rc; }
+    xin = x_out;
+  }
+  ln_fwd_any<<<grid, block, 0, s>>>(xin, gamma, beta, out, mean, rstd, rows, dim, eps);
+  { ns_status _rc = check_launch("ns_layernorm_fwd"); if (_rc != NS_OK) return _rc; }
+  if (out_lo) return ns_split_lo(out, rows, dim, dim, out_lo, stream);
+  return NS_OK;
 }
 
 size_t ns_layernorm_bwd_workspace_size(int rows, int dim) {

@@ -199,6 +199,21 @@ def layernorm_fwd(x, gamma, beta, eps=1e-5):
     return out, mean, rstd
 
 
+def layernorm_fwd_ex(raw, gamma, beta, bias=None, resid=None, want_lo=True, eps=1e-5):
+    """ns_layernorm_fwd_ex: (x, y, y_lo, mean, rstd) with x = resid + (raw + bias) if resid given."""
+    lib = _lib.load()
+    D = raw.shape[-1]
+    N = raw.numel() // D
+    x = torch.empty_like(raw) if resid is not None else None
+    y = torch.empty_like(raw)
+    lo = torch.empty_like(raw) if want_lo else None
+    mean = torch.empty(N, dtype=_f32, device=raw.device)
+    rstd = torch.empty(N, dtype=_f32, device=raw.device)
+    _lib.check(lib.ns_layernorm_fwd_ex(_p(raw), _p(bias), _p(resid), _p(x), _p(gamma), _p(beta),
+                                       _p(y), _p(lo), _p(mean), _p(rstd), N, D, eps, _stream()))
+    return x, y, lo, mean, rstd
+
+
 def layernorm_bwd(dout, x, gamma, mean, rstd, dresid=None):
     """LayerNormBackward (src/tensor.cpp:324-359), plus dresid if given."""
     lib = _lib.load()

@@ -241,6 +241,28 @@ def test_gelu_fwd_lo_matches_parts_bitwise(cuda):
     assert np.array_equal(host(lo).view(np.uint32), want_lo.view(np.uint32))
 
 
+@pytest.mark.parametrize("N,D", [(8192, 768), (300, 128), (257, 132), (64, 100)])
+def test_layernorm_fwd_ex_matches_parts_bitwise(cuda, N, D):
+    """ns_layernorm_fwd_ex = residual add (GEMM epilogue rounding) + LayerNorm + lo split."""
+    r = rng(N + D)
+    raw = dev(normal(r, (N, D)), cuda)
+    resid = dev(normal(r, (N, D)), cuda)
+    bias = dev(normal(r, (D,)), cuda)
+    gamma = dev(normal(r, (D,)), cuda)
+    beta = dev(normal(r, (D,)), cuda)
+    want_x = (host(raw) + host(bias)[None, :]).astype(np.float32) + host(resid)
+    x, y, lo, mean, rstd = nk.layernorm_fwd_ex(raw, gamma, beta, bias=bias, resid=resid)
+    assert np.array_equal(host(x).view(np.uint32), want_x.astype(np.float32).view(np.uint32))
+    y2, m2, r2 = nk.layernorm_fwd(x, gamma, beta)
+    for a, b in ((y, y2), (mean, m2), (rstd, r2)):
+        assert np.array_equal(host(a).view(np.uint32), host(b).view(np.uint32))
+    assert np.array_equal(host(lo).view(np.uint32), host(nk.split_lo(y2)).view(np.uint32))
+    # plain LayerNorm with the lo output only
+    _, y3, lo3, _, _ = nk.layernorm_fwd_ex(x, gamma, beta)
+    assert np.array_equal(host(y3).view(np.uint32), host(y2).view(np.uint32))
+    assert np.array_equal(host(lo3).view(np.uint32), host(lo).view(np.uint32))
+
+
 def test_gemm_split_k_deterministic(cuda):
     """dW-shaped product that the planner splits over K: two runs, same bits."""
     M, Kd, N = 768, 8192, 768
