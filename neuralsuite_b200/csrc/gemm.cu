@@ -104,7 +104,7 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
   // Enough for any plan ns_gemm may pick (every kernel, both store orientations).
   size_t part = 0;
   for (bool wide : {true, false})
-    for (int force = -1; force <= 4; ++force)
+    for (int force = -1; force <= 5; ++force)
       for (int trans = 0; trans <= 1; ++trans) {
         if (!wide && force > 0) continue;
         const tc::Plan p = tc::plan(M, N, K, true, wide, force, trans);
@@ -114,7 +114,7 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine >= 0 && engine <= 7, "ns_gemm_set_engine: engine must be 0..7");
+  NS_REQUIRE(engine >= 0 && engine <= 8, "ns_gemm_set_engine: engine must be 0..8");
   t_engine = engine;
   return NS_OK;
 }
@@ -161,6 +161,7 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
                     : (t_engine == 4 || t_engine == 5) ? 1
                     : t_engine == 6 ? 3
                     : t_engine == 7 ? 4
+                    : t_engine == 8 ? 5
                                     : -1;
   // The wide kernels compute C^T (coalesced column stores); epilogues that
   // read the aux operand then run as a separate pass (tc::run).

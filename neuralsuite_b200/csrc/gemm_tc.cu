@@ -1287,6 +1287,7 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
     if (force_kind >= 0 && force_kind <= 2 && fk != force_kind) continue;
     if (force_kind == 3 && kind != 3) continue;  // pair tiles 256 x 192 only
     if (force_kind == 4 && kind != 4) continue;  // pair tiles 256 x 128 only
+    if (force_kind == 5 && kind != 2) continue;  // pair tiles 256 x 256 only
     const int bm = fk == 2 ? 256 : kBM;
     const int bn = kind == 0 ? 128 : kind == 3 ? 192 : kind == 4 ? 128 : 256;
     const int slots = fk == 2 ? sms / 2 : sms;  // concurrent units

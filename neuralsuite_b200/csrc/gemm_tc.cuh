@@ -27,7 +27,7 @@ struct Plan {
 // allow_wide: 128 x 256 tiles may be chosen (they need pre-split operands).
 // force_kind >= 0 restricts the choice to one kernel: 0 = 128 x 128,
 // 1 = 128 x 256, 2 = CTA-pair tiles of any width, 3 / 4 = pair tiles
-// 256 x 192 / 256 x 128 only (tests and profiling).
+// 256 x 192 / 256 x 128 only, 5 = pair tiles 256 x 256 only (tests and profiling).
 // trans_mode for the wide kernels: 1 = compute C^T (coalesced column stores),
 // 0 = compute C (row stores).
 Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind = -1,
