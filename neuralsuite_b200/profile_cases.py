@@ -3,6 +3,11 @@
     python -m neuralsuite_b200.profile_cases gemm M N K [a_trans b_trans reps [engine [epilogue]]]
     python -m neuralsuite_b200.profile_cases attn B T H D [reps [engine]]
     python -m neuralsuite_b200.profile_cases ln ROWS DIM [reps]
+    python -m neuralsuite_b200.profile_cases bw [M C V]
+
+`bw` runs each bandwidth-bound kernel of a GPT training step once at the
+step's shapes (M = B*T rows, C = width, V = vocab; default 8192 768 256) and
+prints the CUDA-event time and the algorithmic bytes of each launch.
 
 Each case allocates its operands once (seeded normal data), runs the kernel
 `reps` times on the current stream (default 3) and prints the CUDA-event time
@@ -81,6 +86,38 @@ def main(argv):
         f = _time(lambda: nk.layernorm_fwd(x, g, b), reps)
         bw = _time(lambda: nk.layernorm_bwd(x, x, g, m, r, dresid=x), reps)
         print(f"layernorm {rows}x{dim}: fwd {f:.4f} ms, bwd {bw:.4f} ms")
+    elif case == "bw":
+        M, C, V = (int(x) for x in argv[1:4]) if len(argv) > 3 else (8192, 768, 256)
+        F = 4 * C
+        r = lambda *shape: torch.randn(*shape, device=dev)
+        x, resid, raw = r(M, C), r(M, C), r(M, C)
+        g, b, bias = r(C), r(C), r(C)
+        dy3, pre3 = r(M, F), r(M, F)
+        dyq = r(M, 3 * C)
+        logits = r(M, V)
+        tgt = torch.randint(0, V, (M,), device=dev, dtype=torch.int32)
+        tok = torch.randint(0, V, (M // 1024, 1024), device=dev, dtype=torch.int32)
+        wte, wpe = r(V, C), r(1024, C)
+        P = 86_039_040
+        params, grads, m, v = r(P), r(P), torch.zeros(P, device=dev), torch.zeros(P, device=dev)
+        _, _, _, mean, rstd = nk.layernorm_fwd_ex(x, g, b)
+        B4 = 4  # bytes per float
+        cases = [
+            ("ln_fwd_ex (resid + LayerNorm + lo)", (5 * M * C + 2 * M) * B4,
+             lambda: nk.layernorm_fwd_ex(raw, g, b, bias=bias, resid=resid)),
+            ("ln_bwd (+ dresid)", 4 * M * C * B4, lambda: nk.layernorm_bwd(x, x, g, mean, rstd, dresid=resid)),
+            ("bias_grad_split N=3C", 2 * M * 3 * C * B4, lambda: nk.bias_grad_split(dyq)),
+            ("bias_grad_split_gelu N=4C", 4 * M * F * B4, lambda: nk.bias_grad_split_gelu(dy3, pre3)),
+            ("gelu_fwd_lo N=4C", 3 * M * F * B4, lambda: nk.gelu_fwd_lo(pre3)),
+            ("split_lo [M, C]", 2 * M * C * B4, lambda: nk.split_lo(x)),
+            ("cross_entropy", 2 * M * V * B4, lambda: nk.cross_entropy(logits, tgt)),
+            ("embedding_fwd", 2 * M * C * B4, lambda: nk.embedding_fwd(tok, wte, wpe)),
+            ("adamw_flat", 7 * P * B4, lambda: nk.adamw_flat(params, grads, m, v, [0, P], [0.0],
+                                                               3e-4, 0.9, 0.95, 1e-8, 0.1, 0.05)),
+        ]
+        for name, nbytes, fn in cases:
+            ms = _time(fn, 2)
+            print(f"{name:36s} {ms * 1000:8.1f} us  {nbytes / 1e6:8.1f} MB  {nbytes / ms / 1e6:7.0f} GB/s")
     else:
         raise SystemExit(__doc__)
     nk.kernel_health()
