@@ -140,8 +140,13 @@ __global__ void __launch_bounds__(256) ln_fwd_any(const float* __restrict__ x,
 //   xh = (x-m)*rs, dxh = dout*gamma, s1 = sum dxh, s2 = sum dxh*xh,
 //   dx = (rs/D) * (D*dxh - s1 - xh*s2)   [+ dresid]
 // and per-CTA partial column sums of dout*xh (dgamma) and dout (dbeta).
-template <int NV>
-__global__ void __launch_bounds__(256) ln_bwd_vec(
+// Each warp takes R of its rows at a time and issues all of their loads
+// (x, dout, dresid) before any arithmetic, so a row costs one memory latency
+// rather than two (dresid read after the row's reductions was the second); one
+// CTA per SM with the registers that takes.  Rows keep their order, so the
+// dgamma/dbeta partials are summed in the same order as one row at a time.
+template <int NV, int R>
+__global__ void __launch_bounds__(256, 1) ln_bwd_vec(
     const float* __restrict__ dout, const float* __restrict__ x, const float* __restrict__ gamma,
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
@@ -156,50 +161,75 @@ __global__ void __launch_bounds__(256) ln_bwd_vec(
   for (int i = 0; i < NV; ++i) pg[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float fdim = (float)dim;
-  for (int row = r0 + warp; row < r1; row += kRowsWarps) {
-    const float m = mean[row], rs = rstd[row];
-    const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * dim);
-    const float4* d4 = reinterpret_cast<const float4*>(dout + (size_t)row * dim);
-    float4 xh[NV], dh[NV];
-    float s1 = 0.f, s2 = 0.f;
+  for (int row0 = r0 + warp; row0 < r1; row0 += R * kRowsWarps) {
+    // Every load of the R rows first (x, dout, dresid), then the arithmetic.
+    float4 xv[R][NV], dv[R][NV], rv[R][NV];
+    float m[R], rs[R];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + i * 32;
-      if (c < nv) {
-        const float4 xv = x4[c], dv = d4[c], g = g4[c];
-        xh[i].x = __fmul_rn(__fsub_rn(xv.x, m), rs);
-        xh[i].y = __fmul_rn(__fsub_rn(xv.y, m), rs);
-        xh[i].z = __fmul_rn(__fsub_rn(xv.z, m), rs);
-        xh[i].w = __fmul_rn(__fsub_rn(xv.w, m), rs);
-        pg[i].x += dv.x * xh[i].x; pg[i].y += dv.y * xh[i].y;
-        pg[i].z += dv.z * xh[i].z; pg[i].w += dv.w * xh[i].w;
-        pb[i].x += dv.x; pb[i].y += dv.y; pb[i].z += dv.z; pb[i].w += dv.w;
-        dh[i].x = __fmul_rn(dv.x, g.x); dh[i].y = __fmul_rn(dv.y, g.y);
-        dh[i].z = __fmul_rn(dv.z, g.z); dh[i].w = __fmul_rn(dv.w, g.w);
-        s1 += (dh[i].x + dh[i].y) + (dh[i].z + dh[i].w);
-        s2 += (dh[i].x * xh[i].x + dh[i].y * xh[i].y) + (dh[i].z * xh[i].z + dh[i].w * xh[i].w);
+    for (int j = 0; j < R; ++j) {
+      const int row = row0 + j * kRowsWarps;
+      const bool in = row < r1;
+      m[j] = in ? mean[row] : 0.f;
+      rs[j] = in ? rstd[row] : 0.f;
+      const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+      const float4* d4 = reinterpret_cast<const float4*>(dout + (size_t)row * dim);
+      const float4* r4 = reinterpret_cast<const float4*>(dresid + (size_t)row * dim);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = lane + i * 32;
+        const bool ok = in && c < nv;
+        xv[j][i] = ok ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        dv[j][i] = ok ? d4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        rv[j][i] = (ok && dresid) ? r4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
-    const float scale = __fdiv_rn(rs, fdim);
-    float4* o4 = reinterpret_cast<float4*>(dx + (size_t)row * dim);
-    const float4* r4 = dresid ? reinterpret_cast<const float4*>(dresid + (size_t)row * dim) : nullptr;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + i * 32;
-      if (c < nv) {
-        float4 o;
-        o.x = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].x), s1), __fmul_rn(xh[i].x, s2)));
-        o.y = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].y), s1), __fmul_rn(xh[i].y, s2)));
-        o.z = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].z), s1), __fmul_rn(xh[i].z, s2)));
-        o.w = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh[i].w), s1), __fmul_rn(xh[i].w, s2)));
-        if (r4) {
-          const float4 rr = r4[c];
-          o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
-          o.z = __fadd_rn(rr.z, o.z); o.w = __fadd_rn(rr.w, o.w);
+    for (int j = 0; j < R; ++j) {
+      const int row = row0 + j * kRowsWarps;
+      if (row >= r1) break;
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = lane + i * 32;
+        if (c < nv) {
+          const float4 g = g4[c];
+          float4& xh = xv[j][i];
+          float4& dh = dv[j][i];
+          const float4 d = dh;
+          xh.x = __fmul_rn(__fsub_rn(xh.x, m[j]), rs[j]);
+          xh.y = __fmul_rn(__fsub_rn(xh.y, m[j]), rs[j]);
+          xh.z = __fmul_rn(__fsub_rn(xh.z, m[j]), rs[j]);
+          xh.w = __fmul_rn(__fsub_rn(xh.w, m[j]), rs[j]);
+          pg[i].x += d.x * xh.x; pg[i].y += d.y * xh.y;
+          pg[i].z += d.z * xh.z; pg[i].w += d.w * xh.w;
+          pb[i].x += d.x; pb[i].y += d.y; pb[i].z += d.z; pb[i].w += d.w;
+          dh.x = __fmul_rn(d.x, g.x); dh.y = __fmul_rn(d.y, g.y);
+          dh.z = __fmul_rn(d.z, g.z); dh.w = __fmul_rn(d.w, g.w);
+          s1 += (dh.x + dh.y) + (dh.z + dh.w);
+          s2 += (dh.x * xh.x + dh.y * xh.y) + (dh.z * xh.z + dh.w * xh.w);
         }
-        o4[c] = o;
+      }
+      s1 = warp_sum(s1);
+      s2 = warp_sum(s2);
+      const float scale = __fdiv_rn(rs[j], fdim);
+      float4* o4 = reinterpret_cast<float4*>(dx + (size_t)row * dim);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = lane + i * 32;
+        if (c < nv) {
+          const float4 xh = xv[j][i], dh = dv[j][i];
+          float4 o;
+          o.x = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh.x), s1), __fmul_rn(xh.x, s2)));
+          o.y = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh.y), s1), __fmul_rn(xh.y, s2)));
+          o.z = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh.z), s1), __fmul_rn(xh.z, s2)));
+          o.w = __fmul_rn(scale, __fsub_rn(__fsub_rn(__fmul_rn(fdim, dh.w), s1), __fmul_rn(xh.w, s2)));
+          if (dresid) {
+            const float4 rr = rv[j][i];
+            o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
+            o.z = __fadd_rn(rr.z, o.z); o.w = __fadd_rn(rr.w, o.w);
+          }
+          o4[c] = o;
+        }
       }
     }
   }
@@ -323,11 +353,16 @@ __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ p
 // split of y, compact), so the bias gradient of dY costs no extra read.
 // With GELU, y is first replaced in place by y * gelu'(pre) (GeluBackward on
 // the way in: the column sums, the lo part and y itself are of the product).
+// The last CTA of each 128-column block (counted in `done`, zeroed before
+// the launch) then sums that block's partials into out, in colsum_finish's
+// order (the same result as the two-launch form), instead of a second launch.
 template <bool LO, bool GELU>
 __global__ void __launch_bounds__(256) colsum_partial(float* __restrict__ y, int M, int N,
                                                       int rows_per_cta, float* __restrict__ part,
                                                       float* __restrict__ lo,
-                                                      const float* __restrict__ pre) {
+                                                      const float* __restrict__ pre,
+                                                      int* __restrict__ done,
+                                                      float* __restrict__ out) {
   __shared__ float4 red[kRowsWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = (blockIdx.x * 32 + lane) * 4;
@@ -394,6 +429,39 @@ __global__ void __launch_bounds__(256) colsum_partial(float* __restrict__ y, int
     if (col + 1 < N) o[1] = t.y;
     if (col + 2 < N) o[2] = t.z;
     if (col + 3 < N) o[3] = t.w;
+  }
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(done + blockIdx.x, 1) == (int)gridDim.y - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // Warp w sums partial rows w, w+8, ... (ascending), then the eight warp sums
+  // are added in warp order: colsum_finish's order, per column.
+  const int n_part = (int)gridDim.y;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col < N) {
+    for (int q = warp; q < n_part; q += kRowsWarps) {
+      const float* r = part + (size_t)q * N + col;
+      a.x += __ldcg(r);
+      if (col + 1 < N) a.y += __ldcg(r + 1);
+      if (col + 2 < N) a.z += __ldcg(r + 2);
+      if (col + 3 < N) a.w += __ldcg(r + 3);
+    }
+  }
+  red[warp][lane] = a;
+  __syncthreads();
+  if (warp == 0 && col < N) {
+    float4 t = red[0][lane];
+    for (int w = 1; w < kRowsWarps; ++w) {
+      const float4 u = red[w][lane];
+      t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+    }
+    out[col] = t.x;
+    if (col + 1 < N) out[col + 1] = t.y;
+    if (col + 2 < N) out[col + 2] = t.z;
+    if (col + 3 < N) out[col + 3] = t.w;
   }
 }
 
@@ -497,29 +565,29 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
     const int nv = dim / 4;
     const size_t smem = (size_t)kRowsWarps * 2 * dim * sizeof(float);
     if (nv <= 32)
-      ln_bwd_vec<1><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<1, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     else if (nv <= 64)
-      ln_bwd_vec<2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<2, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     else if (nv <= 96)
-      ln_bwd_vec<3><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<3, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     else if (nv <= 128) {
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<4><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<4, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     } else if (nv <= 192) {
       // dim <= 768: six float4 per lane, not eight (registers decide occupancy here)
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<6>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<6, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<6><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<6, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     } else {
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<8><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+      ln_bwd_vec<8, 1><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     }
   } else {
@@ -533,7 +601,9 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
 
 size_t ns_bias_grad_workspace_size(int M, int N) {
   if (M <= 0 || N <= 0) return 0;
-  return (size_t)bias_chunks(M, N) * N * sizeof(float);
+  // partials, then one completion counter per 128-column block
+  const size_t part = ((size_t)bias_chunks(M, N) * N * sizeof(float) + 255) & ~(size_t)255;
+  return part + (size_t)ceil_div(N, 128) * sizeof(int);
 }
 
 ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace,
@@ -551,10 +621,11 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<false, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, nullptr, nullptr);
-  { ns_status _rc = check_launch("ns_bias_grad stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
-  return check_launch("ns_bias_grad stage 2");
+  int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                     (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
+  NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad counters");
+  colsum_partial<false, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, nullptr, nullptr, done, db);
+  return check_launch("ns_bias_grad");
 }
 
 ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy_lo,
@@ -568,10 +639,11 @@ ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<true, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, dy_lo, nullptr);
-  { ns_status _rc = check_launch("ns_bias_grad_split stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
-  return check_launch("ns_bias_grad_split stage 2");
+  int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                     (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
+  NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad_split counters");
+  colsum_partial<true, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, dy_lo, nullptr, done, db);
+  return check_launch("ns_bias_grad_split");
 }
 
 ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, float* db, float* dy_lo,
@@ -587,10 +659,11 @@ ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, flo
   const int chunks = bias_chunks(M, N);
   const int rpc = ceil_div(M, chunks);
   float* part = static_cast<float*>(workspace);
-  colsum_partial<true, true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo, pre);
-  { ns_status _rc = check_launch("ns_bias_grad_split_gelu stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<ceil_div(N, 32), 256, 0, s>>>(part, chunks, N, db, nullptr, nullptr);
-  return check_launch("ns_bias_grad_split_gelu stage 2");
+  int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                     (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
+  NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad_split_gelu counters");
+  colsum_partial<true, true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo, pre, done, db);
+  return check_launch("ns_bias_grad_split_gelu");
 }
 
 }  // extern "C"
