@@ -161,9 +161,12 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_k(const float* __restrict__
 // Delta[bh, r] = sum_d dO[b, r, h*D + d] * O[b, r, h*D + d]: one warp per
 // (b, r) row of all heads, lanes striding the C columns (coalesced), each
 // head's D products summed by its lanes with shuffles.
+// With dout_lo, the pass also writes dout's tf32 lo part (the tensor-core
+// backward's operand split of dO) from the same loads.
 __global__ void __launch_bounds__(256) attn_delta_k(const float* __restrict__ out,
                                                     const float* __restrict__ dout, int B, int T,
-                                                    int H, int D, float* __restrict__ delta) {
+                                                    int H, int D, float* __restrict__ delta,
+                                                    float* __restrict__ dout_lo) {
   const int64_t row = blockIdx.x * 8 + (threadIdx.x >> 5);  // b * T + r
   const int lane = threadIdx.x & 31;
   if (row >= (int64_t)B * T) return;
@@ -175,14 +178,22 @@ __global__ void __launch_bounds__(256) attn_delta_k(const float* __restrict__ ou
     // lanes cover 32 consecutive columns of one head per step
     for (int h = 0; h < H; ++h) {
       float s = 0.0f;
-      for (int d = lane; d < D; d += 32) s = fmaf(g[h * D + d], o[h * D + d], s);
+      for (int d = lane; d < D; d += 32) {
+        const float gv = g[h * D + d];
+        s = fmaf(gv, o[h * D + d], s);
+        if (dout_lo) dout_lo[row * C + h * D + d] = gv - __uint_as_float(__float_as_uint(gv) & 0xFFFFE000u);
+      }
       s = warp_sum(s);
       if (lane == 0) delta[((size_t)b * H + h) * T + r] = s;
     }
   } else {
     for (int h = lane; h < H; h += 32) {
       float s = 0.0f;
-      for (int d = 0; d < D; ++d) s = fmaf(g[h * D + d], o[h * D + d], s);
+      for (int d = 0; d < D; ++d) {
+        const float gv = g[h * D + d];
+        s = fmaf(gv, o[h * D + d], s);
+        if (dout_lo) dout_lo[row * C + h * D + d] = gv - __uint_as_float(__float_as_uint(gv) & 0xFFFFE000u);
+      }
       delta[((size_t)b * H + h) * T + r] = s;
     }
   }
@@ -507,13 +518,17 @@ ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out
   cudaStream_t s = as_stream(stream);
   float* delta = static_cast<float*>(workspace);
   const int64_t n = (int64_t)B * H * T;
-  attn_delta_k<<<(unsigned)ceil_div64((int64_t)B * T, 8), 256, 0, s>>>(out, dout, B, T, H, D, delta);
-  { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
   const size_t delta_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
   float* lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + delta_bytes);
-  if (t_attn_engine == 0 && (D == 32 || D == 64) && (reinterpret_cast<uintptr_t>(lo) & 15) == 0 &&
-      attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D))
-    return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, s);
+  const bool tc = t_attn_engine == 0 && (D == 32 || D == 64) &&
+                  (reinterpret_cast<uintptr_t>(lo) & 15) == 0 &&
+                  attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D);
+  // The tensor-core path takes dO's lo part from the Delta pass.
+  float* dout_lo = tc ? attn_tc::bwd_dout_lo(lo, B, T, H, D) : nullptr;
+  attn_delta_k<<<(unsigned)ceil_div64((int64_t)B * T, 8), 256, 0, s>>>(out, dout, B, T, H, D, delta,
+                                                                     dout_lo);
+  { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
+  if (tc) return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, s);
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 32) return launch_bwd<32>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 64) return launch_bwd<64>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

@@ -1257,7 +1257,7 @@ ns_status launch_bwd(const float* qkv, const float* qkv_lo_in, const float* dout
   ns_status rc = NS_OK;
   if (!qkv_lo_in) rc = split_rows(qkv, rows, 3 * C, qkv_lo_ws, s);
   const float* qkv_lo = qkv_lo_in ? qkv_lo_in : qkv_lo_ws;
-  if (rc == NS_OK) rc = split_rows(dout, rows, C, dout_lo, s);
+
   if (rc != NS_OK) return rc;
   // qkv and dout (and their lo copies), each as a K-major and an MN-major map.
   CUtensorMap qk, qmn, qlk, qlmn, dk, dmn, dlk, dlmn;
@@ -1322,6 +1322,10 @@ bool bwd_supported(const float* qkv, const float* dout, const float* dqkv, int B
 
 size_t bwd_lo_bytes(int B, int T, int H, int D) {
   return (size_t)B * T * 4 * H * D * sizeof(float);
+}
+
+float* bwd_dout_lo(float* lo, int B, int T, int H, int D) {
+  return lo + (size_t)B * T * 3 * H * D;
 }
 
 ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const float* lse,

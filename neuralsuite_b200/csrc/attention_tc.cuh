@@ -27,9 +27,14 @@ bool bwd_supported(const float* qkv, const float* dout, const float* dqkv, int B
 // Bytes of the lo-part copies of qkv and dout the tensor-core backward needs.
 size_t bwd_lo_bytes(int B, int T, int H, int D);
 
+// Where in `lo` (bwd_lo_bytes) bwd expects dout's tf32 lo part, which the
+// caller writes beforehand (with Delta).
+float* bwd_dout_lo(float* lo, int B, int T, int H, int D);
+
 // dqkv from qkv, dout, lse and delta (= rowsum(dout * out)); `lo` holds
-// bwd_lo_bytes, 16-byte aligned.  qkv_lo (optional): the tf32 lo part of qkv,
-// which is then not split again.
+// bwd_lo_bytes, 16-byte aligned, with dout's lo part already at
+// bwd_dout_lo(lo).  qkv_lo (optional): the tf32 lo part of qkv, which is then
+// not split again.
 ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const float* lse,
               const float* delta, int B, int T, int H, int D, float* dqkv, float* lo,
               cudaStream_t s);
