@@ -21,8 +21,6 @@ constexpr int kMaxVec = 8;             // float4 per lane => dim <= 1024 on the 
 // RES: the row is first formed as x = resid + (raw + bias) (the residual add
 // of a GEMM's bias epilogue, same rounding) and written to x_out.  LO: the
 // output's tf32 lo part goes to out_lo as well (the next GEMM's operand split).
-// Each warp takes two consecutive rows and issues both rows' loads before the
-// reductions (the pass is memory-latency bound).
 template <int NV, bool RES, bool LO>
 __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias x_out
                                                   const float* __restrict__ gamma,
@@ -32,85 +30,64 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias 
                                                   float eps, const float* __restrict__ bias,
                                                   const float* __restrict__ resid, float* x_out,
                                                   float* __restrict__ out_lo) {
-  constexpr int R = 2;
-  const int row0 = (blockIdx.x * kRowsWarps + (threadIdx.x >> 5)) * R;
+  const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row0 >= rows) return;
+  if (row >= rows) return;
   const int nv = dim >> 2;
-  float4 v[R][NV];
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+  float4 v[NV];
+  float s = 0.0f;
 #pragma unroll
-  for (int j = 0; j < R; ++j) {
-    const int row = row0 + j;
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    v[i] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (RES && c < nv) {
+      const float4 r = reinterpret_cast<const float4*>(resid + (size_t)row * dim)[c];
+      const float4 b = reinterpret_cast<const float4*>(bias)[c];
+      v[i].x = __fadd_rn(r.x, __fadd_rn(v[i].x, b.x));
+      v[i].y = __fadd_rn(r.y, __fadd_rn(v[i].y, b.y));
+      v[i].z = __fadd_rn(r.z, __fadd_rn(v[i].z, b.z));
+      v[i].w = __fadd_rn(r.w, __fadd_rn(v[i].w, b.w));
+      reinterpret_cast<float4*>(x_out + (size_t)row * dim)[c] = v[i];
+    }
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  s = warp_sum(s);
+  const float m = __fdiv_rn(s, (float)dim);
+  float q = 0.0f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + i * 32;
-      v[j][i] = (row < rows && c < nv) ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nv) {
+      const float a = v[i].x - m, b = v[i].y - m, cc = v[i].z - m, d = v[i].w - m;
+      q += (a * a + b * b) + (cc * cc + d * d);
     }
   }
-  if (RES) {
-#pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const int row = row0 + j;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int c = lane + i * 32;
-        if (row < rows && c < nv) {
-          const float4 r = reinterpret_cast<const float4*>(resid + (size_t)row * dim)[c];
-          const float4 b = reinterpret_cast<const float4*>(bias)[c];
-          v[j][i].x = __fadd_rn(r.x, __fadd_rn(v[j][i].x, b.x));
-          v[j][i].y = __fadd_rn(r.y, __fadd_rn(v[j][i].y, b.y));
-          v[j][i].z = __fadd_rn(r.z, __fadd_rn(v[j][i].z, b.z));
-          v[j][i].w = __fadd_rn(r.w, __fadd_rn(v[j][i].w, b.w));
-          reinterpret_cast<float4*>(x_out + (size_t)row * dim)[c] = v[j][i];
-        }
-      }
-    }
+  q = warp_sum(q);
+  const float var = __fdiv_rn(q, (float)dim);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(var + eps));
+  if (lane == 0) {
+    mean[row] = m;
+    rstd[row] = rs;
   }
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float4* b4 = reinterpret_cast<const float4*>(beta);
+  float4* o4 = reinterpret_cast<float4*>(out + (size_t)row * dim);
 #pragma unroll
-  for (int j = 0; j < R; ++j) {
-    const int row = row0 + j;
-    if (row >= rows) break;
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) s += (v[j][i].x + v[j][i].y) + (v[j][i].z + v[j][i].w);
-    s = warp_sum(s);
-    const float m = __fdiv_rn(s, (float)dim);
-    float q = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + i * 32;
-      if (c < nv) {
-        const float a = v[j][i].x - m, b = v[j][i].y - m, cc = v[j][i].z - m, d = v[j][i].w - m;
-        q += (a * a + b * b) + (cc * cc + d * d);
-      }
-    }
-    q = warp_sum(q);
-    const float var = __fdiv_rn(q, (float)dim);
-    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(var + eps));
-    if (lane == 0) {
-      mean[row] = m;
-      rstd[row] = rs;
-    }
-    float4* o4 = reinterpret_cast<float4*>(out + (size_t)row * dim);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + i * 32;
-      if (c < nv) {
-        const float4 g = g4[c], bb = b4[c];
-        float4 r;
-        r.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][i].x, m), rs), g.x), bb.x);
-        r.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][i].y, m), rs), g.y), bb.y);
-        r.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][i].z, m), rs), g.z), bb.z);
-        r.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][i].w, m), rs), g.w), bb.w);
-        o4[c] = r;
-        if (LO) {
-          auto lo = [](float a) { return a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u); };
-          reinterpret_cast<float4*>(out_lo + (size_t)row * dim)[c] =
-              make_float4(lo(r.x), lo(r.y), lo(r.z), lo(r.w));
-        }
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nv) {
+      const float4 g = g4[c], bb = b4[c];
+      float4 r;
+      r.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].x, m), rs), g.x), bb.x);
+      r.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].y, m), rs), g.y), bb.y);
+      r.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].z, m), rs), g.z), bb.z);
+      r.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i].w, m), rs), g.w), bb.w);
+      o4[c] = r;
+      if (LO) {
+        auto lo = [](float a) { return a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u); };
+        reinterpret_cast<float4*>(out_lo + (size_t)row * dim)[c] =
+            make_float4(lo(r.x), lo(r.y), lo(r.z), lo(r.w));
       }
     }
   }
@@ -527,17 +504,16 @@ ns_status ns_layernorm_fwd_ex(const float* x, const float* bias, const float* re
                         15) == 0;
   if (dim % 4 == 0 && aligned && dim <= 128 * kMaxVec) {
     const int nv = dim / 4;
-    const dim3 vgrid(ceil_div(rows, 2 * kRowsWarps));  // two rows per warp
     auto go = [&](auto nvt) {
       constexpr int NV = decltype(nvt)::value;
       if (resid && out_lo)
-        ln_fwd_vec<NV, true, true><<<vgrid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+        ln_fwd_vec<NV, true, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
       else if (resid)
-        ln_fwd_vec<NV, true, false><<<vgrid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+        ln_fwd_vec<NV, true, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
       else if (out_lo)
-        ln_fwd_vec<NV, false, true><<<vgrid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+        ln_fwd_vec<NV, false, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
       else
-        ln_fwd_vec<NV, false, false><<<vgrid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+        ln_fwd_vec<NV, false, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
     };
     if (nv <= 32) go(std::integral_constant<int, 1>());
     else if (nv <= 64) go(std::integral_constant<int, 2>());
