@@ -1,9 +1,10 @@
 // K5: AdamW over every parameter tensor in one launch (AdamW::Step,
 // include/optimizers.h:206-234).  Parameters, gradients and both moments are
-// flat buffers in registration order; the host cuts them into chunks of at
-// most kChunk elements that never straddle a tensor, and passes the chunk
-// table by value (kernel parameter space), so one CTA = one chunk with a
-// uniform weight decay.  28 bytes of HBM traffic per parameter.
+// flat buffers in registration order; the segment table (tensor boundaries and
+// each tensor's weight decay) travels by value in kernel parameter space.  The
+// launch is one wave of CTAs, each given an equal share of the elements (its
+// range may cross tensor boundaries), so no CTA starts late and none idles:
+// the pass runs at the copy bandwidth.  28 bytes of HBM traffic per parameter.
 #include <algorithm>
 #include <vector>
 
@@ -12,17 +13,13 @@
 namespace nsb {
 namespace {
 
-constexpr int kMaxChunks = 512;      // per launch: 512 x 16 B of kernel parameters
-constexpr int64_t kChunk = 1 << 17;  // elements per CTA
-
-struct AdamChunk {
-  int64_t start;
-  int32_t len;
-  float decay;
-};
+constexpr int kMaxSegs = 512;  // tensors per launch: 512 x 12 B of kernel parameters
 
 struct AdamTable {
-  AdamChunk c[kMaxChunks];
+  int n;                       // segments in this launch
+  int64_t per;                 // elements per CTA
+  int64_t off[kMaxSegs + 1];   // segment t = [off[t], off[t + 1])
+  float decay[kMaxSegs];
 };
 
 // The update, with every multiply/add rounded separately as in the reference.
@@ -43,21 +40,16 @@ struct AdamHyper {
   float lr, b1, b2, eps, bc1, bc2;
 };
 
-__global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __restrict__ P,
-                                               const float* __restrict__ G, float* __restrict__ M,
-                                               float* __restrict__ V, AdamHyper hp) {
-  float lr = hp.lr, b1 = hp.b1, b2 = hp.b2, eps = hp.eps, bc1 = hp.bc1, bc2 = hp.bc2;
-  if (hp.dev) {
-    lr = hp.dev[0]; b1 = hp.dev[1]; b2 = hp.dev[2]; eps = hp.dev[3]; bc1 = hp.dev[4]; bc2 = hp.dev[5];
-  }
-  const AdamChunk ch = tab.c[blockIdx.x];
-  const int64_t s = ch.start;
-  const int n = ch.len;
-  // Scalar head up to a 16-byte boundary, float4 body, scalar tail.
+// One piece [s, s + n) of one tensor: scalar head up to a 16-byte boundary,
+// float4 body, scalar tail.
+__device__ __forceinline__ void adam_piece(int64_t s, int n, float decay, float* __restrict__ P,
+                                           const float* __restrict__ G, float* __restrict__ M,
+                                           float* __restrict__ V, float lr, float b1, float b2,
+                                           float eps, float bc1, float bc2) {
   const int head = min(n, (int)((4 - (s & 3)) & 3));
   for (int i = threadIdx.x; i < head; i += blockDim.x) {
     float p = P[s + i], m = M[s + i], v = V[s + i];
-    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, decay);
     P[s + i] = p; M[s + i] = m; V[s + i] = v;
   }
   const int body4 = (n - head) >> 2;
@@ -68,16 +60,40 @@ __global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __res
   for (int i = threadIdx.x; i < body4; i += blockDim.x) {
     float4 p = P4[i], m = M4[i], v = V4[i];
     const float4 g = G4[i];
-    adam_one(p.x, g.x, m.x, v.x, lr, b1, b2, eps, bc1, bc2, ch.decay);
-    adam_one(p.y, g.y, m.y, v.y, lr, b1, b2, eps, bc1, bc2, ch.decay);
-    adam_one(p.z, g.z, m.z, v.z, lr, b1, b2, eps, bc1, bc2, ch.decay);
-    adam_one(p.w, g.w, m.w, v.w, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p.x, g.x, m.x, v.x, lr, b1, b2, eps, bc1, bc2, decay);
+    adam_one(p.y, g.y, m.y, v.y, lr, b1, b2, eps, bc1, bc2, decay);
+    adam_one(p.z, g.z, m.z, v.z, lr, b1, b2, eps, bc1, bc2, decay);
+    adam_one(p.w, g.w, m.w, v.w, lr, b1, b2, eps, bc1, bc2, decay);
     P4[i] = p; M4[i] = m; V4[i] = v;
   }
   for (int i = head + body4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
     float p = P[s + i], m = M[s + i], v = V[s + i];
-    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, ch.decay);
+    adam_one(p, G[s + i], m, v, lr, b1, b2, eps, bc1, bc2, decay);
     P[s + i] = p; M[s + i] = m; V[s + i] = v;
+  }
+}
+
+__global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __restrict__ P,
+                                               const float* __restrict__ G, float* __restrict__ M,
+                                               float* __restrict__ V, AdamHyper hp) {
+  float lr = hp.lr, b1 = hp.b1, b2 = hp.b2, eps = hp.eps, bc1 = hp.bc1, bc2 = hp.bc2;
+  if (hp.dev) {
+    lr = hp.dev[0]; b1 = hp.dev[1]; b2 = hp.dev[2]; eps = hp.dev[3]; bc1 = hp.dev[4]; bc2 = hp.dev[5];
+  }
+  const int64_t end = tab.off[tab.n];
+  const int64_t lo = tab.off[0] + tab.per * blockIdx.x;
+  const int64_t hi = min(end, lo + tab.per);
+  if (lo >= hi) return;
+  // First segment that ends after lo (segments may be empty).
+  int a = 0, b = tab.n - 1;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    if (tab.off[mid + 1] > lo) b = mid; else a = mid + 1;
+  }
+  for (int t = a; t < tab.n && tab.off[t] < hi; ++t) {
+    const int64_t s = max(lo, tab.off[t]);
+    const int64_t e = min(hi, tab.off[t + 1]);
+    if (e > s) adam_piece(s, (int)(e - s), tab.decay[t], P, G, M, V, lr, b1, b2, eps, bc1, bc2);
   }
 }
 
@@ -119,28 +135,34 @@ ns_status adamw_run(float* params, const float* grads, float* m, float* v, int64
              "ns_adamw_flat: buffers must be 16-byte aligned");
   NS_REQUIRE(host_seg_offsets[0] >= 0 && host_seg_offsets[n_seg] <= n_total,
              "ns_adamw_flat: segments exceed the buffer");
-  AdamTable tab;
-  int used = 0;
-  auto flush = [&]() -> ns_status {
-    if (used == 0) return NS_OK;
-    adamw_k<<<used, 256, 0, s>>>(tab, params, grads, m, v, hp);
-    used = 0;
-    return check_launch("ns_adamw_flat");
-  };
-  for (int t = 0; t < n_seg; ++t) {
-    const int64_t a = host_seg_offsets[t], b = host_seg_offsets[t + 1];
-    NS_REQUIRE(b >= a, "ns_adamw_flat: segment offsets must be ascending");
-    for (int64_t st = a; st < b; st += kChunk) {
-      tab.c[used].start = st;
-      tab.c[used].len = (int32_t)std::min<int64_t>(kChunk, b - st);
-      tab.c[used].decay = host_seg_decay[t];
-      if (++used == kMaxChunks) {
-        ns_status rc = flush();
-        if (rc != NS_OK) return rc;
-      }
-    }
+  for (int t = 0; t < n_seg; ++t)
+    NS_REQUIRE(host_seg_offsets[t + 1] >= host_seg_offsets[t],
+               "ns_adamw_flat: segment offsets must be ascending");
+  // One wave: as many CTAs as fit on the GPU at once, each with an equal
+  // share (a multiple of 1024 elements) of the launch's range.
+  static int waves_cta = 0;
+  if (waves_cta == 0) {
+    int per_sm = 0;
+    NS_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_k, 256, 0),
+                "ns_adamw_flat occupancy");
+    waves_cta = std::max(1, per_sm) * sm_count();
   }
-  return flush();
+  AdamTable tab;
+  for (int t0 = 0; t0 < n_seg; t0 += kMaxSegs) {
+    const int n = std::min(kMaxSegs, n_seg - t0);
+    tab.n = n;
+    for (int t = 0; t <= n; ++t) tab.off[t] = host_seg_offsets[t0 + t];
+    for (int t = 0; t < n; ++t) tab.decay[t] = host_seg_decay[t0 + t];
+    const int64_t len = tab.off[n] - tab.off[0];
+    if (len == 0) continue;
+    const int64_t per = std::max<int64_t>(1024, (len + waves_cta - 1) / waves_cta + 1023) & ~int64_t(1023);
+    tab.per = per;
+    const int grid = (int)((len + per - 1) / per);
+    adamw_k<<<grid, 256, 0, s>>>(tab, params, grads, m, v, hp);
+    ns_status rc = check_launch("ns_adamw_flat");
+    if (rc != NS_OK) return rc;
+  }
+  return NS_OK;
 }
 }  // namespace
 }  // namespace nsb

@@ -753,8 +753,9 @@ __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int 
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (vec) {
     const int c4 = cols >> 2;
+    const bool dense = ld == cols;  // contiguous rows: no row/column split of the index
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total / 4; i += stride) {
-      const int64_t r = i / c4, c = (i % c4) * 4;
+      const int64_t r = dense ? 0 : i / c4, c = dense ? i * 4 : (i % c4) * 4;
       const float4 v = *reinterpret_cast<const float4*>(x + r * ld + c);
       float4 o;
       o.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);

@@ -22,7 +22,9 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -125,10 +127,15 @@ class Parameter {
     value_ = Tensor(value, dims_);
     grad_ = Tensor(grad, dims_);
   }
+  // The value's tf32 lo part, kept by the owning model (refreshed at the
+  // start of every forward pass); nullptr when no model keeps one.
+  void BindLo(const float* lo) { lo_ = lo; }
+  const float* Lo() const { return lo_; }
 
  private:
   std::vector<int> dims_;
   Tensor value_, grad_;
+  const float* lo_ = nullptr;
 };
 
 // Execution context shared by the layers of one model: stream + scratch.
@@ -258,6 +265,12 @@ class Linear : public Layer {
   // products, dY the dX and dW products: each is split once (ns_split_lo)
   // and the copy passed to every product that reads it (ns_gemm_lo).
   bool SplitOk() const { return in_ % 4 == 0 && out_ % 4 == 0; }
+  // W's lo part kept by the owning model, when there is one the GEMM can read
+  // (16-byte aligned); otherwise the layer splits W itself.
+  const float* WeightLo() const {
+    const float* lo = weight_.Lo();
+    return (lo && (reinterpret_cast<uintptr_t>(lo) & 15) == 0) ? lo : nullptr;
+  }
 
   Tensor Run(const Tensor& x, int epi, const float* aux, float* aux_out,
              const float* x_lo_in = nullptr, float* out_lo = nullptr) {
@@ -268,9 +281,13 @@ class Linear : public Layer {
     const float* x_lo = nullptr;
     const float* w_lo = nullptr;
     if (SplitOk()) {
-      Tensor wl = Scratch(w_lo_buf_, in_, out_);
-      Check(ns_split_lo(weight_.Value().Data(), in_, out_, out_, wl.Data(), stream()));
-      w_lo = wl.Data();
+      if (WeightLo()) {
+        w_lo = WeightLo();
+      } else {
+        Tensor wl = Scratch(w_lo_buf_, in_, out_);
+        Check(ns_split_lo(weight_.Value().Data(), in_, out_, out_, wl.Data(), stream()));
+        w_lo = wl.Data();
+      }
       if (x_lo_in) {
         x_lo = x_lo_in;
       } else {
@@ -295,7 +312,7 @@ class Linear : public Layer {
     // The lo copies of X and W made (or taken) by the forward pass are still current.
     const bool lo = SplitOk();
     const float* x_lo = lo ? last_x_lo_ : nullptr;
-    const float* w_lo = lo ? w_lo_buf_.Data() : nullptr;
+    const float* w_lo = lo ? (WeightLo() ? WeightLo() : w_lo_buf_.Data()) : nullptr;
     const float* dy_lo = nullptr;
     if (lo) {
       // db and dY's lo part from one pass over dY (with the GELU backward).
@@ -652,8 +669,13 @@ class GPTModel : public Module {
     values_ = std::make_shared<DeviceBuffer>(total * sizeof(float));
     grads_ = std::make_shared<DeviceBuffer>(total * sizeof(float));
     CheckCuda(cudaMemset(grads_->get(), 0, total * sizeof(float)), "cudaMemset");
-    for (size_t i = 0; i < params.size(); ++i)
+    // The values' tf32 lo parts, one flat copy split in one pass at the start
+    // of every forward (instead of one split per weight per product).
+    values_lo_ = std::make_shared<DeviceBuffer>(total * sizeof(float));
+    for (size_t i = 0; i < params.size(); ++i) {
       params[i]->Bind(Values() + offsets_[i], Grads() + offsets_[i]);
+      params[i]->BindLo(static_cast<const float*>(values_lo_->get()) + offsets_[i]);
+    }
     // One scratch area sized for the largest workspace any kernel of the step needs.
     const int M = max_batch * cfg.block_size, C = cfg.n_embd, V = cfg.vocab_size;
     size_t ws = 0;
@@ -708,6 +730,13 @@ class GPTModel : public Module {
     CheckCuda(cudaMemcpyAsync(tokens_->get(), tokens, (size_t)M * sizeof(int32_t),
                               cudaMemcpyDeviceToDevice, Stream()),
               "token copy");
+    // Parameter lo parts for this pass (the values may have changed since the
+    // last one: optimizer step, broadcast, or a write through ns_gpt_params).
+    constexpr int64_t kSplitChunk = int64_t(1) << 30;
+    for (int64_t o = 0; o < NumParams(); o += kSplitChunk) {
+      const int n = (int)std::min(kSplitChunk, NumParams() - o);
+      Check(ns_split_lo(Values() + o, 1, n, n, static_cast<float*>(values_lo_->get()) + o, Stream()));
+    }
     Tensor x = x0_.View({B, T, C});
     Check(ns_embedding_fwd(Tokens(), B, T, wte_.WeightParam().Value().Data(), config_.vocab_size,
                            wpe_.WeightParam().Value().Data(), config_.block_size, C, x.Data(),
@@ -716,9 +745,10 @@ class GPTModel : public Module {
     xf_ = ln_f_.Forward(x).View({M, C});
     // logits = x_2d . wte^T (gpt.h:226-228): wte read as a K-major operand, no transpose copy.
     logits_ = Scratch(logits_buf_, M, config_.vocab_size);
-    Check(ns_gemm(M, config_.vocab_size, C, xf_.Data(), C, 0, wte_.WeightParam().Value().Data(), C,
-                  1, logits_.Data(), config_.vocab_size, 0.0f, NS_EPI_STORE, nullptr, nullptr,
-                  nullptr, ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
+    Check(ns_gemm_lo(M, config_.vocab_size, C, xf_.Data(), C, 0, nullptr,
+                     wte_.WeightParam().Value().Data(), C, 1, WteLo(), logits_.Data(),
+                     config_.vocab_size, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
+                     ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
     return logits_;
   }
 
@@ -736,9 +766,9 @@ class GPTModel : public Module {
     Tensor dlogits = criterion_.Backward();
     // dx = dlogits . wte  (wte read N-major in place)
     Tensor dx = Scratch(dx_head_, M, C);
-    Check(ns_gemm(M, C, V, dlogits.Data(), V, 0, wte_.WeightParam().Value().Data(), C, 0, dx.Data(),
-                  C, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ctx_storage_.scratch,
-                  ctx_storage_.scratch_bytes, Stream()));
+    Check(ns_gemm_lo(M, C, V, dlogits.Data(), V, 0, nullptr, wte_.WeightParam().Value().Data(), C,
+                     0, WteLo(), dx.Data(), C, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
+                     ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
     // head term of the tied wte gradient, dlogits^T . x, written first (the
     // embedding backward adds its own sum to it at the end, gpt.h:262-269).
     Check(ns_gemm(V, C, M, dlogits.Data(), V, 1, xf_.Data(), C, 0,
@@ -763,6 +793,13 @@ class GPTModel : public Module {
   int32_t* Tokens() { return static_cast<int32_t*>(tokens_->get()); }
 
  private:
+  // wte's lo part for the tied head's products (it needs C % 4 == 0 and a
+  // 16-byte aligned start; otherwise the GEMM splits wte itself).
+  const float* WteLo() {
+    const float* lo = wte_.WeightParam().Lo();
+    return (config_.n_embd % 4 == 0 && (reinterpret_cast<uintptr_t>(lo) & 15) == 0) ? lo : nullptr;
+  }
+
   GPTConfig config_;
   int max_batch_;
   Embedding wte_, wpe_;
@@ -771,7 +808,7 @@ class GPTModel : public Module {
   CrossEntropyLoss criterion_;
   std::vector<int64_t> offsets_;
   std::vector<int> ranks_;
-  std::shared_ptr<DeviceBuffer> values_, grads_, scratch_, small_, tokens_;
+  std::shared_ptr<DeviceBuffer> values_, grads_, values_lo_, scratch_, small_, tokens_;
   Context ctx_storage_;
   Tensor x0_, xf_, logits_, logits_buf_, dx_head_;
   int B_ = 0, T_ = 0;

@@ -494,6 +494,33 @@ def test_adamw_bit_exact(cuda, port):
     assert np.array_equal(host(vd).view(np.uint32), v_ref.view(np.uint32))
 
 
+def test_adamw_many_tensors_bit_exact(cuda, port):
+    """More tensors than one launch's segment table holds (two launches), empty
+    tensors, odd sizes and CTA shares that cross tensor boundaries, against the
+    oracle's AdamW::Step bit for bit."""
+    r = rng(9)
+    sizes = [int(x) for x in r.integers(0, 300, 700)]
+    sizes[5] = sizes[6] = 0
+    sizes[400] = 250_003
+    decay = [0.01 if i % 3 else 0.0 for i in range(len(sizes))]
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    n = int(offs[-1])
+    p = normal(r, n, 0.02)
+    p_ref, m_ref, v_ref = p.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    pd, md, vd = dev(p, cuda), torch.zeros(n, device=cuda), torch.zeros(n, device=cuda)
+    lr, b1, b2, eps = 1e-3, 0.9, 0.95, 1e-8
+    for step in (1, 2):
+        g = normal(r, n, 0.1)
+        port.adamw_flat(p_ref, g, m_ref, v_ref, offs, decay, lr, b1, b2, eps, step)
+        bc1 = np.float32(1.0 - np.power(np.float64(np.float32(b1)), step))
+        bc2 = np.float32(1.0 - np.power(np.float64(np.float32(b2)), step))
+        nk.adamw_flat(pd, dev(g, cuda), md, vd, offs.tolist(), decay, lr, b1, b2, eps, float(bc1),
+                      float(bc2))
+    assert np.array_equal(host(pd).view(np.uint32), p_ref.view(np.uint32))
+    assert np.array_equal(host(md).view(np.uint32), m_ref.view(np.uint32))
+    assert np.array_equal(host(vd).view(np.uint32), v_ref.view(np.uint32))
+
+
 def test_sumsq_and_clip(cuda):
     x = normal(rng(3), 100001, 0.1)
     s = nk.sumsq(dev(x, cuda))
