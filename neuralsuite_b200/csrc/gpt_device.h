@@ -527,19 +527,24 @@ class GPTBlock : public Layer {
   // residual add runs inside ln_2 on c_proj's plain product.
   Tensor Forward(const Tensor& x) override {
     const int C = x.Shape().back(), M = Rows(x, C);
-    const bool lo = C % 4 == 0;
-    float* h1_lo = lo ? Scratch(h1_lo_buf_, M, C).Data() : nullptr;
-    Tensor h1 = ln_1_.ForwardEx(x, nullptr, nullptr, h1_lo);
-    Tensor raw1 = attn_.ForwardNoBias(h1, h1_lo);
-    float* h2_lo = lo ? Scratch(h2_lo_buf_, M, C).Data() : nullptr;
-    const Tensor x2d = x.View({M, C});
-    Tensor h2 = ln_2_.ForwardEx(raw1, attn_.OutBias(), &x2d, h2_lo);
-    x1_ = raw1;  // now x + attn(ln_1(x)), written by ln_2
-    float* gelu_lo = mlp_fc_.Out() % 4 == 0 ? Scratch(gelu_lo_buf_, M, mlp_fc_.Out()).Data() : nullptr;
-    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({M, C}), &gelu_, gelu_lo, h2_lo);
+    const float* gelu_lo = ForwardToGelu(x, nullptr, nullptr);
     Tensor x2 = mlp_proj_.ForwardResidual(gelu_, x1_.View({M, C}), gelu_lo);
     return x2.View(x.Shape());
   }
+  // The block with its last residual add left open: the input arrives as
+  // in_resid + (x + in_bias) (the previous block's open output; in_bias and
+  // in_resid null: x as it is) and ln_1 closes it, writing the sum over x.
+  // Returns mlp_proj's plain product; the block's output is
+  // OpenResid() + (product + OpenBias()), formed by the consumer's LayerNorm
+  // (the next block's ln_1 or ln_f) in its own pass, with the same rounding.
+  Tensor ForwardOpen(const Tensor& x, const float* in_bias, const Tensor* in_resid) {
+    const int C = x.Shape().back(), M = Rows(x, C);
+    const float* gelu_lo = ForwardToGelu(x, in_bias, in_resid);
+    x1_ = x1_.View({M, C});
+    return mlp_proj_.ForwardNoBias(gelu_, gelu_lo).View(x.Shape());
+  }
+  const float* OpenBias() { return mlp_proj_.BiasParam().Value().Data(); }
+  const Tensor& OpenResid() const { return x1_; }
   // GPTBlock::Backward (gpt.h:82-100) with the GELU backward fused into the
   // mlp_fc bias-gradient pass and both residual adds fused into LayerNorm
   // backward.
@@ -555,6 +560,23 @@ class GPTBlock : public Layer {
   }
 
  private:
+  // ln_1 .. GELU (x1 = x + attn(ln_1(x)) kept in x1_, gelu(mlp_fc(ln_2(x1)))
+  // in gelu_); returns the GELU output's lo part (or null).
+  const float* ForwardToGelu(const Tensor& x, const float* in_bias, const Tensor* in_resid) {
+    const int C = x.Shape().back(), M = Rows(x, C);
+    const bool lo = C % 4 == 0;
+    float* h1_lo = lo ? Scratch(h1_lo_buf_, M, C).Data() : nullptr;
+    Tensor h1 = ln_1_.ForwardEx(x, in_bias, in_resid, h1_lo);
+    Tensor raw1 = attn_.ForwardNoBias(h1, h1_lo);
+    float* h2_lo = lo ? Scratch(h2_lo_buf_, M, C).Data() : nullptr;
+    const Tensor x2d = x.View({M, C});
+    Tensor h2 = ln_2_.ForwardEx(raw1, attn_.OutBias(), &x2d, h2_lo);
+    x1_ = raw1;  // now x + attn(ln_1(x)), written by ln_2
+    float* gelu_lo = mlp_fc_.Out() % 4 == 0 ? Scratch(gelu_lo_buf_, M, mlp_fc_.Out()).Data() : nullptr;
+    fc_pre_ = mlp_fc_.ForwardGelu(h2.View({M, C}), &gelu_, gelu_lo, h2_lo);
+    return gelu_lo;
+  }
+
   LayerNormLayer ln_1_;
   MultiHeadAttention attn_;
   LayerNormLayer ln_2_;
@@ -741,11 +763,21 @@ class GPTModel : public Module {
     Check(ns_embedding_fwd(Tokens(), B, T, wte_.WeightParam().Value().Data(), config_.vocab_size,
                            wpe_.WeightParam().Value().Data(), config_.block_size, C, x.Data(),
                            reinterpret_cast<int32_t*>(Small() + 1), Stream()));
-    for (auto& blk : blocks_) x = blk->Forward(x);
-    xf_ = ln_f_.Forward(x).View({M, C});
+    // Each block's last residual add stays open and is formed by the next
+    // LayerNorm (the next block's ln_1, or ln_f) in its own pass.
+    const float* open_bias = nullptr;
+    Tensor open_resid;
+    for (auto& blk : blocks_) {
+      x = blk->ForwardOpen(x, open_bias, open_bias ? &open_resid : nullptr);
+      open_bias = blk->OpenBias();
+      open_resid = blk->OpenResid();
+    }
+    float* xf_lo = C % 4 == 0 ? Scratch(xf_lo_buf_, M, C).Data() : nullptr;
+    xf_ = ln_f_.ForwardEx(x, open_bias, open_bias ? &open_resid : nullptr, xf_lo).View({M, C});
+    xf_lo_ = xf_lo;
     // logits = x_2d . wte^T (gpt.h:226-228): wte read as a K-major operand, no transpose copy.
     logits_ = Scratch(logits_buf_, M, config_.vocab_size);
-    Check(ns_gemm_lo(M, config_.vocab_size, C, xf_.Data(), C, 0, nullptr,
+    Check(ns_gemm_lo(M, config_.vocab_size, C, xf_.Data(), C, 0, xf_lo_,
                      wte_.WeightParam().Value().Data(), C, 1, WteLo(), logits_.Data(),
                      config_.vocab_size, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
                      ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
@@ -764,16 +796,23 @@ class GPTModel : public Module {
   void Backward(OnReady&& on_group_ready) {
     const int M = B_ * T_, C = config_.n_embd, V = config_.vocab_size;
     Tensor dlogits = criterion_.Backward();
+    // dlogits' lo part, split once for both head products.
+    const float* dl_lo = nullptr;
+    if (V % 4 == 0 && C % 4 == 0) {
+      Tensor dl = Scratch(dlogits_lo_buf_, M, V);
+      Check(ns_split_lo(dlogits.Data(), M, V, V, dl.Data(), Stream()));
+      dl_lo = dl.Data();
+    }
     // dx = dlogits . wte  (wte read N-major in place)
     Tensor dx = Scratch(dx_head_, M, C);
-    Check(ns_gemm_lo(M, C, V, dlogits.Data(), V, 0, nullptr, wte_.WeightParam().Value().Data(), C,
+    Check(ns_gemm_lo(M, C, V, dlogits.Data(), V, 0, dl_lo, wte_.WeightParam().Value().Data(), C,
                      0, WteLo(), dx.Data(), C, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr,
                      ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
     // head term of the tied wte gradient, dlogits^T . x, written first (the
     // embedding backward adds its own sum to it at the end, gpt.h:262-269).
-    Check(ns_gemm(V, C, M, dlogits.Data(), V, 1, xf_.Data(), C, 0,
-                  wte_.WeightParam().Grad().Data(), C, 0.0f, NS_EPI_STORE, nullptr, nullptr,
-                  nullptr, ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
+    Check(ns_gemm_lo(V, C, M, dlogits.Data(), V, 1, dl_lo, xf_.Data(), C, 0, xf_lo_,
+                     wte_.WeightParam().Grad().Data(), C, 0.0f, NS_EPI_STORE, nullptr, nullptr,
+                     nullptr, ctx_storage_.scratch, ctx_storage_.scratch_bytes, Stream()));
     Tensor d = ln_f_.Backward(dx.View({B_, T_, C}));
     int group = 0;
     for (int l = (int)blocks_.size() - 1; l >= 0; --l) {
@@ -810,7 +849,8 @@ class GPTModel : public Module {
   std::vector<int> ranks_;
   std::shared_ptr<DeviceBuffer> values_, grads_, values_lo_, scratch_, small_, tokens_;
   Context ctx_storage_;
-  Tensor x0_, xf_, logits_, logits_buf_, dx_head_;
+  Tensor x0_, xf_, logits_, logits_buf_, dx_head_, xf_lo_buf_, dlogits_lo_buf_;
+  const float* xf_lo_ = nullptr;  // ln_f output's lo part (the head's A operand)
   int B_ = 0, T_ = 0;
 };
 
