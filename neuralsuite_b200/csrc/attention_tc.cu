@@ -4,27 +4,28 @@
 // from the interleaved qkv[B*T, 3C] (MultiHeadAttention::Forward,
 // include/layers/attention.h:364-384).
 //
-// One CTA per (b, h, 128-query block), 384 threads, warp-specialised:
+// Persistent: one CTA per SM (384 threads, warp-specialised) loops over work
+// items (b, h, 128-query block):
 //   warp 0      TMA producer: per 64-key block the K and V tiles of this head
-//               and their tf32 lo parts (split beforehand into the workspace)
-//               into a shared-memory ring.  K lands K-major (16-byte chunk
-//               128B swizzle), V MN-major (32-byte chunk 128B swizzle).
+//               and their tf32 lo parts (the caller's, or split beforehand into
+//               the workspace) into a shared-memory ring.  K lands K-major
+//               (16-byte chunk 128B swizzle), V MN-major (32-byte chunk 128B
+//               swizzle).
 //   warp 1      MMA issuer (converged warp, elected lane), A operands from TMEM:
 //                 S_j  = Qhi.Khi + Qhi.Klo + Qlo.Khi      (M=128, N=64,  K=D)
 //                 O_j  = Phi.Vhi + Phi.Vlo + Plo.Vhi      (M=128, N=D,   K=64)
-//   warps 4-7   softmax warpgroup 0 (even key blocks), warps 8-11 softmax
-//               warpgroup 1 (odd key blocks); one query row per thread (TMEM
-//               lane = row).  Each warpgroup keeps its own running max m, sum
-//               l and output accumulator: per block it reads S_j, applies the
-//               causal mask, P = 2^(S*scale*log2e - m*scale*log2e), writes Phi
-//               (over S_j) and Plo to TMEM, and folds the previous O into its
-//               registers as acc = acc * alpha + O with round-to-nearest (each
-//               O_j is a 64-term tensor-core sum; its round-toward-zero
-//               accumulation stays at the 1e-7 level).  The two warpgroups
-//               alternate, so the tensor core always has the other one's S or
-//               O to compute; their partial results merge at the end.
-// TMEM (512 columns): Qhi [0,D), Qlo [D,2D); per warpgroup w: S/Phi at
-// 128+64w, Plo at 256+64w, O at 384+Dw.
+//   warp 2      TMA producer of the next item's Q rows (into shared memory).
+//   warps 4-11  two softmax warpgroups, both on every key block (column halves,
+//               described above the forward kernel); one query row per thread
+//               pair (TMEM lane = row).  Per block: read S_j, apply the causal
+//               mask, exchange the row maxima, P = 2^(S*scale*log2e -
+//               m*scale*log2e), write Phi (over S_j) and Plo to TMEM, and fold
+//               the previous O into registers as acc = acc * alpha + O with
+//               round-to-nearest (each O_j is a 64-term tensor-core sum; its
+//               round-toward-zero accumulation stays at the 1e-7 level).
+// TMEM (512 columns): Qhi [0,D), Qlo [D,2D); S/Phi at 128 + 64b, Plo at
+// 256 + 64b, O at 384 + 64b, b = parity of the key block counted over all of
+// the CTA's items (double buffers: S_{j+1} is computed while S_j turns into P_j).
 // Every mbarrier wait is bounded (2 s); a timeout raises a device flag that
 // ns_kernel_health() reports, and the CTA drains its copies and MMAs and exits.
 #include <algorithm>
