@@ -7,14 +7,16 @@
 // Differences from the CPU reference, all deliberate:
 //  * Forward returns a view of a buffer the layer owns (sized once for the
 //    largest batch), not a fresh deep copy; it stays valid until the layer's
-//    next Forward, which is what the training loop needs and what makes the
-//    step free of allocations (so it can be captured in a CUDA graph).
+//    next Forward, which is what the training loop needs and what keeps the
+//    step free of allocations after the first one.
 //  * Layers remember a view of their input instead of deep-copying it
 //    (reference: last_input_ = input); callers keep inputs alive until
 //    Backward, as GPTBlock / GPTModel do.
-//  * GPTBlock fuses what the reference does in separate passes: GELU into
-//    the mlp_fc GEMM, the residual adds into the c_proj / mlp_proj GEMMs and
-//    into LayerNorm backward, the GELU backward into the mlp_proj dX GEMM.
+//  * GPTBlock fuses what the reference does in separate passes: each residual
+//    add into the LayerNorm that reads the sum (ln_2 for the first, the next
+//    block's ln_1 or ln_f for the second) and the residual gradient adds into
+//    LayerNorm backward; GELU runs with its lo part as one pass after the
+//    mlp_fc GEMM, and the GELU backward inside mlp_fc's bias-gradient pass.
 //  * Errors surface as the reference's exception types (std::invalid_argument,
 //    std::out_of_range) from the C++ layer; the C ABI turns them into status
 //    codes.
