@@ -140,13 +140,14 @@ ns_status adamw_run(float* params, const float* grads, float* m, float* v, int64
                "ns_adamw_flat: segment offsets must be ascending");
   // One wave: as many CTAs as fit on the GPU at once, each with an equal
   // share (a multiple of 1024 elements) of the launch's range.
-  static int waves_cta = 0;
-  if (waves_cta == 0) {
-    int per_sm = 0;
-    NS_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_k, 256, 0),
-                "ns_adamw_flat occupancy");
-    waves_cta = std::max(1, per_sm) * sm_count();
-  }
+  // (CTAs per SM depend only on the kernel; the SM count is the current device's.)
+  static const int per_sm = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, adamw_k, 256, 0) == cudaSuccess) return n;
+    (void)cudaGetLastError();  // one CTA per SM then; the launch reports any real fault
+    return 0;
+  }();
+  const int waves_cta = std::max(1, per_sm) * sm_count();
   AdamTable tab;
   for (int t0 = 0; t0 < n_seg; t0 += kMaxSegs) {
     const int n = std::min(kMaxSegs, n_seg - t0);
