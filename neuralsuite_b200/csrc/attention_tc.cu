@@ -1300,8 +1300,7 @@ bool fwd_supported(const float* qkv, const float* out, int B, int T, int H, int 
   if (D != 32 && D != 64) return false;
   if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out)) & 15) != 0) return false;
   if ((int64_t)B * T >= (1ll << 31) || (int64_t)3 * H * D >= (1ll << 31)) return false;
-  static int supported = -1;
-  if (supported < 0) supported = ns_device_supported();
+  static const int supported = ns_device_supported();  // thread-safe, once
   return supported == 1;
 }
 

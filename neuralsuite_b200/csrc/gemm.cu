@@ -87,8 +87,7 @@ bool use_tc(int M, int N, int K, const float* A, int lda, const float* B, int ld
   if (t_engine == 1) return false;
   if (M <= 0 || N <= 0 || K <= 0) return false;
   if (!tma_ok(A, lda) || !tma_ok(B, ldb)) return false;
-  static int supported = -1;
-  if (supported < 0) supported = ns_device_supported();
+  static const int supported = ns_device_supported();  // thread-safe, once
   return supported == 1;
 }
 
