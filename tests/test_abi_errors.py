@@ -1,0 +1,109 @@
+"""CPU checks of the C ABI's error behaviour: invalid arguments come back as
+the status codes of the reference's exception types, with a message, before
+any device work is issued.
+
+Every call below is rejected by the library's own argument checks before it
+touches a pointer or launches a kernel, so these tests need no GPU and are
+safe where one is present.  The pointers passed are never dereferenced.
+"""
+import ctypes
+
+import pytest
+
+NS_OK, NS_ERR_INVALID_ARGUMENT, NS_ERR_OUT_OF_RANGE = 0, 1, 2
+
+FAKE = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced (rejected first)
+FAKE_MISALIGNED = ctypes.c_void_p(0x10004)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from neuralsuite_b200 import _lib
+
+    return _lib.load()
+
+
+def _err(lib, rc, code, text):
+    assert rc == code, (rc, lib.ns_last_error())
+    assert text in lib.ns_last_error().decode(), lib.ns_last_error()
+
+
+def test_gpt_create_rejects_n_embd_not_divisible_by_n_head(lib):
+    """MultiHeadAttention's constructor check (include/layers/attention.h)."""
+    from neuralsuite_b200 import _lib
+
+    cfg = _lib.ns_gpt_config(256, 64, 2, 4, 130, 1)
+    h = ctypes.c_void_p()
+    _err(lib, lib.ns_gpt_create(ctypes.byref(cfg), ctypes.byref(h)), NS_ERR_INVALID_ARGUMENT,
+         "n_head")
+    assert not h.value
+
+
+@pytest.mark.parametrize("field", ["vocab", "block", "embd", "batch"])
+def test_gpt_create_rejects_non_positive_sizes(lib, field):
+    from neuralsuite_b200 import _lib
+
+    v = dict(vocab=256, block=64, embd=128, batch=1)
+    v[field] = 0
+    cfg = _lib.ns_gpt_config(v["vocab"], v["block"], 2, 4, v["embd"], v["batch"])
+    h = ctypes.c_void_p()
+    rc = lib.ns_gpt_create(ctypes.byref(cfg), ctypes.byref(h))
+    assert rc == NS_ERR_INVALID_ARGUMENT, lib.ns_last_error()
+    assert not h.value
+
+
+def test_gpt_create_rejects_null(lib):
+    h = ctypes.c_void_p()
+    _err(lib, lib.ns_gpt_create(None, ctypes.byref(h)), NS_ERR_INVALID_ARGUMENT, "NULL")
+
+
+def _gemm(lib, M=4, N=4, K=4, lda=4, ldb=4, ldc=4, beta=0.0, epi=0, bias=None):
+    return lib.ns_gemm(M, N, K, FAKE, lda, 0, FAKE, ldb, 0, FAKE, ldc, beta, epi, bias, None,
+                       None, None, 0, None)
+
+
+def test_gemm_argument_checks(lib):
+    _err(lib, _gemm(lib, M=-1), NS_ERR_INVALID_ARGUMENT, "negative dimension")
+    _err(lib, _gemm(lib, beta=0.5), NS_ERR_INVALID_ARGUMENT, "beta")
+    _err(lib, _gemm(lib, ldc=3), NS_ERR_INVALID_ARGUMENT, "ldc")
+    _err(lib, _gemm(lib, lda=3), NS_ERR_INVALID_ARGUMENT, "leading dimension")
+    _err(lib, _gemm(lib, epi=99), NS_ERR_INVALID_ARGUMENT, "epilogue")
+    _err(lib, _gemm(lib, epi=1), NS_ERR_INVALID_ARGUMENT, "bias")  # NS_EPI_BIAS without bias
+
+
+def test_gemm_with_an_empty_output_is_a_no_op(lib):
+    assert _gemm(lib, M=0) == NS_OK
+    assert _gemm(lib, N=0, ldc=0, ldb=0) == NS_OK
+
+
+def test_layernorm_backward_checks(lib):
+    rc = lib.ns_layernorm_bwd(FAKE, FAKE, FAKE, FAKE, FAKE, None, FAKE, FAKE, FAKE, -1, 16, None,
+                              0, None)
+    _err(lib, rc, NS_ERR_INVALID_ARGUMENT, "rows")
+    rc = lib.ns_layernorm_bwd(FAKE, FAKE, FAKE, FAKE, FAKE, None, FAKE, FAKE, FAKE, 8, 16, None,
+                              0, None)
+    _err(lib, rc, NS_ERR_INVALID_ARGUMENT, "workspace")
+
+
+def test_embedding_rejects_a_sequence_longer_than_block_size(lib):
+    """The reference throws std::out_of_range (include/gpt.h Forward)."""
+    rc = lib.ns_embedding_fwd(FAKE, 1, 65, FAKE, 256, FAKE, 64, 128, FAKE, FAKE, None)
+    _err(lib, rc, NS_ERR_OUT_OF_RANGE, "block_size")
+
+
+def _adamw(lib, offsets, decay, ptr=FAKE, n_total=None):
+    n = len(decay)
+    offs = (ctypes.c_int64 * (n + 1))(*offsets)
+    dec = (ctypes.c_float * max(1, n))(*decay)
+    total = offsets[-1] if n_total is None else n_total
+    return lib.ns_adamw_flat(ptr, FAKE, FAKE, FAKE, total, ctypes.cast(offs, ctypes.c_void_p),
+                             ctypes.cast(dec, ctypes.c_void_p), n, 1e-3, 0.9, 0.95, 1e-8, 0.1,
+                             0.05, None)
+
+
+def test_adamw_checks_the_segment_table_before_launching(lib):
+    _err(lib, _adamw(lib, [0, 8, 4, 12], [0.0, 0.1, 0.0]), NS_ERR_INVALID_ARGUMENT, "ascending")
+    _err(lib, _adamw(lib, [0, 8, 16], [0.0, 0.1], n_total=12), NS_ERR_INVALID_ARGUMENT,
+         "exceed")
+    _err(lib, _adamw(lib, [0, 8], [0.0], ptr=FAKE_MISALIGNED), NS_ERR_INVALID_ARGUMENT,
+         "aligned")
