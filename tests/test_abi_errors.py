@@ -107,3 +107,50 @@ def test_adamw_checks_the_segment_table_before_launching(lib):
          "exceed")
     _err(lib, _adamw(lib, [0, 8], [0.0], ptr=FAKE_MISALIGNED), NS_ERR_INVALID_ARGUMENT,
          "aligned")
+
+
+def test_attention_backward_checks(lib):
+    def bwd(B, T, H, D, ws=None):
+        return lib.ns_attn_bwd(FAKE, FAKE, FAKE, FAKE, B, T, H, D, FAKE, ws, 0, None)
+
+    _err(lib, bwd(1, 4, 1, 256), NS_ERR_INVALID_ARGUMENT, "head_dim")
+    _err(lib, bwd(1, 4, 0, 64), NS_ERR_INVALID_ARGUMENT, "bad shape")
+    _err(lib, bwd(1, 4, 1, 64), NS_ERR_INVALID_ARGUMENT, "workspace")
+    assert bwd(0, 4, 1, 64) == NS_OK  # an empty batch is no work
+
+
+def test_cross_entropy_checks(lib):
+    def ce(rows, classes, denom, ws=None):
+        return lib.ns_cross_entropy(FAKE, FAKE, rows, classes, denom, FAKE, FAKE, FAKE, ws, 0,
+                                    None)
+
+    _err(lib, ce(0, 256, 1.0), NS_ERR_INVALID_ARGUMENT, "positive")
+    _err(lib, ce(8, 0, 1.0), NS_ERR_INVALID_ARGUMENT, "positive")
+    _err(lib, ce(8, 256, 0.0), NS_ERR_INVALID_ARGUMENT, "denom")
+    _err(lib, ce(8, 256, 8.0), NS_ERR_INVALID_ARGUMENT, "workspace")
+
+
+def test_bias_gradient_split_checks(lib):
+    def bgs(M, N, dy=FAKE, ws=None):
+        return lib.ns_bias_grad_split(dy, M, N, FAKE, FAKE, ws, 0, None)
+
+    _err(lib, bgs(8, 6), NS_ERR_INVALID_ARGUMENT, "multiple of 4")
+    _err(lib, bgs(8, 8, dy=FAKE_MISALIGNED), NS_ERR_INVALID_ARGUMENT, "aligned")
+    _err(lib, bgs(8, 8), NS_ERR_INVALID_ARGUMENT, "workspace")
+
+
+def test_layernorm_forward_checks(lib):
+    _err(lib, lib.ns_layernorm_fwd(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 0, 1e-5, None),
+         NS_ERR_INVALID_ARGUMENT, "dim")
+    # a residual to add needs the bias and the buffer the sum goes to
+    rc = lib.ns_layernorm_fwd_ex(FAKE, None, FAKE, FAKE, FAKE, FAKE, FAKE, None, FAKE, FAKE, 8,
+                                 16, 1e-5, None)
+    _err(lib, rc, NS_ERR_INVALID_ARGUMENT, "resid")
+
+
+def test_pointwise_and_split_checks(lib):
+    _err(lib, lib.ns_gelu_fwd_lo(FAKE, FAKE, FAKE_MISALIGNED, 16, None), NS_ERR_INVALID_ARGUMENT,
+         "aligned")
+    _err(lib, lib.ns_gelu_fwd(FAKE, FAKE, -1, None), NS_ERR_INVALID_ARGUMENT, "n < 0")
+    _err(lib, lib.ns_split_lo(FAKE, 4, 8, 4, FAKE, None), NS_ERR_INVALID_ARGUMENT, "bad shape")
+    assert lib.ns_split_lo(FAKE, 0, 8, 8, FAKE, None) == NS_OK
