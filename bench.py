@@ -15,11 +15,11 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -40,7 +40,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true",
-                    help="skip the reference CPU sample (it costs ~15-25 s)")
+                    help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
     return ap.parse_args()
 
 
@@ -61,15 +61,9 @@ def peaks():
 
 # ----------------------------------------------------------- reference CPU leg
 
-def reference_sample(seconds_hint=False):
-    """The NeuralSuite reference (oracle/_ref, built from its own sources) on
-    the host cores: one sequence of 1024 tokens (one of the 8 sequences a GPU
-    processes per step) through the full 12-layer model, forward +
-    CrossEntropy + backward + AdamW.  Returns (tokens/s, cores, kind, sample
-    description)."""
+def _reference_model():
     import oracle
 
-    Ts = T
     if oracle.ref_available():
         o = oracle.ref()
         cores = os.cpu_count() or 1
@@ -83,35 +77,62 @@ def reference_sample(seconds_hint=False):
     r = np.random.default_rng(5)
     g.set_params((r.standard_normal(g.num_params()) * 0.02).astype(np.float32))
     g.adamw_init(LR)
-    idx = r.integers(0, V, (1, Ts)).astype(np.float32)
-    tgt = r.integers(0, V, Ts).astype(np.float32)
+    return g, r, cores, kind
+
+
+def _reference_step(g, r, nseq):
+    idx = r.integers(0, V, (nseq, T)).astype(np.float32)
+    tgt = r.integers(0, V, nseq * T).astype(np.float32)
     t0 = time.perf_counter()
     g.fwd_bwd(idx, tgt)
     g.adamw_step()
-    dt = time.perf_counter() - t0
-    desc = (f"1 of the 8 sequences of a step: {Ts} tokens through all {LAYERS} layers "
-            f"(forward + CrossEntropy + backward + AdamW), {cores} host thread(s)")
-    return Ts / dt, cores, kind, desc
+    return nseq * T / (time.perf_counter() - t0)
+
+
+def reference_run(steps, warmup, calibrate=True):
+    """The NeuralSuite reference (oracle/_ref, built from its own sources) on
+    the host cores.  Each step is a bounded sample of the workload: one of the
+    8 sequences of a step (1024 tokens) through the full 12-layer model,
+    forward + CrossEntropy + backward + AdamW.  With calibrate, one full
+    8-sequence step (8192 tokens, the GPU arm's per-GPU batch) is timed once
+    in the same run, so the per-token rate of the sample can be set against
+    the rate of the real configuration (the reference's attention and its
+    [B,H,T,T] probability cache scale with the batch).  Returns (median
+    sample tokens/s, cores, kind, description, calibration dict or None)."""
+    g, r, cores, kind = _reference_model()
+    vals = []
+    for i in range(warmup + steps):
+        v = _reference_step(g, r, 1)
+        if i >= warmup:
+            vals.append(v)
+    sample = statistics.median(vals)
+    cal = None
+    if calibrate:
+        full = _reference_step(g, r, B_PER_GPU)
+        cal = {"full_step_tokens_per_s": full, "full_step_tokens": B_PER_GPU * T,
+               "sample_tokens_per_s": sample, "full_over_sample": full / sample,
+               "note": "one full 8-sequence step timed once after the samples, same run"}
+    desc = (f"1 of the 8 sequences of a step per timed step: {T} tokens through all {LAYERS} "
+            f"layers (forward + CrossEntropy + backward + AdamW), {cores} host thread(s)")
+    return sample, cores, kind, desc, cal
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    vals = []
-    for i in range(args.warmup + args.steps):
-        v, cores, kind, desc = reference_sample()
-        if i >= args.warmup:
-            vals.append(v)
-    value = statistics.median(vals)
+    value, cores, kind, desc, cal = reference_run(args.steps, args.warmup)
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": T / value * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform byte tokens, seeded)",
-        "config": {"workload": WORKLOAD, "global_batch": "1 sequence sampled per step",
+        "config": {"workload": WORKLOAD,
+                   "global_batch": "1 of the 8 sequences per timed step (bounded sample); "
+                                   "one full 8-sequence step in calibration",
                    "seq_len": T, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
                          "sample": desc},
+        "calibration": cal,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -128,12 +149,12 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(HERE, "gpurun_out", f"clocks_rank{index}.csv")
+        self.path = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix=f"ns_clocks_{self.index}_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
@@ -151,7 +172,10 @@ class ClockSampler:
             self.proc.kill()
         self.f.close()
         sm, mx, reasons = [], None, set()
-        for line in open(self.path):
+        with open(self.path) as fh:
+            lines = fh.readlines()
+        os.unlink(self.path)
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -185,10 +209,14 @@ def gemm_shapes():
     ]
 
 
-def gemm_roofline(torch, nk):
+def gemm_roofline(torch, nk, presplit):
     """Times every GEMM shape of the step with CUDA events on the current
     stream (alone, warm, operands > L2 for the big ones) and returns step-
-    weighted achieved TFLOP/s for all GEMMs and for the backward ones."""
+    weighted achieved TFLOP/s for all GEMMs and for the backward ones.
+    presplit: the operands' tf32 lo parts are made once beforehand and passed
+    in (ns_gemm_lo, the form the training step runs, where each producer
+    writes the lo part of its output); otherwise ns_gemm splits them into its
+    workspace inside every call."""
     dev = torch.device("cuda")
     tot_f = tot_t = bwd_f = bwd_t = 0.0
     launches = 0
@@ -197,14 +225,17 @@ def gemm_roofline(torch, nk):
         A = torch.randn((k, m) if at else (m, k), device=dev)
         Bm = torch.randn((n, k) if bt else (k, n), device=dev)
         out = torch.empty(m, n, device=dev)
+        kw = dict(a_trans=bool(at), b_trans=bool(bt), out=out)
+        if presplit:
+            kw.update(a_lo=nk.split_lo(A), b_lo=nk.split_lo(Bm))
         for _ in range(2):
-            nk.gemm(A, Bm, a_trans=bool(at), b_trans=bool(bt), out=out)
+            nk.gemm(A, Bm, **kw)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 5
         torch.cuda.synchronize()
         s.record()
         for _ in range(reps):
-            nk.gemm(A, Bm, a_trans=bool(at), b_trans=bool(bt), out=out)
+            nk.gemm(A, Bm, **kw)
         e.record()
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / reps
@@ -217,8 +248,69 @@ def gemm_roofline(torch, nk):
         if bwd:
             bwd_f += cnt * flops
             bwd_t += cnt * ms
-        del A, Bm, out
+        del A, Bm, out, kw
     return tot_f / tot_t / 1e9, bwd_f / bwd_t / 1e9, tot_f / launches, tot_t / launches, per
+
+
+def make_batches(rank, n_batches):
+    """Seeded uniform byte tokens and targets of one rank (int32, host)."""
+    r = np.random.default_rng(1000 + rank)
+    tok = [r.integers(0, V, (B_PER_GPU, T)).astype(np.int32) for _ in range(n_batches)]
+    tgt = [r.integers(0, V, (B_PER_GPU * T,)).astype(np.int32) for _ in range(n_batches)]
+    return tok, tgt
+
+
+def dp_checks(torch, dist, model, cfg, rank, world, n_batches):
+    """Data-parallel correctness after the timed steps (untimed).
+
+    replicas_identical: rank 0's parameter buffer broadcast to every rank and
+    compared bit for bit with the rank's own.  Then one forward + loss +
+    backward on every rank's first batch with the gradient all-reduce (no
+    optimizer step), against rank 0 recomputing each rank's shard alone
+    (world 1) on the same parameters: the global loss against the mean of the
+    shard losses, and the all-reduced gradient against the mean of the shard
+    gradients, |x - ref| <= 1e-5 + 1e-4 |ref|."""
+    from neuralsuite_b200 import GPTModel
+
+    mine = model.params()
+    ref = mine.clone()
+    dist.broadcast(ref, src=0)
+    same = torch.tensor([1 if torch.equal(mine, ref) else 0], device="cuda", dtype=torch.int32)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    del ref
+    tok, tgt = make_batches(rank, n_batches)
+    model.forward(torch.from_numpy(tok[0]).cuda())
+    model.loss_backward(torch.from_numpy(tgt[0]).cuda())
+    model.backward()
+    torch.cuda.synchronize()
+    loss_dp = float(model.loss_tensor().item()) / world
+    out = {"replicas_identical": bool(same.item() == 1)}
+    if rank == 0:
+        solo = GPTModel(cfg, max_batch=B_PER_GPU)
+        solo.params().copy_(model.params())
+        acc = torch.zeros(model.n_params, dtype=torch.float64, device="cuda")
+        losses = []
+        for r in range(world):
+            t_r, g_r = make_batches(r, 1)
+            solo.forward(torch.from_numpy(t_r[0]).cuda())
+            losses.append(float(solo.loss_backward(torch.from_numpy(g_r[0]).cuda()).item()))
+            solo.backward()
+            acc += solo.grads().double()
+        want = acc / world
+        got = model.grads().double()
+        err = (got - want).abs()
+        bad = int((err > 1e-5 + 1e-4 * want.abs()).sum().item())
+        loss_1 = sum(losses) / world
+        out.update({
+            "loss_dp": loss_dp, "loss_1gpu_recompute": loss_1,
+            "loss_rel_err": abs(loss_dp - loss_1) / abs(loss_1),
+            "grad_max_abs_err": float(err.max().item()), "grad_elements_outside_tol": bad,
+            "ok": bool(out["replicas_identical"] and bad == 0
+                       and abs(loss_dp - loss_1) <= 1e-5 + 1e-4 * abs(loss_1)),
+        })
+        del solo, acc, want, got, err
+    dist.barrier()
+    return out
 
 
 # ----------------------------------------------------------- our leg
@@ -248,12 +340,10 @@ def run_ours(args, rank, world, local):
     if world > 1:
         comm = Comm(rank, world)
         model.set_comm(comm, world)
-    r = np.random.default_rng(1000 + rank)
     n_batches = 4  # distinct batches cycled through the timed steps
-    host_tok = [torch.from_numpy(r.integers(0, V, (B_PER_GPU, T)).astype(np.int32)).pin_memory()
-                for _ in range(n_batches)]
-    host_tgt = [torch.from_numpy(r.integers(0, V, (B_PER_GPU * T,)).astype(np.int32)).pin_memory()
-                for _ in range(n_batches)]
+    tok_np, tgt_np = make_batches(rank, n_batches)
+    host_tok = [torch.from_numpy(t).pin_memory() for t in tok_np]
+    host_tgt = [torch.from_numpy(t).pin_memory() for t in tgt_np]
     dev_tok = [t.cuda() for t in host_tok]
     dev_tgt = [t.cuda() for t in host_tgt]
     torch.cuda.synchronize()
@@ -315,10 +405,13 @@ def run_ours(args, rank, world, local):
     value = tokens_per_step / (ms / 1e3)
     e2e_value = tokens_per_step / (ms_e2e / 1e3)
 
+    dp = dp_checks(torch, dist, model, cfg, rank, world, n_batches) if world > 1 else None
+
     out = None
     if rank == 0:
         bf16_burst, bf16_sust, hbm, peak_src = peaks()
-        all_tf, bwd_tf, flops_per_launch, ms_per_launch, per = gemm_roofline(torch, nk)
+        all_tf, bwd_tf, flops_per_launch, ms_per_launch, per = gemm_roofline(torch, nk, True)
+        all_tf_ws, bwd_tf_ws, _, _, per_ws = gemm_roofline(torch, nk, False)
         nk.kernel_health()
         tf32_peak = bf16_burst / 2.0  # dense TF32 = half the dense BF16 rate (datasheet ratio)
         peak_3x = tf32_peak / 3.0     # 3xTF32: three tensor passes per fp32 product
@@ -350,9 +443,19 @@ def run_ours(args, rank, world, local):
                 "bwd_gemm_tflops": bwd_tf, "bwd_gemm_frac": bwd_tf / peak_3x,
                 "bwd_tensor_issue_frac_of_tf32_peak": 3 * bwd_tf / tf32_peak,
                 "algorithmic_flops_per_launch": flops_per_launch,
-                "avg_launch_ms": ms_per_launch, "shapes": per,
+                "avg_launch_ms": ms_per_launch,
+                "operands": "tf32 lo parts made by the producers and passed in (ns_gemm_lo), "
+                            "as the training step runs the products",
+                "shapes": per,
+                "split_in_call": {"achieved": all_tf_ws, "frac": all_tf_ws / peak_3x,
+                                  "bwd_gemm_tflops": bwd_tf_ws,
+                                  "note": "ns_gemm splitting both operands into its workspace "
+                                          "inside every call", "shapes": per_ws},
             },
         }
+        if dp is not None:
+            out["dp_check"] = dp
+            out["replicas_identical"] = dp["replicas_identical"]
     if world > 1:
         model.set_comm(None, 1)
         comm.destroy()
@@ -360,9 +463,10 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            v, cores, kind, desc = reference_sample()
+            v, cores, kind, desc, cal = reference_run(steps=3, warmup=1)
             out["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
-                                   "sample": desc}
+                                   "sample": desc + "; median of 3 after 1 warm-up",
+                                   "calibration": cal}
         print(json.dumps(out), flush=True)
 
 

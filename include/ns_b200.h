@@ -136,7 +136,10 @@ NS_API ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, in
  * the engines. */
 NS_API ns_status ns_gemm_set_engine(int engine);
 /* NS_ERR_TIMEOUT if any kernel of this library gave up a bounded wait on the
- * current device since the last call (the flag is cleared by the call). */
+ * current device since the last call (the flag is cleared by the call);
+ * NS_ERR_CUDA if the flag cannot be read (a sticky CUDA error on the device).
+ * It synchronises with the device: do not call it while a stream is being
+ * captured. */
 NS_API ns_status ns_kernel_health(void);
 
 /* Column sums db[n] = sum_m dY[m,n]: the bias gradient of Linear::Backward
@@ -256,8 +259,9 @@ NS_API ns_status ns_cross_entropy(const float* logits, const int32_t* targets, i
  * that loads the library until the process exits), so nothing is allocated
  * and no workspace is passed.  rows > NS_CE_NOALLOC_MAX_ROWS is rejected with
  * NS_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture.  All calls share the one array, so calls that may
+ * array's device address (cudaGetSymbolAddress), and so does the first call
+ * after the device's context has changed (cudaDeviceReset); make that first
+ * call before any stream capture.  All calls share the one array, so calls that may
  * overlap on the GPU (different streams without ordering) race; each call
  * overwrites every scratch entry it reads, so no clearing is needed. */
 #define NS_CE_NOALLOC_MAX_ROWS 65536

@@ -1337,14 +1337,19 @@ ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const fl
                  : launch_bwd<32>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo, s);
 }
 
+// 1 if a kernel of this file raised the timeout flag since the last call
+// (the flag is cleared), 0 if not, or -(CUDA error) if the flag could not be
+// read or cleared (a sticky error, or a call during stream capture).
 int consume_timeout_flag() {
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int)) != cudaSuccess) return 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int));
+  if (e != cudaSuccess) return -(int)e;
   if (v) {
     const int zero = 0;
-    cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    e = cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) return -(int)e;
   }
-  return v;
+  return v ? 1 : 0;
 }
 
 }  // namespace attn_tc

@@ -235,10 +235,12 @@ ns_status ns_split_lo(const float* x, int rows, int cols, int ld, float* lo, voi
 }
 
 ns_status ns_kernel_health(void) {
-  if (tc::consume_timeout_flag())
-    return fail(NS_ERR_TIMEOUT, "a tcgen05 GEMM gave up a bounded wait (see ns_gemm)");
-  if (attn_tc::consume_timeout_flag())
-    return fail(NS_ERR_TIMEOUT, "a tcgen05 attention kernel gave up a bounded wait");
+  const int g = tc::consume_timeout_flag();
+  const int a = attn_tc::consume_timeout_flag();
+  if (g < 0) return cuda_fail((cudaError_t)(-g), "ns_kernel_health: reading the GEMM flag");
+  if (a < 0) return cuda_fail((cudaError_t)(-a), "ns_kernel_health: reading the attention flag");
+  if (g) return fail(NS_ERR_TIMEOUT, "a tcgen05 GEMM gave up a bounded wait (see ns_gemm)");
+  if (a) return fail(NS_ERR_TIMEOUT, "a tcgen05 attention kernel gave up a bounded wait");
   return NS_OK;
 }
 

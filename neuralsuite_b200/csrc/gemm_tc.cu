@@ -1444,14 +1444,19 @@ ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, c
   return split_lo(x, rows, cols, ld, lo, s);
 }
 
+// 1 if a kernel of this file raised the timeout flag since the last call
+// (the flag is cleared), 0 if not, or -(CUDA error) if the flag could not be
+// read or cleared (a sticky error, or a call during stream capture).
 int consume_timeout_flag() {
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int)) != cudaSuccess) return 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int));
+  if (e != cudaSuccess) return -(int)e;
   if (v) {
     const int zero = 0;
-    cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    e = cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) return -(int)e;
   }
-  return v;
+  return v ? 1 : 0;
 }
 
 }  // namespace tc

@@ -127,19 +127,26 @@ ns_status ns_gpt_destroy(ns_gpt* h) {
   return NS_OK;
 }
 
-int ns_gpt_num_tensors(const ns_gpt* h) { return (int)h->model->Ranks().size(); }
-int64_t ns_gpt_tensor_numel(const ns_gpt* h, int i) {
-  return h->model->Offsets()[i + 1] - h->model->Offsets()[i];
+int ns_gpt_num_tensors(const ns_gpt* h) { return h ? (int)h->model->Ranks().size() : 0; }
+// Getters: 0 / NULL for a NULL handle or a tensor index out of range.
+static bool valid_tensor(const ns_gpt* h, int i) {
+  return h && i >= 0 && i < (int)h->model->Ranks().size();
 }
-int ns_gpt_tensor_rank(const ns_gpt* h, int i) { return h->model->Ranks()[i]; }
-int64_t ns_gpt_tensor_offset(const ns_gpt* h, int i) { return h->model->Offsets()[i]; }
-int64_t ns_gpt_num_params(const ns_gpt* h) { return h->model->NumParams(); }
-float* ns_gpt_params(ns_gpt* h) { return h->model->Values(); }
-float* ns_gpt_grads(ns_gpt* h) { return h->model->Grads(); }
-float* ns_gpt_logits(ns_gpt* h) { return h->model->Logits().Data(); }
-float* ns_gpt_loss(ns_gpt* h) { return h->model->Small(); }
+int64_t ns_gpt_tensor_numel(const ns_gpt* h, int i) {
+  return valid_tensor(h, i) ? h->model->Offsets()[i + 1] - h->model->Offsets()[i] : 0;
+}
+int ns_gpt_tensor_rank(const ns_gpt* h, int i) { return valid_tensor(h, i) ? h->model->Ranks()[i] : 0; }
+int64_t ns_gpt_tensor_offset(const ns_gpt* h, int i) {
+  return valid_tensor(h, i) ? h->model->Offsets()[i] : 0;
+}
+int64_t ns_gpt_num_params(const ns_gpt* h) { return h ? h->model->NumParams() : 0; }
+float* ns_gpt_params(ns_gpt* h) { return h ? h->model->Values() : nullptr; }
+float* ns_gpt_grads(ns_gpt* h) { return h ? h->model->Grads() : nullptr; }
+float* ns_gpt_logits(ns_gpt* h) { return h ? h->model->Logits().Data() : nullptr; }
+float* ns_gpt_loss(ns_gpt* h) { return h ? h->model->Small() : nullptr; }
 
 ns_status ns_gpt_forward(ns_gpt* h, const int32_t* tokens, int B, int T, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_forward: NULL model");
   return Guard([&]() -> ns_status {
     h->model->SetStream(nsb::as_stream(stream));
     h->model->Forward(tokens, B, T);
@@ -150,6 +157,7 @@ ns_status ns_gpt_forward(ns_gpt* h, const int32_t* tokens, int B, int T, void* s
 }
 
 ns_status ns_gpt_loss_backward(ns_gpt* h, const int32_t* targets, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_loss_backward: NULL model");
   return Guard([&]() -> ns_status {
     NS_REQUIRE(h->B > 0, "ns_gpt_loss_backward: no forward pass yet");
     h->model->SetStream(nsb::as_stream(stream));
@@ -159,10 +167,12 @@ ns_status ns_gpt_loss_backward(ns_gpt* h, const int32_t* targets, void* stream) 
 }
 
 ns_status ns_gpt_backward(ns_gpt* h, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_backward: NULL model");
   return Guard([&]() -> ns_status { return backward_impl(h, nsb::as_stream(stream)); });
 }
 
 ns_status ns_gpt_adamw_init(ns_gpt* h, float lr, float b1, float b2, float eps, float wd) {
+  NS_REQUIRE(h, "ns_gpt_adamw_init: NULL model");
   return Guard([&]() -> ns_status {
     h->opt = std::make_unique<AdamW>(*h->model, lr, b1, b2, eps, wd);
     return NS_OK;
@@ -170,6 +180,7 @@ ns_status ns_gpt_adamw_init(ns_gpt* h, float lr, float b1, float b2, float eps, 
 }
 
 ns_status ns_gpt_adamw_set_lr(ns_gpt* h, float lr) {
+  NS_REQUIRE(h, "ns_gpt_adamw_set_lr: NULL model");
   NS_REQUIRE(h->opt, "ns_gpt_adamw_set_lr: optimizer not initialised");
   return Guard([&]() -> ns_status {
     h->opt->SetLearningRate(lr);
@@ -178,6 +189,7 @@ ns_status ns_gpt_adamw_set_lr(ns_gpt* h, float lr) {
 }
 
 ns_status ns_gpt_adamw_step(ns_gpt* h, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_adamw_step: NULL model");
   NS_REQUIRE(h->opt, "ns_gpt_adamw_step: optimizer not initialised");
   return Guard([&]() -> ns_status {
     h->model->SetStream(nsb::as_stream(stream));
@@ -187,6 +199,7 @@ ns_status ns_gpt_adamw_step(ns_gpt* h, void* stream) {
 }
 
 ns_status ns_gpt_clip_gradients(ns_gpt* h, float max_norm, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_clip_gradients: NULL model");
   GPTModel& m = *h->model;
   cudaStream_t s = nsb::as_stream(stream);
   float* sumsq = m.Small() + 3;
@@ -197,6 +210,7 @@ ns_status ns_gpt_clip_gradients(ns_gpt* h, float max_norm, void* stream) {
 
 ns_status ns_gpt_train_step(ns_gpt* h, const int32_t* tokens, const int32_t* targets, int B, int T,
                             float max_norm, float* host_loss, void* stream) {
+  NS_REQUIRE(h, "ns_gpt_train_step: NULL model");
   NS_REQUIRE(h->opt, "ns_gpt_train_step: call ns_gpt_adamw_init first");
   cudaStream_t s = nsb::as_stream(stream);
   ns_status rc = ns_gpt_forward(h, tokens, B, T, stream);
@@ -229,6 +243,7 @@ ns_status ns_gpt_train_step(ns_gpt* h, const int32_t* tokens, const int32_t* tar
 }
 
 ns_status ns_gpt_set_comm(ns_gpt* h, ns_comm* comm, int world_size, int64_t bucket_floats) {
+  NS_REQUIRE(h, "ns_gpt_set_comm: NULL model");
   NS_REQUIRE(world_size >= 1, "ns_gpt_set_comm: world_size < 1");
   NS_TRY_CUDA(cudaDeviceSynchronize(), "ns_gpt_set_comm sync");
   release_comm_resources(h);

@@ -94,9 +94,10 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias 
 }
 
 // x_out = resid + (raw + bias), element-wise (the fused LayerNorm's fallback
-// for shapes without its vector path).
-__global__ void resid_bias_add_k(const float* __restrict__ raw, const float* __restrict__ bias,
-                                 const float* __restrict__ resid, float* __restrict__ x_out,
+// for shapes without its vector path).  x_out may be raw (the model writes the
+// sum over the GEMM product), so neither carries __restrict__.
+__global__ void resid_bias_add_k(const float* raw, const float* __restrict__ bias,
+                                 const float* __restrict__ resid, float* x_out,
                                  int64_t rows, int dim) {
   const int64_t n = rows * dim;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;

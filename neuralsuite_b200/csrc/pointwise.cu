@@ -2,6 +2,8 @@
 // sum-of-squares and clip.  All HBM-bound; float4 grid-stride loops, one warp
 // per row for the cross-entropy, deterministic fixed-order reductions.
 #include <algorithm>
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -272,22 +274,53 @@ namespace {
 
 static __device__ __align__(256) float g_ce_noalloc_rows[NS_CE_NOALLOC_MAX_ROWS];
 
-// Device address of g_ce_noalloc_rows for the current device, looked up once
-// per device with that device current.  Host code must not pass the symbol
-// itself to a kernel: on the host it names a shadow variable, not device
-// memory.
+// Device address of g_ce_noalloc_rows for the current device, looked up with
+// that device current on its first call and again whenever the device's
+// context has changed since (cudaDeviceReset destroys the context the
+// address belonged to; the next call runs in a new one).  Host code must not
+// pass the symbol itself to a kernel: on the host it names a shadow variable,
+// not device memory.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static const CtxGetCurrentFn fn = []() -> CtxGetCurrentFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return nullptr;
+  }();
+  return fn;
+}
+
 ns_status ce_noalloc_scratch(float** out) {
   static std::mutex mu;
   static float* addr[64] = {};
+  static CUcontext ctx_of[64] = {};
   int dev = 0;
   NS_TRY_CUDA(cudaGetDevice(&dev), "ns_cross_entropy_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(NS_ERR_UNSUPPORTED, "ns_cross_entropy_noalloc: device index >= 64");
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return fail(NS_ERR_UNSUPPORTED, "ns_cross_entropy_noalloc: cuCtxGetCurrent unavailable");
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS)
+    return fail(NS_ERR_CUDA, "ns_cross_entropy_noalloc: cuCtxGetCurrent failed");
+  if (!ctx) {
+    // No context on this thread yet (so no capture can be running either):
+    // cudaFree(NULL) makes the device's primary context current, allocating
+    // nothing.
+    NS_TRY_CUDA(cudaFree(nullptr), "ns_cross_entropy_noalloc: context");
+    if (get(&ctx) != CUDA_SUCCESS || !ctx)
+      return fail(NS_ERR_CUDA, "ns_cross_entropy_noalloc: no current context");
+  }
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!addr[dev] || ctx_of[dev] != ctx) {
     void* p = nullptr;
     NS_TRY_CUDA(cudaGetSymbolAddress(&p, g_ce_noalloc_rows),
                 "ns_cross_entropy_noalloc: cudaGetSymbolAddress");
     addr[dev] = static_cast<float*>(p);
+    ctx_of[dev] = ctx;
   }
   *out = addr[dev];
   return NS_OK;

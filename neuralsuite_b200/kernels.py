@@ -199,12 +199,14 @@ def layernorm_fwd(x, gamma, beta, eps=1e-5):
     return out, mean, rstd
 
 
-def layernorm_fwd_ex(raw, gamma, beta, bias=None, resid=None, want_lo=True, eps=1e-5):
-    """ns_layernorm_fwd_ex: (x, y, y_lo, mean, rstd) with x = resid + (raw + bias) if resid given."""
+def layernorm_fwd_ex(raw, gamma, beta, bias=None, resid=None, want_lo=True, eps=1e-5,
+                     in_place=False):
+    """ns_layernorm_fwd_ex: (x, y, y_lo, mean, rstd) with x = resid + (raw + bias) if resid
+    given; in_place writes x over raw (as the model does)."""
     lib = _lib.load()
     D = raw.shape[-1]
     N = raw.numel() // D
-    x = torch.empty_like(raw) if resid is not None else None
+    x = (raw if in_place else torch.empty_like(raw)) if resid is not None else None
     y = torch.empty_like(raw)
     lo = torch.empty_like(raw) if want_lo else None
     mean = torch.empty(N, dtype=_f32, device=raw.device)

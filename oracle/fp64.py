@@ -137,9 +137,12 @@ def split_params(flat, V, block, L, C):
     return out
 
 
-def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C):
+def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C, keep_probs=True):
     """GPTModel Forward -> CrossEntropy -> Backward (include/gpt.h:192-272) in float64.
 
+    keep_probs=False recomputes each layer's [B,H,T,T] probabilities in the
+    backward instead of keeping all of them (9.7 GB at 12 layers, B=8,
+    T=1024, H=12), the same numbers with less memory.
     Returns (loss, logits [B,T,V], grads flat)."""
     P = split_params(flat, V, block, L, C)
     idx = np.asarray(idx).astype(np.int64)
@@ -153,6 +156,8 @@ def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C):
         h1, m1, r1 = layernorm_fwd(x, g1, b1)
         qkv = h1 @ Wa + ba
         att, probs = attention_fwd(qkv, B, T, H, D)
+        if not keep_probs:
+            probs = None
         x1 = x + (att @ Wp + bp)
         h2, m2, r2 = layernorm_fwd(x1, g2, b2)
         fc = h2 @ Wf + bf
@@ -183,7 +188,10 @@ def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C):
         G[o + 4] = att.T @ dx1
         G[o + 5] = dx1.sum(0)
         datt = dx1 @ Wp.T
+        if probs is None:
+            probs = attention_fwd(qkv, B, T, H, D)[1]
         dqkv = attention_bwd(qkv, probs, datt, B, T, H, D)
+        del probs
         G[o + 2] = h1.T @ dqkv
         G[o + 3] = dqkv.sum(0)
         dh1 = dqkv @ Wa.T

@@ -154,3 +154,37 @@ def test_pointwise_and_split_checks(lib):
     _err(lib, lib.ns_gelu_fwd(FAKE, FAKE, -1, None), NS_ERR_INVALID_ARGUMENT, "n < 0")
     _err(lib, lib.ns_split_lo(FAKE, 4, 8, 4, FAKE, None), NS_ERR_INVALID_ARGUMENT, "bad shape")
     assert lib.ns_split_lo(FAKE, 0, 8, 8, FAKE, None) == NS_OK
+
+
+@pytest.mark.parametrize("call", ["forward", "loss_backward", "backward", "adamw_init",
+                                  "adamw_set_lr", "adamw_step", "clip_gradients", "train_step",
+                                  "set_comm"])
+def test_model_entry_points_reject_a_null_handle(lib, call):
+    args = {
+        "forward": (None, FAKE, 1, 1, None),
+        "loss_backward": (None, FAKE, None),
+        "backward": (None, None),
+        "adamw_init": (None, 1e-3, 0.9, 0.95, 1e-8, 0.01),
+        "adamw_set_lr": (None, 1e-3),
+        "adamw_step": (None, None),
+        "clip_gradients": (None, 1.0, None),
+        "train_step": (None, FAKE, FAKE, 1, 1, 0.0, None, None),
+        "set_comm": (None, None, 1, 0),
+    }[call]
+    _err(lib, getattr(lib, "ns_gpt_" + call)(*args), NS_ERR_INVALID_ARGUMENT, "NULL model")
+
+
+def test_model_getters_tolerate_a_null_handle(lib):
+    assert lib.ns_gpt_num_tensors(None) == 0
+    assert lib.ns_gpt_num_params(None) == 0
+    assert lib.ns_gpt_tensor_numel(None, 0) == 0
+    assert not lib.ns_gpt_params(None)
+
+
+def test_noalloc_cross_entropy_rejects_rows_beyond_its_static_scratch(lib):
+    """ns_cross_entropy_noalloc keeps its per-row scratch in a fixed device
+    array of NS_CE_NOALLOC_MAX_ROWS floats; a larger call is refused before
+    any device work, so this runs without a GPU."""
+    rows = 65536 + 1
+    rc = lib.ns_cross_entropy_noalloc(FAKE, FAKE, rows, 4, float(rows), FAKE, FAKE, FAKE, None)
+    _err(lib, rc, NS_ERR_INVALID_ARGUMENT, "NS_CE_NOALLOC_MAX_ROWS")

@@ -241,9 +241,10 @@ def test_gelu_fwd_lo_matches_parts_bitwise(cuda):
     assert np.array_equal(host(lo).view(np.uint32), want_lo.view(np.uint32))
 
 
-@pytest.mark.parametrize("N,D", [(8192, 768), (300, 128), (257, 132), (64, 100)])
+@pytest.mark.parametrize("N,D", [(8192, 768), (300, 128), (257, 132), (64, 100), (77, 130)])
 def test_layernorm_fwd_ex_matches_parts_bitwise(cuda, N, D):
-    """ns_layernorm_fwd_ex = residual add (GEMM epilogue rounding) + LayerNorm + lo split."""
+    """ns_layernorm_fwd_ex = residual add (GEMM epilogue rounding) + LayerNorm + lo split.
+    D=130 (not a multiple of 4) takes the scalar fallback path."""
     r = rng(N + D)
     raw = dev(normal(r, (N, D)), cuda)
     resid = dev(normal(r, (N, D)), cuda)
@@ -261,6 +262,14 @@ def test_layernorm_fwd_ex_matches_parts_bitwise(cuda, N, D):
     _, y3, lo3, _, _ = nk.layernorm_fwd_ex(x, gamma, beta)
     assert np.array_equal(host(y3).view(np.uint32), host(y2).view(np.uint32))
     assert np.array_equal(host(lo3).view(np.uint32), host(lo).view(np.uint32))
+    # the sum written over the GEMM product (x_out == x_raw), as GPTBlock does
+    raw2 = raw.clone()
+    x4, y4, lo4, _, _ = nk.layernorm_fwd_ex(raw2, gamma, beta, bias=bias, resid=resid,
+                                            in_place=True)
+    assert x4.data_ptr() == raw2.data_ptr()
+    assert np.array_equal(host(x4).view(np.uint32), host(x).view(np.uint32))
+    assert np.array_equal(host(y4).view(np.uint32), host(y).view(np.uint32))
+    assert np.array_equal(host(lo4).view(np.uint32), host(lo).view(np.uint32))
 
 
 def test_gemm_split_k_deterministic(cuda):

@@ -113,17 +113,28 @@ def test_train_step_matches_parts_and_learns(cuda):
     assert abs(l0 - losses[0]) <= 1e-6 * abs(l0), (l0, losses[0])
 
 
-def test_clip_gradients(cuda, port):
-    """ClipGradients(params, 1.0) of train_llm.cpp:112-129 on device."""
+@pytest.mark.parametrize("max_norm", [0.01, 1e6])
+def test_clip_gradients(cuda, port, max_norm):
+    """ClipGradients(params, max_norm) of train_llm.cpp:112-129 on device
+    against the oracle's restatement (serial float sum of squares, then the
+    in-place scale by max_norm / norm when norm > max_norm) after the same
+    forward/backward; 1e6 leaves the gradients untouched."""
     cfg, flat, idx, tgt = c1_inputs(seed=3)
     m = GPTModel(cfg, max_batch=8)
     m.set_params(flat)
     m.fwd_bwd(idx, tgt)
-    g = m.get_grads().astype(np.float64)
-    m.clip_gradients(0.01)
-    norm = np.sqrt((g * g).sum())
-    assert norm > 0.01
-    assert np.allclose(m.get_grads(), g * (0.01 / norm), rtol=1e-5, atol=1e-9)
+    o = port.gpt(cfg.vocab_size, cfg.block_size, cfg.n_layer, cfg.n_head, cfg.n_embd)
+    o.set_params(flat)
+    o.fwd_bwd(idx, tgt)
+    norm_ref = o.clip_gradients(max_norm)
+    _, _, g64 = fp64.gpt_fwd_bwd(flat, idx, tgt, cfg.vocab_size, cfg.block_size, cfg.n_layer,
+                                 cfg.n_head, cfg.n_embd)
+    norm64 = float(np.sqrt((g64 * g64).sum()))
+    assert abs(norm_ref - norm64) <= 1e-4 * norm64, (norm_ref, norm64)
+    m.clip_gradients(max_norm)
+    want64 = g64 * (max_norm / norm64) if norm64 > max_norm else g64
+    ok, info = close_report(m.get_grads(), o.get_grads(), want64)
+    assert ok, info
 
 
 def test_step_is_deterministic(cuda):
