@@ -41,6 +41,18 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
+    ap.add_argument("--case", default="step",
+                    choices=["step", "c1", "c2", "c3", "gemm", "attn", "bw"],
+                    help="step: the training-step benchmark (default, the one-line contract); "
+                         "c1 / c2 / c3: the 4-layer/128 step, the MatMul sweep, the "
+                         "MultiHeadAttention layer at B8/T1024/H12, each beside the reference "
+                         "on the host cores; gemm / attn / bw: single-kernel cases for profilers")
+    ap.add_argument("--shape", default="",
+                    help="gemm: M,N,K[,a_trans,b_trans]; attn: B,T,H,D; bw: M,C,V")
+    ap.add_argument("--reps", type=int, default=3, help="launches per kernel case")
+    ap.add_argument("--engine", type=int, default=0, help="gemm / attn engine of the case")
+    ap.add_argument("--epilogue", type=int, default=0, help="gemm case epilogue")
+    ap.add_argument("--presplit", action="store_true", help="gemm case: pass the lo parts in")
     return ap.parse_args()
 
 
@@ -470,9 +482,313 @@ def run_ours(args, rank, world, local):
         print(json.dumps(out), flush=True)
 
 
+# ----------------------------------------------------------- other configurations
+
+def _event_ms(torch, fn, reps, warm=1):
+    """Median CUDA-event time (ms) of fn over reps launches on the current stream."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        out.append(s.elapsed_time(e))
+    return statistics.median(out)
+
+
+def _host_ms(fn, reps, warm=1):
+    """Median wall time (ms) of a host call (the reference's MedianMs pattern,
+    benchmarks/benchmark.cpp:37-50)."""
+    for _ in range(warm):
+        fn()
+    out = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        out.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(out)
+
+
+def _ref_or_none(args):
+    import oracle
+
+    if args.no_cpu_baseline or not oracle.ref_available():
+        return None
+    o = oracle.ref()
+    o.set_threads(os.cpu_count() or 1)
+    return o
+
+
+def case_c1(args, torch):
+    """GPTModel 4 layers / n_embd 128 / 4 heads, T=64, B=8, vocab 256, AdamW
+    lr 3e-4: the full training step (forward + CrossEntropy + backward +
+    AdamW) from plain stream launches and from a CUDA-graph replay of the
+    same launches; the forward + CrossEntropy + backward part alone (the
+    reference's benchmark --train pattern, benchmarks/benchmark.cpp:118-157);
+    the reference's full step on the host cores beside it."""
+    from neuralsuite_b200 import GPTConfig, GPTModel, init_params
+
+    Vc, L, H, C, Tc, Bc = 256, 4, 4, 128, 64, 8
+    cfg = GPTConfig(Vc, Tc, L, H, C)
+    flat = init_params(cfg, np.random.default_rng(1234))
+    m = GPTModel(cfg, max_batch=Bc)
+    m.set_params(flat)
+    m.adamw_init(3e-4)
+    r = np.random.default_rng(7)
+    tok = torch.as_tensor(r.integers(0, Vc, (Bc, Tc)).astype(np.int32), device="cuda")
+    tgt = torch.as_tensor(r.integers(0, Vc, Bc * Tc).astype(np.int32), device="cuda")
+    steps = max(args.steps, 20)
+
+    def step():
+        m.train_step(tok, tgt, read_loss=False)
+
+    def fwd_bwd():
+        m.forward(tok)
+        m.loss_backward(tgt)
+        m.backward()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ms_step = _event_ms(torch, lambda: [step() for _ in range(steps)], 3) / steps
+    ms_fb = _event_ms(torch, lambda: [fwd_bwd() for _ in range(steps)], 3) / steps
+    graph_ms, graph_note = None, None
+    try:
+        g = torch.cuda.CUDAGraph()
+        sidestream = torch.cuda.Stream()
+        sidestream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(sidestream):
+            step()
+        torch.cuda.current_stream().wait_stream(sidestream)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            step()
+        graph_ms = _event_ms(torch, lambda: [g.replay() for _ in range(steps)], 3) / steps
+        del g
+    except Exception as ex:  # capture is reported, not required
+        graph_note = f"capture failed: {ex}"
+    toks = Bc * Tc
+    out = {"case": "c1", "workload": "GPTModel 4L/128/4h, T=64, B=8, vocab 256, AdamW lr 3e-4",
+           "unit": "tokens/s", "tokens_per_step": toks,
+           "step_us": ms_step * 1e3, "step_tokens_per_s": toks / ms_step * 1e3,
+           "fwd_bwd_us": ms_fb * 1e3, "fwd_bwd_tokens_per_s": toks / ms_fb * 1e3,
+           "graph_step_us": None if graph_ms is None else graph_ms * 1e3,
+           "graph_step_tokens_per_s": None if graph_ms is None else toks / graph_ms * 1e3,
+           "graph_note": graph_note,
+           "roofline": "latency-bound (2.62 GFLOP per 512-token step); no roofline fraction"}
+    o = _ref_or_none(args)
+    if o is not None:
+        gr = o.gpt(Vc, Tc, L, H, C)
+        gr.set_params(flat)
+        gr.adamw_init(3e-4)
+        idx, tg = tok.cpu().numpy().astype(np.float32), tgt.cpu().numpy().astype(np.float32)
+
+        def ref_step():
+            gr.fwd_bwd(idx, tg)
+            gr.adamw_step()
+
+        rms = _host_ms(ref_step, 10)
+        rfb = _host_ms(lambda: gr.fwd_bwd(idx, tg), 10)
+        out["reference"] = {"step_ms": rms, "step_tokens_per_s": toks / rms * 1e3,
+                            "fwd_bwd_ms": rfb, "fwd_bwd_tokens_per_s": toks / rfb * 1e3,
+                            "cores": os.cpu_count(), "how": "median of 10 after 1 warm-up"}
+    return out
+
+
+def case_c2(args, torch):
+    """The MatMul sweep: X[M,K], W[K,N], dY[M,N] ~ N(0,1); Y = X.W, dX = dY.W^T,
+    dW = X^T.dY per shape, each a single ns_gemm call on fresh operands (the
+    3xTF32 operand split inside the call), beside the reference's MatMul
+    (src/tensor.cpp:198-271) on the host cores (its Transpose copies are made
+    outside the timed region)."""
+    from neuralsuite_b200 import kernels as nk
+
+    bf16_burst, _, _, src = peaks()
+    peak3 = bf16_burst / 2 / 3
+    o = _ref_or_none(args)
+    rows = []
+    for M, K, N in [(512, 128, 512), (8192, 768, 3072), (8192, 3072, 768), (16384, 1024, 4096)]:
+        g = torch.Generator(device="cuda").manual_seed(M + K + N)
+        X = torch.randn(M, K, device="cuda", generator=g)
+        W = torch.randn(K, N, device="cuda", generator=g)
+        dY = torch.randn(M, N, device="cuda", generator=g)
+        fl = 2.0 * M * N * K
+        row = {"mkn": [M, K, N], "gflop": fl / 1e9}
+        forms = {"Y": (X, W, False, False), "dX": (dY, W, False, True), "dW": (X, dY, True, False)}
+        for name, (A, Bm, at, bt) in forms.items():
+            ms = _event_ms(torch, lambda: nk.gemm(A, Bm, a_trans=at, b_trans=bt), max(args.reps, 5))
+            row[name] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms / 1e9 / peak3}
+        if o is not None:
+            Xh, Wh, dYh = X.cpu().numpy(), W.cpu().numpy(), dY.cpu().numpy()
+            host = {"Y": (Xh, Wh), "dX": (dYh, np.ascontiguousarray(Wh.T)),
+                    "dW": (np.ascontiguousarray(Xh.T), dYh)}
+            for name, (A, Bm) in host.items():
+                ms = _host_ms(lambda: o.matmul(A, Bm), 3)
+                row[name]["reference_ms"] = ms
+                row[name]["reference_gflops"] = fl / ms / 1e6
+        rows.append(row)
+        del X, W, dY
+    return {"case": "c2", "workload": "MatMul sweep, fp32 N(0,1) operands", "unit": "TFLOP/s",
+            "peak": peak3, "peak_source": f"{src}: bf16 burst {bf16_burst} / 2 (TF32) / 3 (3xTF32)",
+            "reference_cores": os.cpu_count() if o is not None else None, "shapes": rows}
+
+
+def case_c3(args, torch):
+    """MultiHeadAttention layer, B=8, T=1024, 12 heads, n_embd 768: forward
+    (c_attn + causal attention + c_proj) and backward (the four projection
+    gradients, dqkv, dx) composed from the C ABI, and the attention core
+    alone, beside the reference layer's Forward + Backward on the host."""
+    from neuralsuite_b200 import _lib
+    from neuralsuite_b200 import kernels as nk
+
+    Bc, Tc, H, C = 8, 1024, 12, 768
+    D = C // H
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(Bc * Tc, C, device="cuda", generator=g)
+    dy = torch.randn(Bc * Tc, C, device="cuda", generator=g)
+    wa = torch.randn(C, 3 * C, device="cuda", generator=g) * 0.02
+    ba = torch.zeros(3 * C, device="cuda")
+    wp = torch.randn(C, C, device="cuda", generator=g) * 0.02
+    bp = torch.zeros(C, device="cuda")
+    st = {}
+
+    def fwd():
+        st["qkv"] = nk.gemm(x, wa, epilogue=_lib.EPI_BIAS, bias=ba)
+        st["att"], st["lse"] = nk.attn_fwd(st["qkv"], Bc, Tc, H, D)
+        st["y"] = nk.gemm(st["att"], wp, epilogue=_lib.EPI_BIAS, bias=bp)
+
+    def bwd():
+        nk.gemm(st["att"], dy, a_trans=True)
+        nk.bias_grad(dy)
+        datt = nk.gemm(dy, wp, b_trans=True)
+        dqkv = nk.attn_bwd(st["qkv"], st["att"], datt, st["lse"], Bc, Tc, H, D)
+        nk.gemm(x, dqkv, a_trans=True)
+        nk.bias_grad(dqkv)
+        nk.gemm(dqkv, wa, b_trans=True)
+
+    reps = max(args.reps, 5)
+    f_ms = _event_ms(torch, fwd, reps)
+    fwd()
+    b_ms = _event_ms(torch, bwd, reps)
+    datt = nk.gemm(dy, wp, b_trans=True)
+    cf = _event_ms(torch, lambda: nk.attn_fwd(st["qkv"], Bc, Tc, H, D), reps)
+    cb = _event_ms(torch, lambda: nk.attn_bwd(st["qkv"], st["att"], datt, st["lse"], Bc, Tc, H, D),
+                   reps)
+    bf16_burst, _, _, src = peaks()
+    peak3 = bf16_burst / 2 / 3
+    core_f, core_b = 4.0 * Bc * H * D * Tc * (Tc + 1) / 2, 8.0 * Bc * H * D * Tc * (Tc + 1) / 2
+    proj_f = 2.0 * Bc * Tc * C * 4 * C
+    out = {"case": "c3", "workload": "MultiHeadAttention B=8, T=1024, H=12, C=768 (D=64)",
+           "layer_fwd_ms": f_ms, "layer_bwd_ms": b_ms,
+           "layer_fwd_tflops": (core_f + proj_f) / f_ms / 1e9,
+           "layer_bwd_tflops": (core_b + 2 * proj_f) / b_ms / 1e9,
+           "core_fwd_ms": cf, "core_bwd_ms": cb,
+           "core_fwd_tflops": core_f / cf / 1e9, "core_bwd_tflops": core_b / cb / 1e9,
+           "core_fwd_frac": core_f / cf / 1e9 / peak3, "core_bwd_frac": core_b / cb / 1e9 / peak3,
+           "peak": peak3, "peak_source": f"{src}: bf16 burst {bf16_burst} / 2 / 3",
+           "flops_note": "causal triangle: core fwd 4*B*H*D*T(T+1)/2 (S, O), bwd "
+                         "8*B*H*D*T(T+1)/2 (dP, dV, dQ, dK; the recomputed S not counted); "
+                         "projections 2*M*C*4C forward, twice that backward"}
+    o = _ref_or_none(args)
+    if o is not None:
+        xh = x.cpu().numpy().reshape(Bc, Tc, C)
+        dyh = dy.cpu().numpy().reshape(Bc, Tc, C)
+        wah, bah, wph, bph = (t.cpu().numpy() for t in (wa, ba, wp, bp))
+        rms = _host_ms(lambda: o.mha(Bc, Tc, C, H, wah, bah, wph, bph, xh, dyh), 1)
+        out["reference"] = {"layer_fwd_bwd_ms": rms, "cores": os.cpu_count(),
+                            "how": "one Forward + Backward after 1 warm-up"}
+    return out
+
+
+def case_kernel(args, torch):
+    """Single-kernel cases sized for profiler captures (a few GB at most)."""
+    from neuralsuite_b200 import kernels as nk
+
+    dev = torch.device("cuda")
+    torch.manual_seed(0)
+    shape = [int(v) for v in args.shape.split(",")] if args.shape else []
+    if args.case == "gemm":
+        M, N, K = shape[:3]
+        at, bt = (bool(shape[3]), bool(shape[4])) if len(shape) > 4 else (False, False)
+        nk.set_gemm_engine(args.engine)
+        A = torch.randn((K, M) if at else (M, K), device=dev)
+        Bm = torch.randn((N, K) if bt else (K, N), device=dev)
+        kw = {"out": torch.empty(M, N, device=dev), "epilogue": args.epilogue}
+        if args.epilogue in (1, 2, 3):
+            kw["bias"] = torch.randn(N, device=dev)
+        if args.epilogue in (3, 4):
+            kw["aux"] = torch.randn(M, N, device=dev)
+        if args.presplit:
+            kw.update(a_lo=nk.split_lo(A), b_lo=nk.split_lo(Bm))
+        ms = _event_ms(torch, lambda: nk.gemm(A, Bm, a_trans=at, b_trans=bt, **kw), args.reps, 0)
+        nk.set_gemm_engine(0)
+        out = {"case": "gemm", "mnk": [M, N, K], "a_trans": at, "b_trans": bt,
+               "epilogue": args.epilogue, "presplit": args.presplit, "ms": ms,
+               "tflops": 2.0 * M * N * K / ms / 1e9}
+    elif args.case == "attn":
+        Bc, Tc, H, D = shape[:4]
+        qkv = torch.randn(Bc * Tc, 3 * H * D, device=dev)
+        dout = torch.randn(Bc * Tc, H * D, device=dev)
+        nk.attn_set_engine(args.engine)
+        o, lse = nk.attn_fwd(qkv, Bc, Tc, H, D)
+        f = _event_ms(torch, lambda: nk.attn_fwd(qkv, Bc, Tc, H, D), args.reps, 0)
+        b = _event_ms(torch, lambda: nk.attn_bwd(qkv, o, dout, lse, Bc, Tc, H, D), args.reps, 0)
+        nk.attn_set_engine(0)
+        out = {"case": "attn", "bthd": [Bc, Tc, H, D], "engine": args.engine, "fwd_ms": f,
+               "bwd_ms": b}
+    else:
+        M, C, Vc = shape[:3] if shape else (8192, 768, 256)
+        F = 4 * C
+        rn = lambda *sh: torch.randn(*sh, device=dev)
+        x, resid, raw = rn(M, C), rn(M, C), rn(M, C)
+        g, b, bias = rn(C), rn(C), rn(C)
+        dy3, pre3, dyq, logits = rn(M, F), rn(M, F), rn(M, 3 * C), rn(M, Vc)
+        tgt = torch.randint(0, Vc, (M,), device=dev, dtype=torch.int32)
+        tok = torch.randint(0, Vc, (M // 1024, 1024), device=dev, dtype=torch.int32)
+        wte, wpe = rn(Vc, C), rn(1024, C)
+        P = 86_039_040
+        params, grads = rn(P), rn(P)
+        mm, vv = torch.zeros(P, device=dev), torch.zeros(P, device=dev)
+        _, _, _, mean, rstd = nk.layernorm_fwd_ex(x, g, b)
+        cases = [
+            ("ln_fwd_ex (resid + LayerNorm + lo)", (5 * M * C + 2 * M) * 4,
+             lambda: nk.layernorm_fwd_ex(raw, g, b, bias=bias, resid=resid)),
+            ("ln_bwd (+ dresid)", 4 * M * C * 4, lambda: nk.layernorm_bwd(x, x, g, mean, rstd, dresid=resid)),
+            ("bias_grad_split N=3C", 2 * M * 3 * C * 4, lambda: nk.bias_grad_split(dyq)),
+            ("bias_grad_split_gelu N=4C", 4 * M * F * 4, lambda: nk.bias_grad_split_gelu(dy3, pre3)),
+            ("gelu_fwd_lo N=4C", 3 * M * F * 4, lambda: nk.gelu_fwd_lo(pre3)),
+            ("split_lo [M, C]", 2 * M * C * 4, lambda: nk.split_lo(x)),
+            ("cross_entropy", 2 * M * Vc * 4, lambda: nk.cross_entropy(logits, tgt)),
+            ("embedding_fwd", 2 * M * C * 4, lambda: nk.embedding_fwd(tok, wte, wpe)),
+            ("adamw_flat", 7 * P * 4, lambda: nk.adamw_flat(params, grads, mm, vv, [0, P], [0.0],
+                                                           3e-4, 0.9, 0.95, 1e-8, 0.1, 0.05)),
+        ]
+        rows = []
+        for name, nbytes, fn in cases:
+            ms = _event_ms(torch, fn, args.reps)
+            rows.append({"kernel": name, "us": ms * 1e3, "mb": nbytes / 1e6, "gbs": nbytes / ms / 1e6})
+        out = {"case": "bw", "m_c_v": [M, C, Vc], "kernels": rows}
+    nk.kernel_health()
+    return out
+
+
+def run_case(args):
+    import torch
+
+    fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3}.get(args.case, case_kernel)
+    print(json.dumps(fn(args, torch)), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.case != "step":
+        run_case(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

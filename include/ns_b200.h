@@ -141,6 +141,13 @@ NS_API ns_status ns_gemm_set_engine(int engine);
  * It synchronises with the device: do not call it while a stream is being
  * captured. */
 NS_API ns_status ns_kernel_health(void);
+/* No reference counterpart: a self-test of the bounded device waits above.
+ * Launches one warp that waits, with the kernels' own wait routine but a limit
+ * of limit_us microseconds (at most 1 s) instead of 2 s, on an mbarrier that
+ * nothing arrives at; the wait runs out, raises the flag, and the kernel
+ * returns, leaving the context usable.  The next ns_kernel_health() returns
+ * NS_ERR_TIMEOUT. */
+NS_API ns_status ns_selftest_device_wait(int limit_us, void* stream);
 
 /* Column sums db[n] = sum_m dY[m,n]: the bias gradient of Linear::Backward
  * (include/layers/linear.h:104-111, overwritten).  Deterministic two-stage
@@ -324,6 +331,12 @@ NS_API ns_status ns_clip_scale(float* x, int64_t n, const float* sumsq, float ma
  * reference has no distributed code; these exist for the data-parallel step. */
 typedef struct ns_comm ns_comm;
 NS_API ns_status ns_comm_unique_id(uint8_t host_id_out[128]);
+/* Creates the communicator non-blocking and polls it until it is ready, with
+ * a 300 s deadline: a rank that never joins makes the others return
+ * NS_ERR_TIMEOUT (communicator aborted) instead of blocking inside NCCL.
+ * Collectives that NCCL reports as still being enqueued, and the end-of-step
+ * wait of ns_gpt_train_step, are polled with deadlines the same way, and an
+ * asynchronous NCCL error aborts the communicator (NS_ERR_COMM). */
 NS_API ns_status ns_comm_init(const uint8_t host_id[128], int world_size, int rank, ns_comm** out);
 /* In-place sum over ranks of count floats on `stream`. */
 NS_API ns_status ns_comm_allreduce_sum(ns_comm* comm, float* buf, int64_t count, void* stream);
@@ -331,6 +344,17 @@ NS_API ns_status ns_comm_allreduce_sum(ns_comm* comm, float* buf, int64_t count,
 NS_API ns_status ns_comm_check(ns_comm* comm);
 NS_API ns_status ns_comm_abort(ns_comm* comm);
 NS_API ns_status ns_comm_destroy(ns_comm* comm);
+/* No reference counterpart: a self-test of the deadline and abort logic above
+ * against a fake NCCL (no GPU and no NCCL needed).  The communicator's real
+ * poll loop runs on a fake communicator whose behaviour the scenario sets:
+ *   0  the awaited work finishes after a few polls        -> NS_OK
+ *   1  it never finishes                                  -> NS_ERR_TIMEOUT
+ *   2  NCCL reports an asynchronous (remote) error        -> NS_ERR_COMM
+ *   3  a non-blocking creation that never completes       -> NS_ERR_TIMEOUT
+ *   4  a non-blocking creation that completes             -> NS_OK
+ * timeout_s is the deadline; *aborts (may be NULL) receives how many times the
+ * loop aborted the communicator (1 in scenarios 1-3, 0 otherwise). */
+NS_API ns_status ns_comm_selftest(int scenario, double timeout_s, int* aborts);
 
 /* ------------------------------------------------------------ GPT model
  * The device GPTModel (include/gpt.h:136-327) + CrossEntropyLoss + AdamW, with

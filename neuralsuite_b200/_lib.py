@@ -56,6 +56,7 @@ _SIGS = {
     "ns_split_lo": (c_int, [P, c_int, c_int, c_int, P, P]),
     "ns_gemm_set_engine": (c_int, [c_int]),
     "ns_kernel_health": (c_int, []),
+    "ns_selftest_device_wait": (c_int, [c_int, P]),
     "ns_bias_grad_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_bias_grad": (c_int, [P, c_int, c_int, P, P, c_size_t, P]),
     "ns_bias_grad_split": (c_int, [P, c_int, c_int, P, P, P, c_size_t, P]),
@@ -92,6 +93,7 @@ _SIGS = {
     "ns_comm_check": (c_int, [P]),
     "ns_comm_abort": (c_int, [P]),
     "ns_comm_destroy": (c_int, [P]),
+    "ns_comm_selftest": (c_int, [c_int, ctypes.c_double, P]),
     "ns_gpt_create": (c_int, [P, P]),
     "ns_gpt_destroy": (c_int, [P]),
     "ns_gpt_num_tensors": (c_int, [P]),

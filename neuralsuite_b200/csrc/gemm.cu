@@ -234,6 +234,12 @@ ns_status ns_split_lo(const float* x, int rows, int cols, int ld, float* lo, voi
   return tc::split_operand(x, rows, cols, ld, lo, as_stream(stream));
 }
 
+ns_status ns_selftest_device_wait(int limit_us, void* stream) {
+  NS_REQUIRE(limit_us > 0 && limit_us <= 1000000, "ns_selftest_device_wait: limit_us must be in (0, 1e6]");
+  if (ns_device_supported() != 1) return fail(NS_ERR_UNSUPPORTED, "ns_selftest_device_wait: no sm_100 device");
+  return tc::wait_probe(limit_us, as_stream(stream));
+}
+
 ns_status ns_kernel_health(void) {
   const int g = tc::consume_timeout_flag();
   const int a = attn_tc::consume_timeout_flag();

@@ -1444,6 +1444,29 @@ ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, c
   return split_lo(x, rows, cols, ld, lo, s);
 }
 
+// Self-test of the bounded waits: one warp waits on an mbarrier that nothing
+// arrives at, with the kernels' wait function and a short limit, so the wait
+// runs out, raises the timeout flag and the kernel returns.
+__global__ void wait_probe_k(unsigned long long limit_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  __shared__ int abort_flag;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const bool ok = mbar_wait_limit(b, 0, &abort_flag, &g_timeout, limit_ns);
+  __syncwarp();
+  if (threadIdx.x == 0 && ok) abort_flag = 2;  // unreachable: no thread arrives
+}
+
+ns_status wait_probe(int limit_us, cudaStream_t s) {
+  wait_probe_k<<<1, 32, 0, s>>>((unsigned long long)limit_us * 1000ull);
+  return check_launch("ns_selftest_device_wait");
+}
+
 // 1 if a kernel of this file raised the timeout flag since the last call
 // (the flag is cleared), 0 if not, or -(CUDA error) if the flag could not be
 // read or cleared (a sticky error, or a call during stream capture).

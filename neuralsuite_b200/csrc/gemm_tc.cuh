@@ -52,8 +52,13 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
 // lo = x - trunc_tf32(x) of a [rows, cols] matrix with row stride ld, compact.
 ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s);
 
-// 1 if a kernel hit a bounded-wait timeout since the last call (clears it).
+// 1 if a kernel hit a bounded-wait timeout since the last call (clears it);
+// -(CUDA error) if the flag could not be read.
 int consume_timeout_flag();
+
+// Launches the bounded-wait self-test kernel (a wait that runs out after
+// limit_us microseconds and raises the flag consume_timeout_flag reads).
+ns_status wait_probe(int limit_us, cudaStream_t s);
 
 }  // namespace tc
 }  // namespace nsb

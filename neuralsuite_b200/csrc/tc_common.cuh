@@ -63,23 +63,30 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of `parity`.  Returns false if the CTA is
-// aborting or this wait ran out of time (then it raises *abort and *flag).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int* flag) {
+// Bounded wait for the phase of `parity`, giving up after limit_ns.  Returns
+// false if the CTA is aborting or this wait ran out of time (then it raises
+// *abort and *flag).
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                int* flag, unsigned long long limit_ns) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 63) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kTimeoutNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         atomicExch(flag, 1);
         return false;
       }
     }
   }
+}
+
+// The kernels' wait: bounded at kTimeoutNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          int* flag) {
+  return mbar_wait_limit(bar, parity, abort, flag, kTimeoutNs);
 }
 
 // Wait that ignores the abort flag (used while draining), still bounded.
