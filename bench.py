@@ -303,7 +303,7 @@ def dp_checks(torch, dist, model, cfg, rank, world, n_batches):
         acc = torch.zeros(model.n_params, dtype=torch.float64, device="cuda")
         losses = []
         for r in range(world):
-            t_r, g_r = make_batches(r, 1)
+            t_r, g_r = make_batches(r, n_batches)  # the same draws as rank r's own
             solo.forward(torch.from_numpy(t_r[0]).cuda())
             losses.append(float(solo.loss_backward(torch.from_numpy(g_r[0]).cuda()).item()))
             solo.backward()

@@ -403,6 +403,34 @@ NS_API ns_status ns_gpt_clip_gradients(ns_gpt* model, float max_norm, void* stre
  * the step synchronises the stream and returns the loss. */
 NS_API ns_status ns_gpt_train_step(ns_gpt* model, const int32_t* tokens, const int32_t* targets, int B,
                             int T, float max_norm, float* host_loss, void* stream);
+/* ------------------------------------------------------------ checkpoints
+ * NSF weight files, byte for byte the format of the reference's
+ * nsf::Save / nsf::Load (include/serialization.h:128-287): magic, version,
+ * the architecture metadata of GPTModel::ArchitectureMetadata (gpt.h:309-316),
+ * then every parameter with its NamedParameters() path ("wte.weight",
+ * "blocks.0.attn.c_attn.weight", ...), shape and float32 data, and an FNV-1a
+ * checksum.  Files written here load in the reference and the reference's
+ * load here.  A load checks magic, version, every metadata value, tensor
+ * count, names, shapes, byte counts and the checksum before anything is
+ * copied to the model, so a rejected file (NS_ERR_INVALID_ARGUMENT, the
+ * reason in ns_last_error) leaves the parameters unchanged.
+ * GPTModel::SaveWeights / LoadWeights, include/gpt.h:293-306: */
+NS_API ns_status ns_gpt_save_weights(ns_gpt* model, const char* path, void* stream);
+NS_API ns_status ns_gpt_load_weights(ns_gpt* model, const char* path, void* stream);
+/* The same file format for a flat host array of parameters in registration
+ * order (no GPU needed): converting, inspecting or preparing checkpoints. */
+NS_API ns_status ns_nsf_save_gpt(const ns_gpt_config* cfg, const float* host_params, const char* path);
+NS_API ns_status ns_nsf_load_gpt(const ns_gpt_config* cfg, const char* path, float* host_params);
+/* No reference counterpart (the reference saves weights only, so a run
+ * cannot resume its optimizer): AdamW's first and second moments as tensors
+ * "m.<name>" / "v.<name>" in an NSF file whose metadata add arch
+ * "gpt-adamw", step, lr, beta1, beta2, eps and weight_decay.  Loading needs
+ * ns_gpt_adamw_init first (with the file's weight decay); it restores the
+ * moments, the step count and lr/betas/eps, so the next step continues the
+ * saved run bit for bit. */
+NS_API ns_status ns_gpt_save_optimizer(ns_gpt* model, const char* path, void* stream);
+NS_API ns_status ns_gpt_load_optimizer(ns_gpt* model, const char* path, void* stream);
+
 /* Data parallel: attach a communicator (NULL detaches).  bucket_floats caps a
  * gradient bucket (0 = one bucket per GPTBlock). */
 NS_API ns_status ns_gpt_set_comm(ns_gpt* model, ns_comm* comm, int world_size, int64_t bucket_floats);

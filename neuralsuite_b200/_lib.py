@@ -94,6 +94,12 @@ _SIGS = {
     "ns_comm_abort": (c_int, [P]),
     "ns_comm_destroy": (c_int, [P]),
     "ns_comm_selftest": (c_int, [c_int, ctypes.c_double, P]),
+    "ns_gpt_save_weights": (c_int, [P, ctypes.c_char_p, P]),
+    "ns_gpt_load_weights": (c_int, [P, ctypes.c_char_p, P]),
+    "ns_nsf_save_gpt": (c_int, [P, P, ctypes.c_char_p]),
+    "ns_nsf_load_gpt": (c_int, [P, ctypes.c_char_p, P]),
+    "ns_gpt_save_optimizer": (c_int, [P, ctypes.c_char_p, P]),
+    "ns_gpt_load_optimizer": (c_int, [P, ctypes.c_char_p, P]),
     "ns_gpt_create": (c_int, [P, P]),
     "ns_gpt_destroy": (c_int, [P]),
     "ns_gpt_num_tensors": (c_int, [P]),

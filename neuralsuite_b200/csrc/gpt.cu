@@ -8,14 +8,18 @@
 // stream joins the comm stream before the optimizer.  Because the
 // cross-entropy gradient is divided by rows * world_size, the sum over ranks
 // is the gradient of the global-batch mean loss.
+#include <cstdio>
 #include <cstring>
 #include <exception>
+#include <map>
+#include <string>
 #include <memory>
 #include <vector>
 
 #include "comm.h"
 #include "common.cuh"
 #include "gpt_device.h"
+#include "nsf.h"
 
 using neuralsuite::cuda::AdamW;
 using neuralsuite::cuda::Bucket;
@@ -100,9 +104,208 @@ ns_status backward_impl(ns_gpt* h, cudaStream_t s) {
   return NS_OK;
 }
 
+// ------------------------------------------------------------ checkpoints
+//
+// Names and shapes of GPTModel::NamedParameters() in registration order
+// (include/module.h:62-73 over the Register calls of include/gpt.h:59-63,
+// 143-149 and the layers'), and the architecture metadata of
+// GPTModel::ArchitectureMetadata() (include/gpt.h:309-316).
+std::vector<nsb::nsf::Entry> gpt_entries(const ns_gpt_config& c) {
+  const int V = c.vocab_size, B = c.block_size, C = c.n_embd;
+  std::vector<nsb::nsf::Entry> e;
+  auto add = [&](const std::string& name, std::vector<int> dims) { e.push_back({name, dims}); };
+  add("wte.weight", {V, C});
+  add("wpe.weight", {B, C});
+  for (int i = 0; i < c.n_layer; ++i) {
+    const std::string p = "blocks." + std::to_string(i) + ".";
+    add(p + "ln_1.gamma", {C});
+    add(p + "ln_1.beta", {C});
+    add(p + "attn.c_attn.weight", {C, 3 * C});
+    add(p + "attn.c_attn.bias", {3 * C});
+    add(p + "attn.c_proj.weight", {C, C});
+    add(p + "attn.c_proj.bias", {C});
+    add(p + "ln_2.gamma", {C});
+    add(p + "ln_2.beta", {C});
+    add(p + "mlp_fc.weight", {C, 4 * C});
+    add(p + "mlp_fc.bias", {4 * C});
+    add(p + "mlp_proj.weight", {4 * C, C});
+    add(p + "mlp_proj.bias", {C});
+  }
+  add("ln_f.gamma", {C});
+  add("ln_f.beta", {C});
+  return e;
+}
+
+std::map<std::string, std::string> gpt_meta(const ns_gpt_config& c) {
+  return {{"arch", "gpt"},
+          {"vocab_size", std::to_string(c.vocab_size)},
+          {"block_size", std::to_string(c.block_size)},
+          {"n_layer", std::to_string(c.n_layer)},
+          {"n_head", std::to_string(c.n_head)},
+          {"n_embd", std::to_string(c.n_embd)}};
+}
+
+ns_gpt_config config_of(const ns_gpt* h) {
+  const GPTConfig& g = h->model->Config();
+  return ns_gpt_config{g.vocab_size, g.block_size, g.n_layer, g.n_head, g.n_embd, 1};
+}
+
+// Points entries at consecutive slices of `base` (the flat registration-order
+// buffer); false if the table does not cover exactly n floats.
+bool bind_flat(std::vector<nsb::nsf::Entry>& e, float* base, int64_t n) {
+  int64_t off = 0;
+  for (auto& x : e) {
+    x.data = base + off;
+    x.out = base + off;
+    off += (int64_t)x.numel();
+  }
+  return off == n;
+}
+
+std::string fmt_float(float v) {
+  char b[32];
+  std::snprintf(b, sizeof(b), "%.9g", (double)v);
+  return b;
+}
+
 }  // namespace
 
 extern "C" {
+
+ns_status ns_nsf_save_gpt(const ns_gpt_config* cfg, const float* host_params, const char* path) {
+  NS_REQUIRE(cfg && host_params && path, "ns_nsf_save_gpt: NULL argument");
+  auto e = gpt_entries(*cfg);
+  int64_t n = 0;
+  for (auto& x : e) n += (int64_t)x.numel();
+  bind_flat(e, const_cast<float*>(host_params), n);
+  const std::string err = nsb::nsf::Write(path, gpt_meta(*cfg), e);
+  if (!err.empty()) return nsb::fail(NS_ERR_INVALID_ARGUMENT, "ns_nsf_save_gpt: " + err);
+  return NS_OK;
+}
+
+ns_status ns_nsf_load_gpt(const ns_gpt_config* cfg, const char* path, float* host_params) {
+  NS_REQUIRE(cfg && host_params && path, "ns_nsf_load_gpt: NULL argument");
+  auto e = gpt_entries(*cfg);
+  int64_t n = 0;
+  for (auto& x : e) n += (int64_t)x.numel();
+  // Read into a private buffer: the caller's array changes only on success.
+  std::vector<float> tmp((size_t)n);
+  bind_flat(e, tmp.data(), n);
+  const std::string err = nsb::nsf::Read(path, gpt_meta(*cfg), e);
+  if (!err.empty()) return nsb::fail(NS_ERR_INVALID_ARGUMENT, "ns_nsf_load_gpt: " + err);
+  std::memcpy(host_params, tmp.data(), tmp.size() * sizeof(float));
+  return NS_OK;
+}
+
+ns_status ns_gpt_save_weights(ns_gpt* h, const char* path, void* stream) {
+  NS_REQUIRE(h && path, "ns_gpt_save_weights: NULL argument");
+  return Guard([&]() -> ns_status {
+    GPTModel& m = *h->model;
+    std::vector<float> host((size_t)m.NumParams());
+    cudaStream_t s = nsb::as_stream(stream);
+    NS_TRY_CUDA(cudaMemcpyAsync(host.data(), m.Values(), host.size() * sizeof(float),
+                                cudaMemcpyDeviceToHost, s),
+                "ns_gpt_save_weights copy");
+    NS_TRY_CUDA(cudaStreamSynchronize(s), "ns_gpt_save_weights sync");
+    const ns_gpt_config c = config_of(h);
+    return ns_nsf_save_gpt(&c, host.data(), path);
+  });
+}
+
+ns_status ns_gpt_load_weights(ns_gpt* h, const char* path, void* stream) {
+  NS_REQUIRE(h && path, "ns_gpt_load_weights: NULL argument");
+  return Guard([&]() -> ns_status {
+    GPTModel& m = *h->model;
+    std::vector<float> host((size_t)m.NumParams());
+    const ns_gpt_config c = config_of(h);
+    ns_status rc = ns_nsf_load_gpt(&c, path, host.data());
+    if (rc != NS_OK) return rc;  // the device parameters are untouched
+    cudaStream_t s = nsb::as_stream(stream);
+    NS_TRY_CUDA(cudaMemcpyAsync(m.Values(), host.data(), host.size() * sizeof(float),
+                                cudaMemcpyHostToDevice, s),
+                "ns_gpt_load_weights copy");
+    NS_TRY_CUDA(cudaStreamSynchronize(s), "ns_gpt_load_weights sync");
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_save_optimizer(ns_gpt* h, const char* path, void* stream) {
+  NS_REQUIRE(h && path, "ns_gpt_save_optimizer: NULL argument");
+  NS_REQUIRE(h->opt, "ns_gpt_save_optimizer: optimizer not initialised");
+  return Guard([&]() -> ns_status {
+    GPTModel& m = *h->model;
+    const size_t n = (size_t)m.NumParams();
+    std::vector<float> host(2 * n);
+    float hyper[7];
+    cudaStream_t s = nsb::as_stream(stream);
+    NS_TRY_CUDA(cudaMemcpyAsync(host.data(), h->opt->M(), n * 4, cudaMemcpyDeviceToHost, s), "copy");
+    NS_TRY_CUDA(cudaMemcpyAsync(host.data() + n, h->opt->V(), n * 4, cudaMemcpyDeviceToHost, s), "copy");
+    NS_TRY_CUDA(cudaMemcpyAsync(hyper, h->opt->Hyper(), sizeof(hyper), cudaMemcpyDeviceToHost, s), "copy");
+    NS_TRY_CUDA(cudaStreamSynchronize(s), "ns_gpt_save_optimizer sync");
+    const ns_gpt_config c = config_of(h);
+    auto pm = gpt_entries(c), pv = gpt_entries(c);
+    bind_flat(pm, host.data(), (int64_t)n);
+    bind_flat(pv, host.data() + n, (int64_t)n);
+    std::vector<nsb::nsf::Entry> e;
+    for (auto& x : pm) e.push_back({"m." + x.name, x.dims, x.data, x.out});
+    for (auto& x : pv) e.push_back({"v." + x.name, x.dims, x.data, x.out});
+    int32_t step = 0;
+    std::memcpy(&step, &hyper[6], 4);
+    auto meta = gpt_meta(c);
+    meta["arch"] = "gpt-adamw";
+    meta["step"] = std::to_string(step);
+    meta["lr"] = fmt_float(hyper[0]);
+    meta["beta1"] = fmt_float(hyper[1]);
+    meta["beta2"] = fmt_float(hyper[2]);
+    meta["eps"] = fmt_float(hyper[3]);
+    meta["weight_decay"] = fmt_float(h->opt->WeightDecay());
+    const std::string err = nsb::nsf::Write(path, meta, e);
+    if (!err.empty()) return nsb::fail(NS_ERR_INVALID_ARGUMENT, "ns_gpt_save_optimizer: " + err);
+    return NS_OK;
+  });
+}
+
+ns_status ns_gpt_load_optimizer(ns_gpt* h, const char* path, void* stream) {
+  NS_REQUIRE(h && path, "ns_gpt_load_optimizer: NULL argument");
+  NS_REQUIRE(h->opt, "ns_gpt_load_optimizer: call ns_gpt_adamw_init first");
+  return Guard([&]() -> ns_status {
+    GPTModel& m = *h->model;
+    const size_t n = (size_t)m.NumParams();
+    std::vector<float> host(2 * n);
+    const ns_gpt_config c = config_of(h);
+    auto pm = gpt_entries(c), pv = gpt_entries(c);
+    bind_flat(pm, host.data(), (int64_t)n);
+    bind_flat(pv, host.data() + n, (int64_t)n);
+    std::vector<nsb::nsf::Entry> e;
+    for (auto& x : pm) e.push_back({"m." + x.name, x.dims, x.data, x.out});
+    for (auto& x : pv) e.push_back({"v." + x.name, x.dims, x.data, x.out});
+    auto expect = gpt_meta(c);
+    expect["arch"] = "gpt-adamw";
+    expect["weight_decay"] = fmt_float(h->opt->WeightDecay());
+    std::map<std::string, std::string> meta;
+    const std::string err = nsb::nsf::Read(path, expect, e, &meta);
+    if (!err.empty()) return nsb::fail(NS_ERR_INVALID_ARGUMENT, "ns_gpt_load_optimizer: " + err);
+    float hyper[7];
+    try {
+      hyper[0] = std::stof(meta.at("lr"));
+      hyper[1] = std::stof(meta.at("beta1"));
+      hyper[2] = std::stof(meta.at("beta2"));
+      hyper[3] = std::stof(meta.at("eps"));
+      hyper[4] = hyper[5] = 1.0f;  // bias corrections: recomputed by the next step
+      const int32_t step = (int32_t)std::stol(meta.at("step"));
+      std::memcpy(&hyper[6], &step, 4);
+    } catch (const std::exception&) {
+      return nsb::fail(NS_ERR_INVALID_ARGUMENT,
+                       "ns_gpt_load_optimizer: missing or malformed step / lr / beta / eps");
+    }
+    cudaStream_t s = nsb::as_stream(stream);
+    NS_TRY_CUDA(cudaMemcpyAsync(h->opt->M(), host.data(), n * 4, cudaMemcpyHostToDevice, s), "copy");
+    NS_TRY_CUDA(cudaMemcpyAsync(h->opt->V(), host.data() + n, n * 4, cudaMemcpyHostToDevice, s), "copy");
+    NS_TRY_CUDA(cudaMemcpyAsync(h->opt->Hyper(), hyper, sizeof(hyper), cudaMemcpyHostToDevice, s), "copy");
+    NS_TRY_CUDA(cudaStreamSynchronize(s), "ns_gpt_load_optimizer sync");
+    return NS_OK;
+  });
+}
 
 ns_status ns_gpt_create(const ns_gpt_config* cfg, ns_gpt** out) {
   NS_REQUIRE(cfg && out, "ns_gpt_create: NULL argument");

@@ -869,6 +869,7 @@ class AdamW {
     v_ = std::make_shared<DeviceBuffer>(n * sizeof(float));
     CheckCuda(cudaMemset(m_->get(), 0, n * sizeof(float)), "cudaMemset");
     CheckCuda(cudaMemset(v_->get(), 0, n * sizeof(float)), "cudaMemset");
+    wd_ = wd;
     for (int r : model.Ranks()) decay_.push_back(r >= 2 ? wd : 0.0f);
     const float h[7] = {lr, b1, b2, eps, 1.0f, 1.0f, 0.0f};
     CheckCuda(cudaMemcpy(Hyper(), h, sizeof(h), cudaMemcpyHostToDevice), "cudaMemcpy");
@@ -891,11 +892,17 @@ class AdamW {
               "cudaMemsetAsync");
   }
   float* Hyper() { return model_.Small() + 8; }
+  // Optimizer state, for checkpoints: first and second moments (flat, the
+  // parameters' offsets) and the weight decay given to rank >= 2 tensors.
+  float* M() { return static_cast<float*>(m_->get()); }
+  float* V() { return static_cast<float*>(v_->get()); }
+  float WeightDecay() const { return wd_; }
 
  private:
   GPTModel& model_;
   std::shared_ptr<DeviceBuffer> m_, v_;
   std::vector<float> decay_;
+  float wd_ = 0.0f;
   float lr_host_ = 0.0f;
 };
 

@@ -75,6 +75,24 @@ def init_params(cfg: GPTConfig, rng: np.random.Generator, std: float = 0.02,
     return np.concatenate(parts).astype(np.float32)
 
 
+def nsf_save(cfg: GPTConfig, flat, path: str) -> None:
+    """Flat host parameters (registration order) to an NSF file (no GPU)."""
+    lib = _lib.load()
+    a = np.ascontiguousarray(np.asarray(flat, dtype=np.float32))
+    c = _lib.ns_gpt_config(cfg.vocab_size, cfg.block_size, cfg.n_layer, cfg.n_head, cfg.n_embd, 1)
+    _lib.check(lib.ns_nsf_save_gpt(ctypes.byref(c), a.ctypes.data, str(path).encode()))
+
+
+def nsf_load(cfg: GPTConfig, path: str) -> np.ndarray:
+    """NSF file to flat host parameters, checked against cfg (no GPU)."""
+    lib = _lib.load()
+    n = sum(int(np.prod(s)) for s in param_shapes(cfg))
+    out = np.zeros(n, np.float32)
+    c = _lib.ns_gpt_config(cfg.vocab_size, cfg.block_size, cfg.n_layer, cfg.n_head, cfg.n_embd, 1)
+    _lib.check(lib.ns_nsf_load_gpt(ctypes.byref(c), str(path).encode(), out.ctypes.data))
+    return out
+
+
 def plan_buckets(cfg: GPTConfig, bucket_floats: int = 0):
     """Gradient all-reduce buckets [(begin, end), ...] in launch order (host only)."""
     lib = _lib.load()
@@ -223,6 +241,25 @@ class GPTModel:
                                               max_norm, ctypes.byref(out) if read_loss else None,
                                               self._stream()))
         return float(out.value) if read_loss else None
+
+    # ------------------------------------------------------------ checkpoints
+    def save_weights(self, path: str) -> None:
+        """GPTModel::SaveWeights (include/gpt.h:293-300): an NSF file the
+        reference reads."""
+        _lib.check(self.lib.ns_gpt_save_weights(self.h, str(path).encode(), self._stream()))
+
+    def load_weights(self, path: str) -> None:
+        """GPTModel::LoadWeights (include/gpt.h:302-306); raises ValueError with
+        the reason (wrong architecture, truncated, corrupt) and leaves the
+        parameters unchanged."""
+        _lib.check(self.lib.ns_gpt_load_weights(self.h, str(path).encode(), self._stream()))
+
+    def save_optimizer(self, path: str) -> None:
+        """AdamW moments, step count and hyper-parameters (NSF)."""
+        _lib.check(self.lib.ns_gpt_save_optimizer(self.h, str(path).encode(), self._stream()))
+
+    def load_optimizer(self, path: str) -> None:
+        _lib.check(self.lib.ns_gpt_load_optimizer(self.h, str(path).encode(), self._stream()))
 
     # ------------------------------------------------------------ data parallel
     def set_comm(self, comm, world: int, bucket_floats: int = 0):

@@ -19,6 +19,7 @@
 //   MultiHeadAttention      include/layers/attention.h:330-588
 //   GPTModel                include/gpt.h:136-327
 //   AdamW                   include/optimizers.h:143-253
+//   SaveWeights/LoadWeights include/gpt.h:293-306 (NSF, include/serialization.h)
 //   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
 //                           function of the training program, not a library
 //                           symbol)
@@ -324,6 +325,17 @@ void nsref_gpt_adamw_set_lr(void* handle, float lr) {
 int nsref_gpt_adamw_step(void* handle) {
   GptHandle* h = static_cast<GptHandle*>(handle);
   return Guard([&] { h->opt->Step(); });
+}
+
+// GPTModel::SaveWeights / LoadWeights (include/gpt.h:293-306): the NSF file
+// of include/serialization.h.  1 on success, 0 on failure (the reference
+// returns bool and prints the reason).
+int nsref_gpt_save_weights(void* handle, const char* path) {
+  return static_cast<GptHandle*>(handle)->model->SaveWeights(path) ? 1 : 0;
+}
+
+int nsref_gpt_load_weights(void* handle, const char* path) {
+  return static_cast<GptHandle*>(handle)->model->LoadWeights(path) ? 1 : 0;
 }
 
 int nsref_gpt_zero_grad(void* handle) {
