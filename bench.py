@@ -42,11 +42,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
     ap.add_argument("--case", default="step",
-                    choices=["step", "c1", "c2", "c3", "gemm", "attn", "bw"],
+                    choices=["step", "c1", "c2", "c3", "decode", "gemm", "attn", "bw"],
                     help="step: the training-step benchmark (default, the one-line contract); "
                          "c1 / c2 / c3: the 4-layer/128 step, the MatMul sweep, the "
                          "MultiHeadAttention layer at B8/T1024/H12, each beside the reference "
-                         "on the host cores; gemm / attn / bw: single-kernel cases for profilers")
+                         "on the host cores; decode: KV-cache decoding of the 12-layer model; "
+                         "gemm / attn / bw: single-kernel cases for profilers")
     ap.add_argument("--shape", default="",
                     help="gemm: M,N,K[,a_trans,b_trans]; attn: B,T,H,D; bw: M,C,V")
     ap.add_argument("--reps", type=int, default=3, help="launches per kernel case")
@@ -704,6 +705,68 @@ def case_c3(args, torch):
     return out
 
 
+def case_decode(args, torch):
+    """KV-cache decoding (GPTModel::ForwardWithKVCache) of the 12-layer/768
+    model: a prompt by prefill, then timed decode steps (CUDA events over
+    consecutive steps), for 1 and 8 sequences at a short and a long context.
+    Roofline: a step must read every weight once (86,039,040 floats) and the
+    cached K and V of every sequence and layer; achieved GB/s = those bytes /
+    step time, against the measured HBM copy bandwidth.  The reference's
+    ForwardWithKVCache is timed on the host at the short context."""
+    from neuralsuite_b200 import Decoder, GPTConfig, GPTModel, init_params
+
+    cfg = GPTConfig(V, BLOCK, LAYERS, HEADS, EMBD)
+    flat = init_params(cfg, np.random.default_rng(1234))
+    _, _, hbm, src = peaks()
+    steps = max(args.steps, 16)
+    rows = []
+    m = GPTModel(cfg, max_batch=8)
+    m.set_params(flat)
+    for B in (1, 8):
+        dec = Decoder(m, max_batch=B)
+        for ctx in (64, 960):
+            dec.clear()
+            r = np.random.default_rng(ctx + B)
+            dec.prefill(r.integers(0, V, (B, ctx)))
+            toks = [torch.as_tensor(r.integers(0, V, B).astype(np.int32), device="cuda")
+                    for _ in range(steps + 2)]
+            for i in range(2):
+                dec.step(toks[i], ctx + i)
+            torch.cuda.synchronize()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for i in range(steps):
+                dec.step(toks[2 + i], ctx + 2 + i)
+            e0.record()
+            torch.cuda.synchronize()
+            ms = s0.elapsed_time(e0) / steps
+            n_mid = ctx + 2 + steps // 2  # cached positions at the middle step
+            nbytes = 4 * (m.n_params + B * LAYERS * 2 * EMBD * n_mid)
+            rows.append({"sequences": B, "context": n_mid, "step_ms": ms,
+                         "tokens_per_s": B / ms * 1e3, "bytes_per_step": nbytes,
+                         "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm})
+        del dec
+    out = {"case": "decode", "workload": "GPTModel 12L/768/12h KV-cache decoding",
+           "peak_gbs": hbm, "peak_source": src, "rows": rows}
+    o = _ref_or_none(args)
+    if o is not None:
+        g = o.gpt(V, BLOCK, LAYERS, HEADS, EMBD)
+        g.set_params(flat)
+        g.clear_kv()
+        r = np.random.default_rng(9)
+        prompt = r.integers(0, V, 64)
+        for p, t in enumerate(prompt):
+            g.decode(int(t), p)
+        ts = []
+        for i in range(4):
+            t0 = time.perf_counter()
+            g.decode(int(r.integers(0, V)), 64 + i)
+            ts.append(time.perf_counter() - t0)
+        out["reference"] = {"sequences": 1, "context": 66, "step_ms": statistics.median(ts) * 1e3,
+                            "tokens_per_s": 1.0 / statistics.median(ts), "cores": os.cpu_count()}
+    return out
+
+
 def case_kernel(args, torch):
     """Single-kernel cases sized for profiler captures (a few GB at most)."""
     from neuralsuite_b200 import kernels as nk
@@ -779,7 +842,8 @@ def case_kernel(args, torch):
 def run_case(args):
     import torch
 
-    fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3}.get(args.case, case_kernel)
+    fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3, "decode": case_decode}.get(args.case,
+                                                                                 case_kernel)
     print(json.dumps(fn(args, torch)), flush=True)
 
 

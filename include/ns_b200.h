@@ -431,6 +431,37 @@ NS_API ns_status ns_nsf_load_gpt(const ns_gpt_config* cfg, const char* path, flo
 NS_API ns_status ns_gpt_save_optimizer(ns_gpt* model, const char* path, void* stream);
 NS_API ns_status ns_gpt_load_optimizer(ns_gpt* model, const char* path, void* stream);
 
+/* ------------------------------------------------------- KV-cache decoding
+ * GPTModel::ForwardWithKVCache (include/gpt.h:159-190, with
+ * MultiHeadAttention::ForwardWithKVCache, include/layers/attention.h:481-546)
+ * for B sequences that advance together, one token each per step.  The
+ * decoder owns a device KV cache of block_size positions for up to max_batch
+ * sequences of `model` and reads the model's current parameters at every
+ * step.  ns_gpt_decoder_clear is ClearKVCache (gpt.h:153-157).
+ * ns_gpt_decode_step: tokens (device int32 [B]) at position `pos` (the wpe
+ * row, as the reference's pos_idx; the token's K and V are appended to the
+ * cache whatever pos is, as in the reference) -> logits [B, vocab] in
+ * logits_out (device; NULL: the decoder's own buffer, ns_gpt_decoder_logits).
+ * A token outside [0, vocab) sets *err_flag (device int; NULL: an internal
+ * flag).  pos >= block_size or a full cache: NS_ERR_OUT_OF_RANGE.
+ * ns_gpt_decoder_prefill: the prompt tokens [B, T] (device int32) through
+ * the model's batched forward; the cache then holds what decoding the prompt
+ * token by token at positions 0..T-1 leaves (ns_gpt_decoder_length = T), and
+ * logits_out receives each sequence's last-position logits [B, vocab].  No
+ * reference counterpart for the prefill (the reference decodes the prompt
+ * one token at a time, generate_llm.cpp:146-149); B <= the model's
+ * max_batch. */
+typedef struct ns_gpt_decoder ns_gpt_decoder;
+NS_API ns_status ns_gpt_decoder_create(ns_gpt* model, int max_batch, ns_gpt_decoder** out);
+NS_API ns_status ns_gpt_decoder_destroy(ns_gpt_decoder* dec);
+NS_API ns_status ns_gpt_decoder_clear(ns_gpt_decoder* dec);
+NS_API int ns_gpt_decoder_length(const ns_gpt_decoder* dec);
+NS_API float* ns_gpt_decoder_logits(ns_gpt_decoder* dec);
+NS_API ns_status ns_gpt_decode_step(ns_gpt_decoder* dec, const int32_t* tokens, int B, int pos,
+                                    float* logits_out, int32_t* err_flag, void* stream);
+NS_API ns_status ns_gpt_decoder_prefill(ns_gpt_decoder* dec, const int32_t* tokens, int B, int T,
+                                        float* logits_out, void* stream);
+
 /* Data parallel: attach a communicator (NULL detaches).  bucket_floats caps a
  * gradient bucket (0 = one bucket per GPTBlock). */
 NS_API ns_status ns_gpt_set_comm(ns_gpt* model, ns_comm* comm, int world_size, int64_t bucket_floats);

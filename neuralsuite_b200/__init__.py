@@ -5,9 +5,12 @@ C ABI of ``include/ns_b200.h``); this package is its Python face:
 
 * ``kernels`` -- one wrapper per kernel entry point (MatMul, attention,
   LayerNorm, GELU, cross-entropy, embedding, AdamW), for tests and tools;
-* ``model`` -- the device GPTModel + CrossEntropyLoss + AdamW step and the
-  NCCL communicator used for data parallel training.
+* ``model`` -- the device GPTModel + CrossEntropyLoss + AdamW step, its NSF
+  checkpoints, the KV-cache ``Decoder`` and the NCCL communicator used for
+  data parallel training.
 """
-from .model import Comm, GPTConfig, GPTModel, init_params, param_shapes, plan_buckets  # noqa: F401
+from .model import (Comm, Decoder, GPTConfig, GPTModel, init_params, nsf_load,  # noqa: F401
+                    nsf_save, param_shapes, plan_buckets)
 
-__all__ = ["Comm", "GPTConfig", "GPTModel", "init_params", "param_shapes", "plan_buckets"]
+__all__ = ["Comm", "Decoder", "GPTConfig", "GPTModel", "init_params", "nsf_load", "nsf_save",
+           "param_shapes", "plan_buckets"]

@@ -100,6 +100,13 @@ _SIGS = {
     "ns_nsf_load_gpt": (c_int, [P, ctypes.c_char_p, P]),
     "ns_gpt_save_optimizer": (c_int, [P, ctypes.c_char_p, P]),
     "ns_gpt_load_optimizer": (c_int, [P, ctypes.c_char_p, P]),
+    "ns_gpt_decoder_create": (c_int, [P, c_int, P]),
+    "ns_gpt_decoder_destroy": (c_int, [P]),
+    "ns_gpt_decoder_clear": (c_int, [P]),
+    "ns_gpt_decoder_length": (c_int, [P]),
+    "ns_gpt_decoder_logits": (P, [P]),
+    "ns_gpt_decode_step": (c_int, [P, P, c_int, c_int, P, P, P]),
+    "ns_gpt_decoder_prefill": (c_int, [P, P, c_int, c_int, P, P]),
     "ns_gpt_create": (c_int, [P, P]),
     "ns_gpt_destroy": (c_int, [P]),
     "ns_gpt_num_tensors": (c_int, [P]),

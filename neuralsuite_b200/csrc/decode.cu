@@ -1,0 +1,543 @@
+// KV-cache decoding: GPTModel::ForwardWithKVCache (include/gpt.h:159-190),
+// GPTBlock::ForwardWithKVCache (gpt.h:102-116) and
+// MultiHeadAttention::ForwardWithKVCache (include/layers/attention.h:481-546)
+// for B sequences that advance in lockstep, one token each per step.
+//
+// The reference decodes one token of one sequence with scalar loops and keeps
+// its cache as vectors of per-position rows.  Here the cache lives in HBM as
+// K and V arrays [layer][sequence][head][position][head_dim] (one head's keys
+// are one contiguous block), and a step is bandwidth-bound: every weight is
+// read once per step (344 MB for the 12-layer/768 model) plus the cached
+// keys and values of every sequence.  So:
+//  * the projections are split-K CUDA-core GEMVs (gemv_partial_k): each CTA
+//    streams a [K-chunk x 128-column] slab of the weight with 16-byte loads
+//    and applies it to all (up to 8) sequences at once; the partials are
+//    summed in a fixed order by gemv_finish_k, which also adds the bias and
+//    applies the residual add or the GELU of the layer (Linear::Forward,
+//    ElementwiseAdd, GeluForward order of operations);
+//  * attention is split over key chunks (dec_attn_partial_k: one CTA per
+//    sequence, head and chunk, an online softmax per warp) and merged by
+//    dec_attn_combine_k in chunk order, so results do not depend on timing;
+//  * a prefill (ns_gpt_decoder_prefill) runs the batched training forward on
+//    the prompt (tensor cores) and copies each layer's K and V columns into
+//    the cache, which is what decoding the prompt token by token computes.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gpt_handle.h"
+
+using neuralsuite::cuda::GPTModel;
+
+struct ns_gpt_decoder {
+  ns_gpt* owner = nullptr;
+  int max_batch = 0, cap = 0, L = 0, H = 0, D = 0, C = 0, V = 0;
+  int B = 0, len = 0;  // sequences in the cache and cached positions per sequence
+  float* kc = nullptr;  // [L][max_batch][H][cap][D]
+  float* vc = nullptr;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *x1 = nullptr, *g = nullptr;
+  float *xf = nullptr, *logits = nullptr, *mean = nullptr, *rstd = nullptr, *part = nullptr;
+  size_t part_floats = 0;
+  int32_t* err = nullptr;
+  std::vector<void*> allocs;
+};
+
+namespace nsb {
+namespace decode {
+namespace {
+
+constexpr int kGvCols = 128;  // columns per CTA: 32 lanes x 4
+constexpr int kGvWarps = 8;
+constexpr int kGvRows = 8;    // sequences per CTA (more go to further grid.z slices)
+
+enum GvMode { kBias = 0, kBiasResid = 1, kBiasGelu = 2 };
+
+// part[s][b][n] = sum over k in split s of X[b][k] * W[k][n].  grid: x =
+// column block, y = K split, z = group of 8 sequences.  Each warp takes every
+// 8th row of the split; the eight warps' sums are added in warp order.
+__global__ void __launch_bounds__(256) gemv_partial_k(const float* __restrict__ X, int B, int K,
+                                                      const float* __restrict__ W, int N, int kchunk,
+                                                      int vec, float* __restrict__ part) {
+  extern __shared__ float sm[];
+  float* sx = sm;                          // [kGvRows][kchunk]
+  float* red = sm + kGvRows * kchunk;      // [kGvWarps][kGvRows][kGvCols]
+  const int n0 = blockIdx.x * kGvCols, s = blockIdx.y, b0 = blockIdx.z * kGvRows;
+  const int k0 = s * kchunk, kc = min(K, k0 + kchunk) - k0;
+  const int nb = min(kGvRows, B - b0);
+  for (int i = threadIdx.x; i < kGvRows * kchunk; i += blockDim.x) {
+    const int b = i / kchunk, k = i % kchunk;
+    sx[i] = (b < nb && k < kc) ? X[(size_t)(b0 + b) * K + k0 + k] : 0.0f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = n0 + lane * 4;
+  float acc[kGvRows][4];
+#pragma unroll
+  for (int b = 0; b < kGvRows; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.0f;
+  for (int k = warp; k < kc; k += kGvWarps) {
+    const float* wrow = W + (size_t)(k0 + k) * N;
+    float4 w;
+    if (vec && n + 3 < N) {
+      w = __ldg(reinterpret_cast<const float4*>(wrow + n));
+    } else {
+      w.x = n < N ? wrow[n] : 0.0f;
+      w.y = n + 1 < N ? wrow[n + 1] : 0.0f;
+      w.z = n + 2 < N ? wrow[n + 2] : 0.0f;
+      w.w = n + 3 < N ? wrow[n + 3] : 0.0f;
+    }
+#pragma unroll
+    for (int b = 0; b < kGvRows; ++b) {
+      const float xv = sx[b * kchunk + k];
+      acc[b][0] = fmaf(xv, w.x, acc[b][0]);
+      acc[b][1] = fmaf(xv, w.y, acc[b][1]);
+      acc[b][2] = fmaf(xv, w.z, acc[b][2]);
+      acc[b][3] = fmaf(xv, w.w, acc[b][3]);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < kGvRows; ++b)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[(warp * kGvRows + b) * kGvCols + lane * 4 + j] = acc[b][j];
+  __syncthreads();
+  for (int i = threadIdx.x; i < nb * kGvCols; i += blockDim.x) {
+    const int b = i / kGvCols, c = i % kGvCols;
+    if (n0 + c >= N) continue;
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kGvWarps; ++w) sum += red[(w * kGvRows + b) * kGvCols + c];
+    part[((size_t)s * B + b0 + b) * N + n0 + c] = sum;
+  }
+}
+
+// out[b][n] = epilogue(sum over splits s in order of part[s][b][n] + bias[n]).
+__global__ void gemv_finish_k(const float* __restrict__ part, int splits, int B, int N,
+                              const float* __restrict__ bias, int mode,
+                              const float* __restrict__ resid, float* __restrict__ out) {
+  const int64_t total = (int64_t)B * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float sum = 0.0f;
+    for (int s = 0; s < splits; ++s) sum += part[(size_t)s * total + i];
+    const float v = __fadd_rn(sum, bias[i % N]);
+    out[i] = mode == kBiasResid ? __fadd_rn(resid[i], v) : mode == kBiasGelu ? gelu_f(v) : v;
+  }
+}
+
+// x[b] = wte[tok[b]] + wpe[pos] (GPTModel::ForwardWithKVCache's embedding add).
+__global__ void dec_embed_k(const int32_t* __restrict__ tok, int B, const float* __restrict__ wte,
+                            int V, const float* __restrict__ wpe, int pos, int C,
+                            float* __restrict__ x, int32_t* err) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * C; i += gridDim.x * blockDim.x) {
+    const int b = i / C, c = i % C;
+    int t = tok[b];
+    if (t < 0 || t >= V) {
+      if (err) atomicExch(err, 1);
+      x[i] = 0.0f;
+      continue;
+    }
+    x[i] = __fadd_rn(wte[(size_t)t * C + c], wpe[(size_t)pos * C + c]);
+  }
+}
+
+// K and V of rows [row0, row0 + nrows) of each sequence's qkv ([rows, 3C],
+// sequence b's row r at b * seq_stride + r) to cache positions [idx, idx + nrows).
+__global__ void dec_append_k(const float* __restrict__ qkv, int B, int nrows, int seq_stride, int C,
+                             int H, int D, float* __restrict__ kc, float* __restrict__ vc, int cap,
+                             int idx) {
+  const int64_t total = (int64_t)B * nrows * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int r = (int)((i / C) % nrows);
+    const int b = (int)(i / ((int64_t)C * nrows));
+    const int h = c / D, d = c % D;
+    const float* src = qkv + ((size_t)b * seq_stride + r) * 3 * C;
+    const size_t dst = (((size_t)b * H + h) * cap + idx + r) * D + d;
+    kc[dst] = src[C + c];
+    vc[dst] = src[2 * C + c];
+  }
+}
+
+// Partial attention of the query of sequence b, head h over cached keys
+// [s*kch, min(n, (s+1)*kch)): per warp an online softmax (running max m,
+// sum l, output o); the four warps merged in order.  part: [B*H][S][2 + D].
+constexpr int kAttThreads = 128;
+__global__ void __launch_bounds__(kAttThreads) dec_attn_partial_k(
+    const float* __restrict__ qkv, int C, int H, int D, const float* __restrict__ kc,
+    const float* __restrict__ vc, int cap, int n, int kch, float scale, float* __restrict__ part) {
+  __shared__ float wm[4], wl[4];
+  __shared__ float wo[4][128];
+  const int bh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const int b = bh / H, h = bh % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* q = qkv + (size_t)b * 3 * C + h * D;
+  float qv[4], o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d = lane + 32 * j;
+    qv[j] = d < D ? q[d] : 0.0f;
+    o[j] = 0.0f;
+  }
+  const float* kb = kc + ((size_t)b * H + h) * cap * D;
+  const float* vb = vc + ((size_t)b * H + h) * cap * D;
+  const int t0 = s * kch, t1 = min(n, t0 + kch);
+  float m = -INFINITY, l = 0.0f;
+  for (int t = t0 + warp; t < t1; t += 4) {
+    float dot = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = lane + 32 * j;
+      if (d < D) dot = fmaf(qv[j], kb[(size_t)t * D + d], dot);
+    }
+    const float sc = warp_sum(dot) * scale;
+    const float mn = fmaxf(m, sc);
+    const float corr = expf(m - mn);
+    const float p = expf(sc - mn);
+    l = l * corr + p;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = lane + 32 * j;
+      o[j] = o[j] * corr + (d < D ? p * vb[(size_t)t * D + d] : 0.0f);
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    wm[warp] = m;
+    wl[warp] = l;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (lane + 32 * j < D) wo[warp][lane + 32 * j] = o[j];
+  __syncthreads();
+  float* dst = part + ((size_t)bh * S + s) * (2 + D);
+  float M = -INFINITY;
+  for (int w = 0; w < 4; ++w)
+    if (wl[w] > 0.0f) M = fmaxf(M, wm[w]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float od = 0.0f;
+    for (int w = 0; w < 4; ++w)
+      if (wl[w] > 0.0f) od += wo[w][d] * expf(wm[w] - M);
+    dst[2 + d] = od;
+  }
+  if (threadIdx.x == 0) {
+    float Lsum = 0.0f;
+    for (int w = 0; w < 4; ++w)
+      if (wl[w] > 0.0f) Lsum += wl[w] * expf(wm[w] - M);
+    dst[0] = M;
+    dst[1] = Lsum;
+  }
+}
+
+// att[b][h*D + d] = (sum over chunks of o * e^(m - M)) / (sum of l * e^(m - M)).
+__global__ void dec_attn_combine_k(const float* __restrict__ part, int S, int H, int D, int C,
+                                   float* __restrict__ att) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const float* p = part + (size_t)bh * S * (2 + D);
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s)
+    if (p[(size_t)s * (2 + D) + 1] > 0.0f) M = fmaxf(M, p[(size_t)s * (2 + D)]);
+  float Lsum = 0.0f;
+  for (int s = 0; s < S; ++s) {
+    const float* ps = p + (size_t)s * (2 + D);
+    if (ps[1] > 0.0f) Lsum += ps[1] * expf(ps[0] - M);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float od = 0.0f;
+    for (int s = 0; s < S; ++s) {
+      const float* ps = p + (size_t)s * (2 + D);
+      if (ps[1] > 0.0f) od += ps[2 + d] * expf(ps[0] - M);
+    }
+    att[(size_t)b * C + h * D + d] = od / Lsum;
+  }
+}
+
+// logits[b][v] = sum_c xf[b][c] * wte[v][c]: one warp per vocabulary row
+// (read once, 16-byte loads), up to 8 sequences from shared memory.
+__global__ void __launch_bounds__(256) dec_logits_k(const float* __restrict__ xf, int B, int C,
+                                                    const float* __restrict__ wte, int V, int vec,
+                                                    float* __restrict__ logits) {
+  extern __shared__ float sxf[];  // [8][C]
+  const int b0 = blockIdx.y * 8, nb = min(8, B - b0);
+  for (int i = threadIdx.x; i < 8 * C; i += blockDim.x) {
+    const int b = i / C;
+    sxf[i] = b < nb ? xf[(size_t)(b0 + b) * C + i % C] : 0.0f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int v = blockIdx.x * 8 + warp;
+  if (v >= V) return;
+  const float* row = wte + (size_t)v * C;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (vec) {
+    for (int c = lane * 4; c < C; c += 128) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(row + c));
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const float* xb = sxf + b * C + c;
+        acc[b] = fmaf(xb[0], w.x, fmaf(xb[1], w.y, fmaf(xb[2], w.z, fmaf(xb[3], w.w, acc[b]))));
+      }
+    }
+  } else {
+    for (int c = lane; c < C; c += 32) {
+      const float w = row[c];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) acc[b] = fmaf(sxf[b * C + c], w, acc[b]);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const float t = warp_sum(acc[b]);
+    if (lane == 0 && b < nb) logits[(size_t)(b0 + b) * V + v] = t;
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((work + threads - 1) / threads,
+                                                     (int64_t)sm_count() * 8));
+}
+
+// Split of a [K x N] product: (column blocks, K splits, rows per split).
+struct GvPlan {
+  int cols, splits, kchunk;
+};
+GvPlan gv_plan(int K, int N) {
+  GvPlan p;
+  p.cols = (N + kGvCols - 1) / kGvCols;
+  const int target = 2 * sm_count();
+  int s = std::max(1, std::min((target + p.cols - 1) / p.cols, (K + kGvWarps - 1) / kGvWarps));
+  p.kchunk = ((K + s - 1) / s + kGvWarps - 1) / kGvWarps * kGvWarps;
+  p.splits = (K + p.kchunk - 1) / p.kchunk;
+  return p;
+}
+
+size_t gv_part_floats(int B, int K, int N) {
+  const GvPlan p = gv_plan(K, N);
+  return (size_t)p.splits * B * N;
+}
+
+ns_status gemv(ns_gpt_decoder* d, const float* X, int B, int K, const float* W, int N,
+               const float* bias, int mode, const float* resid, float* out, cudaStream_t s) {
+  const GvPlan p = gv_plan(K, N);
+  if ((size_t)p.splits * B * N > d->part_floats) return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small");
+  const int vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
+  const size_t smem = (size_t)(kGvRows * p.kchunk + kGvWarps * kGvRows * kGvCols) * sizeof(float);
+  if (smem > 48 * 1024)
+    NS_TRY_CUDA(cudaFuncSetAttribute(gemv_partial_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "decode gemv attr");
+  dim3 grid(p.cols, p.splits, (B + kGvRows - 1) / kGvRows);
+  gemv_partial_k<<<grid, 256, smem, s>>>(X, B, K, W, N, p.kchunk, vec, d->part);
+  ns_status rc = check_launch("decode gemv");
+  if (rc != NS_OK) return rc;
+  gemv_finish_k<<<grid_for((int64_t)B * N, 256), 256, 0, s>>>(d->part, p.splits, B, N, bias, mode,
+                                                              resid, out);
+  return check_launch("decode gemv finish");
+}
+
+// Attention of the B current queries (in d->qkv) over n cached positions per sequence of layer l.
+ns_status attend(ns_gpt_decoder* d, int l, int B, int n, cudaStream_t s) {
+  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
+  const int kch = 64;
+  const int S = (n + kch - 1) / kch;
+  if ((size_t)B * d->H * S * (2 + d->D) > d->part_floats)
+    return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small for attention");
+  dim3 grid(B * d->H, S);
+  dec_attn_partial_k<<<grid, kAttThreads, 0, s>>>(d->qkv, d->C, d->H, d->D, d->kc + l * per_layer,
+                                                  d->vc + l * per_layer, d->cap, n, kch,
+                                                  1.0f / std::sqrt((float)d->D), d->part);
+  ns_status rc = check_launch("decode attention");
+  if (rc != NS_OK) return rc;
+  dec_attn_combine_k<<<B * d->H, 128, 0, s>>>(d->part, S, d->H, d->D, d->C, d->att);
+  return check_launch("decode attention combine");
+}
+
+template <typename T>
+ns_status dev_alloc(ns_gpt_decoder* d, T** p, size_t count) {
+  void* q = nullptr;
+  NS_TRY_CUDA(cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T)), "ns_gpt_decoder_create");
+  d->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return NS_OK;
+}
+
+void free_all(ns_gpt_decoder* d) {
+  for (void* p : d->allocs) cudaFree(p);
+  d->allocs.clear();
+}
+
+}  // namespace
+}  // namespace decode
+}  // namespace nsb
+
+using namespace nsb;
+using namespace nsb::decode;
+
+extern "C" {
+
+ns_status ns_gpt_decoder_create(ns_gpt* model, int max_batch, ns_gpt_decoder** out) {
+  NS_REQUIRE(model && out, "ns_gpt_decoder_create: NULL argument");
+  NS_REQUIRE(max_batch >= 1 && max_batch <= 64, "ns_gpt_decoder_create: max_batch must be in [1, 64]");
+  const auto& cfg = model->model->Config();
+  NS_REQUIRE(cfg.n_head > 0 && cfg.n_embd % cfg.n_head == 0 && cfg.n_embd / cfg.n_head <= 128,
+             "ns_gpt_decoder_create: head_dim must be at most 128");
+  auto* d = new ns_gpt_decoder();
+  d->owner = model;
+  d->max_batch = max_batch;
+  d->cap = cfg.block_size;
+  d->L = cfg.n_layer;
+  d->H = cfg.n_head;
+  d->C = cfg.n_embd;
+  d->D = cfg.n_embd / cfg.n_head;
+  d->V = cfg.vocab_size;
+  const size_t Bm = (size_t)max_batch, C = d->C;
+  const size_t cache = (size_t)std::max(d->L, 1) * Bm * d->H * d->cap * d->D;
+  size_t part = 0;
+  for (auto kn : {std::make_pair(C, 3 * C), std::make_pair(C, C), std::make_pair(C, 4 * C),
+                  std::make_pair(4 * C, C)})
+    part = std::max(part, gv_part_floats((int)Bm, (int)kn.first, (int)kn.second));
+  part = std::max(part, Bm * d->H * (size_t)((d->cap + 63) / 64) * (2 + d->D));
+  d->part_floats = part;
+  ns_status rc = NS_OK;
+  auto A = [&](float** p, size_t n) {
+    if (rc == NS_OK) rc = dev_alloc(d, p, n);
+  };
+  A(&d->kc, cache);
+  A(&d->vc, cache);
+  A(&d->x, Bm * C);
+  A(&d->h, Bm * C);
+  A(&d->qkv, Bm * 3 * C);
+  A(&d->att, Bm * C);
+  A(&d->x1, Bm * C);
+  A(&d->g, Bm * 4 * C);
+  A(&d->xf, Bm * C);
+  A(&d->logits, Bm * d->V);
+  A(&d->mean, Bm);
+  A(&d->rstd, Bm);
+  A(&d->part, part);
+  if (rc == NS_OK) rc = dev_alloc(d, &d->err, 1);
+  if (rc == NS_OK) {
+    cudaError_t e = cudaMemset(d->err, 0, sizeof(int32_t));
+    if (e != cudaSuccess) rc = cuda_fail(e, "ns_gpt_decoder_create");
+  }
+  if (rc != NS_OK) {
+    free_all(d);
+    delete d;
+    return rc;
+  }
+  *out = d;
+  return NS_OK;
+}
+
+ns_status ns_gpt_decoder_destroy(ns_gpt_decoder* d) {
+  if (!d) return NS_OK;
+  cudaDeviceSynchronize();
+  free_all(d);
+  delete d;
+  return NS_OK;
+}
+
+ns_status ns_gpt_decoder_clear(ns_gpt_decoder* d) {
+  NS_REQUIRE(d, "ns_gpt_decoder_clear: NULL decoder");
+  d->len = 0;
+  d->B = 0;
+  return NS_OK;
+}
+
+int ns_gpt_decoder_length(const ns_gpt_decoder* d) { return d ? d->len : 0; }
+
+float* ns_gpt_decoder_logits(ns_gpt_decoder* d) { return d ? d->logits : nullptr; }
+
+ns_status ns_gpt_decode_step(ns_gpt_decoder* d, const int32_t* tokens, int B, int pos,
+                             float* logits_out, int32_t* err_flag, void* stream) {
+  NS_REQUIRE(d && tokens, "ns_gpt_decode_step: NULL argument");
+  NS_REQUIRE(B >= 1 && B <= d->max_batch, "ns_gpt_decode_step: B must be in [1, max_batch]");
+  NS_REQUIRE(d->len == 0 || B == d->B,
+             "ns_gpt_decode_step: B differs from the sequences in the cache (clear it first)");
+  if (pos < 0 || pos >= d->cap)
+    return fail(NS_ERR_OUT_OF_RANGE, "ns_gpt_decode_step: position outside [0, block_size)");
+  if (d->len >= d->cap)
+    return fail(NS_ERR_OUT_OF_RANGE, "ns_gpt_decode_step: the KV cache is full (block_size positions)");
+  cudaStream_t s = as_stream(stream);
+  GPTModel& m = *d->owner->model;
+  const float* P = m.Values();
+  const auto& off = m.Offsets();
+  const int C = d->C, L = d->L;
+  auto prm = [&](int i) { return P + off[i]; };
+  int32_t* err = err_flag ? err_flag : d->err;
+  dec_embed_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(tokens, B, prm(0), d->V, prm(1), pos, C,
+                                                           d->x, err);
+  ns_status rc = check_launch("decode embedding");
+  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
+  for (int l = 0; l < L && rc == NS_OK; ++l) {
+    const int t = 2 + 12 * l;
+    // x1 = x + c_proj(attention(c_attn(ln_1(x))))
+    rc = ns_layernorm_fwd(d->x, prm(t), prm(t + 1), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
+    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 2), 3 * C, prm(t + 3), kBias, nullptr, d->qkv, s);
+    if (rc == NS_OK) {
+      dec_append_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->qkv, B, 1, 1, C, d->H, d->D,
+                                                                 d->kc + l * per_layer,
+                                                                 d->vc + l * per_layer, d->cap, d->len);
+      rc = check_launch("decode cache append");
+    }
+    if (rc == NS_OK) rc = attend(d, l, B, d->len + 1, s);
+    if (rc == NS_OK) rc = gemv(d, d->att, B, C, prm(t + 4), C, prm(t + 5), kBiasResid, d->x, d->x1, s);
+    // x = x1 + mlp_proj(gelu(mlp_fc(ln_2(x1))))
+    if (rc == NS_OK)
+      rc = ns_layernorm_fwd(d->x1, prm(t + 6), prm(t + 7), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
+    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 8), 4 * C, prm(t + 9), kBiasGelu, nullptr, d->g, s);
+    if (rc == NS_OK) rc = gemv(d, d->g, B, 4 * C, prm(t + 10), C, prm(t + 11), kBiasResid, d->x1, d->x, s);
+  }
+  if (rc != NS_OK) return rc;
+  const int f = 2 + 12 * L;
+  rc = ns_layernorm_fwd(d->x, prm(f), prm(f + 1), d->xf, d->mean, d->rstd, B, C, 1e-5f, stream);
+  if (rc != NS_OK) return rc;
+  float* lg = logits_out ? logits_out : d->logits;
+  const int vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(prm(0)) & 15) == 0);
+  const size_t smem = (size_t)8 * C * sizeof(float);
+  if (smem > 48 * 1024)
+    NS_TRY_CUDA(cudaFuncSetAttribute(dec_logits_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "decode logits attr");
+  dim3 grid((d->V + 7) / 8, (B + 7) / 8);
+  dec_logits_k<<<grid, 256, smem, s>>>(d->xf, B, C, prm(0), d->V, vec, lg);
+  rc = check_launch("decode logits");
+  if (rc != NS_OK) return rc;
+  d->B = B;
+  d->len += 1;
+  return NS_OK;
+}
+
+ns_status ns_gpt_decoder_prefill(ns_gpt_decoder* d, const int32_t* tokens, int B, int T,
+                                 float* logits_out, void* stream) {
+  NS_REQUIRE(d && tokens, "ns_gpt_decoder_prefill: NULL argument");
+  NS_REQUIRE(d->len == 0, "ns_gpt_decoder_prefill: the cache is not empty (clear it first)");
+  NS_REQUIRE(B >= 1 && B <= d->max_batch, "ns_gpt_decoder_prefill: B must be in [1, max_batch]");
+  NS_REQUIRE(B <= d->owner->model->MaxBatch(), "ns_gpt_decoder_prefill: B exceeds the model's max_batch");
+  if (T < 1 || T > d->cap)
+    return fail(NS_ERR_OUT_OF_RANGE, "ns_gpt_decoder_prefill: T outside [1, block_size]");
+  ns_status rc = ns_gpt_forward(d->owner, tokens, B, T, stream);
+  if (rc != NS_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  GPTModel& m = *d->owner->model;
+  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
+  for (int l = 0; l < d->L; ++l) {
+    const float* qkv = m.Block(l).Attn().Qkv().Data();
+    dec_append_k<<<grid_for((int64_t)B * T * d->C, 256), 256, 0, s>>>(
+        qkv, B, T, T, d->C, d->H, d->D, d->kc + l * per_layer, d->vc + l * per_layer, d->cap, 0);
+    rc = check_launch("prefill cache fill");
+    if (rc != NS_OK) return rc;
+  }
+  // The last position's logits of each sequence.
+  float* lg = logits_out ? logits_out : d->logits;
+  NS_TRY_CUDA(cudaMemcpy2DAsync(lg, (size_t)d->V * sizeof(float),
+                                m.Logits().Data() + (size_t)(T - 1) * d->V,
+                                (size_t)T * d->V * sizeof(float), (size_t)d->V * sizeof(float), B,
+                                cudaMemcpyDeviceToDevice, s),
+              "prefill logits");
+  d->B = B;
+  d->len = T;
+  return NS_OK;
+}
+
+}  // extern "C"

@@ -19,6 +19,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "gpt_device.h"
+#include "gpt_handle.h"
 #include "nsf.h"
 
 using neuralsuite::cuda::AdamW;
@@ -26,19 +27,6 @@ using neuralsuite::cuda::Bucket;
 using neuralsuite::cuda::GPTConfig;
 using neuralsuite::cuda::GPTModel;
 
-struct ns_gpt {
-  std::unique_ptr<GPTModel> model;
-  std::unique_ptr<AdamW> opt;
-  ns_comm* comm = nullptr;
-  int world = 1;
-  std::vector<Bucket> buckets;
-  cudaStream_t comm_stream = nullptr;
-  std::vector<cudaEvent_t> group_ready;
-  cudaEvent_t comm_done = nullptr;
-  cudaEvent_t step_done = nullptr;
-  float* host_small = nullptr;  // pinned: loss + error flags
-  int B = 0, T = 0;
-};
 
 namespace {
 

@@ -455,6 +455,9 @@ class MultiHeadAttention : public Layer {
   }
   Linear& AttnProjection() { return c_attn_; }
   Linear& OutProjection() { return c_proj_; }
+  // The last forward's c_attn output [B*T, 3C] (the KV-cache prefill reads
+  // its K and V columns).
+  const Tensor& Qkv() const { return qkv_; }
 
  private:
   Tensor ForwardImpl(const Tensor& x, const Tensor* resid, const float* x_lo, bool no_bias) {
@@ -547,6 +550,7 @@ class GPTBlock : public Layer {
   }
   const float* OpenBias() { return mlp_proj_.BiasParam().Value().Data(); }
   const Tensor& OpenResid() const { return x1_; }
+  MultiHeadAttention& Attn() { return attn_; }
   // GPTBlock::Backward (gpt.h:82-100) with the GELU backward fused into the
   // mlp_fc bias-gradient pass and both residual adds fused into LayerNorm
   // backward.
@@ -729,6 +733,7 @@ class GPTModel : public Module {
 
   const GPTConfig& Config() const { return config_; }
   int MaxBatch() const { return max_batch_; }
+  GPTBlock& Block(int i) { return *blocks_[i]; }
   float* Values() { return static_cast<float*>(values_->get()); }
   float* Grads() { return static_cast<float*>(grads_->get()); }
   int64_t NumParams() const { return offsets_.back(); }

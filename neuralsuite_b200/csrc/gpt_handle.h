@@ -1,0 +1,23 @@
+// The model handle behind the ns_gpt_* C ABI (shared by gpt.cu and the
+// KV-cache decoder in decode.cu).
+#pragma once
+
+#include <memory>
+#include <vector>
+
+#include "comm.h"
+#include "gpt_device.h"
+
+struct ns_gpt {
+  std::unique_ptr<neuralsuite::cuda::GPTModel> model;
+  std::unique_ptr<neuralsuite::cuda::AdamW> opt;
+  ns_comm* comm = nullptr;
+  int world = 1;
+  std::vector<neuralsuite::cuda::Bucket> buckets;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> group_ready;
+  cudaEvent_t comm_done = nullptr;
+  cudaEvent_t step_done = nullptr;
+  float* host_small = nullptr;  // pinned: loss + error flags
+  int B = 0, T = 0;
+};

@@ -273,6 +273,57 @@ class GPTModel:
         return torch.cuda.current_stream().cuda_stream
 
 
+class Decoder:
+    """KV-cache decoding of B sequences in lockstep on a GPTModel
+    (GPTModel::ForwardWithKVCache / ClearKVCache, include/gpt.h:153-190)."""
+
+    def __init__(self, model: GPTModel, max_batch: int = 1):
+        self.model = model
+        self.lib = model.lib
+        h = ctypes.c_void_p()
+        _lib.check(self.lib.ns_gpt_decoder_create(model.h, max_batch, ctypes.byref(h)))
+        self.h = h
+        self.err = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h:
+            self.lib.ns_gpt_decoder_destroy(h)
+            self.h = None
+
+    def clear(self):
+        _lib.check(self.lib.ns_gpt_decoder_clear(self.h))
+
+    def __len__(self):
+        return int(self.lib.ns_gpt_decoder_length(self.h))
+
+    def step(self, tokens, pos: int, out: torch.Tensor = None) -> torch.Tensor:
+        """One token per sequence at position pos -> logits [B, V] (device)."""
+        t = self.model._ids(tokens, "token", self.model.cfg.vocab_size).reshape(-1)
+        B = t.numel()
+        if out is None:
+            out = torch.empty(B, self.model.cfg.vocab_size, device="cuda")
+        _lib.check(self.lib.ns_gpt_decode_step(self.h, t.data_ptr(), B, pos, out.data_ptr(),
+                                               self.err.data_ptr(), GPTModel._stream()))
+        return out
+
+    def prefill(self, tokens) -> torch.Tensor:
+        """Prompt tokens [B, T] through the batched forward; fills the cache
+        and returns the last position's logits [B, V]."""
+        t = self.model._ids(tokens, "token", self.model.cfg.vocab_size)
+        B, T = t.shape
+        out = torch.empty(B, self.model.cfg.vocab_size, device="cuda")
+        _lib.check(self.lib.ns_gpt_decoder_prefill(self.h, t.data_ptr(), B, T, out.data_ptr(),
+                                                   GPTModel._stream()))
+        return out
+
+    def check(self):
+        """Raises IndexError if a token of an earlier step was out of range."""
+        if int(self.err.item()):
+            self.err.zero_()
+            raise IndexError("a decoded token id is outside [0, vocab_size)")
+
+
 class Comm:
     """NCCL communicator of the C ABI; the unique id travels over an existing
     torch.distributed process group (plumbing only)."""

@@ -218,6 +218,8 @@ class _RefGpt(_PortGpt):
                                 ("nsref_gpt_adamw_set_lr", None, [_p, _f]),
                                 ("nsref_gpt_adamw_step", _i, [_p]),
                                 ("nsref_gpt_destroy", None, [_p]),
+                                ("nsref_gpt_decode", _i, [_p, _i, _i, _p]),
+                                ("nsref_gpt_clear_kv", None, [_p]),
                                 ("nsref_last_error", ctypes.c_char_p, [])]:
             fn = getattr(lib, name)
             fn.restype = res
@@ -277,6 +279,19 @@ class _RefGpt(_PortGpt):
 
     def adamw_step(self):
         self.o.lib.nsref_gpt_adamw_step(self.h)
+
+    def decode(self, token, pos):
+        """ForwardWithKVCache(token, pos) -> logits [V] (include/gpt.h:159-190)."""
+        out = np.zeros(self.V, np.float32)
+        rc = self.o.lib.nsref_gpt_decode(self.h, int(token), int(pos), _ptr(out))
+        if rc == 3:
+            raise IndexError(self.o.lib.nsref_last_error().decode())
+        if rc != 0:
+            raise OracleError(self.o.lib.nsref_last_error().decode())
+        return out
+
+    def clear_kv(self):
+        self.o.lib.nsref_gpt_clear_kv(self.h)
 
 
 class Port(_Base):

@@ -204,3 +204,37 @@ def gpt_fwd_bwd(flat, idx, targets, V, block, L, H, C, keep_probs=True):
     dwpe[:T] = dcur.reshape(B, T, C).sum(0)
     G[1] = dwpe
     return loss, logits.reshape(B, T, V), np.concatenate([g.reshape(-1) for g in G])
+
+
+def gpt_decode(flat, steps, V, block, L, H, C):
+    """GPTModel::ForwardWithKVCache (include/gpt.h:159-190) in float64 for one
+    sequence: steps is a list of (token, pos); each step appends its K and V
+    to the cache (include/layers/attention.h:481-546) and returns the
+    logits [V] of that step.  Returns an array [len(steps), V]."""
+    P = split_params(flat, V, block, L, C)
+    D = C // H
+    wte, wpe = P[0], P[1]
+    kc = [[] for _ in range(L)]
+    vc = [[] for _ in range(L)]
+    out = []
+    for tok, pos in steps:
+        x = wte[int(tok)] + wpe[int(pos)]
+        for l in range(L):
+            g1, b1, Wa, ba, Wp, bp, g2, b2, Wf, bf, Wm, bm = P[2 + 12 * l: 14 + 12 * l]
+            h1 = layernorm_fwd(x[None], g1, b1)[0][0]
+            qkv = h1 @ Wa + ba
+            q = qkv[:C].reshape(H, D)
+            kc[l].append(qkv[C:2 * C].reshape(H, D))
+            vc[l].append(qkv[2 * C:].reshape(H, D))
+            K = np.stack(kc[l], 1)  # [H, t, D]
+            Vv = np.stack(vc[l], 1)
+            s = np.einsum("hd,htd->ht", q, K) / np.sqrt(D)
+            s = np.exp(s - s.max(-1, keepdims=True))
+            p = s / s.sum(-1, keepdims=True)
+            att = np.einsum("ht,htd->hd", p, Vv).reshape(C)
+            x1 = x + (att @ Wp + bp)
+            h2 = layernorm_fwd(x1[None], g2, b2)[0][0]
+            x = x1 + (gelu(h2 @ Wf + bf) @ Wm + bm)
+        xf = layernorm_fwd(x[None], P[-2], P[-1])[0][0]
+        out.append(xf @ wte.T)
+    return np.array(out)

@@ -20,6 +20,7 @@
 //   GPTModel                include/gpt.h:136-327
 //   AdamW                   include/optimizers.h:143-253
 //   SaveWeights/LoadWeights include/gpt.h:293-306 (NSF, include/serialization.h)
+//   ForwardWithKVCache      include/gpt.h:153-190, include/layers/attention.h:481-546
 //   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
 //                           function of the training program, not a library
 //                           symbol)
@@ -337,6 +338,16 @@ int nsref_gpt_save_weights(void* handle, const char* path) {
 int nsref_gpt_load_weights(void* handle, const char* path) {
   return static_cast<GptHandle*>(handle)->model->LoadWeights(path) ? 1 : 0;
 }
+
+// GPTModel::ForwardWithKVCache(token, pos) (include/gpt.h:159-190): one
+// token through the cached model; logits_out receives vocab floats.
+int nsref_gpt_decode(void* handle, int token, int pos, float* logits_out) {
+  GptHandle* h = static_cast<GptHandle*>(handle);
+  return Guard([&] { ToHost(h->model->ForwardWithKVCache(token, pos), logits_out); });
+}
+
+// GPTModel::ClearKVCache (include/gpt.h:153-157).
+void nsref_gpt_clear_kv(void* handle) { static_cast<GptHandle*>(handle)->model->ClearKVCache(); }
 
 int nsref_gpt_zero_grad(void* handle) {
   GptHandle* h = static_cast<GptHandle*>(handle);
