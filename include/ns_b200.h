@@ -276,6 +276,28 @@ NS_API ns_status ns_cross_entropy_noalloc(const float* logits, const int32_t* ta
                                    int classes, float denom, float* loss_out, float* dlogits,
                                    int32_t* err_flag, void* stream);
 
+/* ------------------------------------------------------------ Conv2D
+ * Conv2D::Forward / ::Backward (include/layers/conv2d.h:192-414), NCHW:
+ * x [B, IC, H, W], weight [OC, IC, k, k], bias [OC] (may be NULL in the
+ * forward), y [B, OC, OH, OW] with OH = (H + 2*pad - k)/stride + 1 (likewise
+ * OW).  The batch's im2col columns [IC*k*k, B*OH*OW] go through one 3xTF32
+ * tcgen05 GEMM per product.  Backward overwrites dweight [OC, IC, k, k] and
+ * dbias [OC] (the reference zeroes them first) and writes dx (NULL: skipped,
+ * for a first layer); the weight gradient is a deterministic split-K product
+ * and dx a gather in the reference's window order (no atomics).  Both need
+ * `workspace` of ns_conv2d_workspace_size bytes, 256-byte aligned.  Bad
+ * parameters (non-positive sizes, a kernel larger than the padded input) are
+ * NS_ERR_INVALID_ARGUMENT, the reference's std::invalid_argument. */
+NS_API size_t ns_conv2d_workspace_size(int B, int IC, int H, int W, int OC, int k, int stride,
+                                       int pad);
+NS_API ns_status ns_conv2d_fwd(const float* x, int B, int IC, int H, int W, const float* weight,
+                               const float* bias, int OC, int k, int stride, int pad, float* y,
+                               void* workspace, size_t workspace_bytes, void* stream);
+NS_API ns_status ns_conv2d_bwd(const float* x, const float* dy, int B, int IC, int H, int W,
+                               const float* weight, int OC, int k, int stride, int pad, float* dx,
+                               float* dweight, float* dbias, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------ K4 embedding
  * out[b,t,:] = wte[tok[b,t],:] + wpe[t,:]  (Embedding::Forward twice plus the
  * add of GPTModel::Forward, include/layers/embedding.h:34-59,

@@ -79,6 +79,11 @@ _SIGS = {
     "ns_cross_entropy_workspace_size": (c_size_t, [c_int, c_int]),
     "ns_cross_entropy": (c_int, [P, P, c_int, c_int, c_float, P, P, P, P, c_size_t, P]),
     "ns_cross_entropy_noalloc": (c_int, [P, P, c_int, c_int, c_float, P, P, P, P]),
+    "ns_conv2d_workspace_size": (c_size_t, [c_int] * 8),
+    "ns_conv2d_fwd": (c_int, [P, c_int, c_int, c_int, c_int, P, P, c_int, c_int, c_int, c_int, P,
+                              P, c_size_t, P]),
+    "ns_conv2d_bwd": (c_int, [P, P, c_int, c_int, c_int, c_int, P, c_int, c_int, c_int, c_int, P,
+                              P, P, P, c_size_t, P]),
     "ns_embedding_fwd": (c_int, [P, c_int, c_int, P, c_int, P, c_int, c_int, P, P, P]),
     "ns_embedding_bwd": (c_int, [P, c_int, c_int, P, c_int, c_int, c_int, P, c_int, P, P]),
     "ns_adamw_flat": (c_int, [P, P, P, P, c_int64, P, P, c_int, c_float, c_float, c_float,

@@ -335,3 +335,37 @@ def sumsq(x):
 
 def clip_scale(x, sumsq_t, max_norm):
     _lib.check(_lib.load().ns_clip_scale(_p(x), x.numel(), _p(sumsq_t), max_norm, _stream()))
+
+
+def conv2d_fwd(x, weight, bias, stride=1, pad=0):
+    """Conv2D::Forward (include/layers/conv2d.h:211-266): x [B, IC, H, W],
+    weight [OC, IC, k, k] -> y [B, OC, OH, OW]."""
+    lib = _lib.load()
+    _req(x, "x")
+    _req(weight, "weight")
+    B, IC, H, W = x.shape
+    OC, _, k, _ = weight.shape
+    OH, OW = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    y = torch.empty((B, OC, OH, OW), dtype=_f32, device=x.device)
+    nb = lib.ns_conv2d_workspace_size(B, IC, H, W, OC, k, stride, pad)
+    ws = _ws(nb, x.device)
+    _lib.check(lib.ns_conv2d_fwd(_p(x), B, IC, H, W, _p(weight), _p(bias), OC, k, stride, pad,
+                                 _p(y), _p(ws), nb, _stream()))
+    return y
+
+
+def conv2d_bwd(x, dy, weight, stride=1, pad=0, want_dx=True):
+    """Conv2D::Backward (include/layers/conv2d.h:268-331): (dx, dweight, dbias)."""
+    lib = _lib.load()
+    for t, n in ((x, "x"), (dy, "dy"), (weight, "weight")):
+        _req(t, n)
+    B, IC, H, W = x.shape
+    OC, _, k, _ = weight.shape
+    dx = torch.empty_like(x) if want_dx else None
+    dw = torch.empty_like(weight)
+    db = torch.empty(OC, dtype=_f32, device=x.device)
+    nb = lib.ns_conv2d_workspace_size(B, IC, H, W, OC, k, stride, pad)
+    ws = _ws(nb, x.device)
+    _lib.check(lib.ns_conv2d_bwd(_p(x), _p(dy), B, IC, H, W, _p(weight), OC, k, stride, pad,
+                                 _p(dx), _p(dw), _p(db), _p(ws), nb, _stream()))
+    return dx, dw, db

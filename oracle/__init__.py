@@ -435,6 +435,19 @@ class Ref(_Base):
                    _ptr(dx), *[_ptr(a) for a in g])
         return y, dx, g
 
+    def conv2d(self, x, weight, bias, stride, pad, dout=None):
+        """Conv2D::Forward (+ ::Backward with dout): y, and (dx, dweight, dbias)."""
+        x, weight, bias = f32(x), f32(weight), f32(bias)
+        B, IC, H, W = x.shape
+        OC, _, k, _ = weight.shape
+        OH, OW = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+        y = np.zeros((B, OC, OH, OW), np.float32)
+        dx, dw, db = np.zeros_like(x), np.zeros_like(weight), np.zeros_like(bias)
+        self._call("conv2d", [_i] * 8 + [_p] * 8, B, IC, H, W, OC, k, stride, pad, _ptr(weight),
+                   _ptr(bias), _ptr(x), _ptr(f32(dout)) if dout is not None else None, _ptr(y),
+                   _ptr(dx), _ptr(dw), _ptr(db))
+        return (y, dx, dw, db) if dout is not None else y
+
 
 _port = None
 _ref = None

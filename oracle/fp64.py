@@ -238,3 +238,42 @@ def gpt_decode(flat, steps, V, block, L, H, C):
         xf = layernorm_fwd(x[None], P[-2], P[-1])[0][0]
         out.append(xf @ wte.T)
     return np.array(out)
+
+
+def _im2col(x, k, s, p):
+    """[B, IC, H, W] -> columns [B, IC*k*k, OH*OW] (Conv2D's Im2Col,
+    include/layers/conv2d.h:348-375), float64."""
+    x = f64(x)
+    B, IC, H, W = x.shape
+    OH, OW = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    xp = np.zeros((B, IC, H + 2 * p, W + 2 * p))
+    xp[:, :, p:p + H, p:p + W] = x
+    cols = np.empty((B, IC, k, k, OH, OW))
+    for kh in range(k):
+        for kw in range(k):
+            cols[:, :, kh, kw] = xp[:, :, kh:kh + s * OH:s, kw:kw + s * OW:s]
+    return cols.reshape(B, IC * k * k, OH * OW), OH, OW
+
+
+def conv2d_fwd(x, w, b, s, p):
+    """Conv2D::Forward (include/layers/conv2d.h:211-266) in float64."""
+    OC, IC, k, _ = w.shape
+    cols, OH, OW = _im2col(x, k, s, p)
+    y = np.einsum("ok,bkp->bop", f64(w).reshape(OC, -1), cols) + f64(b)[None, :, None]
+    return y.reshape(x.shape[0], OC, OH, OW)
+
+
+def conv2d_bwd(x, w, dy, s, p):
+    """Conv2D::Backward (include/layers/conv2d.h:268-331) in float64 -> (dx, dw, db)."""
+    OC, IC, k, _ = w.shape
+    B, _, H, W = x.shape
+    cols, OH, OW = _im2col(x, k, s, p)
+    d = f64(dy).reshape(B, OC, OH * OW)
+    dw = np.einsum("bop,bkp->ok", d, cols).reshape(w.shape)
+    db = d.sum((0, 2))
+    dcols = np.einsum("ok,bop->bkp", f64(w).reshape(OC, -1), d).reshape(B, IC, k, k, OH, OW)
+    dxp = np.zeros((B, IC, H + 2 * p, W + 2 * p))
+    for kh in range(k):
+        for kw in range(k):
+            dxp[:, :, kh:kh + s * OH:s, kw:kw + s * OW:s] += dcols[:, :, kh, kw]
+    return dxp[:, :, p:p + H, p:p + W], dw, db

@@ -21,6 +21,7 @@
 //   AdamW                   include/optimizers.h:143-253
 //   SaveWeights/LoadWeights include/gpt.h:293-306 (NSF, include/serialization.h)
 //   ForwardWithKVCache      include/gpt.h:153-190, include/layers/attention.h:481-546
+//   Conv2D                  include/layers/conv2d.h:192-414
 //   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
 //                           function of the training program, not a library
 //                           symbol)
@@ -35,6 +36,7 @@
 #include <vector>
 
 #include "gpt.h"
+#include "layers/conv2d.h"
 #include "losses.h"
 #include "optimizers.h"
 #include "parallel.h"
@@ -212,6 +214,29 @@ int nsref_mha(int B, int T, int C, int H, const float* w_attn, const float* b_at
     ToHost(*g[1], g_b_attn);
     ToHost(*g[2], g_w_proj);
     ToHost(*g[3], g_b_proj);
+  });
+}
+
+// Conv2D::Forward + ::Backward (include/layers/conv2d.h:192-414) with the
+// given weights: y [B, OC, OH, OW], dx, dweight, dbias.
+int nsref_conv2d(int B, int IC, int H, int W, int OC, int k, int stride, int pad,
+                 const float* weight, const float* bias, const float* x, const float* dout,
+                 float* y, float* dx, float* dweight, float* dbias) {
+  return Guard([&] {
+    Conv2D conv(IC, OC, k, stride, pad);
+    std::memcpy(conv.Weight().Data(), weight, sizeof(float) * OC * IC * k * k);
+    std::memcpy(conv.Bias().Data(), bias, sizeof(float) * OC);
+    Tensor tx = FromHost(x, {B, IC, H, W});
+    Tensor ty = conv.Forward(tx);
+    ToHost(ty, y);
+    if (dout != nullptr) {
+      Tensor td = FromHost(dout, ty.Shape());
+      Tensor tdx = conv.Backward(td);
+      ToHost(tdx, dx);
+      std::vector<Tensor*> g = conv.GetGradients();
+      ToHost(*g[0], dweight);
+      ToHost(*g[1], dbias);
+    }
   });
 }
 

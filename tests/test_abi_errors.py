@@ -188,3 +188,15 @@ def test_noalloc_cross_entropy_rejects_rows_beyond_its_static_scratch(lib):
     rows = 65536 + 1
     rc = lib.ns_cross_entropy_noalloc(FAKE, FAKE, rows, 4, float(rows), FAKE, FAKE, FAKE, None)
     _err(lib, rc, NS_ERR_INVALID_ARGUMENT, "NS_CE_NOALLOC_MAX_ROWS")
+
+
+def test_conv2d_rejects_bad_parameters(lib):
+    """Conv2D's constructor and Forward checks (include/layers/conv2d.h:203-224)
+    as std::invalid_argument, before any device work."""
+    assert lib.ns_conv2d_workspace_size(1, 3, 2, 2, 4, 5, 1, 0) == 0  # kernel larger than input
+    _err(lib, lib.ns_conv2d_fwd(FAKE, 1, 3, 2, 2, FAKE, FAKE, 4, 5, 1, 0, FAKE, None, 0, None),
+         NS_ERR_INVALID_ARGUMENT, "does not fit")
+    _err(lib, lib.ns_conv2d_fwd(FAKE, 1, 3, 8, 8, FAKE, FAKE, 4, 3, 0, 1, FAKE, None, 0, None),
+         NS_ERR_INVALID_ARGUMENT, "bad convolution")
+    _err(lib, lib.ns_conv2d_fwd(FAKE, 1, 3, 8, 8, FAKE, FAKE, 4, 3, 1, 1, FAKE, FAKE, 0, None),
+         NS_ERR_INVALID_ARGUMENT, "workspace")
