@@ -42,11 +42,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
     ap.add_argument("--case", default="step",
-                    choices=["step", "c1", "c2", "c3", "decode", "gemm", "attn", "bw"],
+                    choices=["step", "c1", "c2", "c3", "c5", "decode", "gemm", "attn", "bw"],
                     help="step: the training-step benchmark (default, the one-line contract); "
                          "c1 / c2 / c3: the 4-layer/128 step, the MatMul sweep, the "
                          "MultiHeadAttention layer at B8/T1024/H12, each beside the reference "
-                         "on the host cores; decode: KV-cache decoding of the 12-layer model; "
+                         "on the host cores; c5: the diffusion U-Net step (data parallel under "
+                         "torchrun); decode: KV-cache decoding of the 12-layer model; "
                          "gemm / attn / bw: single-kernel cases for profilers")
     ap.add_argument("--shape", default="",
                     help="gemm: M,N,K[,a_trans,b_trans]; attn: B,T,H,D; bw: M,C,V")
@@ -705,6 +706,102 @@ def case_c3(args, torch):
     return out
 
 
+def unet_flops(B, in_ch=3, base=64, S=64):
+    """Algorithmic FLOP of one U-Net training step: 3 x 2*MNK per convolution
+    (forward, weight gradient, input gradient; conv_in has no input
+    gradient), M = output channels, N = output pixels * B, K = 9 * input
+    channels."""
+    convs = [(in_ch, base, S), (base, 2 * base, S // 2), (2 * base, 4 * base, S // 4),
+             (4 * base, 2 * base, S // 2), (2 * base, base, S), (base, in_ch, S)]
+    convs += [(c, c, s) for c, s in ((base, S), (2 * base, S // 2), (4 * base, S // 4),
+                                      (2 * base, S // 2), (base, S))]
+    total = 0.0
+    for i, (ic, oc, s) in enumerate(convs):
+        f = 2.0 * oc * (B * s * s) * 9 * ic
+        total += f * (2 if i == 0 else 3)
+    return total
+
+
+def case_c5(args, torch):
+    """The diffusion U-Net training step of config 5: 64x64x3 images N(0,1),
+    base channels 64, noise target N(0,1), MSELoss, AdamW, 32 images per GPU;
+    data parallel (gradient all-reduce over NCCL) when launched under
+    torchrun.  images/s over all ranks (max-over-ranks step time), the
+    convolutions' algorithmic TFLOP/s, the reference's step on the host."""
+    import torch.distributed as dist
+
+    from neuralsuite_b200 import Comm, UNet
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    B = 32
+    net = UNet(3, 64, 64, max_batch=B)
+    r = np.random.default_rng(77)
+    net.set_params((r.standard_normal(net.n_params) * 0.02).astype(np.float32))
+    net.adamw_init(1e-4)
+    comm = None
+    if world > 1:
+        comm = Comm(rank, world)
+        net.set_comm(comm, world)
+    rr = np.random.default_rng(100 + rank)
+    xs = [torch.as_tensor(rr.standard_normal((B, 3, 64, 64)).astype(np.float32), device="cuda")
+          for _ in range(2)]
+    ts = [torch.as_tensor(rr.standard_normal((B, 3, 64, 64)).astype(np.float32), device="cuda")
+          for _ in range(2)]
+    for i in range(max(args.warmup, 3)):
+        net.train_step(xs[i % 2], ts[i % 2], read_loss=False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = max(args.steps, 10)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for i in range(steps):
+        net.train_step(xs[i % 2], ts[i % 2], read_loss=False)
+    e0.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(e0) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        net.set_comm(None, 1)
+        comm.destroy()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    bf16_burst, _, _, src = peaks()
+    fl = unet_flops(B)
+    out = {"case": "c5", "workload": "diffusion U-Net, 64x64x3, base 64, 32 images/GPU, MSE, AdamW",
+           "n_gpus": world, "step_ms": ms, "images_per_s": world * B / ms * 1e3,
+           "conv_tflops_per_gpu": fl / ms / 1e9, "frac_of_3xtf32_peak": fl / ms / 1e9 / (bf16_burst / 6),
+           "peak_source": src}
+    o = _ref_or_none(args) if world == 1 else None
+    if o is not None:
+        from oracle import RefUNet
+
+        ref_net = RefUNet(o, 3, 64, 64)
+        ref_net.set_params((r.standard_normal(ref_net.n) * 0.02).astype(np.float32))
+        ref_net.adamw_init(1e-4)
+        xb = xs[0][:2].cpu().numpy()
+        tb = ts[0][:2].cpu().numpy()
+
+        def ref_step():
+            ref_net.fwd_bwd(xb, tb)
+            ref_net.adamw_step()
+
+        rms = _host_ms(ref_step, 2)
+        out["reference"] = {"images_per_s": 2 / rms * 1e3, "step_ms_for_2_images": rms,
+                            "cores": os.cpu_count(), "sample": "2 of the 32 images per step"}
+    return out
+
+
 def case_decode(args, torch):
     """KV-cache decoding (GPTModel::ForwardWithKVCache) of the 12-layer/768
     model: a prompt by prefill, then timed decode steps (CUDA events over
@@ -842,9 +939,11 @@ def case_kernel(args, torch):
 def run_case(args):
     import torch
 
-    fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3, "decode": case_decode}.get(args.case,
-                                                                                 case_kernel)
-    print(json.dumps(fn(args, torch)), flush=True)
+    fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3, "c5": case_c5,
+          "decode": case_decode}.get(args.case, case_kernel)
+    out = fn(args, torch)
+    if out is not None:
+        print(json.dumps(out), flush=True)
 
 
 def main():

@@ -378,6 +378,48 @@ NS_API ns_status ns_comm_destroy(ns_comm* comm);
  * loop aborted the communicator (1 in scenarios 1-3, 0 otherwise). */
 NS_API ns_status ns_comm_selftest(int scenario, double timeout_s, int* aborts);
 
+/* -------------------------------------------------- diffusion U-Net step
+ * The denoising U-Net training step (no reference counterpart as a model:
+ * the reference has its layers -- Conv2D, ResidualBlock
+ * include/layers/residual.h:23-64, LayerNormLayer, MSELoss
+ * include/losses.h:97-124 -- but no U-Net and no upsample).  NCHW, image
+ * size S (a multiple of 4), base channels c:
+ *   e0 = LN0(Res0(conv_in(x)))            c,  S
+ *   e1 = LN1(Res1(down1(e0)))             2c, S/2  (3x3, stride 2, pad 1)
+ *   m  = LN2(Res2(down2(e1)))             4c, S/4
+ *   u1 = LN3(Res3(up1(Up(m)) + e1))       2c, S/2  (Up: nearest 2x)
+ *   u0 = LN4(Res4(up0(Up(u1)) + e0))      c,  S
+ *   y  = conv_out(u0); loss = MSELoss(y, target)
+ * Res(a) = ReLU(Conv2D_3x3(a) + a); LN normalises the last axis (W), as the
+ * reference's LayerNormLayer does on an NCHW tensor.  Parameters are a flat
+ * buffer in registration order (conv_in, res0, ln0, down1, res1, ln1, down2,
+ * res2, ln2, up1, res3, ln3, up0, res4, ln4, conv_out; each conv weight then
+ * bias, each LN gamma then beta); AdamW decays rank >= 2 tensors (the conv
+ * weights), as the reference's AdamW does.  With a communicator attached the
+ * gradient and the loss are summed over ranks after the backward (the MSE
+ * gradient is divided by the global element count). */
+typedef struct ns_unet ns_unet;
+typedef struct {
+  int in_channels, base_channels, image_size, max_batch;
+} ns_unet_config;
+NS_API ns_status ns_unet_create(const ns_unet_config* cfg, ns_unet** out);
+NS_API ns_status ns_unet_destroy(ns_unet* net);
+NS_API int ns_unet_num_tensors(const ns_unet* net);
+NS_API int64_t ns_unet_tensor_numel(const ns_unet* net, int i);
+NS_API int64_t ns_unet_num_params(const ns_unet* net);
+NS_API float* ns_unet_params(ns_unet* net);
+NS_API float* ns_unet_grads(ns_unet* net);
+NS_API float* ns_unet_output(ns_unet* net); /* device [B, in_channels, S, S] */
+NS_API float* ns_unet_loss(ns_unet* net);   /* device, 1 float (summed over ranks) */
+NS_API ns_status ns_unet_forward(ns_unet* net, const float* x, int B, void* stream);
+NS_API ns_status ns_unet_loss_backward(ns_unet* net, const float* target, void* stream);
+NS_API ns_status ns_unet_backward(ns_unet* net, void* stream);
+NS_API ns_status ns_unet_adamw_init(ns_unet* net, float lr, float b1, float b2, float eps, float wd);
+NS_API ns_status ns_unet_adamw_step(ns_unet* net, void* stream);
+NS_API ns_status ns_unet_train_step(ns_unet* net, const float* x, const float* target, int B,
+                                    float* host_loss, void* stream);
+NS_API ns_status ns_unet_set_comm(ns_unet* net, ns_comm* comm, int world_size);
+
 /* ------------------------------------------------------------ GPT model
  * The device GPTModel (include/gpt.h:136-327) + CrossEntropyLoss + AdamW, with
  * parameters, gradients, optimizer state and every activation resident in

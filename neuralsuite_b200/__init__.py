@@ -6,11 +6,11 @@ C ABI of ``include/ns_b200.h``); this package is its Python face:
 * ``kernels`` -- one wrapper per kernel entry point (MatMul, attention,
   LayerNorm, GELU, cross-entropy, embedding, AdamW), for tests and tools;
 * ``model`` -- the device GPTModel + CrossEntropyLoss + AdamW step, its NSF
-  checkpoints, the KV-cache ``Decoder`` and the NCCL communicator used for
-  data parallel training.
+  checkpoints, the KV-cache ``Decoder``, the diffusion ``UNet`` step and the
+  NCCL communicator used for data parallel training.
 """
-from .model import (Comm, Decoder, GPTConfig, GPTModel, init_params, nsf_load,  # noqa: F401
-                    nsf_save, param_shapes, plan_buckets)
+from .model import (Comm, Decoder, GPTConfig, GPTModel, UNet, init_params,  # noqa: F401
+                    nsf_load, nsf_save, param_shapes, plan_buckets)
 
-__all__ = ["Comm", "Decoder", "GPTConfig", "GPTModel", "init_params", "nsf_load", "nsf_save",
-           "param_shapes", "plan_buckets"]
+__all__ = ["Comm", "Decoder", "GPTConfig", "GPTModel", "UNet", "init_params", "nsf_load",
+           "nsf_save", "param_shapes", "plan_buckets"]

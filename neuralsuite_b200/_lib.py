@@ -35,6 +35,11 @@ class NsError(RuntimeError):
         self.code = code
 
 
+class ns_unet_config(ctypes.Structure):
+    _fields_ = [("in_channels", c_int), ("base_channels", c_int), ("image_size", c_int),
+                ("max_batch", c_int)]
+
+
 class ns_gpt_config(ctypes.Structure):
     _fields_ = [("vocab_size", c_int), ("block_size", c_int), ("n_layer", c_int),
                 ("n_head", c_int), ("n_embd", c_int), ("max_batch", c_int)]
@@ -112,6 +117,22 @@ _SIGS = {
     "ns_gpt_decoder_logits": (P, [P]),
     "ns_gpt_decode_step": (c_int, [P, P, c_int, c_int, P, P, P]),
     "ns_gpt_decoder_prefill": (c_int, [P, P, c_int, c_int, P, P]),
+    "ns_unet_create": (c_int, [P, P]),
+    "ns_unet_destroy": (c_int, [P]),
+    "ns_unet_num_tensors": (c_int, [P]),
+    "ns_unet_tensor_numel": (c_int64, [P, c_int]),
+    "ns_unet_num_params": (c_int64, [P]),
+    "ns_unet_params": (P, [P]),
+    "ns_unet_grads": (P, [P]),
+    "ns_unet_output": (P, [P]),
+    "ns_unet_loss": (P, [P]),
+    "ns_unet_forward": (c_int, [P, P, c_int, P]),
+    "ns_unet_loss_backward": (c_int, [P, P, P]),
+    "ns_unet_backward": (c_int, [P, P]),
+    "ns_unet_adamw_init": (c_int, [P, c_float, c_float, c_float, c_float, c_float]),
+    "ns_unet_adamw_step": (c_int, [P, P]),
+    "ns_unet_train_step": (c_int, [P, P, P, c_int, P, P]),
+    "ns_unet_set_comm": (c_int, [P, P, c_int]),
     "ns_gpt_create": (c_int, [P, P]),
     "ns_gpt_destroy": (c_int, [P]),
     "ns_gpt_num_tensors": (c_int, [P]),

@@ -324,6 +324,82 @@ class Decoder:
             raise IndexError("a decoded token id is outside [0, vocab_size)")
 
 
+class UNet:
+    """The diffusion U-Net training step on the device (ns_unet_*): Conv2D,
+    ResidualBlock, LayerNormLayer and MSELoss of the reference wired as a
+    two-level U-Net with nearest-neighbour upsampling."""
+
+    def __init__(self, in_channels=3, base_channels=64, image_size=64, max_batch=32):
+        self.lib = _lib.load()
+        c = _lib.ns_unet_config(in_channels, base_channels, image_size, max_batch)
+        h = ctypes.c_void_p()
+        _lib.check(self.lib.ns_unet_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+        self.in_channels, self.image_size, self.max_batch = in_channels, image_size, max_batch
+        self.n_params = int(self.lib.ns_unet_num_params(h))
+        self.n_tensors = int(self.lib.ns_unet_num_tensors(h))
+        self.world = 1
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h:
+            self.lib.ns_unet_destroy(h)
+            self.h = None
+
+    def params(self) -> torch.Tensor:
+        return _device_tensor(self.lib.ns_unet_params(self.h), self.n_params)
+
+    def grads(self) -> torch.Tensor:
+        return _device_tensor(self.lib.ns_unet_grads(self.h), self.n_params)
+
+    def set_params(self, flat) -> None:
+        src = torch.as_tensor(np.asarray(flat, dtype=np.float32))
+        if src.numel() != self.n_params:
+            raise ValueError(f"expected {self.n_params} parameters, got {src.numel()}")
+        self.params().copy_(src.reshape(-1))
+        torch.cuda.synchronize()
+
+    def get_params(self) -> np.ndarray:
+        torch.cuda.synchronize()
+        return self.params().cpu().numpy().copy()
+
+    def get_grads(self) -> np.ndarray:
+        torch.cuda.synchronize()
+        return self.grads().cpu().numpy().copy()
+
+    def fwd_bwd(self, x, target):
+        """Forward -> MSELoss -> Backward; returns (loss, prediction numpy)."""
+        xd = torch.as_tensor(np.asarray(x, np.float32), device="cuda").contiguous()
+        td = torch.as_tensor(np.asarray(target, np.float32), device="cuda").contiguous()
+        B = xd.shape[0]
+        s = GPTModel._stream()
+        _lib.check(self.lib.ns_unet_forward(self.h, xd.data_ptr(), B, s))
+        _lib.check(self.lib.ns_unet_loss_backward(self.h, td.data_ptr(), s))
+        _lib.check(self.lib.ns_unet_backward(self.h, s))
+        torch.cuda.synchronize()
+        n = B * self.in_channels * self.image_size ** 2
+        out = _device_tensor(self.lib.ns_unet_output(self.h), n).cpu().numpy()
+        loss = float(_device_tensor(self.lib.ns_unet_loss(self.h), 1).item()) / self.world
+        return loss, out.reshape(B, self.in_channels, self.image_size, self.image_size)
+
+    def adamw_init(self, lr=1e-3, b1=0.9, b2=0.95, eps=1e-8, wd=0.01):
+        _lib.check(self.lib.ns_unet_adamw_init(self.h, lr, b1, b2, eps, wd))
+
+    def adamw_step(self):
+        _lib.check(self.lib.ns_unet_adamw_step(self.h, GPTModel._stream()))
+
+    def train_step(self, x: torch.Tensor, target: torch.Tensor, read_loss: bool = True):
+        out = ctypes.c_float(0.0)
+        _lib.check(self.lib.ns_unet_train_step(self.h, x.data_ptr(), target.data_ptr(), x.shape[0],
+                                               ctypes.byref(out) if read_loss else None,
+                                               GPTModel._stream()))
+        return float(out.value) if read_loss else None
+
+    def set_comm(self, comm, world: int):
+        _lib.check(self.lib.ns_unet_set_comm(self.h, comm.handle if comm else None, world))
+        self.world = world if comm else 1
+
+
 class Comm:
     """NCCL communicator of the C ABI; the unique id travels over an existing
     torch.distributed process group (plumbing only)."""

@@ -449,6 +449,73 @@ class Ref(_Base):
         return (y, dx, dw, db) if dout is not None else y
 
 
+class RefUNet:
+    """The diffusion U-Net built from the reference's Conv2D / ResidualBlock /
+    LayerNormLayer / MSELoss / AdamW (ref_harness.cpp; only the nearest
+    upsample is written there)."""
+
+    def __init__(self, o, in_ch, base, hw):
+        lib = o.lib
+        for name, res, args in [("nsref_unet_create", _p, [_i, _i, _i]),
+                                ("nsref_unet_destroy", None, [_p]),
+                                ("nsref_unet_num_tensors", _i, [_p]),
+                                ("nsref_unet_tensor_numel", _ll, [_p, _i]),
+                                ("nsref_unet_set_params", None, [_p, _p]),
+                                ("nsref_unet_get", None, [_p, _i, _p]),
+                                ("nsref_unet_fwd_bwd", _i, [_p, _i, _p, _p, _p, _p]),
+                                ("nsref_unet_adamw_init", _i, [_p, _f]),
+                                ("nsref_unet_adamw_step", _i, [_p])]:
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        self.o, self.lib = o, lib
+        self.h = lib.nsref_unet_create(in_ch, base, hw)
+        self.in_ch, self.hw = in_ch, hw
+        self.n = sum(int(lib.nsref_unet_tensor_numel(self.h, i))
+                     for i in range(lib.nsref_unet_num_tensors(self.h)))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.nsref_unet_destroy(self.h)
+            self.h = None
+
+    def tensor_sizes(self):
+        return [int(self.lib.nsref_unet_tensor_numel(self.h, i))
+                for i in range(self.lib.nsref_unet_num_tensors(self.h))]
+
+    def set_params(self, flat):
+        flat = f32(flat)
+        assert flat.size == self.n
+        self.lib.nsref_unet_set_params(self.h, _ptr(flat))
+
+    def _get(self, grads):
+        out = np.zeros(self.n, np.float32)
+        self.lib.nsref_unet_get(self.h, grads, _ptr(out))
+        return out
+
+    def get_params(self):
+        return self._get(0)
+
+    def get_grads(self):
+        return self._get(1)
+
+    def fwd_bwd(self, x, target):
+        x, target = f32(x), f32(target)
+        loss = _f(0.0)
+        out = np.zeros_like(x)
+        rc = self.lib.nsref_unet_fwd_bwd(self.h, x.shape[0], _ptr(x), _ptr(target),
+                                         ctypes.cast(ctypes.byref(loss), _p), _ptr(out))
+        if rc != 0:
+            raise OracleError(self.lib.nsref_last_error().decode())
+        return float(loss.value), out
+
+    def adamw_init(self, lr):
+        self.lib.nsref_unet_adamw_init(self.h, lr)
+
+    def adamw_step(self):
+        self.lib.nsref_unet_adamw_step(self.h)
+
+
 _port = None
 _ref = None
 

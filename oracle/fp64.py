@@ -277,3 +277,75 @@ def conv2d_bwd(x, w, dy, s, p):
         for kw in range(k):
             dxp[:, :, kh:kh + s * OH:s, kw:kw + s * OW:s] += dcols[:, :, kh, kw]
     return dxp[:, :, p:p + H, p:p + W], dw, db
+
+
+def unet_fwd_bwd(flat, sizes, x, target, in_ch, base, hw):
+    """The diffusion U-Net step of ref_harness.cpp in float64: forward, MSE,
+    backward.  sizes: the tensor sizes in registration order.  Returns
+    (loss, prediction, grads flat).  Nearest 2x upsampling is the only layer
+    the reference does not have."""
+    parts, off = [], 0
+    for n in sizes:
+        parts.append(f64(flat[off:off + n]))
+        off += n
+    c = [base, 2 * base, 4 * base, 2 * base, base]
+    w = [hw, hw // 2, hw // 4, hw // 2, hw]
+    cin = [in_ch, base, 2 * base, 4 * base, 2 * base]
+    stride = [1, 2, 2, 1, 1]
+    # per level: conv (w, b), res conv (w, b), ln (g, b); then conv_out (w, b)
+    P = []
+    for l in range(5):
+        k = 6 * l
+        P.append(dict(cw=parts[k].reshape(c[l], cin[l], 3, 3), cb=parts[k + 1],
+                      rw=parts[k + 2].reshape(c[l], c[l], 3, 3), rb=parts[k + 3],
+                      g=parts[k + 4], b=parts[k + 5]))
+    ow, ob = parts[30].reshape(in_ch, base, 3, 3), parts[31]
+
+    def up(t):
+        return t.repeat(2, axis=2).repeat(2, axis=3)
+
+    def up_bwd(d):
+        B, C, H, W = d.shape
+        return d.reshape(B, C, H // 2, 2, W // 2, 2).sum((3, 5))
+
+    cache = []
+
+    def level_fwd(l, inp, skip=None):
+        a = conv2d_fwd(inp, P[l]["cw"], P[l]["cb"], stride[l], 1)
+        if skip is not None:
+            a = a + skip
+        f = conv2d_fwd(a, P[l]["rw"], P[l]["rb"], 1, 1)
+        r = np.maximum(f + a, 0.0)
+        e, m, s = layernorm_fwd(r, P[l]["g"], P[l]["b"])
+        cache.append((inp, a, r, m, s))
+        return e
+
+    x = f64(x)
+    e0 = level_fwd(0, x)
+    e1 = level_fwd(1, e0)
+    mm = level_fwd(2, e1)
+    u1 = level_fwd(3, up(mm), e1)
+    u0 = level_fwd(4, up(u1), e0)
+    y = conv2d_fwd(u0, ow, ob, 1, 1)
+    n = y.size
+    diff = y - f64(target)
+    loss = float((diff * diff).sum() / n)
+    dy = 2.0 * diff / n
+    G = [None] * 32
+
+    def level_bwd(l, de):
+        inp, a, r, m, s = cache[l]
+        dr, G[6 * l + 4], G[6 * l + 5] = layernorm_bwd(de, r, P[l]["g"], m, s)
+        dsum = np.where(r > 0, dr, 0.0)
+        dfa, G[6 * l + 2], G[6 * l + 3] = conv2d_bwd(a, P[l]["rw"], dsum, 1, 1)
+        da = dfa + dsum
+        dinp, G[6 * l], G[6 * l + 1] = conv2d_bwd(inp, P[l]["cw"], da, stride[l], 1)
+        return dinp, da
+
+    du0, G[30], G[31] = conv2d_bwd(u0, ow, dy, 1, 1)
+    dup1, ds0 = level_bwd(4, du0)
+    dup0, ds1 = level_bwd(3, up_bwd(dup1))
+    de1_part, _ = level_bwd(2, up_bwd(dup0))
+    de0_part, _ = level_bwd(1, de1_part + ds1)
+    level_bwd(0, de0_part + ds0)
+    return loss, y, np.concatenate([g.reshape(-1) for g in G])

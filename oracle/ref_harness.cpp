@@ -22,6 +22,8 @@
 //   SaveWeights/LoadWeights include/gpt.h:293-306 (NSF, include/serialization.h)
 //   ForwardWithKVCache      include/gpt.h:153-190, include/layers/attention.h:481-546
 //   Conv2D                  include/layers/conv2d.h:192-414
+//   ResidualBlock           include/layers/residual.h:23-64
+//   MSELoss                 include/losses.h:97-124
 //   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
 //                           function of the training program, not a library
 //                           symbol)
@@ -37,6 +39,8 @@
 
 #include "gpt.h"
 #include "layers/conv2d.h"
+#include "layers/layernorm.h"
+#include "layers/residual.h"
 #include "losses.h"
 #include "optimizers.h"
 #include "parallel.h"
@@ -238,6 +242,159 @@ int nsref_conv2d(int B, int IC, int H, int W, int OC, int k, int stride, int pad
       ToHost(*g[1], dbias);
     }
   });
+}
+
+// ------------------------------------------------------ diffusion U-Net
+//
+// The U-Net of the diffusion training step (the reference has none): two
+// stride-2 levels down and two nearest-neighbour levels up with skip sums,
+// each level Conv2D -> ResidualBlock(Conv2D 3x3) -> LayerNormLayer (last
+// axis, as the reference's LayerNorm normalises), a 3x3 head and MSELoss.
+// Every layer is the reference's own class (include/layers/conv2d.h,
+// residual.h, layernorm.h, include/losses.h:97-124); only the nearest
+// upsample, which the reference lacks, is written here (UpNearest2x).
+namespace {
+
+// y[b][c][i][j] = x[b][c][i/2][j/2]; backward sums each 2x2 block in
+// (0,0), (0,1), (1,0), (1,1) order.
+Tensor UpNearest2x(const Tensor& x) {
+  const int B = x.Shape()[0], C = x.Shape()[1], H = x.Shape()[2], W = x.Shape()[3];
+  Tensor y({B, C, 2 * H, 2 * W});
+  for (int bc = 0; bc < B * C; ++bc)
+    for (int i = 0; i < 2 * H; ++i)
+      for (int j = 0; j < 2 * W; ++j)
+        y[((size_t)bc * 2 * H + i) * 2 * W + j] = x[((size_t)bc * H + i / 2) * W + j / 2];
+  return y;
+}
+Tensor UpNearest2xBackward(const Tensor& dy) {
+  const int B = dy.Shape()[0], C = dy.Shape()[1], H = dy.Shape()[2] / 2, W = dy.Shape()[3] / 2;
+  Tensor dx({B, C, H, W});
+  for (int bc = 0; bc < B * C; ++bc)
+    for (int i = 0; i < H; ++i)
+      for (int j = 0; j < W; ++j) {
+        const size_t r0 = ((size_t)bc * 2 * H + 2 * i) * 2 * W + 2 * j, r1 = r0 + 2 * W;
+        float s = 0.0f;
+        s += dy[r0];
+        s += dy[r0 + 1];
+        s += dy[r1];
+        s += dy[r1 + 1];
+        dx[((size_t)bc * H + i) * W + j] = s;
+      }
+  return dx;
+}
+Tensor Add(const Tensor& a, const Tensor& b) {
+  Tensor out(a.Shape());
+  ElementwiseAdd(a, b, out);
+  return out;
+}
+
+struct UNet {
+  int C0, HW;
+  std::shared_ptr<Conv2D> conv_in, down1, down2, up1, up0, conv_out;
+  std::shared_ptr<ResidualBlock> res[5];
+  std::shared_ptr<LayerNormLayer> ln[5];
+  std::vector<Parameter*> params;
+  MSELoss mse;
+  std::unique_ptr<AdamW> opt;
+  Tensor e0, e1;
+
+  UNet(int in_ch, int base, int hw) : C0(base), HW(hw) {
+    const int c[3] = {base, 2 * base, 4 * base};
+    const int w[3] = {hw, hw / 2, hw / 4};
+    conv_in = std::make_shared<Conv2D>(in_ch, c[0], 3, 1, 1);
+    down1 = std::make_shared<Conv2D>(c[0], c[1], 3, 2, 1);
+    down2 = std::make_shared<Conv2D>(c[1], c[2], 3, 2, 1);
+    up1 = std::make_shared<Conv2D>(c[2], c[1], 3, 1, 1);
+    up0 = std::make_shared<Conv2D>(c[1], c[0], 3, 1, 1);
+    conv_out = std::make_shared<Conv2D>(c[0], in_ch, 3, 1, 1);
+    const int rc[5] = {c[0], c[1], c[2], c[1], c[0]};
+    const int rw[5] = {w[0], w[1], w[2], w[1], w[0]};
+    for (int i = 0; i < 5; ++i) {
+      res[i] = std::make_shared<ResidualBlock>(std::make_shared<Conv2D>(rc[i], rc[i], 3, 1, 1));
+      ln[i] = std::make_shared<LayerNormLayer>(rw[i]);
+    }
+    // Registration order: conv_in, res0, ln0, down1, res1, ln1, down2, res2,
+    // ln2, up1, res3, ln3, up0, res4, ln4, conv_out.
+    auto add = [&](Layer* l) {
+      for (Parameter* p : l->Parameters()) params.push_back(p);
+    };
+    add(conv_in.get()); add(res[0].get()); add(ln[0].get());
+    add(down1.get()); add(res[1].get()); add(ln[1].get());
+    add(down2.get()); add(res[2].get()); add(ln[2].get());
+    add(up1.get()); add(res[3].get()); add(ln[3].get());
+    add(up0.get()); add(res[4].get()); add(ln[4].get());
+    add(conv_out.get());
+  }
+
+  Tensor Forward(const Tensor& x) {
+    e0 = ln[0]->Forward(res[0]->Forward(conv_in->Forward(x)));
+    e1 = ln[1]->Forward(res[1]->Forward(down1->Forward(e0)));
+    Tensor m = ln[2]->Forward(res[2]->Forward(down2->Forward(e1)));
+    Tensor u1 = ln[3]->Forward(res[3]->Forward(Add(up1->Forward(UpNearest2x(m)), e1)));
+    Tensor u0 = ln[4]->Forward(res[4]->Forward(Add(up0->Forward(UpNearest2x(u1)), e0)));
+    return conv_out->Forward(u0);
+  }
+
+  void Backward(const Tensor& dout) {
+    Tensor du0 = conv_out->Backward(dout);
+    Tensor ds0 = res[4]->Backward(ln[4]->Backward(du0));           // d(up0 out + e0)
+    Tensor du1 = UpNearest2xBackward(up0->Backward(ds0));
+    Tensor ds1 = res[3]->Backward(ln[3]->Backward(du1));           // d(up1 out + e1)
+    Tensor dm = UpNearest2xBackward(up1->Backward(ds1));
+    Tensor de1 = Add(down2->Backward(res[2]->Backward(ln[2]->Backward(dm))), ds1);
+    Tensor de0 = Add(down1->Backward(res[1]->Backward(ln[1]->Backward(de1))), ds0);
+    conv_in->Backward(res[0]->Backward(ln[0]->Backward(de0)));
+  }
+};
+
+}  // namespace
+
+void* nsref_unet_create(int in_ch, int base, int hw) {
+  UNet* u = nullptr;
+  Guard([&] { u = new UNet(in_ch, base, hw); });
+  return u;
+}
+void nsref_unet_destroy(void* h) { delete static_cast<UNet*>(h); }
+int nsref_unet_num_tensors(void* h) { return (int)static_cast<UNet*>(h)->params.size(); }
+long long nsref_unet_tensor_numel(void* h, int i) {
+  return (long long)static_cast<UNet*>(h)->params[i]->Value().TotalSize();
+}
+void nsref_unet_set_params(void* h, const float* flat) {
+  size_t off = 0;
+  for (Parameter* p : static_cast<UNet*>(h)->params) {
+    std::memcpy(p->Value().Data(), flat + off, p->Value().TotalSize() * sizeof(float));
+    off += p->Value().TotalSize();
+  }
+}
+void nsref_unet_get(void* h, int grads, float* flat) {
+  size_t off = 0;
+  for (Parameter* p : static_cast<UNet*>(h)->params) {
+    const Tensor& t = grads ? p->Grad() : p->Value();
+    std::memcpy(flat + off, t.Data(), t.TotalSize() * sizeof(float));
+    off += t.TotalSize();
+  }
+}
+// Forward -> MSELoss -> Backward on x, target [B, in_ch, hw, hw]; out = the
+// prediction.
+int nsref_unet_fwd_bwd(void* h, int B, const float* x, const float* target, float* loss,
+                       float* out) {
+  UNet* u = static_cast<UNet*>(h);
+  return Guard([&] {
+    const int ic = u->conv_in->Weight().Shape()[1];
+    Tensor tx = FromHost(x, {B, ic, u->HW, u->HW});
+    Tensor tt = FromHost(target, {B, ic, u->HW, u->HW});
+    Tensor y = u->Forward(tx);
+    ToHost(y, out);
+    *loss = u->mse.Forward(y, tt);
+    u->Backward(u->mse.Backward());
+  });
+}
+int nsref_unet_adamw_init(void* h, float lr) {
+  UNet* u = static_cast<UNet*>(h);
+  return Guard([&] { u->opt = std::make_unique<AdamW>(u->params, lr); });
+}
+int nsref_unet_adamw_step(void* h) {
+  return Guard([&] { static_cast<UNet*>(h)->opt->Step(); });
 }
 
 // ---------------------------------------------------------------- GPT model
