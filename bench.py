@@ -42,7 +42,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
     ap.add_argument("--case", default="step",
-                    choices=["step", "c1", "c2", "c3", "c5", "decode", "gemm", "attn", "bw"],
+                    choices=["step", "c1", "c2", "c3", "c5", "decode", "lstm", "gemm", "attn",
+                             "bw"],
                     help="step: the training-step benchmark (default, the one-line contract); "
                          "c1 / c2 / c3: the 4-layer/128 step, the MatMul sweep, the "
                          "MultiHeadAttention layer at B8/T1024/H12, each beside the reference "
@@ -802,6 +803,32 @@ def case_c5(args, torch):
     return out
 
 
+def case_lstm(args, torch):
+    """BiLSTM forward + backward at a CRNN size (T 64 positions, 32 images,
+    256 features, 256 hidden per direction), beside the reference's BiLSTM
+    on the host cores; FLOP = 3 products x 2 directions x (input projection +
+    recurrence) of 2*T*B*4H*(IN + H) each."""
+    from neuralsuite_b200 import kernels as nk
+
+    T, B, IN, H = 64, 32, 256, 256
+    r = np.random.default_rng(8)
+    n1 = 4 * H * IN + 4 * H * H + 8 * H
+    p = torch.as_tensor((r.standard_normal(2 * n1) / 16).astype(np.float32), device="cuda")
+    x = torch.as_tensor(r.standard_normal((T, B, IN)).astype(np.float32), device="cuda")
+    d = torch.as_tensor(r.standard_normal((T, B, 2 * H)).astype(np.float32), device="cuda")
+    ms = _event_ms(torch, lambda: nk.lstm_fwd_bwd(x, p, d, H, True), max(args.reps, 5))
+    fl = 3 * 2 * 2.0 * T * B * 4 * H * (IN + H)
+    out = {"case": "lstm", "workload": "BiLSTM T=64, B=32, IN=256, H=256, forward + backward",
+           "ms": ms, "tflops": fl / ms / 1e9,
+           "note": "the recurrence is 2 x 64 sequential steps each way (one launch per step)"}
+    o = _ref_or_none(args)
+    if o is not None:
+        ph, xh, dh = p.cpu().numpy(), x.cpu().numpy(), d.cpu().numpy()
+        rms = _host_ms(lambda: o.lstm(xh, ph, dh, H, True), 2)
+        out["reference"] = {"ms": rms, "cores": os.cpu_count()}
+    return out
+
+
 def case_decode(args, torch):
     """KV-cache decoding (GPTModel::ForwardWithKVCache) of the 12-layer/768
     model: a prompt by prefill, then timed decode steps (CUDA events over
@@ -940,7 +967,7 @@ def run_case(args):
     import torch
 
     fn = {"c1": case_c1, "c2": case_c2, "c3": case_c3, "c5": case_c5,
-          "decode": case_decode}.get(args.case, case_kernel)
+          "decode": case_decode, "lstm": case_lstm}.get(args.case, case_kernel)
     out = fn(args, torch)
     if out is not None:
         print(json.dumps(out), flush=True)

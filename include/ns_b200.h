@@ -86,6 +86,15 @@ NS_API int ns_device_supported(void);
  * output has too few tiles to fill the GPU (the dW products); partial tiles
  * are summed in a fixed order, so results do not depend on timing.  With less
  * than ns_gemm_workspace_size bytes the call runs without splitting.
+ *
+ * Accuracy: the tensor core adds into its fp32 accumulator with
+ * round-toward-zero; each 64-term run of K is accumulated in a fresh TMEM
+ * buffer and folded into the result with round-to-nearest, so the error
+ * stays at the level of a sequential fp32 loop (relative L2 ~1e-6 on random
+ * operands, independent of K) except for a bias toward zero of up to about
+ * 3e-6 x (sum of |64-term partial sums|), which shows where long runs of
+ * terms share a sign.  The library's own long sequence reductions (the LSTM
+ * weight gradients) use 32-term runs, which halves it.
  */
 enum {
   NS_EPI_STORE = 0,
@@ -296,6 +305,43 @@ NS_API ns_status ns_conv2d_fwd(const float* x, int B, int IC, int H, int W, cons
 NS_API ns_status ns_conv2d_bwd(const float* x, const float* dy, int B, int IC, int H, int W,
                                const float* weight, int OC, int k, int stride, int pad, float* dx,
                                float* dweight, float* dbias, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ LSTM / BiLSTM
+ * LSTM::Forward / ::Backward (include/layers/lstm.h:320-529) and BiLSTM
+ * (lstm.h:531-664): x [T, B, IN] -> out [T, B, H] (BiLSTM: [T, B, 2H], the
+ * forward cell's state then the reverse cell's), gates i, f, g, o over 4H,
+ * W_ih [4H, IN], W_hh [4H, H], b_ih / b_hh [4H].  The input projection and
+ * the three weight/input-gradient products are tcgen05 GEMMs; the recurrence
+ * is one launch per step.  `cache` (ns_lstm_cache_floats / ns_bilstm_cache_floats
+ * floats, device) carries the gates and cell states from the forward to the
+ * backward; the backward overwrites every gradient (the reference's
+ * MatMul/Zeros) and writes dx unless it is NULL.  B <= 64.
+ * `workspace`: ns_lstm_workspace_size / ns_bilstm_workspace_size bytes. */
+typedef struct {
+  const float *w_ih, *w_hh, *b_ih, *b_hh;
+} ns_lstm_weights;
+typedef struct {
+  float *w_ih, *w_hh, *b_ih, *b_hh;
+} ns_lstm_grads;
+NS_API size_t ns_lstm_cache_floats(int T, int B, int H);
+NS_API size_t ns_lstm_workspace_size(int T, int B, int IN, int H);
+NS_API ns_status ns_lstm_fwd(const float* x, int T, int B, int IN, int H, ns_lstm_weights w,
+                             float* out, float* cache, void* workspace, size_t workspace_bytes,
+                             void* stream);
+/* out is the forward's output (it doubles as the stacked h_{t-1} of dW_hh). */
+NS_API ns_status ns_lstm_bwd(const float* x, const float* out, const float* dout, int T, int B,
+                             int IN, int H, ns_lstm_weights w, float* cache, float* dx,
+                             ns_lstm_grads g, void* workspace, size_t workspace_bytes,
+                             void* stream);
+NS_API size_t ns_bilstm_cache_floats(int T, int B, int H);
+NS_API size_t ns_bilstm_workspace_size(int T, int B, int IN, int H);
+NS_API ns_status ns_bilstm_fwd(const float* x, int T, int B, int IN, int H, ns_lstm_weights fwd,
+                               ns_lstm_weights rev, float* out, float* cache, void* workspace,
+                               size_t workspace_bytes, void* stream);
+NS_API ns_status ns_bilstm_bwd(const float* x, const float* dout, int T, int B, int IN, int H,
+                               ns_lstm_weights fwd, ns_lstm_weights rev, float* cache, float* dx,
+                               ns_lstm_grads gfwd, ns_lstm_grads grev, void* workspace,
                                size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------ K4 embedding

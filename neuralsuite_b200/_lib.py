@@ -35,6 +35,13 @@ class NsError(RuntimeError):
         self.code = code
 
 
+class ns_lstm_weights(ctypes.Structure):
+    _fields_ = [("w_ih", c_void_p), ("w_hh", c_void_p), ("b_ih", c_void_p), ("b_hh", c_void_p)]
+
+
+ns_lstm_grads = ns_lstm_weights  # same layout (four device pointers)
+
+
 class ns_unet_config(ctypes.Structure):
     _fields_ = [("in_channels", c_int), ("base_channels", c_int), ("image_size", c_int),
                 ("max_batch", c_int)]
@@ -89,6 +96,17 @@ _SIGS = {
                               P, c_size_t, P]),
     "ns_conv2d_bwd": (c_int, [P, P, c_int, c_int, c_int, c_int, P, c_int, c_int, c_int, c_int, P,
                               P, P, P, c_size_t, P]),
+    "ns_lstm_cache_floats": (c_size_t, [c_int, c_int, c_int]),
+    "ns_lstm_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "ns_lstm_fwd": (c_int, [P, c_int, c_int, c_int, c_int, ns_lstm_weights, P, P, P, c_size_t, P]),
+    "ns_lstm_bwd": (c_int, [P, P, P, c_int, c_int, c_int, c_int, ns_lstm_weights, P, P,
+                            ns_lstm_weights, P, c_size_t, P]),
+    "ns_bilstm_cache_floats": (c_size_t, [c_int, c_int, c_int]),
+    "ns_bilstm_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "ns_bilstm_fwd": (c_int, [P, c_int, c_int, c_int, c_int, ns_lstm_weights, ns_lstm_weights, P,
+                              P, P, c_size_t, P]),
+    "ns_bilstm_bwd": (c_int, [P, P, c_int, c_int, c_int, c_int, ns_lstm_weights, ns_lstm_weights,
+                              P, P, ns_lstm_weights, ns_lstm_weights, P, c_size_t, P]),
     "ns_embedding_fwd": (c_int, [P, c_int, c_int, P, c_int, P, c_int, c_int, P, P, P]),
     "ns_embedding_bwd": (c_int, [P, c_int, c_int, P, c_int, c_int, c_int, P, c_int, P, P]),
     "ns_adamw_flat": (c_int, [P, P, P, P, c_int64, P, P, c_int, c_float, c_float, c_float,

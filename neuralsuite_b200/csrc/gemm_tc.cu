@@ -54,6 +54,7 @@ constexpr int kEpiThreads = PRE ? 256 : 128;
 
 struct KParams {
   int M, N, K;
+  int chunk;  // k-blocks per TMEM accumulation chunk (1 or 2)
   int tiles_m, tiles_n, splits, kb_total, kb_per;
   int a_mn, b_mn;
   EpiArgs e;
@@ -92,7 +93,9 @@ __device__ __forceinline__ void decode_unit(const KParams& p, int u, int& tm, in
 // at a time into a fresh TMEM buffer, and the epilogue warps fold each chunk
 // into the tile's running sum with round-to-nearest adds, which bounds the
 // error at the level of a sequential fp32 loop whatever K is.
-constexpr int kChunk = 2;
+constexpr int kChunk = 2;  // default; KParams::chunk is what the kernels use
+
+thread_local int t_chunk = kChunk;  // per host thread: see set_accumulation_chunk
 
 template <int BN, int STAGES, bool PRE>
 struct Layout {
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after();
-      for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk) {
+      for (int c0 = kb0; ok && c0 < kb1; c0 += p.chunk) {
         uint32_t d_tmem = tmem_base + r * BN;  // chunk 0 goes straight into the running sum
         int cb = -1;
         if (c0 > kb0) {
@@ -253,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_after();
           d_tmem = tmem_base + (2 + cb) * BN;
         }
-        const int c1 = min(kb1, c0 + kChunk);
+        const int c1 = min(kb1, c0 + p.chunk);
         for (int kb = c0; kb < c1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = uit & 1;
       const uint32_t r_tmem = tmem_base + lane_off + r * BN;
       // Fold chunks 1.. of this tile into the running sum, round to nearest.
-      for (int c0 = kb0 + kChunk; c0 < kb1; c0 += kChunk, ++cit) {
+      for (int c0 = kb0 + p.chunk; c0 < kb1; c0 += p.chunk, ++cit) {
         const int cb = cit & 1;
         if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
           ok = false;
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         int tm, tn, split, kb0, kb1;
         decode_unit(p, u, tm, tn, split, kb0, kb1);
-        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk, ++cit) {
+        for (int c0 = kb0; ok && c0 < kb1; c0 += p.chunk, ++cit) {
           const int cb = cit & 1;
           if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
             ok = false;
@@ -588,7 +591,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           }
           fence_after();
           const uint32_t d_tmem = tmem_base + cb * BN;
-          const int c1 = min(kb1, c0 + kChunk);
+          const int c1 = min(kb1, c0 + p.chunk);
           for (int kb = c0; kb < c1; ++kb, ++it) {
             const int s = it % S;
             const uint32_t ph = (it / S) & 1u;
@@ -650,7 +653,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       decode_unit(p, u, tm, tn, split, kb0, kb1);
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
-      for (int c0 = kb0; c0 < kb1; c0 += kChunk, ++cit) {
+      for (int c0 = kb0; c0 < kb1; c0 += p.chunk, ++cit) {
         const int cb = cit & 1;
         if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
           ok = false;
@@ -1047,7 +1050,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       for (int u = unit0; ok && u < n_units; u += unit_step) {
         int tm, tn, split, kb0, kb1;
         decode_unit(p, u, tm, tn, split, kb0, kb1);
-        for (int c0 = kb0; ok && c0 < kb1; c0 += kChunk, ++cit) {
+        for (int c0 = kb0; ok && c0 < kb1; c0 += p.chunk, ++cit) {
           const int cb = cit & 1;
           if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
             ok = false;
@@ -1055,7 +1058,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
           }
           fence_after();
           const uint32_t d_tmem = tmem_base + cb * BN;
-          const int c1 = min(kb1, c0 + kChunk);
+          const int c1 = min(kb1, c0 + p.chunk);
           for (int kb = c0; kb < c1; ++kb, ++it) {
             const int s = it % S;
             const uint32_t ph = (it / S) & 1u;
@@ -1117,7 +1120,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       decode_unit(p, u, tm, tn, split, kb0, kb1);
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
-      for (int c0 = kb0; c0 < kb1; c0 += kChunk, ++cit) {
+      for (int c0 = kb0; c0 < kb1; c0 += p.chunk, ++cit) {
         const int cb = cit & 1;
         if (!mbar_wait(chf_bar(cb), (cit >> 1) & 1u, abort, &g_timeout)) {
           ok = false;
@@ -1388,6 +1391,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   }
   KParams kp;
   kp.M = M; kp.N = N; kp.K = K;
+  kp.chunk = t_chunk;
   kp.tiles_m = pl.tiles_m; kp.tiles_n = pl.tiles_n; kp.splits = pl.splits;
   kp.kb_total = pl.kb_total; kp.kb_per = pl.kb_per;
   kp.a_mn = a_mn; kp.b_mn = b_mn;
@@ -1442,6 +1446,12 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
 
 ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {
   return split_lo(x, rows, cols, ld, lo, s);
+}
+
+int set_accumulation_chunk(int kblocks) {
+  const int old = t_chunk;
+  t_chunk = kblocks == 1 ? 1 : kChunk;
+  return old;
 }
 
 // Self-test of the bounded waits: one warp waits on an mbarrier that nothing

@@ -56,6 +56,15 @@ ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, c
 // -(CUDA error) if the flag could not be read.
 int consume_timeout_flag();
 
+// The tensor core adds into its fp32 accumulator with round-toward-zero, so
+// each TMEM chunk (kblocks x 32 terms) carries a bias toward zero of up to
+// ~1 ulp of the chunk sum per MMA; chunks are folded with round-to-nearest.
+// For reductions whose partial sums share a sign over many terms (a weight
+// gradient summed over a long sequence) 1-k-block chunks halve that bias at
+// about a quarter of the throughput.  Per host thread; returns the previous
+// setting (2 = default).
+int set_accumulation_chunk(int kblocks);
+
 // Launches the bounded-wait self-test kernel (a wait that runs out after
 // limit_us microseconds and raises the flag consume_timeout_flag reads).
 ns_status wait_probe(int limit_us, cudaStream_t s);

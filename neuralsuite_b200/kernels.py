@@ -369,3 +369,47 @@ def conv2d_bwd(x, dy, weight, stride=1, pad=0, want_dx=True):
     _lib.check(lib.ns_conv2d_bwd(_p(x), _p(dy), B, IC, H, W, _p(weight), OC, k, stride, pad,
                                  _p(dx), _p(dw), _p(db), _p(ws), nb, _stream()))
     return dx, dw, db
+
+
+def _lstm_views(flat, IN, H):
+    """Registration-order views (weight_ih [4H, IN], weight_hh [4H, H], bias_ih,
+    bias_hh) of one cell's flat parameter (or gradient) tensor."""
+    a, b = 4 * H * IN, 4 * H * IN + 4 * H * H
+    return flat[:a].view(4 * H, IN), flat[a:b].view(4 * H, H), flat[b:b + 4 * H], flat[b + 4 * H:b + 8 * H]
+
+
+def _lstm_struct(views):
+    return _lib.ns_lstm_weights(*[v.data_ptr() for v in views])
+
+
+def lstm_fwd_bwd(x, params, dout, H, bidir=False, want_dx=True):
+    """LSTM / BiLSTM Forward then Backward (include/layers/lstm.h:320-664):
+    x [T, B, IN], params flat in registration order -> (out, dx, grads flat)."""
+    lib = _lib.load()
+    _req(x, "x")
+    T, B, IN = x.shape
+    n1 = 4 * H * IN + 4 * H * H + 8 * H
+    grads = torch.empty_like(params)
+    dx = torch.empty_like(x) if want_dx else None
+    if bidir:
+        out = torch.empty((T, B, 2 * H), dtype=_f32, device=x.device)
+        cache = torch.empty(lib.ns_bilstm_cache_floats(T, B, H), dtype=_f32, device=x.device)
+        nb = lib.ns_bilstm_workspace_size(T, B, IN, H)
+        ws = _ws(nb, x.device)
+        wf, wr = (_lstm_struct(_lstm_views(params[o:o + n1], IN, H)) for o in (0, n1))
+        gf, gr = (_lstm_struct(_lstm_views(grads[o:o + n1], IN, H)) for o in (0, n1))
+        _lib.check(lib.ns_bilstm_fwd(_p(x), T, B, IN, H, wf, wr, _p(out), _p(cache), _p(ws), nb,
+                                     _stream()))
+        _lib.check(lib.ns_bilstm_bwd(_p(x), _p(dout), T, B, IN, H, wf, wr, _p(cache), _p(dx), gf,
+                                     gr, _p(ws), nb, _stream()))
+    else:
+        out = torch.empty((T, B, H), dtype=_f32, device=x.device)
+        cache = torch.empty(lib.ns_lstm_cache_floats(T, B, H), dtype=_f32, device=x.device)
+        nb = lib.ns_lstm_workspace_size(T, B, IN, H)
+        ws = _ws(nb, x.device)
+        w = _lstm_struct(_lstm_views(params, IN, H))
+        g = _lstm_struct(_lstm_views(grads, IN, H))
+        _lib.check(lib.ns_lstm_fwd(_p(x), T, B, IN, H, w, _p(out), _p(cache), _p(ws), nb, _stream()))
+        _lib.check(lib.ns_lstm_bwd(_p(x), _p(out), _p(dout), T, B, IN, H, w, _p(cache), _p(dx), g,
+                                   _p(ws), nb, _stream()))
+    return out, dx, grads

@@ -435,6 +435,18 @@ class Ref(_Base):
                    _ptr(dx), *[_ptr(a) for a in g])
         return y, dx, g
 
+    def lstm(self, x, params, dout, hidden, bidir=False):
+        """LSTM / BiLSTM Forward + Backward: (out, dx, grads), params and grads
+        flat in registration order."""
+        x, params, dout = f32(x), f32(params), f32(dout)
+        T, B, IN = x.shape
+        out = np.zeros((T, B, (2 if bidir else 1) * hidden), np.float32)
+        dx = np.zeros_like(x)
+        grads = np.zeros_like(params)
+        self._call("lstm", [_i] * 5 + [_p] * 6, T, B, IN, hidden, int(bidir), _ptr(params),
+                   _ptr(x), _ptr(dout), _ptr(out), _ptr(dx), _ptr(grads))
+        return out, dx, grads
+
     def conv2d(self, x, weight, bias, stride, pad, dout=None):
         """Conv2D::Forward (+ ::Backward with dout): y, and (dx, dweight, dbias)."""
         x, weight, bias = f32(x), f32(weight), f32(bias)

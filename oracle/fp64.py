@@ -349,3 +349,55 @@ def unet_fwd_bwd(flat, sizes, x, target, in_ch, base, hw):
     de0_part, _ = level_bwd(1, de1_part + ds1)
     level_bwd(0, de0_part + ds0)
     return loss, y, np.concatenate([g.reshape(-1) for g in G])
+
+
+def _sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def lstm_fwd_bwd(x, w_ih, w_hh, b_ih, b_hh, dout):
+    """LSTM::Forward / ::Backward (include/layers/lstm.h:348-529) in float64:
+    returns (out [T,B,H], dx, [dW_ih, dW_hh, db_ih, db_hh])."""
+    x, w_ih, w_hh, b = f64(x), f64(w_ih), f64(w_hh), f64(b_ih) + f64(b_hh)
+    T, B, _ = x.shape
+    H = w_hh.shape[1]
+    h = np.zeros((B, H))
+    c = np.zeros((B, H))
+    cache, outs = [], []
+    for t in range(T):
+        pre = x[t] @ w_ih.T + h @ w_hh.T + b
+        i, f, g, o = (_sigmoid(pre[:, :H]), _sigmoid(pre[:, H:2 * H]), np.tanh(pre[:, 2 * H:3 * H]),
+                      _sigmoid(pre[:, 3 * H:]))
+        c_new = f * c + i * g
+        tc = np.tanh(c_new)
+        cache.append((h, c, i, f, g, o, tc))
+        h, c = o * tc, c_new
+        outs.append(h)
+    d = f64(dout)
+    dW_ih, dW_hh, db = np.zeros_like(w_ih), np.zeros_like(w_hh), np.zeros(4 * H)
+    dx = np.zeros_like(x)
+    dh_next = np.zeros((B, H))
+    dc_next = np.zeros((B, H))
+    for t in reversed(range(T)):
+        h_prev, c_prev, i, f, g, o, tc = cache[t]
+        dh = d[t] + dh_next
+        dc = dh * o * (1 - tc * tc) + dc_next
+        dpre = np.concatenate([dc * g * i * (1 - i), dc * c_prev * f * (1 - f),
+                               dc * i * (1 - g * g), dh * tc * o * (1 - o)], 1)
+        dc_next = dc * f
+        dh_next = dpre @ w_hh
+        dW_ih += dpre.T @ x[t]
+        dW_hh += dpre.T @ h_prev
+        db += dpre.sum(0)
+        dx[t] = dpre @ w_ih
+    return np.stack(outs), dx, [dW_ih, dW_hh, db, db.copy()]
+
+
+def bilstm_fwd_bwd(x, wf, wr, dout):
+    """BiLSTM (include/layers/lstm.h:531-664) in float64; wf / wr are
+    (w_ih, w_hh, b_ih, b_hh).  Returns (out [T,B,2H], dx, grads fwd + rev)."""
+    H = f64(wf[1]).shape[1]
+    d = f64(dout)
+    of, dxf, gf = lstm_fwd_bwd(x, *wf, d[:, :, :H])
+    orr, dxr, gr = lstm_fwd_bwd(f64(x)[::-1], *wr, d[::-1, :, H:])
+    return np.concatenate([of, orr[::-1]], 2), dxf + dxr[::-1], gf + gr

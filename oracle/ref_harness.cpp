@@ -24,6 +24,7 @@
 //   Conv2D                  include/layers/conv2d.h:192-414
 //   ResidualBlock           include/layers/residual.h:23-64
 //   MSELoss                 include/losses.h:97-124
+//   LSTM / BiLSTM           include/layers/lstm.h:320-664
 //   ClipGradients           train_llm.cpp:112-129 (restated: it is a static
 //                           function of the training program, not a library
 //                           symbol)
@@ -40,6 +41,7 @@
 #include "gpt.h"
 #include "layers/conv2d.h"
 #include "layers/layernorm.h"
+#include "layers/lstm.h"
 #include "layers/residual.h"
 #include "losses.h"
 #include "optimizers.h"
@@ -240,6 +242,34 @@ int nsref_conv2d(int B, int IC, int H, int W, int OC, int k, int stride, int pad
       std::vector<Tensor*> g = conv.GetGradients();
       ToHost(*g[0], dweight);
       ToHost(*g[1], dbias);
+    }
+  });
+}
+
+// LSTM (bidir = 0) or BiLSTM (bidir = 1) Forward + Backward
+// (include/layers/lstm.h:320-664) with the flat parameters in registration
+// order (weight_ih, weight_hh, bias_ih, bias_hh; BiLSTM: forward's then
+// reverse's); grads likewise.
+int nsref_lstm(int T, int B, int IN, int H, int bidir, const float* params, const float* x,
+               const float* dout, float* out, float* dx, float* grads) {
+  return Guard([&] {
+    std::unique_ptr<Layer> layer;
+    if (bidir) layer = std::make_unique<BiLSTM>(IN, H);
+    else layer = std::make_unique<LSTM>(IN, H);
+    size_t off = 0;
+    for (Tensor* t : layer->GetParameters()) {
+      std::memcpy(t->Data(), params + off, t->TotalSize() * sizeof(float));
+      off += t->TotalSize();
+    }
+    Tensor tx = FromHost(x, {T, B, IN});
+    Tensor ty = layer->Forward(tx);
+    ToHost(ty, out);
+    Tensor td = FromHost(dout, ty.Shape());
+    ToHost(layer->Backward(td), dx);
+    off = 0;
+    for (Tensor* t : layer->GetGradients()) {
+      std::memcpy(grads + off, t->Data(), t->TotalSize() * sizeof(float));
+      off += t->TotalSize();
     }
   });
 }
