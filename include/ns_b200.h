@@ -207,8 +207,9 @@ NS_API ns_status ns_attn_fwd_lo(const float* qkv, const float* qkv_lo, int B, in
                          float* out, float* out_lo, float* lse, void* workspace,
                          size_t workspace_bytes, void* stream);
 /* 0 (default): head_dim 32 / 64 run on the tensor cores (3xTF32, tcgen05) in
- * both directions, other sizes on the SIMT kernels; 1: SIMT kernels for every
- * size.  Per host thread.
+ * both directions (the backward's dK and dV from one kernel), other sizes on
+ * the SIMT kernels; 1: SIMT kernels for every size; 2: as 0 with dK and dV
+ * from two separate kernels.  Per host thread.
  * No reference counterpart (engine selection for tests and profiling). */
 NS_API ns_status ns_attn_set_engine(int engine);
 NS_API size_t ns_attn_bwd_workspace_size(int B, int T, int H, int D);

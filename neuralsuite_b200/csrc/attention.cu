@@ -23,7 +23,9 @@
 namespace nsb {
 namespace {
 
-thread_local int t_attn_engine = 0;  // 0 auto (tensor cores where supported), 1 SIMT
+// 0 auto (tensor cores where supported, dK and dV from one kernel), 1 SIMT,
+// 2 tensor cores with dK and dV from separate kernels (a cross-check).
+thread_local int t_attn_engine = 0;
 
 constexpr int kBr = 64;   // query rows per block
 constexpr int kBc = 64;   // keys per block
@@ -452,7 +454,7 @@ size_t ns_attn_fwd_workspace_size(int B, int T, int H, int D) {
 }
 
 ns_status ns_attn_set_engine(int engine) {
-  NS_REQUIRE(engine == 0 || engine == 1, "ns_attn_set_engine: engine must be 0 or 1");
+  NS_REQUIRE(engine >= 0 && engine <= 2, "ns_attn_set_engine: engine must be 0, 1 or 2");
   t_attn_engine = engine;
   return NS_OK;
 }
@@ -479,7 +481,7 @@ ns_status ns_attn_fwd_lo(const float* qkv, const float* qkv_lo, int B, int T, in
              "ns_attn_fwd: workspace too small");
   cudaStream_t s = as_stream(stream);
   const bool ws_ok = qkv_lo ? true : (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0);
-  if (t_attn_engine == 0 && (D == 32 || D == 64) && ws_ok &&
+  if (t_attn_engine != 1 && (D == 32 || D == 64) && ws_ok &&
       attn_tc::fwd_supported(qkv, out, B, T, H, D))
     return attn_tc::fwd(qkv, qkv_lo, B, T, H, D, out, out_lo, lse, static_cast<float*>(workspace), s);
   ns_status rc;
@@ -520,7 +522,7 @@ ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out
   const int64_t n = (int64_t)B * H * T;
   const size_t delta_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
   float* lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + delta_bytes);
-  const bool tc = t_attn_engine == 0 && (D == 32 || D == 64) &&
+  const bool tc = t_attn_engine != 1 && (D == 32 || D == 64) &&
                   (reinterpret_cast<uintptr_t>(lo) & 15) == 0 &&
                   attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D);
   // The tensor-core path takes dO's lo part from the Delta pass.
@@ -528,7 +530,8 @@ ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out
   attn_delta_k<<<(unsigned)ceil_div64((int64_t)B * T, 8), 256, 0, s>>>(out, dout, B, T, H, D, delta,
                                                                      dout_lo);
   { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
-  if (tc) return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, s);
+  if (tc)
+    return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, t_attn_engine == 0, s);
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 32) return launch_bwd<32>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);
   if (D <= 64) return launch_bwd<64>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

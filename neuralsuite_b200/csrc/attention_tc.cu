@@ -1211,6 +1211,542 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------- fused dK + dV
+//
+// One persistent kernel for both key-side gradients (rows = keys, minor
+// blocks = 64 queries): per block j
+//   S^T = K.Q^T -> P^T = exp(S^T*scale - lse);   dP^T = V.dO^T
+//   dV += P^T.dO;   dS^T = P^T o (dP^T - Delta);   dK += dS^T.Q
+// so S^T is computed once for both products (the two-kernel path computes it
+// twice and streams Q and lse twice).  TMEM has the same map as the dK
+// kernel's: K and V rows (hi / lo) as A operands, S (then P^T hi), dP (then
+// dS^T hi), one lo column block shared in turn by P^T lo and dS^T lo, and one
+// product accumulator shared in turn by the dV and dK products, which the
+// element-wise warps fold into two register accumulators.  The tensor core
+// runs, per block,
+//   prodV_j | S_{j+1} | prodK_j | dP_{j+1} | prodV_{j+1} | ...
+// and each MMA group waits only for the element-wise step it reads
+// (ew_p: P^T written, ew_ds: dS^T written); the element-wise warps, per block:
+//   read S_j -> P_j (registers) -> fold prodK_{j-1} -> write P^T hi/lo ->
+//   fold prodV_j -> read dP_j -> dS_j -> write dS^T hi/lo.
+// Rings: Q K-major (with the block's lse*log2e / Delta vectors, in a
+// separate vector ring deep enough that a vector is never overwritten before
+// its dS step), dO K-major, dO MN-major, Q MN-major.
+template <int D>
+struct KvLayout {
+  static constexpr int kR0 = D == 64 ? 2 : 4;  // Q K-major / dO K-major slots
+  static constexpr int kR2 = D == 64 ? 1 : 2;  // dO MN-major / Q MN-major slots
+  static constexpr int kVec = 2 * kR0;         // vector slots (see the producer)
+  static constexpr uint32_t kTile = kBKV * D * 4;
+  static constexpr uint32_t kSlot = 2 * kTile;  // raw | lo
+  static constexpr uint32_t kRing0 = 0;
+  static constexpr uint32_t kRing1 = kRing0 + kR0 * kSlot;
+  static constexpr uint32_t kRing2 = kRing1 + kR0 * kSlot;
+  static constexpr uint32_t kRing3 = kRing2 + kR2 * kSlot;
+  static constexpr uint32_t kVecs = kRing3 + kR2 * kSlot;  // [kVec][2][64] floats
+  static constexpr uint32_t kBars = kVecs + kVec * 2 * kBKV * 4;
+  static constexpr uint32_t kNumBars = 4 * kR0 + 4 * kR2 + kVec + 10;
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  static constexpr uint32_t kDynSmem = kBytes + 1024;
+  static_assert(kDynSmem <= 232448, "shared memory budget");
+  static_assert(kDynSmem > 232448 / 2, "one CTA per SM (the CTA takes all 512 TMEM columns)");
+  // The Q-ring producer runs at most kR0 + 1 blocks ahead of the element-wise
+  // warps, so a vector slot is rewritten only after its block's dS step.
+  static_assert(kVec >= kR0 + 2, "vector ring depth");
+};
+
+// Producer of one ring (raw and lo tiles of each block of every item of this
+// CTA); with VEC > 0, also the block's lse*log2e and Delta into vector slot
+// g % VEC, announced on that slot's barrier (vfull0 + 8 * slot).
+template <int D, int R, int VEC>
+__device__ void produce_kv(uint32_t ring, uint32_t full0, uint32_t empty0, const CUtensorMap* m,
+                           const CUtensorMap* mlo, int xb, float* vecs, uint32_t vfull0,
+                           const BwdParams& p, volatile int* abort) {
+  constexpr uint32_t kTile = kBKV * D * 4, kSlot = 2 * kTile;
+  const int lane = threadIdx.x & 31;
+  bool issued[R];
+  uint32_t issued_ph[R];
+#pragma unroll
+  for (int s = 0; s < R; ++s) issued[s] = false, issued_ph[s] = 0;
+  bool ok = true;
+  uint32_t g = 0;
+  for (int k = 0; ok; ++k) {
+    const int w = work_item((int)blockIdx.x, k, (int)gridDim.x, p.n_items);
+    if (w < 0) break;
+    const BwdItem it = bwd_item<true>(w, p);
+    const int xcol = xb + it.h * D;
+    for (int i = 0; i < it.n_blk; ++i, ++g) {
+      const int s = g % R;
+      const uint32_t ph = (g / R) & 1u;
+      if (!warp_wait(empty0 + 8u * s, ph ^ 1u, abort, &g_timeout)) {
+        ok = false;
+        break;
+      }
+      issued[s] = true;
+      issued_ph[s] = ph;
+      const int blk = it.blk0 + i;
+      const int row = it.b * p.T + blk * kBKV;
+      const uint32_t dst = ring + s * kSlot;
+      if (elect_one()) {
+        mbar_expect_tx(full0 + 8u * s, 2 * kTile);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_2d(dst + c * 8192, m, full0 + 8u * s, xcol + 32 * c, row);
+          tma_load_2d(dst + kTile + c * 8192, mlo, full0 + 8u * s, xcol + 32 * c, row);
+        }
+      }
+      __syncwarp();
+      if (VEC > 0) {
+        float* vec = vecs + (g % VEC) * 2 * kBKV;
+        for (int c = lane; c < kBKV; c += 32) {
+          const int q = blk * kBKV + c;
+          const bool in = q < p.T;
+          vec[c] = in ? p.lse[(size_t)it.bh * p.T + q] * kLog2e : 0.0f;
+          vec[kBKV + c] = in ? p.delta[(size_t)it.bh * p.T + q] : 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(vfull0 + 8u * (g % VEC));
+        __syncwarp();
+      }
+    }
+  }
+  if (!ok && lane == 0)
+    for (int s = 0; s < R; ++s)
+      if (issued[s]) mbar_wait_drain(full0 + 8u * s, issued_ph[s], &g_timeout);
+}
+
+// Producer of the two MN-major rings, block by block in consumption order
+// (dO for prodV_j, then Q for prodK_j).
+template <int D, int R>
+__device__ void produce_kv_mn(uint32_t ring2, uint32_t full2, uint32_t empty2, uint32_t ring3,
+                              uint32_t full3, uint32_t empty3, const CUtensorMap* mdo,
+                              const CUtensorMap* mdolo, const CUtensorMap* mq,
+                              const CUtensorMap* mqlo, const BwdParams& p, volatile int* abort) {
+  constexpr uint32_t kTile = kBKV * D * 4, kSlot = 2 * kTile;
+  const int lane = threadIdx.x & 31;
+  bool issued[2][R];
+  uint32_t issued_ph[2][R];
+#pragma unroll
+  for (int s = 0; s < R; ++s) issued[0][s] = issued[1][s] = false, issued_ph[0][s] = issued_ph[1][s] = 0;
+  bool ok = true;
+  uint32_t g = 0;
+  for (int k = 0; ok; ++k) {
+    const int w = work_item((int)blockIdx.x, k, (int)gridDim.x, p.n_items);
+    if (w < 0) break;
+    const BwdItem it = bwd_item<true>(w, p);
+    for (int i = 0; i < it.n_blk && ok; ++i, ++g) {
+      const int s = g % R;
+      const uint32_t ph = (g / R) & 1u;
+      const int row = it.b * p.T + (it.blk0 + i) * kBKV;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t full = (r ? full3 : full2) + 8u * s, empty = (r ? empty3 : empty2) + 8u * s;
+        if (!warp_wait(empty, ph ^ 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        issued[r][s] = true;
+        issued_ph[r][s] = ph;
+        const uint32_t dst = (r ? ring3 : ring2) + s * kSlot;
+        const CUtensorMap* m = r ? mq : mdo;
+        const CUtensorMap* mlo = r ? mqlo : mdolo;
+        const int xcol = it.h * D;  // Q's columns in qkv, dO's in dout
+        if (elect_one()) {
+          mbar_expect_tx(full, 2 * kTile);
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_2d(dst + c * 8192, m, full, xcol + 32 * c, row);
+            tma_load_2d(dst + kTile + c * 8192, mlo, full, xcol + 32 * c, row);
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  if (!ok && lane == 0)
+    for (int r = 0; r < 2; ++r)
+      for (int s = 0; s < R; ++s)
+        if (issued[r][s]) mbar_wait_drain((r ? full3 : full2) + 8u * s, issued_ph[r][s], &g_timeout);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQklo,
+                       const __grid_constant__ CUtensorMap tmDk, const __grid_constant__ CUtensorMap tmDklo,
+                       const __grid_constant__ CUtensorMap tmDmn, const __grid_constant__ CUtensorMap tmDmnlo,
+                       const __grid_constant__ CUtensorMap tmQmn, const __grid_constant__ CUtensorMap tmQmnlo,
+                       const BwdParams p) {
+  using L = KvLayout<D>;
+  constexpr int R0 = L::kR0, R2 = L::kR2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBars;
+  const uint32_t full0 = bar0, empty0 = bar0 + 8u * R0;
+  const uint32_t full1 = bar0 + 16u * R0, empty1 = bar0 + 24u * R0;
+  const uint32_t full2 = bar0 + 32u * R0, empty2 = full2 + 8u * R2;
+  const uint32_t full3 = empty2 + 8u * R2, empty3 = full3 + 8u * R2;
+  const uint32_t a_ready = empty3 + 8u * R2;
+  const uint32_t a_free = a_ready + 8u, s_full = a_ready + 16u, dp_full = a_ready + 24u;
+  const uint32_t ew_p = a_ready + 32u, ew_ds = a_ready + 40u, out_v = a_ready + 48u;
+  const uint32_t out_k = a_ready + 56u, drain = a_ready + 64u, vfull = a_ready + 72u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* vecs = reinterpret_cast<float*>(smem + L::kVecs);
+
+  const int cta = (int)blockIdx.x, G = (int)gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R0; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+      mbar_init(full1 + 8u * s, 1);
+      mbar_init(empty1 + 8u * s, 1);
+    }
+    for (int s = 0; s < R2; ++s) {
+      mbar_init(full2 + 8u * s, 1);
+      mbar_init(empty2 + 8u * s, 1);
+      mbar_init(full3 + 8u * s, 1);
+      mbar_init(empty3 + 8u * s, 1);
+    }
+    mbar_init(a_ready, 2 * kWgThreads);
+    mbar_init(a_free, 1);
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(ew_p, 2 * kWgThreads);
+    mbar_init(ew_ds, 2 * kWgThreads);
+    mbar_init(out_v, 1);
+    mbar_init(out_k, 1);
+    mbar_init(drain, 1);
+    for (int v = 0; v < L::kVec; ++v) mbar_init(vfull + 8u * v, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    reg_dec();
+    if (warp == 0) {
+      produce_kv<D, R0, L::kVec>(sbase + L::kRing0, full0, empty0, &tmQk, &tmQklo, 0, vecs, vfull,
+                                 p, abort);
+    } else if (warp == 2) {
+      produce_kv<D, R0, 0>(sbase + L::kRing1, full1, empty1, &tmDk, &tmDklo, 0, nullptr, 0u, p,
+                           abort);
+    } else if (warp == 3) {
+      produce_kv_mn<D, R2>(sbase + L::kRing2, full2, empty2, sbase + L::kRing3, full3, empty3,
+                           &tmDmn, &tmDmnlo, &tmQmn, &tmQmnlo, p, abort);
+    } else {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t id_s = instr_desc(kBKV, 0, 0);
+      constexpr uint32_t id_o = instr_desc(D, 0, 1);
+      auto issue_k = [&](uint32_t d, uint32_t a, uint32_t t) {
+#pragma unroll
+        for (int kk = 0; kk < D / 8; ++kk)
+          mma_ts(d, a + kk * 8, k_desc(t, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < D / 8; ++kk) {
+          mma_ts(d, a + kk * 8, k_desc(t + L::kTile, kk), id_s, 1u);
+          mma_ts(d, a + D + kk * 8, k_desc(t, kk), id_s, 1u);
+        }
+      };
+      // Product into O: A hi at column a_hi, lo at kBElo; B the MN-major tile at tb.
+      auto issue_prod = [&](uint32_t a_hi, uint32_t tb) {
+        const uint32_t tblo = tb + L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 8; ++kk)
+          mma_ts(tmem + kBO, tmem + a_hi + kk * 8, v_desc(tb, kk), id_o, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 8; ++kk) {
+          mma_ts(tmem + kBO, tmem + a_hi + kk * 8, v_desc(tblo, kk), id_o, 1u);
+          mma_ts(tmem + kBO, tmem + kBElo + kk * 8, v_desc(tb, kk), id_o, 1u);
+        }
+      };
+      // Each operation waits for its operand tile (and, for the products, the
+      // element-wise step that wrote its A operand), then issues from one
+      // elected lane of the converged warp and commits.
+      auto op_s = [&](uint32_t g) -> bool {
+        const int s = g % R0;
+        if (!warp_wait(full0 + 8u * s, (g / R0) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s * L::kSlot);
+          commit(empty0 + 8u * s);
+          commit(s_full);
+        }
+        __syncwarp();
+        return true;
+      };
+      auto op_dp = [&](uint32_t g) -> bool {
+        const int s = g % R0;
+        if (!warp_wait(full1 + 8u * s, (g / R0) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s * L::kSlot);
+          commit(empty1 + 8u * s);
+          commit(dp_full);
+        }
+        __syncwarp();
+        return true;
+      };
+      auto op_prod = [&](uint32_t g, bool dk) -> bool {
+        const int s = g % R2;
+        if (!warp_wait(dk ? ew_ds : ew_p, g & 1u, abort, &g_timeout)) return false;
+        if (!warp_wait((dk ? full3 : full2) + 8u * s, (g / R2) & 1u, abort, &g_timeout)) return false;
+        fence_after();
+        if (elect_one()) {
+          issue_prod(dk ? kBdP : kBS, sbase + (dk ? L::kRing3 : L::kRing2) + s * L::kSlot);
+          commit((dk ? empty3 : empty2) + 8u * s);
+          commit(dk ? out_k : out_v);
+        }
+        __syncwarp();
+        return true;
+      };
+      auto release_a = [&]() {
+        if (elect_one()) commit(a_free);
+        __syncwarp();
+      };
+      bool ok = true;
+      uint32_t g = 0;
+      for (int k = 0; ok; ++k) {
+        const int w = work_item(cta, k, G, p.n_items);
+        if (w < 0) break;
+        const int n_blk = bwd_item<true>(w, p).n_blk;
+        ok = warp_wait(a_ready, (uint32_t)k & 1u, abort, &g_timeout);
+        fence_after();
+        if (ok) ok = op_s(g);
+        if (ok) ok = op_dp(g);
+        if (ok && n_blk == 1) release_a();
+        for (int i = 0; ok && i < n_blk; ++i) {
+          const uint32_t gi = g + (uint32_t)i;
+          // prodV_i (after P_i), then S_{i+1} over P_i's columns (in issue order).
+          ok = op_prod(gi, false);
+          if (ok && i + 1 < n_blk) ok = op_s(gi + 1);
+          // prodK_i (after dS_i), then dP_{i+1} over dS_i's columns.
+          if (ok) ok = op_prod(gi, true);
+          if (ok && i + 1 < n_blk) {
+            ok = op_dp(gi + 1);
+            if (ok && i + 2 == n_blk) release_a();  // the item's last S and dP are issued
+          }
+        }
+        g += (uint32_t)n_blk;
+      }
+      if (!ok) {
+        if (elect_one()) commit(drain);
+        __syncwarp();
+        mbar_wait_drain(drain, 0, &g_timeout);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ element-wise
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
+    const int wg = (warp - 4) >> 2;
+    const int ew = warp & 3;
+    const int row = ew * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    const size_t ld = (size_t)3 * p.C;
+    const bool folds = D == 64 || wg == 0;
+    const float c2 = p.scale_log2;
+    auto a_rows = [&](const BwdItem& it, const float*& a1, const float*& a2) -> bool {
+      const int r = it.r0 + row;
+      const bool r_in = r < p.T;
+      const size_t grow = (size_t)it.b * p.T + (r_in ? r : 0);
+      a1 = p.qkv + grow * ld + p.C + (size_t)it.h * D;
+      a2 = p.qkv + grow * ld + 2 * (size_t)p.C + (size_t)it.h * D;
+      return r_in;
+    };
+    float acc_v[32], acc_k[32];
+    bool ok = true;
+    uint32_t g = 0;
+    int prev_w = -1;
+    auto fold = [&](uint32_t bar, uint32_t gi, float (&acc)[32]) -> bool {
+      if (!mbar_wait(bar, gi & 1u, abort, &g_timeout)) return false;
+      fence_after();
+      if (folds) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + kBO + 32 * wg, v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) acc[c] = __fadd_rn(acc[c], __uint_as_float(v[c]));
+      }
+      return true;
+    };
+    // The previous item's last dK product, then its dK and dV rows.
+    auto finish = [&](int w, uint32_t last) -> bool {
+      if (!fold(out_k, last, acc_k)) return false;
+      fence_before();  // the product's TMEM columns are read before the next prodV writes them
+      const BwdItem it = bwd_item<true>(w, p);
+      const int r = it.r0 + row;
+      if (r < p.T && folds) {
+        const size_t base = ((size_t)it.b * p.T + r) * ld + it.h * D + 32 * wg;
+        float* dk = p.dqkv + base + p.C;
+        float* dv = p.dqkv + base + 2 * (size_t)p.C;
+        const float f = p.scale;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          *reinterpret_cast<float4*>(dk + c) =
+              make_float4(acc_k[c] * f, acc_k[c + 1] * f, acc_k[c + 2] * f, acc_k[c + 3] * f);
+          *reinterpret_cast<float4*>(dv + c) =
+              make_float4(acc_v[c], acc_v[c + 1], acc_v[c + 2], acc_v[c + 3]);
+        }
+      }
+      return true;
+    };
+    uint32_t prev_last = 0;
+    for (int k = 0; ok; ++k) {
+      const int w = work_item(cta, k, G, p.n_items);
+      if (w < 0) break;
+      const BwdItem it = bwd_item<true>(w, p);
+      const int r = it.r0 + row;  // key index
+      {
+        const float* a1;
+        const float* a2;
+        const bool r_in = a_rows(it, a1, a2);
+        if (k > 0 && !mbar_wait(a_free, (uint32_t)(k - 1) & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const float* src = t ? a2 : a1;
+          const uint32_t base = tmem + lane_off + (t ? kBA2 : kBA1);
+          for (int cc = wg; cc < D / 32; cc += 2) {
+            uint32_t hi[32], lo[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 x = r_in ? *reinterpret_cast<const float4*>(src + 32 * cc + i)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                hi[i + e] = __float_as_uint(tf32_hi(xs[e]));
+                lo[i + e] = __float_as_uint(tf32_lo(xs[e]));
+              }
+            }
+            tmem_st32(base + 32 * cc, hi);
+            tmem_st32(base + D + 32 * cc, lo);
+          }
+        }
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(a_ready);
+        const int wn = work_item(cta, k + 1, G, p.n_items);
+        if (wn >= 0) {
+          const float* n1;
+          const float* n2;
+          if (a_rows(bwd_item<true>(wn, p), n1, n2)) {
+            for (int cc = wg; cc < D / 32; cc += 2) {
+              asm volatile("prefetch.L2 [%0];" ::"l"(n1 + 32 * cc));
+              asm volatile("prefetch.L2 [%0];" ::"l"(n2 + 32 * cc));
+            }
+          }
+        }
+      }
+      if (prev_w >= 0 && !finish(prev_w, prev_last)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) acc_v[c] = acc_k[c] = 0.0f;
+      for (int i = 0; i < it.n_blk; ++i) {
+        const uint32_t gi = g + (uint32_t)i;
+        if (!mbar_wait(s_full, gi & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        uint32_t sv[32];
+        tmem_ld32(tmem + lane_off + kBS + 32 * wg, sv);
+        // The vectors of block gi.
+        if (!mbar_wait(vfull + 8u * (gi % L::kVec), (gi / L::kVec) & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        const float* vec = vecs + (gi % L::kVec) * 2 * kBKV + 32 * wg;
+        const int m0 = (it.blk0 + i) * kBKV + 32 * wg;
+        const int mb0 = (it.blk0 + i) * kBKV;
+        const bool full = mb0 >= it.r0 + kBQ - 1 && mb0 + kBKV <= p.T;
+        float e[32];
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) e[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -vec[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int m = m0 + c;
+            const bool valid = m >= r && m < p.T;
+            e[c] = valid ? fast_exp2(fmaf(__uint_as_float(sv[c]), c2, -vec[c])) : 0.0f;
+          }
+        }
+        // prodK of the previous block of this item reads the lo columns and
+        // writes O: fold it before P^T's lo part goes there.
+        if (i > 0 && !fold(out_k, gi - 1, acc_k)) {
+          ok = false;
+          break;
+        }
+        {
+          uint32_t hv[32], lv[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            hv[c] = __float_as_uint(tf32_hi(e[c]));
+            lv[c] = __float_as_uint(tf32_lo(e[c]));
+          }
+          tmem_st32(tmem + lane_off + kBS + 32 * wg, hv);
+          tmem_st32(tmem + lane_off + kBElo + 32 * wg, lv);
+          tmem_wait_st();
+          fence_before();
+          mbar_arrive(ew_p);
+        }
+        // dV product of this block, then dS^T = P^T o (dP^T - Delta).
+        if (!fold(out_v, gi, acc_v) || !mbar_wait(dp_full, gi & 1u, abort, &g_timeout)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        uint32_t dv[32];
+        tmem_ld32(tmem + lane_off + kBdP + 32 * wg, dv);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) e[c] = e[c] * (__uint_as_float(dv[c]) - vec[kBKV + c]);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sv[c] = __float_as_uint(tf32_hi(e[c]));
+          dv[c] = __float_as_uint(tf32_lo(e[c]));
+        }
+        tmem_st32(tmem + lane_off + kBdP + 32 * wg, sv);
+        tmem_st32(tmem + lane_off + kBElo + 32 * wg, dv);
+        tmem_wait_st();
+        fence_before();
+        mbar_arrive(ew_ds);
+      }
+      if (!ok) break;
+      g += (uint32_t)it.n_blk;
+      prev_w = w;
+      prev_last = g - 1u;
+    }
+    if (ok && prev_w >= 0) ok = finish(prev_w, prev_last);
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 // lo[r, c] = tf32 lo part of x[r, c] for a [rows, cols] matrix with row
 // stride ld, written compact (row stride cols).  cols and ld are multiples of 4.
 __global__ void split_lo_rows_k(const float* __restrict__ x, int64_t rows, int cols, int64_t ld,
@@ -1251,9 +1787,24 @@ ns_status launch_bwd_mode(const CUtensorMap* maps, const BwdParams& p, int B, in
 }
 
 template <int D>
+ns_status launch_bwd_kv(const CUtensorMap* m, const BwdParams& p, cudaStream_t s) {
+  using L = KvLayout<D>;
+  auto kern = attn_bwd_kv_kernel<D>;
+  NS_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynSmem),
+              "ns_attn_bwd attr");
+  cudaFuncAttributes fa;
+  NS_TRY_CUDA(cudaFuncGetAttributes(&fa, kern), "ns_attn_bwd attributes");
+  if (fa.numRegs < kMinLaunchRegs)
+    return fail(NS_ERR_UNSUPPORTED, "ns_attn_bwd: kernel compiled with too few registers for its split");
+  const int grid = std::min(p.n_items, sm_count());
+  kern<<<grid, kThreads, L::kDynSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], p);
+  return check_launch("ns_attn_bwd dK+dV tcgen05");
+}
+
+template <int D>
 ns_status launch_bwd(const float* qkv, const float* qkv_lo_in, const float* dout, const float* lse,
                      const float* delta, int B, int T, int H, float* dqkv, float* qkv_lo_ws,
-                     float* dout_lo, cudaStream_t s) {
+                     float* dout_lo, bool fused, cudaStream_t s) {
   const int C = H * D, rows = B * T;
   ns_status rc = NS_OK;
   if (!qkv_lo_in) rc = split_rows(qkv, rows, 3 * C, qkv_lo_ws, s);
@@ -1274,6 +1825,11 @@ ns_status launch_bwd(const float* qkv, const float* qkv_lo_in, const float* dout
   const float scale = 1.0f / sqrtf((float)D);
   const int nrb = (T + kBQ - 1) / kBQ;
   BwdParams p{qkv, dout, lse, delta, dqkv, T, H, C, scale, scale * kLog2e, 0, 0, 0, nrb * B * H, nrb};
+  if (fused) {  // dK and dV: Q and dO, each K-major and MN-major
+    const CUtensorMap m[8] = {qk, qlk, dk, dlk, dmn, dlmn, qmn, qlmn};
+    rc = launch_bwd_kv<D>(m, p, s);
+    if (rc != NS_OK) return rc;
+  } else {
   {  // dV: Q (K-major), dO (MN-major)
     const CUtensorMap m[6] = {qk, qlk, dmn, dlmn, dmn, dlmn};
     p.xb0 = 0; p.xb1 = 0; p.xb2 = 0;
@@ -1285,6 +1841,7 @@ ns_status launch_bwd(const float* qkv, const float* qkv_lo_in, const float* dout
     p.xb0 = 0; p.xb1 = 0; p.xb2 = 0;
     rc = launch_bwd_mode<kDK, D>(m, p, B, T, H, s);
     if (rc != NS_OK) return rc;
+  }
   }
   {  // dQ: K (K-major), V (K-major), K (MN-major)
     const CUtensorMap m[6] = {qk, qlk, qk, qlk, qmn, qlmn};
@@ -1329,12 +1886,14 @@ float* bwd_dout_lo(float* lo, int B, int T, int H, int D) {
 }
 
 ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const float* lse,
-              const float* delta, int B, int T, int H, int D, float* dqkv, float* lo,
+              const float* delta, int B, int T, int H, int D, float* dqkv, float* lo, bool fused,
               cudaStream_t s) {
   float* qkv_lo_ws = lo;
   float* dout_lo = lo + (size_t)B * T * 3 * H * D;
-  return D == 64 ? launch_bwd<64>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo, s)
-                 : launch_bwd<32>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo, s);
+  return D == 64 ? launch_bwd<64>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo,
+                                  fused, s)
+                 : launch_bwd<32>(qkv, qkv_lo, dout, lse, delta, B, T, H, dqkv, qkv_lo_ws, dout_lo,
+                                  fused, s);
 }
 
 // 1 if a kernel of this file raised the timeout flag since the last call

@@ -34,9 +34,9 @@ float* bwd_dout_lo(float* lo, int B, int T, int H, int D);
 // dqkv from qkv, dout, lse and delta (= rowsum(dout * out)); `lo` holds
 // bwd_lo_bytes, 16-byte aligned, with dout's lo part already at
 // bwd_dout_lo(lo).  qkv_lo (optional): the tf32 lo part of qkv, which is then
-// not split again.
+// not split again.  fused: dK and dV from one kernel (else one kernel each).
 ns_status bwd(const float* qkv, const float* qkv_lo, const float* dout, const float* lse,
-              const float* delta, int B, int T, int H, int D, float* dqkv, float* lo,
+              const float* delta, int B, int T, int H, int D, float* dqkv, float* lo, bool fused,
               cudaStream_t s);
 
 // 1 if an attention kernel hit a bounded-wait timeout since the last call (clears it).

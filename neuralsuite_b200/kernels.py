@@ -140,7 +140,9 @@ def attn_bwd_lo(qkv, qkv_lo, out, dout, lse, B, T, H, D):
 
 
 def attn_set_engine(engine):
-    """0: tensor-core attention where the head size has a kernel; 1: SIMT only."""
+    """0: tensor-core attention where the head size has a kernel (dK and dV
+    from one backward kernel); 1: SIMT only; 2: as 0 with dK and dV from two
+    kernels."""
     _lib.check(_lib.load().ns_attn_set_engine(engine))
 
 

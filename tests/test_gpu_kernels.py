@@ -353,6 +353,26 @@ def test_attention_core(cuda, attn_engine, B, T, H, D):
     assert np.allclose(dq, dq64, rtol=1e-4, atol=1e-5), np.abs(dq - dq64).max()
 
 
+@pytest.mark.parametrize("B,T,H,D", [(8, 1024, 12, 64), (2, 300, 3, 64), (3, 200, 2, 32),
+                                     (1, 1, 1, 64), (2, 129, 2, 32)])
+def test_attn_fused_dkdv_equals_separate_kernels_bitwise(cuda, B, T, H, D):
+    """The fused dK+dV backward kernel (engine 0) performs the separate dV and
+    dK kernels' operations in the same order (engine 2): same bits."""
+    r = rng(B * T * H + D)
+    C = H * D
+    qkv = dev(normal(r, (B * T, 3 * C)), cuda)
+    dout = dev(normal(r, (B * T, C)), cuda)
+    out, lse = nk.attn_fwd(qkv, B, T, H, D)
+    fused = host(nk.attn_bwd(qkv, out, dout, lse, B, T, H, D))
+    nk.attn_set_engine(2)
+    try:
+        separate = host(nk.attn_bwd(qkv, out, dout, lse, B, T, H, D))
+    finally:
+        nk.attn_set_engine(0)
+    assert np.array_equal(fused.view(np.uint32), separate.view(np.uint32))
+    nk.kernel_health()
+
+
 @pytest.mark.slow
 def test_attention_full_size_deterministic(cuda):
     """B=8, T=1024, H=12, D=64: float64 check on two (b, h) slices, and two
