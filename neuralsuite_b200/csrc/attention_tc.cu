@@ -1528,17 +1528,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) ok = op_s(g);
         if (ok) ok = op_dp(g);
         if (ok && n_blk == 1) release_a();
+        // The tensor core queues almost no MMAs, so every wait between two
+        // groups idles it: after each element-wise wait (the real dependency)
+        // the tile barriers, nearly always complete, are only tested, and the
+        // product and the next S (or dP) go out in one elected run.
+        auto batch = [&](uint32_t gi, bool dk, bool next) -> bool {
+          if (!warp_wait(dk ? ew_ds : ew_p, gi & 1u, abort, &g_timeout)) return false;
+          const int s2 = gi % R2, s0 = (gi + 1) % R0;
+          const uint32_t tfull = (dk ? full3 : full2) + 8u * s2;
+          const uint32_t nfull = (dk ? full1 : full0) + 8u * s0;
+          const bool r2 = mbar_test(tfull, (gi / R2) & 1u);
+          const bool r0 = next ? mbar_test(nfull, ((gi + 1) / R0) & 1u) : true;
+          const uint32_t bits = __shfl_sync(0xffffffffu, (r2 ? 1u : 0u) | (r0 ? 2u : 0u), 0);
+          if (bits != 3u) {  // a tile is late: the plain waits
+            if (!op_prod(gi, dk)) return false;
+            return !next || (dk ? op_dp(gi + 1) : op_s(gi + 1));
+          }
+          fence_after();
+          if (elect_one()) {
+            issue_prod(dk ? kBdP : kBS, sbase + (dk ? L::kRing3 : L::kRing2) + s2 * L::kSlot);
+            commit((dk ? empty3 : empty2) + 8u * s2);
+            commit(dk ? out_k : out_v);
+            if (next) {
+              if (dk) {
+                issue_k(tmem + kBdP, tmem + kBA2, sbase + L::kRing1 + s0 * L::kSlot);
+                commit(empty1 + 8u * s0);
+                commit(dp_full);
+              } else {
+                issue_k(tmem + kBS, tmem + kBA1, sbase + L::kRing0 + s0 * L::kSlot);
+                commit(empty0 + 8u * s0);
+                commit(s_full);
+              }
+            }
+          }
+          __syncwarp();
+          return true;
+        };
         for (int i = 0; ok && i < n_blk; ++i) {
           const uint32_t gi = g + (uint32_t)i;
-          // prodV_i (after P_i), then S_{i+1} over P_i's columns (in issue order).
-          ok = op_prod(gi, false);
-          if (ok && i + 1 < n_blk) ok = op_s(gi + 1);
+          const bool next = i + 1 < n_blk;
+          // prodV_i (after P_i), then S_{i+1} over P_i's columns (in issue order);
           // prodK_i (after dS_i), then dP_{i+1} over dS_i's columns.
-          if (ok) ok = op_prod(gi, true);
-          if (ok && i + 1 < n_blk) {
-            ok = op_dp(gi + 1);
-            if (ok && i + 2 == n_blk) release_a();  // the item's last S and dP are issued
-          }
+          ok = batch(gi, false, next);
+          if (ok) ok = batch(gi, true, next);
+          if (ok && next && i + 2 == n_blk) release_a();  // the item's last S and dP are issued
         }
         g += (uint32_t)n_blk;
       }
