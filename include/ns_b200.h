@@ -141,8 +141,11 @@ NS_API ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, in
  * computed inside the kernel (never pre-split into the workspace), 3 / 4 =
  * pre-split operands on CTA-pair tiles (256 x 256, 192 or 128) / 128 x 256 tiles only
  * (where the workspace allows), 5 = as 4 but storing rows of C instead of
- * computing C^T, 6 / 7 / 8 = CTA-pair tiles 256 x 192 / 256 x 128 / 256 x 256 only.  Used by tests and profiling to cross-check
- * the engines. */
+ * computing C^T, 6 / 7 / 8 = CTA-pair tiles 256 x 192 / 256 x 128 / 256 x 256 only.
+ * TEST AND PROFILING ONLY: engines 1-8 exist so tests can cross-check the
+ * kernels against one another and profiles can time one tile shape alone;
+ * production callers leave the engine at 0, the only setting the planner's
+ * shape choices are tuned for. */
 NS_API ns_status ns_gemm_set_engine(int engine);
 /* NS_ERR_TIMEOUT if any kernel of this library gave up a bounded wait on the
  * current device since the last call (the flag is cleared by the call);
