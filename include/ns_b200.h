@@ -83,9 +83,11 @@ NS_API int ns_device_supported(void);
  * only accepted with NS_EPI_STORE.  aux/aux_out rows use stride ldc.
  *
  * `workspace` (may be NULL) lets the kernel split K across CTAs when the
- * output has too few tiles to fill the GPU (the dW products); partial tiles
- * are summed in a fixed order, so results do not depend on timing.  With less
- * than ns_gemm_workspace_size bytes the call runs without splitting.
+ * output has too few tiles to fill the GPU (the dW products), or run a
+ * part-filled last wave of tiles as a stream-K tail (the leftover tiles'
+ * k-blocks shared evenly by all CTA pairs); partial tiles are summed in a
+ * fixed order, so results do not depend on timing.  With less than
+ * ns_gemm_workspace_size bytes the call runs without either.
  *
  * Accuracy: the tensor core adds into its fp32 accumulator with
  * round-toward-zero; each 64-term run of K is accumulated in a fresh TMEM
@@ -141,8 +143,10 @@ NS_API ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, in
  * computed inside the kernel (never pre-split into the workspace), 3 / 4 =
  * pre-split operands on CTA-pair tiles (256 x 256, 192 or 128) / 128 x 256 tiles only
  * (where the workspace allows), 5 = as 4 but storing rows of C instead of
- * computing C^T, 6 / 7 / 8 = CTA-pair tiles 256 x 192 / 256 x 128 / 256 x 256 only.
- * TEST AND PROFILING ONLY: engines 1-8 exist so tests can cross-check the
+ * computing C^T, 6 / 7 / 8 = CTA-pair tiles 256 x 192 / 256 x 128 / 256 x 256 only,
+ * 9 = as 0 but never running a part-filled last wave of CTA-pair tiles as a
+ * stream-K tail (the leftover tiles' k-blocks shared by all pairs).
+ * TEST AND PROFILING ONLY: engines 1-9 exist so tests can cross-check the
  * kernels against one another and profiles can time one tile shape alone;
  * production callers leave the engine at 0, the only setting the planner's
  * shape choices are tuned for. */

@@ -113,7 +113,7 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine >= 0 && engine <= 8, "ns_gemm_set_engine: engine must be 0..8");
+  NS_REQUIRE(engine >= 0 && engine <= 9, "ns_gemm_set_engine: engine must be 0..9");
   t_engine = engine;
   return NS_OK;
 }
@@ -171,19 +171,19 @@ ns_status gemm_impl(int M, int N, int K, const float* A, int lda, int a_trans, c
   size_t part = 0;
   float* lo = nullptr;
   bool chosen = false;
-  for (bool wide : {true, false}) {
+  const bool stream_k = t_engine != 9;
+  for (int attempt = 0; attempt < 3 && !chosen; ++attempt) {
+    // wide tiles with split-K / stream-K, wide tiles without, then 128 x 128 tiles
+    const bool wide = attempt < 2;
     if (!pre_ok) break;
     if (force >= 0 && !wide) break;
-    pl = tc::plan(M, N, K, ws_ok, wide, force, trans_mode);
+    pl = tc::plan(M, N, K, ws_ok && attempt != 1, wide, force, trans_mode, stream_k);
     part = (tc::split_workspace_bytes(pl, M, N) + 255) & ~(size_t)255;
     if (lo_bytes == 0 && part == 0) {
       chosen = true;
-      break;
-    }
-    if (ws_ok && part + lo_bytes <= workspace_bytes) {
+    } else if (ws_ok && part + lo_bytes <= workspace_bytes) {
       if (lo_bytes) lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
       chosen = true;
-      break;
     }
   }
   if (!chosen) {

@@ -25,11 +25,16 @@
 //               GELU-backward, fp32 stores.  Running sums are double buffered,
 //               so tile t+1 accumulates while tile t drains.
 // K can be split over CTAs for the small-output dW products; partial tiles go
-// to caller workspace and are summed in split order (deterministic).
+// to caller workspace and are summed in split order (deterministic).  On
+// CTA-pair tiles a shape whose tiles leave a part-filled last wave can run
+// that wave as a stream-K tail instead: the leftover tiles' k-blocks are cut
+// into one equal run per pair, partials go to the workspace, and the warp
+// that completes a tile sums its partials in k order (deterministic too).
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); a timeout raises a
 // device flag that ns_kernel_health() reports, and the CTA drains and exits.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "gemm_tc.cuh"
@@ -39,6 +44,15 @@ namespace nsb {
 namespace tc {
 
 __device__ int g_timeout;
+
+// Stream-K tail counters: kSkRegions regions of 16 counters (2 CTAs x 8 fold
+// warps) per tail tile.  Launches take the regions in turn, so up to
+// kSkRegions stream-K GEMMs may be in flight at once (on any streams) without
+// sharing counters; each counter returns to 0 when its tile completes.
+constexpr int kMaxTailTiles = 128;
+constexpr int kSkRegionCounters = 16 * kMaxTailTiles;
+constexpr int kSkRegions = 16;
+__device__ unsigned g_sk_count[kSkRegions * kSkRegionCounters];
 
 namespace {
 
@@ -64,6 +78,18 @@ struct KParams {
   // tile are columns of C); the epilogue stores tile element (r, c) to C[c][r].
   int trans_out;
   int out_m, out_n;  // C's shape
+  // Stream-K tail (CTA-pair kernel only).  The first dp_units units (tiles x
+  // splits) run whole, one cluster each in turn; the k-blocks of the last
+  // sk_tiles tiles (splits == 1) are cut into sk_slots equal runs, one per
+  // cluster.  Each run leaves its partial tile in sk_ws
+  // ([cluster][run 0/1][cta 0/1][column][row], 128 x BN floats per CTA);
+  // per tile, CTA half and fold warp, a counter in sk_count records the
+  // partials in, and the warp that completes the set adds them in k order
+  // and runs the epilogue.  No CTA waits on another.
+  int dp_units;
+  int sk_tiles, sk_slots;
+  float* sk_ws;
+  unsigned* sk_count;
 };
 
 // Descriptor of MMA k-step kk (8 tf32) of an operand tile at `base`.
@@ -86,6 +112,57 @@ __device__ __forceinline__ void decode_unit(const KParams& p, int u, int& tm, in
   kb0 = split * p.kb_per;
   kb1 = min(p.kb_total, kb0 + p.kb_per);
 }
+
+// First k-block (counted over the tail's tiles, kb_total per tile) of the
+// stream-K run of cluster `slot`; runs are non-empty (sk_tiles * kb_total >=
+// sk_slots) and at most kb_total long (sk_tiles <= sk_slots), so a run covers
+// parts of at most two tiles.
+// The planner keeps sk_tiles * kb_total * (sk_slots + 1) below 2^31, so
+// 32-bit arithmetic is exact here.
+__device__ __forceinline__ int tail_begin(const KParams& p, int slot) {
+  return (int)((unsigned)(slot * p.sk_tiles * p.kb_total) / (unsigned)p.sk_slots);
+}
+// The cluster whose run holds tail k-block i: the largest s with tail_begin(s) <= i.
+__device__ __forceinline__ int tail_slot(const KParams& p, int i) {
+  return (int)((unsigned)((i + 1) * p.sk_slots - 1) / (unsigned)(p.sk_tiles * p.kb_total));
+}
+
+// The sequence of work one cluster of the pair kernel takes: its
+// data-parallel units, then its stream-K run (one or two pieces).  Producer,
+// MMA issuer and fold warps walk the same sequence.
+struct PairWork {
+  int u, a, b;  // next data-parallel unit; remaining tail k-blocks [a, b)
+  int tm, tn, split, kb0, kb1;
+  int tail;  // tile index within the tail, or -1 for a data-parallel unit
+  int run;   // 0 / 1: first or second piece of this cluster's run
+  __device__ __forceinline__ PairWork(const KParams& p, int cluster)
+      : u(cluster), a(0), b(0), tm(0), tn(0), split(0), kb0(0), kb1(0), tail(-1), run(-1) {
+    if (p.sk_tiles > 0) {
+      a = tail_begin(p, cluster);
+      b = tail_begin(p, cluster + 1);
+    }
+  }
+  __device__ __forceinline__ bool next(const KParams& p, int step) {
+    if (u < p.dp_units) {
+      decode_unit(p, u, tm, tn, split, kb0, kb1);
+      tail = -1;
+      u += step;
+      return true;
+    }
+    if (a >= b) return false;
+    const int t = a / p.kb_total;
+    kb0 = a - t * p.kb_total;
+    kb1 = min(p.kb_total, kb0 + (b - a));
+    const int tile = p.dp_units + t;  // stream-K plans have splits == 1
+    tm = tile / p.tiles_n;
+    tn = tile - tm * p.tiles_n;
+    split = 0;
+    tail = t;
+    ++run;
+    a += kb1 - kb0;
+    return true;
+  }
+};
 
 // Accumulation chunk: the tensor core adds into its fp32 accumulator with
 // round-toward-zero, a bias that grows linearly with K (relative error ~1e-5
@@ -914,6 +991,49 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
       : "memory");
 }
 
+// A stream-K piece of tail tile w.tail has been accumulated in acc (this fold
+// warp's slice: 32 rows x HB columns of this CTA's half).  The slice goes to
+// the cluster's partial buffer and is counted in; the warp whose partial
+// completes the slice's set (one per cluster whose run covers the tile) adds
+// the partials in k order (cluster order) into acc and returns true, to run
+// the epilogue; the others return false.  The sum's order does not depend on
+// which warp finishes, so the result is deterministic.
+template <int HB>
+__device__ __forceinline__ bool tail_settle(const KParams& p, const PairWork& w, int cluster,
+                                            uint32_t rank, int fold_warp, int row, int col0,
+                                            float (&acc)[HB]) {
+  constexpr size_t kPart = (size_t)kBM * 2 * HB;  // floats of one CTA's partial tile
+  const size_t offs = (size_t)col0 * kBM + row;
+  float* mine = p.sk_ws + ((size_t)(cluster * 2 + w.run) * 2 + rank) * kPart + offs;
+#pragma unroll
+  for (int j = 0; j < HB; ++j) __stcg(mine + (size_t)j * kBM, acc[j]);
+  const int kbt = p.kb_total;
+  const int s0 = tail_slot(p, w.tail * kbt), s1 = tail_slot(p, w.tail * kbt + kbt - 1);
+  __syncwarp();
+  unsigned last = 0;
+  if ((threadIdx.x & 31) == 0) {
+    __threadfence();  // the warp's partial before its count (release)
+    unsigned* cnt = p.sk_count + ((size_t)w.tail * 2 + rank) * 8 + fold_warp;
+    // atomicInc wraps to 0 after s1 - s0: the counter is clean for the next launch.
+    last = atomicInc(cnt, (unsigned)(s1 - s0)) == (unsigned)(s1 - s0) ? 1u : 0u;
+    __threadfence();  // the other partials after the count (acquire)
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return false;
+  for (int s = s0; s <= s1; ++s) {
+    const int run = tail_begin(p, s) / kbt == w.tail ? 0 : 1;
+    const float* src = p.sk_ws + ((size_t)(s * 2 + run) * 2 + rank) * kPart + offs;
+    if (s == s0) {
+#pragma unroll
+      for (int j = 0; j < HB; ++j) acc[j] = __ldcg(src + (size_t)j * kBM);
+    } else {
+#pragma unroll
+      for (int j = 0; j < HB; ++j) acc[j] = __fadd_rn(acc[j], __ldcg(src + (size_t)j * kBM));
+    }
+  }
+  return true;
+}
+
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -966,7 +1086,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
   cluster_sync();  // both CTAs' barriers initialised before any remote arrive
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int n_units = p.tiles_m * p.tiles_n * p.splits;
   const int unit0 = (int)cluster_id_x(), unit_step = (int)cluster_count_x();
 
   if (warp < 4) {
@@ -974,16 +1093,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     if (warp == 0) {
       // ---------------------------------------------------------- producer (both CTAs)
       if (lane == 0) {
-        uint32_t it = 0;
-        int issued[S];
-        uint32_t issued_ph[S];
-        for (int s = 0; s < S; ++s) issued[s] = 0, issued_ph[s] = 0;
+        uint32_t it = 0;  // stage fills issued (an abort breaks before its own fill)
         bool ok = true;
-        for (int u = unit0; ok && u < n_units; u += unit_step) {
-          int tm, tn, split, kb0, kb1;
-          decode_unit(p, u, tm, tn, split, kb0, kb1);
-          const int m0 = tm * 256 + (int)rank * kBM, n0 = tn * BN + (int)rank * HB;
-          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        PairWork w(p, unit0);
+        while (ok && w.next(p, unit_step)) {
+          const int m0 = w.tm * 256 + (int)rank * kBM, n0 = w.tn * BN + (int)rank * HB;
+          for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
             const int s = it % S;
             const uint32_t ph = (it / S) & 1u;
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort, &g_timeout)) {
@@ -996,8 +1111,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
               mbar_expect_tx(full_bar(s), 2 * L::kRaw);
               mbar_expect_tx(lofull_bar(s), 2 * L::kRaw);
             }
-            issued[s] = 1;
-            issued_ph[s] = ph;
             const uint32_t a_dst = sbase + s * L::kStage;
             const uint32_t b_dst = a_dst + L::kA;
             const int k0 = kb * kBK;
@@ -1026,11 +1139,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         }
         if (!ok) {
           if (rank == 0) {
-            for (int s = 0; s < S; ++s)
-              if (issued[s]) {
-                mbar_wait_drain(full_bar(s), issued_ph[s], &g_timeout);
-                mbar_wait_drain(lofull_bar(s), issued_ph[s], &g_timeout);
-              }
+            for (uint32_t s = 0; s < (uint32_t)S && s < it; ++s) {
+              // the last fill of stage s and its phase
+              const uint32_t j = it - 1 - ((it - 1 - s) % S);
+              mbar_wait_drain(full_bar(s), (j / S) & 1u, &g_timeout);
+              mbar_wait_drain(lofull_bar(s), (j / S) & 1u, &g_timeout);
+            }
           } else {
             // This CTA's copies complete on the other CTA's barriers: give
             // any in flight time to land (bounded) before the CTA can exit.
@@ -1047,9 +1161,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                              ((uint32_t)(256 >> 4) << 24);
       uint32_t it = 0, cit = 0;
       bool ok = true;
-      for (int u = unit0; ok && u < n_units; u += unit_step) {
-        int tm, tn, split, kb0, kb1;
-        decode_unit(p, u, tm, tn, split, kb0, kb1);
+      PairWork w(p, unit0);
+      while (ok && w.next(p, unit_step)) {
+        const int kb0 = w.kb0, kb1 = w.kb1;
         for (int c0 = kb0; ok && c0 < kb1; c0 += p.chunk, ++cit) {
           const int cb = cit & 1;
           if (!warp_wait(che_bar(cb), ((cit >> 1) & 1u) ^ 1u, abort, &g_timeout)) {
@@ -1115,9 +1229,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     uint32_t cit = 0;
     bool ok = true;
     float acc[HB];
-    for (int u = unit0; ok && u < n_units; u += unit_step) {
-      int tm, tn, split, kb0, kb1;
-      decode_unit(p, u, tm, tn, split, kb0, kb1);
+    PairWork w(p, unit0);
+    while (ok && w.next(p, unit_step)) {
+      const int tm = w.tm, tn = w.tn, split = w.split, kb0 = w.kb0, kb1 = w.kb1;
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
       for (int c0 = kb0; c0 < kb1; c0 += p.chunk, ++cit) {
@@ -1151,6 +1265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         }
       }
       if (!ok) break;
+      if (w.tail >= 0 && !tail_settle<HB>(p, w, unit0, rank, warp - 4, ew * 32 + lane, col0, acc)) continue;
       const int m = tm * 256 + (int)rank * kBM + ew * 32 + lane;
       const int n_base = tn * BN + col0;
       if (p.trans_out) {
@@ -1265,6 +1380,22 @@ ns_status launch_wide(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& 
   return check_launch("ns_gemm tcgen05 wide");
 }
 
+// Device address of this device's stream-K counters (looked up once per device).
+ns_status sk_counters(unsigned** out) {
+  static std::atomic<unsigned*> cache[64];
+  int dev = 0;
+  NS_TRY_CUDA(cudaGetDevice(&dev), "ns_gemm device");
+  unsigned* p = dev < 64 ? cache[dev].load(std::memory_order_relaxed) : nullptr;
+  if (!p) {
+    void* addr = nullptr;
+    NS_TRY_CUDA(cudaGetSymbolAddress(&addr, g_sk_count), "ns_gemm stream-K counters");
+    p = static_cast<unsigned*>(addr);
+    if (dev < 64) cache[dev].store(p, std::memory_order_relaxed);
+  }
+  *out = p;
+  return NS_OK;
+}
+
 ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {
   const int64_t total = (int64_t)rows * cols;
   const int vec = ((cols & 3) == 0 && (ld & 3) == 0 &&
@@ -1277,7 +1408,8 @@ ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaSt
 
 }  // namespace
 
-Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind, int trans_mode) {
+Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind, int trans_mode,
+          bool allow_stream_k) {
   const int sms = sm_count();
   const int kb_total = std::max(1, ceil_div(K, kBK));
   Plan best{};
@@ -1325,6 +1457,42 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
         best.kb_total = kb_total;
         best.kb_per = kb_per;
         best.grid = std::min(units, slots);
+        best.sk_tiles = 0;
+      }
+      // Stream-K tail (pair tiles): the whole waves run as they are and the
+      // r leftover tiles' k-blocks are shared by all pairs, instead of a
+      // last wave that keeps only r of them busy.  Each pair's run (under
+      // one tile of k-blocks, so parts of at most two tiles) costs per piece
+      // a partial tile out (store, fence, count: measured ~3 us, longer than
+      // the two chunks the MMA can run ahead) and, for the pair that
+      // completes a tile, the tile's partials back in at the end of the
+      // kernel.  Measured on B200: a clear gain after at least one whole
+      // wave when the tail is long (K >= 2304); a loss with no whole wave
+      // (a separate split-K reduce over all SMs is faster than one finishing
+      // warp per slice reading many partials), so that case is excluded.
+      const int r = tiles % slots;
+      if (fk == 2 && sp == 1 && allow_split && allow_stream_k && r > 0 && r <= kMaxTailTiles &&
+          tiles >= slots &&
+          (long long)r * kb_total >= 2LL * slots &&
+          (long long)r * kb_total * (slots + 1) < (1LL << 31)) {
+        const int full = tiles / slots;
+        const int run = ceil_div(r * kb_total, slots);
+        const double fixup = (3.0 + (double)slots / r) * 4.0 * bn;
+        const double sk_cost = full * (kb_total * kb_cycles + 3000.0) + run * kb_cycles + 15000.0 + fixup;
+        if (sk_cost < best_cost * 0.98) {
+          best_cost = sk_cost;
+          best.bn = bn;
+          best.pair = 1;
+          best.trans = tr ? 1 : 0;
+          best.stages = 0;
+          best.tiles_m = tiles_m;
+          best.tiles_n = tiles_n;
+          best.splits = 1;
+          best.kb_total = kb_total;
+          best.kb_per = kb_total;
+          best.grid = slots;
+          best.sk_tiles = r;
+        }
       }
     }
   }
@@ -1332,6 +1500,8 @@ Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind
 }
 
 size_t split_workspace_bytes(const Plan& p, int M, int N) {
+  if (p.sk_tiles > 0)  // [pair][run 0/1][cta 0/1][128 x bn] partial tiles
+    return (size_t)p.grid * 4 * kBM * p.bn * sizeof(float);
   return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
 }
 
@@ -1406,6 +1576,21 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   kp.trans_out = pl.trans;
   kp.out_m = out_m;
   kp.out_n = out_n;
+  kp.dp_units = pl.tiles_m * pl.tiles_n * pl.splits - pl.sk_tiles;
+  kp.sk_tiles = pl.sk_tiles;
+  kp.sk_slots = pl.grid;
+  kp.sk_ws = pl.sk_tiles > 0 ? ws : nullptr;
+  kp.sk_count = nullptr;
+  if (pl.sk_tiles > 0) {
+    if (!pl.pair || pl.splits != 1 || pl.sk_tiles > kMaxTailTiles || !ws)
+      return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: inconsistent stream-K plan");
+    unsigned* base = nullptr;
+    rc = sk_counters(&base);
+    if (rc != NS_OK) return rc;
+    static std::atomic<unsigned> next_region{0};
+    kp.sk_count = base + (size_t)(next_region.fetch_add(1, std::memory_order_relaxed) % kSkRegions) *
+                             kSkRegionCounters;
+  }
   // Transposed single-pass plans store the raw product and apply epilogues
   // that read aux in a separate coalesced pass.
   const bool late_epi = pl.trans && pl.splits == 1 &&
@@ -1487,6 +1672,12 @@ int consume_timeout_flag() {
   if (v) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) return -(int)e;
+    // A kernel that gave up may have left stream-K counters part-way.
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_sk_count);
+    if (e == cudaSuccess) e = cudaMemset(addr, 0, sizeof(unsigned) * kSkRegions * kSkRegionCounters);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return -(int)e;
   }
   return v ? 1 : 0;

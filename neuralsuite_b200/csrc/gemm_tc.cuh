@@ -21,7 +21,10 @@ struct Plan {
   int splits;      // K splits (>= 1), every split non-empty
   int kb_total;    // ceil(K / kBK)
   int kb_per;      // k-blocks per split
-  int grid;        // persistent CTAs
+  int grid;        // persistent CTAs (CTA pairs for pair tiles)
+  // CTA-pair plans with splits == 1 only: the last sk_tiles tiles run as a
+  // stream-K tail, their k-blocks shared evenly by all `grid` pairs (0: none).
+  int sk_tiles;
 };
 
 // allow_wide: 128 x 256 tiles may be chosen (they need pre-split operands).
@@ -30,8 +33,9 @@ struct Plan {
 // 256 x 192 / 256 x 128 only, 5 = pair tiles 256 x 256 only (tests and profiling).
 // trans_mode for the wide kernels: 1 = compute C^T (coalesced column stores),
 // 0 = compute C (row stores).
+// allow_split also allows the stream-K tail unless allow_stream_k is false.
 Plan plan(int M, int N, int K, bool allow_split, bool allow_wide, int force_kind = -1,
-          int trans_mode = 1);
+          int trans_mode = 1, bool allow_stream_k = true);
 size_t split_workspace_bytes(const Plan& p, int M, int N);
 
 size_t lo_elems_a(int M, int K);

@@ -35,7 +35,10 @@ def _ws(nbytes, device):
 def set_gemm_engine(engine: int) -> None:
     """0 = automatic (tcgen05 where TMA allows), 1 = SIMT fp32 everywhere,
     2 = tcgen05 with the operand split done inside the kernel, 3 / 4 = only
-    256 x 256 CTA-pair / 128 x 256 tiles (pre-split operands)."""
+    256 x 256 CTA-pair / 128 x 256 tiles (pre-split operands), 5 = as 4 with
+    row stores, 6 / 7 / 8 = pair tiles 256 x 192 / 256 x 128 / 256 x 256 only,
+    9 = automatic without the stream-K tail.  Engines 1-9 are for tests and
+    profiling."""
     _lib.check(_lib.load().ns_gemm_set_engine(engine))
 
 
