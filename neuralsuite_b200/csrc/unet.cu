@@ -13,7 +13,9 @@
 // with a 3x3 Conv2D inside), LN normalises the last axis (LayerNormLayer,
 // include/layers/layernorm.h), Up is nearest-neighbour 2x (not in the
 // reference), MSE is MSELoss (include/losses.h:97-124).  Convolutions run
-// through ns_conv2d_fwd/bwd (im2col columns + tcgen05 3xTF32 GEMMs); the
+// as ns_conv2d_fwd/bwd do (im2col columns + tcgen05 3xTF32 GEMMs), each
+// keeping its forward's columns for its backward (one column buffer per
+// convolution, 4.6 GB at 32 images of 64 x 64, base 64); the
 // element-wise steps are fused passes: residual add + ReLU, ReLU mask +
 // skip add in the backward, upsample and its 2x2 sum, MSE with a two-stage
 // ordered loss sum.  Parameters and gradients are flat buffers in
@@ -25,6 +27,7 @@
 
 #include "comm.h"
 #include "common.cuh"
+#include "conv.h"
 
 struct ns_unet {
   int in_ch = 3, base = 64, S = 64, max_batch = 1, B = 0;
@@ -33,6 +36,7 @@ struct ns_unet {
   struct Conv {
     int ic, oc, stride, in_hw;
     int64_t w_off, b_off;
+    float *cols = nullptr, *cols_lo = nullptr;  // the forward's columns, kept for the backward
   };
   std::vector<Conv> conv;
   int64_t ln_off[5][2];  // gamma, beta of LN0..LN4
@@ -158,16 +162,19 @@ ns_status dev_alloc(ns_unet* u, T** p, size_t count) {
 
 ns_status conv_fwd(ns_unet* u, int i, const float* in, float* out, int B, cudaStream_t s) {
   const auto& c = u->conv[i];
-  return ns_conv2d_fwd(in, B, c.ic, c.in_hw, c.in_hw, u->params + c.w_off, u->params + c.b_off, c.oc,
-                       3, c.stride, 1, out, u->conv_ws, u->conv_ws_bytes, s);
+  return conv::forward_keep(in, B, c.ic, c.in_hw, c.in_hw, u->params + c.w_off,
+                            u->params + c.b_off, c.oc, 3, c.stride, 1, out, c.cols, c.cols_lo,
+                            u->conv_ws, u->conv_ws_bytes, s);
 }
 
-ns_status conv_bwd(ns_unet* u, int i, const float* in, const float* dy, float* dx, int B,
-                   cudaStream_t s) {
+// The backward of conv i on the columns its forward kept (its input is not
+// read again).
+ns_status conv_bwd(ns_unet* u, int i, const float* dy, float* dx, int B, cudaStream_t s) {
   const auto& c = u->conv[i];
-  return ns_conv2d_bwd(in, dy, B, c.ic, c.in_hw, c.in_hw, u->params + c.w_off, c.oc, 3, c.stride,
-                       1, dx, u->grads + c.w_off, u->grads + c.b_off, u->conv_ws, u->conv_ws_bytes,
-                       s);
+  return conv::backward_from_cols(c.cols, c.cols_lo, dy, B, c.ic, c.in_hw, c.in_hw,
+                                  u->params + c.w_off, c.oc, 3, c.stride, 1, dx,
+                                  u->grads + c.w_off, u->grads + c.b_off, u->conv_ws,
+                                  u->conv_ws_bytes, s);
 }
 
 int64_t level_numel(const ns_unet* u, int l, int B) {
@@ -200,7 +207,7 @@ ns_status res_ln_bwd(ns_unet* u, int l, const float* de, float* da, int B, cudaS
   relu_mask_k<<<grid_for(n), 256, 0, s>>>(u->t1, u->r[l], n, u->t1);
   rc = check_launch("ns_unet relu backward");
   if (rc != NS_OK) return rc;
-  rc = conv_bwd(u, 6 + l, u->a[l], u->t1, u->t2, B, s);
+  rc = conv_bwd(u, 6 + l, u->t1, u->t2, B, s);
   if (rc != NS_OK) return rc;
   return ns_add(u->t2, u->t1, da, n, s);  // dinput = dfx + dsum (residual.h:50-55)
 }
@@ -264,8 +271,8 @@ ns_status ns_unet_create(const ns_unet_config* cfg, ns_unet** out) {
   const size_t Bm = (size_t)u->max_batch;
   size_t ws = 0;
   for (const auto& cv : u->conv)
-    ws = std::max(ws, ns_conv2d_workspace_size((int)Bm, cv.ic, cv.in_hw, cv.in_hw, cv.oc, 3,
-                                               cv.stride, 1));
+    ws = std::max(ws, conv::keep_workspace_size((int)Bm, cv.ic, cv.in_hw, cv.in_hw, cv.oc, 3,
+                                                cv.stride, 1));
   u->conv_ws_bytes = ws;
   size_t lnws = 0;
   for (int l = 0; l < 5; ++l)
@@ -301,6 +308,11 @@ ns_status ns_unet_create(const ns_unet_config* cfg, ns_unet** out) {
   A(&u->g1, Bm * 2 * b * (S / 2) * (S / 2));
   A(&u->small, 64);
   A(&u->loss_part, kMseBlocks);
+  for (auto& cv : u->conv) {
+    const int64_t n = conv::cols_floats((int)Bm, cv.ic, cv.in_hw, cv.in_hw, cv.oc, 3, cv.stride, 1);
+    A(&cv.cols, (size_t)n);
+    A(&cv.cols_lo, (size_t)n);
+  }
   if (rc == NS_OK) {
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, ws);
@@ -398,27 +410,27 @@ ns_status ns_unet_backward(ns_unet* u, void* stream) {
   // The skip sums' gradients live in g0 / g1 until the encoder side adds
   // them; the other gradients reuse the e[] slots of values the backward has
   // already consumed (u0 after conv_out, u1 and m after their upsamples).
-  ns_status rc = conv_bwd(u, 5, u->e[4], u->dout, u->t0, B, s);                  // conv_out
+  ns_status rc = conv_bwd(u, 5, u->dout, u->t0, B, s);                           // conv_out
   if (rc == NS_OK) rc = res_ln_bwd(u, 4, u->t0, u->g0, B, s);                    // ds0
-  if (rc == NS_OK) rc = conv_bwd(u, 4, u->up_b, u->g0, u->t0, B, s);             // up0
+  if (rc == NS_OK) rc = conv_bwd(u, 4, u->g0, u->t0, B, s);                      // up0
   if (rc != NS_OK) return rc;
   up2_bwd_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->t0, (int64_t)B * 2 * b, S / 2,
                                                            S / 2, u->e[3]);     // du1
   rc = check_launch("ns_unet upsample backward");
   if (rc == NS_OK) rc = res_ln_bwd(u, 3, u->e[3], u->g1, B, s);                  // ds1
-  if (rc == NS_OK) rc = conv_bwd(u, 3, u->up_a, u->g1, u->t0, B, s);             // up1
+  if (rc == NS_OK) rc = conv_bwd(u, 3, u->g1, u->t0, B, s);                      // up1
   if (rc != NS_OK) return rc;
   up2_bwd_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->t0, (int64_t)B * 4 * b, S / 4,
                                                            S / 4, u->e[2]);     // dm
   rc = check_launch("ns_unet upsample backward");
   if (rc == NS_OK) rc = res_ln_bwd(u, 2, u->e[2], u->t0, B, s);                  // d a2
-  if (rc == NS_OK) rc = conv_bwd(u, 2, u->e[1], u->t0, u->t1, B, s);             // down2
+  if (rc == NS_OK) rc = conv_bwd(u, 2, u->t0, u->t1, B, s);                      // down2
   if (rc == NS_OK) rc = ns_add(u->t1, u->g1, u->e[3], level_numel(u, 1, B), s);    // de1
   if (rc == NS_OK) rc = res_ln_bwd(u, 1, u->e[3], u->t0, B, s);                  // d a1
-  if (rc == NS_OK) rc = conv_bwd(u, 1, u->e[0], u->t0, u->t1, B, s);             // down1
+  if (rc == NS_OK) rc = conv_bwd(u, 1, u->t0, u->t1, B, s);                      // down1
   if (rc == NS_OK) rc = ns_add(u->t1, u->g0, u->e[4], level_numel(u, 0, B), s);    // de0
   if (rc == NS_OK) rc = res_ln_bwd(u, 0, u->e[4], u->t0, B, s);                  // d a0
-  if (rc == NS_OK) rc = conv_bwd(u, 0, u->x, u->t0, nullptr, B, s);              // conv_in
+  if (rc == NS_OK) rc = conv_bwd(u, 0, u->t0, nullptr, B, s);                    // conv_in
   if (rc != NS_OK || !u->comm || u->world == 1) return rc;
   rc = comm::allreduce(u->comm, u->grads, u->n_params, s);
   if (rc == NS_OK) rc = comm::allreduce(u->comm, u->small, 1, s);
