@@ -420,6 +420,24 @@ def run_ours(args, rank, world, local):
     value = tokens_per_step / (ms / 1e3)
     e2e_value = tokens_per_step / (ms_e2e / 1e3)
 
+    # -- where the data-parallel step loses time to communication (untimed
+    # extra steps, each read back): the compute stream's wait for the
+    # gradient all-reduces after its backward, and their span
+    comm_info = None
+    if world > 1:
+        model.set_comm_timing(True)
+        exposed, span = [], []
+        for i in range(5):
+            model.train_step(dev_tok[i % n_batches], dev_tgt[i % n_batches], read_loss=False)
+            x, y = model.comm_times()
+            exposed.append(x)
+            span.append(y)
+        model.set_comm_timing(False)
+        comm_info = {"exposed_ms": max_over_ranks(statistics.median(exposed)),
+                     "allreduce_span_ms": max_over_ranks(statistics.median(span)),
+                     "how": "median of 5 extra steps, max over ranks; exposed = the compute "
+                            "stream's wait for the all-reduces after its own backward"}
+
     dp = dp_checks(torch, dist, model, cfg, rank, world, n_batches) if world > 1 else None
 
     out = None
@@ -468,6 +486,8 @@ def run_ours(args, rank, world, local):
                                           "inside every call", "shapes": per_ws},
             },
         }
+        if comm_info is not None:
+            out["comm"] = comm_info
         if dp is not None:
             out["dp_check"] = dp
             out["replicas_identical"] = dp["replicas_identical"]

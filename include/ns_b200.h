@@ -583,6 +583,17 @@ NS_API ns_status ns_gpt_decoder_prefill(ns_gpt_decoder* dec, const int32_t* toke
 /* Data parallel: attach a communicator (NULL detaches).  bucket_floats caps a
  * gradient bucket (0 = one bucket per GPTBlock). */
 NS_API ns_status ns_gpt_set_comm(ns_gpt* model, ns_comm* comm, int world_size, int64_t bucket_floats);
+/* Data-parallel diagnostics (no reference counterpart).  With timing on, each
+ * backward records three events: on the comm stream when the first bucket's
+ * all-reduce may start and when the last (the loss sum) has finished, and on
+ * the compute stream when its own backward work has been issued up to the
+ * join.  ns_gpt_comm_times waits for the last backward's events and reports
+ * exposed_ms, how long the compute stream waited for the all-reduces after
+ * its backward (0 when they had finished), and span_ms, the time from the
+ * first bucket's start to the last one's end.  Timing needs an attached
+ * communicator with world_size > 1. */
+NS_API ns_status ns_gpt_set_comm_timing(ns_gpt* model, int enable);
+NS_API ns_status ns_gpt_comm_times(ns_gpt* model, float* exposed_ms, float* span_ms);
 /* Gradient-bucket plan of the attached world (host-only; usable without a
  * GPU): writes up to max_buckets [begin, end) float ranges in launch order. */
 NS_API int ns_gpt_plan_buckets(const ns_gpt_config* cfg, int64_t bucket_floats, int64_t* begin,

@@ -58,6 +58,11 @@ void release_comm_resources(ns_gpt* h) {
   h->group_ready.clear();
   if (h->comm_done) cudaEventDestroy(h->comm_done);
   h->comm_done = nullptr;
+  for (cudaEvent_t* e : {&h->t_bwd_end, &h->t_comm_begin, &h->t_comm_end}) {
+    if (*e) cudaEventDestroy(*e);
+    *e = nullptr;
+  }
+  h->comm_timed = false;
   if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
   h->comm_stream = nullptr;
 }
@@ -70,11 +75,16 @@ ns_status backward_impl(ns_gpt* h, cudaStream_t s) {
     return NS_OK;
   }
   ns_status rc = NS_OK;
+  const bool timing = h->comm_timing && h->t_bwd_end;
   m.Backward([&](int g) {
     if (rc != NS_OK) return;
     cudaEvent_t ev = h->group_ready[g];
     if (cudaEventRecord(ev, s) != cudaSuccess || cudaStreamWaitEvent(h->comm_stream, ev, 0) != cudaSuccess) {
       rc = nsb::fail(NS_ERR_CUDA, "bucket event");
+      return;
+    }
+    if (timing && g == 0 && cudaEventRecord(h->t_comm_begin, h->comm_stream) != cudaSuccess) {
+      rc = nsb::fail(NS_ERR_CUDA, "timing event");
       return;
     }
     for (const Bucket& b : h->buckets) {
@@ -88,6 +98,11 @@ ns_status backward_impl(ns_gpt* h, cudaStream_t s) {
   rc = nsb::comm::allreduce(h->comm, m.Small(), 1, h->comm_stream);
   if (rc != NS_OK) return rc;
   NS_TRY_CUDA(cudaEventRecord(h->comm_done, h->comm_stream), "comm join");
+  if (timing) {
+    NS_TRY_CUDA(cudaEventRecord(h->t_comm_end, h->comm_stream), "timing event");
+    NS_TRY_CUDA(cudaEventRecord(h->t_bwd_end, s), "timing event");
+    h->comm_timed = true;
+  }
   NS_TRY_CUDA(cudaStreamWaitEvent(s, h->comm_done, 0), "comm join");
   return NS_OK;
 }
@@ -451,6 +466,32 @@ ns_status ns_gpt_set_comm(ns_gpt* h, ns_comm* comm, int world_size, int64_t buck
     h->group_ready.push_back(e);
   }
   NS_TRY_CUDA(cudaEventCreateWithFlags(&h->comm_done, cudaEventDisableTiming), "event");
+  return NS_OK;
+}
+
+ns_status ns_gpt_set_comm_timing(ns_gpt* h, int enable) {
+  NS_REQUIRE(h, "ns_gpt_set_comm_timing: NULL model");
+  NS_REQUIRE(h->comm && h->world > 1, "ns_gpt_set_comm_timing: no communicator attached");
+  h->comm_timing = enable != 0;
+  h->comm_timed = false;
+  for (cudaEvent_t* e : {&h->t_bwd_end, &h->t_comm_begin, &h->t_comm_end})
+    if (!*e) NS_TRY_CUDA(cudaEventCreate(e), "ns_gpt_set_comm_timing");
+  return NS_OK;
+}
+
+ns_status ns_gpt_comm_times(ns_gpt* h, float* exposed_ms, float* span_ms) {
+  NS_REQUIRE(h, "ns_gpt_comm_times: NULL model");
+  NS_REQUIRE(exposed_ms && span_ms, "ns_gpt_comm_times: NULL argument");
+  NS_REQUIRE(h->comm_timed, "ns_gpt_comm_times: no timed backward since timing was enabled");
+  NS_TRY_CUDA(cudaEventSynchronize(h->t_comm_end), "ns_gpt_comm_times");
+  NS_TRY_CUDA(cudaEventSynchronize(h->t_bwd_end), "ns_gpt_comm_times");
+  float exposed = 0.0f, span = 0.0f;
+  // Negative when the compute stream reached its join after the last
+  // all-reduce had finished: nothing was exposed.
+  NS_TRY_CUDA(cudaEventElapsedTime(&exposed, h->t_bwd_end, h->t_comm_end), "ns_gpt_comm_times");
+  NS_TRY_CUDA(cudaEventElapsedTime(&span, h->t_comm_begin, h->t_comm_end), "ns_gpt_comm_times");
+  *exposed_ms = exposed > 0.0f ? exposed : 0.0f;
+  *span_ms = span;
   return NS_OK;
 }
 

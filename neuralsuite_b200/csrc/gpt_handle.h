@@ -18,6 +18,11 @@ struct ns_gpt {
   std::vector<cudaEvent_t> group_ready;
   cudaEvent_t comm_done = nullptr;
   cudaEvent_t step_done = nullptr;
+  // Communication timing (ns_gpt_set_comm_timing): the compute stream's end
+  // of backward, the comm stream's start of the first bucket and its end.
+  bool comm_timing = false;
+  bool comm_timed = false;  // the events hold a backward's marks
+  cudaEvent_t t_bwd_end = nullptr, t_comm_begin = nullptr, t_comm_end = nullptr;
   float* host_small = nullptr;  // pinned: loss + error flags
   int B = 0, T = 0;
 };

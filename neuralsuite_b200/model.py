@@ -268,6 +268,19 @@ class GPTModel:
         self._comm = comm
         self.world = world if comm else 1
 
+    def set_comm_timing(self, enable: bool = True) -> None:
+        """Record, in every backward, when the gradient all-reduces start and
+        end and when the backward's own work ends (needs world > 1)."""
+        _lib.check(self.lib.ns_gpt_set_comm_timing(self.h, 1 if enable else 0))
+
+    def comm_times(self):
+        """(exposed_ms, span_ms) of the last backward: the time the compute
+        stream waited for the all-reduces after its backward, and the time
+        from the first bucket's start to the last one's end."""
+        exposed, span = ctypes.c_float(), ctypes.c_float()
+        _lib.check(self.lib.ns_gpt_comm_times(self.h, ctypes.byref(exposed), ctypes.byref(span)))
+        return float(exposed.value), float(span.value)
+
     @staticmethod
     def _stream():
         return torch.cuda.current_stream().cuda_stream

@@ -158,7 +158,7 @@ def test_pointwise_and_split_checks(lib):
 
 @pytest.mark.parametrize("call", ["forward", "loss_backward", "backward", "adamw_init",
                                   "adamw_set_lr", "adamw_step", "clip_gradients", "train_step",
-                                  "set_comm"])
+                                  "set_comm", "set_comm_timing", "comm_times"])
 def test_model_entry_points_reject_a_null_handle(lib, call):
     args = {
         "forward": (None, FAKE, 1, 1, None),
@@ -170,6 +170,8 @@ def test_model_entry_points_reject_a_null_handle(lib, call):
         "clip_gradients": (None, 1.0, None),
         "train_step": (None, FAKE, FAKE, 1, 1, 0.0, None, None),
         "set_comm": (None, None, 1, 0),
+        "set_comm_timing": (None, 1),
+        "comm_times": (None, FAKE, FAKE),
     }[call]
     _err(lib, getattr(lib, "ns_gpt_" + call)(*args), NS_ERR_INVALID_ARGUMENT, "NULL model")
 
