@@ -20,11 +20,19 @@
 //    dec_attn_combine_k in chunk order, so results do not depend on timing;
 //  * a prefill (ns_gpt_decoder_prefill) runs the batched training forward on
 //    the prompt (tensor cores) and copies each layer's K and V columns into
-//    the cache, which is what decoding the prompt token by token computes.
+//    the cache, which is what decoding the prompt token by token computes;
+//  * a step's ~160 small launches are one CUDA graph, captured once per
+//    (batch, output buffers) on a private stream and replayed: the position,
+//    the cached length and the tokens reach it through a small device state
+//    that one kernel fills before each replay, and the attention grid covers
+//    the whole cache (chunks past the cached length do nothing), so the same
+//    graph serves every step.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "common.cuh"
@@ -42,6 +50,11 @@ struct ns_gpt_decoder {
   float *xf = nullptr, *logits = nullptr, *mean = nullptr, *rstd = nullptr, *part = nullptr;
   size_t part_floats = 0;
   int32_t* err = nullptr;
+  int32_t* state = nullptr;  // device: [0] wpe position, [1] cached positions before the step
+  int32_t* tok = nullptr;    // device: the step's tokens [max_batch]
+  cudaStream_t capture = nullptr;
+  // One instantiated step graph per (B, logits_out, err_flag).
+  std::map<std::tuple<int, float*, int32_t*>, cudaGraphExec_t> graphs;
   std::vector<void*> allocs;
 };
 
@@ -128,8 +141,9 @@ __global__ void gemv_finish_k(const float* __restrict__ part, int splits, int B,
 
 // x[b] = wte[tok[b]] + wpe[pos] (GPTModel::ForwardWithKVCache's embedding add).
 __global__ void dec_embed_k(const int32_t* __restrict__ tok, int B, const float* __restrict__ wte,
-                            int V, const float* __restrict__ wpe, int pos, int C,
-                            float* __restrict__ x, int32_t* err) {
+                            int V, const float* __restrict__ wpe, const int32_t* __restrict__ state,
+                            int C, float* __restrict__ x, int32_t* err) {
+  const int pos = state[0];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * C; i += gridDim.x * blockDim.x) {
     const int b = i / C, c = i % C;
     int t = tok[b];
@@ -143,10 +157,12 @@ __global__ void dec_embed_k(const int32_t* __restrict__ tok, int B, const float*
 }
 
 // K and V of rows [row0, row0 + nrows) of each sequence's qkv ([rows, 3C],
-// sequence b's row r at b * seq_stride + r) to cache positions [idx, idx + nrows).
+// sequence b's row r at b * seq_stride + r) to cache positions [idx, idx + nrows),
+// idx = state[1] when state is given.
 __global__ void dec_append_k(const float* __restrict__ qkv, int B, int nrows, int seq_stride, int C,
                              int H, int D, float* __restrict__ kc, float* __restrict__ vc, int cap,
-                             int idx) {
+                             int idx, const int32_t* __restrict__ state) {
+  if (state) idx = state[1];
   const int64_t total = (int64_t)B * nrows * C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -162,12 +178,16 @@ __global__ void dec_append_k(const float* __restrict__ qkv, int B, int nrows, in
 }
 
 // Partial attention of the query of sequence b, head h over cached keys
-// [s*kch, min(n, (s+1)*kch)): per warp an online softmax (running max m,
-// sum l, output o); the four warps merged in order.  part: [B*H][S][2 + D].
+// [s*kch, min(n, (s+1)*kch)), n = state[1] + 1: per warp an online softmax
+// (running max m, sum l, output o); the four warps merged in order.  part:
+// [B*H][S][2 + D] with S = gridDim.y chunks covering the whole cache; a
+// chunk past n writes l = 0, which the combine skips.
 constexpr int kAttThreads = 128;
 __global__ void __launch_bounds__(kAttThreads) dec_attn_partial_k(
     const float* __restrict__ qkv, int C, int H, int D, const float* __restrict__ kc,
-    const float* __restrict__ vc, int cap, int n, int kch, float scale, float* __restrict__ part) {
+    const float* __restrict__ vc, int cap, const int32_t* __restrict__ state, int kch, float scale,
+    float* __restrict__ part) {
+  const int n = state[1] + 1;
   __shared__ float wm[4], wl[4];
   __shared__ float wo[4][128];
   const int bh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
@@ -336,21 +356,111 @@ ns_status gemv(ns_gpt_decoder* d, const float* X, int B, int K, const float* W, 
   return check_launch("decode gemv finish");
 }
 
-// Attention of the B current queries (in d->qkv) over n cached positions per sequence of layer l.
-ns_status attend(ns_gpt_decoder* d, int l, int B, int n, cudaStream_t s) {
+// Attention of the B current queries (in d->qkv) over the state[1] + 1
+// cached positions per sequence of layer l; the grid covers the whole cache.
+ns_status attend(ns_gpt_decoder* d, int l, int B, cudaStream_t s) {
   const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
   const int kch = 64;
-  const int S = (n + kch - 1) / kch;
+  const int S = (d->cap + kch - 1) / kch;
   if ((size_t)B * d->H * S * (2 + d->D) > d->part_floats)
     return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small for attention");
   dim3 grid(B * d->H, S);
   dec_attn_partial_k<<<grid, kAttThreads, 0, s>>>(d->qkv, d->C, d->H, d->D, d->kc + l * per_layer,
-                                                  d->vc + l * per_layer, d->cap, n, kch,
+                                                  d->vc + l * per_layer, d->cap, d->state, kch,
                                                   1.0f / std::sqrt((float)d->D), d->part);
   ns_status rc = check_launch("decode attention");
   if (rc != NS_OK) return rc;
   dec_attn_combine_k<<<B * d->H, 128, 0, s>>>(d->part, S, d->H, d->D, d->C, d->att);
   return check_launch("decode attention combine");
+}
+
+// The step's inputs for the graph: its tokens and the state it reads.
+__global__ void dec_state_k(const int32_t* __restrict__ tokens, int B, int pos, int len,
+                            int32_t* __restrict__ state, int32_t* __restrict__ tok) {
+  for (int i = threadIdx.x; i < B; i += blockDim.x) tok[i] = tokens[i];
+  if (threadIdx.x == 0) {
+    state[0] = pos;
+    state[1] = len;
+  }
+}
+
+// Every launch of one decode step (GPTModel::ForwardWithKVCache) on stream s,
+// reading the tokens from d->tok and the position and cached length from
+// d->state.
+ns_status enqueue_step(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaStream_t s) {
+  GPTModel& m = *d->owner->model;
+  const float* P = m.Values();
+  const auto& off = m.Offsets();
+  const int C = d->C, L = d->L;
+  void* stream = s;
+  auto prm = [&](int i) { return P + off[i]; };
+  dec_embed_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->tok, B, prm(0), d->V, prm(1),
+                                                           d->state, C, d->x, err);
+  ns_status rc = check_launch("decode embedding");
+  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
+  for (int l = 0; l < L && rc == NS_OK; ++l) {
+    const int t = 2 + 12 * l;
+    // x1 = x + c_proj(attention(c_attn(ln_1(x))))
+    rc = ns_layernorm_fwd(d->x, prm(t), prm(t + 1), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
+    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 2), 3 * C, prm(t + 3), kBias, nullptr, d->qkv, s);
+    if (rc == NS_OK) {
+      dec_append_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->qkv, B, 1, 1, C, d->H, d->D,
+                                                                 d->kc + l * per_layer,
+                                                                 d->vc + l * per_layer, d->cap, 0,
+                                                                 d->state);
+      rc = check_launch("decode cache append");
+    }
+    if (rc == NS_OK) rc = attend(d, l, B, s);
+    if (rc == NS_OK) rc = gemv(d, d->att, B, C, prm(t + 4), C, prm(t + 5), kBiasResid, d->x, d->x1, s);
+    // x = x1 + mlp_proj(gelu(mlp_fc(ln_2(x1))))
+    if (rc == NS_OK)
+      rc = ns_layernorm_fwd(d->x1, prm(t + 6), prm(t + 7), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
+    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 8), 4 * C, prm(t + 9), kBiasGelu, nullptr, d->g, s);
+    if (rc == NS_OK) rc = gemv(d, d->g, B, 4 * C, prm(t + 10), C, prm(t + 11), kBiasResid, d->x1, d->x, s);
+  }
+  if (rc != NS_OK) return rc;
+  const int f = 2 + 12 * L;
+  rc = ns_layernorm_fwd(d->x, prm(f), prm(f + 1), d->xf, d->mean, d->rstd, B, C, 1e-5f, stream);
+  if (rc != NS_OK) return rc;
+  const int vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(prm(0)) & 15) == 0);
+  const size_t smem = (size_t)8 * C * sizeof(float);
+  if (smem > 48 * 1024)
+    NS_TRY_CUDA(cudaFuncSetAttribute(dec_logits_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "decode logits attr");
+  dim3 grid((d->V + 7) / 8, (B + 7) / 8);
+  dec_logits_k<<<grid, 256, smem, s>>>(d->xf, B, C, prm(0), d->V, vec, lg);
+  return check_launch("decode logits");
+}
+
+// The instantiated step graph for (B, lg, err), captured on first use on
+// the decoder's own stream (the caller's may be the legacy default stream,
+// which cannot be captured).
+ns_status step_graph(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaGraphExec_t* out) {
+  const auto key = std::make_tuple(B, lg, err);
+  auto it = d->graphs.find(key);
+  if (it != d->graphs.end()) {
+    *out = it->second;
+    return NS_OK;
+  }
+  if (!d->capture)
+    NS_TRY_CUDA(cudaStreamCreateWithFlags(&d->capture, cudaStreamNonBlocking), "decode graph stream");
+  NS_TRY_CUDA(cudaStreamBeginCapture(d->capture, cudaStreamCaptureModeThreadLocal),
+              "decode graph capture");
+  ns_status rc = enqueue_step(d, B, lg, err, d->capture);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(d->capture, &g);
+  if (rc != NS_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "decode graph capture");
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ei != cudaSuccess) return cuda_fail(ei, "decode graph instantiate");
+  d->graphs.emplace(key, exec);
+  *out = exec;
+  return NS_OK;
 }
 
 template <typename T>
@@ -363,6 +473,10 @@ ns_status dev_alloc(ns_gpt_decoder* d, T** p, size_t count) {
 }
 
 void free_all(ns_gpt_decoder* d) {
+  for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+  d->graphs.clear();
+  if (d->capture) cudaStreamDestroy(d->capture);
+  d->capture = nullptr;
   for (void* p : d->allocs) cudaFree(p);
   d->allocs.clear();
 }
@@ -417,6 +531,8 @@ ns_status ns_gpt_decoder_create(ns_gpt* model, int max_batch, ns_gpt_decoder** o
   A(&d->rstd, Bm);
   A(&d->part, part);
   if (rc == NS_OK) rc = dev_alloc(d, &d->err, 1);
+  if (rc == NS_OK) rc = dev_alloc(d, &d->state, 2);
+  if (rc == NS_OK) rc = dev_alloc(d, &d->tok, Bm);
   if (rc == NS_OK) {
     cudaError_t e = cudaMemset(d->err, 0, sizeof(int32_t));
     if (e != cudaSuccess) rc = cuda_fail(e, "ns_gpt_decoder_create");
@@ -460,49 +576,15 @@ ns_status ns_gpt_decode_step(ns_gpt_decoder* d, const int32_t* tokens, int B, in
   if (d->len >= d->cap)
     return fail(NS_ERR_OUT_OF_RANGE, "ns_gpt_decode_step: the KV cache is full (block_size positions)");
   cudaStream_t s = as_stream(stream);
-  GPTModel& m = *d->owner->model;
-  const float* P = m.Values();
-  const auto& off = m.Offsets();
-  const int C = d->C, L = d->L;
-  auto prm = [&](int i) { return P + off[i]; };
-  int32_t* err = err_flag ? err_flag : d->err;
-  dec_embed_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(tokens, B, prm(0), d->V, prm(1), pos, C,
-                                                           d->x, err);
-  ns_status rc = check_launch("decode embedding");
-  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
-  for (int l = 0; l < L && rc == NS_OK; ++l) {
-    const int t = 2 + 12 * l;
-    // x1 = x + c_proj(attention(c_attn(ln_1(x))))
-    rc = ns_layernorm_fwd(d->x, prm(t), prm(t + 1), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
-    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 2), 3 * C, prm(t + 3), kBias, nullptr, d->qkv, s);
-    if (rc == NS_OK) {
-      dec_append_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->qkv, B, 1, 1, C, d->H, d->D,
-                                                                 d->kc + l * per_layer,
-                                                                 d->vc + l * per_layer, d->cap, d->len);
-      rc = check_launch("decode cache append");
-    }
-    if (rc == NS_OK) rc = attend(d, l, B, d->len + 1, s);
-    if (rc == NS_OK) rc = gemv(d, d->att, B, C, prm(t + 4), C, prm(t + 5), kBiasResid, d->x, d->x1, s);
-    // x = x1 + mlp_proj(gelu(mlp_fc(ln_2(x1))))
-    if (rc == NS_OK)
-      rc = ns_layernorm_fwd(d->x1, prm(t + 6), prm(t + 7), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
-    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 8), 4 * C, prm(t + 9), kBiasGelu, nullptr, d->g, s);
-    if (rc == NS_OK) rc = gemv(d, d->g, B, 4 * C, prm(t + 10), C, prm(t + 11), kBiasResid, d->x1, d->x, s);
-  }
-  if (rc != NS_OK) return rc;
-  const int f = 2 + 12 * L;
-  rc = ns_layernorm_fwd(d->x, prm(f), prm(f + 1), d->xf, d->mean, d->rstd, B, C, 1e-5f, stream);
-  if (rc != NS_OK) return rc;
   float* lg = logits_out ? logits_out : d->logits;
-  const int vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(prm(0)) & 15) == 0);
-  const size_t smem = (size_t)8 * C * sizeof(float);
-  if (smem > 48 * 1024)
-    NS_TRY_CUDA(cudaFuncSetAttribute(dec_logits_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                "decode logits attr");
-  dim3 grid((d->V + 7) / 8, (B + 7) / 8);
-  dec_logits_k<<<grid, 256, smem, s>>>(d->xf, B, C, prm(0), d->V, vec, lg);
-  rc = check_launch("decode logits");
+  int32_t* err = err_flag ? err_flag : d->err;
+  cudaGraphExec_t exec = nullptr;
+  ns_status rc = step_graph(d, B, lg, err, &exec);
   if (rc != NS_OK) return rc;
+  dec_state_k<<<1, 64, 0, s>>>(tokens, B, pos, d->len, d->state, d->tok);
+  rc = check_launch("decode state");
+  if (rc != NS_OK) return rc;
+  NS_TRY_CUDA(cudaGraphLaunch(exec, s), "decode graph launch");
   d->B = B;
   d->len += 1;
   return NS_OK;
@@ -524,7 +606,8 @@ ns_status ns_gpt_decoder_prefill(ns_gpt_decoder* d, const int32_t* tokens, int B
   for (int l = 0; l < d->L; ++l) {
     const float* qkv = m.Block(l).Attn().Qkv().Data();
     dec_append_k<<<grid_for((int64_t)B * T * d->C, 256), 256, 0, s>>>(
-        qkv, B, T, T, d->C, d->H, d->D, d->kc + l * per_layer, d->vc + l * per_layer, d->cap, 0);
+        qkv, B, T, T, d->C, d->H, d->D, d->kc + l * per_layer, d->vc + l * per_layer, d->cap, 0,
+        nullptr);
     rc = check_launch("prefill cache fill");
     if (rc != NS_OK) return rc;
   }
