@@ -249,11 +249,299 @@ __global__ void __launch_bounds__(256) col2im_fixed_k(const float* __restrict__ 
   }
 }
 
+// ---------------------------------------------------------------- direct paths
+//
+// Convolutions with very few output channels (the U-Net's 3-channel head) or
+// very few column rows (its 3-channel input layer) would fill a few percent
+// of a tensor-core tile, so they run as direct CUDA-core loops on the input
+// (no columns) in fp32, with the reference's order where it has one, and
+// their operands staged in shared memory.
+constexpr int kDirectMaxOC = 4;     // output channels per thread (forward, dx, dW groups)
+constexpr int kDirectMaxTaps = 9;   // k x k <= 9 for the direct weight gradient
+constexpr int kDirectGroup = 16;    // input channels staged per round (forward)
+constexpr int kDirectDxGroup = 16;  // input channels per CTA (dx)
+constexpr int kDirectSmemFloats = 24576;  // 96 KB of staged planes (dW)
+
+// Asynchronous global -> shared copies (cp.async): every copy of a staging
+// round is in flight at once, then one wait.  16-byte copies where both
+// addresses allow, 4-byte copies otherwise.
+__device__ __forceinline__ uint32_t sm_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+// n floats from src to dst, shared by the CTA's threads (no wait).
+__device__ __forceinline__ void stage(float* dst, const float* src, int n) {
+  const bool vec = ((n & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0) &&
+                   ((sm_addr(dst) & 15) == 0);
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) cp_async16(dst + i, src + i);
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) cp_async4(dst + i, src + i);
+  }
+}
+
+// Output rows per CTA of the direct forward (R * OW <= 256: one pixel per thread).
+__host__ __device__ inline int direct_rows(int OW, int OH) {
+  const int r = 256 / OW;
+  return r < 1 ? 1 : (r > OH ? OH : r);
+}
+// Input rows per CTA of the direct dx (R * W <= 512).
+__host__ __device__ inline int direct_dx_rows(int W, int H) {
+  const int r = 512 / W;
+  return r < 1 ? 1 : (r > H ? H : r);
+}
+
+// y[b][oc][oh][ow] = (sum over k = (ic*k + kh)*k + kw ascending of
+// W[oc][k] * x[b][ic][ih][iw]) + bias[oc]: MatMul's k-ascending sum with
+// separate multiplies and adds (src/tensor.cpp:236-257), then the bias
+// (conv2d.h:255-263).  A CTA computes R output rows of one image for every
+// channel, one pixel per thread, staging kDirectGroup input channels' rows
+// at a time (rows outside the image as zeros).
+__global__ void __launch_bounds__(256) conv_direct_fwd_k(const float* __restrict__ x, Shape sh,
+                                                         const float* __restrict__ w,
+                                                         const float* __restrict__ bias,
+                                                         float* __restrict__ y) {
+  extern __shared__ __align__(16) float sm[];
+  const int R = direct_rows(sh.OW, sh.OH), nrows = (R - 1) * sh.s + sh.k;
+  const int kk2 = sh.k * sh.k, K = sh.IC * kk2, P = sh.OH * sh.OW;
+  const int rowlen = (sh.W + 3) & ~3;             // staged row pitch (16-byte rows)
+  float* xs = sm;                                   // [group][nrows][rowlen]
+  float* ws = sm + kDirectGroup * nrows * rowlen;   // [oc][K] (all weights)
+  const int tiles = (sh.OH + R - 1) / R;
+  const int b = blockIdx.x / tiles, oh0 = (blockIdx.x - b * tiles) * R;
+  const int ih0 = oh0 * sh.s - sh.p;
+  const int npix = min(R, sh.OH - oh0) * sh.OW;
+  const int q = threadIdx.x, r = q / sh.OW, ow = q - r * sh.OW;
+  stage(ws, w, sh.OC * K);
+  float acc[kDirectMaxOC];
+#pragma unroll
+  for (int o = 0; o < kDirectMaxOC; ++o) acc[o] = 0.0f;
+  for (int c0 = 0; c0 < sh.IC; c0 += kDirectGroup) {
+    const int ng = min(kDirectGroup, sh.IC - c0);
+    __syncthreads();  // the previous round's reads are done
+    for (int g = 0; g < ng; ++g)
+      for (int rr = threadIdx.x >> 5; rr < nrows; rr += blockDim.x >> 5) {
+        const int ih = ih0 + rr;
+        float* dst = xs + (g * nrows + rr) * rowlen;
+        if (ih >= 0 && ih < sh.H) {
+          const float* src = x + (((size_t)b * sh.IC + c0 + g) * sh.H + ih) * sh.W;
+          for (int c = threadIdx.x & 31; c < sh.W; c += 32) cp_async4(dst + c, src + c);
+        } else {
+          for (int c = threadIdx.x & 31; c < sh.W; c += 32) dst[c] = 0.0f;
+        }
+      }
+    cp_async_wait_all();
+    __syncthreads();
+    if (q < npix) {
+      for (int g = 0; g < ng; ++g)
+        for (int kh = 0; kh < sh.k; ++kh) {
+          const float* xr = xs + (g * nrows + r * sh.s + kh) * rowlen;
+          for (int kw = 0; kw < sh.k; ++kw) {
+            const int iw = ow * sh.s + kw - sh.p;
+            const float v = (iw >= 0 && iw < sh.W) ? xr[iw] : 0.0f;
+            const float* wt = ws + (c0 + g) * kk2 + kh * sh.k + kw;
+#pragma unroll
+            for (int o = 0; o < kDirectMaxOC; ++o)
+              if (o < sh.OC) acc[o] = __fadd_rn(acc[o], __fmul_rn(wt[o * K], v));
+          }
+        }
+    }
+  }
+  if (q < npix) {
+#pragma unroll
+    for (int o = 0; o < kDirectMaxOC; ++o)
+      if (o < sh.OC) {
+        const float v = bias ? __fadd_rn(acc[o], __ldg(bias + o)) : acc[o];
+        y[((size_t)b * sh.OC + o) * P + oh0 * sh.OW + q] = v;
+      }
+  }
+}
+
+// dx[b][ic][ih][iw] = sum over (kh, kw) in order of t(kh, kw), with
+// t = sum over oc ascending of W[oc][ic][kh][kw] * dy[b][oc][oh][ow] for each
+// window (oh, ow) = (ih + p - kh, iw + p - kw) inside the output: the
+// reference's dcols = W^T . dout (an oc-ascending MatMul sum) gathered by
+// Col2Im in (kh, kw) order (conv2d.h:321-324, 378-403).  Stride 1.  A CTA
+// takes R input rows of one image for kDirectDxGroup channels, with the dy
+// rows they read and their weights in shared memory.
+__global__ void __launch_bounds__(256) conv_direct_dx_k(const float* __restrict__ dy, Shape sh,
+                                                        const float* __restrict__ w,
+                                                        float* __restrict__ dx) {
+  extern __shared__ __align__(16) float sm[];
+  const int R = direct_dx_rows(sh.W, sh.H), nrows = R + sh.k - 1;
+  const int kk2 = sh.k * sh.k, K = sh.IC * kk2, P = sh.OH * sh.OW;
+  float* ds = sm;                                // [oc][nrows][OW]
+  float* ws = sm + sh.OC * nrows * sh.OW;        // [oc][K] (all weights)
+  const int tiles = (sh.H + R - 1) / R, groups = (sh.IC + kDirectDxGroup - 1) / kDirectDxGroup;
+  int t = blockIdx.x;
+  const int grp = t % groups;
+  t /= groups;
+  const int tile = t % tiles, b = t / tiles;
+  const int ih0 = tile * R, c0 = grp * kDirectDxGroup, ng = min(kDirectDxGroup, sh.IC - c0);
+  const int oh0 = ih0 + sh.p - (sh.k - 1);  // dy row held in smem row 0
+  stage(ws, w, sh.OC * K);
+  for (int i = threadIdx.x >> 5; i < sh.OC * nrows; i += blockDim.x >> 5) {
+    const int o = i / nrows, rr = i - o * nrows, oh = oh0 + rr;
+    float* dst = ds + i * sh.OW;
+    if (oh >= 0 && oh < sh.OH) {
+      const float* src = dy + ((size_t)b * sh.OC + o) * P + (size_t)oh * sh.OW;
+      for (int c = threadIdx.x & 31; c < sh.OW; c += 32) cp_async4(dst + c, src + c);
+    } else {
+      for (int c = threadIdx.x & 31; c < sh.OW; c += 32) dst[c] = 0.0f;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int rows = min(R, sh.H - ih0), npix = rows * sh.W;
+  for (int item = threadIdx.x; item < ng * npix; item += blockDim.x) {
+    const int g = item / npix, q = item - g * npix;
+    const int r = q / sh.W, iw = q - r * sh.W, ih = ih0 + r;
+    float acc = 0.0f;
+    for (int kh = 0; kh < sh.k; ++kh) {
+      const int oh = ih + sh.p - kh;
+      if (oh < 0 || oh >= sh.OH) continue;
+      const int srow = oh - oh0;
+      for (int kw = 0; kw < sh.k; ++kw) {
+        const int ow = iw + sh.p - kw;
+        if (ow < 0 || ow >= sh.OW) continue;
+        const float* wt = ws + (c0 + g) * kk2 + kh * sh.k + kw;
+        float tv = 0.0f;
+#pragma unroll
+        for (int o = 0; o < kDirectMaxOC; ++o)
+          if (o < sh.OC)
+            tv = __fadd_rn(tv, __fmul_rn(wt[o * K], ds[(o * nrows + srow) * sh.OW + ow]));
+        acc += tv;
+      }
+    }
+    dx[(((size_t)b * sh.IC + c0 + g) * sh.H + ih) * sh.W + iw] = acc;
+  }
+}
+
+// part[(b * OC + oc) * K + (ic * k + kh) * k + kw] = sum over the positions
+// of image b of dy[b][oc][p] * x[b][ic][oh*s + kh - p][ow*s + kw - p]: one CTA
+// per (image, input channel, group of up to kDirectMaxOC output channels),
+// with the input plane and the group's dy planes in shared memory; each
+// thread sums a strided share of the positions, the threads' sums meet in a
+// fixed order (warp shuffles, then warps in order).
+__global__ void __launch_bounds__(256) conv_direct_dw_k(const float* __restrict__ x,
+                                                        const float* __restrict__ dy, Shape sh,
+                                                        float* __restrict__ part) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float wred[8][kDirectMaxOC * kDirectMaxTaps];
+  const int HW = sh.H * sh.W, P = sh.OH * sh.OW, kk2 = sh.k * sh.k, K = sh.IC * kk2;
+  const int ogroups = (sh.OC + kDirectMaxOC - 1) / kDirectMaxOC;
+  int t = blockIdx.x;
+  const int og = t % ogroups;
+  t /= ogroups;
+  const int ic = t % sh.IC, b = t / sh.IC;
+  const int o0 = og * kDirectMaxOC, no = min(kDirectMaxOC, sh.OC - o0);
+  const int hw4 = (HW + 3) & ~3;
+  float* xs = sm;         // [H*W]
+  float* ds = sm + hw4;   // [no][P]
+  stage(xs, x + ((size_t)b * sh.IC + ic) * HW, HW);
+  stage(ds, dy + ((size_t)b * sh.OC + o0) * P, no * P);
+  cp_async_wait_all();
+  __syncthreads();
+  // Tap offsets of the window, once.
+  int tdh[kDirectMaxTaps], tdw[kDirectMaxTaps];
+#pragma unroll
+  for (int tt = 0; tt < kDirectMaxTaps; ++tt) {
+    const int kh = tt / sh.k;
+    tdh[tt] = kh - sh.p;
+    tdw[tt] = tt - kh * sh.k - sh.p;
+  }
+  float acc[kDirectMaxOC * kDirectMaxTaps];
+#pragma unroll
+  for (int j = 0; j < kDirectMaxOC * kDirectMaxTaps; ++j) acc[j] = 0.0f;
+  for (int q = threadIdx.x; q < P; q += blockDim.x) {
+    const int oh = q / sh.OW, ow = q - oh * sh.OW;
+    float g[kDirectMaxOC];
+#pragma unroll
+    for (int o = 0; o < kDirectMaxOC; ++o) g[o] = o < no ? ds[o * P + q] : 0.0f;
+#pragma unroll
+    for (int tt = 0; tt < kDirectMaxTaps; ++tt) {
+      if (tt < kk2) {
+        const int ih = oh * sh.s + tdh[tt], iw = ow * sh.s + tdw[tt];
+        const float v = (ih >= 0 && ih < sh.H && iw >= 0 && iw < sh.W) ? xs[ih * sh.W + iw] : 0.0f;
+#pragma unroll
+        for (int o = 0; o < kDirectMaxOC; ++o) acc[o * kDirectMaxTaps + tt] = fmaf(g[o], v, acc[o * kDirectMaxTaps + tt]);
+      }
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kDirectMaxOC * kDirectMaxTaps; ++j) {
+    const float v = warp_sum(acc[j]);
+    if (lane == 0) wred[warp][j] = v;
+  }
+  __syncthreads();
+  const int j = threadIdx.x;
+  if (j < kDirectMaxOC * kDirectMaxTaps) {
+    const int o = j / kDirectMaxTaps, tt = j - o * kDirectMaxTaps;
+    if (o < no && tt < kk2) {
+      float sum = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) sum += wred[w][j];
+      part[((size_t)b * sh.OC + o0 + o) * K + ic * kk2 + tt] = sum;
+    }
+  }
+}
+
+// dw[oc][kk] = the per-image sums added in image order (conv2d.h:326-331).
+__global__ void conv_direct_dw_finish_k(const float* __restrict__ part, int OC, int K, int B,
+                                        float* __restrict__ dw) {
+  const int64_t n = (int64_t)OC * K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float total = 0.0f;
+    for (int b = 0; b < B; ++b) total += part[(size_t)b * n + i];
+    dw[i] = total;
+  }
+}
+
+// Shared memory of the direct kernels (floats).
+size_t direct_fwd_smem(const Shape& sh) {
+  const int R = direct_rows(sh.OW, sh.OH);
+  return (size_t)kDirectGroup * ((R - 1) * sh.s + sh.k) * ((sh.W + 3) & ~3) +
+         (size_t)sh.OC * sh.IC * sh.k * sh.k;
+}
+size_t direct_dx_smem(const Shape& sh) {
+  const int R = direct_dx_rows(sh.W, sh.H);
+  return (size_t)sh.OC * (R + sh.k - 1) * sh.OW + (size_t)sh.OC * sh.IC * sh.k * sh.k;
+}
+size_t direct_dw_smem(const Shape& sh) {
+  return (size_t)((sh.H * sh.W + 3) & ~3) + (size_t)kDirectMaxOC * sh.OH * sh.OW;
+}
+
 int grid_runs(int64_t runs) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(runs, (int64_t)sm_count() * 32));
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Which products run on the direct CUDA-core paths instead of the GEMM: few
+// output channels (forward, dx, weight gradient) or few column rows (weight
+// gradient), small windows, and planes that fit the staging buffers.  A
+// direct forward implies a direct weight gradient, so no columns are needed.
+bool direct_dw(const Shape& sh) {
+  return (sh.OC <= kDirectMaxOC || sh.K() <= 32) && sh.k * sh.k <= kDirectMaxTaps &&
+         direct_dw_smem(sh) <= (size_t)kDirectSmemFloats;
+}
+bool direct_fwd(const Shape& sh) {
+  return sh.OC <= kDirectMaxOC && sh.OW <= 256 && direct_dw(sh) &&
+         direct_fwd_smem(sh) * sizeof(float) <= 48 * 1024;
+}
+bool direct_dx(const Shape& sh) {
+  return sh.OC <= kDirectMaxOC && sh.s == 1 && sh.W <= 512 &&
+         direct_dx_smem(sh) * sizeof(float) <= 48 * 1024;
+}
 
 ns_status make_shape(int B, int IC, int H, int W, int OC, int k, int stride, int pad, Shape* sh) {
   if (B < 0 || IC <= 0 || H <= 0 || W <= 0 || OC <= 0 || k <= 0 || stride <= 0 || pad < 0)
@@ -272,7 +560,7 @@ ns_status make_shape(int B, int IC, int H, int W, int OC, int k, int stride, int
 // (only when the columns live in the workspace), w_lo, yc | dyc, dyc_lo,
 // dcols, the bias partials, then the GEMM workspace.
 struct Ws {
-  float *cols, *cols_lo, *w_lo, *yc, *dyc, *dyc_lo, *dcols, *bias_part;
+  float *cols, *cols_lo, *w_lo, *yc, *dyc, *dyc_lo, *dcols, *bias_part, *dw_part;
   void* gemm;
   size_t gemm_bytes, total;
 };
@@ -303,6 +591,7 @@ Ws layout(const Shape& sh, void* base, bool with_cols) {
   w.dyc_lo = take(ON);
   w.dcols = take(KN);
   w.bias_part = take(al64((size_t)sh.OC * std::max(sh.B, 1)));
+  w.dw_part = direct_dw(sh) ? take(al64((size_t)sh.OC * sh.K() * std::max(sh.B, 1))) : nullptr;
   const int M = sh.OC, N = (int)sh.N(), K = (int)sh.K();
   w.gemm_bytes = std::max({ns_gemm_workspace_size(M, N, K), ns_gemm_workspace_size(M, K, N),
                            ns_gemm_workspace_size(K, N, M)});
@@ -330,6 +619,14 @@ ns_status launch_im2col(const float* x, const Shape& sh, float* cols, float* col
   return check_launch("ns_conv2d im2col");
 }
 
+ns_status launch_direct_fwd(const float* x, const Shape& sh, const float* weight,
+                            const float* bias, float* y, cudaStream_t s) {
+  const int R = direct_rows(sh.OW, sh.OH);
+  const int grid = sh.B * ((sh.OH + R - 1) / R);
+  conv_direct_fwd_k<<<grid, 256, direct_fwd_smem(sh) * sizeof(float), s>>>(x, sh, weight, bias, y);
+  return check_launch("ns_conv2d_fwd direct");
+}
+
 // The forward once the columns are in place: Yc = W . cols, then NCHW + bias.
 ns_status forward_body(const Shape& sh, const float* weight, const float* bias, float* y,
                        const float* cols, const float* cols_lo, const Ws& ws, cudaStream_t s) {
@@ -345,27 +642,53 @@ ns_status forward_body(const Shape& sh, const float* weight, const float* bias, 
   return check_launch("ns_conv2d_fwd layout");
 }
 
-// The backward once the columns are in place.
-ns_status backward_body(const Shape& sh, const float* cols, const float* cols_lo, const float* dy,
-                        const float* weight, float* dx, float* dweight, float* dbias, const Ws& ws,
-                        cudaStream_t s) {
+// The backward: x is read by the direct paths, the columns (of x) by the
+// weight-gradient GEMM.
+ns_status backward_body(const Shape& sh, const float* x, const float* cols, const float* cols_lo,
+                        const float* dy, const float* weight, float* dx, float* dweight,
+                        float* dbias, const Ws& ws, cudaStream_t s) {
   const int M = sh.OC, N = (int)sh.N(), K = (int)sh.K();
-  const int vec = (sh.P() % 4 == 0 && aligned16(dy) && aligned16(ws.dyc) && aligned16(ws.dyc_lo))
-                      ? 1 : 0;
-  nchw_to_cnhw_k<<<grid_runs((int64_t)sh.B * sh.OC), 256, 0, s>>>(dy, sh, ws.dyc, ws.dyc_lo, vec);
-  ns_status rc = check_launch("ns_conv2d_bwd layout");
-  if (rc != NS_OK) return rc;
+  ns_status rc = NS_OK;
+  const bool gemm_dw = !direct_dw(sh), gemm_dx = dx && !direct_dx(sh);
+  if (gemm_dw || gemm_dx) {
+    const int vec = (sh.P() % 4 == 0 && aligned16(dy) && aligned16(ws.dyc) && aligned16(ws.dyc_lo))
+                        ? 1 : 0;
+    nchw_to_cnhw_k<<<grid_runs((int64_t)sh.B * sh.OC), 256, 0, s>>>(dy, sh, ws.dyc, ws.dyc_lo, vec);
+    rc = check_launch("ns_conv2d_bwd layout");
+    if (rc != NS_OK) return rc;
+  }
   bias_part_k<<<dim3(sh.OC, sh.B), 256, 0, s>>>(dy, sh, ws.bias_part);
   rc = check_launch("ns_conv2d_bwd bias");
   if (rc != NS_OK) return rc;
   bias_finish_k<<<ceil_div(sh.OC, 128), 128, 0, s>>>(ws.bias_part, sh.OC, sh.B, dbias);
   rc = check_launch("ns_conv2d_bwd bias");
   if (rc != NS_OK) return rc;
-  // dW[OC, K] = dYc[OC, B*P] . cols[K, B*P]^T (overwritten, as the reference zeroes it first)
-  rc = ns_gemm_lo(M, K, N, ws.dyc, N, 0, lo_if(ws.dyc_lo, N), cols, N, 1, lo_if(cols_lo, N),
-                  dweight, K, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ws.gemm,
-                  ws.gemm_bytes, s);
+  if (gemm_dw) {
+    // dW[OC, K] = dYc[OC, B*P] . cols[K, B*P]^T (overwritten, as the reference zeroes it first)
+    rc = ns_gemm_lo(M, K, N, ws.dyc, N, 0, lo_if(ws.dyc_lo, N), cols, N, 1, lo_if(cols_lo, N),
+                    dweight, K, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ws.gemm,
+                    ws.gemm_bytes, s);
+  } else {
+    const size_t smem = direct_dw_smem(sh) * sizeof(float);
+    if (smem > 48 * 1024)
+      NS_TRY_CUDA(cudaFuncSetAttribute(conv_direct_dw_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem),
+                  "ns_conv2d_bwd direct weight gradient");
+    const int ogroups = (M + kDirectMaxOC - 1) / kDirectMaxOC;
+    conv_direct_dw_k<<<sh.B * sh.IC * ogroups, 256, smem, s>>>(x, dy, sh, ws.dw_part);
+    rc = check_launch("ns_conv2d_bwd direct weight gradient");
+    if (rc != NS_OK) return rc;
+    conv_direct_dw_finish_k<<<grid_runs(ceil_div64((int64_t)M * K, 256)), 256, 0, s>>>(
+        ws.dw_part, M, K, sh.B, dweight);
+    rc = check_launch("ns_conv2d_bwd direct weight gradient");
+  }
   if (rc != NS_OK || !dx) return rc;
+  if (!gemm_dx) {
+    const int R = direct_dx_rows(sh.W, sh.H);
+    const int grid = sh.B * ((sh.H + R - 1) / R) * ((sh.IC + kDirectDxGroup - 1) / kDirectDxGroup);
+    conv_direct_dx_k<<<grid, 256, direct_dx_smem(sh) * sizeof(float), s>>>(dy, sh, weight, dx);
+    return check_launch("ns_conv2d_bwd direct dx");
+  }
   rc = ns_split_lo(weight, M, K, K, ws.w_lo, s);
   if (rc != NS_OK) return rc;
   // dcols[K, B*P] = W[OC, K]^T . dYc[OC, B*P]
@@ -395,7 +718,7 @@ ns_status zero_grads(const Shape& sh, float* dweight, float* dbias, cudaStream_t
 int64_t cols_floats(int B, int IC, int H, int W, int OC, int k, int stride, int pad) {
   Shape sh;
   if (make_shape(B, IC, H, W, OC, k, stride, pad, &sh) != NS_OK) return 0;
-  return sh.K() * sh.N();
+  return direct_fwd(sh) && direct_dw(sh) ? 0 : sh.K() * sh.N();
 }
 
 size_t keep_workspace_size(int B, int IC, int H, int W, int OC, int k, int stride, int pad) {
@@ -411,7 +734,9 @@ ns_status forward_keep(const float* x, int B, int IC, int H, int W, const float*
   Shape sh;
   ns_status rc = make_shape(B, IC, H, W, OC, k, stride, pad, &sh);
   if (rc != NS_OK || B == 0) return rc;
-  NS_REQUIRE(x && weight && y && cols && cols_lo, "conv forward: NULL argument");
+  NS_REQUIRE(x && weight && y, "conv forward: NULL argument");
+  if (direct_fwd(sh)) return launch_direct_fwd(x, sh, weight, bias, y, s);
+  NS_REQUIRE(cols && cols_lo, "conv forward: NULL column buffer");
   Ws ws;
   rc = check_ws(sh, workspace, workspace_bytes, false, "conv forward", &ws);
   if (rc != NS_OK) return rc;
@@ -420,19 +745,21 @@ ns_status forward_keep(const float* x, int B, int IC, int H, int W, const float*
   return forward_body(sh, weight, bias, y, cols, cols_lo, ws, s);
 }
 
-ns_status backward_from_cols(const float* cols, const float* cols_lo, const float* dy, int B,
-                             int IC, int H, int W, const float* weight, int OC, int k, int stride,
-                             int pad, float* dx, float* dweight, float* dbias, void* workspace,
-                             size_t workspace_bytes, cudaStream_t s) {
+ns_status backward_from_cols(const float* x, const float* cols, const float* cols_lo,
+                             const float* dy, int B, int IC, int H, int W, const float* weight,
+                             int OC, int k, int stride, int pad, float* dx, float* dweight,
+                             float* dbias, void* workspace, size_t workspace_bytes,
+                             cudaStream_t s) {
   Shape sh;
   ns_status rc = make_shape(B, IC, H, W, OC, k, stride, pad, &sh);
   if (rc != NS_OK) return rc;
-  NS_REQUIRE(cols && cols_lo && dy && weight && dweight && dbias, "conv backward: NULL argument");
+  NS_REQUIRE(x && dy && weight && dweight && dbias, "conv backward: NULL argument");
+  NS_REQUIRE(direct_dw(sh) || (cols && cols_lo), "conv backward: NULL column buffer");
   if (B == 0) return zero_grads(sh, dweight, dbias, s);
   Ws ws;
   rc = check_ws(sh, workspace, workspace_bytes, false, "conv backward", &ws);
   if (rc != NS_OK) return rc;
-  return backward_body(sh, cols, cols_lo, dy, weight, dx, dweight, dbias, ws, s);
+  return backward_body(sh, x, cols, cols_lo, dy, weight, dx, dweight, dbias, ws, s);
 }
 
 }  // namespace conv
@@ -461,6 +788,7 @@ ns_status ns_conv2d_fwd(const float* x, int B, int IC, int H, int W, const float
   rc = check_ws(sh, workspace, workspace_bytes, true, "ns_conv2d_fwd", &ws);
   if (rc != NS_OK) return rc;
   cudaStream_t s = as_stream(stream);
+  if (direct_fwd(sh)) return launch_direct_fwd(x, sh, weight, bias, y, s);
   rc = launch_im2col(x, sh, ws.cols, ws.cols_lo, s);
   if (rc != NS_OK) return rc;
   return forward_body(sh, weight, bias, y, ws.cols, ws.cols_lo, ws, s);
@@ -479,9 +807,11 @@ ns_status ns_conv2d_bwd(const float* x, const float* dy, int B, int IC, int H, i
   Ws ws;
   rc = check_ws(sh, workspace, workspace_bytes, true, "ns_conv2d_bwd", &ws);
   if (rc != NS_OK) return rc;
-  rc = launch_im2col(x, sh, ws.cols, ws.cols_lo, s);
-  if (rc != NS_OK) return rc;
-  return backward_body(sh, ws.cols, ws.cols_lo, dy, weight, dx, dweight, dbias, ws, s);
+  if (!direct_dw(sh)) {
+    rc = launch_im2col(x, sh, ws.cols, ws.cols_lo, s);
+    if (rc != NS_OK) return rc;
+  }
+  return backward_body(sh, x, ws.cols, ws.cols_lo, dy, weight, dx, dweight, dbias, ws, s);
 }
 
 }  // extern "C"

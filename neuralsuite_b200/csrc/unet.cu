@@ -89,31 +89,30 @@ __global__ void relu_mask_k(const float* dy, const float* __restrict__ y, int64_
     dsum[i] = y[i] > 0.0f ? dy[i] : 0.0f;
 }
 
-// y[bc][i][j] = x[bc][i/2][j/2].
-__global__ void up2_k(const float* __restrict__ x, int64_t BC, int H, int W, float* __restrict__ y) {
-  const int64_t n = BC * 4 * H * W;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int j = (int)(i % (2 * W)), r = (int)((i / (2 * W)) % (2 * H));
-    const int64_t bc = i / (4 * (int64_t)H * W);
-    y[i] = x[(bc * H + r / 2) * W + j / 2];
+// y[bc][i][j] = x[bc][i/2][j/2]: one thread per input element writes its
+// 2 x 2 block as two 8-byte stores (32-bit indexing: n < 2^31).
+__global__ void up2_k(const float* __restrict__ x, int n, int W, float* __restrict__ y) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int row = i / W, j = i - row * W;  // row = bc * H + r
+    const float v = x[i];
+    float* o = y + (size_t)row * 4 * W + 2 * j;  // output row 2r of plane bc
+    *reinterpret_cast<float2*>(o) = make_float2(v, v);
+    *reinterpret_cast<float2*>(o + 2 * W) = make_float2(v, v);
   }
 }
 
 // dx[bc][i][j] = dy[2i][2j] + dy[2i][2j+1] + dy[2i+1][2j] + dy[2i+1][2j+1], in that order.
-__global__ void up2_bwd_k(const float* __restrict__ dy, int64_t BC, int H, int W,
-                          float* __restrict__ dx) {
-  const int64_t n = BC * H * W;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int j = (int)(i % W), r = (int)((i / W) % H);
-    const int64_t bc = i / ((int64_t)H * W);
-    const float* p = dy + ((bc * 2 * H + 2 * r) * 2 * W + 2 * j);
+__global__ void up2_bwd_k(const float* __restrict__ dy, int n, int W, float* __restrict__ dx) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int row = i / W, j = i - row * W;
+    const float* p = dy + (size_t)row * 4 * W + 2 * j;
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    const float2 b = *reinterpret_cast<const float2*>(p + 2 * W);
     float s = 0.0f;
-    s += p[0];
-    s += p[1];
-    s += p[2 * W];
-    s += p[2 * W + 1];
+    s += a.x;
+    s += a.y;
+    s += b.x;
+    s += b.y;
     dx[i] = s;
   }
 }
@@ -167,11 +166,12 @@ ns_status conv_fwd(ns_unet* u, int i, const float* in, float* out, int B, cudaSt
                             u->conv_ws, u->conv_ws_bytes, s);
 }
 
-// The backward of conv i on the columns its forward kept (its input is not
-// read again).
-ns_status conv_bwd(ns_unet* u, int i, const float* dy, float* dx, int B, cudaStream_t s) {
+// The backward of conv i on the columns its forward kept (its input `in` is
+// read again only by the direct paths of the 3-channel convolutions).
+ns_status conv_bwd(ns_unet* u, int i, const float* in, const float* dy, float* dx, int B,
+                   cudaStream_t s) {
   const auto& c = u->conv[i];
-  return conv::backward_from_cols(c.cols, c.cols_lo, dy, B, c.ic, c.in_hw, c.in_hw,
+  return conv::backward_from_cols(in, c.cols, c.cols_lo, dy, B, c.ic, c.in_hw, c.in_hw,
                                   u->params + c.w_off, c.oc, 3, c.stride, 1, dx,
                                   u->grads + c.w_off, u->grads + c.b_off, u->conv_ws,
                                   u->conv_ws_bytes, s);
@@ -207,7 +207,7 @@ ns_status res_ln_bwd(ns_unet* u, int l, const float* de, float* da, int B, cudaS
   relu_mask_k<<<grid_for(n), 256, 0, s>>>(u->t1, u->r[l], n, u->t1);
   rc = check_launch("ns_unet relu backward");
   if (rc != NS_OK) return rc;
-  rc = conv_bwd(u, 6 + l, u->t1, u->t2, B, s);
+  rc = conv_bwd(u, 6 + l, u->a[l], u->t1, u->t2, B, s);
   if (rc != NS_OK) return rc;
   return ns_add(u->t2, u->t1, da, n, s);  // dinput = dfx + dsum (residual.h:50-55)
 }
@@ -230,6 +230,9 @@ ns_status ns_unet_create(const ns_unet_config* cfg, ns_unet** out) {
   NS_REQUIRE(cfg && out, "ns_unet_create: NULL argument");
   NS_REQUIRE(cfg->in_channels > 0 && cfg->base_channels > 0 && cfg->max_batch > 0,
              "ns_unet_create: sizes must be positive");
+  NS_REQUIRE((int64_t)cfg->max_batch * 4 * cfg->base_channels * cfg->image_size * cfg->image_size <
+                 (int64_t(1) << 31),
+             "ns_unet_create: feature maps must stay below 2^31 floats");
   NS_REQUIRE(cfg->image_size >= 4 && cfg->image_size % 4 == 0,
              "ns_unet_create: image_size must be a positive multiple of 4");
   auto u = std::make_unique<ns_unet>();
@@ -361,7 +364,7 @@ ns_status ns_unet_forward(ns_unet* u, const float* x, int B, void* stream) {
   NS_REQUIRE(B >= 1 && B <= u->max_batch, "ns_unet_forward: B must be in [1, max_batch]");
   cudaStream_t s = as_stream(stream);
   u->B = B;
-  const int b = u->base, S = u->S;
+  const int S = u->S;
   NS_TRY_CUDA(cudaMemcpyAsync(u->x, x, (size_t)B * u->in_ch * S * S * sizeof(float),
                               cudaMemcpyDeviceToDevice, s),
               "ns_unet_forward input");
@@ -372,15 +375,15 @@ ns_status ns_unet_forward(ns_unet* u, const float* x, int B, void* stream) {
   if (rc == NS_OK) rc = conv_fwd(u, 2, u->e[1], u->a[2], B, s);          // down2
   if (rc == NS_OK) rc = res_ln_fwd(u, 2, B, s);                          // m
   if (rc != NS_OK) return rc;
-  up2_k<<<grid_for(level_numel(u, 2, B) * 4), 256, 0, s>>>(u->e[2], (int64_t)B * 4 * b, S / 4, S / 4,
-                                                           u->up_a);
+  up2_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->e[2], (int)level_numel(u, 2, B), S / 4,
+                                                       u->up_a);
   rc = check_launch("ns_unet upsample");
   if (rc == NS_OK) rc = conv_fwd(u, 3, u->up_a, u->t0, B, s);            // up1
   if (rc == NS_OK) rc = ns_add(u->t0, u->e[1], u->a[3], level_numel(u, 3, B), s);  // + e1
   if (rc == NS_OK) rc = res_ln_fwd(u, 3, B, s);                          // u1
   if (rc != NS_OK) return rc;
-  up2_k<<<grid_for(level_numel(u, 3, B) * 4), 256, 0, s>>>(u->e[3], (int64_t)B * 2 * b, S / 2, S / 2,
-                                                           u->up_b);
+  up2_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->e[3], (int)level_numel(u, 3, B), S / 2,
+                                                       u->up_b);
   rc = check_launch("ns_unet upsample");
   if (rc == NS_OK) rc = conv_fwd(u, 4, u->up_b, u->t0, B, s);            // up0
   if (rc == NS_OK) rc = ns_add(u->t0, u->e[0], u->a[4], level_numel(u, 4, B), s);  // + e0
@@ -406,31 +409,31 @@ ns_status ns_unet_backward(ns_unet* u, void* stream) {
   NS_REQUIRE(u, "ns_unet_backward: NULL argument");
   NS_REQUIRE(u->B > 0, "ns_unet_backward: no forward pass yet");
   cudaStream_t s = as_stream(stream);
-  const int B = u->B, b = u->base, S = u->S;
+  const int B = u->B, S = u->S;
   // The skip sums' gradients live in g0 / g1 until the encoder side adds
   // them; the other gradients reuse the e[] slots of values the backward has
   // already consumed (u0 after conv_out, u1 and m after their upsamples).
-  ns_status rc = conv_bwd(u, 5, u->dout, u->t0, B, s);                           // conv_out
+  ns_status rc = conv_bwd(u, 5, u->e[4], u->dout, u->t0, B, s);                  // conv_out
   if (rc == NS_OK) rc = res_ln_bwd(u, 4, u->t0, u->g0, B, s);                    // ds0
-  if (rc == NS_OK) rc = conv_bwd(u, 4, u->g0, u->t0, B, s);                      // up0
+  if (rc == NS_OK) rc = conv_bwd(u, 4, u->up_b, u->g0, u->t0, B, s);             // up0
   if (rc != NS_OK) return rc;
-  up2_bwd_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->t0, (int64_t)B * 2 * b, S / 2,
+  up2_bwd_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->t0, (int)level_numel(u, 3, B),
                                                            S / 2, u->e[3]);     // du1
   rc = check_launch("ns_unet upsample backward");
   if (rc == NS_OK) rc = res_ln_bwd(u, 3, u->e[3], u->g1, B, s);                  // ds1
-  if (rc == NS_OK) rc = conv_bwd(u, 3, u->g1, u->t0, B, s);                      // up1
+  if (rc == NS_OK) rc = conv_bwd(u, 3, u->up_a, u->g1, u->t0, B, s);             // up1
   if (rc != NS_OK) return rc;
-  up2_bwd_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->t0, (int64_t)B * 4 * b, S / 4,
+  up2_bwd_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->t0, (int)level_numel(u, 2, B),
                                                            S / 4, u->e[2]);     // dm
   rc = check_launch("ns_unet upsample backward");
   if (rc == NS_OK) rc = res_ln_bwd(u, 2, u->e[2], u->t0, B, s);                  // d a2
-  if (rc == NS_OK) rc = conv_bwd(u, 2, u->t0, u->t1, B, s);                      // down2
+  if (rc == NS_OK) rc = conv_bwd(u, 2, u->e[1], u->t0, u->t1, B, s);             // down2
   if (rc == NS_OK) rc = ns_add(u->t1, u->g1, u->e[3], level_numel(u, 1, B), s);    // de1
   if (rc == NS_OK) rc = res_ln_bwd(u, 1, u->e[3], u->t0, B, s);                  // d a1
-  if (rc == NS_OK) rc = conv_bwd(u, 1, u->t0, u->t1, B, s);                      // down1
+  if (rc == NS_OK) rc = conv_bwd(u, 1, u->e[0], u->t0, u->t1, B, s);             // down1
   if (rc == NS_OK) rc = ns_add(u->t1, u->g0, u->e[4], level_numel(u, 0, B), s);    // de0
   if (rc == NS_OK) rc = res_ln_bwd(u, 0, u->e[4], u->t0, B, s);                  // d a0
-  if (rc == NS_OK) rc = conv_bwd(u, 0, u->t0, nullptr, B, s);                    // conv_in
+  if (rc == NS_OK) rc = conv_bwd(u, 0, u->x, u->t0, nullptr, B, s);              // conv_in
   if (rc != NS_OK || !u->comm || u->world == 1) return rc;
   rc = comm::allreduce(u->comm, u->grads, u->n_params, s);
   if (rc == NS_OK) rc = comm::allreduce(u->comm, u->small, 1, s);

@@ -3,8 +3,9 @@
 the north-star tolerance with float64 adjudication of the elements that miss
 (oracle/fp64.conv2d_*).  Shapes: the reference test's odd sizes, 1x1 and
 5x5 kernels, stride 2 with padding 1 (the U-Net's down path), channel counts
-whose k*k*IC rows do not fill a tensor-core tile, and the diffusion U-Net's
-first levels at 64x64 (batch 32 per GPU).
+whose k*k*IC rows do not fill a tensor-core tile, few output channels or
+column rows (the direct CUDA-core paths, stride 1 and 2), and the diffusion
+U-Net's first levels and head at 64x64 (batch 32 per GPU).
 """
 import numpy as np
 import pytest
@@ -45,6 +46,8 @@ CASES = [
     (2, 16, 16, 16, 32, 3, 1, 1),
     (4, 64, 32, 32, 64, 3, 2, 1),
     (2, 3, 64, 64, 64, 3, 1, 1),
+    (3, 6, 10, 12, 3, 3, 2, 1),
+    (2, 64, 64, 64, 3, 3, 1, 1),
 ]
 
 
