@@ -12,21 +12,28 @@
 //  * the projections are split-K CUDA-core GEMVs (gemv_partial_k): each CTA
 //    streams a [K-chunk x 128-column] slab of the weight with 16-byte loads
 //    and applies it to all (up to 8) sequences at once; the partials are
-//    summed in a fixed order by gemv_finish_k, which also adds the bias and
-//    applies the residual add or the GELU of the layer (Linear::Forward,
-//    ElementwiseAdd, GeluForward order of operations);
+//    summed in a fixed order (split by split) by whichever kernel comes next;
 //  * attention is split over key chunks (dec_attn_partial_k: one CTA per
-//    sequence, head and chunk, an online softmax per warp) and merged by
-//    dec_attn_combine_k in chunk order, so results do not depend on timing;
+//    sequence, head and 64-position chunk, one position per lane for the
+//    scores, one head dimension per lane for the output); the chunks are
+//    merged in order, so results do not depend on timing;
+//  * kernels are fused where one only fed the next: c_attn's partial sums are
+//    finished together with the cache append (gemv_finish_append_k); the
+//    attention merge and the GELU of mlp_fc run in the prologue of the GEMV
+//    that reads them; each residual add runs with the following LayerNorm in
+//    one CTA per sequence (row_finish_ln_k): seven launches per block;
 //  * a prefill (ns_gpt_decoder_prefill) runs the batched training forward on
 //    the prompt (tensor cores) and copies each layer's K and V columns into
 //    the cache, which is what decoding the prompt token by token computes;
-//  * a step's ~160 small launches are one CUDA graph, captured once per
-//    (batch, output buffers) on a private stream and replayed: the position,
-//    the cached length and the tokens reach it through a small device state
-//    that one kernel fills before each replay, and the attention grid covers
-//    the whole cache (chunks past the cached length do nothing), so the same
-//    graph serves every step.
+//  * a step's ~90 launches are one CUDA graph, captured once per (batch,
+//    output buffers) on a private stream and replayed: the position, the
+//    cached length and the tokens reach it through a small device state that
+//    one kernel fills before each replay, and the attention grid covers the
+//    whole cache (chunks past the cached length do nothing), so the same graph
+//    serves every step.
+// The arithmetic of every fused piece is that of the separate pass it
+// replaces (Linear::Forward, ElementwiseAdd, GeluForward, LayerNormForward
+// order of operations); the LayerNorm's row sums are block reductions.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -46,8 +53,9 @@ struct ns_gpt_decoder {
   int B = 0, len = 0;  // sequences in the cache and cached positions per sequence
   float* kc = nullptr;  // [L][max_batch][H][cap][D]
   float* vc = nullptr;
-  float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *x1 = nullptr, *g = nullptr;
-  float *xf = nullptr, *logits = nullptr, *mean = nullptr, *rstd = nullptr, *part = nullptr;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *x1 = nullptr;
+  float *xf = nullptr, *logits = nullptr, *mean = nullptr, *rstd = nullptr;
+  float *part = nullptr, *part2 = nullptr;  // GEMV / attention partials, used in turn
   size_t part_floats = 0;
   int32_t* err = nullptr;
   int32_t* state = nullptr;  // device: [0] wpe position, [1] cached positions before the step
@@ -66,23 +74,114 @@ constexpr int kGvCols = 128;  // columns per CTA: 32 lanes x 4
 constexpr int kGvWarps = 8;
 constexpr int kGvRows = 8;    // sequences per CTA (more go to further grid.z slices)
 
-enum GvMode { kBias = 0, kBiasResid = 1, kBiasGelu = 2 };
+// Where a GEMV's input rows come from.  kInRows: X [B, K] as stored.  The
+// other two form the input in the GEMV's prologue from the previous step's
+// partial results, so the kernel that would have produced it is not launched:
+// kInAttention: the attention output, dec_attn_partial_k's chunks merged in
+// chunk order (max over the chunks that saw a key, normaliser and output
+// rescaled by e^(m - max), then output / normaliser; part [B*H][S][2 + D]);
+// kInGelu: gelu(bias[k] + the sum over splits s in order of part[s][b][k])
+// (part [S][B][K]).
+enum GvInMode { kInRows = 0, kInAttention = 1, kInGelu = 2 };
+struct GvIn {
+  int mode = kInRows;
+  const float* X = nullptr;
+  const float* part = nullptr;
+  int S = 0, H = 0, D = 0;
+  const float* bias = nullptr;
+};
+
+// sum over s = 0 .. splits-1, in order, of p[s * stride]; the loads of eight
+// splits are issued before their adds.
+__device__ __forceinline__ float sum_splits(const float* __restrict__ p, int splits,
+                                            size_t stride) {
+  float sum = 0.0f;
+  int s = 0;
+  for (; s + 8 <= splits; s += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = p[(size_t)(s + j) * stride];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += v[j];
+  }
+  for (; s < splits; ++s) sum += p[(size_t)s * stride];
+  return sum;
+}
+
+// W[k][n..n+3] as a float4 (zeros past N).
+__device__ __forceinline__ float4 load_w4(const float* __restrict__ wrow, int n, int N, int vec) {
+  if (vec && n + 3 < N) return __ldg(reinterpret_cast<const float4*>(wrow + n));
+  float4 w;
+  w.x = n < N ? wrow[n] : 0.0f;
+  w.y = n + 1 < N ? wrow[n + 1] : 0.0f;
+  w.z = n + 2 < N ? wrow[n + 2] : 0.0f;
+  w.w = n + 3 < N ? wrow[n + 3] : 0.0f;
+  return w;
+}
 
 // part[s][b][n] = sum over k in split s of X[b][k] * W[k][n].  grid: x =
 // column block, y = K split, z = group of 8 sequences.  Each warp takes every
 // 8th row of the split; the eight warps' sums are added in warp order.
-__global__ void __launch_bounds__(256) gemv_partial_k(const float* __restrict__ X, int B, int K,
+__global__ void __launch_bounds__(256) gemv_partial_k(GvIn in, int B, int K,
                                                       const float* __restrict__ W, int N, int kchunk,
                                                       int vec, float* __restrict__ part) {
   extern __shared__ float sm[];
   float* sx = sm;                          // [kGvRows][kchunk]
   float* red = sm + kGvRows * kchunk;      // [kGvWarps][kGvRows][kGvCols]
+  float* stats = red + kGvWarps * kGvRows * kGvCols;  // attention: [kGvRows][heads][2]
   const int n0 = blockIdx.x * kGvCols, s = blockIdx.y, b0 = blockIdx.z * kGvRows;
   const int k0 = s * kchunk, kc = min(K, k0 + kchunk) - k0;
   const int nb = min(kGvRows, B - b0);
-  for (int i = threadIdx.x; i < kGvRows * kchunk; i += blockDim.x) {
-    const int b = i / kchunk, k = i % kchunk;
-    sx[i] = (b < nb && k < kc) ? X[(size_t)(b0 + b) * K + k0 + k] : 0.0f;
+  if (in.mode == kInAttention) {
+    // Per (row, head) of this split: the merged maximum and normaliser.
+    const int h0 = k0 / in.D, nh = kc > 0 ? (k0 + kc - 1) / in.D - h0 + 1 : 0;
+    const int stride = 2 + in.D;
+    for (int i = threadIdx.x; i < nb * nh; i += blockDim.x) {
+      const int b = i / nh, h = h0 + i % nh;
+      const float* p = in.part + ((size_t)(b0 + b) * in.H + h) * in.S * stride;
+      float M = -INFINITY;
+      for (int c = 0; c < in.S; ++c)
+        if (p[(size_t)c * stride + 1] > 0.0f) M = fmaxf(M, p[(size_t)c * stride]);
+      float Lsum = 0.0f;
+      for (int c = 0; c < in.S; ++c) {
+        const float* pc = p + (size_t)c * stride;
+        if (pc[1] > 0.0f) Lsum += pc[1] * expf(pc[0] - M);
+      }
+      stats[2 * i] = M;
+      stats[2 * i + 1] = Lsum;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kGvRows * kchunk; i += blockDim.x) {
+      const int b = i / kchunk, k = i % kchunk;
+      float v = 0.0f;
+      if (b < nb && k < kc) {
+        const int kk = k0 + k, h = kk / in.D, d = kk - h * in.D;
+        const float M = stats[2 * (b * nh + h - h0)], Lsum = stats[2 * (b * nh + h - h0) + 1];
+        const float* p = in.part + ((size_t)(b0 + b) * in.H + h) * in.S * stride;
+        float od = 0.0f;
+        for (int c = 0; c < in.S; ++c) {
+          const float* pc = p + (size_t)c * stride;
+          if (pc[1] > 0.0f) od += pc[2 + d] * expf(pc[0] - M);
+        }
+        v = od / Lsum;
+      }
+      sx[i] = v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < kGvRows * kchunk; i += blockDim.x) {
+      const int b = i / kchunk, k = i % kchunk;
+      float v = 0.0f;
+      if (b < nb && k < kc) {
+        const int kk = k0 + k;
+        if (in.mode == kInRows) {
+          v = in.X[(size_t)(b0 + b) * K + kk];
+        } else {
+          const float sum = sum_splits(in.part + (size_t)(b0 + b) * K + kk, in.S, (size_t)B * K);
+          v = gelu_f(__fadd_rn(sum, in.bias[kk]));
+        }
+      }
+      sx[i] = v;
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -90,17 +189,25 @@ __global__ void __launch_bounds__(256) gemv_partial_k(const float* __restrict__ 
   float acc[kGvRows][4];
 #pragma unroll
   for (int b = 0; b < kGvRows; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.0f;
-  for (int k = warp; k < kc; k += kGvWarps) {
-    const float* wrow = W + (size_t)(k0 + k) * N;
-    float4 w;
-    if (vec && n + 3 < N) {
-      w = __ldg(reinterpret_cast<const float4*>(wrow + n));
-    } else {
-      w.x = n < N ? wrow[n] : 0.0f;
-      w.y = n + 1 < N ? wrow[n + 1] : 0.0f;
-      w.z = n + 2 < N ? wrow[n + 2] : 0.0f;
-      w.w = n + 3 < N ? wrow[n + 3] : 0.0f;
-    }
+  // Rows k = warp, warp + 8, ... in order; four rows' weights loaded first.
+  int k = warp;
+  for (; k + 3 * kGvWarps < kc; k += 4 * kGvWarps) {
+    float4 w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w[u] = load_w4(W + (size_t)(k0 + k + u * kGvWarps) * N, n, N, vec);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int b = 0; b < kGvRows; ++b) {
+        const float xv = sx[b * kchunk + k + u * kGvWarps];
+        acc[b][0] = fmaf(xv, w[u].x, acc[b][0]);
+        acc[b][1] = fmaf(xv, w[u].y, acc[b][1]);
+        acc[b][2] = fmaf(xv, w[u].z, acc[b][2]);
+        acc[b][3] = fmaf(xv, w[u].w, acc[b][3]);
+      }
+  }
+  for (; k < kc; k += kGvWarps) {
+    const float4 w = load_w4(W + (size_t)(k0 + k) * N, n, N, vec);
 #pragma unroll
     for (int b = 0; b < kGvRows; ++b) {
       const float xv = sx[b * kchunk + k];
@@ -125,18 +232,74 @@ __global__ void __launch_bounds__(256) gemv_partial_k(const float* __restrict__ 
   }
 }
 
-// out[b][n] = epilogue(sum over splits s in order of part[s][b][n] + bias[n]).
-__global__ void gemv_finish_k(const float* __restrict__ part, int splits, int B, int N,
-                              const float* __restrict__ bias, int mode,
-                              const float* __restrict__ resid, float* __restrict__ out) {
+// c_attn's finish: qkv[b][n] = (sum over splits in order of part) + bias[n],
+// and the K and V columns also to the cache at position state[1].
+__global__ void gemv_finish_append_k(const float* __restrict__ part, int splits, int B, int C,
+                                     const float* __restrict__ bias, float* __restrict__ qkv,
+                                     int H, int D, float* __restrict__ kc, float* __restrict__ vc,
+                                     int cap, const int32_t* __restrict__ state) {
+  const int N = 3 * C, idx = state[1];
   const int64_t total = (int64_t)B * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float sum = 0.0f;
-    for (int s = 0; s < splits; ++s) sum += part[(size_t)s * total + i];
-    const float v = __fadd_rn(sum, bias[i % N]);
-    out[i] = mode == kBiasResid ? __fadd_rn(resid[i], v) : mode == kBiasGelu ? gelu_f(v) : v;
+    const float sum = sum_splits(part + i, splits, (size_t)total);
+    const int b = (int)(i / N), n = (int)(i - (int64_t)b * N);
+    const float v = __fadd_rn(sum, bias[n]);
+    qkv[i] = v;
+    if (n >= C) {
+      const int c = n >= 2 * C ? n - 2 * C : n - C;
+      const int h = c / D, d = c - h * D;
+      const size_t dst = (((size_t)b * H + h) * cap + idx) * D + d;
+      (n >= 2 * C ? vc : kc)[dst] = v;
+    }
   }
+}
+
+// One row per CTA (kFinishThreads threads): x_out[b] = resid[b] + ((sum over
+// splits in order of part[s][b]) + bias) (Linear::Forward then
+// ElementwiseAdd), then h[b] = LayerNorm(x_out[b]) * gamma + beta
+// (src/tensor.cpp:290-315; the next layer's ln_1 or ln_2, or ln_f).  Dynamic
+// shared memory: C floats.
+constexpr int kFinishThreads = 1024;
+__global__ void __launch_bounds__(kFinishThreads) row_finish_ln_k(
+    const float* __restrict__ part, int splits, int B, int C, const float* __restrict__ bias,
+    const float* __restrict__ resid, float* __restrict__ x_out, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, float* __restrict__ h) {
+  extern __shared__ float row[];
+  __shared__ float wsum[kFinishThreads / 32];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  const int64_t total = (int64_t)B * C;
+  float s1 = 0.0f;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const size_t i = (size_t)b * C + c;
+    const float sum = sum_splits(part + i, splits, (size_t)total);
+    const float v = __fadd_rn(resid[i], __fadd_rn(sum, bias[c]));
+    x_out[i] = v;
+    row[c] = v;
+    s1 += v;
+  }
+  s1 = warp_sum(s1);
+  if (lane == 0) wsum[warp] = s1;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < nw; ++w) tot += wsum[w];
+  const float m = __fdiv_rn(tot, (float)C);
+  __syncthreads();
+  float q = 0.0f;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float d = row[c] - m;
+    q += d * d;
+  }
+  q = warp_sum(q);
+  if (lane == 0) wsum[warp] = q;
+  __syncthreads();
+  float qt = 0.0f;
+  for (int w = 0; w < nw; ++w) qt += wsum[w];
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(qt, (float)C) + eps));
+  for (int c = threadIdx.x; c < C; c += blockDim.x)
+    h[(size_t)b * C + c] =
+        __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(row[c], m), rs), gamma[c]), beta[c]);
 }
 
 // x[b] = wte[tok[b]] + wpe[pos] (GPTModel::ForwardWithKVCache's embedding add).
@@ -178,99 +341,88 @@ __global__ void dec_append_k(const float* __restrict__ qkv, int B, int nrows, in
 }
 
 // Partial attention of the query of sequence b, head h over cached keys
-// [s*kch, min(n, (s+1)*kch)), n = state[1] + 1: per warp an online softmax
-// (running max m, sum l, output o); the four warps merged in order.  part:
-// [B*H][S][2 + D] with S = gridDim.y chunks covering the whole cache; a
-// chunk past n writes l = 0, which the combine skips.
-constexpr int kAttThreads = 128;
+// [s*kch, min(n, (s+1)*kch)), n = state[1] + 1, kch = 32 * kAttWarps: each
+// warp takes 32 positions, one per lane (score = q . k over the head
+// dimension in order, the 32 scores' softmax by warp max and sum), then
+// accumulates p . V with one output dimension per lane; the warps' (m, l, o)
+// are merged in warp order.  part: [B*H][S][2 + D] with S = gridDim.y chunks
+// covering the whole cache; a chunk past n writes l = 0, which the merge in
+// the next GEMV skips.
+constexpr int kAttWarps = 2;
+constexpr int kAttThreads = 32 * kAttWarps;
 __global__ void __launch_bounds__(kAttThreads) dec_attn_partial_k(
     const float* __restrict__ qkv, int C, int H, int D, const float* __restrict__ kc,
     const float* __restrict__ vc, int cap, const int32_t* __restrict__ state, int kch, float scale,
     float* __restrict__ part) {
   const int n = state[1] + 1;
-  __shared__ float wm[4], wl[4];
-  __shared__ float wo[4][128];
+  __shared__ float qs[128];
+  __shared__ float wm[kAttWarps], wl[kAttWarps];
+  __shared__ float wo[kAttWarps][128];
   const int bh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
   const int b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* q = qkv + (size_t)b * 3 * C + h * D;
-  float qv[4], o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int d = lane + 32 * j;
-    qv[j] = d < D ? q[d] : 0.0f;
-    o[j] = 0.0f;
-  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = q[d];
+  __syncthreads();
   const float* kb = kc + ((size_t)b * H + h) * cap * D;
   const float* vb = vc + ((size_t)b * H + h) * cap * D;
-  const int t0 = s * kch, t1 = min(n, t0 + kch);
-  float m = -INFINITY, l = 0.0f;
-  for (int t = t0 + warp; t < t1; t += 4) {
+  const int t0 = s * kch + warp * 32, t1 = min(n, s * kch + kch);
+  const int t = t0 + lane;
+  float sc = -INFINITY;
+  if (t < t1) {
+    const float* kr = kb + (size_t)t * D;
     float dot = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = lane + 32 * j;
-      if (d < D) dot = fmaf(qv[j], kb[(size_t)t * D + d], dot);
+    if ((D & 3) == 0) {
+      for (int d = 0; d < D; d += 4) {
+        const float4 kv = __ldg(reinterpret_cast<const float4*>(kr + d));
+        dot = fmaf(qs[d], kv.x, dot);
+        dot = fmaf(qs[d + 1], kv.y, dot);
+        dot = fmaf(qs[d + 2], kv.z, dot);
+        dot = fmaf(qs[d + 3], kv.w, dot);
+      }
+    } else {
+      for (int d = 0; d < D; ++d) dot = fmaf(qs[d], __ldg(kr + d), dot);
     }
-    const float sc = warp_sum(dot) * scale;
-    const float mn = fmaxf(m, sc);
-    const float corr = expf(m - mn);
-    const float p = expf(sc - mn);
-    l = l * corr + p;
+    sc = dot * scale;
+  }
+  const float m = warp_max(sc);
+  const float p = (t < t1) ? expf(sc - m) : 0.0f;
+  const float l = warp_sum(p);
+  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int nv = min(32, max(0, t1 - t0));
+  for (int j = 0; j < nv; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, p, j);
+    const float* vr = vb + (size_t)(t0 + j) * D;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = lane + 32 * j;
-      o[j] = o[j] * corr + (d < D ? p * vb[(size_t)t * D + d] : 0.0f);
+    for (int i = 0; i < 4; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) o[i] = fmaf(pj, __ldg(vr + d), o[i]);
     }
-    m = mn;
   }
   if (lane == 0) {
     wm[warp] = m;
     wl[warp] = l;
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if (lane + 32 * j < D) wo[warp][lane + 32 * j] = o[j];
+  for (int i = 0; i < 4; ++i)
+    if (lane + 32 * i < D) wo[warp][lane + 32 * i] = o[i];
   __syncthreads();
   float* dst = part + ((size_t)bh * S + s) * (2 + D);
   float M = -INFINITY;
-  for (int w = 0; w < 4; ++w)
+  for (int w = 0; w < kAttWarps; ++w)
     if (wl[w] > 0.0f) M = fmaxf(M, wm[w]);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float od = 0.0f;
-    for (int w = 0; w < 4; ++w)
+    for (int w = 0; w < kAttWarps; ++w)
       if (wl[w] > 0.0f) od += wo[w][d] * expf(wm[w] - M);
     dst[2 + d] = od;
   }
   if (threadIdx.x == 0) {
     float Lsum = 0.0f;
-    for (int w = 0; w < 4; ++w)
+    for (int w = 0; w < kAttWarps; ++w)
       if (wl[w] > 0.0f) Lsum += wl[w] * expf(wm[w] - M);
     dst[0] = M;
     dst[1] = Lsum;
-  }
-}
-
-// att[b][h*D + d] = (sum over chunks of o * e^(m - M)) / (sum of l * e^(m - M)).
-__global__ void dec_attn_combine_k(const float* __restrict__ part, int S, int H, int D, int C,
-                                   float* __restrict__ att) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const float* p = part + (size_t)bh * S * (2 + D);
-  float M = -INFINITY;
-  for (int s = 0; s < S; ++s)
-    if (p[(size_t)s * (2 + D) + 1] > 0.0f) M = fmaxf(M, p[(size_t)s * (2 + D)]);
-  float Lsum = 0.0f;
-  for (int s = 0; s < S; ++s) {
-    const float* ps = p + (size_t)s * (2 + D);
-    if (ps[1] > 0.0f) Lsum += ps[1] * expf(ps[0] - M);
-  }
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float od = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      const float* ps = p + (size_t)s * (2 + D);
-      if (ps[1] > 0.0f) od += ps[2 + d] * expf(ps[0] - M);
-    }
-    att[(size_t)b * C + h * D + d] = od / Lsum;
   }
 }
 
@@ -338,40 +490,54 @@ size_t gv_part_floats(int B, int K, int N) {
   return (size_t)p.splits * B * N;
 }
 
-ns_status gemv(ns_gpt_decoder* d, const float* X, int B, int K, const float* W, int N,
-               const float* bias, int mode, const float* resid, float* out, cudaStream_t s) {
+// Partials of one GEMV into `part`; its input rows as `in` says.
+ns_status gemv_part(ns_gpt_decoder* d, const GvIn& in, int B, int K, const float* W, int N,
+                    float* part, int* splits, cudaStream_t s) {
   const GvPlan p = gv_plan(K, N);
   if ((size_t)p.splits * B * N > d->part_floats) return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small");
   const int vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
-  const size_t smem = (size_t)(kGvRows * p.kchunk + kGvWarps * kGvRows * kGvCols) * sizeof(float);
+  const int heads = in.mode == kInAttention ? p.kchunk / in.D + 2 : 0;
+  const size_t smem = (size_t)(kGvRows * p.kchunk + kGvWarps * kGvRows * kGvCols +
+                               2 * kGvRows * heads) * sizeof(float);
   if (smem > 48 * 1024)
     NS_TRY_CUDA(cudaFuncSetAttribute(gemv_partial_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "decode gemv attr");
   dim3 grid(p.cols, p.splits, (B + kGvRows - 1) / kGvRows);
-  gemv_partial_k<<<grid, 256, smem, s>>>(X, B, K, W, N, p.kchunk, vec, d->part);
-  ns_status rc = check_launch("decode gemv");
-  if (rc != NS_OK) return rc;
-  gemv_finish_k<<<grid_for((int64_t)B * N, 256), 256, 0, s>>>(d->part, p.splits, B, N, bias, mode,
-                                                              resid, out);
-  return check_launch("decode gemv finish");
+  gemv_partial_k<<<grid, 256, smem, s>>>(in, B, K, W, N, p.kchunk, vec, part);
+  *splits = p.splits;
+  return check_launch("decode gemv");
 }
 
-// Attention of the B current queries (in d->qkv) over the state[1] + 1
-// cached positions per sequence of layer l; the grid covers the whole cache.
-ns_status attend(ns_gpt_decoder* d, int l, int B, cudaStream_t s) {
+// Attention partials of the B current queries (in d->qkv) over the
+// state[1] + 1 cached positions per sequence of layer l, into `part`
+// ([B*H][S][2 + D], S chunks covering the whole cache); the next GEMV merges
+// them in its prologue.
+ns_status attend(ns_gpt_decoder* d, int l, int B, float* part, int* chunks, cudaStream_t s) {
   const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
-  const int kch = 64;
+  const int kch = 32 * kAttWarps;
   const int S = (d->cap + kch - 1) / kch;
   if ((size_t)B * d->H * S * (2 + d->D) > d->part_floats)
     return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small for attention");
   dim3 grid(B * d->H, S);
   dec_attn_partial_k<<<grid, kAttThreads, 0, s>>>(d->qkv, d->C, d->H, d->D, d->kc + l * per_layer,
                                                   d->vc + l * per_layer, d->cap, d->state, kch,
-                                                  1.0f / std::sqrt((float)d->D), d->part);
-  ns_status rc = check_launch("decode attention");
-  if (rc != NS_OK) return rc;
-  dec_attn_combine_k<<<B * d->H, 128, 0, s>>>(d->part, S, d->H, d->D, d->C, d->att);
-  return check_launch("decode attention combine");
+                                                  1.0f / std::sqrt((float)d->D), part);
+  *chunks = S;
+  return check_launch("decode attention");
+}
+
+// x_out = resid + (partials + bias); h = LayerNorm(x_out) with gamma, beta.
+ns_status row_finish_ln(ns_gpt_decoder* d, const float* part, int splits, int B,
+                        const float* bias, const float* resid, float* x_out, const float* gamma,
+                        const float* beta, float* h, cudaStream_t s) {
+  const size_t smem = (size_t)d->C * sizeof(float);
+  if (smem > 48 * 1024)
+    NS_TRY_CUDA(cudaFuncSetAttribute(row_finish_ln_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "decode finish attr");
+  const int threads = std::min(kFinishThreads, (d->C + 31) / 32 * 32);
+  row_finish_ln_k<<<B, threads, smem, s>>>(part, splits, B, d->C, bias, resid, x_out, gamma, beta,
+                                           1e-5f, h);
+  return check_launch("decode finish + LayerNorm");
 }
 
 // The step's inputs for the graph: its tokens and the state it reads.
@@ -397,31 +563,59 @@ ns_status enqueue_step(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaSt
   dec_embed_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->tok, B, prm(0), d->V, prm(1),
                                                            d->state, C, d->x, err);
   ns_status rc = check_launch("decode embedding");
-  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
+  // ln_1 of the first block; every later LayerNorm runs inside the finish of
+  // the GEMV before it.
+  if (rc == NS_OK && L > 0)
+    rc = ns_layernorm_fwd(d->x, prm(2), prm(3), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
+  float *p1 = d->part, *p2 = d->part2;
+  const int f = 2 + 12 * L;
   for (int l = 0; l < L && rc == NS_OK; ++l) {
     const int t = 2 + 12 * l;
-    // x1 = x + c_proj(attention(c_attn(ln_1(x))))
-    rc = ns_layernorm_fwd(d->x, prm(t), prm(t + 1), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
-    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 2), 3 * C, prm(t + 3), kBias, nullptr, d->qkv, s);
+    int splits = 0, chunks = 0;
+    // x1 = x + c_proj(attention(c_attn(h))), h = ln_1(x)
+    GvIn rows;
+    rows.X = d->h;
+    rc = gemv_part(d, rows, B, C, prm(t + 2), 3 * C, p1, &splits, s);
     if (rc == NS_OK) {
-      dec_append_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->qkv, B, 1, 1, C, d->H, d->D,
-                                                                 d->kc + l * per_layer,
-                                                                 d->vc + l * per_layer, d->cap, 0,
-                                                                 d->state);
-      rc = check_launch("decode cache append");
+      gemv_finish_append_k<<<grid_for((int64_t)B * 3 * C, 256), 256, 0, s>>>(
+          p1, splits, B, C, prm(t + 3), d->qkv, d->H, d->D, d->kc + l * (size_t)d->max_batch * d->H * d->cap * d->D,
+          d->vc + l * (size_t)d->max_batch * d->H * d->cap * d->D, d->cap, d->state);
+      rc = check_launch("decode qkv + cache append");
     }
-    if (rc == NS_OK) rc = attend(d, l, B, s);
-    if (rc == NS_OK) rc = gemv(d, d->att, B, C, prm(t + 4), C, prm(t + 5), kBiasResid, d->x, d->x1, s);
-    // x = x1 + mlp_proj(gelu(mlp_fc(ln_2(x1))))
+    if (rc == NS_OK) rc = attend(d, l, B, p2, &chunks, s);
+    if (rc == NS_OK) {
+      GvIn att;
+      att.mode = kInAttention;
+      att.part = p2;
+      att.S = chunks;
+      att.H = d->H;
+      att.D = d->D;
+      rc = gemv_part(d, att, B, C, prm(t + 4), C, p1, &splits, s);
+    }
+    // x1 and h = ln_2(x1)
     if (rc == NS_OK)
-      rc = ns_layernorm_fwd(d->x1, prm(t + 6), prm(t + 7), d->h, d->mean, d->rstd, B, C, 1e-5f, stream);
-    if (rc == NS_OK) rc = gemv(d, d->h, B, C, prm(t + 8), 4 * C, prm(t + 9), kBiasGelu, nullptr, d->g, s);
-    if (rc == NS_OK) rc = gemv(d, d->g, B, 4 * C, prm(t + 10), C, prm(t + 11), kBiasResid, d->x1, d->x, s);
+      rc = row_finish_ln(d, p1, splits, B, prm(t + 5), d->x, d->x1, prm(t + 6), prm(t + 7), d->h, s);
+    // x = x1 + mlp_proj(gelu(mlp_fc(h)))
+    if (rc == NS_OK) rc = gemv_part(d, rows, B, C, prm(t + 8), 4 * C, p2, &splits, s);
+    if (rc == NS_OK) {
+      GvIn gel;
+      gel.mode = kInGelu;
+      gel.part = p2;
+      gel.S = splits;
+      gel.bias = prm(t + 9);
+      rc = gemv_part(d, gel, B, 4 * C, prm(t + 10), C, p1, &splits, s);
+    }
+    // x and h = the next block's ln_1(x), or ln_f(x) after the last block
+    const int g = l + 1 < L ? t + 12 : f;
+    if (rc == NS_OK)
+      rc = row_finish_ln(d, p1, splits, B, prm(t + 11), d->x1, d->x, prm(g), prm(g + 1),
+                         l + 1 < L ? d->h : d->xf, s);
   }
   if (rc != NS_OK) return rc;
-  const int f = 2 + 12 * L;
-  rc = ns_layernorm_fwd(d->x, prm(f), prm(f + 1), d->xf, d->mean, d->rstd, B, C, 1e-5f, stream);
-  if (rc != NS_OK) return rc;
+  if (L == 0) {
+    rc = ns_layernorm_fwd(d->x, prm(f), prm(f + 1), d->xf, d->mean, d->rstd, B, C, 1e-5f, stream);
+    if (rc != NS_OK) return rc;
+  }
   const int vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(prm(0)) & 15) == 0);
   const size_t smem = (size_t)8 * C * sizeof(float);
   if (smem > 48 * 1024)
@@ -511,7 +705,8 @@ ns_status ns_gpt_decoder_create(ns_gpt* model, int max_batch, ns_gpt_decoder** o
   for (auto kn : {std::make_pair(C, 3 * C), std::make_pair(C, C), std::make_pair(C, 4 * C),
                   std::make_pair(4 * C, C)})
     part = std::max(part, gv_part_floats((int)Bm, (int)kn.first, (int)kn.second));
-  part = std::max(part, Bm * d->H * (size_t)((d->cap + 63) / 64) * (2 + d->D));
+  const int kch = 32 * kAttWarps;
+  part = std::max(part, Bm * d->H * (size_t)((d->cap + kch - 1) / kch) * (2 + d->D));
   d->part_floats = part;
   ns_status rc = NS_OK;
   auto A = [&](float** p, size_t n) {
@@ -522,14 +717,13 @@ ns_status ns_gpt_decoder_create(ns_gpt* model, int max_batch, ns_gpt_decoder** o
   A(&d->x, Bm * C);
   A(&d->h, Bm * C);
   A(&d->qkv, Bm * 3 * C);
-  A(&d->att, Bm * C);
   A(&d->x1, Bm * C);
-  A(&d->g, Bm * 4 * C);
   A(&d->xf, Bm * C);
   A(&d->logits, Bm * d->V);
   A(&d->mean, Bm);
   A(&d->rstd, Bm);
   A(&d->part, part);
+  A(&d->part2, part);
   if (rc == NS_OK) rc = dev_alloc(d, &d->err, 1);
   if (rc == NS_OK) rc = dev_alloc(d, &d->state, 2);
   if (rc == NS_OK) rc = dev_alloc(d, &d->tok, Bm);
