@@ -43,15 +43,16 @@ def parse():
                     help="skip the reference CPU leg (it costs ~1-2 min: samples + one full step)")
     ap.add_argument("--case", default="step",
                     choices=["step", "c1", "c2", "c3", "c5", "decode", "lstm", "gemm", "attn",
-                             "bw"],
+                             "bw", "conv"],
                     help="step: the training-step benchmark (default, the one-line contract); "
                          "c1 / c2 / c3: the 4-layer/128 step, the MatMul sweep, the "
                          "MultiHeadAttention layer at B8/T1024/H12, each beside the reference "
                          "on the host cores; c5: the diffusion U-Net step (data parallel under "
                          "torchrun); decode: KV-cache decoding of the 12-layer model; "
-                         "gemm / attn / bw: single-kernel cases for profilers")
+                         "gemm / attn / bw / conv: single-kernel cases for profilers")
     ap.add_argument("--shape", default="",
-                    help="gemm: M,N,K[,a_trans,b_trans]; attn: B,T,H,D; bw: M,C,V")
+                    help="gemm: M,N,K[,a_trans,b_trans]; attn: B,T,H,D; bw: M,C,V; "
+                         "conv: B,IC,H,W,OC,k,stride,pad")
     ap.add_argument("--reps", type=int, default=3, help="launches per kernel case")
     ap.add_argument("--engine", type=int, default=0, help="gemm / attn engine of the case")
     ap.add_argument("--epilogue", type=int, default=0, help="gemm case epilogue")
@@ -433,10 +434,25 @@ def run_ours(args, rank, world, local):
             exposed.append(x)
             span.append(y)
         model.set_comm_timing(False)
+        # the same steps with the communicator detached: each rank's step alone
+        model.set_comm(None, 1)
+        barrier()
+        torch.cuda.synchronize()
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for i in range(5):
+            model.train_step(dev_tok[i % n_batches], dev_tgt[i % n_batches], read_loss=False)
+        e3.record()
+        torch.cuda.synchronize()
+        local_ms = max_over_ranks(s3.elapsed_time(e3) / 5)
+        model.set_comm(comm, world)
         comm_info = {"exposed_ms": max_over_ranks(statistics.median(exposed)),
                      "allreduce_span_ms": max_over_ranks(statistics.median(span)),
+                     "local_step_ms": local_ms,
                      "how": "median of 5 extra steps, max over ranks; exposed = the compute "
-                            "stream's wait for the all-reduces after its own backward"}
+                            "stream's wait for the all-reduces after its own backward; "
+                            "local_step_ms = 5 more steps with the communicator detached "
+                            "(no all-reduce), mean, max over ranks"}
 
     dp = dp_checks(torch, dist, model, cfg, rank, world, n_batches) if world > 1 else None
 
@@ -936,6 +952,18 @@ def case_kernel(args, torch):
         out = {"case": "gemm", "mnk": [M, N, K], "a_trans": at, "b_trans": bt,
                "epilogue": args.epilogue, "presplit": args.presplit, "ms": ms,
                "tflops": 2.0 * M * N * K / ms / 1e9}
+    elif args.case == "conv":
+        Bc, IC, H, W, OC, kk, st, pd = shape[:8] if shape else (32, 64, 64, 64, 3, 3, 1, 1)
+        OH, OW = (H + 2 * pd - kk) // st + 1, (W + 2 * pd - kk) // st + 1
+        x = torch.randn(Bc, IC, H, W, device=dev)
+        w = torch.randn(OC, IC, kk, kk, device=dev) * 0.05
+        bias = torch.randn(OC, device=dev)
+        dy = torch.randn(Bc, OC, OH, OW, device=dev)
+        f = _event_ms(torch, lambda: nk.conv2d_fwd(x, w, bias, stride=st, pad=pd), args.reps, 0)
+        b = _event_ms(torch, lambda: nk.conv2d_bwd(x, dy, w, stride=st, pad=pd), args.reps, 0)
+        fl = 2.0 * OC * Bc * OH * OW * IC * kk * kk
+        out = {"case": "conv", "shape": [Bc, IC, H, W, OC, kk, st, pd], "fwd_ms": f, "bwd_ms": b,
+               "fwd_tflops": fl / f / 1e9, "bwd_tflops": 2 * fl / b / 1e9}
     elif args.case == "attn":
         Bc, Tc, H, D = shape[:4]
         qkv = torch.randn(Bc * Tc, 3 * H * D, device=dev)
