@@ -257,10 +257,9 @@ __global__ void __launch_bounds__(256) col2im_fixed_k(const float* __restrict__ 
 // (no columns) in fp32, with the reference's order where it has one, and
 // their operands staged in shared memory.
 constexpr int kDirectMaxOC = 4;     // output channels per thread (forward, dx, dW groups)
-constexpr int kDirectMaxTaps = 9;   // k x k <= 9 for the direct weight gradient
-constexpr int kDirectGroup = 16;    // input channels staged per round (forward)
+constexpr int kDirectGroup = 8;     // input channels staged per round (forward)
 constexpr int kDirectDxGroup = 16;  // input channels per CTA (dx)
-constexpr int kDirectSmemFloats = 24576;  // 96 KB of staged planes (dW)
+constexpr int kDirectSmemFloats = 49152;  // 192 KB of staged planes at most
 
 // Asynchronous global -> shared copies (cp.async): every copy of a staging
 // round is in flight at once, then one wait.  16-byte copies where both
@@ -288,209 +287,269 @@ __device__ __forceinline__ void stage(float* dst, const float* src, int n) {
   }
 }
 
-// Output rows per CTA of the direct forward (R * OW <= 256: one pixel per thread).
-__host__ __device__ inline int direct_rows(int OW, int OH) {
-  const int r = 256 / OW;
-  return r < 1 ? 1 : (r > OH ? OH : r);
-}
-// Input rows per CTA of the direct dx (R * W <= 512).
-__host__ __device__ inline int direct_dx_rows(int W, int H) {
-  const int r = 512 / W;
-  return r < 1 ? 1 : (r > H ? H : r);
+// The direct kernels work on kDirectPx consecutive pixels of one row per
+// thread (rows a multiple of kDirectPx long), with the window (KS x KS, 1 or
+// 3) and the channel count NOC (1..4) known at compile time and operands
+// staged in shared memory with zero halos (no bounds tests in the inner
+// loops).  The forward and dx keep the reference's operation order (separate
+// multiplies and adds; a tap outside the image contributes an exact +0), the
+// weight gradient uses FMA partial sums in a fixed order.
+constexpr int kDirectPx = 4;
+constexpr int kDirectThreads = 128;
+constexpr int kDirectPixels = kDirectThreads * kDirectPx;  // pixels per CTA
+
+// Rows per CTA: R * width = kDirectPixels (width divides it or R = 1).
+__host__ __device__ inline int direct_rows(int width, int height) {
+  const int r = kDirectPixels / width;
+  return r < 1 ? 1 : (r > height ? height : r);
 }
 
 // y[b][oc][oh][ow] = (sum over k = (ic*k + kh)*k + kw ascending of
-// W[oc][k] * x[b][ic][ih][iw]) + bias[oc]: MatMul's k-ascending sum with
-// separate multiplies and adds (src/tensor.cpp:236-257), then the bias
-// (conv2d.h:255-263).  A CTA computes R output rows of one image for every
-// channel, one pixel per thread, staging kDirectGroup input channels' rows
-// at a time (rows outside the image as zeros).
-__global__ void __launch_bounds__(256) conv_direct_fwd_k(const float* __restrict__ x, Shape sh,
-                                                         const float* __restrict__ w,
-                                                         const float* __restrict__ bias,
-                                                         float* __restrict__ y) {
+// W[oc][k] * x[b][ic][ih][iw]) + bias[oc] (the reference adds the bias after
+// the product, conv2d.h:255-263).  A CTA computes R output rows of one image,
+// staging kDirectGroup input channels' rows (with zero halos) per round and
+// every weight once.
+template <int KS, int NOC>
+__global__ void __launch_bounds__(kDirectThreads) conv_direct_fwd_k(
+    const float* __restrict__ x, Shape sh, const float* __restrict__ w,
+    const float* __restrict__ bias, float* __restrict__ y) {
   extern __shared__ __align__(16) float sm[];
-  const int R = direct_rows(sh.OW, sh.OH), nrows = (R - 1) * sh.s + sh.k;
-  const int kk2 = sh.k * sh.k, K = sh.IC * kk2, P = sh.OH * sh.OW;
-  const int rowlen = (sh.W + 3) & ~3;             // staged row pitch (16-byte rows)
-  float* xs = sm;                                   // [group][nrows][rowlen]
-  float* ws = sm + kDirectGroup * nrows * rowlen;   // [oc][K] (all weights)
+  const int R = direct_rows(sh.OW, sh.OH), nrows = (R - 1) * sh.s + KS;
+  const int pitch = sh.W + 2 * sh.p;          // staged row: p zeros | W values | p zeros
+  const int K = sh.IC * KS * KS, P = sh.OH * sh.OW;
+  float* xs = sm;                             // [group][nrows][pitch]
+  float* ws = sm + kDirectGroup * nrows * pitch;  // [oc][K]
   const int tiles = (sh.OH + R - 1) / R;
   const int b = blockIdx.x / tiles, oh0 = (blockIdx.x - b * tiles) * R;
   const int ih0 = oh0 * sh.s - sh.p;
-  const int npix = min(R, sh.OH - oh0) * sh.OW;
-  const int q = threadIdx.x, r = q / sh.OW, ow = q - r * sh.OW;
-  stage(ws, w, sh.OC * K);
-  float acc[kDirectMaxOC];
+  const int rows = min(R, sh.OH - oh0);
+  const int q0 = threadIdx.x * kDirectPx;     // this thread's first pixel of the tile
+  const int r = q0 / sh.OW, ow0 = q0 - r * sh.OW;
+  const bool active = r < rows;
+  for (int i = threadIdx.x; i < NOC * K; i += blockDim.x) ws[i] = __ldg(w + i);
+  float acc[kDirectPx][NOC];
 #pragma unroll
-  for (int o = 0; o < kDirectMaxOC; ++o) acc[o] = 0.0f;
+  for (int j = 0; j < kDirectPx; ++j)
+#pragma unroll
+    for (int o = 0; o < NOC; ++o) acc[j][o] = 0.0f;
+  constexpr int kSpan = (kDirectPx - 1) * 2 + KS;  // input values one row of taps reads (stride <= 2)
   for (int c0 = 0; c0 < sh.IC; c0 += kDirectGroup) {
     const int ng = min(kDirectGroup, sh.IC - c0);
     __syncthreads();  // the previous round's reads are done
-    for (int g = 0; g < ng; ++g)
-      for (int rr = threadIdx.x >> 5; rr < nrows; rr += blockDim.x >> 5) {
-        const int ih = ih0 + rr;
-        float* dst = xs + (g * nrows + rr) * rowlen;
-        if (ih >= 0 && ih < sh.H) {
-          const float* src = x + (((size_t)b * sh.IC + c0 + g) * sh.H + ih) * sh.W;
-          for (int c = threadIdx.x & 31; c < sh.W; c += 32) cp_async4(dst + c, src + c);
-        } else {
-          for (int c = threadIdx.x & 31; c < sh.W; c += 32) dst[c] = 0.0f;
-        }
+    const int nrow_all = ng * nrows;
+    for (int rr = threadIdx.x >> 5; rr < nrow_all; rr += blockDim.x >> 5) {
+      const int g = rr / nrows, ih = ih0 + (rr - g * nrows);
+      float* dst = xs + rr * pitch;
+      const bool in = ih >= 0 && ih < sh.H;
+      const float* src = x + (((size_t)b * sh.IC + c0 + g) * sh.H + (in ? ih : 0)) * sh.W;
+      for (int c = threadIdx.x & 31; c < pitch; c += 32) {
+        const int iw = c - sh.p;
+        if (in && iw >= 0 && iw < sh.W) cp_async4(dst + c, src + iw);
+        else dst[c] = 0.0f;
       }
+    }
     cp_async_wait_all();
     __syncthreads();
-    if (q < npix) {
-      for (int g = 0; g < ng; ++g)
-        for (int kh = 0; kh < sh.k; ++kh) {
-          const float* xr = xs + (g * nrows + r * sh.s + kh) * rowlen;
-          for (int kw = 0; kw < sh.k; ++kw) {
-            const int iw = ow * sh.s + kw - sh.p;
-            const float v = (iw >= 0 && iw < sh.W) ? xr[iw] : 0.0f;
-            const float* wt = ws + (c0 + g) * kk2 + kh * sh.k + kw;
+    if (active) {
+      for (int g = 0; g < ng; ++g) {
+        const float* wg = ws + (c0 + g) * KS * KS;
 #pragma unroll
-            for (int o = 0; o < kDirectMaxOC; ++o)
-              if (o < sh.OC) acc[o] = __fadd_rn(acc[o], __fmul_rn(wt[o * K], v));
+        for (int kh = 0; kh < KS; ++kh) {
+          const float* xr = xs + (g * nrows + r * sh.s + kh) * pitch + ow0 * sh.s;
+          float xv[kSpan];
+#pragma unroll
+          for (int u = 0; u < kSpan; ++u)
+            xv[u] = (u < (kDirectPx - 1) * sh.s + KS) ? xr[u] : 0.0f;
+#pragma unroll
+          for (int kw = 0; kw < KS; ++kw) {
+            float wv[NOC];
+#pragma unroll
+            for (int o = 0; o < NOC; ++o) wv[o] = wg[o * K + kh * KS + kw];
+#pragma unroll
+            for (int j = 0; j < kDirectPx; ++j) {
+              const float v = sh.s == 1 ? xv[j + kw] : xv[2 * j + kw];
+#pragma unroll
+              for (int o = 0; o < NOC; ++o) acc[j][o] = __fadd_rn(acc[j][o], __fmul_rn(wv[o], v));
+            }
           }
         }
+      }
     }
   }
-  if (q < npix) {
+  if (active) {
 #pragma unroll
-    for (int o = 0; o < kDirectMaxOC; ++o)
-      if (o < sh.OC) {
-        const float v = bias ? __fadd_rn(acc[o], __ldg(bias + o)) : acc[o];
-        y[((size_t)b * sh.OC + o) * P + oh0 * sh.OW + q] = v;
-      }
+    for (int o = 0; o < NOC; ++o) {
+      const float bv = bias ? __ldg(bias + o) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < kDirectPx; ++j)
+        y[((size_t)b * NOC + o) * P + (oh0 + r) * sh.OW + ow0 + j] =
+            bias ? __fadd_rn(acc[j][o], bv) : acc[j][o];
+    }
   }
 }
 
 // dx[b][ic][ih][iw] = sum over (kh, kw) in order of t(kh, kw), with
-// t = sum over oc ascending of W[oc][ic][kh][kw] * dy[b][oc][oh][ow] for each
-// window (oh, ow) = (ih + p - kh, iw + p - kw) inside the output: the
-// reference's dcols = W^T . dout (an oc-ascending MatMul sum) gathered by
-// Col2Im in (kh, kw) order (conv2d.h:321-324, 378-403).  Stride 1.  A CTA
-// takes R input rows of one image for kDirectDxGroup channels, with the dy
-// rows they read and their weights in shared memory.
-__global__ void __launch_bounds__(256) conv_direct_dx_k(const float* __restrict__ dy, Shape sh,
-                                                        const float* __restrict__ w,
-                                                        float* __restrict__ dx) {
+// t = sum over oc ascending of W[oc][ic][kh][kw] * dy[b][oc][ih + p - kh][iw + p - kw]
+// (zero outside the output): the reference's dcols = W^T . dout (an
+// oc-ascending MatMul sum) gathered by Col2Im in (kh, kw) order
+// (conv2d.h:321-324, 378-403).  Stride 1.
+// A CTA takes R input rows of one image for kDirectDxGroup channels: the dy
+// rows they read (zero halos) and their weights in shared memory, each
+// thread's dy values in registers across the channels.
+template <int KS, int NOC>
+__global__ void __launch_bounds__(kDirectThreads) conv_direct_dx_k(
+    const float* __restrict__ dy, Shape sh, const float* __restrict__ w, float* __restrict__ dx) {
   extern __shared__ __align__(16) float sm[];
-  const int R = direct_dx_rows(sh.W, sh.H), nrows = R + sh.k - 1;
-  const int kk2 = sh.k * sh.k, K = sh.IC * kk2, P = sh.OH * sh.OW;
-  float* ds = sm;                                // [oc][nrows][OW]
-  float* ws = sm + sh.OC * nrows * sh.OW;        // [oc][K] (all weights)
+  const int R = direct_rows(sh.W, sh.H), nrows = R + KS - 1;
+  const int halo = KS - 1 - sh.p;  // zeros left of column 0 (dy column ow at halo + ow)
+  const int pitch = sh.OW + 2 * (KS - 1);
+  const int K = sh.IC * KS * KS, P = sh.OH * sh.OW;
+  float* ds = sm;                                // [oc][nrows][pitch]
+  float* ws = sm + NOC * nrows * pitch;          // [oc][K]
   const int tiles = (sh.H + R - 1) / R, groups = (sh.IC + kDirectDxGroup - 1) / kDirectDxGroup;
   int t = blockIdx.x;
   const int grp = t % groups;
   t /= groups;
   const int tile = t % tiles, b = t / tiles;
   const int ih0 = tile * R, c0 = grp * kDirectDxGroup, ng = min(kDirectDxGroup, sh.IC - c0);
-  const int oh0 = ih0 + sh.p - (sh.k - 1);  // dy row held in smem row 0
-  stage(ws, w, sh.OC * K);
-  for (int i = threadIdx.x >> 5; i < sh.OC * nrows; i += blockDim.x >> 5) {
-    const int o = i / nrows, rr = i - o * nrows, oh = oh0 + rr;
-    float* dst = ds + i * sh.OW;
-    if (oh >= 0 && oh < sh.OH) {
-      const float* src = dy + ((size_t)b * sh.OC + o) * P + (size_t)oh * sh.OW;
-      for (int c = threadIdx.x & 31; c < sh.OW; c += 32) cp_async4(dst + c, src + c);
-    } else {
-      for (int c = threadIdx.x & 31; c < sh.OW; c += 32) dst[c] = 0.0f;
+  const int oh0 = ih0 + sh.p - (KS - 1);  // dy row held in smem row 0
+  for (int i = threadIdx.x; i < NOC * K; i += blockDim.x) ws[i] = __ldg(w + i);
+  for (int rr = threadIdx.x >> 5; rr < NOC * nrows; rr += blockDim.x >> 5) {
+    const int o = rr / nrows, oh = oh0 + (rr - o * nrows);
+    float* dst = ds + rr * pitch;
+    const bool in = oh >= 0 && oh < sh.OH;
+    const float* src = dy + ((size_t)b * NOC + o) * P + (size_t)(in ? oh : 0) * sh.OW;
+    for (int c = threadIdx.x & 31; c < pitch; c += 32) {
+      const int ow = c - halo;
+      if (in && ow >= 0 && ow < sh.OW) cp_async4(dst + c, src + ow);
+      else dst[c] = 0.0f;
     }
   }
   cp_async_wait_all();
   __syncthreads();
-  const int rows = min(R, sh.H - ih0), npix = rows * sh.W;
-  for (int item = threadIdx.x; item < ng * npix; item += blockDim.x) {
-    const int g = item / npix, q = item - g * npix;
-    const int r = q / sh.W, iw = q - r * sh.W, ih = ih0 + r;
-    float acc = 0.0f;
-    for (int kh = 0; kh < sh.k; ++kh) {
-      const int oh = ih + sh.p - kh;
-      if (oh < 0 || oh >= sh.OH) continue;
-      const int srow = oh - oh0;
-      for (int kw = 0; kw < sh.k; ++kw) {
-        const int ow = iw + sh.p - kw;
-        if (ow < 0 || ow >= sh.OW) continue;
-        const float* wt = ws + (c0 + g) * kk2 + kh * sh.k + kw;
-        float tv = 0.0f;
+  const int rows = min(R, sh.H - ih0);
+  const int q0 = threadIdx.x * kDirectPx;
+  const int r = q0 / sh.W, iw0 = q0 - r * sh.W;
+  if (r >= rows) return;
+  const int ih = ih0 + r;
+  // dy values of this thread's windows: row srow = r + KS - 1 - kh, columns
+  // halo + iw0 + j + p - kw = iw0 + j + (KS - 1 - kw) in the staged row.
+  constexpr int kSpan = kDirectPx + KS - 1;
+  float dv[NOC][KS][kSpan];
 #pragma unroll
-        for (int o = 0; o < kDirectMaxOC; ++o)
-          if (o < sh.OC)
-            tv = __fadd_rn(tv, __fmul_rn(wt[o * K], ds[(o * nrows + srow) * sh.OW + ow]));
-        acc += tv;
-      }
+  for (int o = 0; o < NOC; ++o)
+#pragma unroll
+    for (int kh = 0; kh < KS; ++kh) {
+      const float* row = ds + (o * nrows + r + KS - 1 - kh) * pitch + iw0;
+#pragma unroll
+      for (int u = 0; u < kSpan; ++u) dv[o][kh][u] = row[u];
     }
-    dx[(((size_t)b * sh.IC + c0 + g) * sh.H + ih) * sh.W + iw] = acc;
+  for (int g = 0; g < ng; ++g) {
+    const float* wg = ws + (c0 + g) * KS * KS;
+    float acc[kDirectPx];
+#pragma unroll
+    for (int j = 0; j < kDirectPx; ++j) acc[j] = 0.0f;
+#pragma unroll
+    for (int kh = 0; kh < KS; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < KS; ++kw) {
+        float wv[NOC];
+#pragma unroll
+        for (int o = 0; o < NOC; ++o) wv[o] = wg[o * K + kh * KS + kw];
+#pragma unroll
+        for (int j = 0; j < kDirectPx; ++j) {
+          float tv = 0.0f;
+#pragma unroll
+          for (int o = 0; o < NOC; ++o)
+            tv = __fadd_rn(tv, __fmul_rn(wv[o], dv[o][kh][j + KS - 1 - kw]));
+          acc[j] += tv;
+        }
+      }
+    float* out = dx + (((size_t)b * sh.IC + c0 + g) * sh.H + ih) * sh.W + iw0;
+#pragma unroll
+    for (int j = 0; j < kDirectPx; ++j) out[j] = acc[j];
   }
 }
 
 // part[(b * OC + oc) * K + (ic * k + kh) * k + kw] = sum over the positions
 // of image b of dy[b][oc][p] * x[b][ic][oh*s + kh - p][ow*s + kw - p]: one CTA
-// per (image, input channel, group of up to kDirectMaxOC output channels),
-// with the input plane and the group's dy planes in shared memory; each
-// thread sums a strided share of the positions, the threads' sums meet in a
-// fixed order (warp shuffles, then warps in order).
-__global__ void __launch_bounds__(256) conv_direct_dw_k(const float* __restrict__ x,
-                                                        const float* __restrict__ dy, Shape sh,
-                                                        float* __restrict__ part) {
+// per (image, input channel, group of NOC output channels), with the input
+// plane (zero halos) and the group's dy planes in shared memory; each thread
+// sums kDirectPx consecutive positions of a row at a time over a strided
+// share of the rows, the threads' sums meet in a fixed order (warp shuffles,
+// then warps in order).
+template <int KS, int NOC>
+__global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
+    const float* __restrict__ x, const float* __restrict__ dy, Shape sh,
+    float* __restrict__ part) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ float wred[8][kDirectMaxOC * kDirectMaxTaps];
-  const int HW = sh.H * sh.W, P = sh.OH * sh.OW, kk2 = sh.k * sh.k, K = sh.IC * kk2;
-  const int ogroups = (sh.OC + kDirectMaxOC - 1) / kDirectMaxOC;
+  __shared__ float wred[kDirectThreads / 32][NOC * KS * KS];
+  const int P = sh.OH * sh.OW, K = sh.IC * KS * KS;
+  const int ph = sh.H + 2 * sh.p, pw = sh.W + 2 * sh.p;  // padded plane
+  const int ogroups = sh.OC / NOC;
   int t = blockIdx.x;
   const int og = t % ogroups;
   t /= ogroups;
   const int ic = t % sh.IC, b = t / sh.IC;
-  const int o0 = og * kDirectMaxOC, no = min(kDirectMaxOC, sh.OC - o0);
-  const int hw4 = (HW + 3) & ~3;
-  float* xs = sm;         // [H*W]
-  float* ds = sm + hw4;   // [no][P]
-  stage(xs, x + ((size_t)b * sh.IC + ic) * HW, HW);
-  stage(ds, dy + ((size_t)b * sh.OC + o0) * P, no * P);
+  const int o0 = og * NOC;
+  float* xs = sm;                          // [ph][pw]
+  float* ds = sm + ((ph * pw + 3) & ~3);   // [NOC][P]
+  const float* xp = x + ((size_t)b * sh.IC + ic) * sh.H * sh.W;
+  for (int rr = threadIdx.x >> 5; rr < ph; rr += blockDim.x >> 5) {
+    const int ih = rr - sh.p;
+    const bool in = ih >= 0 && ih < sh.H;
+    for (int c = threadIdx.x & 31; c < pw; c += 32) {
+      const int iw = c - sh.p;
+      if (in && iw >= 0 && iw < sh.W) cp_async4(xs + rr * pw + c, xp + (size_t)ih * sh.W + iw);
+      else xs[rr * pw + c] = 0.0f;
+    }
+  }
+  stage(ds, dy + ((size_t)b * sh.OC + o0) * P, NOC * P);
   cp_async_wait_all();
   __syncthreads();
-  // Tap offsets of the window, once.
-  int tdh[kDirectMaxTaps], tdw[kDirectMaxTaps];
+  float acc[NOC][KS * KS];
 #pragma unroll
-  for (int tt = 0; tt < kDirectMaxTaps; ++tt) {
-    const int kh = tt / sh.k;
-    tdh[tt] = kh - sh.p;
-    tdw[tt] = tt - kh * sh.k - sh.p;
-  }
-  float acc[kDirectMaxOC * kDirectMaxTaps];
+  for (int o = 0; o < NOC; ++o)
 #pragma unroll
-  for (int j = 0; j < kDirectMaxOC * kDirectMaxTaps; ++j) acc[j] = 0.0f;
-  for (int q = threadIdx.x; q < P; q += blockDim.x) {
-    const int oh = q / sh.OW, ow = q - oh * sh.OW;
-    float g[kDirectMaxOC];
+    for (int tt = 0; tt < KS * KS; ++tt) acc[o][tt] = 0.0f;
+  constexpr int kSpan = (kDirectPx - 1) * 2 + KS;
+  for (int q0 = threadIdx.x * kDirectPx; q0 < P; q0 += blockDim.x * kDirectPx) {
+    const int oh = q0 / sh.OW, ow0 = q0 - oh * sh.OW;
+    float g[NOC][kDirectPx];
 #pragma unroll
-    for (int o = 0; o < kDirectMaxOC; ++o) g[o] = o < no ? ds[o * P + q] : 0.0f;
+    for (int o = 0; o < NOC; ++o)
 #pragma unroll
-    for (int tt = 0; tt < kDirectMaxTaps; ++tt) {
-      if (tt < kk2) {
-        const int ih = oh * sh.s + tdh[tt], iw = ow * sh.s + tdw[tt];
-        const float v = (ih >= 0 && ih < sh.H && iw >= 0 && iw < sh.W) ? xs[ih * sh.W + iw] : 0.0f;
+      for (int j = 0; j < kDirectPx; ++j) g[o][j] = ds[o * P + q0 + j];
 #pragma unroll
-        for (int o = 0; o < kDirectMaxOC; ++o) acc[o * kDirectMaxTaps + tt] = fmaf(g[o], v, acc[o * kDirectMaxTaps + tt]);
-      }
+    for (int kh = 0; kh < KS; ++kh) {
+      const float* xr = xs + (oh * sh.s + kh) * pw + ow0 * sh.s;
+      float xv[kSpan];
+#pragma unroll
+      for (int u = 0; u < kSpan; ++u) xv[u] = (u < (kDirectPx - 1) * sh.s + KS) ? xr[u] : 0.0f;
+#pragma unroll
+      for (int kw = 0; kw < KS; ++kw)
+#pragma unroll
+        for (int j = 0; j < kDirectPx; ++j) {
+          const float v = sh.s == 1 ? xv[j + kw] : xv[2 * j + kw];
+#pragma unroll
+          for (int o = 0; o < NOC; ++o) acc[o][kh * KS + kw] = fmaf(g[o][j], v, acc[o][kh * KS + kw]);
+        }
     }
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-  for (int j = 0; j < kDirectMaxOC * kDirectMaxTaps; ++j) {
-    const float v = warp_sum(acc[j]);
-    if (lane == 0) wred[warp][j] = v;
-  }
-  __syncthreads();
-  const int j = threadIdx.x;
-  if (j < kDirectMaxOC * kDirectMaxTaps) {
-    const int o = j / kDirectMaxTaps, tt = j - o * kDirectMaxTaps;
-    if (o < no && tt < kk2) {
-      float sum = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) sum += wred[w][j];
-      part[((size_t)b * sh.OC + o0 + o) * K + ic * kk2 + tt] = sum;
+  for (int o = 0; o < NOC; ++o)
+#pragma unroll
+    for (int tt = 0; tt < KS * KS; ++tt) {
+      const float v = warp_sum(acc[o][tt]);
+      if (lane == 0) wred[warp][o * KS * KS + tt] = v;
     }
+  __syncthreads();
+  for (int j = threadIdx.x; j < NOC * KS * KS; j += blockDim.x) {
+    const int o = j / (KS * KS), tt = j - o * KS * KS;
+    float sum = 0.0f;
+    for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) sum += wred[wi][j];
+    part[((size_t)b * sh.OC + o0 + o) * K + ic * KS * KS + tt] = sum;
   }
 }
 
@@ -506,18 +565,28 @@ __global__ void conv_direct_dw_finish_k(const float* __restrict__ part, int OC, 
   }
 }
 
+// Channels per thread of the direct weight gradient: the largest of 4..1
+// that divides OC.
+int direct_dw_noc(int OC) {
+  for (int n = kDirectMaxOC; n > 1; --n)
+    if (OC % n == 0) return n;
+  return 1;
+}
+
 // Shared memory of the direct kernels (floats).
 size_t direct_fwd_smem(const Shape& sh) {
   const int R = direct_rows(sh.OW, sh.OH);
-  return (size_t)kDirectGroup * ((R - 1) * sh.s + sh.k) * ((sh.W + 3) & ~3) +
+  return (size_t)kDirectGroup * ((R - 1) * sh.s + sh.k) * (sh.W + 2 * sh.p) +
          (size_t)sh.OC * sh.IC * sh.k * sh.k;
 }
 size_t direct_dx_smem(const Shape& sh) {
-  const int R = direct_dx_rows(sh.W, sh.H);
-  return (size_t)sh.OC * (R + sh.k - 1) * sh.OW + (size_t)sh.OC * sh.IC * sh.k * sh.k;
+  const int R = direct_rows(sh.W, sh.H);
+  return (size_t)sh.OC * (R + sh.k - 1) * (sh.OW + 2 * (sh.k - 1)) +
+         (size_t)sh.OC * sh.IC * sh.k * sh.k;
 }
 size_t direct_dw_smem(const Shape& sh) {
-  return (size_t)((sh.H * sh.W + 3) & ~3) + (size_t)kDirectMaxOC * sh.OH * sh.OW;
+  return (size_t)(((sh.H + 2 * sh.p) * (sh.W + 2 * sh.p) + 3) & ~3) +
+         (size_t)direct_dw_noc(sh.OC) * sh.OH * sh.OW;
 }
 
 int grid_runs(int64_t runs) {
@@ -528,20 +597,86 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 // Which products run on the direct CUDA-core paths instead of the GEMM: few
 // output channels (forward, dx, weight gradient) or few column rows (weight
-// gradient), small windows, and planes that fit the staging buffers.  A
-// direct forward implies a direct weight gradient, so no columns are needed.
+// gradient), 1x1 or 3x3 windows, stride 1 or 2 (dx: 1), rows a multiple of
+// kDirectPx long, and operands that fit the staging buffers.  A direct
+// forward implies a direct weight gradient, so no columns are needed.
+bool direct_window(const Shape& sh) { return (sh.k == 1 || sh.k == 3) && sh.s <= 2; }
 bool direct_dw(const Shape& sh) {
-  return (sh.OC <= kDirectMaxOC || sh.K() <= 32) && sh.k * sh.k <= kDirectMaxTaps &&
-         direct_dw_smem(sh) <= (size_t)kDirectSmemFloats;
+  return (sh.OC <= kDirectMaxOC || sh.K() <= 32) && direct_window(sh) &&
+         sh.OW % kDirectPx == 0 && direct_dw_smem(sh) <= (size_t)kDirectSmemFloats;
 }
 bool direct_fwd(const Shape& sh) {
-  return sh.OC <= kDirectMaxOC && sh.OW <= 256 && direct_dw(sh) &&
-         direct_fwd_smem(sh) * sizeof(float) <= 48 * 1024;
+  return sh.OC <= kDirectMaxOC && direct_dw(sh) && sh.OW <= kDirectPixels &&
+         direct_fwd_smem(sh) <= (size_t)kDirectSmemFloats;
 }
 bool direct_dx(const Shape& sh) {
-  return sh.OC <= kDirectMaxOC && sh.s == 1 && sh.W <= 512 &&
-         direct_dx_smem(sh) * sizeof(float) <= 48 * 1024;
+  return sh.OC <= kDirectMaxOC && direct_window(sh) && sh.s == 1 && sh.p <= sh.k - 1 &&
+         sh.W % kDirectPx == 0 && sh.W <= kDirectPixels &&
+         direct_dx_smem(sh) <= (size_t)kDirectSmemFloats;
 }
+
+// Launches a direct kernel instantiated for (KS, NOC).
+template <template <int, int> class Launch, typename... Args>
+ns_status direct_dispatch(int KS, int NOC, Args&&... args) {
+  switch (KS * 8 + NOC) {
+    case 1 * 8 + 1: return Launch<1, 1>::run(args...);
+    case 1 * 8 + 2: return Launch<1, 2>::run(args...);
+    case 1 * 8 + 3: return Launch<1, 3>::run(args...);
+    case 1 * 8 + 4: return Launch<1, 4>::run(args...);
+    case 3 * 8 + 1: return Launch<3, 1>::run(args...);
+    case 3 * 8 + 2: return Launch<3, 2>::run(args...);
+    case 3 * 8 + 3: return Launch<3, 3>::run(args...);
+    case 3 * 8 + 4: return Launch<3, 4>::run(args...);
+    default: return fail(NS_ERR_INVALID_ARGUMENT, "ns_conv2d: no direct kernel for this window");
+  }
+}
+
+template <typename K>
+ns_status set_smem(K kernel, size_t bytes, const char* what) {
+  if (bytes > 48 * 1024)
+    NS_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                what);
+  return NS_OK;
+}
+
+template <int KS, int NOC>
+struct DirectFwd {
+  static ns_status run(const float* x, const Shape& sh, const float* w, const float* bias,
+                       float* y, cudaStream_t s) {
+    const size_t smem = direct_fwd_smem(sh) * sizeof(float);
+    ns_status rc = set_smem(conv_direct_fwd_k<KS, NOC>, smem, "ns_conv2d_fwd direct");
+    if (rc != NS_OK) return rc;
+    const int R = direct_rows(sh.OW, sh.OH);
+    conv_direct_fwd_k<KS, NOC><<<sh.B * ((sh.OH + R - 1) / R), kDirectThreads, smem, s>>>(
+        x, sh, w, bias, y);
+    return check_launch("ns_conv2d_fwd direct");
+  }
+};
+template <int KS, int NOC>
+struct DirectDx {
+  static ns_status run(const float* dy, const Shape& sh, const float* w, float* dx,
+                       cudaStream_t s) {
+    const size_t smem = direct_dx_smem(sh) * sizeof(float);
+    ns_status rc = set_smem(conv_direct_dx_k<KS, NOC>, smem, "ns_conv2d_bwd direct dx");
+    if (rc != NS_OK) return rc;
+    const int R = direct_rows(sh.W, sh.H);
+    const int grid = sh.B * ((sh.H + R - 1) / R) * ((sh.IC + kDirectDxGroup - 1) / kDirectDxGroup);
+    conv_direct_dx_k<KS, NOC><<<grid, kDirectThreads, smem, s>>>(dy, sh, w, dx);
+    return check_launch("ns_conv2d_bwd direct dx");
+  }
+};
+template <int KS, int NOC>
+struct DirectDw {
+  static ns_status run(const float* x, const float* dy, const Shape& sh, float* part,
+                       cudaStream_t s) {
+    const size_t smem = direct_dw_smem(sh) * sizeof(float);
+    ns_status rc = set_smem(conv_direct_dw_k<KS, NOC>, smem, "ns_conv2d_bwd direct weight gradient");
+    if (rc != NS_OK) return rc;
+    conv_direct_dw_k<KS, NOC><<<sh.B * sh.IC * (sh.OC / NOC), kDirectThreads, smem, s>>>(
+        x, dy, sh, part);
+    return check_launch("ns_conv2d_bwd direct weight gradient");
+  }
+};
 
 ns_status make_shape(int B, int IC, int H, int W, int OC, int k, int stride, int pad, Shape* sh) {
   if (B < 0 || IC <= 0 || H <= 0 || W <= 0 || OC <= 0 || k <= 0 || stride <= 0 || pad < 0)
@@ -621,10 +756,7 @@ ns_status launch_im2col(const float* x, const Shape& sh, float* cols, float* col
 
 ns_status launch_direct_fwd(const float* x, const Shape& sh, const float* weight,
                             const float* bias, float* y, cudaStream_t s) {
-  const int R = direct_rows(sh.OW, sh.OH);
-  const int grid = sh.B * ((sh.OH + R - 1) / R);
-  conv_direct_fwd_k<<<grid, 256, direct_fwd_smem(sh) * sizeof(float), s>>>(x, sh, weight, bias, y);
-  return check_launch("ns_conv2d_fwd direct");
+  return direct_dispatch<DirectFwd>(sh.k, sh.OC, x, sh, weight, bias, y, s);
 }
 
 // The forward once the columns are in place: Yc = W . cols, then NCHW + bias.
@@ -669,14 +801,7 @@ ns_status backward_body(const Shape& sh, const float* x, const float* cols, cons
                     dweight, K, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ws.gemm,
                     ws.gemm_bytes, s);
   } else {
-    const size_t smem = direct_dw_smem(sh) * sizeof(float);
-    if (smem > 48 * 1024)
-      NS_TRY_CUDA(cudaFuncSetAttribute(conv_direct_dw_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem),
-                  "ns_conv2d_bwd direct weight gradient");
-    const int ogroups = (M + kDirectMaxOC - 1) / kDirectMaxOC;
-    conv_direct_dw_k<<<sh.B * sh.IC * ogroups, 256, smem, s>>>(x, dy, sh, ws.dw_part);
-    rc = check_launch("ns_conv2d_bwd direct weight gradient");
+    rc = direct_dispatch<DirectDw>(sh.k, direct_dw_noc(M), x, dy, sh, ws.dw_part, s);
     if (rc != NS_OK) return rc;
     conv_direct_dw_finish_k<<<grid_runs(ceil_div64((int64_t)M * K, 256)), 256, 0, s>>>(
         ws.dw_part, M, K, sh.B, dweight);
@@ -684,10 +809,7 @@ ns_status backward_body(const Shape& sh, const float* x, const float* cols, cons
   }
   if (rc != NS_OK || !dx) return rc;
   if (!gemm_dx) {
-    const int R = direct_dx_rows(sh.W, sh.H);
-    const int grid = sh.B * ((sh.H + R - 1) / R) * ((sh.IC + kDirectDxGroup - 1) / kDirectDxGroup);
-    conv_direct_dx_k<<<grid, 256, direct_dx_smem(sh) * sizeof(float), s>>>(dy, sh, weight, dx);
-    return check_launch("ns_conv2d_bwd direct dx");
+    return direct_dispatch<DirectDx>(sh.k, sh.OC, dy, sh, weight, dx, s);
   }
   rc = ns_split_lo(weight, M, K, K, ws.w_lo, s);
   if (rc != NS_OK) return rc;

@@ -47,6 +47,8 @@ CASES = [
     (4, 64, 32, 32, 64, 3, 2, 1),
     (2, 3, 64, 64, 64, 3, 1, 1),
     (3, 6, 10, 12, 3, 3, 2, 1),
+    (3, 6, 16, 16, 3, 3, 2, 1),
+    (2, 5, 12, 8, 2, 1, 1, 0),
     (2, 64, 64, 64, 3, 3, 1, 1),
 ]
 
