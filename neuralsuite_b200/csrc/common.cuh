@@ -34,6 +34,35 @@ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 int sm_count();  // multiprocessors of the current device (cached per device)
 
+// Programmatic dependent launch: a kernel launched by launch_pdl may be
+// scheduled while the kernel before it in the stream is still running, so it
+// must call pdl_wait() before it reads anything an earlier kernel wrote (the
+// wait returns once those kernels have finished and their writes are
+// visible); pdl_trigger() then lets the next kernel's CTAs be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+ns_status launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t s, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  count_launch();
+  return NS_OK;
+}
+
 }  // namespace nsb
 
 #define NS_TRY_CUDA(call, what)                          \

@@ -26,7 +26,10 @@
 //    the prompt (tensor cores) and copies each layer's K and V columns into
 //    the cache, which is what decoding the prompt token by token computes;
 //  * a step's ~90 launches are one CUDA graph, captured once per (batch,
-//    output buffers) on a private stream and replayed: the position, the
+//    output buffers) on a private stream and replayed, each kernel launched
+//    as a programmatic dependent of the one before (it starts while that one
+//    finishes, prefetching the weights or cached rows it will read into L2,
+//    and waits for it before reading its outputs): the position, the
 //    cached length and the tokens reach it through a small device state that
 //    one kernel fills before each replay, and the attention grid covers the
 //    whole cache (chunks past the cached length do nothing), so the same graph
@@ -91,6 +94,11 @@ struct GvIn {
   const float* bias = nullptr;
 };
 
+// L2 prefetch of the 128-byte line holding p (a hint: no fault, no data).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // sum over s = 0 .. splits-1, in order, of p[s * stride]; the loads of eight
 // splits are issued before their adds.
 __device__ __forceinline__ float sum_splits(const float* __restrict__ p, int splits,
@@ -132,6 +140,15 @@ __global__ void __launch_bounds__(256) gemv_partial_k(GvIn in, int B, int K,
   const int n0 = blockIdx.x * kGvCols, s = blockIdx.y, b0 = blockIdx.z * kGvRows;
   const int k0 = s * kchunk, kc = min(K, k0 + kchunk) - k0;
   const int nb = min(kGvRows, B - b0);
+  // Launched while the previous kernel finishes (launch_pdl): the weight
+  // slab does not depend on it, so it is brought toward L2 first.
+  {
+    const int n = n0 + (threadIdx.x & 31) * 4;
+    if (n < N)
+      for (int k = threadIdx.x >> 5; k < kc; k += kGvWarps) prefetch_l2(W + (size_t)(k0 + k) * N + n);
+  }
+  pdl_wait();
+  pdl_trigger();
   if (in.mode == kInAttention) {
     // Per (row, head) of this split: the merged maximum and normaliser.
     const int h0 = k0 / in.D, nh = kc > 0 ? (k0 + kc - 1) / in.D - h0 + 1 : 0;
@@ -238,6 +255,8 @@ __global__ void gemv_finish_append_k(const float* __restrict__ part, int splits,
                                      const float* __restrict__ bias, float* __restrict__ qkv,
                                      int H, int D, float* __restrict__ kc, float* __restrict__ vc,
                                      int cap, const int32_t* __restrict__ state) {
+  pdl_wait();
+  pdl_trigger();
   const int N = 3 * C, idx = state[1];
   const int64_t total = (int64_t)B * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -265,6 +284,8 @@ __global__ void __launch_bounds__(kFinishThreads) row_finish_ln_k(
     const float* __restrict__ part, int splits, int B, int C, const float* __restrict__ bias,
     const float* __restrict__ resid, float* __restrict__ x_out, const float* __restrict__ gamma,
     const float* __restrict__ beta, float eps, float* __restrict__ h) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float row[];
   __shared__ float wsum[kFinishThreads / 32];
   const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -306,6 +327,8 @@ __global__ void __launch_bounds__(kFinishThreads) row_finish_ln_k(
 __global__ void dec_embed_k(const int32_t* __restrict__ tok, int B, const float* __restrict__ wte,
                             int V, const float* __restrict__ wpe, const int32_t* __restrict__ state,
                             int C, float* __restrict__ x, int32_t* err) {
+  pdl_wait();
+  pdl_trigger();
   const int pos = state[0];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * C; i += gridDim.x * blockDim.x) {
     const int b = i / C, c = i % C;
@@ -354,13 +377,28 @@ __global__ void __launch_bounds__(kAttThreads) dec_attn_partial_k(
     const float* __restrict__ qkv, int C, int H, int D, const float* __restrict__ kc,
     const float* __restrict__ vc, int cap, const int32_t* __restrict__ state, int kch, float scale,
     float* __restrict__ part) {
-  const int n = state[1] + 1;
+  const int n = state[1] + 1;  // written before the step's graph was launched
   __shared__ float qs[128];
   __shared__ float wm[kAttWarps], wl[kAttWarps];
   __shared__ float wo[kAttWarps][128];
   const int bh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
   const int b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    // Launched while the previous kernel finishes (launch_pdl): the cached
+    // rows of this lane's position are brought toward L2 first (the newest
+    // one is being written; L2 is where that write lands).
+    const int tp = s * kch + warp * 32 + lane;
+    if (tp < min(n, s * kch + kch)) {
+      const size_t o = (((size_t)b * H + h) * cap + tp) * D;
+      for (int d = 0; d < D; d += 32) {
+        prefetch_l2(kc + o + d);
+        prefetch_l2(vc + o + d);
+      }
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
   const float* q = qkv + (size_t)b * 3 * C + h * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = q[d];
   __syncthreads();
@@ -433,6 +471,13 @@ __global__ void __launch_bounds__(256) dec_logits_k(const float* __restrict__ xf
                                                     float* __restrict__ logits) {
   extern __shared__ float sxf[];  // [8][C]
   const int b0 = blockIdx.y * 8, nb = min(8, B - b0);
+  {
+    const int v = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (v < V)
+      for (int c = (threadIdx.x & 31) * 32; c < C; c += 32 * 32) prefetch_l2(wte + (size_t)v * C + c);
+  }
+  pdl_wait();
+  pdl_trigger();
   for (int i = threadIdx.x; i < 8 * C; i += blockDim.x) {
     const int b = i / C;
     sxf[i] = b < nb ? xf[(size_t)(b0 + b) * C + i % C] : 0.0f;
@@ -503,9 +548,9 @@ ns_status gemv_part(ns_gpt_decoder* d, const GvIn& in, int B, int K, const float
     NS_TRY_CUDA(cudaFuncSetAttribute(gemv_partial_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "decode gemv attr");
   dim3 grid(p.cols, p.splits, (B + kGvRows - 1) / kGvRows);
-  gemv_partial_k<<<grid, 256, smem, s>>>(in, B, K, W, N, p.kchunk, vec, part);
   *splits = p.splits;
-  return check_launch("decode gemv");
+  return launch_pdl(gemv_partial_k, grid, dim3(256), smem, s, "decode gemv", in, B, K, W, N,
+                    p.kchunk, vec, part);
 }
 
 // Attention partials of the B current queries (in d->qkv) over the
@@ -519,11 +564,11 @@ ns_status attend(ns_gpt_decoder* d, int l, int B, float* part, int* chunks, cuda
   if ((size_t)B * d->H * S * (2 + d->D) > d->part_floats)
     return fail(NS_ERR_INVALID_ARGUMENT, "decode: partial buffer too small for attention");
   dim3 grid(B * d->H, S);
-  dec_attn_partial_k<<<grid, kAttThreads, 0, s>>>(d->qkv, d->C, d->H, d->D, d->kc + l * per_layer,
-                                                  d->vc + l * per_layer, d->cap, d->state, kch,
-                                                  1.0f / std::sqrt((float)d->D), part);
   *chunks = S;
-  return check_launch("decode attention");
+  return launch_pdl(dec_attn_partial_k, grid, dim3(kAttThreads), 0, s, "decode attention",
+                    (const float*)d->qkv, d->C, d->H, d->D, (const float*)(d->kc + l * per_layer),
+                    (const float*)(d->vc + l * per_layer), d->cap, (const int32_t*)d->state, kch,
+                    1.0f / std::sqrt((float)d->D), part);
 }
 
 // x_out = resid + (partials + bias); h = LayerNorm(x_out) with gamma, beta.
@@ -535,9 +580,8 @@ ns_status row_finish_ln(ns_gpt_decoder* d, const float* part, int splits, int B,
     NS_TRY_CUDA(cudaFuncSetAttribute(row_finish_ln_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "decode finish attr");
   const int threads = std::min(kFinishThreads, (d->C + 31) / 32 * 32);
-  row_finish_ln_k<<<B, threads, smem, s>>>(part, splits, B, d->C, bias, resid, x_out, gamma, beta,
-                                           1e-5f, h);
-  return check_launch("decode finish + LayerNorm");
+  return launch_pdl(row_finish_ln_k, dim3(B), dim3(threads), smem, s, "decode finish + LayerNorm",
+                    part, splits, B, d->C, bias, resid, x_out, gamma, beta, 1e-5f, h);
 }
 
 // The step's inputs for the graph: its tokens and the state it reads.
@@ -558,6 +602,7 @@ ns_status enqueue_step(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaSt
   const float* P = m.Values();
   const auto& off = m.Offsets();
   const int C = d->C, L = d->L;
+  const size_t per_layer = (size_t)d->max_batch * d->H * d->cap * d->D;
   void* stream = s;
   auto prm = [&](int i) { return P + off[i]; };
   dec_embed_k<<<grid_for((int64_t)B * C, 256), 256, 0, s>>>(d->tok, B, prm(0), d->V, prm(1),
@@ -577,10 +622,9 @@ ns_status enqueue_step(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaSt
     rows.X = d->h;
     rc = gemv_part(d, rows, B, C, prm(t + 2), 3 * C, p1, &splits, s);
     if (rc == NS_OK) {
-      gemv_finish_append_k<<<grid_for((int64_t)B * 3 * C, 256), 256, 0, s>>>(
-          p1, splits, B, C, prm(t + 3), d->qkv, d->H, d->D, d->kc + l * (size_t)d->max_batch * d->H * d->cap * d->D,
-          d->vc + l * (size_t)d->max_batch * d->H * d->cap * d->D, d->cap, d->state);
-      rc = check_launch("decode qkv + cache append");
+      rc = launch_pdl(gemv_finish_append_k, dim3(grid_for((int64_t)B * 3 * C, 256)), dim3(256), 0, s,
+                      "decode qkv + cache append", p1, splits, B, C, prm(t + 3), d->qkv, d->H, d->D,
+                      d->kc + l * per_layer, d->vc + l * per_layer, d->cap, d->state);
     }
     if (rc == NS_OK) rc = attend(d, l, B, p2, &chunks, s);
     if (rc == NS_OK) {
@@ -622,8 +666,8 @@ ns_status enqueue_step(ns_gpt_decoder* d, int B, float* lg, int32_t* err, cudaSt
     NS_TRY_CUDA(cudaFuncSetAttribute(dec_logits_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "decode logits attr");
   dim3 grid((d->V + 7) / 8, (B + 7) / 8);
-  dec_logits_k<<<grid, 256, smem, s>>>(d->xf, B, C, prm(0), d->V, vec, lg);
-  return check_launch("decode logits");
+  return launch_pdl(dec_logits_k, grid, dim3(256), smem, s, "decode logits", d->xf, B, C, prm(0),
+                    d->V, vec, lg);
 }
 
 // The instantiated step graph for (B, lg, err), captured on first use on
