@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(256) attn_delta_k(const float* __restrict__ ou
                                                     const float* __restrict__ dout, int B, int T,
                                                     int H, int D, float* __restrict__ delta,
                                                     float* __restrict__ dout_lo) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t row = blockIdx.x * 8 + (threadIdx.x >> 5);  // b * T + r
   const int lane = threadIdx.x & 31;
   if (row >= (int64_t)B * T) return;

@@ -198,6 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  // Launched as a programmatic dependent (launch_pdl): the set-up above ran
+  // while the previous kernel finished; its outputs are read only from here.
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
@@ -567,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // columns, compact (row stride 2C).  2C is a multiple of 4.
 __global__ void split_kv_lo_k(const float* __restrict__ qkv, int64_t rows, int C,
                               float* __restrict__ lo) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int c4 = (2 * C) >> 2;
   const int64_t total = rows * c4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -618,8 +623,8 @@ ns_status launch_fwd(const float* qkv, const float* qkv_lo, int B, int T, int H,
       return fail(NS_ERR_UNSUPPORTED, "ns_attn_fwd: kernel compiled with too few registers for its split");
   }
   const int grid = std::min(n_items, sm_count());
-  attn_fwd_tc_kernel<D><<<grid, kThreads, L::kDynSmem, s>>>(tq, tk, tklo, tv, tvlo, p);
-  return check_launch("ns_attn_fwd tcgen05");
+  return launch_pdl(attn_fwd_tc_kernel<D>, dim3(grid), dim3(kThreads), L::kDynSmem, s,
+                    "ns_attn_fwd tcgen05", tq, tk, tklo, tv, tvlo, p);
 }
 
 // ------------------------------------------------------------------ backward
@@ -846,6 +851,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  // Launched as a programmatic dependent (launch_pdl): the set-up above ran
+  // while the previous kernel finished; its outputs are read only from here.
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
@@ -1296,7 +1305,7 @@ __device__ void produce_kv(uint32_t ring, uint32_t full0, uint32_t empty0, const
         }
       }
       __syncwarp();
-      if (VEC > 0) {
+      if constexpr (VEC > 0) {
         float* vec = vecs + (g % VEC) * 2 * kBKV;
         for (int c = lane; c < kBKV; c += 32) {
           const int q = blk * kBKV + c;
@@ -1434,6 +1443,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  // Launched as a programmatic dependent (launch_pdl): the set-up above ran
+  // while the previous kernel finished; its outputs are read only from here.
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
@@ -1784,6 +1797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // stride ld, written compact (row stride cols).  cols and ld are multiples of 4.
 __global__ void split_lo_rows_k(const float* __restrict__ x, int64_t rows, int cols, int64_t ld,
                                 float* __restrict__ lo) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int c4 = cols >> 2;
   const int64_t total = rows * c4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1814,9 +1828,10 @@ ns_status launch_bwd_mode(const CUtensorMap* maps, const BwdParams& p, int B, in
   if (fa.numRegs < kMinLaunchRegs)
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_bwd: kernel compiled with too few registers for its split");
   const int grid = std::min(p.n_items, sm_count());
-  kern<<<grid, kThreads, L::kDynSmem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
-  return check_launch(MODE == kDV ? "ns_attn_bwd dV tcgen05"
-                                  : MODE == kDK ? "ns_attn_bwd dK tcgen05" : "ns_attn_bwd dQ tcgen05");
+  return launch_pdl(kern, dim3(grid), dim3(kThreads), L::kDynSmem, s,
+                    MODE == kDV ? "ns_attn_bwd dV tcgen05"
+                                : MODE == kDK ? "ns_attn_bwd dK tcgen05" : "ns_attn_bwd dQ tcgen05",
+                    maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
 }
 
 template <int D>
@@ -1830,8 +1845,8 @@ ns_status launch_bwd_kv(const CUtensorMap* m, const BwdParams& p, cudaStream_t s
   if (fa.numRegs < kMinLaunchRegs)
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_bwd: kernel compiled with too few registers for its split");
   const int grid = std::min(p.n_items, sm_count());
-  kern<<<grid, kThreads, L::kDynSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], p);
-  return check_launch("ns_attn_bwd dK+dV tcgen05");
+  return launch_pdl(kern, dim3(grid), dim3(kThreads), L::kDynSmem, s, "ns_attn_bwd dK+dV tcgen05",
+                    m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], p);
 }
 
 template <int D>

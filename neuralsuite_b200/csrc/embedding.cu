@@ -20,6 +20,7 @@ __global__ void __launch_bounds__(256) emb_fwd_k(const int32_t* __restrict__ tok
                                                  const float* __restrict__ wpe, int dim,
                                                  float* __restrict__ out,
                                                  int32_t* __restrict__ err) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   // blockDim.x = 256: 8 warps, one row each; lanes stride the columns.
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;

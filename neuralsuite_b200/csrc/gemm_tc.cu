@@ -829,6 +829,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
 // tensor core reads from a tf32 operand, so hi + lo == x exactly.
 __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int ld,
                            float* __restrict__ lo, int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t total = (int64_t)rows * cols;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (vec) {
@@ -858,6 +859,7 @@ __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int 
 // own stores cannot issue those loads efficiently.  Same operations, same
 // order as the fused epilogue.
 __global__ void epi_apply_k(int M, int N, const EpiArgs e_param, int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const EpiArgs e = e_param;
   const int64_t total = (int64_t)M * N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -878,6 +880,7 @@ __global__ void epi_apply_k(int M, int N, const EpiArgs e_param, int vec) {
 // Ordered sum of the split-K partial tiles, then the epilogue.
 __global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M, int N,
                                 const EpiArgs e_param, int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const EpiArgs e = e_param;  // in registers, not re-read from parameter space
   const int64_t total = (int64_t)M * N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1085,6 +1088,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
   __syncthreads();
   cluster_sync();  // both CTAs' barriers initialised before any remote arrive
   fence_after();
+  // Launched as a programmatic dependent (launch_pdl): the set-up above ran
+  // while the previous kernel finished; global memory is touched only from here.
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const int unit0 = (int)cluster_id_x(), unit_step = (int)cluster_count_x();
 
@@ -1349,8 +1356,8 @@ ns_status launch_pair_bn(const Plan& pl, const CUtensorMap& ta, const CUtensorMa
   NS_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_pair_kernel<BN>), "ns_gemm attributes");
   if (fa.numRegs < kWideMinLaunchRegs)
     return fail(NS_ERR_UNSUPPORTED, "ns_gemm: pair kernel compiled with too few registers for its split");
-  gemm_pair_kernel<BN><<<2 * pl.grid, kWideThreads, L::kDynSmem, s>>>(ta, tb, ta_lo, tb_lo, kp);
-  return check_launch("ns_gemm tcgen05 pair");
+  return launch_pdl(gemm_pair_kernel<BN>, dim3(2 * pl.grid), dim3(kWideThreads), L::kDynSmem, s,
+                    "ns_gemm tcgen05 pair", ta, tb, ta_lo, tb_lo, kp);
 }
 
 ns_status launch_pair(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias 
                                                   float eps, const float* __restrict__ bias,
                                                   const float* __restrict__ resid, float* x_out,
                                                   float* __restrict__ out_lo) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_vec(
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
     float* __restrict__ part_b, int rows, int dim, int rows_per_cta) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ float red[];  // [kRowsWarps][2][dim]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = dim >> 2;
@@ -316,6 +318,7 @@ __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ p
                                                      int N, float* __restrict__ out,
                                                      const float* __restrict__ part2,
                                                      float* __restrict__ out2) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float red[kRowsWarps][32];
   if (blockIdx.y == 1) {
     part = part2;
@@ -364,6 +367,7 @@ __global__ void __launch_bounds__(256) colsum_partial(float* __restrict__ y, int
                                                       const float* __restrict__ pre,
                                                       int* __restrict__ done,
                                                       float* __restrict__ out) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float4 red[kRowsWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = (blockIdx.x * 32 + lane) * 4;

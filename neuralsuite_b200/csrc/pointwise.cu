@@ -31,6 +31,7 @@ __global__ void gelu_fwd_k(const float* __restrict__ x, float* __restrict__ y, i
 // y = gelu(x) and y_lo = y - trunc_tf32(y) (the next GEMM's operand split).
 __global__ void gelu_fwd_lo_k(const float* __restrict__ x, float* __restrict__ y,
                               float* __restrict__ y_lo, int64_t n) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   auto lo = [](float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); };
@@ -86,6 +87,7 @@ __global__ void __launch_bounds__(256) ce_rows_k(const float* __restrict__ logit
                                                  float* __restrict__ dlogits,
                                                  float* __restrict__ row_loss,
                                                  int32_t* __restrict__ err) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
