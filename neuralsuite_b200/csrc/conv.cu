@@ -53,6 +53,7 @@ __device__ __forceinline__ float lo_of(float x) {
 __global__ void __launch_bounds__(256) im2col_k(const float* __restrict__ x, Shape sh,
                                                 float* __restrict__ cols,
                                                 float* __restrict__ cols_lo, int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW, K = sh.IC * sh.k * sh.k, kk2 = sh.k * sh.k;
   const int64_t N = sh.N(), runs = (int64_t)K * sh.B;
   for (int64_t r = blockIdx.x; r < runs; r += gridDim.x) {
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(256) cnhw_to_nchw_bias_k(const float* __restri
                                                            const float* __restrict__ bias,
                                                            Shape sh, float* __restrict__ y,
                                                            int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW;
   const int64_t runs = (int64_t)sh.B * sh.OC;
   for (int64_t r = blockIdx.x; r < runs; r += gridDim.x) {
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(256) cnhw_to_nchw_bias_k(const float* __restri
 __global__ void __launch_bounds__(256) nchw_to_cnhw_k(const float* __restrict__ dy, Shape sh,
                                                       float* __restrict__ dyc,
                                                       float* __restrict__ dyc_lo, int vec) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW;
   const int64_t runs = (int64_t)sh.B * sh.OC;
   for (int64_t r = blockIdx.x; r < runs; r += gridDim.x) {
@@ -152,6 +155,7 @@ __global__ void __launch_bounds__(256) nchw_to_cnhw_k(const float* __restrict__ 
 // (one CTA per image and channel; blockDim 256).
 __global__ void __launch_bounds__(256) bias_part_k(const float* __restrict__ dy, Shape sh,
                                                    float* __restrict__ part) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float red[256];
   const int oc = blockIdx.x, b = blockIdx.y;
   const int64_t P = sh.P();
@@ -170,6 +174,7 @@ __global__ void __launch_bounds__(256) bias_part_k(const float* __restrict__ dy,
 // db[oc] = the per-image sums added in image order (conv2d.h:326-331).
 __global__ void bias_finish_k(const float* __restrict__ part, int OC, int B,
                               float* __restrict__ db) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int oc = blockIdx.x * blockDim.x + threadIdx.x;
   if (oc >= OC) return;
   float total = 0.0f;
@@ -184,6 +189,7 @@ __global__ void bias_finish_k(const float* __restrict__ part, int OC, int B,
 // term is a coalesced read of one column row.
 __global__ void __launch_bounds__(256) col2im_k(const float* __restrict__ dcols, Shape sh,
                                                 float* __restrict__ dx) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int HW = sh.H * sh.W, P = sh.OH * sh.OW;
   const int64_t N = sh.N(), planes = (int64_t)sh.B * sh.IC;
   for (int64_t r = blockIdx.x; r < planes; r += gridDim.x) {
@@ -219,6 +225,7 @@ __global__ void __launch_bounds__(256) col2im_k(const float* __restrict__ dcols,
 template <int KS, int ST>
 __global__ void __launch_bounds__(256) col2im_fixed_k(const float* __restrict__ dcols, Shape sh,
                                                       float* __restrict__ dx) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int HW = sh.H * sh.W, P = sh.OH * sh.OW;
   const int64_t N = sh.N(), planes = (int64_t)sh.B * sh.IC;
   for (int64_t r = blockIdx.x; r < planes; r += gridDim.x) {
@@ -313,6 +320,7 @@ template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_fwd_k(
     const float* __restrict__ x, Shape sh, const float* __restrict__ w,
     const float* __restrict__ bias, float* __restrict__ y) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   const int R = direct_rows(sh.OW, sh.OH), nrows = (R - 1) * sh.s + KS;
   const int pitch = sh.W + 2 * sh.p;          // staged row: p zeros | W values | p zeros
@@ -399,6 +407,7 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_fwd_k(
 template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_dx_k(
     const float* __restrict__ dy, Shape sh, const float* __restrict__ w, float* __restrict__ dx) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   const int R = direct_rows(sh.W, sh.H), nrows = R + KS - 1;
   const int halo = KS - 1 - sh.p;  // zeros left of column 0 (dy column ow at halo + ow)
@@ -482,6 +491,7 @@ template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
     const float* __restrict__ x, const float* __restrict__ dy, Shape sh,
     float* __restrict__ part) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   __shared__ float wred[kDirectThreads / 32][NOC * KS * KS];
   const int P = sh.OH * sh.OW, K = sh.IC * KS * KS;
@@ -556,6 +566,7 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
 // dw[oc][kk] = the per-image sums added in image order (conv2d.h:326-331).
 __global__ void conv_direct_dw_finish_k(const float* __restrict__ part, int OC, int K, int B,
                                         float* __restrict__ dw) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n = (int64_t)OC * K;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {

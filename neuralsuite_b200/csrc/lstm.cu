@@ -9,7 +9,9 @@
 //    the backward's dW_ih = dpre^T . x, dW_hh = dpre^T . H_prev and
 //    dx = dpre . W_ih; H_prev (the state entering each step) is the output
 //    itself shifted by one step, so no stacked copy is made.
-//  * The recurrence is one launch per step.  Each CTA owns kUnits hidden
+//  * The recurrence is one launch per step (each launched as a programmatic
+//    dependent of the one before, so its launch overlaps that step's end).
+//    Each CTA owns kUnits hidden
 //    units: it forms their 4 gate pre-activations for every sequence from
 //    h_{t-1} . W_hh^T (both streamed through shared memory in chunks) and
 //    applies the cell update in the same launch, so a step needs no
@@ -52,6 +54,8 @@ __global__ void __launch_bounds__(kThreads) lstm_step_fwd_k(
   __shared__ float sh[kMaxB][kChunk + 1];
   __shared__ float sw[kRows][kChunk + 1];
   __shared__ float gates[kMaxB][kRows];
+  pdl_wait();  // launched as a programmatic dependent of the previous step
+  pdl_trigger();
   const int k0 = blockIdx.x * kUnits;
   const int r = threadIdx.x % kRows, bq = threadIdx.x / kRows;  // 8 groups of sequences
   const int g = r / kUnits, u = r % kUnits;
@@ -139,6 +143,8 @@ __global__ void __launch_bounds__(kThreads) lstm_step_bwd_k(
   __shared__ float sd[kMaxB][kChunk + 1];
   __shared__ float sw[kUnits][kChunk + 1];
   __shared__ float dhn[kMaxB][kUnits];
+  pdl_wait();  // launched as a programmatic dependent of the previous step
+  pdl_trigger();
   const int k0 = blockIdx.x * kUnits;
   const int G = 4 * H;
   // dh_next for (b, unit): one output per thread (B * kUnits <= 512: two rounds).
@@ -275,8 +281,8 @@ ns_status fwd_impl(const float* x, int T, int B, int IN, int H, const ns_lstm_we
   const Cache c = cache_at(cache, (int64_t)T * B * H);
   const int grid = (H + kUnits - 1) / kUnits;
   for (int t = 0; t < T; ++t) {
-    lstm_step_fwd_k<<<grid, kThreads, 0, s>>>(pre, w.w_hh, w.b_ih, w.b_hh, t, B, H, out, c);
-    rc = check_launch("ns_lstm_fwd step");
+    rc = launch_pdl(lstm_step_fwd_k, dim3(grid), dim3(kThreads), 0, s, "ns_lstm_fwd step", pre,
+                    w.w_hh, w.b_ih, w.b_hh, t, B, H, out, c);
     if (rc != NS_OK) return rc;
   }
   return NS_OK;
@@ -297,8 +303,8 @@ ns_status bwd_impl(const float* x, const float* out, const float* dout, int T, i
   const Cache c = cache_at(cache, (int64_t)T * B * H);
   const int grid = (H + kUnits - 1) / kUnits;
   for (int t = T - 1; t >= 0 && rc == NS_OK; --t) {
-    lstm_step_bwd_k<<<grid, kThreads, 0, s>>>(dout, w_t, t, T, B, H, c, dc, dpre);
-    rc = check_launch("ns_lstm_bwd step");
+    rc = launch_pdl(lstm_step_bwd_k, dim3(grid), dim3(kThreads), 0, s, "ns_lstm_bwd step", dout,
+                    w_t, t, T, B, H, c, dc, dpre);
   }
   if (rc != NS_OK) return rc;
   // The weight gradients sum over all T*B rows and their partial sums keep a

@@ -66,6 +66,7 @@ __global__ void gelu_bwd_k(const float* __restrict__ d, const float* __restrict_
 
 __global__ void add_k(const float* __restrict__ a, const float* __restrict__ b,
                       float* __restrict__ o, int64_t n) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {

@@ -74,6 +74,7 @@ int grid_for(int64_t work) {
 // y = ReLU(f + x) (ResidualBlock::Forward's sum then Activation(kRelu)).
 __global__ void resid_relu_k(const float* __restrict__ f, const float* __restrict__ x, int64_t n,
                              float* __restrict__ y) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float s = __fadd_rn(f[i], x[i]);
@@ -84,6 +85,7 @@ __global__ void resid_relu_k(const float* __restrict__ f, const float* __restric
 // dsum = y > 0 ? dy : 0 (ReluBackward on the pre-activation sum, whose sign
 // is that of the output).  dsum may be dy.
 __global__ void relu_mask_k(const float* dy, const float* __restrict__ y, int64_t n, float* dsum) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     dsum[i] = y[i] > 0.0f ? dy[i] : 0.0f;
@@ -92,6 +94,7 @@ __global__ void relu_mask_k(const float* dy, const float* __restrict__ y, int64_
 // y[bc][i][j] = x[bc][i/2][j/2]: one thread per input element writes its
 // 2 x 2 block as two 8-byte stores (32-bit indexing: n < 2^31).
 __global__ void up2_k(const float* __restrict__ x, int n, int W, float* __restrict__ y) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int row = i / W, j = i - row * W;  // row = bc * H + r
     const float v = x[i];
@@ -103,6 +106,7 @@ __global__ void up2_k(const float* __restrict__ x, int n, int W, float* __restri
 
 // dx[bc][i][j] = dy[2i][2j] + dy[2i][2j+1] + dy[2i+1][2j] + dy[2i+1][2j+1], in that order.
 __global__ void up2_bwd_k(const float* __restrict__ dy, int n, int W, float* __restrict__ dx) {
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int row = i / W, j = i - row * W;
     const float* p = dy + (size_t)row * 4 * W + 2 * j;
