@@ -268,32 +268,6 @@ constexpr int kDirectGroup = 8;     // input channels staged per round (forward)
 constexpr int kDirectDxGroup = 16;  // input channels per CTA (dx)
 constexpr int kDirectSmemFloats = 49152;  // 192 KB of staged planes at most
 
-// Asynchronous global -> shared copies (cp.async): every copy of a staging
-// round is in flight at once, then one wait.  16-byte copies where both
-// addresses allow, 4-byte copies otherwise.
-__device__ __forceinline__ uint32_t sm_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
-// n floats from src to dst, shared by the CTA's threads (no wait).
-__device__ __forceinline__ void stage(float* dst, const float* src, int n) {
-  const bool vec = ((n & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0) &&
-                   ((sm_addr(dst) & 15) == 0);
-  if (vec) {
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) cp_async16(dst + i, src + i);
-  } else {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) cp_async4(dst + i, src + i);
-  }
-}
-
 // The direct kernels work on kDirectPx consecutive pixels of one row per
 // thread (rows a multiple of kDirectPx long), with the window (KS x KS, 1 or
 // 3) and the channel count NOC (1..4) known at compile time and operands
@@ -514,7 +488,7 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
       else xs[rr * pw + c] = 0.0f;
     }
   }
-  stage(ds, dy + ((size_t)b * sh.OC + o0) * P, NOC * P);
+  stage_async(ds, dy + ((size_t)b * sh.OC + o0) * P, NOC * P);
   cp_async_wait_all();
   __syncthreads();
   float acc[NOC][KS * KS];

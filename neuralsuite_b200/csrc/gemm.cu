@@ -10,6 +10,9 @@
 #include "gemm_tc.cuh"
 
 namespace nsb {
+namespace lstm {
+int consume_timeout_flag();  // lstm.cu
+}  // namespace lstm
 namespace {
 
 // 0 auto, 1 SIMT, 2 tcgen05 with in-kernel operand split, 3 / 4: pre-split operands on
@@ -243,10 +246,13 @@ ns_status ns_selftest_device_wait(int limit_us, void* stream) {
 ns_status ns_kernel_health(void) {
   const int g = tc::consume_timeout_flag();
   const int a = attn_tc::consume_timeout_flag();
+  const int l = lstm::consume_timeout_flag();
   if (g < 0) return cuda_fail((cudaError_t)(-g), "ns_kernel_health: reading the GEMM flag");
   if (a < 0) return cuda_fail((cudaError_t)(-a), "ns_kernel_health: reading the attention flag");
+  if (l < 0) return cuda_fail((cudaError_t)(-l), "ns_kernel_health: reading the LSTM flag");
   if (g) return fail(NS_ERR_TIMEOUT, "a tcgen05 GEMM gave up a bounded wait (see ns_gemm)");
   if (a) return fail(NS_ERR_TIMEOUT, "a tcgen05 attention kernel gave up a bounded wait");
+  if (l) return fail(NS_ERR_TIMEOUT, "an LSTM whole-sequence kernel gave up its grid barrier");
   return NS_OK;
 }
 

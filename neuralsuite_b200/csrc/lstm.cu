@@ -9,9 +9,11 @@
 //    the backward's dW_ih = dpre^T . x, dW_hh = dpre^T . H_prev and
 //    dx = dpre . W_ih; H_prev (the state entering each step) is the output
 //    itself shifted by one step, so no stacked copy is made.
-//  * The recurrence is one launch per step (each launched as a programmatic
-//    dependent of the one before, so its launch overlaps that step's end).
-//    Each CTA owns kUnits hidden
+//  * The recurrence runs as one cooperative kernel over the whole sequence
+//    (lstm_seq_fwd_k / lstm_seq_bwd_k: each CTA keeps its units' weight rows
+//    in shared memory, a grid barrier between steps) when every CTA fits on
+//    the GPU at once, else as one launch per step (each a programmatic
+//    dependent of the one before).  Each CTA owns kUnits hidden
 //    units: it forms their 4 gate pre-activations for every sequence from
 //    h_{t-1} . W_hh^T (both streamed through shared memory in chunks) and
 //    applies the cell update in the same launch, so a step needs no
@@ -122,6 +124,198 @@ __global__ void __launch_bounds__(kThreads) lstm_step_fwd_k(
     cache.c[s] = c;
     cache.tc[s] = tc;
     out[s] = __fmul_rn(og, tc);
+  }
+}
+
+// ------------------------------------------------------------ whole sequences
+//
+// The recurrence in one cooperative launch (all CTAs resident at once): CTA c
+// owns hidden units [c*kUnits, (c+1)*kUnits) for every step, keeps the weight
+// rows those units need in shared memory for the whole sequence, and meets
+// the other CTAs at a grid barrier after each step, since the next step reads
+// every unit's output.  Each step does the same sums in the same order as the
+// per-step kernels above, so the results are the same bits.  The barrier is
+// a counter in the caller's workspace (zeroed before the launch); its wait is
+// bounded (2 s of %globaltimer), after which the CTA raises g_timeout, which
+// ns_kernel_health() reports, and returns.
+__device__ int g_timeout;
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// This CTA's writes of the step, then its arrival.
+__device__ __forceinline__ void grid_arrive(unsigned* bar) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+  }
+}
+// Until `target` arrivals (false after the time limit; every thread gets the answer).
+__device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const unsigned long long t0 = now_ns();
+    int good = 1;
+    while (ld_acquire(bar) < target) {
+      if (now_ns() - t0 > 2000000000ull) {
+        atomicExch(&g_timeout, 1);
+        good = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    ok = good;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Dynamic shared memory of the whole-sequence kernels (bytes).
+__host__ __device__ inline size_t seq_fwd_smem(int B, int H) {
+  return ((((size_t)kRows * (H + 1) + 3) & ~(size_t)3) + (size_t)B * H) * sizeof(float);
+}
+__host__ __device__ inline size_t seq_bwd_smem(int B, int H) {
+  return ((((size_t)kUnits * (4 * H + 1) + 3) & ~(size_t)3) + (size_t)B * 4 * H) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kThreads) lstm_seq_fwd_k(
+    const float* __restrict__ pre, const float* __restrict__ w_hh, const float* __restrict__ b_ih,
+    const float* __restrict__ b_hh, int T, int B, int H, float* __restrict__ out, Cache cache,
+    unsigned* bar) {
+  extern __shared__ __align__(16) float sm[];
+  const int pitch = H + 1;          // odd row pitch: the 32 rows of a warp in different banks
+  float* sw = sm;                   // [kRows][pitch]: W_hh row g*H + k0 + u at g*kUnits + u
+  float* shp = sm + ((kRows * pitch + 3) & ~3);  // [B][H]: h_{t-1} (16-byte aligned)
+  __shared__ float gates[kMaxB][kRows];
+  const int k0 = blockIdx.x * kUnits;
+  const int r = threadIdx.x % kRows, bq = threadIdx.x / kRows;
+  const int g = r / kUnits, u = r % kUnits;
+  const int row = g * H + k0 + u;
+  for (int i = threadIdx.x; i < kRows * H; i += kThreads) {
+    const int rr = i / H, j = i - rr * H;
+    const int gg = rr / kUnits, uu = rr % kUnits;
+    sw[rr * pitch + j] = k0 + uu < H ? w_hh[(size_t)(gg * H + k0 + uu) * H + j] : 0.0f;
+  }
+  for (int t = 0; t < T; ++t) {
+    float acc[kMaxB / 8];
+#pragma unroll
+    for (int q = 0; q < kMaxB / 8; ++q) acc[q] = 0.0f;
+    if (t > 0) {
+      if (!grid_wait(bar, (unsigned)t * gridDim.x)) return;
+      stage_async(shp, out + (size_t)(t - 1) * B * H, B * H);  // through L2: other SMs' writes
+      cp_async_wait_all();
+      __syncthreads();
+      const float* wr = sw + r * pitch;
+#pragma unroll
+      for (int q = 0; q < kMaxB / 8; ++q) {
+        const int b = bq + 8 * q;
+        if (b < B) {
+          const float* hb = shp + (size_t)b * H;
+          float a = 0.0f;
+          for (int j = 0; j < H; ++j) a = fmaf(hb[j], wr[j], a);
+          acc[q] = a;
+        }
+      }
+    } else {
+      __syncthreads();  // the weight rows are in place
+    }
+    if (k0 + u < H) {
+#pragma unroll
+      for (int q = 0; q < kMaxB / 8; ++q) {
+        const int b = bq + 8 * q;
+        if (b < B) {
+          float v = __fadd_rn(__fadd_rn(pre[((size_t)t * B + b) * 4 * H + row], b_ih[row]), b_hh[row]);
+          if (t > 0) v = __fadd_rn(v, acc[q]);
+          gates[b][r] = v;
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < B * kUnits; i += kThreads) {
+      const int b = i / kUnits, uu = i % kUnits, k = k0 + uu;
+      if (k >= H) continue;
+      const float ig = sigmoid_f(gates[b][0 * kUnits + uu]);
+      const float fg = sigmoid_f(gates[b][1 * kUnits + uu]);
+      const float gg = tanhf(gates[b][2 * kUnits + uu]);
+      const float og = sigmoid_f(gates[b][3 * kUnits + uu]);
+      const size_t s = ((size_t)t * B + b) * H + k;
+      const float c_prev = t > 0 ? cache.c[s - (size_t)B * H] : 0.0f;
+      const float c = __fadd_rn(__fmul_rn(fg, c_prev), __fmul_rn(ig, gg));
+      const float tc = tanhf(c);
+      cache.i[s] = ig;
+      cache.f[s] = fg;
+      cache.g[s] = gg;
+      cache.o[s] = og;
+      cache.c[s] = c;
+      cache.tc[s] = tc;
+      out[s] = __fmul_rn(og, tc);
+    }
+    grid_arrive(bar);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) lstm_seq_bwd_k(
+    const float* __restrict__ dout, const float* __restrict__ w_t, int T, int B, int H,
+    Cache cache, float* __restrict__ dc_next, float* __restrict__ dpre, unsigned* bar) {
+  extern __shared__ __align__(16) float sm[];
+  const int G = 4 * H, pitch = G + 1;
+  float* sw = sm;                    // [kUnits][pitch]: rows k0 .. k0+kUnits-1 of W_hh^T
+  float* sd = sm + ((kUnits * pitch + 3) & ~3);  // [B][G]: dpre_{t+1} (16-byte aligned)
+  __shared__ float dhn[kMaxB][kUnits];
+  const int k0 = blockIdx.x * kUnits;
+  for (int i = threadIdx.x; i < kUnits * G; i += kThreads) {
+    const int uu = i / G, j = i - uu * G;
+    sw[uu * pitch + j] = k0 + uu < H ? w_t[(size_t)(k0 + uu) * G + j] : 0.0f;
+  }
+  __syncthreads();
+  unsigned round = 0;
+  for (int t = T - 1; t >= 0; --t, ++round) {
+    if (t < T - 1) {
+      if (!grid_wait(bar, round * gridDim.x)) return;
+      stage_async(sd, dpre + (size_t)(t + 1) * B * G, B * G);  // through L2: other SMs' writes
+      cp_async_wait_all();
+      __syncthreads();
+    }
+    for (int base = 0; base < B * kUnits; base += kThreads) {
+      const int o = base + threadIdx.x;
+      if (o >= B * kUnits) break;
+      const int b = o / kUnits, uu = o % kUnits;
+      float a = 0.0f;
+      if (t < T - 1) {
+        const float* db = sd + (size_t)b * G;
+        const float* wr = sw + uu * pitch;
+        for (int j = 0; j < G; ++j) a = fmaf(db[j], wr[j], a);
+      }
+      dhn[b][uu] = a;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < B * kUnits; i += kThreads) {
+      const int b = i / kUnits, uu = i % kUnits, k = k0 + uu;
+      if (k >= H) continue;
+      const size_t s = ((size_t)t * B + b) * H + k;
+      const float ig = cache.i[s], fg = cache.f[s], gg = cache.g[s], og = cache.o[s], tc = cache.tc[s];
+      const float c_prev = t > 0 ? cache.c[s - (size_t)B * H] : 0.0f;
+      const float dh = __fadd_rn(dout[s], dhn[b][uu]);
+      const float do_g = __fmul_rn(dh, tc);
+      const float dc = __fadd_rn(
+          __fmul_rn(__fmul_rn(dh, og), __fsub_rn(1.0f, __fmul_rn(tc, tc))),
+          dc_next[(size_t)b * H + k]);
+      float* dr = dpre + ((size_t)t * B + b) * G;
+      dr[k] = __fmul_rn(__fmul_rn(__fmul_rn(dc, gg), ig), __fsub_rn(1.0f, ig));
+      dr[H + k] = __fmul_rn(__fmul_rn(__fmul_rn(dc, c_prev), fg), __fsub_rn(1.0f, fg));
+      dr[2 * H + k] = __fmul_rn(__fmul_rn(dc, ig), __fsub_rn(1.0f, __fmul_rn(gg, gg)));
+      dr[3 * H + k] = __fmul_rn(__fmul_rn(do_g, og), __fsub_rn(1.0f, og));
+      dc_next[(size_t)b * H + k] = __fmul_rn(dc, fg);
+    }
+    grid_arrive(bar);
   }
 }
 
@@ -255,10 +449,49 @@ size_t gemm_ws(int T, int B, int IN, int H) {
                    ns_gemm_workspace_size(G, H, M), ns_gemm_workspace_size(G, H, std::max(M - B, 1)),
                    ns_gemm_workspace_size(M, IN, G), ns_bias_grad_workspace_size(M, G)});
 }
+// Workspace (floats, 64-aligned pieces): pre | dpre | W_hh^T | dc | the
+// grid-barrier counter of the whole-sequence kernels | the GEMM workspace.
 size_t ws_floats(int T, int B, int IN, int H) {
   const size_t M = (size_t)T * B, G = 4 * (size_t)H;
-  return 2 * al64(M * G) + al64((size_t)H * G) + al64((size_t)B * H) +
+  return 2 * al64(M * G) + al64((size_t)H * G) + al64((size_t)B * H) + 64 +
          (gemm_ws(T, B, IN, H) + 255) / sizeof(float);
+}
+
+// The whole-sequence kernel when the GPU can hold every CTA at once with its
+// shared memory (a cooperative launch), else false: the caller then runs the
+// per-step kernels.
+template <typename... Args>
+bool launch_seq(void (*kernel)(Args...), int grid, size_t smem, cudaStream_t s, void** args,
+                ns_status* rc) {
+  *rc = NS_OK;
+  if (smem > 227 * 1024) return false;
+  static thread_local int coop = -1;
+  if (coop < 0) {
+    int dev = 0, v = 0;
+    coop = (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&v, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && v)
+               ? 1 : 0;
+  }
+  if (!coop) return false;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if ((int64_t)per_sm * sm_count() < grid) return false;
+  const cudaError_t e = cudaLaunchCooperativeKernel((const void*)kernel, dim3(grid), dim3(kThreads),
+                                                    args, smem, s);
+  if (e != cudaSuccess) {
+    *rc = cuda_fail(e, "ns_lstm whole-sequence kernel");
+    return true;
+  }
+  count_launch();
+  return true;
 }
 
 ns_status check(int T, int B, int IN, int H) {
@@ -272,14 +505,25 @@ ns_status fwd_impl(const float* x, int T, int B, int IN, int H, const ns_lstm_we
                    float* out, float* cache, float* ws, cudaStream_t s) {
   const int M = T * B, G = 4 * H;
   float* pre = ws;
-  float* gws = ws + 2 * al64((size_t)M * G) + al64((size_t)H * G) + al64((size_t)B * H);
+  float* gws = ws + 2 * al64((size_t)M * G) + al64((size_t)H * G) + al64((size_t)B * H) + 64;
   const size_t gbytes = gemm_ws(T, B, IN, H);
   // pre = x . W_ih^T  ([T*B, IN] x [IN, 4H]; W_ih stored [4H, IN])
   ns_status rc = ns_gemm(M, G, IN, x, IN, 0, w.w_ih, IN, 1, pre, G, 0.0f, NS_EPI_STORE, nullptr,
                          nullptr, nullptr, gws, gbytes, s);
   if (rc != NS_OK) return rc;
-  const Cache c = cache_at(cache, (int64_t)T * B * H);
+  Cache c = cache_at(cache, (int64_t)T * B * H);
   const int grid = (H + kUnits - 1) / kUnits;
+  if (T > 1) {
+    unsigned* bar = reinterpret_cast<unsigned*>(ws + 2 * al64((size_t)M * G) + al64((size_t)H * G) +
+                                                al64((size_t)B * H));
+    NS_TRY_CUDA(cudaMemsetAsync(bar, 0, sizeof(unsigned), s), "ns_lstm_fwd");
+    const float* w_hh = w.w_hh;
+    const float* b_ih = w.b_ih;
+    const float* b_hh = w.b_hh;
+    int T_ = T, B_ = B, H_ = H;
+    void* args[] = {&pre, &w_hh, &b_ih, &b_hh, &T_, &B_, &H_, &out, &c, &bar};
+    if (launch_seq(lstm_seq_fwd_k, grid, seq_fwd_smem(B, H), s, args, &rc)) return rc;
+  }
   for (int t = 0; t < T; ++t) {
     rc = launch_pdl(lstm_step_fwd_k, dim3(grid), dim3(kThreads), 0, s, "ns_lstm_fwd step", pre,
                     w.w_hh, w.b_ih, w.b_hh, t, B, H, out, c);
@@ -295,14 +539,23 @@ ns_status bwd_impl(const float* x, const float* out, const float* dout, int T, i
   float* dpre = ws + al64((size_t)M * G);
   float* w_t = dpre + al64((size_t)M * G);
   float* dc = w_t + al64((size_t)H * G);
-  float* gws = dc + al64((size_t)B * H);
+  unsigned* bar = reinterpret_cast<unsigned*>(dc + al64((size_t)B * H));
+  float* gws = dc + al64((size_t)B * H) + 64;
   const size_t gbytes = gemm_ws(T, B, IN, H);
   NS_TRY_CUDA(cudaMemsetAsync(dc, 0, (size_t)B * H * sizeof(float), s), "ns_lstm_bwd");
   transpose_k<<<grid_for((int64_t)G * H), 256, 0, s>>>(w.w_hh, G, H, w_t);
   ns_status rc = check_launch("ns_lstm_bwd transpose");
-  const Cache c = cache_at(cache, (int64_t)T * B * H);
+  Cache c = cache_at(cache, (int64_t)T * B * H);
   const int grid = (H + kUnits - 1) / kUnits;
-  for (int t = T - 1; t >= 0 && rc == NS_OK; --t) {
+  bool whole = false;
+  if (rc == NS_OK && T > 1) {
+    NS_TRY_CUDA(cudaMemsetAsync(bar, 0, sizeof(unsigned), s), "ns_lstm_bwd");
+    int T_ = T, B_ = B, H_ = H;
+    const float* w_tc = w_t;
+    void* args[] = {&dout, &w_tc, &T_, &B_, &H_, &c, &dc, &dpre, &bar};
+    whole = launch_seq(lstm_seq_bwd_k, grid, seq_bwd_smem(B, H), s, args, &rc);
+  }
+  for (int t = T - 1; !whole && t >= 0 && rc == NS_OK; --t) {
     rc = launch_pdl(lstm_step_bwd_k, dim3(grid), dim3(kThreads), 0, s, "ns_lstm_bwd step", dout,
                     w_t, t, T, B, H, c, dc, dpre);
   }
@@ -343,6 +596,21 @@ ns_status bwd_impl(const float* x, const float* out, const float* dout, int T, i
 }
 
 }  // namespace
+
+// 1 if a whole-sequence kernel gave up its grid barrier since the last call
+// (the flag is cleared), 0 if not, -(CUDA error) if the flag cannot be read.
+int consume_timeout_flag() {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_timeout, sizeof(int));
+  if (e != cudaSuccess) return -(int)e;
+  if (v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) return -(int)e;
+  }
+  return v ? 1 : 0;
+}
+
 }  // namespace lstm
 }  // namespace nsb
 
