@@ -321,7 +321,10 @@ NS_API ns_status ns_conv2d_bwd(const float* x, const float* dy, int B, int IC, i
  * forward cell's state then the reverse cell's), gates i, f, g, o over 4H,
  * W_ih [4H, IN], W_hh [4H, H], b_ih / b_hh [4H].  The input projection and
  * the three weight/input-gradient products are tcgen05 GEMMs; the recurrence
- * is one launch per step.  `cache` (ns_lstm_cache_floats / ns_bilstm_cache_floats
+ * is one cooperative kernel over the whole sequence (a grid barrier between
+ * steps, bounded and reported by ns_kernel_health) where every CTA fits on
+ * the GPU at once, else one launch per step; both give the same bits.
+ * `cache` (ns_lstm_cache_floats / ns_bilstm_cache_floats
  * floats, device) carries the gates and cell states from the forward to the
  * backward; the backward overwrites every gradient (the reference's
  * MatMul/Zeros) and writes dx unless it is NULL.  B <= 64.
@@ -342,6 +345,10 @@ NS_API ns_status ns_lstm_bwd(const float* x, const float* out, const float* dout
                              int IN, int H, ns_lstm_weights w, float* cache, float* dx,
                              ns_lstm_grads g, void* workspace, size_t workspace_bytes,
                              void* stream);
+/* 0 (default): the whole-sequence recurrence where it fits, else one launch
+ * per step; 1: always one launch per step.  Per host thread.  No reference
+ * counterpart (engine selection for tests and profiling). */
+NS_API ns_status ns_lstm_set_engine(int engine);
 NS_API size_t ns_bilstm_cache_floats(int T, int B, int H);
 NS_API size_t ns_bilstm_workspace_size(int T, int B, int IN, int H);
 NS_API ns_status ns_bilstm_fwd(const float* x, int T, int B, int IN, int H, ns_lstm_weights fwd,

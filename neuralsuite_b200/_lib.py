@@ -172,6 +172,7 @@ _SIGS = {
     "ns_gpt_train_step": (c_int, [P, P, P, c_int, c_int, c_float, P, P]),
     "ns_gpt_set_comm": (c_int, [P, P, c_int, c_int64]),
     "ns_gpt_plan_buckets": (c_int, [P, c_int64, P, P, c_int]),
+    "ns_lstm_set_engine": (c_int, [c_int]),
     "ns_gpt_set_comm_timing": (c_int, [P, c_int]),
     "ns_gpt_comm_times": (c_int, [P, P, P]),
 }

@@ -460,11 +460,13 @@ size_t ws_floats(int T, int B, int IN, int H) {
 // The whole-sequence kernel when the GPU can hold every CTA at once with its
 // shared memory (a cooperative launch), else false: the caller then runs the
 // per-step kernels.
+thread_local int t_engine = 0;  // ns_lstm_set_engine
+
 template <typename... Args>
 bool launch_seq(void (*kernel)(Args...), int grid, size_t smem, cudaStream_t s, void** args,
                 ns_status* rc) {
   *rc = NS_OK;
-  if (smem > 227 * 1024) return false;
+  if (t_engine == 1 || smem > 227 * 1024) return false;
   static thread_local int coop = -1;
   if (coop < 0) {
     int dev = 0, v = 0;
@@ -624,6 +626,12 @@ size_t ns_lstm_cache_floats(int T, int B, int H) { return (size_t)6 * T * B * H;
 size_t ns_lstm_workspace_size(int T, int B, int IN, int H) {
   if (check(T, B, IN, H) != NS_OK) return 0;
   return std::max<size_t>(ws_floats(T, B, IN, H) * sizeof(float), 256);
+}
+
+ns_status ns_lstm_set_engine(int engine) {
+  NS_REQUIRE(engine == 0 || engine == 1, "ns_lstm_set_engine: engine must be 0 or 1");
+  t_engine = engine;
+  return NS_OK;
 }
 
 ns_status ns_lstm_fwd(const float* x, int T, int B, int IN, int H, ns_lstm_weights w, float* out,

@@ -569,7 +569,10 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
   if (dim % 4 == 0 && (al & 15) == 0 && dim <= 128 * kMaxVec) {
     const int nv = dim / 4;
     const size_t smem = (size_t)kRowsWarps * 2 * dim * sizeof(float);
-    if (nv <= 32)
+    if (nv <= 16)  // short rows (the U-Net's last-axis LayerNorms): more rows in flight
+      ln_bwd_vec<1, 8><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
+                                              part_b, rows, dim, rpc);
+    else if (nv <= 32)
       ln_bwd_vec<1, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
                                               part_b, rows, dim, rpc);
     else if (nv <= 64)

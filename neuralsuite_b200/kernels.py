@@ -387,6 +387,11 @@ def _lstm_struct(views):
     return _lib.ns_lstm_weights(*[v.data_ptr() for v in views])
 
 
+def lstm_set_engine(engine: int) -> None:
+    """0: the whole-sequence recurrence where it fits; 1: one launch per step."""
+    _lib.check(_lib.load().ns_lstm_set_engine(engine))
+
+
 def lstm_fwd_bwd(x, params, dout, H, bidir=False, want_dx=True):
     """LSTM / BiLSTM Forward then Backward (include/layers/lstm.h:320-664):
     x [T, B, IN], params flat in registration order -> (out, dx, grads flat)."""

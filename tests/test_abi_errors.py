@@ -202,3 +202,8 @@ def test_conv2d_rejects_bad_parameters(lib):
          NS_ERR_INVALID_ARGUMENT, "bad convolution")
     _err(lib, lib.ns_conv2d_fwd(FAKE, 1, 3, 8, 8, FAKE, FAKE, 4, 3, 1, 1, FAKE, FAKE, 0, None),
          NS_ERR_INVALID_ARGUMENT, "workspace")
+
+
+def test_lstm_engine_checks(lib):
+    _err(lib, lib.ns_lstm_set_engine(2), NS_ERR_INVALID_ARGUMENT, "engine")
+    assert lib.ns_lstm_set_engine(0) == NS_OK

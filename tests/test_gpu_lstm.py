@@ -89,3 +89,23 @@ def test_lstm_is_deterministic(cuda):
     b = nk.lstm_fwd_bwd(x, p, d, H, True)
     for u, v in zip(a, b):
         assert torch.equal(u, v)
+
+
+def test_whole_sequence_recurrence_equals_per_step_launches(cuda):
+    """The cooperative whole-sequence kernels and the per-step kernels do the
+    same sums in the same order: every output bit-identical."""
+    T, B, IN, H = 24, 8, 32, 64
+    r = np.random.default_rng(13)
+    n1 = 4 * H * IN + 4 * H * H + 8 * H
+    p = torch.as_tensor((r.standard_normal(2 * n1) / 8).astype(np.float32), device="cuda")
+    x = torch.as_tensor(r.standard_normal((T, B, IN)).astype(np.float32), device="cuda")
+    d = torch.as_tensor(r.standard_normal((T, B, 2 * H)).astype(np.float32), device="cuda")
+    try:
+        whole = [t.cpu().numpy() for t in nk.lstm_fwd_bwd(x, p, d, H, True)]
+        nk.lstm_set_engine(1)
+        steps = [t.cpu().numpy() for t in nk.lstm_fwd_bwd(x, p, d, H, True)]
+    finally:
+        nk.lstm_set_engine(0)
+    nk.kernel_health()
+    for a, b in zip(whole, steps):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
