@@ -76,6 +76,8 @@ __device__ __forceinline__ void adam_piece(int64_t s, int n, float decay, float*
 __global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __restrict__ P,
                                                const float* __restrict__ G, float* __restrict__ M,
                                                float* __restrict__ V, AdamHyper hp) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   float lr = hp.lr, b1 = hp.b1, b2 = hp.b2, eps = hp.eps, bc1 = hp.bc1, bc2 = hp.bc2;
   if (hp.dev) {
     lr = hp.dev[0]; b1 = hp.dev[1]; b2 = hp.dev[2]; eps = hp.dev[3]; bc1 = hp.dev[4]; bc2 = hp.dev[5];
@@ -101,6 +103,8 @@ __global__ void __launch_bounds__(256) adamw_k(const AdamTable tab, float* __res
 // lines, include/optimizers.h:208-210): step += 1; bc = 1 - pow(beta, step)
 // evaluated in double and rounded to float, as std::pow(float, int) does.
 __global__ void adamw_prep_k(float* hyper) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   int step = __float_as_int(hyper[6]) + 1;
   hyper[6] = __int_as_float(step);
   hyper[4] = (float)(1.0 - pow((double)hyper[1], (double)step));
@@ -118,8 +122,10 @@ ns_status adamw_step_device(float* params, const float* grads, float* m, float* 
                             int64_t n_total, const int64_t* host_seg_offsets,
                             const float* host_seg_decay, int n_seg, float* hyper,
                             cudaStream_t s) {
-  adamw_prep_k<<<1, 1, 0, s>>>(hyper);
-  { ns_status _rc = check_launch("adamw prep"); if (_rc != NS_OK) return _rc; }
+  {
+    const ns_status rc = launch_pdl(adamw_prep_k, dim3(1), dim3(1), 0, s, "adamw prep", hyper);
+    if (rc != NS_OK) return rc;
+  }
   AdamHyper hp{hyper, 0.f, 0.f, 0.f, 0.f, 1.f, 1.f};
   return adamw_run(params, grads, m, v, n_total, host_seg_offsets, host_seg_decay, n_seg, hp, s);
 }
@@ -159,8 +165,8 @@ ns_status adamw_run(float* params, const float* grads, float* m, float* v, int64
     const int64_t per = std::max<int64_t>(1024, (len + waves_cta - 1) / waves_cta + 1023) & ~int64_t(1023);
     tab.per = per;
     const int grid = (int)((len + per - 1) / per);
-    adamw_k<<<grid, 256, 0, s>>>(tab, params, grads, m, v, hp);
-    ns_status rc = check_launch("ns_adamw_flat");
+    ns_status rc = launch_pdl(adamw_k, dim3(grid), dim3(256), 0, s, "ns_adamw_flat", tab, params,
+                              grads, m, v, hp);
     if (rc != NS_OK) return rc;
   }
   return NS_OK;

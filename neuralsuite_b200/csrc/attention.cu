@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(256) attn_delta_k(const float* __restrict__ ou
                                                     const float* __restrict__ dout, int B, int T,
                                                     int H, int D, float* __restrict__ delta,
                                                     float* __restrict__ dout_lo) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t row = blockIdx.x * 8 + (threadIdx.x >> 5);  // b * T + r
   const int lane = threadIdx.x & 31;
@@ -528,9 +529,12 @@ ns_status ns_attn_bwd_lo(const float* qkv, const float* qkv_lo, const float* out
                   attn_tc::bwd_supported(qkv, dout, dqkv, B, T, H, D);
   // The tensor-core path takes dO's lo part from the Delta pass.
   float* dout_lo = tc ? attn_tc::bwd_dout_lo(lo, B, T, H, D) : nullptr;
-  attn_delta_k<<<(unsigned)ceil_div64((int64_t)B * T, 8), 256, 0, s>>>(out, dout, B, T, H, D, delta,
-                                                                     dout_lo);
-  { ns_status _rc = check_launch("ns_attn_bwd delta"); if (_rc != NS_OK) return _rc; }
+  {
+    const ns_status rc = launch_pdl(attn_delta_k, dim3((unsigned)ceil_div64((int64_t)B * T, 8)),
+                                    dim3(256), 0, s, "ns_attn_bwd delta", out, dout, B, T, H, D,
+                                    delta, dout_lo);
+    if (rc != NS_OK) return rc;
+  }
   if (tc)
     return attn_tc::bwd(qkv, qkv_lo, dout, lse, delta, B, T, H, D, dqkv, lo, t_attn_engine == 0, s);
   if (D <= 16) return launch_bwd<16>(qkv, dout, lse, delta, B, T, H, D, dqkv, s);

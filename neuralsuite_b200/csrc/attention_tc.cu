@@ -571,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // columns, compact (row stride 2C).  2C is a multiple of 4.
 __global__ void split_kv_lo_k(const float* __restrict__ qkv, int64_t rows, int C,
                               float* __restrict__ lo) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int c4 = (2 * C) >> 2;
   const int64_t total = rows * c4;
@@ -593,8 +594,8 @@ ns_status launch_fwd(const float* qkv, const float* qkv_lo, int B, int T, int H,
   if (!qkv_lo) {
     const int64_t work = (int64_t)rows * (2 * C / 4);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
-    split_kv_lo_k<<<grid, 256, 0, s>>>(qkv, rows, C, lo);
-    ns_status rc = check_launch("ns_attn_fwd kv split");
+    ns_status rc = launch_pdl(split_kv_lo_k, dim3(grid), dim3(256), 0, s, "ns_attn_fwd kv split",
+                              qkv, rows, C, lo);
     if (rc != NS_OK) return rc;
   }
   const float* lo_t = qkv_lo ? qkv_lo : lo;
@@ -1797,6 +1798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // stride ld, written compact (row stride cols).  cols and ld are multiples of 4.
 __global__ void split_lo_rows_k(const float* __restrict__ x, int64_t rows, int cols, int64_t ld,
                                 float* __restrict__ lo) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int c4 = cols >> 2;
   const int64_t total = rows * c4;
@@ -1812,8 +1814,8 @@ __global__ void split_lo_rows_k(const float* __restrict__ x, int64_t rows, int c
 ns_status split_rows(const float* x, int64_t rows, int cols, float* lo, cudaStream_t s) {
   const int64_t work = rows * (cols / 4);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
-  split_lo_rows_k<<<grid, 256, 0, s>>>(x, rows, cols, cols, lo);
-  return check_launch("ns_attn_bwd operand split");
+  return launch_pdl(split_lo_rows_k, dim3(grid), dim3(256), 0, s, "ns_attn_bwd operand split", x,
+                    rows, cols, cols, lo);
 }
 
 template <int MODE, int D>

@@ -53,6 +53,7 @@ __device__ __forceinline__ float lo_of(float x) {
 __global__ void __launch_bounds__(256) im2col_k(const float* __restrict__ x, Shape sh,
                                                 float* __restrict__ cols,
                                                 float* __restrict__ cols_lo, int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW, K = sh.IC * sh.k * sh.k, kk2 = sh.k * sh.k;
   const int64_t N = sh.N(), runs = (int64_t)K * sh.B;
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(256) cnhw_to_nchw_bias_k(const float* __restri
                                                            const float* __restrict__ bias,
                                                            Shape sh, float* __restrict__ y,
                                                            int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW;
   const int64_t runs = (int64_t)sh.B * sh.OC;
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(256) cnhw_to_nchw_bias_k(const float* __restri
 __global__ void __launch_bounds__(256) nchw_to_cnhw_k(const float* __restrict__ dy, Shape sh,
                                                       float* __restrict__ dyc,
                                                       float* __restrict__ dyc_lo, int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int P = sh.OH * sh.OW;
   const int64_t runs = (int64_t)sh.B * sh.OC;
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(256) nchw_to_cnhw_k(const float* __restrict__ 
 // (one CTA per image and channel; blockDim 256).
 __global__ void __launch_bounds__(256) bias_part_k(const float* __restrict__ dy, Shape sh,
                                                    float* __restrict__ part) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float red[256];
   const int oc = blockIdx.x, b = blockIdx.y;
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(256) bias_part_k(const float* __restrict__ dy,
 // db[oc] = the per-image sums added in image order (conv2d.h:326-331).
 __global__ void bias_finish_k(const float* __restrict__ part, int OC, int B,
                               float* __restrict__ db) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int oc = blockIdx.x * blockDim.x + threadIdx.x;
   if (oc >= OC) return;
@@ -189,6 +194,7 @@ __global__ void bias_finish_k(const float* __restrict__ part, int OC, int B,
 // term is a coalesced read of one column row.
 __global__ void __launch_bounds__(256) col2im_k(const float* __restrict__ dcols, Shape sh,
                                                 float* __restrict__ dx) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int HW = sh.H * sh.W, P = sh.OH * sh.OW;
   const int64_t N = sh.N(), planes = (int64_t)sh.B * sh.IC;
@@ -225,6 +231,7 @@ __global__ void __launch_bounds__(256) col2im_k(const float* __restrict__ dcols,
 template <int KS, int ST>
 __global__ void __launch_bounds__(256) col2im_fixed_k(const float* __restrict__ dcols, Shape sh,
                                                       float* __restrict__ dx) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int HW = sh.H * sh.W, P = sh.OH * sh.OW;
   const int64_t N = sh.N(), planes = (int64_t)sh.B * sh.IC;
@@ -294,6 +301,7 @@ template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_fwd_k(
     const float* __restrict__ x, Shape sh, const float* __restrict__ w,
     const float* __restrict__ bias, float* __restrict__ y) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   const int R = direct_rows(sh.OW, sh.OH), nrows = (R - 1) * sh.s + KS;
@@ -381,6 +389,7 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_fwd_k(
 template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_dx_k(
     const float* __restrict__ dy, Shape sh, const float* __restrict__ w, float* __restrict__ dx) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   const int R = direct_rows(sh.W, sh.H), nrows = R + KS - 1;
@@ -465,6 +474,7 @@ template <int KS, int NOC>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
     const float* __restrict__ x, const float* __restrict__ dy, Shape sh,
     float* __restrict__ part) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ __align__(16) float sm[];
   __shared__ float wred[kDirectThreads / 32][NOC * KS * KS];
@@ -540,6 +550,7 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_dw_k(
 // dw[oc][kk] = the per-image sums added in image order (conv2d.h:326-331).
 __global__ void conv_direct_dw_finish_k(const float* __restrict__ part, int OC, int K, int B,
                                         float* __restrict__ dw) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n = (int64_t)OC * K;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -632,9 +643,8 @@ struct DirectFwd {
     ns_status rc = set_smem(conv_direct_fwd_k<KS, NOC>, smem, "ns_conv2d_fwd direct");
     if (rc != NS_OK) return rc;
     const int R = direct_rows(sh.OW, sh.OH);
-    conv_direct_fwd_k<KS, NOC><<<sh.B * ((sh.OH + R - 1) / R), kDirectThreads, smem, s>>>(
-        x, sh, w, bias, y);
-    return check_launch("ns_conv2d_fwd direct");
+    return launch_pdl(conv_direct_fwd_k<KS, NOC>, dim3(sh.B * ((sh.OH + R - 1) / R)),
+                      dim3(kDirectThreads), smem, s, "ns_conv2d_fwd direct", x, sh, w, bias, y);
   }
 };
 template <int KS, int NOC>
@@ -646,8 +656,8 @@ struct DirectDx {
     if (rc != NS_OK) return rc;
     const int R = direct_rows(sh.W, sh.H);
     const int grid = sh.B * ((sh.H + R - 1) / R) * ((sh.IC + kDirectDxGroup - 1) / kDirectDxGroup);
-    conv_direct_dx_k<KS, NOC><<<grid, kDirectThreads, smem, s>>>(dy, sh, w, dx);
-    return check_launch("ns_conv2d_bwd direct dx");
+    return launch_pdl(conv_direct_dx_k<KS, NOC>, dim3(grid), dim3(kDirectThreads), smem, s,
+                      "ns_conv2d_bwd direct dx", dy, sh, w, dx);
   }
 };
 template <int KS, int NOC>
@@ -657,9 +667,9 @@ struct DirectDw {
     const size_t smem = direct_dw_smem(sh) * sizeof(float);
     ns_status rc = set_smem(conv_direct_dw_k<KS, NOC>, smem, "ns_conv2d_bwd direct weight gradient");
     if (rc != NS_OK) return rc;
-    conv_direct_dw_k<KS, NOC><<<sh.B * sh.IC * (sh.OC / NOC), kDirectThreads, smem, s>>>(
-        x, dy, sh, part);
-    return check_launch("ns_conv2d_bwd direct weight gradient");
+    return launch_pdl(conv_direct_dw_k<KS, NOC>, dim3(sh.B * sh.IC * (sh.OC / NOC)),
+                      dim3(kDirectThreads), smem, s, "ns_conv2d_bwd direct weight gradient", x,
+                      dy, sh, part);
   }
 };
 
@@ -735,8 +745,8 @@ ns_status launch_im2col(const float* x, const Shape& sh, float* cols, float* col
                         cudaStream_t s) {
   const int vec = (sh.P() % 4 == 0 && sh.OW % 4 == 0 && aligned16(cols) &&
                    (!cols_lo || aligned16(cols_lo))) ? 1 : 0;
-  im2col_k<<<grid_runs(sh.K() * sh.B), 256, 0, s>>>(x, sh, cols, cols_lo, vec);
-  return check_launch("ns_conv2d im2col");
+  return launch_pdl(im2col_k, dim3(grid_runs(sh.K() * sh.B)), dim3(256), 0, s, "ns_conv2d im2col",
+                    x, sh, cols, cols_lo, vec);
 }
 
 ns_status launch_direct_fwd(const float* x, const Shape& sh, const float* weight,
@@ -755,8 +765,8 @@ ns_status forward_body(const Shape& sh, const float* weight, const float* bias, 
                   N, 0.0f, NS_EPI_STORE, nullptr, nullptr, nullptr, ws.gemm, ws.gemm_bytes, s);
   if (rc != NS_OK) return rc;
   const int vec = (sh.P() % 4 == 0 && aligned16(ws.yc) && aligned16(y)) ? 1 : 0;
-  cnhw_to_nchw_bias_k<<<grid_runs((int64_t)sh.B * sh.OC), 256, 0, s>>>(ws.yc, bias, sh, y, vec);
-  return check_launch("ns_conv2d_fwd layout");
+  return launch_pdl(cnhw_to_nchw_bias_k, dim3(grid_runs((int64_t)sh.B * sh.OC)), dim3(256), 0, s,
+                    "ns_conv2d_fwd layout", ws.yc, bias, sh, y, vec);
 }
 
 // The backward: x is read by the direct paths, the columns (of x) by the
@@ -770,15 +780,15 @@ ns_status backward_body(const Shape& sh, const float* x, const float* cols, cons
   if (gemm_dw || gemm_dx) {
     const int vec = (sh.P() % 4 == 0 && aligned16(dy) && aligned16(ws.dyc) && aligned16(ws.dyc_lo))
                         ? 1 : 0;
-    nchw_to_cnhw_k<<<grid_runs((int64_t)sh.B * sh.OC), 256, 0, s>>>(dy, sh, ws.dyc, ws.dyc_lo, vec);
-    rc = check_launch("ns_conv2d_bwd layout");
+    rc = launch_pdl(nchw_to_cnhw_k, dim3(grid_runs((int64_t)sh.B * sh.OC)), dim3(256), 0, s,
+                    "ns_conv2d_bwd layout", dy, sh, ws.dyc, ws.dyc_lo, vec);
     if (rc != NS_OK) return rc;
   }
-  bias_part_k<<<dim3(sh.OC, sh.B), 256, 0, s>>>(dy, sh, ws.bias_part);
-  rc = check_launch("ns_conv2d_bwd bias");
+  rc = launch_pdl(bias_part_k, dim3(sh.OC, sh.B), dim3(256), 0, s, "ns_conv2d_bwd bias", dy, sh,
+                  ws.bias_part);
   if (rc != NS_OK) return rc;
-  bias_finish_k<<<ceil_div(sh.OC, 128), 128, 0, s>>>(ws.bias_part, sh.OC, sh.B, dbias);
-  rc = check_launch("ns_conv2d_bwd bias");
+  rc = launch_pdl(bias_finish_k, dim3(ceil_div(sh.OC, 128)), dim3(128), 0, s, "ns_conv2d_bwd bias",
+                  ws.bias_part, sh.OC, sh.B, dbias);
   if (rc != NS_OK) return rc;
   if (gemm_dw) {
     // dW[OC, K] = dYc[OC, B*P] . cols[K, B*P]^T (overwritten, as the reference zeroes it first)
@@ -788,9 +798,9 @@ ns_status backward_body(const Shape& sh, const float* x, const float* cols, cons
   } else {
     rc = direct_dispatch<DirectDw>(sh.k, direct_dw_noc(M), x, dy, sh, ws.dw_part, s);
     if (rc != NS_OK) return rc;
-    conv_direct_dw_finish_k<<<grid_runs(ceil_div64((int64_t)M * K, 256)), 256, 0, s>>>(
-        ws.dw_part, M, K, sh.B, dweight);
-    rc = check_launch("ns_conv2d_bwd direct weight gradient");
+    rc = launch_pdl(conv_direct_dw_finish_k, dim3(grid_runs(ceil_div64((int64_t)M * K, 256))),
+                    dim3(256), 0, s, "ns_conv2d_bwd direct weight gradient", ws.dw_part, M, K,
+                    sh.B, dweight);
   }
   if (rc != NS_OK || !dx) return rc;
   if (!gemm_dx) {
@@ -805,12 +815,13 @@ ns_status backward_body(const Shape& sh, const float* x, const float* cols, cons
   if (rc != NS_OK) return rc;
   const int g = grid_runs((int64_t)sh.B * sh.IC);
   if (sh.k == 3 && sh.s == 1)
-    col2im_fixed_k<3, 1><<<g, 256, 0, s>>>(ws.dcols, sh, dx);
-  else if (sh.k == 3 && sh.s == 2)
-    col2im_fixed_k<3, 2><<<g, 256, 0, s>>>(ws.dcols, sh, dx);
-  else
-    col2im_k<<<g, 256, 0, s>>>(ws.dcols, sh, dx);
-  return check_launch("ns_conv2d_bwd col2im");
+    return launch_pdl(col2im_fixed_k<3, 1>, dim3(g), dim3(256), 0, s, "ns_conv2d_bwd col2im",
+                      ws.dcols, sh, dx);
+  if (sh.k == 3 && sh.s == 2)
+    return launch_pdl(col2im_fixed_k<3, 2>, dim3(g), dim3(256), 0, s, "ns_conv2d_bwd col2im",
+                      ws.dcols, sh, dx);
+  return launch_pdl(col2im_k, dim3(g), dim3(256), 0, s, "ns_conv2d_bwd col2im", ws.dcols, sh,
+                    dx);
 }
 
 ns_status zero_grads(const Shape& sh, float* dweight, float* dbias, cudaStream_t s) {

@@ -20,6 +20,7 @@ __global__ void __launch_bounds__(256) emb_fwd_k(const int32_t* __restrict__ tok
                                                  const float* __restrict__ wpe, int dim,
                                                  float* __restrict__ out,
                                                  int32_t* __restrict__ err) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   // blockDim.x = 256: 8 warps, one row each; lanes stride the columns.
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -58,6 +59,8 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_wte_k(const int32_t* __re
                                                              const float* __restrict__ dx,
                                                              int dim, float* __restrict__ dwte,
                                                              int accumulate) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ int list[kListChunk];
   __shared__ int warp_cnt[kEmbThreads / 32];
   __shared__ int list_len;
@@ -116,6 +119,8 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_wte_k(const int32_t* __re
 // dwpe[t, c] = sum over b ascending of dx[b, t, c]; rows t >= T are zeroed.
 __global__ void emb_bwd_wpe_k(const float* __restrict__ dx, int B, int T, int block, int dim,
                               float* __restrict__ dwpe) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= (int64_t)block * dim) return;
   const int t = (int)(i / dim), c = (int)(i % dim);
@@ -143,9 +148,8 @@ ns_status ns_embedding_fwd(const int32_t* tokens, int B, int T, const float* wte
   NS_REQUIRE((dim & 3) != 0 || ((reinterpret_cast<uintptr_t>(wte) | reinterpret_cast<uintptr_t>(wpe) |
                                  reinterpret_cast<uintptr_t>(out)) & 15) == 0,
              "ns_embedding_fwd: buffers must be 16-byte aligned");
-  emb_fwd_k<<<ceil_div(rows, 8), 256, 0, as_stream(stream)>>>(tokens, rows, T, wte, vocab, wpe,
-                                                              dim, out, err_flag);
-  return check_launch("ns_embedding_fwd");
+  return launch_pdl(emb_fwd_k, dim3(ceil_div(rows, 8)), dim3(256), 0, as_stream(stream),
+                    "ns_embedding_fwd", tokens, rows, T, wte, vocab, wpe, dim, out, err_flag);
 }
 
 ns_status ns_embedding_bwd(const int32_t* tokens, int B, int T, const float* dx, int vocab,
@@ -157,13 +161,20 @@ ns_status ns_embedding_bwd(const int32_t* tokens, int B, int T, const float* dx,
   cudaStream_t s = as_stream(stream);
   const int rows = B * T;
   if (dwte) {
-    emb_bwd_wte_k<<<vocab, kEmbThreads, 0, s>>>(tokens, rows, dx, dim, dwte, accumulate_wte);
-    { ns_status _rc = check_launch("ns_embedding_bwd wte"); if (_rc != NS_OK) return _rc; }
+    {
+      const ns_status rc = launch_pdl(emb_bwd_wte_k, dim3(vocab), dim3(kEmbThreads), 0, s,
+                                      "ns_embedding_bwd wte", tokens, rows, dx, dim, dwte,
+                                      accumulate_wte);
+      if (rc != NS_OK) return rc;
+    }
   }
   if (dwpe) {
     const int64_t n = (int64_t)block * dim;
-    emb_bwd_wpe_k<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(dx, B, T, block, dim, dwpe);
-    { ns_status _rc = check_launch("ns_embedding_bwd wpe"); if (_rc != NS_OK) return _rc; }
+    {
+      const ns_status rc = launch_pdl(emb_bwd_wpe_k, dim3((unsigned)ceil_div64(n, 256)), dim3(256),
+                                      0, s, "ns_embedding_bwd wpe", dx, B, T, block, dim, dwpe);
+      if (rc != NS_OK) return rc;
+    }
   }
   return NS_OK;
 }

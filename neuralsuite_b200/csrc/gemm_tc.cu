@@ -829,6 +829,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
 // tensor core reads from a tf32 operand, so hi + lo == x exactly.
 __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int ld,
                            float* __restrict__ lo, int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t total = (int64_t)rows * cols;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -859,6 +860,7 @@ __global__ void split_lo_k(const float* __restrict__ x, int rows, int cols, int 
 // own stores cannot issue those loads efficiently.  Same operations, same
 // order as the fused epilogue.
 __global__ void epi_apply_k(int M, int N, const EpiArgs e_param, int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const EpiArgs e = e_param;
   const int64_t total = (int64_t)M * N;
@@ -880,6 +882,7 @@ __global__ void epi_apply_k(int M, int N, const EpiArgs e_param, int vec) {
 // Ordered sum of the split-K partial tiles, then the epilogue.
 __global__ void splitk_reduce_k(const float* __restrict__ ws, int splits, int M, int N,
                                 const EpiArgs e_param, int vec) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const EpiArgs e = e_param;  // in registers, not re-read from parameter space
   const int64_t total = (int64_t)M * N;
@@ -1409,8 +1412,8 @@ ns_status split_lo(const float* x, int rows, int cols, int ld, float* lo, cudaSt
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0);
   const int64_t work = vec ? total / 4 : total;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)sm_count() * 8));
-  split_lo_k<<<grid, 256, 0, s>>>(x, rows, cols, ld, lo, vec);
-  return check_launch("ns_gemm operand split");
+  return launch_pdl(split_lo_k, dim3(grid), dim3(256), 0, s, "ns_gemm operand split", x, rows, cols,
+                    ld, lo, vec);
 }
 
 }  // namespace
@@ -1621,8 +1624,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                      15) == 0 && (e.ldc % 4) == 0 && (out_n % 4) == 0;
     const int64_t work = vec ? total / 4 : total;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
-    epi_apply_k<<<grid, 256, 0, stream>>>(out_m, out_n, e, vec);
-    return check_launch("ns_gemm epilogue pass");
+    return launch_pdl(epi_apply_k, dim3(grid), dim3(256), 0, stream, "ns_gemm epilogue pass", out_m,
+                      out_n, e, vec);
   }
   if (pl.splits == 1) return rc;
   const int64_t total = (int64_t)out_m * out_n;
@@ -1632,8 +1635,8 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
                     reinterpret_cast<uintptr_t>(ws)) & 15) == 0 && (e.ldc % 4) == 0 && (out_n % 4) == 0;
   const int64_t work = vec ? total / 4 : total;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), sm_count() * 8));
-  splitk_reduce_k<<<grid, 256, 0, stream>>>(ws, pl.splits, out_m, out_n, e, vec);
-  return check_launch("ns_gemm split-K reduce");
+  return launch_pdl(splitk_reduce_k, dim3(grid), dim3(256), 0, stream, "ns_gemm split-K reduce", ws,
+                    pl.splits, out_m, out_n, e, vec);
 }
 
 ns_status split_operand(const float* x, int rows, int cols, int ld, float* lo, cudaStream_t s) {

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias 
                                                   float eps, const float* __restrict__ bias,
                                                   const float* __restrict__ resid, float* x_out,
                                                   float* __restrict__ out_lo) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -100,6 +101,8 @@ __global__ void __launch_bounds__(256) ln_fwd_vec(const float* x,  // may alias 
 __global__ void resid_bias_add_k(const float* raw, const float* __restrict__ bias,
                                  const float* __restrict__ resid, float* x_out,
                                  int64_t rows, int dim) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n = rows * dim;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -113,6 +116,8 @@ __global__ void __launch_bounds__(256) ln_fwd_any(const float* __restrict__ x,
                                                   float* __restrict__ out, float* __restrict__ mean,
                                                   float* __restrict__ rstd, int rows, int dim,
                                                   float eps) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int row = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -153,6 +158,7 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_vec(
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
     float* __restrict__ part_b, int rows, int dim, int rows_per_cta) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   extern __shared__ float red[];  // [kRowsWarps][2][dim]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,6 +270,8 @@ __global__ void __launch_bounds__(256) ln_bwd_any(
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ dresid, float* __restrict__ dx, float* __restrict__ part_g,
     float* __restrict__ part_b, int rows, int dim, int rows_per_cta) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   // One CTA walks its rows; each thread owns columns c = tid + k*256 for the
   // dgamma/dbeta partials (kept in the output workspace directly).
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -318,6 +326,7 @@ __global__ void __launch_bounds__(256) colsum_finish(const float* __restrict__ p
                                                      int N, float* __restrict__ out,
                                                      const float* __restrict__ part2,
                                                      float* __restrict__ out2) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float red[kRowsWarps][32];
   if (blockIdx.y == 1) {
@@ -367,6 +376,7 @@ __global__ void __launch_bounds__(256) colsum_partial(float* __restrict__ y, int
                                                       const float* __restrict__ pre,
                                                       int* __restrict__ done,
                                                       float* __restrict__ out) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float4 red[kRowsWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -509,33 +519,34 @@ ns_status ns_layernorm_fwd_ex(const float* x, const float* bias, const float* re
                         15) == 0;
   if (dim % 4 == 0 && aligned && dim <= 128 * kMaxVec) {
     const int nv = dim / 4;
+    auto launch = [&](auto kernel) {
+      return launch_pdl(kernel, grid, block, 0, s, "ns_layernorm_fwd", x, gamma, beta, out, mean,
+                        rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+    };
     auto go = [&](auto nvt) {
       constexpr int NV = decltype(nvt)::value;
-      if (resid && out_lo)
-        ln_fwd_vec<NV, true, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
-      else if (resid)
-        ln_fwd_vec<NV, true, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
-      else if (out_lo)
-        ln_fwd_vec<NV, false, true><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
-      else
-        ln_fwd_vec<NV, false, false><<<grid, block, 0, s>>>(x, gamma, beta, out, mean, rstd, rows, dim, eps, bias, resid, x_out, out_lo);
+      if (resid && out_lo) return launch(ln_fwd_vec<NV, true, true>);
+      if (resid) return launch(ln_fwd_vec<NV, true, false>);
+      if (out_lo) return launch(ln_fwd_vec<NV, false, true>);
+      return launch(ln_fwd_vec<NV, false, false>);
     };
-    if (nv <= 32) go(std::integral_constant<int, 1>());
-    else if (nv <= 64) go(std::integral_constant<int, 2>());
-    else if (nv <= 128) go(std::integral_constant<int, 4>());
-    else go(std::integral_constant<int, 8>());
-    return check_launch("ns_layernorm_fwd");
+    if (nv <= 32) return go(std::integral_constant<int, 1>());
+    if (nv <= 64) return go(std::integral_constant<int, 2>());
+    if (nv <= 128) return go(std::integral_constant<int, 4>());
+    return go(std::integral_constant<int, 8>());
   }
   const float* xin = x;
   if (resid) {
     const int64_t n = (int64_t)rows * dim;
-    resid_bias_add_k<<<(unsigned)std::min<int64_t>(ceil_div64(n, 256), 148 * 8), 256, 0, s>>>(
-        x, bias, resid, x_out, rows, dim);
-    { ns_status _rc = check_launch("ns_layernorm_fwd residual"); if (_rc != NS_OK) return _rc; }
+    const ns_status rc = launch_pdl(
+        resid_bias_add_k, dim3((unsigned)std::min<int64_t>(ceil_div64(n, 256), 148 * 8)),
+        dim3(256), 0, s, "ns_layernorm_fwd residual", x, bias, resid, x_out, (int64_t)rows, dim);
+    if (rc != NS_OK) return rc;
     xin = x_out;
   }
-  ln_fwd_any<<<grid, block, 0, s>>>(xin, gamma, beta, out, mean, rstd, rows, dim, eps);
-  { ns_status _rc = check_launch("ns_layernorm_fwd"); if (_rc != NS_OK) return _rc; }
+  const ns_status rc = launch_pdl(ln_fwd_any, grid, block, 0, s, "ns_layernorm_fwd", xin, gamma,
+                                  beta, out, mean, rstd, rows, dim, eps);
+  if (rc != NS_OK) return rc;
   if (out_lo) return ns_split_lo(out, rows, dim, dim, out_lo, stream);
   return NS_OK;
 }
@@ -566,45 +577,40 @@ ns_status ns_layernorm_bwd(const float* dout, const float* x, const float* gamma
   const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dout) |
                        reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
                        reinterpret_cast<uintptr_t>(dresid);
+  // stage 1: dx and the per-CTA partial column sums; stage 2: the ordered sums
+  auto stage1 = [&](auto kernel, size_t smem) {
+    return launch_pdl(kernel, dim3(ctas), block, smem, s, "ns_layernorm_bwd stage 1", dout, x,
+                      gamma, mean, rstd, dresid, dx, part_g, part_b, rows, dim, rpc);
+  };
+  auto stage1_big = [&](auto kernel, size_t smem) {
+    NS_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem), "ns_layernorm_bwd attr");
+    return stage1(kernel, smem);
+  };
+  ns_status rc;
   if (dim % 4 == 0 && (al & 15) == 0 && dim <= 128 * kMaxVec) {
     const int nv = dim / 4;
     const size_t smem = (size_t)kRowsWarps * 2 * dim * sizeof(float);
     if (nv <= 16)  // short rows (the U-Net's last-axis LayerNorms): more rows in flight
-      ln_bwd_vec<1, 8><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
+      rc = stage1(ln_bwd_vec<1, 8>, smem);
     else if (nv <= 32)
-      ln_bwd_vec<1, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
+      rc = stage1(ln_bwd_vec<1, 2>, smem);
     else if (nv <= 64)
-      ln_bwd_vec<2, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
+      rc = stage1(ln_bwd_vec<2, 2>, smem);
     else if (nv <= 96)
-      ln_bwd_vec<3, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
-    else if (nv <= 128) {
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<4, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
-    } else if (nv <= 192) {
-      // dim <= 768: six float4 per lane, not eight (registers decide occupancy here)
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<6, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<6, 2><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
-    } else {
-      NS_TRY_CUDA(cudaFuncSetAttribute(ln_bwd_vec<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem), "ns_layernorm_bwd attr");
-      ln_bwd_vec<8, 1><<<ctas, block, smem, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g,
-                                              part_b, rows, dim, rpc);
-    }
+      rc = stage1(ln_bwd_vec<3, 2>, smem);
+    else if (nv <= 128)
+      rc = stage1_big(ln_bwd_vec<4, 2>, smem);
+    else if (nv <= 192)  // dim <= 768: six float4 per lane, not eight (registers decide occupancy)
+      rc = stage1_big(ln_bwd_vec<6, 2>, smem);
+    else
+      rc = stage1_big(ln_bwd_vec<8, 1>, smem);
   } else {
-    ln_bwd_any<<<ctas, block, 0, s>>>(dout, x, gamma, mean, rstd, dresid, dx, part_g, part_b,
-                                      rows, dim, rpc);
+    rc = stage1(ln_bwd_any, 0);
   }
-  { ns_status _rc = check_launch("ns_layernorm_bwd stage 1"); if (_rc != NS_OK) return _rc; }
-  colsum_finish<<<dim3(ceil_div(dim, 32), 2), 256, 0, s>>>(part_g, ctas, dim, dgamma, part_b, dbeta);
-  return check_launch("ns_layernorm_bwd stage 2");
+  if (rc != NS_OK) return rc;
+  return launch_pdl(colsum_finish, dim3(ceil_div(dim, 32), 2), dim3(256), 0, s,
+                    "ns_layernorm_bwd stage 2", part_g, ctas, dim, dgamma, part_b, dbeta);
 }
 
 size_t ns_bias_grad_workspace_size(int M, int N) {
@@ -632,8 +638,9 @@ ns_status ns_bias_grad(const float* dY, int M, int N, float* db, void* workspace
   int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
                                      (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
   NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad counters");
-  colsum_partial<false, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, nullptr, nullptr, done, db);
-  return check_launch("ns_bias_grad");
+  return launch_pdl(colsum_partial<false, false>, dim3(ceil_div(N, 128), chunks), dim3(256),
+                    0, s, "ns_bias_grad", const_cast<float*>(dY), M, N, rpc, part, nullptr, nullptr,
+                    done, db);
 }
 
 ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy_lo,
@@ -650,8 +657,9 @@ ns_status ns_bias_grad_split(const float* dY, int M, int N, float* db, float* dy
   int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
                                      (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
   NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad_split counters");
-  colsum_partial<true, false><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(const_cast<float*>(dY), M, N, rpc, part, dy_lo, nullptr, done, db);
-  return check_launch("ns_bias_grad_split");
+  return launch_pdl(colsum_partial<true, false>, dim3(ceil_div(N, 128), chunks), dim3(256), 0,
+                    s, "ns_bias_grad_split", const_cast<float*>(dY), M, N, rpc, part, dy_lo,
+                    nullptr, done, db);
 }
 
 ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, float* db, float* dy_lo,
@@ -670,8 +678,8 @@ ns_status ns_bias_grad_split_gelu(float* dY, const float* pre, int M, int N, flo
   int* done = reinterpret_cast<int*>(static_cast<char*>(workspace) +
                                      (((size_t)chunks * N * sizeof(float) + 255) & ~(size_t)255));
   NS_TRY_CUDA(cudaMemsetAsync(done, 0, (size_t)ceil_div(N, 128) * sizeof(int), s), "ns_bias_grad_split_gelu counters");
-  colsum_partial<true, true><<<dim3(ceil_div(N, 128), chunks), 256, 0, s>>>(dY, M, N, rpc, part, dy_lo, pre, done, db);
-  return check_launch("ns_bias_grad_split_gelu");
+  return launch_pdl(colsum_partial<true, true>, dim3(ceil_div(N, 128), chunks), dim3(256), 0,
+                    s, "ns_bias_grad_split_gelu", dY, M, N, rpc, part, dy_lo, pre, done, db);
 }
 
 }  // extern "C"

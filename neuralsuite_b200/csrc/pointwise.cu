@@ -17,6 +17,8 @@ int pointwise_grid(int64_t n4) {
 }
 
 __global__ void gelu_fwd_k(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -31,6 +33,7 @@ __global__ void gelu_fwd_k(const float* __restrict__ x, float* __restrict__ y, i
 // y = gelu(x) and y_lo = y - trunc_tf32(y) (the next GEMM's operand split).
 __global__ void gelu_fwd_lo_k(const float* __restrict__ x, float* __restrict__ y,
                               float* __restrict__ y_lo, int64_t n) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -50,6 +53,8 @@ __global__ void gelu_fwd_lo_k(const float* __restrict__ x, float* __restrict__ y
 
 __global__ void gelu_bwd_k(const float* __restrict__ d, const float* __restrict__ x,
                            float* __restrict__ dx, int64_t n) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -66,6 +71,7 @@ __global__ void gelu_bwd_k(const float* __restrict__ d, const float* __restrict_
 
 __global__ void add_k(const float* __restrict__ a, const float* __restrict__ b,
                       float* __restrict__ o, int64_t n) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -88,6 +94,7 @@ __global__ void __launch_bounds__(256) ce_rows_k(const float* __restrict__ logit
                                                  float* __restrict__ dlogits,
                                                  float* __restrict__ row_loss,
                                                  int32_t* __restrict__ err) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -120,6 +127,8 @@ __global__ void __launch_bounds__(256) ce_rows_k(const float* __restrict__ logit
 // Ordered single-CTA reduction: out[0] = (sum of x[0..n)) / div.
 __global__ void __launch_bounds__(1024) sum_finish_k(const float* __restrict__ x, int64_t n,
                                                      float div, float* __restrict__ out) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float sh[32];
   float s = 0.f;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
@@ -136,6 +145,8 @@ __global__ void __launch_bounds__(1024) sum_finish_k(const float* __restrict__ x
 // Per-CTA partial sums of squares (grid-stride, float4), one float per CTA.
 __global__ void __launch_bounds__(256) sumsq_partial_k(const float* __restrict__ x, int64_t n,
                                                        float* __restrict__ part) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float sh[8];
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -159,6 +170,8 @@ __global__ void __launch_bounds__(256) sumsq_partial_k(const float* __restrict__
 // ClipGradients' rescale (train_llm.cpp:121-128) with the norm read on device.
 __global__ void clip_scale_k(float* __restrict__ x, int64_t n, const float* __restrict__ sumsq,
                              float max_norm) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   const float norm = __fsqrt_rn(sumsq[0]);
   if (!(norm > max_norm && norm > 0.0f)) return;
   const float scale = __fdiv_rn(max_norm, norm);
@@ -189,32 +202,32 @@ ns_status ns_gelu_fwd(const float* x, float* y, int64_t n, void* stream) {
   NS_REQUIRE(n >= 0, "ns_gelu_fwd: n < 0");
   NS_REQUIRE(al16(x) && al16(y), "ns_gelu_fwd: pointers must be 16-byte aligned");
   if (n == 0) return NS_OK;
-  gelu_fwd_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, y, n);
-  return check_launch("ns_gelu_fwd");
+  return launch_pdl(gelu_fwd_k, dim3(pointwise_grid(ceil_div64(n, 4))), dim3(256), 0,
+                    as_stream(stream), "ns_gelu_fwd", x, y, n);
 }
 
 ns_status ns_gelu_fwd_lo(const float* x, float* y, float* y_lo, int64_t n, void* stream) {
   NS_REQUIRE(n >= 0, "ns_gelu_fwd_lo: n < 0");
   NS_REQUIRE(al16(x) && al16(y) && al16(y_lo), "ns_gelu_fwd_lo: pointers must be 16-byte aligned");
   if (n == 0) return NS_OK;
-  gelu_fwd_lo_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, y, y_lo, n);
-  return check_launch("ns_gelu_fwd_lo");
+  return launch_pdl(gelu_fwd_lo_k, dim3(pointwise_grid(ceil_div64(n, 4))), dim3(256), 0,
+                    as_stream(stream), "ns_gelu_fwd_lo", x, y, y_lo, n);
 }
 
 ns_status ns_gelu_bwd(const float* dout, const float* x, float* dx, int64_t n, void* stream) {
   NS_REQUIRE(n >= 0, "ns_gelu_bwd: n < 0");
   NS_REQUIRE(al16(x) && al16(dout) && al16(dx), "ns_gelu_bwd: pointers must be 16-byte aligned");
   if (n == 0) return NS_OK;
-  gelu_bwd_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(dout, x, dx, n);
-  return check_launch("ns_gelu_bwd");
+  return launch_pdl(gelu_bwd_k, dim3(pointwise_grid(ceil_div64(n, 4))), dim3(256), 0,
+                    as_stream(stream), "ns_gelu_bwd", dout, x, dx, n);
 }
 
 ns_status ns_add(const float* a, const float* b, float* out, int64_t n, void* stream) {
   NS_REQUIRE(n >= 0, "ns_add: n < 0");
   NS_REQUIRE(al16(a) && al16(b) && al16(out), "ns_add: pointers must be 16-byte aligned");
   if (n == 0) return NS_OK;
-  add_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(a, b, out, n);
-  return check_launch("ns_add");
+  return launch_pdl(add_k, dim3(pointwise_grid(ceil_div64(n, 4))), dim3(256), 0, as_stream(stream),
+                    "ns_add", a, b, out, n);
 }
 
 size_t ns_cross_entropy_workspace_size(int rows, int classes) {
@@ -231,11 +244,12 @@ ns_status ns_cross_entropy(const float* logits, const int32_t* targets, int rows
              "ns_cross_entropy: workspace too small");
   cudaStream_t s = as_stream(stream);
   float* row_loss = static_cast<float*>(workspace);
-  ce_rows_k<<<ceil_div(rows, 8), 256, 0, s>>>(logits, targets, rows, classes, denom, dlogits,
-                                              row_loss, err_flag);
-  { ns_status _rc = check_launch("ns_cross_entropy rows"); if (_rc != NS_OK) return _rc; }
-  sum_finish_k<<<1, 1024, 0, s>>>(row_loss, rows, (float)rows, loss_out);
-  return check_launch("ns_cross_entropy finish");
+  const ns_status rc = launch_pdl(ce_rows_k, dim3(ceil_div(rows, 8)), dim3(256), 0, s,
+                                  "ns_cross_entropy rows", logits, targets, rows, classes, denom,
+                                  dlogits, row_loss, err_flag);
+  if (rc != NS_OK) return rc;
+  return launch_pdl(sum_finish_k, dim3(1), dim3(1024), 0, s, "ns_cross_entropy finish", row_loss,
+                    rows, (float)rows, loss_out);
 }
 
 size_t ns_sumsq_workspace_size(int64_t n) {
@@ -251,19 +265,19 @@ ns_status ns_sumsq(const float* x, int64_t n, float* out, void* workspace, size_
              "ns_sumsq: workspace too small");
   cudaStream_t s = as_stream(stream);
   float* part = static_cast<float*>(workspace);
-  sumsq_partial_k<<<kSumsqCtas, 256, 0, s>>>(x, n, part);
-  { ns_status _rc = check_launch("ns_sumsq partial"); if (_rc != NS_OK) return _rc; }
-  sum_finish_k<<<1, 1024, 0, s>>>(part, kSumsqCtas, 1.0f, out);
-  return check_launch("ns_sumsq finish");
+  const ns_status rc = launch_pdl(sumsq_partial_k, dim3(kSumsqCtas), dim3(256), 0, s,
+                                  "ns_sumsq partial", x, n, part);
+  if (rc != NS_OK) return rc;
+  return launch_pdl(sum_finish_k, dim3(1), dim3(1024), 0, s, "ns_sumsq finish", part, kSumsqCtas,
+                    1.0f, out);
 }
 
 ns_status ns_clip_scale(float* x, int64_t n, const float* sumsq, float max_norm, void* stream) {
   NS_REQUIRE(n >= 0, "ns_clip_scale: n < 0");
   NS_REQUIRE(al16(x), "ns_clip_scale: x must be 16-byte aligned");
   if (n == 0) return NS_OK;
-  clip_scale_k<<<pointwise_grid(ceil_div64(n, 4)), 256, 0, as_stream(stream)>>>(x, n, sumsq,
-                                                                                max_norm);
-  return check_launch("ns_clip_scale");
+  return launch_pdl(clip_scale_k, dim3(pointwise_grid(ceil_div64(n, 4))), dim3(256), 0,
+                    as_stream(stream), "ns_clip_scale", x, n, sumsq, max_norm);
 }
 
 }  // extern "C"
@@ -347,10 +361,10 @@ extern "C" ns_status ns_cross_entropy_noalloc(const float* logits, const int32_t
   ns_status rc = ce_noalloc_scratch(&row_loss);
   if (rc != NS_OK) return rc;
   cudaStream_t s = as_stream(stream);
-  ce_rows_k<<<ceil_div(rows, 8), 256, 0, s>>>(logits, targets, rows, classes, denom, dlogits,
-                                              row_loss, err_flag);
-  rc = check_launch("ns_cross_entropy_noalloc rows");
+  rc = launch_pdl(ce_rows_k, dim3(ceil_div(rows, 8)), dim3(256), 0, s,
+                  "ns_cross_entropy_noalloc rows", logits, targets, rows, classes, denom, dlogits,
+                  row_loss, err_flag);
   if (rc != NS_OK) return rc;
-  sum_finish_k<<<1, 1024, 0, s>>>(row_loss, rows, (float)rows, loss_out);
-  return check_launch("ns_cross_entropy_noalloc finish");
+  return launch_pdl(sum_finish_k, dim3(1), dim3(1024), 0, s, "ns_cross_entropy_noalloc finish",
+                    row_loss, rows, (float)rows, loss_out);
 }

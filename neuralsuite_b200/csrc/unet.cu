@@ -74,6 +74,7 @@ int grid_for(int64_t work) {
 // y = ReLU(f + x) (ResidualBlock::Forward's sum then Activation(kRelu)).
 __global__ void resid_relu_k(const float* __restrict__ f, const float* __restrict__ x, int64_t n,
                              float* __restrict__ y) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -85,6 +86,7 @@ __global__ void resid_relu_k(const float* __restrict__ f, const float* __restric
 // dsum = y > 0 ? dy : 0 (ReluBackward on the pre-activation sum, whose sign
 // is that of the output).  dsum may be dy.
 __global__ void relu_mask_k(const float* dy, const float* __restrict__ y, int64_t n, float* dsum) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -94,6 +96,7 @@ __global__ void relu_mask_k(const float* dy, const float* __restrict__ y, int64_
 // y[bc][i][j] = x[bc][i/2][j/2]: one thread per input element writes its
 // 2 x 2 block as two 8-byte stores (32-bit indexing: n < 2^31).
 __global__ void up2_k(const float* __restrict__ x, int n, int W, float* __restrict__ y) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int row = i / W, j = i - row * W;  // row = bc * H + r
@@ -106,6 +109,7 @@ __global__ void up2_k(const float* __restrict__ x, int n, int W, float* __restri
 
 // dx[bc][i][j] = dy[2i][2j] + dy[2i][2j+1] + dy[2i+1][2j] + dy[2i+1][2j+1], in that order.
 __global__ void up2_bwd_k(const float* __restrict__ dy, int n, int W, float* __restrict__ dx) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
   pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int row = i / W, j = i - row * W;
@@ -125,6 +129,8 @@ __global__ void up2_bwd_k(const float* __restrict__ dy, int n, int W, float* __r
 // (p - t)^2 into part[blockIdx.x] (an ordered tree inside the CTA).
 __global__ void mse_k(const float* __restrict__ p, const float* __restrict__ t, int64_t n,
                       float denom, float* __restrict__ d, float* __restrict__ part) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   __shared__ float red[256];
   float s = 0.0f;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -145,6 +151,8 @@ __global__ void mse_k(const float* __restrict__ p, const float* __restrict__ t, 
 // loss = (sum of the CTA partials in order) / n.
 __global__ void mse_finish_k(const float* __restrict__ part, int nparts, float n,
                              float* __restrict__ loss) {
+  pdl_wait();     // the previous kernel's writes are visible (launched by launch_pdl)
+  pdl_trigger();  // the next kernel, if launched as a programmatic dependent, may start
   if (threadIdx.x == 0) {
     float s = 0.0f;
     for (int i = 0; i < nparts; ++i) s += part[i];
@@ -190,8 +198,8 @@ ns_status res_ln_fwd(ns_unet* u, int l, int B, cudaStream_t s) {
   const int64_t n = level_numel(u, l, B);
   ns_status rc = conv_fwd(u, 6 + l, u->a[l], u->t0, B, s);
   if (rc != NS_OK) return rc;
-  resid_relu_k<<<grid_for(n), 256, 0, s>>>(u->t0, u->a[l], n, u->r[l]);
-  rc = check_launch("ns_unet residual");
+  rc = launch_pdl(resid_relu_k, dim3(grid_for(n)), dim3(256), 0, s, "ns_unet residual", u->t0,
+                  u->a[l], n, u->r[l]);
   if (rc != NS_OK) return rc;
   const int rows = (int)(n / u->lvl_hw[l]);
   return ns_layernorm_fwd(u->r[l], u->params + u->ln_off[l][0], u->params + u->ln_off[l][1],
@@ -208,8 +216,8 @@ ns_status res_ln_bwd(ns_unet* u, int l, const float* de, float* da, int B, cudaS
                                   u->grads + u->ln_off[l][1], rows, u->lvl_hw[l], u->ln_ws,
                                   u->ln_ws_bytes, s);
   if (rc != NS_OK) return rc;
-  relu_mask_k<<<grid_for(n), 256, 0, s>>>(u->t1, u->r[l], n, u->t1);
-  rc = check_launch("ns_unet relu backward");
+  rc = launch_pdl(relu_mask_k, dim3(grid_for(n)), dim3(256), 0, s, "ns_unet relu backward", u->t1,
+                  u->r[l], n, u->t1);
   if (rc != NS_OK) return rc;
   rc = conv_bwd(u, 6 + l, u->a[l], u->t1, u->t2, B, s);
   if (rc != NS_OK) return rc;
@@ -379,16 +387,14 @@ ns_status ns_unet_forward(ns_unet* u, const float* x, int B, void* stream) {
   if (rc == NS_OK) rc = conv_fwd(u, 2, u->e[1], u->a[2], B, s);          // down2
   if (rc == NS_OK) rc = res_ln_fwd(u, 2, B, s);                          // m
   if (rc != NS_OK) return rc;
-  up2_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->e[2], (int)level_numel(u, 2, B), S / 4,
-                                                       u->up_a);
-  rc = check_launch("ns_unet upsample");
+  rc = launch_pdl(up2_k, dim3(grid_for(level_numel(u, 2, B))), dim3(256), 0, s, "ns_unet upsample",
+                  u->e[2], (int)level_numel(u, 2, B), S / 4, u->up_a);
   if (rc == NS_OK) rc = conv_fwd(u, 3, u->up_a, u->t0, B, s);            // up1
   if (rc == NS_OK) rc = ns_add(u->t0, u->e[1], u->a[3], level_numel(u, 3, B), s);  // + e1
   if (rc == NS_OK) rc = res_ln_fwd(u, 3, B, s);                          // u1
   if (rc != NS_OK) return rc;
-  up2_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->e[3], (int)level_numel(u, 3, B), S / 2,
-                                                       u->up_b);
-  rc = check_launch("ns_unet upsample");
+  rc = launch_pdl(up2_k, dim3(grid_for(level_numel(u, 3, B))), dim3(256), 0, s, "ns_unet upsample",
+                  u->e[3], (int)level_numel(u, 3, B), S / 2, u->up_b);
   if (rc == NS_OK) rc = conv_fwd(u, 4, u->up_b, u->t0, B, s);            // up0
   if (rc == NS_OK) rc = ns_add(u->t0, u->e[0], u->a[4], level_numel(u, 4, B), s);  // + e0
   if (rc == NS_OK) rc = res_ln_fwd(u, 4, B, s);                          // u0
@@ -401,12 +407,11 @@ ns_status ns_unet_loss_backward(ns_unet* u, const float* target, void* stream) {
   NS_REQUIRE(u->B > 0, "ns_unet_loss_backward: no forward pass yet");
   cudaStream_t s = as_stream(stream);
   const int64_t n = (int64_t)u->B * u->in_ch * u->S * u->S;
-  mse_k<<<kMseBlocks, 256, 0, s>>>(u->out, target, n, (float)((double)n * u->world), u->dout,
-                                   u->loss_part);
-  ns_status rc = check_launch("ns_unet mse");
+  ns_status rc = launch_pdl(mse_k, dim3(kMseBlocks), dim3(256), 0, s, "ns_unet mse", u->out,
+                            target, n, (float)((double)n * u->world), u->dout, u->loss_part);
   if (rc != NS_OK) return rc;
-  mse_finish_k<<<1, 32, 0, s>>>(u->loss_part, kMseBlocks, (float)n, u->small);
-  return check_launch("ns_unet mse finish");
+  return launch_pdl(mse_finish_k, dim3(1), dim3(32), 0, s, "ns_unet mse finish", u->loss_part,
+                    kMseBlocks, (float)n, u->small);
 }
 
 ns_status ns_unet_backward(ns_unet* u, void* stream) {
@@ -421,15 +426,15 @@ ns_status ns_unet_backward(ns_unet* u, void* stream) {
   if (rc == NS_OK) rc = res_ln_bwd(u, 4, u->t0, u->g0, B, s);                    // ds0
   if (rc == NS_OK) rc = conv_bwd(u, 4, u->up_b, u->g0, u->t0, B, s);             // up0
   if (rc != NS_OK) return rc;
-  up2_bwd_k<<<grid_for(level_numel(u, 3, B)), 256, 0, s>>>(u->t0, (int)level_numel(u, 3, B),
-                                                           S / 2, u->e[3]);     // du1
-  rc = check_launch("ns_unet upsample backward");
+  rc = launch_pdl(up2_bwd_k, dim3(grid_for(level_numel(u, 3, B))), dim3(256), 0, s,
+                  "ns_unet upsample backward", u->t0, (int)level_numel(u, 3, B), S / 2,
+                  u->e[3]);  // du1
   if (rc == NS_OK) rc = res_ln_bwd(u, 3, u->e[3], u->g1, B, s);                  // ds1
   if (rc == NS_OK) rc = conv_bwd(u, 3, u->up_a, u->g1, u->t0, B, s);             // up1
   if (rc != NS_OK) return rc;
-  up2_bwd_k<<<grid_for(level_numel(u, 2, B)), 256, 0, s>>>(u->t0, (int)level_numel(u, 2, B),
-                                                           S / 4, u->e[2]);     // dm
-  rc = check_launch("ns_unet upsample backward");
+  rc = launch_pdl(up2_bwd_k, dim3(grid_for(level_numel(u, 2, B))), dim3(256), 0, s,
+                  "ns_unet upsample backward", u->t0, (int)level_numel(u, 2, B), S / 4,
+                  u->e[2]);  // dm
   if (rc == NS_OK) rc = res_ln_bwd(u, 2, u->e[2], u->t0, B, s);                  // d a2
   if (rc == NS_OK) rc = conv_bwd(u, 2, u->e[1], u->t0, u->t1, B, s);             // down2
   if (rc == NS_OK) rc = ns_add(u->t1, u->g1, u->e[3], level_numel(u, 1, B), s);    // de1
