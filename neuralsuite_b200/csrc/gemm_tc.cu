@@ -53,6 +53,11 @@ constexpr int kMaxTailTiles = 128;
 constexpr int kSkRegionCounters = 16 * kMaxTailTiles;
 constexpr int kSkRegions = 16;
 __device__ unsigned g_sk_count[kSkRegions * kSkRegionCounters];
+// Work counters of the CTA-pair kernel's dynamic schedule, one per region (128
+// bytes apart), taken in turn like the stream-K regions; each returns to 0
+// when the launch that used it has handed out all its work.
+constexpr int kPairCounterStride = 32;
+__device__ unsigned g_pair_next[kSkRegions * kPairCounterStride];
 
 namespace {
 
@@ -79,17 +84,27 @@ struct KParams {
   int trans_out;
   int out_m, out_n;  // C's shape
   // Stream-K tail (CTA-pair kernel only).  The first dp_units units (tiles x
-  // splits) run whole, one cluster each in turn; the k-blocks of the last
-  // sk_tiles tiles (splits == 1) are cut into sk_slots equal runs, one per
-  // cluster.  Each run leaves its partial tile in sk_ws
-  // ([cluster][run 0/1][cta 0/1][column][row], 128 x BN floats per CTA);
-  // per tile, CTA half and fold warp, a counter in sk_count records the
-  // partials in, and the warp that completes the set adds them in k order
+  // splits) run whole, one cluster each; the k-blocks of the last sk_tiles
+  // tiles (splits == 1) are cut into sk_slots equal runs (as many as the
+  // launch has clusters), one cluster each.  Each run leaves its partial
+  // tiles in sk_ws ([run][piece 0/1][cta 0/1][column][row], 128 x BN floats
+  // per CTA); per tile, CTA half and fold warp, a counter in sk_count records
+  // the partials in, and the warp that completes the set adds them in k order
   // and runs the epilogue.  No CTA waits on another.
   int dp_units;
   int sk_tiles, sk_slots;
   float* sk_ws;
   unsigned* sk_count;
+  // CTA-pair kernel schedule.  Work items: the dp_units units, then the
+  // tail's sk_slots runs (item dp_units + s is run s).  dyn = 0: cluster c
+  // takes items c, c + clusters, ... below dp_units, then run c.  dyn = 1:
+  // cluster c starts on item c and then takes the next item from next_ctr
+  // whenever its producer is ready for one, so clusters that start late
+  // (their SMs held by another stream's kernel, e.g. a collective) take
+  // fewer items.  Every item is computed the same way whichever cluster
+  // takes it: the results are bit-identical.
+  int dyn;
+  unsigned* next_ctr;
 };
 
 // Descriptor of MMA k-step kk (8 tf32) of an operand tile at `base`.
@@ -127,29 +142,48 @@ __device__ __forceinline__ int tail_slot(const KParams& p, int i) {
   return (int)((unsigned)((i + 1) * p.sk_slots - 1) / (unsigned)(p.sk_tiles * p.kb_total));
 }
 
-// The sequence of work one cluster of the pair kernel takes: its
-// data-parallel units, then its stream-K run (one or two pieces).  Producer,
-// MMA issuer and fold warps walk the same sequence.
+// Work items of the pair kernel: the data-parallel units, then the tail's runs.
+__device__ __forceinline__ int pair_items(const KParams& p) {
+  return p.dp_units + (p.sk_tiles > 0 ? p.sk_slots : 0);
+}
+
+// Item j of cluster `cluster` under the fixed schedule (-1: none left).
+__device__ __forceinline__ int static_item(const KParams& p, int j, int cluster, int clusters) {
+  const int nd = p.dp_units > cluster ? (p.dp_units - cluster + clusters - 1) / clusters : 0;
+  if (j < nd) return cluster + j * clusters;
+  if (j == nd && p.sk_tiles > 0 && cluster < p.sk_slots) return p.dp_units + cluster;
+  return -1;
+}
+
+// The sequence of work one cluster of the pair kernel takes: items (a unit,
+// or a stream-K run of one or two pieces) in the order `take` hands them out.
+// Producer, MMA issuer and fold warps walk the same sequence.
 struct PairWork {
-  int u, a, b;  // next data-parallel unit; remaining tail k-blocks [a, b)
+  int j;     // items taken so far
+  int a, b;  // remaining k-blocks [a, b) of the current tail run
   int tm, tn, split, kb0, kb1;
   int tail;  // tile index within the tail, or -1 for a data-parallel unit
-  int run;   // 0 / 1: first or second piece of this cluster's run
-  __device__ __forceinline__ PairWork(const KParams& p, int cluster)
-      : u(cluster), a(0), b(0), tm(0), tn(0), split(0), kb0(0), kb1(0), tail(-1), run(-1) {
-    if (p.sk_tiles > 0) {
-      a = tail_begin(p, cluster);
-      b = tail_begin(p, cluster + 1);
+  int run;   // 0 / 1: first or second piece of the current tail run
+  int slot;  // the current tail run
+  __device__ __forceinline__ PairWork()
+      : j(0), a(0), b(0), tm(0), tn(0), split(0), kb0(0), kb1(0), tail(-1), run(-1), slot(-1) {}
+  // take(j) returns item j of this cluster, or -1 when there is none (or the
+  // CTA is aborting).
+  template <typename Take>
+  __device__ __forceinline__ bool next(const KParams& p, Take&& take) {
+    if (a >= b) {
+      const int v = take(j++);
+      if (v < 0) return false;
+      if (v < p.dp_units) {
+        decode_unit(p, v, tm, tn, split, kb0, kb1);
+        tail = -1;
+        return true;
+      }
+      slot = v - p.dp_units;
+      a = tail_begin(p, slot);
+      b = tail_begin(p, slot + 1);
+      run = -1;
     }
-  }
-  __device__ __forceinline__ bool next(const KParams& p, int step) {
-    if (u < p.dp_units) {
-      decode_unit(p, u, tm, tn, split, kb0, kb1);
-      tail = -1;
-      u += step;
-      return true;
-    }
-    if (a >= b) return false;
     const int t = a / p.kb_total;
     kb0 = a - t * p.kb_total;
     kb1 = min(p.kb_total, kb0 + (b - a));
@@ -173,6 +207,7 @@ struct PairWork {
 constexpr int kChunk = 2;  // default; KParams::chunk is what the kernels use
 
 thread_local int t_chunk = kChunk;  // per host thread: see set_accumulation_chunk
+thread_local int t_pair_dyn = 1;    // per host thread: see set_pair_schedule
 
 template <int BN, int STAGES, bool PRE>
 struct Layout {
@@ -936,6 +971,13 @@ ns_status launch(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& tb,
 // BN (the tile's second extent: 256, 192 or 128) is a template parameter so
 // that the planner can pick the width that packs a shape's tiles best onto
 // the 74 pairs; narrower tiles leave room for a fourth stage.
+//
+// Work ring of the dynamic schedule: entries in flight between the scheduler
+// and the other roles, and the readers of each entry (the even CTA's MMA warp
+// and fold warps, the odd CTA's producer thread and fold warps).
+constexpr int kRing = 4;
+constexpr int kRingReaders = 1 + kWideFoldThreads / 32 + 1 + kWideFoldThreads / 32;
+
 template <int BN>
 struct PairLayout {
   static constexpr uint32_t kA = kBM * kBK * 4;         // 16 KB: this CTA's 128 rows of A
@@ -944,8 +986,11 @@ struct PairLayout {
   static constexpr uint32_t kStage = 2 * kRaw;  // raw A | raw B | lo A | lo B
   static constexpr int kStages = (4 * kStage + 2048 <= 232448) ? 4 : 3;
   static constexpr uint32_t kBars = kStages * kStage;
-  static constexpr uint32_t kNumBars = 3 * kStages + 5;
-  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16;
+  // stage full / lo full / empty, 2 chunk full, 2 chunk empty, drain; the
+  // work ring's full and empty barriers
+  static constexpr uint32_t kNumBars = 3 * kStages + 5 + 2 * kRing;
+  // barriers, TMEM address + abort flag (16 B), work ring entries
+  static constexpr uint32_t kBytes = kBars + kNumBars * 8 + 16 + 4 * kRing;
   static constexpr uint32_t kDynSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kDynSmem <= 232448, "shared memory budget");
@@ -979,6 +1024,115 @@ __device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
+__device__ __forceinline__ void st_cluster(uint32_t cluster_addr, int v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// mbarrier phase test with acquire at cluster scope: the arrives it pairs
+// with may come from the other CTA of the pair (release.cluster).
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a work-ring barrier (false: aborting or out of time, as
+// mbar_wait).
+__device__ __forceinline__ bool ring_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort = 1;
+        atomicExch(&g_timeout, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// Dynamic schedule: cluster c starts on item c (no counter round trip before
+// the first loads); the launch's counter hands out items clusters, clusters +
+// 1, ... after that.  The work ring carries them: kRing entries in each CTA
+// of the pair, with a full barrier per entry in each CTA (one arrive: the
+// scheduler's) and an empty barrier per entry in the even CTA (one arrive per
+// reader: kRingReaders).  The scheduler is the even CTA's producer thread: it
+// takes the cluster's next item from the counter when it needs one and writes
+// it to entry jr % kRing of both CTAs (jr: the cluster's items after its
+// first); the other roles read it there.
+__device__ __forceinline__ int first_item(const KParams& p, int cluster) {
+  return cluster < pair_items(p) ? cluster : -1;
+}
+
+struct PairRing {
+  uint32_t full0, empty0;  // barrier addresses of entry 0 (entry i: + 8 i)
+  volatile int* entry;     // this CTA's entries
+  volatile int* abort;
+};
+
+// Scheduler: the cluster's item after its first jr + 1 (-1: none left; ok =
+// false on abort).
+__device__ __forceinline__ int ring_put(const KParams& p, const PairRing& r, int jr, bool& ok) {
+  const int i = jr % kRing;
+  // entry i last held item jr - kRing: wait until every reader has it
+  if (jr >= kRing && !ring_wait(r.empty0 + 8u * i, (uint32_t)((jr / kRing) + 1) & 1u, r.abort)) {
+    ok = false;
+    return -1;
+  }
+  // Draws: every cluster with a first item draws until it is handed none, so
+  // a launch makes exactly `total` draws (total - clusters items, then one
+  // empty-handed draw per cluster; with fewer items than clusters, one each
+  // by the clusters that had one).  The last draw puts the counter back to 0
+  // for the next launch that uses it.
+  const unsigned total = (unsigned)pair_items(p);
+  const unsigned raw = atomicAdd(p.next_ctr, 1u);
+  if (raw == total - 1) atomicExch(p.next_ctr, 0u);
+  const unsigned v = raw + cluster_count_x();
+  const int item = v < total ? (int)v : -1;
+  volatile int* e = r.entry + i;
+  *e = item;
+  st_cluster(map_rank(smem_u32(const_cast<int*>(e)), 1), item);
+  mbar_arrive(r.full0 + 8u * i);
+  remote_arrive(map_rank(r.full0 + 8u * i, 1));
+  return item;
+}
+
+// Reader (one thread): the cluster's item after its first jr + 1, then the
+// entry is released.
+__device__ __forceinline__ int ring_get(const PairRing& r, uint32_t rank, int jr, bool& ok) {
+  const int i = jr % kRing;
+  if (!ring_wait(r.full0 + 8u * i, (uint32_t)(jr / kRing) & 1u, r.abort)) {
+    ok = false;
+    return -1;
+  }
+  const int item = r.entry[i];
+  if (rank == 0)
+    mbar_arrive(r.empty0 + 8u * i);
+  else
+    remote_arrive(map_rank(r.empty0 + 8u * i, 0));
+  return item;
+}
+
+// Reader (a converged warp): lane 0 reads for the warp.
+__device__ __forceinline__ int ring_get_warp(const PairRing& r, uint32_t rank, int jr, bool& ok) {
+  int item = -1, good = 1;
+  if ((threadIdx.x & 31) == 0) {
+    bool o = true;
+    item = ring_get(r, rank, jr, o);
+    good = o ? 1 : 0;
+  }
+  good = __shfl_sync(0xffffffffu, good, 0);
+  item = __shfl_sync(0xffffffffu, item, 0);
+  if (!good) ok = false;
+  return item;
+}
 __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -999,18 +1153,17 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
 
 // A stream-K piece of tail tile w.tail has been accumulated in acc (this fold
 // warp's slice: 32 rows x HB columns of this CTA's half).  The slice goes to
-// the cluster's partial buffer and is counted in; the warp whose partial
-// completes the slice's set (one per cluster whose run covers the tile) adds
-// the partials in k order (cluster order) into acc and returns true, to run
+// the run's partial buffer and is counted in; the warp whose partial
+// completes the slice's set (one per run that covers the tile) adds the
+// partials in k order (run order) into acc and returns true, to run
 // the epilogue; the others return false.  The sum's order does not depend on
 // which warp finishes, so the result is deterministic.
 template <int HB>
-__device__ __forceinline__ bool tail_settle(const KParams& p, const PairWork& w, int cluster,
-                                            uint32_t rank, int fold_warp, int row, int col0,
-                                            float (&acc)[HB]) {
+__device__ __forceinline__ bool tail_settle(const KParams& p, const PairWork& w, uint32_t rank,
+                                            int fold_warp, int row, int col0, float (&acc)[HB]) {
   constexpr size_t kPart = (size_t)kBM * 2 * HB;  // floats of one CTA's partial tile
   const size_t offs = (size_t)col0 * kBM + row;
-  float* mine = p.sk_ws + ((size_t)(cluster * 2 + w.run) * 2 + rank) * kPart + offs;
+  float* mine = p.sk_ws + ((size_t)(w.slot * 2 + w.run) * 2 + rank) * kPart + offs;
 #pragma unroll
   for (int j = 0; j < HB; ++j) __stcg(mine + (size_t)j * kBM, acc[j]);
   const int kbt = p.kb_total;
@@ -1062,6 +1215,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
   const uint32_t drain_bar = bar0 + 8u * (3 * S + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBars + L::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const PairRing ring{bar0 + 8u * (3 * S + 5), bar0 + 8u * (3 * S + 5 + kRing),
+                      reinterpret_cast<volatile int*>(tmem_slot + 4), abort};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -1077,6 +1232,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       mbar_init(che_bar(c), kWideFoldThreads + 8);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(ring.full0 + 8u * i, 1);
+      mbar_init(ring.empty0 + 8u * i, kRingReaders);
+    }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1105,8 +1264,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
       if (lane == 0) {
         uint32_t it = 0;  // stage fills issued (an abort breaks before its own fill)
         bool ok = true;
-        PairWork w(p, unit0);
-        while (ok && w.next(p, unit_step)) {
+        PairWork w;
+        auto take = [&](int j) {
+          if (!p.dyn) return static_item(p, j, unit0, unit_step);
+          if (j == 0) return first_item(p, unit0);
+          return rank == 0 ? ring_put(p, ring, j - 1, ok) : ring_get(ring, rank, j - 1, ok);
+        };
+        while (ok && w.next(p, take)) {
           const int m0 = w.tm * 256 + (int)rank * kBM, n0 = w.tn * BN + (int)rank * HB;
           for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
             const int s = it % S;
@@ -1171,8 +1335,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                              ((uint32_t)(256 >> 4) << 24);
       uint32_t it = 0, cit = 0;
       bool ok = true;
-      PairWork w(p, unit0);
-      while (ok && w.next(p, unit_step)) {
+      PairWork w;
+      auto take = [&](int j) {
+        if (!p.dyn) return static_item(p, j, unit0, unit_step);
+        return j == 0 ? first_item(p, unit0) : ring_get_warp(ring, rank, j - 1, ok);
+      };
+      while (ok && w.next(p, take)) {
         const int kb0 = w.kb0, kb1 = w.kb1;
         for (int c0 = kb0; ok && c0 < kb1; c0 += p.chunk, ++cit) {
           const int cb = cit & 1;
@@ -1239,8 +1407,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     uint32_t cit = 0;
     bool ok = true;
     float acc[HB];
-    PairWork w(p, unit0);
-    while (ok && w.next(p, unit_step)) {
+    PairWork w;
+    auto take = [&](int j) {
+      if (!p.dyn) return static_item(p, j, unit0, unit_step);
+      return j == 0 ? first_item(p, unit0) : ring_get_warp(ring, rank, j - 1, ok);
+    };
+    while (ok && w.next(p, take)) {
       const int tm = w.tm, tn = w.tn, split = w.split, kb0 = w.kb0, kb1 = w.kb1;
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
@@ -1275,7 +1447,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         }
       }
       if (!ok) break;
-      if (w.tail >= 0 && !tail_settle<HB>(p, w, unit0, rank, warp - 4, ew * 32 + lane, col0, acc)) continue;
+      if (w.tail >= 0 && !tail_settle<HB>(p, w, rank, warp - 4, ew * 32 + lane, col0, acc)) continue;
       const int m = tm * 256 + (int)rank * kBM + ew * 32 + lane;
       const int n_base = tn * BN + col0;
       if (p.trans_out) {
@@ -1390,17 +1562,21 @@ ns_status launch_wide(const Plan& pl, const CUtensorMap& ta, const CUtensorMap& 
   return check_launch("ns_gemm tcgen05 wide");
 }
 
-// Device address of this device's stream-K counters (looked up once per device).
-ns_status sk_counters(unsigned** out) {
-  static std::atomic<unsigned*> cache[64];
+// Device address of this device's stream-K counters (which = 0) or pair-kernel
+// work counters (which = 1), looked up once per device.
+ns_status counters(int which, unsigned** out) {
+  static std::atomic<unsigned*> cache[2][64];
   int dev = 0;
   NS_TRY_CUDA(cudaGetDevice(&dev), "ns_gemm device");
-  unsigned* p = dev < 64 ? cache[dev].load(std::memory_order_relaxed) : nullptr;
+  unsigned* p = dev < 64 ? cache[which][dev].load(std::memory_order_relaxed) : nullptr;
   if (!p) {
     void* addr = nullptr;
-    NS_TRY_CUDA(cudaGetSymbolAddress(&addr, g_sk_count), "ns_gemm stream-K counters");
+    if (which == 0)
+      NS_TRY_CUDA(cudaGetSymbolAddress(&addr, g_sk_count), "ns_gemm stream-K counters");
+    else
+      NS_TRY_CUDA(cudaGetSymbolAddress(&addr, g_pair_next), "ns_gemm work counters");
     p = static_cast<unsigned*>(addr);
-    if (dev < 64) cache[dev].store(p, std::memory_order_relaxed);
+    if (dev < 64) cache[which][dev].store(p, std::memory_order_relaxed);
   }
   *out = p;
   return NS_OK;
@@ -1591,15 +1767,30 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
   kp.sk_slots = pl.grid;
   kp.sk_ws = pl.sk_tiles > 0 ? ws : nullptr;
   kp.sk_count = nullptr;
-  if (pl.sk_tiles > 0) {
-    if (!pl.pair || pl.splits != 1 || pl.sk_tiles > kMaxTailTiles || !ws)
-      return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: inconsistent stream-K plan");
-    unsigned* base = nullptr;
-    rc = sk_counters(&base);
-    if (rc != NS_OK) return rc;
+  kp.dyn = 0;
+  kp.next_ctr = nullptr;
+  if (pl.pair) {
+    // Each pair launch takes the next counter region (stream-K and work
+    // counters), so launches in flight at once never share counters.
     static std::atomic<unsigned> next_region{0};
-    kp.sk_count = base + (size_t)(next_region.fetch_add(1, std::memory_order_relaxed) % kSkRegions) *
-                             kSkRegionCounters;
+    const size_t region = next_region.fetch_add(1, std::memory_order_relaxed) % kSkRegions;
+    if (pl.sk_tiles > 0) {
+      if (pl.splits != 1 || pl.sk_tiles > kMaxTailTiles || !ws)
+        return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: inconsistent stream-K plan");
+      unsigned* base = nullptr;
+      rc = counters(0, &base);
+      if (rc != NS_OK) return rc;
+      kp.sk_count = base + region * kSkRegionCounters;
+    }
+    if (t_pair_dyn) {
+      unsigned* base = nullptr;
+      rc = counters(1, &base);
+      if (rc != NS_OK) return rc;
+      kp.dyn = 1;
+      kp.next_ctr = base + region * kPairCounterStride;
+    }
+  } else if (pl.sk_tiles > 0) {
+    return fail(NS_ERR_INVALID_ARGUMENT, "ns_gemm: inconsistent stream-K plan");
   }
   // Transposed single-pass plans store the raw product and apply epilogues
   // that read aux in a separate coalesced pass.
@@ -1649,6 +1840,12 @@ int set_accumulation_chunk(int kblocks) {
   return old;
 }
 
+int set_pair_schedule(int dynamic) {
+  const int old = t_pair_dyn;
+  t_pair_dyn = dynamic ? 1 : 0;
+  return old;
+}
+
 // Self-test of the bounded waits: one warp waits on an mbarrier that nothing
 // arrives at, with the kernels' wait function and a short limit, so the wait
 // runs out, raises the timeout flag and the kernel returns.
@@ -1683,10 +1880,13 @@ int consume_timeout_flag() {
     const int zero = 0;
     e = cudaMemcpyToSymbol(g_timeout, &zero, sizeof(int));
     if (e != cudaSuccess) return -(int)e;
-    // A kernel that gave up may have left stream-K counters part-way.
+    // A kernel that gave up may have left stream-K or work counters part-way.
     void* addr = nullptr;
     e = cudaGetSymbolAddress(&addr, g_sk_count);
     if (e == cudaSuccess) e = cudaMemset(addr, 0, sizeof(unsigned) * kSkRegions * kSkRegionCounters);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&addr, g_pair_next);
+    if (e == cudaSuccess)
+      e = cudaMemset(addr, 0, sizeof(unsigned) * kSkRegions * kPairCounterStride);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return -(int)e;
   }

@@ -69,6 +69,13 @@ int consume_timeout_flag();
 // setting (2 = default).
 int set_accumulation_chunk(int kblocks);
 
+// CTA-pair kernel schedule for subsequent launches on this host thread: 1 =
+// dynamic (cluster c starts on item c, then takes its next work item from a
+// per-launch counter when it is ready for one; the default), 0 = fixed
+// (cluster c takes items c, c + clusters, ...).  Results are bit-identical.
+// Returns the previous setting.
+int set_pair_schedule(int dynamic);
+
 // Launches the bounded-wait self-test kernel (a wait that runs out after
 // limit_us microseconds and raises the flag consume_timeout_flag reads).
 ns_status wait_probe(int limit_us, cudaStream_t s);
