@@ -145,11 +145,15 @@ NS_API ns_status ns_gemm_lo_out(int M, int N, int K, const float* A, int lda, in
  * (where the workspace allows), 5 = as 4 but storing rows of C instead of
  * computing C^T, 6 / 7 / 8 = CTA-pair tiles 256 x 192 / 256 x 128 / 256 x 256 only,
  * 9 = as 0 but never running a part-filled last wave of CTA-pair tiles as a
- * stream-K tail (the leftover tiles' k-blocks shared by all pairs), 10 = as 0
- * but with the CTA-pair kernel's work handed out in a fixed order (cluster c
- * takes tiles c, c + clusters, ...) instead of from a per-launch counter as
- * the clusters become ready (results are bit-identical either way).
- * TEST AND PROFILING ONLY: engines 1-10 exist so tests can cross-check the
+ * stream-K tail (the leftover tiles' k-blocks shared by all pairs), 10 / 11
+ * = as 0 but with the CTA-pair kernel's work always handed out in a fixed
+ * order (cluster c takes tiles c, c + clusters, ...) / always from a
+ * per-launch counter as the clusters become ready.  Under engine 0 GEMM calls
+ * use the fixed order and ns_gpt_backward uses the counter when a
+ * communicator with world_size > 1 is attached (the all-reduce beside the
+ * backward holds SMs; clusters that start late then take fewer tiles).
+ * Results are bit-identical either way.
+ * TEST AND PROFILING ONLY: engines 1-11 exist so tests can cross-check the
  * kernels against one another and profiles can time one tile shape alone;
  * production callers leave the engine at 0, the only setting the planner's
  * shape choices are tuned for. */

@@ -116,9 +116,9 @@ size_t ns_gemm_workspace_size(int M, int N, int K) {
 }
 
 ns_status ns_gemm_set_engine(int engine) {
-  NS_REQUIRE(engine >= 0 && engine <= 10, "ns_gemm_set_engine: engine must be 0..10");
+  NS_REQUIRE(engine >= 0 && engine <= 11, "ns_gemm_set_engine: engine must be 0..11");
   t_engine = engine;
-  tc::set_pair_schedule(engine == 10 ? 0 : 1);
+  tc::set_pair_schedule(engine == 10 ? 0 : engine == 11 ? 1 : -1);
   return NS_OK;
 }
 

@@ -207,7 +207,10 @@ struct PairWork {
 constexpr int kChunk = 2;  // default; KParams::chunk is what the kernels use
 
 thread_local int t_chunk = kChunk;  // per host thread: see set_accumulation_chunk
-thread_local int t_pair_dyn = 1;    // per host thread: see set_pair_schedule
+// Per host thread: the pair schedule forced by the engine (-1: none) and the
+// one a model call picked (see set_pair_schedule, PairScheduleScope).
+thread_local int t_pair_forced = -1;
+thread_local int t_pair_model = 0;
 
 template <int BN, int STAGES, bool PRE>
 struct Layout {
@@ -1782,7 +1785,7 @@ ns_status run(const Plan& pl, int M, int N, int K, const float* A, int lda, int 
       if (rc != NS_OK) return rc;
       kp.sk_count = base + region * kSkRegionCounters;
     }
-    if (t_pair_dyn) {
+    if (t_pair_forced >= 0 ? t_pair_forced : t_pair_model) {
       unsigned* base = nullptr;
       rc = counters(1, &base);
       if (rc != NS_OK) return rc;
@@ -1840,11 +1843,16 @@ int set_accumulation_chunk(int kblocks) {
   return old;
 }
 
-int set_pair_schedule(int dynamic) {
-  const int old = t_pair_dyn;
-  t_pair_dyn = dynamic ? 1 : 0;
+int set_pair_schedule(int mode) {
+  const int old = t_pair_forced;
+  t_pair_forced = mode < 0 ? -1 : mode ? 1 : 0;
   return old;
 }
+
+PairScheduleScope::PairScheduleScope(bool dynamic) : saved_(t_pair_model) {
+  t_pair_model = dynamic ? 1 : 0;
+}
+PairScheduleScope::~PairScheduleScope() { t_pair_model = saved_; }
 
 // Self-test of the bounded waits: one warp waits on an mbarrier that nothing
 // arrives at, with the kernels' wait function and a short limit, so the wait

@@ -69,12 +69,31 @@ int consume_timeout_flag();
 // setting (2 = default).
 int set_accumulation_chunk(int kblocks);
 
-// CTA-pair kernel schedule for subsequent launches on this host thread: 1 =
-// dynamic (cluster c starts on item c, then takes its next work item from a
-// per-launch counter when it is ready for one; the default), 0 = fixed
-// (cluster c takes items c, c + clusters, ...).  Results are bit-identical.
-// Returns the previous setting.
-int set_pair_schedule(int dynamic);
+// CTA-pair kernel schedule, fixed (cluster c takes items c, c + clusters,
+// ...) or dynamic (cluster c starts on item c, then takes its next item from
+// a per-launch counter when it is ready for one).  Results are bit-identical.
+// The dynamic order pays when another stream's kernel holds SMs while a GEMM
+// starts (the all-reduce beside a data-parallel backward); alone on the GPU
+// the fixed order measured the same or slightly faster.  So GEMM calls use
+// the fixed order, and a backward whose gradient buckets are all-reduced
+// beside it picks the dynamic one for its own GEMMs (PairScheduleScope).
+// set_pair_schedule forces one for subsequent launches on this host thread
+// (1 dynamic, 0 fixed, -1 none: the rule above) and returns the previous
+// setting.
+int set_pair_schedule(int mode);
+
+// For the lifetime of the object, the GEMMs this host thread launches use the
+// dynamic order if `dynamic` (unless set_pair_schedule forces one).
+class PairScheduleScope {
+ public:
+  explicit PairScheduleScope(bool dynamic);
+  ~PairScheduleScope();
+  PairScheduleScope(const PairScheduleScope&) = delete;
+  PairScheduleScope& operator=(const PairScheduleScope&) = delete;
+
+ private:
+  int saved_;
+};
 
 // Launches the bounded-wait self-test kernel (a wait that runs out after
 // limit_us microseconds and raises the flag consume_timeout_flag reads).

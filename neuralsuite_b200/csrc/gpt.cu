@@ -19,6 +19,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "gpt_device.h"
+#include "gemm_tc.cuh"
 #include "gpt_handle.h"
 #include "nsf.h"
 
@@ -374,6 +375,8 @@ ns_status ns_gpt_loss_backward(ns_gpt* h, const int32_t* targets, void* stream) 
 
 ns_status ns_gpt_backward(ns_gpt* h, void* stream) {
   NS_REQUIRE(h, "ns_gpt_backward: NULL model");
+  // The all-reduce of earlier buckets runs beside these GEMMs: dynamic order.
+  const nsb::tc::PairScheduleScope sched(h->comm && h->world > 1);
   return Guard([&]() -> ns_status { return backward_impl(h, nsb::as_stream(stream)); });
 }
 

@@ -37,9 +37,11 @@ def set_gemm_engine(engine: int) -> None:
     2 = tcgen05 with the operand split done inside the kernel, 3 / 4 = only
     256 x 256 CTA-pair / 128 x 256 tiles (pre-split operands), 5 = as 4 with
     row stores, 6 / 7 / 8 = pair tiles 256 x 192 / 256 x 128 / 256 x 256 only,
-    9 = automatic without the stream-K tail, 10 = automatic with the CTA-pair
-    kernel's work handed out in a fixed order (bit-identical results).
-    Engines 1-10 are for tests and profiling."""
+    9 = automatic without the stream-K tail, 10 / 11 = automatic with the
+    CTA-pair kernel's work always handed out in a fixed order / always from a
+    per-launch counter (engine 0: fixed, except in a data-parallel GPT
+    backward; bit-identical results).  Engines 1-11 are for tests
+    and profiling."""
     _lib.check(_lib.load().ns_gemm_set_engine(engine))
 
 

@@ -1,7 +1,8 @@
-"""The CTA-pair GEMM's work schedule: by default cluster c starts on tile c
-and then takes its next tile (or stream-K run) from a per-launch counter when
-its producer is ready for one; engine 10 hands the same items out in a fixed
-order (cluster c takes items c, c + clusters, ...).  Every item is computed
+"""The CTA-pair GEMM's work schedule: in the dynamic order (engine 11, and a
+data-parallel GPT backward) cluster c starts on tile c and then takes its
+next tile (or stream-K run) from a per-launch counter when its producer is
+ready for one; the fixed order (engine 0's GEMM calls, engine 10) hands the
+same items out as cluster c takes items c, c + clusters, ....  Every item is computed
 the same way whichever cluster takes it, so the two must agree bit for bit,
 on plain, stream-K, split-K and transposed plans, with fewer tiles than
 clusters, and over more launches than there are counter regions (each
@@ -19,6 +20,7 @@ from tests._util import normal, rel_l2, rng
 pytestmark = pytest.mark.gpu
 
 FIXED = 10  # engine: the automatic plan, pair work in a fixed order
+DYNAMIC = 11  # engine: the automatic plan, pair work from a per-launch counter
 
 
 def dev(a, device):
@@ -54,14 +56,17 @@ def test_dynamic_schedule_equals_fixed_order_bitwise(cuda, M, N, K, form):
     r = rng(11 * M + 5 * N + K + len(form))
     A, B, kw, want = operands(r, M, N, K, form)
     Ad, Bd = dev(A, cuda), dev(B, cuda)
-    dyn = host(nk.gemm(Ad, Bd, **kw))
-    nk.set_gemm_engine(FIXED)
-    try:
-        fixed = host(nk.gemm(Ad, Bd, **kw))
-    finally:
-        nk.set_gemm_engine(0)
+    out = {}
+    for engine in (DYNAMIC, FIXED, 0):
+        nk.set_gemm_engine(engine)
+        try:
+            out[engine] = host(nk.gemm(Ad, Bd, **kw))
+        finally:
+            nk.set_gemm_engine(0)
+    dyn, fixed = out[DYNAMIC], out[FIXED]
     assert rel_l2(dyn.astype(np.float64), want) < 5e-6, (form, M, N, K)
     assert np.array_equal(dyn.view(np.uint32), fixed.view(np.uint32)), (form, M, N, K)
+    assert np.array_equal(out[0].view(np.uint32), fixed.view(np.uint32)), (form, M, N, K)
     nk.kernel_health()
 
 
@@ -69,6 +74,14 @@ def test_work_counters_return_to_zero_over_many_launches(cuda):
     """48 launches (three times round the 16 counter regions) of a stream-K
     product and a plain one, interleaved on one stream: every launch gives the
     first launch's bits, so no launch found its counter part-way."""
+    nk.set_gemm_engine(DYNAMIC)
+    try:
+        _many_launches(cuda)
+    finally:
+        nk.set_gemm_engine(0)
+
+
+def _many_launches(cuda):
     r = rng(2024)
     X, W = normal(r, (8192, 3072)), normal(r, (3072, 768))
     P, Q = normal(r, (8192, 768)), normal(r, (768, 3072))
