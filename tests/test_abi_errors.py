@@ -207,3 +207,15 @@ def test_conv2d_rejects_bad_parameters(lib):
 def test_lstm_engine_checks(lib):
     _err(lib, lib.ns_lstm_set_engine(2), NS_ERR_INVALID_ARGUMENT, "engine")
     assert lib.ns_lstm_set_engine(0) == NS_OK
+
+
+def test_gemm_engine_checks(lib):
+    """Engines 0-11 are accepted (10 / 11 force the CTA-pair kernel's fixed or
+    counter-driven work order); anything else is rejected with a message."""
+    for bad in (-1, 12):
+        _err(lib, lib.ns_gemm_set_engine(bad), NS_ERR_INVALID_ARGUMENT, "engine")
+    try:
+        for good in (10, 11, 0):
+            assert lib.ns_gemm_set_engine(good) == NS_OK
+    finally:
+        assert lib.ns_gemm_set_engine(0) == NS_OK
